@@ -1,0 +1,227 @@
+/*
+ * iris_b200 — C ABI of the B200-native exact-integer inference path.
+ *
+ * Conventions (those of the reference's crates/inference/kernels/cuda/
+ * q8_product.cu:129-197 and its Rust binding crates/inference/kernels/src/
+ * gpu.rs:45-62):
+ *   - every entry point returns an int status: 0 on success, otherwise a
+ *     cudaError_t value or one of the IRIS_E* codes below; iris_error() (or
+ *     q8gpu_error()) turns it into a static string;
+ *   - host buffers are owned by the caller and only borrowed for the call;
+ *   - device state lives behind opaque handles freed by the matching *_free;
+ *   - activations are Q16.16 int32, accumulators Q32.32 int64, weights Q8_0
+ *     (34-byte GGUF blocks: little-endian fp16 scale bits, then 32 int8) or
+ *     dense Q16.16 int32;
+ *   - no floating point anywhere: every value equals the reference's Rust CPU
+ *     path (det-num) bit for bit.
+ * A handle may be used by one host thread at a time.
+ */
+#ifndef IRIS_B200_H
+#define IRIS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Status codes beyond cudaError_t (all >= 10000). */
+#define IRIS_EINVAL 10001   /* bad argument, shape or parameter */
+#define IRIS_ESCALE 10002   /* a Q8_0 scale is Inf/NaN (q8.rs:46-48 rejects it) */
+#define IRIS_ERANGE 10003   /* a position past max_positions or the KV capacity */
+#define IRIS_ESTATE 10004   /* call out of order (e.g. decode before prefill) */
+#define IRIS_EWINDOW 10005  /* attention window not covered by the given keys */
+
+/* ---------------------------------------------------------------------------
+ * 1. Drop-in for the reference's q8gpu_* FFI. Same names, signatures and
+ *    semantics as crates/inference/kernels/cuda/q8_product.cu:129-197, so the
+ *    unchanged `extern "C"` block of gpu.rs:45-62 links against this library.
+ * ------------------------------------------------------------------------- */
+typedef struct Q8GpuMatrix Q8GpuMatrix;
+
+/* q8_product.cu:131 — message for a status code (static storage). */
+const char* q8gpu_error(int code);
+/* q8_product.cu:134-139 — 0 when a device is usable. */
+int q8gpu_init(void);
+/* q8_product.cu:141-146 — frees a matrix from q8gpu_upload (NULL is a no-op). */
+void q8gpu_free(Q8GpuMatrix* matrix);
+/* q8_product.cu:150-171 — weights: rows*cols int8 row-major; scales_q24: one
+ * decoded Q.24 block scale per 32 weights (q8.rs:27-43). Each scale must be
+ * the exact image of a finite fp16 scale (what gpu.rs:175-186 passes);
+ * anything else returns IRIS_ESCALE. */
+int q8gpu_upload(const int8_t* weights, const int64_t* scales_q24, uint32_t rows, uint32_t cols,
+                 Q8GpuMatrix** out_matrix);
+/* q8_product.cu:175-195 — out[token*rows + row] = dot_row(activations[token],
+ * row) (q8.rs:56-72) for tokens x cols host activations. */
+int q8gpu_product(const Q8GpuMatrix* matrix, const int32_t* activations, uint32_t tokens,
+                  int32_t* out);
+
+/* ---------------------------------------------------------------------------
+ * 2. Q8_0 products without the host round trip.
+ * ------------------------------------------------------------------------- */
+/* Uploads a matrix from its committed Q8_0 bytes (Q8Source parts concatenated,
+ * crates/inference/kernels/src/tensor.rs:110-115): rows*cols/32*34 bytes.
+ * Replaces the host-side scale decoding of gpu.rs:175-186. */
+int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
+                          Q8GpuMatrix** out_matrix);
+/* The same product as q8gpu_product with device pointers on a CUDA stream
+ * (cudaStream_t passed as void*, NULL = default stream). Asynchronous. */
+int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activations,
+                           uint32_t tokens, int32_t* d_out, void* stream);
+/* Generic-kernel timing hooks for the Q8 sweep: same product, forced through
+ * the decode GEMV (tokens must be 1) or the tiled GEMM. */
+int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_activations,
+                                uint32_t tokens, int32_t* d_out, void* stream, int path);
+#define IRIS_PATH_AUTO 0
+#define IRIS_PATH_GEMV 1
+#define IRIS_PATH_GEMM 2
+
+/* ---------------------------------------------------------------------------
+ * 3. Device-resident models, sessions and the decode loop.
+ * ------------------------------------------------------------------------- */
+typedef struct IrisModel IrisModel;
+typedef struct IrisSession IrisSession;
+
+/* mistral-dense shape (crates/inference/artifacts/src/direct.rs:267-287). */
+typedef struct {
+  uint32_t layers, hidden, ffn, heads, kv_heads, head_dim, vocab;
+  uint32_t max_positions;        /* positions from here on are refused */
+  int64_t norm_eps;              /* Acc bits */
+  uint32_t attention_scale_q32;  /* mistral.rs:148-160 */
+  uint32_t tied_head;            /* head = embedding table */
+  const int64_t* rope_inverse_frequencies; /* head_dim/2 Q32.32 values, copied */
+} IrisMistralShape;
+
+/* gemma-dense shape (direct.rs:241-262) with the per-layer values the
+ * reference derives from it (direct/src/model.rs:802-871). */
+typedef struct {
+  uint32_t layers, hidden, ffn, heads, kv_heads, head_dim, vocab, ple_width;
+  int64_t norm_eps;
+  int32_t embedding_scale, ple_embedding_scale, ple_projection_scalar, ple_input_scale;
+  int32_t final_logit_softcap; /* 0 disables */
+  /* per layer (arrays of `layers` entries, copied) */
+  const uint32_t* sliding_window;     /* 0 = full attention */
+  const int64_t* rope_base;           /* Acc bits */
+  const uint32_t* rotary_dim;
+  const uint32_t* rope_freq_base_dim;
+  const int32_t* kv_donor_layer;      /* -1 = own K/V */
+  const int32_t* layer_scalar;        /* 0 = none */
+} IrisGemmaShape;
+
+/* Tensor kinds for iris_model_set_q8 / iris_model_set_values. */
+enum {
+  IRIS_T_EMBED = 0,       /* [vocab][hidden] Q8_0 */
+  IRIS_T_HEAD = 1,        /* [vocab][hidden] Q8_0 (untied models) */
+  IRIS_T_FINAL_NORM = 2,  /* [hidden] */
+  IRIS_T_W_Q = 3, IRIS_T_W_K = 4, IRIS_T_W_V = 5, IRIS_T_W_O = 6,
+  IRIS_T_W_GATE = 7, IRIS_T_W_UP = 8, IRIS_T_W_DOWN = 9,
+  IRIS_T_NORM_ATTN = 10,  /* mistral input_layernorm / gemma norm_input */
+  IRIS_T_NORM_FFN = 11,   /* mistral pre_feedforward / gemma norm_pre_ffw */
+  IRIS_T_NORM_POST_ATTN = 12, IRIS_T_NORM_POST_FFW = 13,
+  IRIS_T_Q_NORM = 14, IRIS_T_K_NORM = 15, IRIS_T_PLE_POST_NORM = 16,
+  IRIS_T_PLE_INPUT_GATE = 17,       /* [ple][hidden] dense */
+  IRIS_T_PLE_LAYER_PROJECTION = 18, /* [hidden][ple] dense */
+  IRIS_T_PLE_EMBED = 19,            /* [vocab][layers*ple] Q8_0 */
+  IRIS_T_PLE_MODEL_PROJECTION = 20, /* [layers*ple][hidden] dense */
+  IRIS_T_PLE_NORM = 21,             /* [ple] */
+  IRIS_T_COUNT = 22
+};
+
+int iris_model_create_mistral(const IrisMistralShape* shape, IrisModel** out);
+int iris_model_create_gemma(const IrisGemmaShape* shape, IrisModel** out);
+/* Uploads one Q8_0 tensor (layer = -1 for model-level tensors). */
+int iris_model_set_q8(IrisModel* model, int tensor, int32_t layer, const uint8_t* blocks,
+                      uint64_t bytes);
+/* Uploads one dense Q16.16 tensor (norm weights, PLE matrices). */
+int iris_model_set_values(IrisModel* model, int tensor, int32_t layer, const int32_t* values,
+                          uint64_t count);
+/* Fills every tensor with the seeded synthetic weights of iris_synth_* on the
+ * device (no host copy). */
+int iris_model_synthesize(IrisModel* model, uint64_t seed, int per_block_scales);
+/* Reads a tensor back: Q8_0 bytes or int32 values. */
+int iris_model_get_q8(const IrisModel* model, int tensor, int32_t layer, uint8_t* blocks,
+                      uint64_t bytes);
+int iris_model_get_values(const IrisModel* model, int tensor, int32_t layer, int32_t* values,
+                          uint64_t count);
+/* Device bytes held by the model's weights. */
+uint64_t iris_model_weight_bytes(const IrisModel* model);
+void iris_model_free(IrisModel* model);
+
+/* A decoding session: the K/V cache for up to max_positions positions. */
+int iris_session_create(IrisModel* model, uint32_t max_positions, IrisSession** out);
+/* Forgets every position. */
+int iris_session_reset(IrisSession* session);
+/* Prompt pass (executor.rs:143-152): the prompt rows through every layer, K/V
+ * kept, then the head over the last row. logits (vocab values, may be NULL)
+ * and *token (its first maximum, generation.rs:25-58). */
+int iris_session_prefill(IrisSession* session, const uint32_t* ids, uint32_t n, int32_t* logits,
+                         uint32_t* token);
+/* One decode pass (executor.rs:172-184): token_in at the next position, then
+ * the head. */
+int iris_session_decode(IrisSession* session, uint32_t token_in, int32_t* logits,
+                        uint32_t* token_out);
+/* The direct decode loop (executor.rs:136-186): prefill, then up to
+ * max_tokens greedy selections, stopping after an EOS id or the budget (no
+ * pass for the last token). out_tokens holds max_tokens entries; out_logits
+ * (may be NULL) receives [passes][vocab], pass p being the scores that chose
+ * out_tokens[p]. Decode passes replay one captured CUDA graph with the token
+ * id kept on the device. */
+int iris_generate(IrisSession* session, const uint32_t* prompt, uint32_t n_prompt,
+                  uint32_t max_tokens, const uint32_t* eos, uint32_t n_eos, uint32_t* out_tokens,
+                  uint32_t* out_count, int32_t* out_logits);
+/* Positions currently held. */
+uint32_t iris_session_length(const IrisSession* session);
+/* Device-resident decode loop: replays the captured decode pass `steps` times
+ * on the session's stream without waiting (each pass feeds its first-maximum
+ * token to the next). iris_session_synchronize waits for them. */
+int iris_session_decode_steps(IrisSession* session, uint32_t steps);
+int iris_session_synchronize(IrisSession* session);
+/* The session's CUDA stream (cudaStream_t as void*), for timing with events. */
+void* iris_session_stream(IrisSession* session);
+/* Kernel launches in one captured decode pass. */
+uint32_t iris_session_graph_kernels(IrisSession* session);
+/* Launches one decode product of layer `layer` on the session's stream
+ * (which: 0 = fused q|k|v, 1 = o, 2 = gate|up, 3 = down, 4 = head) with the
+ * session's current activations; the result is discarded. For timing. */
+int iris_session_product(IrisSession* session, uint32_t layer, int which);
+/* Reads count K/V rows of one layer starting at position first
+ * (kv_heads*head_dim values each). For a gemma sliding layer these are the
+ * positions the window still holds. */
+int iris_session_get_kv(const IrisSession* session, uint32_t layer, uint32_t first, uint32_t count,
+                        int32_t* k, int32_t* v);
+void iris_session_free(IrisSession* session);
+
+/* ---------------------------------------------------------------------------
+ * 4. The teacher-forced chain stage: one layer over one range of rows
+ *    (mistral/layer.rs:107-270 via stage.rs:172-226; gemma
+ *    prefill_range.rs:307-333). Host buffers in and out.
+ * ------------------------------------------------------------------------- */
+/* mistral-dense: prior_k/prior_v hold the layer's keys for positions
+ * 0..start (start rows). Writes m output rows and the range's own K/V. */
+int iris_mistral_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows_in, uint32_t m,
+                             uint32_t start, const int32_t* prior_k, const int32_t* prior_v,
+                             int32_t* rows_out, int32_t* own_k, int32_t* own_v);
+
+/* ---------------------------------------------------------------------------
+ * 5. Seeded synthetic weights (the benchmark configs' inputs). Host copies of
+ *    the generator the device uses in iris_model_synthesize.
+ * ------------------------------------------------------------------------- */
+int iris_synth_q8(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,
+                  int per_block_scales, uint8_t* blocks);
+int iris_synth_values(uint64_t seed, uint32_t tensor, int32_t layer, uint64_t count, uint32_t fan_in,
+                      int32_t* values);
+
+/* Message for any status this library returns. */
+const char* iris_error(int code);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif /* IRIS_B200_H */

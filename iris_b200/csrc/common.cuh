@@ -1,0 +1,117 @@
+// Shared device helpers: error plumbing, PTX wrappers and the byte-plane
+// activation format the Q8 kernels consume.
+//
+// Byte planes. A Q16.16 activation a (int32) is split into four bytes
+// a = b0 + 2^8 b1 + 2^16 b2 + 2^24 b3 with b0..b2 unsigned and b3 signed. A
+// vector of K activations is stored as four K-byte planes, plane p holding
+// byte p of every value. A Q8_0 block sum sum_j q_j a_j then becomes four
+// dp4a chains, each exact in int32 (|q| <= 128, b <= 255, 16 or 32 terms),
+// recombined exactly in 64 bits. Planes are written once per activation row
+// and read by every block of the product that consumes it.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "detnum.cuh"
+
+namespace iris {
+
+#define IRIS_CHECK(expr)                         \
+  do {                                           \
+    cudaError_t _e = (expr);                     \
+    if (_e != cudaSuccess) return (int)_e;       \
+  } while (0)
+
+__device__ __forceinline__ int dp4a_su(uint32_t w_s8, uint32_t a_u8, int c) {
+  int d;
+  asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(w_s8), "r"(a_u8), "r"(c));
+  return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t w_s8, uint32_t a_s8, int c) {
+  int d;
+  asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(w_s8), "r"(a_s8), "r"(c));
+  return d;
+}
+
+// Streaming 16-byte load that bypasses L1 (weights are read once per pass).
+__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint16_t ld_stream_u16(const uint16_t* p) {
+  uint16_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+// Sixteen weights (one uint4) against the four planes of the same sixteen
+// activations: the exact 64-bit partial block sum.
+__device__ __forceinline__ int64_t q8_partial16(uint4 w, uint4 p0, uint4 p1, uint4 p2, uint4 p3) {
+  int s0 = dp4a_su(w.x, p0.x, 0);
+  s0 = dp4a_su(w.y, p0.y, s0);
+  s0 = dp4a_su(w.z, p0.z, s0);
+  s0 = dp4a_su(w.w, p0.w, s0);
+  int s1 = dp4a_su(w.x, p1.x, 0);
+  s1 = dp4a_su(w.y, p1.y, s1);
+  s1 = dp4a_su(w.z, p1.z, s1);
+  s1 = dp4a_su(w.w, p1.w, s1);
+  int s2 = dp4a_su(w.x, p2.x, 0);
+  s2 = dp4a_su(w.y, p2.y, s2);
+  s2 = dp4a_su(w.z, p2.z, s2);
+  s2 = dp4a_su(w.w, p2.w, s2);
+  int s3 = dp4a_ss(w.x, p3.x, 0);
+  s3 = dp4a_ss(w.y, p3.y, s3);
+  s3 = dp4a_ss(w.z, p3.z, s3);
+  s3 = dp4a_ss(w.w, p3.w, s3);
+  // |s0 + 256 s1| < 2^28 and |s2 + 256 s3| < 2^27: both exact in int32.
+  return (int64_t)(s0 + s1 * 256) + ((int64_t)(s2 + s3 * 256) << 16);
+}
+
+// Warp-wide sum of a 128-bit accumulator (every lane ends with the total).
+__device__ __forceinline__ Acc128 warp_sum_acc128(Acc128 a) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    uint64_t lo = __shfl_xor_sync(0xffffffffu, a.lo, off);
+    int64_t hi = __shfl_xor_sync(0xffffffffu, a.hi, off);
+    acc128_add(a, lo, hi);
+  }
+  return a;
+}
+
+__device__ __forceinline__ int64_t warp_sum_i64(int64_t v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1)
+    v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+__device__ __forceinline__ uint64_t warp_sum_sat_nonneg(uint64_t v) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) v = add_sat_nonneg(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+// Writes one activation into the four planes of a K-wide row.
+__device__ __forceinline__ void put_planes(uint8_t* planes, uint32_t k, uint32_t idx, int32_t v) {
+  uint32_t u = (uint32_t)v;
+  planes[idx] = (uint8_t)u;
+  planes[k + idx] = (uint8_t)(u >> 8);
+  planes[2 * k + idx] = (uint8_t)(u >> 16);
+  planes[3 * k + idx] = (uint8_t)(u >> 24);
+}
+// Four consecutive activations as one 32-bit word per plane.
+__device__ __forceinline__ void put_planes4(uint8_t* planes, uint32_t k, uint32_t idx, int4 v) {
+  uint32_t a = (uint32_t)v.x, b = (uint32_t)v.y, c = (uint32_t)v.z, d = (uint32_t)v.w;
+  uint32_t w0 = __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+  uint32_t w1 = __byte_perm(__byte_perm(a, b, 0x0051), __byte_perm(c, d, 0x0051), 0x5410);
+  uint32_t w2 = __byte_perm(__byte_perm(a, b, 0x0062), __byte_perm(c, d, 0x0062), 0x5410);
+  uint32_t w3 = __byte_perm(__byte_perm(a, b, 0x0073), __byte_perm(c, d, 0x0073), 0x5410);
+  *(uint32_t*)(planes + idx) = w0;
+  *(uint32_t*)(planes + k + idx) = w1;
+  *(uint32_t*)(planes + 2 * k + idx) = w2;
+  *(uint32_t*)(planes + 3 * k + idx) = w3;
+}
+
+}  // namespace iris

@@ -1,0 +1,516 @@
+// Row-level kernels of the mistral-dense and gemma-dense layers.
+//
+// Attention reproduces attention_softmax (crates/det-num/src/ops.rs:233-261)
+// exactly while splitting the positions over many blocks:
+//   1. scores (mistral.rs:130-145 scaled, or tensor.rs:522-528 dot_bits),
+//      and each chunk's first maximum (value, then lowest position);
+//   2. e^(score - max) terms against the global first maximum and their
+//      chunk sums (exact: every term is at most 2^32, so the i64 sum of fewer
+//      than 2^31 terms cannot saturate);
+//   3. weights requantize((term << 32) / sum) (ties to even), the chunk's
+//      weighted value sums (wrapping i64, order-free) and weight sums; the
+//      last block adds the residual 1.0 - sum(weights) times the first
+//      maximum's value row (the same as adding it to that weight first,
+//      since no weight saturates) and requantizes.
+#include <cuda_runtime.h>
+
+#include "layers.cuh"
+
+namespace iris {
+
+__device__ __forceinline__ uint32_t window_start(uint32_t p, uint32_t window) {
+  // prefill_range.rs:866-874
+  if (window == 0) return 0;
+  return p + 1 > window ? p + 1 - window : 0;
+}
+
+__device__ __forceinline__ int32_t finish_score(int64_t sum, int mode, uint32_t scale) {
+  return mode == SCORE_MISTRAL ? scaled_score_finish(sum, scale) : requantize(sum);
+}
+
+__device__ __forceinline__ int64_t ldcg_i64(const int64_t* p) { return (int64_t)__ldcg((const long long*)p); }
+
+// ---------------------------------------------------------------------------
+// Decode attention
+// ---------------------------------------------------------------------------
+
+constexpr int kAttnThreads = 128;
+constexpr int kMaxGroup = 16;  // query heads per kv head
+
+__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) int32_t q_s[];  // [G][d]
+  __shared__ unsigned long long best_s[kMaxGroup];
+  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
+  const uint32_t t0 = ws + c * a.chunk;
+  if (t0 > p) return;
+  for (uint32_t i = threadIdx.x; i < G * a.d; i += blockDim.x) q_s[i] = a.q[g * G * a.d + i];
+  if (threadIdx.x < G) best_s[threadIdx.x] = 0;
+  __syncthreads();
+  const uint32_t hs = blockDim.x / a.chunk;  // threads sharing a position
+  const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
+  const uint32_t t = t0 + lp;
+  if (t <= p) {
+    const int32_t* krow = a.kcache + (size_t)t * a.kvd + g * a.d;
+    for (uint32_t h = hg; h < G; h += hs) {
+      const int32_t* qh = q_s + h * a.d;
+      int64_t sum = 0;
+      for (uint32_t i = 0; i < a.d; i += 4) {
+        int4 k4 = *(const int4*)(krow + i);
+        int4 q4 = *(const int4*)(qh + i);
+        sum = (int64_t)((uint64_t)sum + (uint64_t)((int64_t)q4.x * k4.x) + (uint64_t)((int64_t)q4.y * k4.y) +
+                        (uint64_t)((int64_t)q4.z * k4.z) + (uint64_t)((int64_t)q4.w * k4.w));
+      }
+      int32_t sc = finish_score(sum, a.mode, a.scale_q32);
+      uint32_t hh = g * G + h;
+      a.scores[(size_t)hh * a.cap + t] = sc;
+      atomicMax(&best_s[h], best_key(sc, t));
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < G) a.chunk_best[(g * G + threadIdx.x) * a.nchunks + c] = best_s[threadIdx.x];
+}
+
+__device__ void group_global_best(const AttnArgs& a, uint32_t g, uint32_t G, uint32_t nact,
+                                  unsigned long long* best_s) {
+  if (threadIdx.x < G) {
+    unsigned long long b = 0;
+    const unsigned long long* cb = a.chunk_best + (size_t)(g * G + threadIdx.x) * a.nchunks;
+    for (uint32_t k = 0; k < nact; ++k) b = cb[k] > b ? cb[k] : b;
+    best_s[threadIdx.x] = b;
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
+  __shared__ unsigned long long best_s[kMaxGroup];
+  __shared__ unsigned long long sum_s[kMaxGroup];
+  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
+  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
+  if (c >= nact) return;
+  group_global_best(a, g, G, nact, best_s);
+  if (threadIdx.x < G) sum_s[threadIdx.x] = 0;
+  __syncthreads();
+  const uint32_t hs = blockDim.x / a.chunk;
+  const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
+  const uint32_t t = ws + c * a.chunk + lp;
+  if (t <= p) {
+    for (uint32_t h = hg; h < G; h += hs) {
+      uint32_t hh = g * G + h;
+      int64_t e = softmax_exp_term_act(a.scores[(size_t)hh * a.cap + t], best_key_value(best_s[h]));
+      a.terms[(size_t)hh * a.cap + t] = e;
+      atomicAdd(&sum_s[h], (unsigned long long)e);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < G) a.chunk_sum[(g * G + threadIdx.x) * a.nchunks + c] = sum_s[threadIdx.x];
+}
+
+__global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) int32_t w_s[];  // [G][chunk]
+  __shared__ unsigned long long best_s[kMaxGroup];
+  __shared__ unsigned long long total_s[kMaxGroup];
+  __shared__ int32_t wsum_s[kMaxGroup];
+  __shared__ bool last_s;
+  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
+  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
+  const uint32_t t0 = ws + c * a.chunk;
+  if (c < nact) {
+    if (threadIdx.x < G) {
+      uint64_t tot = 0;
+      const uint64_t* cs = a.chunk_sum + (size_t)(g * G + threadIdx.x) * a.nchunks;
+      for (uint32_t k = 0; k < nact; ++k) tot += cs[k];
+      total_s[threadIdx.x] = tot;
+      wsum_s[threadIdx.x] = 0;
+    }
+    __syncthreads();
+    const uint32_t hs = blockDim.x / a.chunk;
+    const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
+    const uint32_t t = t0 + lp;
+    for (uint32_t h = hg; h < G; h += hs) {
+      int32_t w = 0;
+      if (t <= p) {
+        w = softmax_weight(a.terms[(size_t)(g * G + h) * a.cap + t], total_s[h]);
+        atomicAdd(&wsum_s[h], w);
+      }
+      w_s[h * a.chunk + lp] = w;
+    }
+    __syncthreads();
+    const uint32_t live = min(a.chunk, p + 1 - t0);
+    for (uint32_t o = threadIdx.x; o < G * a.d; o += blockDim.x) {
+      uint32_t h = o / a.d, i = o % a.d;
+      const int32_t* vcol = a.vcache + (size_t)t0 * a.kvd + g * a.d + i;
+      const int32_t* wrow = w_s + h * a.chunk;
+      int64_t acc = 0;
+      for (uint32_t j = 0; j < live; ++j)
+        acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wrow[j] * vcol[(size_t)j * a.kvd]));
+      a.partial[((size_t)c * a.heads + g * G + h) * a.d + i] = acc;
+    }
+    if (threadIdx.x < G) a.chunk_wsum[(g * G + threadIdx.x) * a.nchunks + c] = wsum_s[threadIdx.x];
+  }
+  // The last block of this kv group combines the chunks.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[g], 1u) == gridDim.y - 1;
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  group_global_best(a, g, G, nact, best_s);
+  if (threadIdx.x < G) {
+    int32_t sw = 0;
+    const int32_t* cw = a.chunk_wsum + (size_t)(g * G + threadIdx.x) * a.nchunks;
+    for (uint32_t k = 0; k < nact; ++k) sw += __ldcg(cw + k);
+    wsum_s[threadIdx.x] = sub_sat(kOneAct, sw);  // residual (ops.rs:274-276)
+  }
+  __syncthreads();
+  const uint32_t qd = a.heads * a.d;
+  for (uint32_t o = threadIdx.x; o < G * a.d; o += blockDim.x) {
+    uint32_t h = o / a.d, i = o % a.d, hh = g * G + h;
+    int64_t acc = 0;
+    for (uint32_t k = 0; k < nact; ++k)
+      acc = (int64_t)((uint64_t)acc + (uint64_t)ldcg_i64(a.partial + ((size_t)k * a.heads + hh) * a.d + i));
+    uint32_t tmax = best_key_token(best_s[h]);
+    acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wsum_s[h] * a.vcache[(size_t)tmax * a.kvd + g * a.d + i]));
+    int32_t v = requantize(acc);
+    put_planes(a.ctx_planes, qd, hh * a.d + i, v);
+    if (a.ctx) a.ctx[hh * a.d + i] = v;
+  }
+  if (threadIdx.x == 0) a.counters[g] = 0;
+}
+
+cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
+  uint32_t G = a.heads / a.kv_heads;
+  if (G > kMaxGroup || a.d % 4 || kAttnThreads % a.chunk) return cudaErrorInvalidValue;
+  dim3 grid(a.kv_heads, a.nchunks);
+  attn_scores_kernel<<<grid, kAttnThreads, G * a.d * 4, s>>>(a);
+  attn_exp_kernel<<<grid, kAttnThreads, 0, s>>>(a);
+  attn_out_kernel<<<grid, kAttnThreads, G * a.chunk * 4, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Prefill attention: one block a (query, head)
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ unsigned long long best_s, total_s;
+  __shared__ int32_t wsum_s;
+  const uint32_t tok = blockIdx.x, h = blockIdx.y;
+  const uint32_t G = a.heads / a.kv_heads, g = h / G;
+  const uint32_t p = a.pos0 + tok, ws = window_start(p, a.window), n = p - ws + 1;
+  int32_t* q_s = (int32_t*)sm;                       // [d]
+  int64_t* te = (int64_t*)(sm + ((a.d * 4 + 15) & ~15u));  // [n]
+  int32_t* sc = (int32_t*)(te + n);                  // [n]
+  const uint32_t qd = a.heads * a.d;
+  for (uint32_t i = threadIdx.x; i < a.d; i += blockDim.x) q_s[i] = a.q[(size_t)tok * qd + h * a.d + i];
+  if (threadIdx.x == 0) { best_s = 0; total_s = 0; wsum_s = 0; }
+  __syncthreads();
+  unsigned long long best = 0;
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    const int32_t* krow = a.kcache + (size_t)(ws + j) * a.kvd + g * a.d;
+    int64_t sum = 0;
+    for (uint32_t i = 0; i < a.d; i += 4) {
+      int4 k4 = *(const int4*)(krow + i);
+      int4 q4 = *(const int4*)(q_s + i);
+      sum = (int64_t)((uint64_t)sum + (uint64_t)((int64_t)q4.x * k4.x) + (uint64_t)((int64_t)q4.y * k4.y) +
+                      (uint64_t)((int64_t)q4.z * k4.z) + (uint64_t)((int64_t)q4.w * k4.w));
+    }
+    int32_t s = finish_score(sum, a.mode, a.scale_q32);
+    sc[j] = s;
+    unsigned long long k = best_key(s, j);
+    best = k > best ? k : best;
+  }
+  atomicMax(&best_s, best);
+  __syncthreads();
+  const int32_t mx = best_key_value(best_s);
+  const uint32_t mslot = best_key_token(best_s);
+  unsigned long long tot = 0;
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    int64_t e = softmax_exp_term_act(sc[j], mx);
+    te[j] = e;
+    tot += (unsigned long long)e;
+  }
+  atomicAdd(&total_s, tot);
+  __syncthreads();
+  int32_t ws_local = 0;
+  for (uint32_t j = threadIdx.x; j < n; j += blockDim.x) {
+    int32_t w = softmax_weight(te[j], total_s);
+    sc[j] = w;
+    ws_local += w;
+  }
+  atomicAdd(&wsum_s, ws_local);
+  __syncthreads();
+  if (threadIdx.x == 0) sc[mslot] = add_sat(sc[mslot], sub_sat(kOneAct, wsum_s));
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < a.d; i += blockDim.x) {
+    const int32_t* vcol = a.vcache + (size_t)ws * a.kvd + g * a.d + i;
+    int64_t acc = 0;
+    for (uint32_t j = 0; j < n; ++j)
+      acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)sc[j] * vcol[(size_t)j * a.kvd]));
+    int32_t v = requantize(acc);
+    put_planes(a.ctx_planes + (size_t)tok * 4 * qd, qd, h * a.d + i, v);
+    if (a.ctx) a.ctx[(size_t)tok * qd + h * a.d + i] = v;
+  }
+}
+
+cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_t max_visible,
+                                     cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  if (a.d % 4) return cudaErrorInvalidValue;
+  size_t smem = ((a.d * 4 + 15) & ~15u) + (size_t)max_visible * 12;
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  dim3 grid(tokens, a.heads);
+  attn_prefill_kernel<<<grid, kAttnThreads, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t prepare_layer_kernels() {
+  return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+}
+
+// ---------------------------------------------------------------------------
+// Embeddings, selection bookkeeping
+// ---------------------------------------------------------------------------
+
+__global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t cols,
+                             const uint32_t* ids, int32_t scale, int has_scale, int32_t* out) {
+  uint32_t t = blockIdx.x, id = ids[t];
+  const int8_t* row = q + (size_t)id * cols;
+  const uint16_t* srow = s + (size_t)id * (cols / 32);
+  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    int32_t m, e;
+    q8_scale_parts(srow[i >> 5], &m, &e);
+    int32_t v = q8_dequant(row[i], m, e);  // dequantize_row, q8.rs:76-91
+    if (has_scale) v = mul_sat(v, scale);   // model.rs:316-330 (gemma)
+    out[(size_t)t * cols + i] = v;
+  }
+}
+
+cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32_t tokens,
+                         int has_scale, int32_t scale, int32_t* out, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, d_ids, scale, has_scale, out);
+  return cudaGetLastError();
+}
+
+__global__ void fill_u64_kernel(unsigned long long* p, uint32_t n) {
+  uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) p[i] = 0;
+}
+cudaError_t launch_fill_u64(unsigned long long* p, uint32_t n, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  fill_u64_kernel<<<(n + 255) / 256, 256, 0, s>>>(p, n);
+  return cudaGetLastError();
+}
+
+__global__ void decode_finish_kernel(unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
+                                     uint32_t* d_step, uint32_t* history, uint32_t cap) {
+  uint32_t tok = best_key_token(*best);  // first maximum (generation.rs:25-58)
+  *d_token = tok;
+  *best = 0;
+  uint32_t step = *d_step;
+  if (history && step < cap) history[step] = tok;
+  *d_step = step + 1;
+  *d_pos = *d_pos + 1;
+}
+cudaError_t launch_decode_finish(const unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
+                                 uint32_t* d_step, uint32_t* history, uint32_t history_cap,
+                                 cudaStream_t s) {
+  decode_finish_kernel<<<1, 1, 0, s>>>((unsigned long long*)best, d_token, d_pos, d_step, history,
+                                       history_cap);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Gemma rows
+// ---------------------------------------------------------------------------
+
+__device__ uint64_t block_sumsq(const int32_t* v, uint32_t n, uint64_t* red) {
+  uint64_t ss = 0;
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v[i] * v[i]));
+  ss = warp_sum_sat_nonneg(ss);
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  uint64_t t = 0;
+  for (uint32_t w = 0; w < (blockDim.x + 31) / 32; ++w) t = add_sat_nonneg(t, red[w]);
+  return t;  // every thread
+}
+
+// In-place rms_norm (weighted when w != NULL) of an n-value row in shared memory.
+__device__ void block_rms_norm(int32_t* v, uint32_t n, const int32_t* w, int64_t eps, uint64_t* red) {
+  int32_t scale = rms_scale_from_sumsq(block_sumsq(v, n, red), n, eps);
+  __syncthreads();
+  for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+    int32_t y = mul_sat(v[i], scale);
+    v[i] = w ? mul_sat(y, w[i]) : y;
+  }
+  __syncthreads();
+}
+
+__global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
+  extern __shared__ __align__(16) int32_t hv[];  // [d]
+  __shared__ uint64_t red[32];
+  const uint32_t tok = blockIdx.x, which = blockIdx.y, d = a.d;
+  const uint32_t qd = a.heads * d, kvd = a.kv_heads * d;
+  const uint32_t pos = (a.pos_ptr ? *a.pos_ptr : a.pos0) + tok;
+  const int32_t* src = a.qkv + (size_t)tok * (qd + 2 * kvd) + (size_t)which * d;
+  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) hv[i] = src[i];
+  __syncthreads();
+  bool is_q = which < a.heads, is_k = !is_q && which < a.heads + a.kv_heads;
+  if (is_q || is_k) {
+    block_rms_norm(hv, d, is_q ? a.q_norm : a.k_norm, a.eps, red);  // prefill_range.rs:617-624
+    uint32_t half = a.rotary_dim / 2;
+    if (half && pos) {  // apply_rope, prefill_range.rs:631-647
+      for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
+        int32_t l = hv[i], r = hv[i + half];
+        rotate_half_pair(&l, &r, a.inv_freq[i], pos);
+        hv[i] = l;
+        hv[i + half] = r;
+      }
+      __syncthreads();
+    }
+  } else {
+    block_rms_norm(hv, d, nullptr, a.eps, red);  // value_rms_norm, prefill_range.rs:625-627
+  }
+  int32_t* dst;
+  if (is_q) dst = a.q_out + (size_t)tok * qd + (size_t)which * d;
+  else if (is_k) dst = a.kcache ? a.kcache + (size_t)pos * kvd + (size_t)(which - a.heads) * d : nullptr;
+  else dst = a.vcache ? a.vcache + (size_t)pos * kvd + (size_t)(which - a.heads - a.kv_heads) * d : nullptr;
+  if (dst)
+    for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) dst[i] = hv[i];
+}
+
+cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  dim3 grid(tokens, a.heads + 2 * a.kv_heads);
+  gemma_qkv_finish_kernel<<<grid, 128, a.d * 4, s>>>(a);
+  return cudaGetLastError();
+}
+
+__global__ void gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
+                                       const int32_t* w_pre_ffw, int64_t eps, uint32_t H,
+                                       uint8_t* planes) {
+  extern __shared__ __align__(16) int32_t row[];  // [H]
+  __shared__ uint64_t red[32];
+  const uint32_t t = blockIdx.x;
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) row[i] = o[(size_t)t * H + i];
+  __syncthreads();
+  block_rms_norm(row, H, w_post_attn, eps, red);
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+    int32_t v = add_sat(row[i], x[(size_t)t * H + i]);
+    row[i] = v;
+    x[(size_t)t * H + i] = v;
+  }
+  __syncthreads();
+  block_rms_norm(row, H, w_pre_ffw, eps, red);
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) put_planes(planes + (size_t)t * 4 * H, H, i, row[i]);
+}
+
+cudaError_t launch_gemma_post_attn(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
+                                   const int32_t* w_pre_ffw, int64_t eps, uint32_t tokens,
+                                   uint32_t hidden, uint8_t* planes, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  gemma_post_attn_kernel<<<tokens, 256, hidden * 4, s>>>(o, x, w_post_attn, w_pre_ffw, eps, hidden, planes);
+  return cudaGetLastError();
+}
+
+__global__ void gemma_norm_add_kernel(const int32_t* v_in, const int32_t* add, const int32_t* w,
+                                      int64_t eps, int32_t scalar, uint32_t H, int32_t* out) {
+  extern __shared__ __align__(16) int32_t row[];
+  __shared__ uint64_t red[32];
+  const uint32_t t = blockIdx.x;
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) row[i] = v_in[(size_t)t * H + i];
+  __syncthreads();
+  block_rms_norm(row, H, w, eps, red);
+  for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+    int32_t v = add_sat(row[i], add[(size_t)t * H + i]);
+    if (scalar != 0) v = mul_sat(v, scalar);  // scale_row (finish_layer, :953-955)
+    out[(size_t)t * H + i] = v;
+  }
+}
+
+cudaError_t launch_gemma_post_ffw(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw,
+                                  int64_t eps, uint32_t tokens, uint32_t hidden, int32_t* xs,
+                                  cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  gemma_norm_add_kernel<<<tokens, 256, hidden * 4, s>>>(ff, x, w_post_ffw, eps, 0, hidden, xs);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const int32_t* w_ple_post,
+                                int64_t eps, int32_t layer_scalar, uint32_t tokens, uint32_t hidden,
+                                int32_t* x_out, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  gemma_norm_add_kernel<<<tokens, 256, hidden * 4, s>>>(proj, xs, w_ple_post, eps, layer_scalar, hidden, x_out);
+  return cudaGetLastError();
+}
+
+// Warp per (token, row) dense product.
+__global__ void dense_kernel(const int32_t* __restrict__ w, uint32_t rows, uint32_t cols,
+                             const int32_t* __restrict__ in, uint32_t in_stride, uint32_t tokens,
+                             int32_t* out, uint32_t out_stride, const int32_t* gate, uint32_t gate_stride) {
+  const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows * tokens) return;
+  const uint32_t t = warp / rows, r = warp % rows;
+  const int32_t* x = in + (size_t)t * in_stride;
+  const int32_t* wr = w + (size_t)r * cols;
+  int64_t acc = 0;
+  for (uint32_t i = lane; i < cols; i += 32)
+    acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)x[i] * wr[i]));
+  acc = warp_sum_i64(acc);
+  if (lane == 0) {
+    int32_t v = requantize(acc);
+    if (gate) v = mul_sat(gelu_tanh(v), gate[(size_t)t * gate_stride + r]);  // ple_gate_mul :931-944
+    out[(size_t)t * out_stride + r] = v;
+  }
+}
+
+cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const int32_t* in,
+                         uint32_t in_stride, uint32_t tokens, int32_t* out, uint32_t out_stride,
+                         const int32_t* gelu_gate, uint32_t gate_stride, cudaStream_t s) {
+  uint64_t warps = (uint64_t)rows * tokens;
+  if (warps == 0) return cudaSuccess;
+  dense_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(w, rows, cols, in, in_stride, tokens, out,
+                                                           out_stride, gelu_gate, gate_stride);
+  return cudaGetLastError();
+}
+
+__global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, const uint16_t* es,
+                                   uint32_t ecols, const uint32_t* ids, const int32_t* ple_norm,
+                                   int64_t eps, int32_t projection_scalar, int32_t embedding_scale,
+                                   int32_t input_scale, uint32_t L, uint32_t P, int32_t* out) {
+  extern __shared__ __align__(16) int32_t row[];  // [P]
+  __shared__ uint64_t red[32];
+  const uint32_t t = blockIdx.x, l = blockIdx.y, id = ids[t];
+  for (uint32_t j = threadIdx.x; j < P; j += blockDim.x)
+    row[j] = mul_sat(projected[((size_t)t * L + l) * P + j], projection_scalar);
+  __syncthreads();
+  block_rms_norm(row, P, ple_norm, eps, red);
+  for (uint32_t j = threadIdx.x; j < P; j += blockDim.x) {
+    uint32_t col = l * P + j;
+    int32_t m, e;
+    q8_scale_parts(es[(size_t)id * (ecols / 32) + (col >> 5)], &m, &e);
+    int32_t v = mul_sat(q8_dequant(eq[(size_t)id * ecols + col], m, e), embedding_scale);
+    v = add_sat(v, row[j]);
+    out[((size_t)t * L + l) * P + j] = mul_sat(v, input_scale);
+  }
+}
+
+cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_embed,
+                               const uint32_t* d_ids, const int32_t* ple_norm, int64_t eps,
+                               int32_t projection_scalar, int32_t embedding_scale,
+                               int32_t input_scale, uint32_t tokens, uint32_t layers, uint32_t P,
+                               int32_t* out, cudaStream_t s) {
+  if (tokens == 0) return cudaSuccess;
+  dim3 grid(tokens, layers);
+  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->cols, d_ids,
+                                              ple_norm, eps, projection_scalar, embedding_scale,
+                                              input_scale, layers, P, out);
+  return cudaGetLastError();
+}
+
+}  // namespace iris

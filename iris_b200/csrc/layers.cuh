@@ -1,0 +1,103 @@
+// Row-level kernels of the two layer families: attention, embeddings, norms,
+// Gemma's q/k/v finishing and per-layer inputs, the head's selection.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q8.cuh"
+
+namespace iris {
+
+enum ScoreMode { SCORE_MISTRAL = 0, SCORE_GEMMA = 1 };
+
+// Attention over a linear K/V cache ([positions][kv_dim] int32 per layer).
+struct AttnArgs {
+  const int32_t* q;       // [tokens][heads*d]
+  const int32_t* kcache;  // [positions][kvd]
+  const int32_t* vcache;
+  uint32_t heads, kv_heads, d, kvd;
+  const uint32_t* pos_ptr;  // position of token 0 (decode), or NULL
+  uint32_t pos0;
+  uint32_t window;          // 0 = full causal attention
+  int mode;                 // ScoreMode
+  uint32_t scale_q32;       // mistral score scale
+  uint8_t* ctx_planes;      // [tokens][4][heads*d]
+  int32_t* ctx;             // [tokens][heads*d] or NULL
+  // decode split scratch
+  int32_t* scores;                 // [heads][cap]
+  int64_t* terms;                  // [heads][cap]
+  unsigned long long* chunk_best;  // [heads][nchunks]
+  uint64_t* chunk_sum;             // [heads][nchunks]
+  int32_t* chunk_wsum;             // [heads][nchunks]
+  int64_t* partial;                // [nchunks][heads][d]
+  unsigned int* counters;          // [kv_heads], zero between launches
+  uint32_t cap, chunk, nchunks;
+};
+
+// Decode (one query): three launches split over kv groups x position chunks.
+cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s);
+// Many queries at positions pos0.. (prefill, chain ranges): one block a
+// (query, head). max_visible bounds the shared memory.
+cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_t max_visible,
+                                     cudaStream_t s);
+
+// Embedding rows: out[t] = dequantize_row(embed[ids[t]]), then mul_sat by
+// scale when has_scale (Gemma, direct/src/model.rs:316-330).
+cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32_t tokens,
+                         int has_scale, int32_t scale, int32_t* out, cudaStream_t s);
+// Sets the shared-memory limits of every kernel instantiation (call once per
+// device before any launch or stream capture).
+cudaError_t prepare_layer_kernels();
+cudaError_t prepare_product_kernels();
+
+// Resets first-maximum keys.
+cudaError_t launch_fill_u64(unsigned long long* p, uint32_t n, cudaStream_t s);
+// Decode bookkeeping after the head: token = argmax, pos += 1, history.
+cudaError_t launch_decode_finish(const unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
+                                 uint32_t* d_step, uint32_t* history, uint32_t history_cap,
+                                 cudaStream_t s);
+
+// Gemma: per-head RMSNorm (q_norm/k_norm, weightless for v), rotate-half RoPE,
+// q to q_out, k and v to the cache (when kcache is not NULL).
+struct QkvFinishArgs {
+  const int32_t* qkv;  // [tokens][qd + 2 kvd]
+  int32_t* q_out;      // [tokens][qd]
+  int32_t* kcache;
+  int32_t* vcache;
+  const int32_t* q_norm;
+  const int32_t* k_norm;
+  const int64_t* inv_freq;  // [rotary_dim/2]
+  uint32_t heads, kv_heads, d, rotary_dim;
+  int64_t eps;
+  const uint32_t* pos_ptr;
+  uint32_t pos0;
+};
+cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cudaStream_t s);
+
+// Gemma residual steps (prefill_range.rs:879-957), one block a token:
+//   post_attn: x = add_sat(rms_norm(o, w_post_attn), x); planes = rms_norm(x, w_pre_ffw)
+//   post_ffw:  xs = add_sat(rms_norm(ff, w_post_ffw), x)
+//   finish:    x = [layer_scalar *] add_sat(rms_norm(proj, w_ple_post), xs)
+cudaError_t launch_gemma_post_attn(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
+                                   const int32_t* w_pre_ffw, int64_t eps, uint32_t tokens,
+                                   uint32_t hidden, uint8_t* planes, cudaStream_t s);
+cudaError_t launch_gemma_post_ffw(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw,
+                                  int64_t eps, uint32_t tokens, uint32_t hidden, int32_t* xs,
+                                  cudaStream_t s);
+cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const int32_t* w_ple_post,
+                                int64_t eps, int32_t layer_scalar, uint32_t tokens, uint32_t hidden,
+                                int32_t* x_out, cudaStream_t s);
+// Dense Q16.16 products: out[t][r] = dot_bits(in[t], w[r]) (tensor.rs:522-528),
+// optionally gated: out = mul_sat(gelu(dot), gate_rows[t][r]).
+cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const int32_t* in,
+                         uint32_t in_stride, uint32_t tokens, int32_t* out, uint32_t out_stride,
+                         const int32_t* gelu_gate, uint32_t gate_stride, cudaStream_t s);
+// Gemma per-layer inputs (view_kernels.rs:59-99) for every layer at once,
+// given projected = dot_bits rows of the model projection: out[t][l][P].
+cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_embed,
+                               const uint32_t* d_ids, const int32_t* ple_norm, int64_t eps,
+                               int32_t projection_scalar, int32_t embedding_scale,
+                               int32_t input_scale, uint32_t tokens, uint32_t layers, uint32_t P,
+                               int32_t* out, cudaStream_t s);
+
+}  // namespace iris

@@ -1,0 +1,1029 @@
+// Device-resident models, decoding sessions and the chain-stage entry point.
+//
+// A session holds the K/V cache of every layer as int32 rows
+// [layers][positions][kv_heads * head_dim] in HBM; a pass runs the layers
+// over a range of rows (the prompt in ranges of up to kMaxRows, or one decode
+// token) and the head over its last row. Ranges are processed position-major:
+// range r goes through every layer before range r+1; since every value of a
+// row depends only on its own row and the K/V of earlier positions, this
+// gives the same values as the reference's layer-major order
+// (crates/inference/direct/src/executor.rs:293-401; the reference's own
+// executor test checks the same invariance across chunkings).
+//
+// A decode pass is captured once into a CUDA graph that reads the token id
+// and the position from device memory, so the decode loop replays it with no
+// host round trip: the head's first maximum becomes the next input token on
+// the device (generation.rs:25-58).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../../include/iris_b200.h"
+#include "layers.cuh"
+#include "synth.cuh"
+
+using namespace iris;
+
+namespace {
+
+constexpr uint32_t kMaxRows = 256;  // rows a prefill range holds on the device
+constexpr int kFamilyMistral = 0, kFamilyGemma = 1;
+
+struct LayerDev {
+  Q8GpuMatrix *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+  int32_t *norm_attn = nullptr, *norm_ffn = nullptr;
+  // gemma-dense
+  int32_t *norm_post_attn = nullptr, *norm_post_ffw = nullptr, *q_norm = nullptr, *k_norm = nullptr,
+          *ple_post_norm = nullptr, *ple_gate = nullptr, *ple_proj = nullptr;
+  int64_t* inv_freq = nullptr;
+  uint32_t window = 0, rotary_dim = 0, freq_base_dim = 0;
+  int64_t rope_base = 0;
+  int32_t kv_donor = -1, layer_scalar = 0;
+};
+
+// ---- host restatement of the rotary frequency ladder (ops.rs:558-720) ------
+typedef __int128 i128;
+int64_t clamp64(i128 v) {
+  return v < (i128)INT64_MIN ? INT64_MIN : (v > (i128)INT64_MAX ? INT64_MAX : (int64_t)v);
+}
+i128 div_even(i128 n, i128 d) {  // round_ties_even_division
+  i128 q = n / d, r = n % d;
+  if (r == 0) return q;
+  i128 twice = (r < 0 ? -r : r) * 2, ad = d < 0 ? -d : d, step = ((n < 0) != (d < 0)) ? -1 : 1;
+  if (twice < ad) return q;
+  if (twice > ad) return q + step;
+  return (q & 1) == 0 ? q : q + step;
+}
+int64_t h_acc_mul(int64_t a, int64_t b) { return clamp64(div_even((i128)a * b, (i128)1 << 32)); }
+int64_t h_pow(int64_t b, uint32_t e) {
+  int64_t r = (int64_t)1 << 32;
+  for (uint32_t i = 0; i < e; ++i) r = h_acc_mul(r, b);
+  return r;
+}
+int64_t h_nth_root(int64_t value, uint32_t degree) {  // nth_root_acc, ops.rs:564-606
+  const int64_t one = (int64_t)1 << 32;
+  if (degree == 1 || value == one) return value;
+  int64_t lo = 0, hi = std::max(value, one);
+  while (lo < hi) {
+    int64_t mid = lo + (hi - lo + 1) / 2;
+    if (h_pow(mid, degree) <= value) lo = mid;
+    else hi = mid - 1;
+  }
+  int64_t up = lo == INT64_MAX ? lo : lo + 1;
+  i128 le = (i128)value - h_pow(lo, degree), ue = (i128)h_pow(up, degree) - value;
+  if (le < 0) le = -le;
+  if (ue < 0) ue = -ue;
+  if (ue < le) return up;
+  if (le < ue) return lo;
+  return (lo & 1) == 0 ? lo : up;
+}
+// inv_frequency_i for i < half: the reference's chained acc_mul (ops.rs:178-198).
+std::vector<int64_t> rope_inverse_frequencies(int64_t base, uint32_t freq_base_dim, uint32_t half) {
+  int64_t step = clamp64(div_even((i128)((int64_t)1 << 32) << 32, h_nth_root(base, freq_base_dim / 2)));
+  std::vector<int64_t> f(half);
+  int64_t inv = (int64_t)1 << 32;
+  for (uint32_t i = 0; i < half; ++i) {
+    f[i] = inv;
+    inv = h_acc_mul(inv, step);
+  }
+  return f;
+}
+
+template <class T>
+cudaError_t dalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) return cudaSuccess;
+  return cudaMalloc((void**)p, count * sizeof(T));
+}
+
+}  // namespace
+
+struct IrisModel {
+  int family = 0;
+  uint32_t L = 0, H = 0, F = 0, heads = 0, kvh = 0, d = 0, V = 0, P = 0, max_positions = 0;
+  uint32_t qd = 0, kvd = 0;
+  int64_t eps = 0;
+  uint32_t scale_q32 = 0;
+  bool tied = false;
+  int32_t embedding_scale = 0, ple_embedding_scale = 0, ple_projection_scalar = 0, ple_input_scale = 0,
+          softcap = 0;
+  Q8GpuMatrix *embed = nullptr, *head = nullptr, *ple_embed = nullptr;
+  int32_t *final_norm = nullptr, *ple_model_proj = nullptr, *ple_norm = nullptr;
+  int64_t* freqs = nullptr;  // mistral [d/2]
+  std::vector<LayerDev> layers;
+  uint64_t weight_bytes = 0;
+  IrisSession* scratch = nullptr;  // for the chain-stage entry point
+};
+
+struct IrisSession {
+  IrisModel* m = nullptr;
+  uint32_t cap = 0, len = 0;
+  bool has_logits = false;  // a pass has run since the last reset
+  int32_t *kc = nullptr, *vc = nullptr;
+  int32_t *x = nullptr, *tmp = nullptr, *q = nullptr, *qkv = nullptr, *xs = nullptr, *pg = nullptr,
+          *ple_rows = nullptr, *ple_proj = nullptr, *logits = nullptr;
+  uint8_t *planes = nullptr, *planes2 = nullptr;
+  unsigned long long* best = nullptr;
+  uint32_t *d_ids = nullptr, *d_pos = nullptr, *d_token = nullptr, *d_step = nullptr, *d_history = nullptr;
+  uint32_t history_cap = 0;
+  // decode attention scratch
+  int32_t* scores = nullptr;
+  int64_t* terms = nullptr;
+  unsigned long long* chunk_best = nullptr;
+  uint64_t* chunk_sum = nullptr;
+  int32_t* chunk_wsum = nullptr;
+  int64_t* partial = nullptr;
+  unsigned int* counters = nullptr;
+  uint32_t chunk = 0, nchunks = 0;
+  cudaStream_t stream = nullptr;
+  cudaGraphExec_t graph = nullptr;
+};
+
+namespace {
+
+size_t kv_offset(const IrisSession* s, uint32_t l) { return (size_t)l * s->cap * s->m->kvd; }
+
+void free_session(IrisSession* s) {
+  if (!s) return;
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
+                  s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
+                  s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->chunk_wsum,
+                  s->partial, s->counters};
+  for (void* p : ptrs) cudaFree(p);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
+  *out = nullptr;
+  if (cap == 0) return IRIS_EINVAL;
+  IrisSession* s = new IrisSession();
+  s->m = m;
+  s->cap = cap;
+  const uint32_t R = kMaxRows;
+  size_t wide = std::max({m->H, m->qd, m->F, m->P ? m->P : 1u});
+  cudaError_t e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  size_t kv = (size_t)m->L * cap * m->kvd;
+  if (e == cudaSuccess) e = dalloc(&s->kc, kv);
+  if (e == cudaSuccess) e = dalloc(&s->vc, kv);
+  if (e == cudaSuccess) e = dalloc(&s->x, (size_t)R * m->H);
+  if (e == cudaSuccess) e = dalloc(&s->tmp, (size_t)R * m->H);
+  if (e == cudaSuccess) e = dalloc(&s->q, (size_t)R * m->qd);
+  if (e == cudaSuccess) e = dalloc(&s->planes, (size_t)R * 4 * wide);
+  if (e == cudaSuccess) e = dalloc(&s->planes2, (size_t)R * 4 * wide);
+  if (e == cudaSuccess) e = dalloc(&s->logits, (size_t)m->V);
+  if (e == cudaSuccess) e = dalloc(&s->best, R);
+  if (e == cudaSuccess) e = dalloc(&s->d_ids, R);
+  if (e == cudaSuccess) e = dalloc(&s->d_pos, 1);
+  if (e == cudaSuccess) e = dalloc(&s->d_token, 1);
+  if (e == cudaSuccess) e = dalloc(&s->d_step, 1);
+  if (m->family == kFamilyGemma) {
+    if (e == cudaSuccess) e = dalloc(&s->qkv, (size_t)R * (m->qd + 2 * m->kvd));
+    if (e == cudaSuccess) e = dalloc(&s->xs, (size_t)R * m->H);
+    if (e == cudaSuccess) e = dalloc(&s->pg, (size_t)R * m->P);
+    if (e == cudaSuccess) e = dalloc(&s->ple_rows, (size_t)R * m->L * m->P);
+    if (e == cudaSuccess) e = dalloc(&s->ple_proj, (size_t)R * m->L * m->P);
+  }
+  s->chunk = m->kvh >= 4 ? 128 : 32;
+  s->nchunks = (cap + s->chunk - 1) / s->chunk;
+  if (e == cudaSuccess) e = dalloc(&s->scores, (size_t)m->heads * cap);
+  if (e == cudaSuccess) e = dalloc(&s->terms, (size_t)m->heads * cap);
+  if (e == cudaSuccess) e = dalloc(&s->chunk_best, (size_t)m->heads * s->nchunks);
+  if (e == cudaSuccess) e = dalloc(&s->chunk_sum, (size_t)m->heads * s->nchunks);
+  if (e == cudaSuccess) e = dalloc(&s->chunk_wsum, (size_t)m->heads * s->nchunks);
+  if (e == cudaSuccess) e = dalloc(&s->partial, (size_t)s->nchunks * m->heads * m->d);
+  if (e == cudaSuccess) e = dalloc(&s->counters, m->kvh);
+  if (e == cudaSuccess) e = cudaMemset(s->counters, 0, m->kvh * sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(s->best, 0, R * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(s->d_pos, 0, 4);
+  if (e == cudaSuccess) e = cudaMemset(s->d_step, 0, 4);
+  if (e != cudaSuccess) {
+    free_session(s);
+    return (int)e;
+  }
+  *out = s;
+  return 0;
+}
+
+AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t pos0) {
+  IrisModel* m = s->m;
+  const LayerDev& L = m->layers[l];
+  uint32_t src = (m->family == kFamilyGemma && L.kv_donor >= 0) ? (uint32_t)L.kv_donor : l;
+  AttnArgs a{};
+  a.q = s->q;
+  a.kcache = s->kc + kv_offset(s, src);
+  a.vcache = s->vc + kv_offset(s, src);
+  a.heads = m->heads;
+  a.kv_heads = m->kvh;
+  a.d = m->d;
+  a.kvd = m->kvd;
+  a.pos_ptr = pos_ptr;
+  a.pos0 = pos0;
+  a.window = m->family == kFamilyGemma ? L.window : 0;
+  a.mode = m->family == kFamilyGemma ? SCORE_GEMMA : SCORE_MISTRAL;
+  a.scale_q32 = m->scale_q32;
+  a.ctx_planes = s->planes;
+  a.scores = s->scores;
+  a.terms = s->terms;
+  a.chunk_best = s->chunk_best;
+  a.chunk_sum = s->chunk_sum;
+  a.chunk_wsum = s->chunk_wsum;
+  a.partial = s->partial;
+  a.counters = s->counters;
+  a.cap = s->cap;
+  a.chunk = s->chunk;
+  a.nchunks = s->nchunks;
+  return a;
+}
+
+ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
+  ProductArgs a{};
+  a.q = w->q;
+  a.s = w->s;
+  a.rows = w->rows;
+  a.cols = w->cols;
+  a.tokens = tokens;
+  return a;
+}
+
+// One mistral-dense layer (mistral/layer.rs:107-270) over `tokens` rows in
+// s->x at positions pos0.. (or *pos_ptr for the decode pass).
+cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint32_t* pos_ptr,
+                          uint32_t pos0) {
+  IrisModel* m = s->m;
+  const LayerDev& L = m->layers[l];
+  cudaStream_t st = s->stream;
+  cudaError_t e = cudaSuccess;
+  bool one = tokens == 1;
+  // n = rms_norm(x); q, k, v = W n; rope(q), rope(k); k, v to the cache
+  ProductArgs a = product_args(L.qkv, tokens);
+  a.out = s->q;
+  a.out_stride = m->qd;
+  a.freqs = m->freqs;
+  a.head_dim = m->d;
+  a.qd = m->qd;
+  a.kvd = m->kvd;
+  a.kcache = s->kc + kv_offset(s, l);
+  a.vcache = s->vc + kv_offset(s, l);
+  a.pos_ptr = pos_ptr;
+  a.pos0 = pos0;
+  if (one) {
+    a.x = s->x;
+    a.norm_w = L.norm_attn;
+    a.eps = m->eps;
+    e = launch_product(a, IN_NORM, EPI_QKV_ROPE, st);
+  } else {
+    e = launch_planes(s->x, L.norm_attn, m->eps, tokens, m->H, s->planes, st);
+    a.planes = s->planes;
+    if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_QKV_ROPE, st);
+  }
+  if (e != cudaSuccess) return e;
+  // attention over positions 0..=p, context as planes
+  AttnArgs at = attn_args(s, l, pos_ptr, pos0);
+  e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, pos0 + tokens, st);
+  if (e != cudaSuccess) return e;
+  // x = x + W_o ctx
+  ProductArgs o = product_args(L.o, tokens);
+  o.planes = s->planes;
+  o.out = s->x;
+  o.resid = s->x;
+  e = launch_product(o, IN_PLANES, EPI_RESID, st);
+  if (e != cudaSuccess) return e;
+  // g = silu(W_gate m) * (W_up m), m = rms_norm(x)
+  ProductArgs g = product_args(L.gu, tokens);
+  g.out_planes = s->planes2;
+  if (one) {
+    g.x = s->x;
+    g.norm_w = L.norm_ffn;
+    g.eps = m->eps;
+    e = launch_product(g, IN_NORM, EPI_SILU_MUL, st);
+  } else {
+    e = launch_planes(s->x, L.norm_ffn, m->eps, tokens, m->H, s->planes, st);
+    g.planes = s->planes;
+    if (e == cudaSuccess) e = launch_product(g, IN_PLANES, EPI_SILU_MUL, st);
+  }
+  if (e != cudaSuccess) return e;
+  // x = x + W_down g
+  ProductArgs dn = product_args(L.down, tokens);
+  dn.planes = s->planes2;
+  dn.out = s->x;
+  dn.resid = s->x;
+  return launch_product(dn, IN_PLANES, EPI_RESID, st);
+}
+
+// One gemma-dense layer (prefill_range.rs:307-333, 497-741, 879-957).
+cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint32_t* pos_ptr,
+                        uint32_t pos0) {
+  IrisModel* m = s->m;
+  const LayerDev& L = m->layers[l];
+  cudaStream_t st = s->stream;
+  cudaError_t e;
+  bool one = tokens == 1;
+  ProductArgs a = product_args(L.qkv, tokens);
+  a.out = s->qkv;
+  if (one) {
+    a.x = s->x;
+    a.norm_w = L.norm_attn;
+    a.eps = m->eps;
+    e = launch_product(a, IN_NORM, EPI_STORE, st);
+  } else {
+    e = launch_planes(s->x, L.norm_attn, m->eps, tokens, m->H, s->planes, st);
+    a.planes = s->planes;
+    if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, st);
+  }
+  if (e != cudaSuccess) return e;
+  QkvFinishArgs f{};
+  f.qkv = s->qkv;
+  f.q_out = s->q;
+  bool own = L.kv_donor < 0;  // a sharing layer attends over its donor's cache
+  f.kcache = own ? s->kc + kv_offset(s, l) : nullptr;
+  f.vcache = own ? s->vc + kv_offset(s, l) : nullptr;
+  f.q_norm = L.q_norm;
+  f.k_norm = L.k_norm;
+  f.inv_freq = L.inv_freq;
+  f.heads = m->heads;
+  f.kv_heads = m->kvh;
+  f.d = m->d;
+  f.rotary_dim = L.rotary_dim;
+  f.eps = m->eps;
+  f.pos_ptr = pos_ptr;
+  f.pos0 = pos0;
+  e = launch_gemma_qkv_finish(f, tokens, st);
+  if (e != cudaSuccess) return e;
+  AttnArgs at = attn_args(s, l, pos_ptr, pos0);
+  uint32_t max_vis = L.window ? std::min(L.window, pos0 + tokens) : pos0 + tokens;
+  e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, max_vis, st);
+  if (e != cudaSuccess) return e;
+  ProductArgs o = product_args(L.o, tokens);
+  o.planes = s->planes;
+  o.out = s->tmp;
+  e = launch_product(o, IN_PLANES, EPI_STORE, st);
+  if (e == cudaSuccess)
+    e = launch_gemma_post_attn(s->tmp, s->x, L.norm_post_attn, L.norm_ffn, m->eps, tokens, m->H, s->planes, st);
+  if (e != cudaSuccess) return e;
+  ProductArgs g = product_args(L.gu, tokens);
+  g.planes = s->planes;
+  g.out_planes = s->planes2;
+  e = launch_product(g, IN_PLANES, EPI_GELU_MUL, st);
+  if (e != cudaSuccess) return e;
+  ProductArgs dn = product_args(L.down, tokens);
+  dn.planes = s->planes2;
+  dn.out = s->tmp;
+  e = launch_product(dn, IN_PLANES, EPI_STORE, st);
+  if (e == cudaSuccess) e = launch_gemma_post_ffw(s->tmp, s->x, L.norm_post_ffw, m->eps, tokens, m->H, s->xs, st);
+  if (e == cudaSuccess)
+    e = launch_dense(L.ple_gate, m->P, m->H, s->xs, m->H, tokens, s->pg, m->P,
+                     s->ple_rows + (size_t)l * m->P, m->L * m->P, st);
+  if (e == cudaSuccess) e = launch_dense(L.ple_proj, m->H, m->P, s->pg, m->P, tokens, s->tmp, m->H, nullptr, 0, st);
+  if (e == cudaSuccess)
+    e = launch_gemma_finish(s->tmp, s->xs, L.ple_post_norm, m->eps, L.layer_scalar, tokens, m->H, s->x, st);
+  return e;
+}
+
+// Embeds the ids in s->d_ids (or *d_token) into s->x, prepares Gemma's
+// per-layer inputs, runs every layer and the head over the last row.
+cudaError_t run_pass(IrisSession* s, uint32_t tokens, const uint32_t* ids_dev, const uint32_t* pos_ptr,
+                     uint32_t pos0, bool head, bool store_logits) {
+  IrisModel* m = s->m;
+  cudaStream_t st = s->stream;
+  bool gemma = m->family == kFamilyGemma;
+  cudaError_t e = launch_embed(m->embed, ids_dev, tokens, gemma, m->embedding_scale, s->x, st);
+  if (e != cudaSuccess) return e;
+  if (gemma) {  // view_kernels.rs:59-99, every layer's PLE row for these tokens
+    e = launch_dense(m->ple_model_proj, m->L * m->P, m->H, s->x, m->H, tokens, s->ple_proj, m->L * m->P,
+                     nullptr, 0, st);
+    if (e == cudaSuccess)
+      e = launch_ple_prepare(s->ple_proj, m->ple_embed, ids_dev, m->ple_norm, m->eps, m->ple_projection_scalar,
+                             m->ple_embedding_scale, m->ple_input_scale, tokens, m->L, m->P, s->ple_rows, st);
+    if (e != cudaSuccess) return e;
+  }
+  for (uint32_t l = 0; l < m->L; ++l) {
+    e = gemma ? gemma_layer(s, l, tokens, pos_ptr, pos0) : mistral_layer(s, l, tokens, pos_ptr, pos0);
+    if (e != cudaSuccess) return e;
+  }
+  if (!head) return cudaSuccess;
+  // head: rms_norm(final) -> dot_row over the vocabulary -> softcap -> first max
+  ProductArgs h = product_args(m->head, 1);
+  h.x = s->x + (size_t)(tokens - 1) * m->H;
+  h.norm_w = m->final_norm;
+  h.eps = m->eps;
+  h.out = store_logits ? s->logits : nullptr;
+  h.best = s->best;
+  h.softcap = m->softcap;
+  return launch_product(h, IN_NORM, EPI_LOGITS, st, IRIS_PATH_GEMV);
+}
+
+int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits, uint32_t* token) {
+  IrisModel* m = s->m;
+  if (n == 0) return IRIS_EINVAL;
+  if ((uint64_t)s->len + n > s->cap || (uint64_t)s->len + n > m->max_positions) return IRIS_ERANGE;
+  for (uint32_t i = 0; i < n; ++i)
+    if (ids[i] >= m->V) return IRIS_EINVAL;
+  cudaError_t e = cudaSuccess;
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->d_ids, ids + r0, cnt * 4, cudaMemcpyHostToDevice, s->stream);
+    bool last = r0 + cnt == n;
+    if (e == cudaSuccess) e = run_pass(s, cnt, s->d_ids, nullptr, s->len + r0, last, logits != nullptr);
+  }
+  unsigned long long key = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&key, s->best, 8, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && logits) e = cudaMemcpyAsync(logits, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess) e = launch_fill_u64(s->best, 1, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return (int)e;
+  s->len += n;
+  s->has_logits = true;
+  uint32_t tok = best_key_token(key);
+  if (token) *token = tok;
+  // device state for the decode graph: next input token and its position
+  uint32_t state[2] = {tok, s->len};
+  e = cudaMemcpy(s->d_token, &state[0], 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(s->d_pos, &state[1], 4, cudaMemcpyHostToDevice);
+  return (int)e;
+}
+
+int ensure_graph(IrisSession* s) {
+  if (s->graph) return 0;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return (int)e;
+  cudaError_t body = run_pass(s, 1, s->d_token, s->d_pos, 0, true, true);
+  if (body == cudaSuccess)
+    body = launch_decode_finish(s->best, s->d_token, s->d_pos, s->d_step, s->d_history, s->history_cap, s->stream);
+  e = cudaStreamEndCapture(s->stream, &g);
+  if (body != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return (int)body;
+  }
+  if (e != cudaSuccess) return (int)e;
+  e = cudaGraphInstantiate(&s->graph, g, 0);
+  cudaGraphDestroy(g);
+  return (int)e;
+}
+
+// Replays the decode graph `steps` times (positions len, len+1, ...).
+int decode_steps(IrisSession* s, uint32_t steps) {
+  if (!s->has_logits) return IRIS_ESTATE;
+  if ((uint64_t)s->len + steps > s->cap || (uint64_t)s->len + steps > s->m->max_positions) return IRIS_ERANGE;
+  int rc = ensure_graph(s);
+  if (rc) return rc;
+  for (uint32_t i = 0; i < steps; ++i) {
+    cudaError_t e = cudaGraphLaunch(s->graph, s->stream);
+    if (e != cudaSuccess) return (int)e;
+  }
+  s->len += steps;
+  return 0;
+}
+
+int check_model_ready(const IrisModel* m) {
+  if (!m->embed || !m->head || !m->final_norm) return IRIS_ESTATE;
+  for (const LayerDev& L : m->layers)
+    if (!L.qkv || !L.o || !L.gu || !L.down || !L.norm_attn || !L.norm_ffn) return IRIS_ESTATE;
+  return 0;
+}
+
+// Model tensor plumbing ------------------------------------------------------
+
+struct Q8Target {
+  Q8GpuMatrix* m;
+  uint32_t rows, cols, stride, offset;
+};
+
+int q8_target(IrisModel* m, int tensor, int32_t layer, Q8Target* t) {
+  if (tensor == IRIS_T_EMBED) { *t = {m->embed, m->V, m->H, 1, 0}; return 0; }
+  if (tensor == IRIS_T_HEAD) {
+    if (m->tied) return IRIS_EINVAL;
+    *t = {m->head, m->V, m->H, 1, 0};
+    return 0;
+  }
+  if (tensor == IRIS_T_PLE_EMBED) {
+    if (m->family != kFamilyGemma) return IRIS_EINVAL;
+    *t = {m->ple_embed, m->V, m->L * m->P, 1, 0};
+    return 0;
+  }
+  if (layer < 0 || (uint32_t)layer >= m->L) return IRIS_EINVAL;
+  LayerDev& L = m->layers[layer];
+  switch (tensor) {
+    case IRIS_T_W_Q: *t = {L.qkv, m->qd, m->H, 1, 0}; return 0;
+    case IRIS_T_W_K: *t = {L.qkv, m->kvd, m->H, 1, m->qd}; return 0;
+    case IRIS_T_W_V: *t = {L.qkv, m->kvd, m->H, 1, m->qd + m->kvd}; return 0;
+    case IRIS_T_W_O: *t = {L.o, m->H, m->qd, 1, 0}; return 0;
+    case IRIS_T_W_GATE: *t = {L.gu, m->F, m->H, 2, 0}; return 0;
+    case IRIS_T_W_UP: *t = {L.gu, m->F, m->H, 2, 1}; return 0;
+    case IRIS_T_W_DOWN: *t = {L.down, m->H, m->F, 1, 0}; return 0;
+  }
+  return IRIS_EINVAL;
+}
+
+int32_t** value_target(IrisModel* m, int tensor, int32_t layer, uint64_t* count, uint32_t* fan_in) {
+  *fan_in = 0;
+  if (tensor == IRIS_T_FINAL_NORM) { *count = m->H; return &m->final_norm; }
+  if (tensor == IRIS_T_PLE_MODEL_PROJECTION && m->family == kFamilyGemma) {
+    *count = (uint64_t)m->L * m->P * m->H;
+    *fan_in = m->H;
+    return &m->ple_model_proj;
+  }
+  if (tensor == IRIS_T_PLE_NORM && m->family == kFamilyGemma) { *count = m->P; return &m->ple_norm; }
+  if (layer < 0 || (uint32_t)layer >= m->L) return nullptr;
+  LayerDev& L = m->layers[layer];
+  bool g = m->family == kFamilyGemma;
+  switch (tensor) {
+    case IRIS_T_NORM_ATTN: *count = m->H; return &L.norm_attn;
+    case IRIS_T_NORM_FFN: *count = m->H; return &L.norm_ffn;
+  }
+  if (!g) return nullptr;
+  switch (tensor) {
+    case IRIS_T_NORM_POST_ATTN: *count = m->H; return &L.norm_post_attn;
+    case IRIS_T_NORM_POST_FFW: *count = m->H; return &L.norm_post_ffw;
+    case IRIS_T_Q_NORM: *count = m->d; return &L.q_norm;
+    case IRIS_T_K_NORM: *count = m->d; return &L.k_norm;
+    case IRIS_T_PLE_POST_NORM: *count = m->H; return &L.ple_post_norm;
+    case IRIS_T_PLE_INPUT_GATE: *count = (uint64_t)m->P * m->H; *fan_in = m->H; return &L.ple_gate;
+    case IRIS_T_PLE_LAYER_PROJECTION: *count = (uint64_t)m->H * m->P; *fan_in = m->P; return &L.ple_proj;
+  }
+  return nullptr;
+}
+
+int alloc_layers(IrisModel* m) {
+  cudaError_t e = cudaSuccess;
+  auto q8 = [&](uint32_t rows, uint32_t cols) -> Q8GpuMatrix* {
+    if (e != cudaSuccess) return nullptr;
+    Q8GpuMatrix* r = alloc_q8(rows, cols, &e);
+    if (r) m->weight_bytes += (uint64_t)rows * cols + (uint64_t)rows * (cols / 32) * 2;
+    return r;
+  };
+  m->embed = q8(m->V, m->H);
+  m->head = m->tied ? m->embed : q8(m->V, m->H);
+  if (e == cudaSuccess) e = dalloc(&m->final_norm, m->H);
+  for (uint32_t l = 0; l < m->L; ++l) {
+    LayerDev& L = m->layers[l];
+    L.qkv = q8(m->qd + 2 * m->kvd, m->H);
+    L.o = q8(m->H, m->qd);
+    L.gu = q8(2 * m->F, m->H);
+    L.down = q8(m->H, m->F);
+    if (e == cudaSuccess) e = dalloc(&L.norm_attn, m->H);
+    if (e == cudaSuccess) e = dalloc(&L.norm_ffn, m->H);
+    if (m->family == kFamilyGemma) {
+      if (e == cudaSuccess) e = dalloc(&L.norm_post_attn, m->H);
+      if (e == cudaSuccess) e = dalloc(&L.norm_post_ffw, m->H);
+      if (e == cudaSuccess) e = dalloc(&L.q_norm, m->d);
+      if (e == cudaSuccess) e = dalloc(&L.k_norm, m->d);
+      if (e == cudaSuccess) e = dalloc(&L.ple_post_norm, m->H);
+      if (e == cudaSuccess) e = dalloc(&L.ple_gate, (size_t)m->P * m->H);
+      if (e == cudaSuccess) e = dalloc(&L.ple_proj, (size_t)m->H * m->P);
+      m->weight_bytes += (uint64_t)2 * m->P * m->H * 4;
+    }
+  }
+  if (m->family == kFamilyGemma) {
+    m->ple_embed = q8(m->V, m->L * m->P);
+    if (e == cudaSuccess) e = dalloc(&m->ple_model_proj, (size_t)m->L * m->P * m->H);
+    if (e == cudaSuccess) e = dalloc(&m->ple_norm, m->P);
+    m->weight_bytes += (uint64_t)m->L * m->P * m->H * 4;
+  }
+  if (e == cudaSuccess) e = prepare_product_kernels();
+  if (e == cudaSuccess) e = prepare_layer_kernels();
+  return (int)e;
+}
+
+}  // namespace
+
+extern "C" {
+
+void iris_model_free(IrisModel* m) {
+  if (!m) return;
+  free_session(m->scratch);
+  if (m->head != m->embed) free_q8(m->head);
+  free_q8(m->embed);
+  free_q8(m->ple_embed);
+  cudaFree(m->final_norm);
+  cudaFree(m->ple_model_proj);
+  cudaFree(m->ple_norm);
+  cudaFree(m->freqs);
+  for (LayerDev& L : m->layers) {
+    free_q8(L.qkv);
+    free_q8(L.o);
+    free_q8(L.gu);
+    free_q8(L.down);
+    void* ptrs[] = {L.norm_attn, L.norm_ffn, L.norm_post_attn, L.norm_post_ffw, L.q_norm, L.k_norm,
+                    L.ple_post_norm, L.ple_gate, L.ple_proj, L.inv_freq};
+    for (void* p : ptrs) cudaFree(p);
+  }
+  delete m;
+}
+
+int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
+  *out = nullptr;
+  if (!sh || !sh->layers || !sh->hidden || !sh->ffn || !sh->heads || !sh->kv_heads || !sh->head_dim ||
+      !sh->vocab || sh->heads % sh->kv_heads || sh->head_dim % 4 || sh->hidden % 32 || sh->ffn % 32 ||
+      (sh->heads * sh->head_dim) % 32 || sh->norm_eps < 0 || !sh->rope_inverse_frequencies ||
+      sh->heads / sh->kv_heads > 16)
+    return IRIS_EINVAL;
+  for (uint32_t i = 0; i < sh->head_dim / 2; ++i)  // layer.rs:71-78
+    if (sh->rope_inverse_frequencies[i] < 0 || sh->rope_inverse_frequencies[i] > ((int64_t)1 << 32))
+      return IRIS_EINVAL;
+  IrisModel* m = new IrisModel();
+  m->family = kFamilyMistral;
+  m->L = sh->layers;
+  m->H = sh->hidden;
+  m->F = sh->ffn;
+  m->heads = sh->heads;
+  m->kvh = sh->kv_heads;
+  m->d = sh->head_dim;
+  m->V = sh->vocab;
+  m->max_positions = sh->max_positions;
+  m->qd = m->heads * m->d;
+  m->kvd = m->kvh * m->d;
+  m->eps = sh->norm_eps;
+  m->scale_q32 = sh->attention_scale_q32;
+  m->tied = sh->tied_head != 0;
+  m->layers.resize(m->L);
+  int rc = alloc_layers(m);
+  if (rc == 0) rc = (int)dalloc(&m->freqs, m->d / 2);
+  if (rc == 0)
+    rc = (int)cudaMemcpy(m->freqs, sh->rope_inverse_frequencies, (m->d / 2) * 8, cudaMemcpyHostToDevice);
+  if (rc) {
+    iris_model_free(m);
+    return rc;
+  }
+  *out = m;
+  return 0;
+}
+
+int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
+  *out = nullptr;
+  if (!sh || !sh->layers || !sh->hidden || !sh->ffn || !sh->heads || !sh->kv_heads || !sh->head_dim ||
+      !sh->vocab || !sh->ple_width || sh->heads % sh->kv_heads || sh->head_dim % 4 || sh->hidden % 32 ||
+      sh->ffn % 32 || (sh->heads * sh->head_dim) % 32 || sh->ple_width % 32 || sh->norm_eps < 0 ||
+      sh->heads / sh->kv_heads > 16 || !sh->sliding_window || !sh->rope_base || !sh->rotary_dim ||
+      !sh->rope_freq_base_dim || !sh->kv_donor_layer || !sh->layer_scalar)
+    return IRIS_EINVAL;
+  for (uint32_t l = 0; l < sh->layers; ++l) {  // prefill_range.rs:403-484
+    uint32_t rd = sh->rotary_dim[l], fbd = sh->rope_freq_base_dim[l];
+    if (rd % 2 || rd > sh->head_dim) return IRIS_EINVAL;
+    if (rd && (fbd < 2 || fbd % 2 || sh->rope_base[l] <= 0)) return IRIS_EINVAL;
+    int32_t donor = sh->kv_donor_layer[l];
+    if (donor >= (int32_t)l || donor < -1) return IRIS_EINVAL;
+    if (donor >= 0 && sh->kv_donor_layer[donor] >= 0) return IRIS_EINVAL;
+  }
+  IrisModel* m = new IrisModel();
+  m->family = kFamilyGemma;
+  m->L = sh->layers;
+  m->H = sh->hidden;
+  m->F = sh->ffn;
+  m->heads = sh->heads;
+  m->kvh = sh->kv_heads;
+  m->d = sh->head_dim;
+  m->V = sh->vocab;
+  m->P = sh->ple_width;
+  m->max_positions = UINT32_MAX;
+  m->qd = m->heads * m->d;
+  m->kvd = m->kvh * m->d;
+  m->eps = sh->norm_eps;
+  m->tied = true;  // direct/src/model.rs:577-597 (the Gemma configs tie the head)
+  m->embedding_scale = sh->embedding_scale;
+  m->ple_embedding_scale = sh->ple_embedding_scale;
+  m->ple_projection_scalar = sh->ple_projection_scalar;
+  m->ple_input_scale = sh->ple_input_scale;
+  m->softcap = sh->final_logit_softcap;
+  m->layers.resize(m->L);
+  int rc = alloc_layers(m);
+  for (uint32_t l = 0; l < m->L && rc == 0; ++l) {
+    LayerDev& L = m->layers[l];
+    L.window = sh->sliding_window[l];
+    L.rotary_dim = sh->rotary_dim[l];
+    L.freq_base_dim = sh->rope_freq_base_dim[l];
+    L.rope_base = sh->rope_base[l];
+    L.kv_donor = sh->kv_donor_layer[l];
+    L.layer_scalar = sh->layer_scalar[l];
+    uint32_t half = L.rotary_dim / 2;
+    if (half) {
+      std::vector<int64_t> f = rope_inverse_frequencies(L.rope_base, L.freq_base_dim, half);
+      rc = (int)dalloc(&L.inv_freq, half);
+      if (rc == 0) rc = (int)cudaMemcpy(L.inv_freq, f.data(), half * 8, cudaMemcpyHostToDevice);
+    }
+  }
+  if (rc) {
+    iris_model_free(m);
+    return rc;
+  }
+  *out = m;
+  return 0;
+}
+
+int iris_model_set_q8(IrisModel* m, int tensor, int32_t layer, const uint8_t* blocks, uint64_t bytes) {
+  if (!m || !blocks) return IRIS_EINVAL;
+  Q8Target t;
+  int rc = q8_target(m, tensor, layer, &t);
+  if (rc) return rc;
+  if (bytes != (uint64_t)t.rows * (t.cols / 32) * 34) return IRIS_EINVAL;
+  int bad = 0;
+  cudaError_t e = upload_q8_blocks(t.m, blocks, t.rows, t.cols, t.stride, t.offset, &bad);
+  if (e != cudaSuccess) return (int)e;
+  return bad ? IRIS_ESCALE : 0;
+}
+
+int iris_model_get_q8(const IrisModel* mc, int tensor, int32_t layer, uint8_t* blocks, uint64_t bytes) {
+  IrisModel* m = const_cast<IrisModel*>(mc);
+  if (!m || !blocks) return IRIS_EINVAL;
+  Q8Target t;
+  int rc = q8_target(m, tensor, layer, &t);
+  if (tensor == IRIS_T_HEAD && m->tied) {
+    t = {m->head, m->V, m->H, 1, 0};
+    rc = 0;
+  }
+  if (rc) return rc;
+  if (bytes != (uint64_t)t.rows * (t.cols / 32) * 34) return IRIS_EINVAL;
+  return (int)download_q8_blocks(t.m, blocks, t.rows, t.cols, t.stride, t.offset);
+}
+
+int iris_model_set_values(IrisModel* m, int tensor, int32_t layer, const int32_t* values, uint64_t count) {
+  if (!m || !values) return IRIS_EINVAL;
+  uint64_t want;
+  uint32_t fan;
+  int32_t** dst = value_target(m, tensor, layer, &want, &fan);
+  if (!dst || count != want) return IRIS_EINVAL;
+  return (int)cudaMemcpy(*dst, values, count * 4, cudaMemcpyHostToDevice);
+}
+
+int iris_model_get_values(const IrisModel* mc, int tensor, int32_t layer, int32_t* values, uint64_t count) {
+  IrisModel* m = const_cast<IrisModel*>(mc);
+  if (!m || !values) return IRIS_EINVAL;
+  uint64_t want;
+  uint32_t fan;
+  int32_t** src = value_target(m, tensor, layer, &want, &fan);
+  if (!src || count != want) return IRIS_EINVAL;
+  return (int)cudaMemcpy(values, *src, count * 4, cudaMemcpyDeviceToHost);
+}
+
+int iris_model_synthesize(IrisModel* m, uint64_t seed, int per_block) {
+  if (!m) return IRIS_EINVAL;
+  cudaError_t e = cudaSuccess;
+  auto q8 = [&](int tensor, int32_t layer) {
+    Q8Target t;
+    if (e != cudaSuccess || q8_target(m, tensor, layer, &t)) return;
+    e = synth_q8_rows(t.m, seed, (uint32_t)tensor, layer, t.rows, t.cols, t.stride, t.offset, per_block, 0);
+  };
+  auto vals = [&](int tensor, int32_t layer) {
+    uint64_t count;
+    uint32_t fan;
+    int32_t** dst = value_target(m, tensor, layer, &count, &fan);
+    if (e != cudaSuccess || !dst) return;
+    e = synth_values_dev(*dst, seed, (uint32_t)tensor, layer, count, fan, 0);
+  };
+  q8(IRIS_T_EMBED, -1);
+  if (!m->tied) q8(IRIS_T_HEAD, -1);
+  vals(IRIS_T_FINAL_NORM, -1);
+  if (m->family == kFamilyGemma) {
+    q8(IRIS_T_PLE_EMBED, -1);
+    vals(IRIS_T_PLE_MODEL_PROJECTION, -1);
+    vals(IRIS_T_PLE_NORM, -1);
+  }
+  for (uint32_t l = 0; l < m->L; ++l) {
+    for (int t : {IRIS_T_W_Q, IRIS_T_W_K, IRIS_T_W_V, IRIS_T_W_O, IRIS_T_W_GATE, IRIS_T_W_UP, IRIS_T_W_DOWN})
+      q8(t, (int32_t)l);
+    for (int t : {IRIS_T_NORM_ATTN, IRIS_T_NORM_FFN, IRIS_T_NORM_POST_ATTN, IRIS_T_NORM_POST_FFW, IRIS_T_Q_NORM,
+                  IRIS_T_K_NORM, IRIS_T_PLE_POST_NORM, IRIS_T_PLE_INPUT_GATE, IRIS_T_PLE_LAYER_PROJECTION})
+      vals(t, (int32_t)l);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return (int)e;
+}
+
+uint64_t iris_model_weight_bytes(const IrisModel* m) { return m ? m->weight_bytes : 0; }
+
+int iris_session_create(IrisModel* m, uint32_t max_positions, IrisSession** out) {
+  if (!m || !out) return IRIS_EINVAL;
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  return create_session(m, max_positions, out);
+}
+
+int iris_session_reset(IrisSession* s) {
+  if (!s) return IRIS_EINVAL;
+  s->len = 0;
+  s->has_logits = false;
+  cudaError_t e = cudaMemsetAsync(s->d_pos, 0, 4, s->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->d_step, 0, 4, s->stream);
+  if (e == cudaSuccess) e = launch_fill_u64(s->best, kMaxRows, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  return (int)e;
+}
+
+int iris_session_prefill(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits, uint32_t* token) {
+  if (!s || !ids) return IRIS_EINVAL;
+  return prefill_ids(s, ids, n, logits, token);
+}
+
+int iris_session_decode(IrisSession* s, uint32_t token_in, int32_t* logits, uint32_t* token_out) {
+  if (!s) return IRIS_EINVAL;
+  if (token_in >= s->m->V) return IRIS_EINVAL;
+  if (!s->has_logits) return IRIS_ESTATE;
+  cudaError_t e = cudaMemcpyAsync(s->d_token, &token_in, 4, cudaMemcpyHostToDevice, s->stream);
+  if (e != cudaSuccess) return (int)e;
+  int rc = decode_steps(s, 1);
+  if (rc) return rc;
+  uint32_t tok = 0;
+  e = cudaMemcpyAsync(&tok, s->d_token, 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpyAsync(logits, s->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e == cudaSuccess && token_out) *token_out = tok;
+  return (int)e;
+}
+
+int iris_generate(IrisSession* s, const uint32_t* prompt, uint32_t n_prompt, uint32_t max_tokens,
+                  const uint32_t* eos, uint32_t n_eos, uint32_t* out_tokens, uint32_t* out_count,
+                  int32_t* out_logits) {
+  if (!s || !prompt || !out_tokens || !out_count) return IRIS_EINVAL;
+  *out_count = 0;
+  if (max_tokens == 0) return 0;
+  int rc = iris_session_reset(s);
+  if (rc) return rc;
+  const uint32_t V = s->m->V;
+  uint32_t tok = 0;
+  rc = prefill_ids(s, prompt, n_prompt, out_logits, &tok);
+  if (rc) return rc;
+  auto is_eos = [&](uint32_t t) {
+    for (uint32_t i = 0; i < n_eos; ++i)
+      if (eos[i] == t) return true;
+    return false;
+  };
+  uint32_t count = 0;
+  out_tokens[count++] = tok;  // executor.rs:157-171
+  if (is_eos(tok) || count == max_tokens) {
+    *out_count = count;
+    return 0;
+  }
+  if (out_logits) {  // one pass at a time, every pass's logits copied out
+    while (true) {
+      rc = iris_session_decode(s, tok, out_logits + (size_t)count * V, &tok);
+      if (rc) return rc;
+      out_tokens[count++] = tok;
+      if (is_eos(tok) || count == max_tokens) break;
+    }
+    *out_count = count;
+    return 0;
+  }
+  // Batches of graph replays, the token staying on the device; the history
+  // buffer records each pass's selection.
+  const uint32_t batch = 16;
+  if (s->history_cap < batch) {
+    cudaFree(s->d_history);
+    s->d_history = nullptr;
+    if (s->graph) {
+      cudaGraphExecDestroy(s->graph);
+      s->graph = nullptr;
+    }
+    cudaError_t e = dalloc(&s->d_history, batch);
+    if (e != cudaSuccess) return (int)e;
+    s->history_cap = batch;
+  }
+  std::vector<uint32_t> hist(batch);
+  while (count < max_tokens) {
+    uint32_t n = std::min(batch, max_tokens - count);
+    cudaError_t e = cudaMemsetAsync(s->d_step, 0, 4, s->stream);
+    if (e != cudaSuccess) return (int)e;
+    uint32_t len0 = s->len;
+    rc = decode_steps(s, n);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(hist.data(), s->d_history, n * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return (int)e;
+    for (uint32_t i = 0; i < n; ++i) {
+      out_tokens[count++] = hist[i];
+      if (is_eos(hist[i]) || count == max_tokens) {
+        // passes after this one were not the reference's: forget them
+        s->len = len0 + i + 1;
+        uint32_t state[2] = {hist[i], s->len};
+        e = cudaMemcpy(s->d_token, &state[0], 4, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(s->d_pos, &state[1], 4, cudaMemcpyHostToDevice);
+        *out_count = count;
+        return (int)e;
+      }
+    }
+  }
+  *out_count = count;
+  return 0;
+}
+
+uint32_t iris_session_length(const IrisSession* s) { return s ? s->len : 0; }
+
+int iris_session_decode_steps(IrisSession* s, uint32_t steps) {
+  if (!s) return IRIS_EINVAL;
+  return decode_steps(s, steps);
+}
+
+int iris_session_synchronize(IrisSession* s) {
+  if (!s) return IRIS_EINVAL;
+  return (int)cudaStreamSynchronize(s->stream);
+}
+
+void* iris_session_stream(IrisSession* s) { return s ? (void*)s->stream : nullptr; }
+
+uint32_t iris_session_graph_kernels(IrisSession* s) {
+  if (!s || ensure_graph(s)) return 0;
+  cudaGraph_t g = nullptr;
+  // Count kernel nodes by re-capturing the pass into a throwaway graph
+  // (capture records launches without running them).
+  if (cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return 0;
+  cudaError_t body = run_pass(s, 1, s->d_token, s->d_pos, 0, true, true);
+  if (body == cudaSuccess)
+    body = launch_decode_finish(s->best, s->d_token, s->d_pos, s->d_step, s->d_history, s->history_cap, s->stream);
+  if (cudaStreamEndCapture(s->stream, &g) != cudaSuccess || body != cudaSuccess || !g) return 0;
+  size_t n = 0;
+  cudaGraphGetNodes(g, nullptr, &n);
+  std::vector<cudaGraphNode_t> nodes(n);
+  cudaGraphGetNodes(g, nodes.data(), &n);
+  uint32_t kernels = 0;
+  for (cudaGraphNode_t nd : nodes) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++kernels;
+  }
+  cudaGraphDestroy(g);
+  return kernels;
+}
+
+int iris_session_product(IrisSession* s, uint32_t layer, int which) {
+  if (!s || layer >= s->m->L || which < 0 || which > 4) return IRIS_EINVAL;
+  IrisModel* m = s->m;
+  const LayerDev& L = m->layers[layer];
+  const Q8GpuMatrix* w = which == 0 ? L.qkv : which == 1 ? L.o : which == 2 ? L.gu : which == 3 ? L.down : m->head;
+  ProductArgs a = product_args(w, 1);
+  if (which == 1 || which == 3) {  // inputs from byte planes, as in the pass
+    a.planes = which == 1 ? s->planes : s->planes2;
+    a.out = s->tmp;
+    return (int)launch_product(a, IN_PLANES, EPI_STORE, s->stream);
+  }
+  a.x = s->x;
+  a.norm_w = which == 4 ? m->final_norm : L.norm_attn;
+  a.eps = m->eps;
+  if (which == 2) {
+    a.out_planes = s->planes;
+    return (int)launch_product(a, IN_NORM, m->family == kFamilyGemma ? EPI_GELU_MUL : EPI_SILU_MUL, s->stream);
+  }
+  if (which == 4) {
+    a.out = s->logits;
+    a.best = s->best + 1;  // not the decode pass's key
+    return (int)launch_product(a, IN_NORM, EPI_LOGITS, s->stream);
+  }
+  a.out = s->tmp;  // kMaxRows * hidden values >= one token's q|k|v rows
+  return (int)launch_product(a, IN_NORM, EPI_STORE, s->stream);
+}
+
+int iris_session_get_kv(const IrisSession* s, uint32_t layer, uint32_t first, uint32_t count, int32_t* k,
+                        int32_t* v) {
+  if (!s || layer >= s->m->L || (uint64_t)first + count > s->len) return IRIS_EINVAL;
+  size_t off = kv_offset(s, layer) + (size_t)first * s->m->kvd, n = (size_t)count * s->m->kvd * 4;
+  cudaError_t e = cudaSuccess;
+  if (k) e = cudaMemcpy(k, s->kc + off, n, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v) e = cudaMemcpy(v, s->vc + off, n, cudaMemcpyDeviceToHost);
+  return (int)e;
+}
+
+void iris_session_free(IrisSession* s) { free_session(s); }
+
+int iris_mistral_layer_range(IrisModel* m, uint32_t layer, const int32_t* rows_in, uint32_t n, uint32_t start,
+                             const int32_t* prior_k, const int32_t* prior_v, int32_t* rows_out, int32_t* own_k,
+                             int32_t* own_v) {
+  if (!m || m->family != kFamilyMistral || layer >= m->L || !rows_in || !rows_out) return IRIS_EINVAL;
+  if (n == 0) return 0;  // layer.rs:117-119: a range with no rows produces nothing
+  if ((uint64_t)start + n > m->max_positions) return IRIS_ERANGE;  // layer.rs:121-127
+  if (start && (!prior_k || !prior_v)) return IRIS_EINVAL;
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  if (!m->scratch || m->scratch->cap < start + n) {
+    free_session(m->scratch);
+    m->scratch = nullptr;
+    rc = create_session(m, std::max<uint32_t>(start + n, 512), &m->scratch);
+    if (rc) return rc;
+  }
+  IrisSession* s = m->scratch;
+  size_t kvd = m->kvd, H = m->H;
+  int32_t* kc = s->kc + kv_offset(s, layer);
+  int32_t* vc = s->vc + kv_offset(s, layer);
+  cudaError_t e = cudaSuccess;
+  if (start) {
+    e = cudaMemcpyAsync(kc, prior_k, (size_t)start * kvd * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(vc, prior_v, (size_t)start * kvd * 4, cudaMemcpyHostToDevice, s->stream);
+  }
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->x, rows_in + (size_t)r0 * H, (size_t)cnt * H * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = mistral_layer(s, layer, cnt, nullptr, start + r0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rows_out + (size_t)r0 * H, s->x, (size_t)cnt * H * 4, cudaMemcpyDeviceToHost, s->stream);
+  }
+  if (e == cudaSuccess && own_k)
+    e = cudaMemcpyAsync(own_k, kc + (size_t)start * kvd, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && own_v)
+    e = cudaMemcpyAsync(own_v, vc + (size_t)start * kvd, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  return (int)e;
+}
+
+}  // extern "C"

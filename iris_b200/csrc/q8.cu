@@ -1,0 +1,761 @@
+// Exact Q8_0 x Q16.16 products on B200 (sm_100a).
+//
+// Every output equals det_num::q8::dot_row (crates/det-num/src/q8.rs:56-72):
+// exact block sums, each times its Q.24 block scale, summed in 128 bits,
+// rounded once to Q16.16 with ties to even and saturated. Here a block sum is
+// formed from four byte planes with dp4a (common.cuh), multiplied by the
+// scale's 11-bit mantissa (exact in int64) and added, shifted by the scale's
+// exponent, into a 128-bit accumulator. Integer addition is associative, so
+// the order in which lanes, warps or blocks combine partial sums never
+// changes a value.
+//
+// Two kernels:
+//  - q8_gemv_kernel: one token (the decode step). Each warp owns R rows and
+//    streams them with 128-bit non-allocating loads; activations sit in
+//    shared memory as byte planes, built either from planes in global memory
+//    or, fused, from the int32 row and its RMSNorm (ops.rs:98-114).
+//  - q8_gemm_kernel: many tokens (prefill, the chain's ranges), a 64-row x
+//    32-token tile per block staged through shared memory.
+// Both end in a fused epilogue (residual add, RoPE and K/V store, SiLU/GELU
+// gating, logits with a first-maximum key).
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/iris_b200.h"
+#include "q8.cuh"
+#include "synth.cuh"
+
+namespace iris {
+
+// ---------------------------------------------------------------------------
+// Upload / download / synthesis
+// ---------------------------------------------------------------------------
+
+__global__ void repack_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t rows, uint32_t cols,
+                                     uint32_t row_stride, uint32_t row_offset, int8_t* q,
+                                     uint16_t* s, int* bad) {
+  uint32_t nb = cols / 32;
+  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= (uint64_t)rows * nb) return;
+  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  const uint8_t* src = raw + b * 34;
+  uint16_t bits = (uint16_t)(src[0] | (src[1] << 8));
+  if (((bits >> 10) & 0x1f) == 0x1f) atomicExch(bad, 1);
+  uint64_t dr = (uint64_t)r * row_stride + row_offset;
+  s[dr * nb + blk] = bits;
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) |
+           ((uint32_t)src[4 + 4 * i] << 16) | ((uint32_t)src[5 + 4 * i] << 24);
+  uint4* dst = (uint4*)(q + dr * cols + (uint64_t)blk * 32);
+  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__global__ void unpack_blocks_kernel(const int8_t* q, const uint16_t* s, uint32_t rows, uint32_t cols,
+                                     uint32_t row_stride, uint32_t row_offset, uint8_t* raw) {
+  uint32_t nb = cols / 32;
+  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= (uint64_t)rows * nb) return;
+  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  uint64_t dr = (uint64_t)r * row_stride + row_offset;
+  uint16_t bits = s[dr * nb + blk];
+  uint8_t* dst = raw + b * 34;
+  dst[0] = (uint8_t)bits;
+  dst[1] = (uint8_t)(bits >> 8);
+  const int8_t* src = q + dr * cols + (uint64_t)blk * 32;
+  for (int i = 0; i < 32; ++i) dst[2 + i] = (uint8_t)src[i];
+}
+
+__global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint64_t seed, uint32_t tensor,
+                                int32_t layer, uint32_t rows, uint32_t cols, uint32_t row_stride,
+                                uint32_t row_offset, int per_block) {
+  uint32_t nb = cols / 32;
+  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= (uint64_t)rows * nb) return;
+  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  uint64_t dr = (uint64_t)r * row_stride + row_offset;
+  s[dr * nb + blk] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v |= (uint32_t)(uint8_t)synth_q(seed, tensor, layer, r, blk * 32 + i * 4 + j, cols) << (8 * j);
+    w[i] = v;
+  }
+  uint4* dst = (uint4*)(q + dr * cols + (uint64_t)blk * 32);
+  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__global__ void synth_values_kernel(int32_t* dst, uint64_t seed, uint32_t tensor, int32_t layer,
+                                    uint64_t count, uint32_t fan_in) {
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) dst[i] = synth_value(seed, tensor, layer, i, fan_in);
+}
+
+Q8GpuMatrix* alloc_q8(uint32_t rows, uint32_t cols, cudaError_t* err) {
+  Q8GpuMatrix* m = (Q8GpuMatrix*)std::calloc(1, sizeof(Q8GpuMatrix));
+  if (!m) {
+    *err = cudaErrorMemoryAllocation;
+    return nullptr;
+  }
+  m->rows = rows;
+  m->cols = cols;
+  m->owns = true;
+  *err = cudaMalloc((void**)&m->q, (size_t)rows * cols);
+  if (*err == cudaSuccess) *err = cudaMalloc((void**)&m->s, (size_t)rows * (cols / 32) * 2);
+  if (*err != cudaSuccess) {
+    free_q8(m);
+    return nullptr;
+  }
+  return m;
+}
+
+void free_q8(Q8GpuMatrix* m) {
+  if (!m) return;
+  if (m->owns) {
+    cudaFree(m->q);
+    cudaFree(m->s);
+  }
+  std::free(m);
+}
+
+cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
+                             uint32_t cols, uint32_t row_stride, uint32_t row_offset,
+                             int* bad_scale) {
+  size_t bytes = (size_t)rows * (cols / 32) * 34;
+  uint8_t* staging = nullptr;
+  int* bad = nullptr;
+  cudaError_t e = cudaMalloc((void**)&staging, bytes);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&bad, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(bad, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    uint64_t nblk = (uint64_t)rows * (cols / 32);
+    repack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(staging, rows, cols, row_stride,
+                                                                  row_offset, dst->q, dst->s, bad);
+    e = cudaGetLastError();
+  }
+  int h_bad = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h_bad, bad, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(staging);
+  cudaFree(bad);
+  *bad_scale = h_bad;
+  return e;
+}
+
+cudaError_t download_q8_blocks(const Q8GpuMatrix* src, uint8_t* host_blocks, uint32_t rows,
+                               uint32_t cols, uint32_t row_stride, uint32_t row_offset) {
+  size_t bytes = (size_t)rows * (cols / 32) * 34;
+  uint8_t* staging = nullptr;
+  cudaError_t e = cudaMalloc((void**)&staging, bytes);
+  if (e == cudaSuccess) {
+    uint64_t nblk = (uint64_t)rows * (cols / 32);
+    unpack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(src->q, src->s, rows, cols,
+                                                                  row_stride, row_offset, staging);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(host_blocks, staging, bytes, cudaMemcpyDeviceToHost);
+  cudaFree(staging);
+  return e;
+}
+
+cudaError_t synth_q8_rows(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int32_t layer,
+                          uint32_t rows, uint32_t cols, uint32_t row_stride, uint32_t row_offset,
+                          int per_block, cudaStream_t stream) {
+  uint64_t nblk = (uint64_t)rows * (cols / 32);
+  synth_q8_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream>>>(
+      dst->q, dst->s, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
+  return cudaGetLastError();
+}
+
+cudaError_t synth_values_dev(int32_t* dst, uint64_t seed, uint32_t tensor, int32_t layer,
+                             uint64_t count, uint32_t fan_in, cudaStream_t stream) {
+  if (count == 0) return cudaSuccess;
+  synth_values_kernel<<<(unsigned)((count + 255) / 256), 256, 0, stream>>>(dst, seed, tensor, layer,
+                                                                           count, fan_in);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Byte planes
+// ---------------------------------------------------------------------------
+
+// Block-wide saturating sum of non-negative values (result valid in thread 0).
+__device__ uint64_t block_sum_sat(uint64_t v, uint64_t* red) {
+  v = warp_sum_sat_nonneg(v);
+  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  uint64_t t = 0;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0;
+    t = warp_sum_sat_nonneg(t);
+  }
+  return t;
+}
+
+// Builds the byte planes of one K-wide row into `planes` (shared or global),
+// RMS-normalising first when norm_w is given (ops.rs:98-114: two mul_sat per
+// value, by the inverse-RMS scale and then by the weight).
+__device__ void row_to_planes(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
+                              int64_t eps, uint32_t K, uint8_t* planes, uint64_t* red,
+                              int32_t* s_scale) {
+  int32_t scale = 0;
+  if (norm_w) {
+    uint64_t ss = 0;
+    for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+      int4 v = *(const int4*)(x + i);
+      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.x * v.x));
+      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.y * v.y));
+      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.z * v.z));
+      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.w * v.w));
+    }
+    uint64_t total = block_sum_sat(ss, red);
+    if (threadIdx.x == 0) *s_scale = rms_scale_from_sumsq(total, K, eps);
+    __syncthreads();
+    scale = *s_scale;
+  }
+  for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
+    int4 v = *(const int4*)(x + i);
+    if (norm_w) {
+      int4 w = *(const int4*)(norm_w + i);
+      v.x = mul_sat(mul_sat(v.x, scale), w.x);
+      v.y = mul_sat(mul_sat(v.y, scale), w.y);
+      v.z = mul_sat(mul_sat(v.z, scale), w.z);
+      v.w = mul_sat(mul_sat(v.w, scale), w.w);
+    }
+    put_planes4(planes, K, i, v);
+  }
+}
+
+__global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
+                              int64_t eps, uint32_t K, uint8_t* planes) {
+  __shared__ uint64_t red[32];
+  __shared__ int32_t s_scale;
+  uint32_t t = blockIdx.x;
+  row_to_planes(x + (size_t)t * K, norm_w, eps, K, planes + (size_t)t * 4 * K, red, &s_scale);
+}
+
+cudaError_t launch_planes(const int32_t* x, const int32_t* norm_w, int64_t eps, uint32_t tokens,
+                          uint32_t cols, uint8_t* planes, cudaStream_t stream) {
+  if (tokens == 0) return cudaSuccess;
+  planes_kernel<<<tokens, 256, 0, stream>>>(x, norm_w, eps, cols, planes);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue helpers shared by both kernels
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t token_position(const ProductArgs& a, uint32_t t) {
+  return (a.pos_ptr ? *a.pos_ptr : a.pos0) + t;
+}
+
+// A finished (even, odd) row pair of a paired epilogue for token t.
+template <int EPI>
+__device__ __forceinline__ void epi_pair(const ProductArgs& a, uint32_t t, uint32_t row, int32_t v0,
+                                         int32_t v1) {
+  if (EPI == EPI_QKV_ROPE) {
+    uint32_t pos = token_position(a, t);
+    if (row < a.qd) {
+      rotate_pair_q30(&v0, &v1, a.freqs[(row % a.head_dim) >> 1], pos);
+      int32_t* o = a.out + (size_t)t * a.out_stride + row;
+      o[0] = v0;
+      o[1] = v1;
+    } else if (row < a.qd + a.kvd) {
+      uint32_t c = row - a.qd;
+      rotate_pair_q30(&v0, &v1, a.freqs[(c % a.head_dim) >> 1], pos);
+      int32_t* o = a.kcache + (size_t)pos * a.kvd + c;
+      o[0] = v0;
+      o[1] = v1;
+    } else {
+      uint32_t c = row - a.qd - a.kvd;
+      int32_t* o = a.vcache + (size_t)pos * a.kvd + c;
+      o[0] = v0;
+      o[1] = v1;
+    }
+  } else {  // gated: v0 = gate_j, v1 = up_j
+    int32_t g = EPI == EPI_SILU_MUL ? silu(v0) : gelu_tanh(v0);
+    int32_t y = mul_sat(g, v1);
+    uint32_t F = a.rows >> 1;
+    put_planes(a.out_planes + (size_t)t * 4 * F, F, row >> 1, y);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uint32_t row, int32_t v) {
+  size_t o = (size_t)t * a.out_stride + row;
+  if (EPI == EPI_STORE) a.out[o] = v;
+  else if (EPI == EPI_RESID) a.out[o] = add_sat(v, a.resid[o]);
+  else if (EPI == EPI_LOGITS) {
+    if (a.softcap > 0) v = softcap_act(v, a.softcap);
+    if (a.out) a.out[o] = v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMV: one token, R rows a warp
+// ---------------------------------------------------------------------------
+
+constexpr int kGemvWarps = 4;
+constexpr int kGemvRows = 4;  // rows a warp (even: paired epilogues)
+
+template <int R, int IN, int EPI>
+__global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint64_t red[32];
+  __shared__ int32_t s_scale;
+  const uint32_t K = a.cols;
+  if (IN == IN_PLANES) {
+    const uint4* src = (const uint4*)a.planes;
+    for (uint32_t i = threadIdx.x; i < K / 4; i += blockDim.x) ((uint4*)smem)[i] = src[i];
+  } else {
+    row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, smem, red, &s_scale);
+  }
+  __syncthreads();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row0 = (blockIdx.x * kGemvWarps + warp) * R;
+  if (row0 >= a.rows) return;
+  const uint4* P0 = (const uint4*)smem;
+  const uint4* P1 = P0 + K / 16;
+  const uint4* P2 = P1 + K / 16;
+  const uint4* P3 = P2 + K / 16;
+  const uint32_t nchunk = K / 16, nblk = K / 32;
+  const int8_t* wrow = a.q + (size_t)row0 * K;
+  const uint16_t* srow = a.s + (size_t)row0 * nblk;
+  const uint32_t live = min((uint32_t)R, a.rows - row0);
+
+  Acc128 acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = Acc128{0, 0};
+
+#pragma unroll 2
+  for (uint32_t c = lane; c < nchunk; c += 32) {
+    uint4 w[R];
+    uint16_t sb[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if ((uint32_t)r < live) {
+        w[r] = ld_stream_v4(wrow + (size_t)r * K + (size_t)c * 16);
+        sb[r] = ld_stream_u16(srow + (size_t)r * nblk + (c >> 1));
+      } else {
+        w[r] = make_uint4(0, 0, 0, 0);
+        sb[r] = 0;
+      }
+    }
+    uint4 p0 = P0[c], p1 = P1[c], p2 = P2[c], p3 = P3[c];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      int64_t part = q8_partial16(w[r], p0, p1, p2, p3);
+      int32_t m, e;
+      q8_scale_parts(sb[r], &m, &e);  // finite: checked at upload
+      acc128_add_shifted(acc[r], part * m, e);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = warp_sum_acc128(acc[r]);
+
+  if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+#pragma unroll
+    for (int j = 0; j < R / 2; ++j)
+      if (lane == j && (uint32_t)(2 * j + 1) < live)
+        epi_pair<EPI>(a, 0, row0 + 2 * j, acc128_round_q24(acc[2 * j]), acc128_round_q24(acc[2 * j + 1]));
+  } else if (EPI == EPI_LOGITS) {
+    unsigned long long key = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if ((uint32_t)r < live) {
+        int32_t v = acc128_round_q24(acc[r]);
+        if (a.softcap > 0) v = softcap_act(v, a.softcap);
+        if (lane == r && a.out) a.out[row0 + r] = v;
+        unsigned long long k = best_key(v, row0 + r);
+        key = k > key ? k : key;
+      }
+    }
+    if (lane == 0) atomicMax(a.best, key);
+  } else {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (lane == r && (uint32_t)r < live) epi_single<EPI>(a, 0, row0 + r, acc128_round_q24(acc[r]));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Tiled GEMM: 64 rows x 32 tokens a block, 4 rows x 2 tokens a thread
+// ---------------------------------------------------------------------------
+
+constexpr int kTileN = 64, kTileM = 32, kWPitch = 48;
+
+template <int EPI>
+__global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
+  __shared__ __align__(16) uint8_t sw[kTileN * kWPitch];
+  __shared__ uint16_t ssc[kTileN];
+  __shared__ __align__(16) uint8_t sp[kTileM * 4 * 32];
+  const uint32_t K = a.cols, nblk = K / 32;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const uint32_t n0 = blockIdx.x * kTileN, m0 = blockIdx.y * kTileM;
+
+  Acc128 acc[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) acc[i][j] = Acc128{0, 0};
+
+  for (uint32_t kb = 0; kb < nblk; ++kb) {
+    if (tid < 128) {
+      int r = tid >> 1, h = tid & 1;
+      uint32_t row = n0 + r;
+      uint4 v = row < a.rows ? ld_stream_v4(a.q + (size_t)row * K + kb * 32 + h * 16)
+                             : make_uint4(0, 0, 0, 0);
+      *(uint4*)(sw + r * kWPitch + h * 16) = v;
+    } else if (tid < 128 + kTileN) {
+      int r = tid - 128;
+      uint32_t row = n0 + r;
+      ssc[r] = row < a.rows ? a.s[(size_t)row * nblk + kb] : (uint16_t)0;
+    }
+    {
+      int t = tid >> 3, p = (tid >> 1) & 3, h = tid & 1;
+      uint32_t tok = m0 + t;
+      uint4 v = tok < a.tokens
+                    ? *(const uint4*)(a.planes + (size_t)tok * 4 * K + (size_t)p * K + kb * 32 + h * 16)
+                    : make_uint4(0, 0, 0, 0);
+      *(uint4*)(sp + (t * 4 + p) * 32 + h * 16) = v;
+    }
+    __syncthreads();
+    int32_t m[4], e[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (!q8_scale_parts(ssc[tx + 16 * i], &m[i], &e[i])) { m[i] = 0; e[i] = 0; }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = *(const uint4*)(sw + (tx + 16 * i) * kWPitch + h * 16);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint8_t* pb = sp + (ty * 2 + j) * 128 + h * 16;
+        uint4 p0 = *(const uint4*)(pb), p1 = *(const uint4*)(pb + 32), p2 = *(const uint4*)(pb + 64),
+              p3 = *(const uint4*)(pb + 96);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc128_add_shifted(acc[i][j], q8_partial16(w[i], p0, p1, p2, p3) * m[i], e[i]);
+      }
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    uint32_t tok = m0 + ty * 2 + j;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t row = n0 + tx + 16 * i;
+      int32_t v = acc128_round_q24(acc[i][j]);
+      if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+        int32_t partner = __shfl_xor_sync(0xffffffffu, v, 1);
+        if ((tx & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
+      } else if (EPI == EPI_LOGITS) {
+        if (tok < a.tokens && row < a.rows) {
+          if (a.softcap > 0) v = softcap_act(v, a.softcap);
+          if (a.out) a.out[(size_t)tok * a.out_stride + row] = v;
+          atomicMax(a.best + tok, best_key(v, row));
+        }
+      } else if (tok < a.tokens && row < a.rows) {
+        epi_single<EPI>(a, tok, row, v);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+
+constexpr size_t kGemvMaxSmem = 200 * 1024;  // activations up to 51200 wide
+
+template <int IN, int EPI>
+cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
+  auto kern = q8_gemv_kernel<kGemvRows, IN, EPI>;
+  size_t smem = (size_t)a.cols * 4;
+  if (smem > kGemvMaxSmem) return cudaErrorInvalidValue;
+  unsigned rows_per_block = kGemvWarps * kGemvRows;
+  unsigned grid = (a.rows + rows_per_block - 1) / rows_per_block;
+  kern<<<grid, kGemvWarps * 32, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <int IN>
+cudaError_t prepare_gemv_in() {
+  const void* kerns[] = {
+      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_STORE>, (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_RESID>,
+      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_QKV_ROPE>,
+      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_SILU_MUL>,
+      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_GELU_MUL>,
+      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_LOGITS>};
+  for (const void* k : kerns) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t prepare_product_kernels() {
+  cudaError_t e = prepare_gemv_in<IN_PLANES>();
+  if (e == cudaSuccess) e = prepare_gemv_in<IN_NORM>();
+  if (e == cudaSuccess) e = prepare_gemv_in<IN_RAW>();
+  return e;
+}
+
+template <int EPI>
+cudaError_t launch_gemm(const ProductArgs& a, cudaStream_t stream) {
+  dim3 grid((a.rows + kTileN - 1) / kTileN, (a.tokens + kTileM - 1) / kTileM);
+  q8_gemm_kernel<EPI><<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <int IN>
+cudaError_t dispatch_gemv(const ProductArgs& a, EpiMode epi, cudaStream_t s) {
+  switch (epi) {
+    case EPI_STORE: return launch_gemv<IN, EPI_STORE>(a, s);
+    case EPI_RESID: return launch_gemv<IN, EPI_RESID>(a, s);
+    case EPI_QKV_ROPE: return launch_gemv<IN, EPI_QKV_ROPE>(a, s);
+    case EPI_SILU_MUL: return launch_gemv<IN, EPI_SILU_MUL>(a, s);
+    case EPI_GELU_MUL: return launch_gemv<IN, EPI_GELU_MUL>(a, s);
+    case EPI_LOGITS: return launch_gemv<IN, EPI_LOGITS>(a, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaStream_t stream,
+                           int path) {
+  ProductArgs a = a0;
+  if (a.out_stride == 0) a.out_stride = a.rows;
+  if (a.tokens == 0 || a.rows == 0) return cudaSuccess;
+  if (a.cols == 0 || a.cols % 32) return cudaErrorInvalidValue;
+  bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
+  if (gemv) {
+    if (a.tokens != 1) return cudaErrorInvalidValue;
+    switch (in) {
+      case IN_PLANES: return dispatch_gemv<IN_PLANES>(a, epi, stream);
+      case IN_NORM: return dispatch_gemv<IN_NORM>(a, epi, stream);
+      case IN_RAW: return dispatch_gemv<IN_RAW>(a, epi, stream);
+    }
+    return cudaErrorInvalidValue;
+  }
+  if (in != IN_PLANES) return cudaErrorInvalidValue;  // callers build planes first
+  switch (epi) {
+    case EPI_STORE: return launch_gemm<EPI_STORE>(a, stream);
+    case EPI_RESID: return launch_gemm<EPI_RESID>(a, stream);
+    case EPI_QKV_ROPE: return launch_gemm<EPI_QKV_ROPE>(a, stream);
+    case EPI_SILU_MUL: return launch_gemm<EPI_SILU_MUL>(a, stream);
+    case EPI_GELU_MUL: return launch_gemm<EPI_GELU_MUL>(a, stream);
+    case EPI_LOGITS: return launch_gemm<EPI_LOGITS>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace iris
+
+// ===========================================================================
+// C ABI: the reference's q8gpu_* (drop-in) and the device-pointer products
+// ===========================================================================
+
+using namespace iris;
+
+namespace {
+std::mutex g_product_mutex;  // the drop-in's scratch buffers (one product at a time, as gpu.rs)
+int32_t* g_act = nullptr;
+int32_t* g_out = nullptr;
+uint8_t* g_planes = nullptr;
+size_t g_act_bytes = 0, g_out_bytes = 0, g_planes_bytes = 0;
+
+template <class T>
+cudaError_t reserve(T** buf, size_t* cap, size_t bytes) {
+  if (bytes <= *cap) return cudaSuccess;
+  cudaFree(*buf);
+  *buf = nullptr;
+  *cap = 0;
+  cudaError_t e = cudaMalloc((void**)buf, bytes);
+  if (e == cudaSuccess) *cap = bytes;
+  return e;
+}
+
+// The fp16 bits whose exact Q.24 value is v (inverse of q8.rs:27-43).
+bool q24_to_half_bits(int64_t v, uint16_t* bits) {
+  uint16_t sign = v < 0 ? 0x8000 : 0;
+  uint64_t mag = v < 0 ? (uint64_t)0 - (uint64_t)v : (uint64_t)v;
+  if (mag < 1024) {  // subnormal (or zero)
+    *bits = sign | (uint16_t)mag;
+    return true;
+  }
+  for (uint32_t ex = 1; ex <= 30; ++ex) {
+    uint64_t unit = (uint64_t)1 << (ex - 1);
+    if (mag % unit) return false;
+    uint64_t m = mag / unit;
+    if (m >= 1024 && m <= 2047) {
+      *bits = sign | (uint16_t)(ex << 10) | (uint16_t)(m - 1024);
+      return true;
+    }
+  }
+  return false;
+}
+}  // namespace
+
+extern "C" {
+
+const char* iris_error(int code) {
+  switch (code) {
+    case 0: return "no error";
+    case IRIS_EINVAL: return "iris: invalid argument or shape";
+    case IRIS_ESCALE: return "iris: Q8_0 block scale is not finite";
+    case IRIS_ERANGE: return "iris: position out of range";
+    case IRIS_ESTATE: return "iris: call out of order";
+    case IRIS_EWINDOW: return "iris: attention window not covered by the keys";
+    default: return cudaGetErrorString((cudaError_t)code);
+  }
+}
+
+const char* q8gpu_error(int code) { return iris_error(code); }
+
+int q8gpu_init(void) {
+  void* probe = nullptr;
+  cudaError_t e = cudaMalloc(&probe, 1 << 20);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaFree(probe);
+  if (e == cudaSuccess) e = prepare_product_kernels();
+  return (int)e;
+}
+
+void q8gpu_free(Q8GpuMatrix* matrix) { free_q8(matrix); }
+
+int q8gpu_upload(const int8_t* weights, const int64_t* scales_q24, uint32_t rows, uint32_t cols,
+                 Q8GpuMatrix** out_matrix) {
+  *out_matrix = nullptr;
+  if (rows == 0 || cols == 0 || cols % 32) return IRIS_EINVAL;
+  size_t nblk = (size_t)rows * (cols / 32);
+  std::vector<uint16_t> bits(nblk);
+  for (size_t i = 0; i < nblk; ++i)
+    if (!q24_to_half_bits(scales_q24[i], &bits[i])) return IRIS_ESCALE;
+  cudaError_t e;
+  Q8GpuMatrix* m = alloc_q8(rows, cols, &e);
+  if (!m) return (int)e;
+  e = cudaMemcpy(m->q, weights, (size_t)rows * cols, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(m->s, bits.data(), nblk * 2, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    free_q8(m);
+    return (int)e;
+  }
+  *out_matrix = m;
+  return 0;
+}
+
+int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
+                          Q8GpuMatrix** out_matrix) {
+  *out_matrix = nullptr;
+  if (rows == 0 || cols == 0 || cols % 32) return IRIS_EINVAL;
+  cudaError_t e;
+  Q8GpuMatrix* m = alloc_q8(rows, cols, &e);
+  if (!m) return (int)e;
+  int bad = 0;
+  e = upload_q8_blocks(m, blocks, rows, cols, 1, 0, &bad);
+  if (e != cudaSuccess || bad) {
+    free_q8(m);
+    return e != cudaSuccess ? (int)e : IRIS_ESCALE;
+  }
+  *out_matrix = m;
+  return 0;
+}
+
+int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
+                                int32_t* d_out, void* stream, int path) {
+  if (!m || tokens == 0) return tokens == 0 ? 0 : IRIS_EINVAL;
+  cudaStream_t s = (cudaStream_t)stream;
+  ProductArgs a{};
+  a.q = m->q;
+  a.s = m->s;
+  a.rows = m->rows;
+  a.cols = m->cols;
+  a.tokens = tokens;
+  a.out = d_out;
+  bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
+  if (gemv) {
+    a.x = d_act;
+    return (int)launch_product(a, IN_RAW, EPI_STORE, s, IRIS_PATH_GEMV);
+  }
+  // The tiled GEMM reads byte planes: build them into the shared scratch.
+  std::lock_guard<std::mutex> lock(g_product_mutex);
+  cudaError_t e = reserve(&g_planes, &g_planes_bytes, (size_t)tokens * m->cols * 4);
+  if (e == cudaSuccess) e = launch_planes(d_act, nullptr, 0, tokens, m->cols, g_planes, s);
+  a.planes = g_planes;
+  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, IRIS_PATH_GEMM);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // scratch is reused by the next call
+  return (int)e;
+}
+
+int iris_q8_product_device(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
+                           int32_t* d_out, void* stream) {
+  return iris_q8_product_device_path(m, d_act, tokens, d_out, stream, IRIS_PATH_AUTO);
+}
+
+int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tokens, int32_t* out) {
+  if (!m) return IRIS_EINVAL;
+  if (tokens == 0) return 0;
+  size_t act_bytes = (size_t)tokens * m->cols * 4, out_bytes = (size_t)tokens * m->rows * 4;
+  std::lock_guard<std::mutex> lock(g_product_mutex);
+  cudaError_t e = reserve(&g_act, &g_act_bytes, act_bytes);
+  if (e == cudaSuccess) e = reserve(&g_out, &g_out_bytes, out_bytes);
+  if (e == cudaSuccess && tokens > 1) e = reserve(&g_planes, &g_planes_bytes, act_bytes);
+  if (e == cudaSuccess) e = cudaMemcpy(g_act, activations, act_bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return (int)e;
+  ProductArgs a{};
+  a.q = m->q;
+  a.s = m->s;
+  a.rows = m->rows;
+  a.cols = m->cols;
+  a.tokens = tokens;
+  a.out = g_out;
+  if (tokens == 1) {
+    a.x = g_act;
+    e = launch_product(a, IN_RAW, EPI_STORE, 0, IRIS_PATH_GEMV);
+  } else {
+    e = launch_planes(g_act, nullptr, 0, tokens, m->cols, g_planes, 0);
+    a.planes = g_planes;
+    if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, 0, IRIS_PATH_GEMM);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(out, g_out, out_bytes, cudaMemcpyDeviceToHost);
+  return (int)e;
+}
+
+int iris_synth_q8(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,
+                  int per_block_scales, uint8_t* blocks) {
+  if (cols == 0 || cols % 32) return IRIS_EINVAL;
+  uint32_t nb = cols / 32;
+  for (uint32_t r = 0; r < rows; ++r)
+    for (uint32_t b = 0; b < nb; ++b) {
+      uint8_t* dst = blocks + ((size_t)r * nb + b) * 34;
+      uint16_t bits = synth_scale_bits(seed, tensor, layer, r, b, cols, per_block_scales);
+      dst[0] = (uint8_t)bits;
+      dst[1] = (uint8_t)(bits >> 8);
+      for (uint32_t j = 0; j < 32; ++j) dst[2 + j] = (uint8_t)synth_q(seed, tensor, layer, r, b * 32 + j, cols);
+    }
+  return 0;
+}
+
+int iris_synth_values(uint64_t seed, uint32_t tensor, int32_t layer, uint64_t count, uint32_t fan_in,
+                      int32_t* values) {
+  for (uint64_t i = 0; i < count; ++i) values[i] = synth_value(seed, tensor, layer, i, fan_in);
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,262 @@
+"""Device-resident models and decoding sessions (the direct-infer path).
+
+Host-side mirror of the reference's direct executor
+(crates/inference/direct/src/executor.rs:41-186): a model is loaded once into
+HBM; a Session keeps every layer's K/V on the device; `generate` is the decode
+loop (prefill, then greedy first-maximum selection until EOS or the budget).
+All arithmetic runs in libiris_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _lib
+from ._lib import T, check, lib, ptr
+from .shapes import GemmaConfig, MistralConfig
+
+Key = Tuple[str, int]  # (tensor name, layer or -1)
+
+
+def tensor_table(cfg) -> Dict[Key, tuple]:
+    """(kind, rows, cols, fan_in) of every tensor; kind is 'q8' or 'values'."""
+    H, F, V, L = cfg.hidden, cfg.ffn, cfg.vocab, cfg.layers
+    qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    t: Dict[Key, tuple] = {("EMBED", -1): ("q8", V, H, 0), ("FINAL_NORM", -1): ("values", 1, H, 0)}
+    if cfg.family == "mistral" and not cfg.tied:
+        t[("HEAD", -1)] = ("q8", V, H, 0)
+    for l in range(L):
+        t[("W_Q", l)] = ("q8", qd, H, 0)
+        t[("W_K", l)] = ("q8", kvd, H, 0)
+        t[("W_V", l)] = ("q8", kvd, H, 0)
+        t[("W_O", l)] = ("q8", H, qd, 0)
+        t[("W_GATE", l)] = ("q8", F, H, 0)
+        t[("W_UP", l)] = ("q8", F, H, 0)
+        t[("W_DOWN", l)] = ("q8", H, F, 0)
+        t[("NORM_ATTN", l)] = ("values", 1, H, 0)
+        t[("NORM_FFN", l)] = ("values", 1, H, 0)
+        if cfg.family == "gemma":
+            P, d = cfg.ple_width, cfg.head_dim
+            for n in ("NORM_POST_ATTN", "NORM_POST_FFW", "PLE_POST_NORM"):
+                t[(n, l)] = ("values", 1, H, 0)
+            t[("Q_NORM", l)] = ("values", 1, d, 0)
+            t[("K_NORM", l)] = ("values", 1, d, 0)
+            t[("PLE_INPUT_GATE", l)] = ("values", P, H, H)
+            t[("PLE_LAYER_PROJECTION", l)] = ("values", H, P, P)
+    if cfg.family == "gemma":
+        P = cfg.ple_width
+        t[("PLE_EMBED", -1)] = ("q8", V, L * P, 0)
+        t[("PLE_MODEL_PROJECTION", -1)] = ("values", L * P, H, H)
+        t[("PLE_NORM", -1)] = ("values", 1, P, 0)
+    return t
+
+
+def synth_host_weights(cfg, seed: int, per_block: bool = False,
+                       only: Optional[Iterable[Key]] = None) -> Dict[Key, np.ndarray]:
+    """The seeded synthetic tensors, generated on the host by the same code the
+    device runs in `DeviceModel.synthesize` (iris_b200/csrc/synth.cuh)."""
+    out = {}
+    table = tensor_table(cfg)
+    keys = list(only) if only is not None else list(table)
+    for key in keys:
+        kind, rows, cols, fan = table[key]
+        name, layer = key
+        if kind == "q8":
+            out[key] = _lib.synth_q8(seed, T[name], layer, rows, cols, per_block)
+        else:
+            out[key] = _lib.synth_values(seed, T[name], layer, rows * cols, fan)
+    return out
+
+
+class DeviceModel:
+    """A model whose weights live in HBM (IrisModel)."""
+
+    def __init__(self, cfg, weights: Optional[Dict[Key, np.ndarray]] = None, seed: Optional[int] = None,
+                 per_block: bool = False):
+        self.cfg = cfg
+        self._h = C.c_void_p()
+        L = lib()
+        if cfg.family == "mistral":
+            self._freqs = np.array(cfg.freqs, dtype=np.int64)
+            shape = _lib.MistralShape(cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim,
+                                      cfg.vocab, cfg.max_positions, cfg.norm_eps, cfg.scale_q32, int(cfg.tied),
+                                      ptr(self._freqs, C.c_int64))
+            check(L.iris_model_create_mistral(C.byref(shape), C.byref(self._h)), "iris_model_create_mistral")
+        else:
+            n = cfg.layers
+            self._win = np.array([cfg.window(l) for l in range(n)], np.uint32)
+            rope = [cfg.rope(l) for l in range(n)]
+            self._base = np.array([r[0] for r in rope], np.int64)
+            self._rot = np.array([r[1] for r in rope], np.uint32)
+            self._fbd = np.array([r[2] for r in rope], np.uint32)
+            self._donor = np.array([cfg.kv_donor(l) for l in range(n)], np.int32)
+            self._scal = np.array(cfg.layer_scalars or [0] * n, np.int32)
+            shape = _lib.GemmaShape(n, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.vocab,
+                                    cfg.ple_width, cfg.norm_eps, cfg.embedding_scale, cfg.ple_embedding_scale,
+                                    cfg.ple_projection_scalar, cfg.ple_input_scale, cfg.softcap_bits,
+                                    ptr(self._win, C.c_uint32), ptr(self._base, C.c_int64),
+                                    ptr(self._rot, C.c_uint32), ptr(self._fbd, C.c_uint32),
+                                    ptr(self._donor, C.c_int32), ptr(self._scal, C.c_int32))
+            check(L.iris_model_create_gemma(C.byref(shape), C.byref(self._h)), "iris_model_create_gemma")
+        if weights is not None:
+            self.load(weights)
+        elif seed is not None:
+            self.synthesize(seed, per_block)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def load(self, weights: Dict[Key, np.ndarray]) -> None:
+        table = tensor_table(self.cfg)
+        for key, arr in weights.items():
+            name, layer = key
+            kind = table[key][0]
+            if kind == "q8":
+                a = np.ascontiguousarray(arr, dtype=np.uint8)
+                check(lib().iris_model_set_q8(self._h, T[name], layer, ptr(a, C.c_uint8), a.size),
+                      f"iris_model_set_q8 {key}")
+            else:
+                a = np.ascontiguousarray(arr, dtype=np.int32)
+                check(lib().iris_model_set_values(self._h, T[name], layer, ptr(a, C.c_int32), a.size),
+                      f"iris_model_set_values {key}")
+
+    def synthesize(self, seed: int, per_block: bool = False) -> None:
+        check(lib().iris_model_synthesize(self._h, seed, int(per_block)), "iris_model_synthesize")
+
+    def get(self, key: Key) -> np.ndarray:
+        kind, rows, cols, _ = tensor_table(self.cfg)[key]
+        name, layer = key
+        if kind == "q8":
+            out = np.empty(rows * (cols // 32) * 34, np.uint8)
+            check(lib().iris_model_get_q8(self._h, T[name], layer, ptr(out, C.c_uint8), out.size), "get_q8")
+        else:
+            out = np.empty(rows * cols, np.int32)
+            check(lib().iris_model_get_values(self._h, T[name], layer, ptr(out, C.c_int32), out.size),
+                  "get_values")
+        return out
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(lib().iris_model_weight_bytes(self._h))
+
+    def session(self, max_positions: int) -> "Session":
+        return Session(self, max_positions)
+
+    def layer_range(self, layer: int, rows: np.ndarray, start: int, prior_k: Optional[np.ndarray],
+                    prior_v: Optional[np.ndarray]):
+        """One mistral-dense layer over a range (mistral/stage.rs:172-226):
+        returns (rows_out, own_k, own_v)."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        m = rows.shape[0]
+        kvd = self.cfg.kv_heads * self.cfg.head_dim
+        out = np.empty_like(rows)
+        ok = np.empty((m, kvd), np.int32)
+        ov = np.empty((m, kvd), np.int32)
+        pk = np.ascontiguousarray(prior_k if prior_k is not None else np.zeros((0, kvd)), np.int32)
+        pv = np.ascontiguousarray(prior_v if prior_v is not None else np.zeros((0, kvd)), np.int32)
+        check(lib().iris_mistral_layer_range(self._h, layer, ptr(rows, C.c_int32), m, start,
+                                             ptr(pk, C.c_int32) if start else None,
+                                             ptr(pv, C.c_int32) if start else None,
+                                             ptr(out, C.c_int32), ptr(ok, C.c_int32), ptr(ov, C.c_int32)),
+              "iris_mistral_layer_range")
+        return out, ok, ov
+
+    def close(self) -> None:
+        if self._h:
+            lib().iris_model_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """A decoding session: the K/V cache of every layer, in HBM."""
+
+    def __init__(self, model: DeviceModel, max_positions: int):
+        self.model = model
+        self._h = C.c_void_p()
+        check(lib().iris_session_create(model.handle, max_positions, C.byref(self._h)), "iris_session_create")
+
+    @property
+    def handle(self):
+        return self._h
+
+    def reset(self) -> None:
+        check(lib().iris_session_reset(self._h), "iris_session_reset")
+
+    def prefill(self, ids: Sequence[int], want_logits: bool = False):
+        a = np.ascontiguousarray(ids, np.uint32)
+        logits = np.empty(self.model.cfg.vocab, np.int32) if want_logits else None
+        tok = C.c_uint32()
+        check(lib().iris_session_prefill(self._h, ptr(a, C.c_uint32), a.size,
+                                         ptr(logits, C.c_int32) if logits is not None else None,
+                                         C.byref(tok)), "iris_session_prefill")
+        return tok.value, logits
+
+    def decode(self, token: int, want_logits: bool = False):
+        logits = np.empty(self.model.cfg.vocab, np.int32) if want_logits else None
+        tok = C.c_uint32()
+        check(lib().iris_session_decode(self._h, token, ptr(logits, C.c_int32) if logits is not None else None,
+                                        C.byref(tok)), "iris_session_decode")
+        return tok.value, logits
+
+    def generate(self, prompt: Sequence[int], max_tokens: int, eos: Sequence[int] = (),
+                 want_logits: bool = False):
+        p = np.ascontiguousarray(prompt, np.uint32)
+        e = np.ascontiguousarray(list(eos) or [0], np.uint32)
+        out = np.zeros(max(max_tokens, 1), np.uint32)
+        count = C.c_uint32()
+        logits = np.zeros((max(max_tokens, 1), self.model.cfg.vocab), np.int32) if want_logits else None
+        check(lib().iris_generate(self._h, ptr(p, C.c_uint32), p.size, max_tokens, ptr(e, C.c_uint32),
+                                  len(list(eos)), ptr(out, C.c_uint32), C.byref(count),
+                                  ptr(logits, C.c_int32) if logits is not None else None), "iris_generate")
+        n = count.value
+        return out[:n].tolist(), (logits[:n] if logits is not None else None)
+
+    @property
+    def length(self) -> int:
+        return int(lib().iris_session_length(self._h))
+
+    def decode_steps(self, steps: int) -> None:
+        """Replays the captured decode pass `steps` times without waiting."""
+        check(lib().iris_session_decode_steps(self._h, steps), "iris_session_decode_steps")
+
+    def synchronize(self) -> None:
+        check(lib().iris_session_synchronize(self._h), "iris_session_synchronize")
+
+    @property
+    def stream_ptr(self) -> int:
+        return int(lib().iris_session_stream(self._h) or 0)
+
+    @property
+    def kernels_per_pass(self) -> int:
+        return int(lib().iris_session_graph_kernels(self._h))
+
+    def product(self, layer: int, which: int) -> None:
+        check(lib().iris_session_product(self._h, layer, which), "iris_session_product")
+
+    def kv(self, layer: int, first: int, count: int):
+        kvd = self.model.cfg.kv_heads * self.model.cfg.head_dim
+        k = np.empty((count, kvd), np.int32)
+        v = np.empty((count, kvd), np.int32)
+        check(lib().iris_session_get_kv(self._h, layer, first, count, ptr(k, C.c_int32), ptr(v, C.c_int32)),
+              "iris_session_get_kv")
+        return k, v
+
+    def close(self) -> None:
+        if self._h:
+            lib().iris_session_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
