@@ -30,6 +30,12 @@ __device__ __forceinline__ int32_t finish_score(int64_t sum, int mode, uint32_t 
 
 __device__ __forceinline__ int64_t ldcg_i64(const int64_t* p) { return (int64_t)__ldcg((const long long*)p); }
 
+// The decode query's position: from device memory inside the captured decode
+// pass, else the host-given position (a single-row chain range).
+__device__ __forceinline__ uint32_t query_position(const AttnArgs& a) {
+  return a.pos_ptr ? *a.pos_ptr : a.pos0;
+}
+
 // ---------------------------------------------------------------------------
 // Decode attention
 // ---------------------------------------------------------------------------
@@ -40,7 +46,7 @@ constexpr int kMaxGroup = 16;  // query heads per kv head
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
   extern __shared__ __align__(16) int32_t q_s[];  // [G][d]
   __shared__ unsigned long long best_s[kMaxGroup];
-  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t p = query_position(a), ws = window_start(p, a.window);
   const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
   const uint32_t t0 = ws + c * a.chunk;
   if (t0 > p) return;
@@ -84,7 +90,7 @@ __device__ void group_global_best(const AttnArgs& a, uint32_t g, uint32_t G, uin
 __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
   __shared__ unsigned long long best_s[kMaxGroup];
   __shared__ unsigned long long sum_s[kMaxGroup];
-  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t p = query_position(a), ws = window_start(p, a.window);
   const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
   const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
   if (c >= nact) return;
@@ -112,7 +118,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
   __shared__ unsigned long long total_s[kMaxGroup];
   __shared__ int32_t wsum_s[kMaxGroup];
   __shared__ bool last_s;
-  const uint32_t p = *a.pos_ptr, ws = window_start(p, a.window);
+  const uint32_t p = query_position(a), ws = window_start(p, a.window);
   const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
   const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
   const uint32_t t0 = ws + c * a.chunk;

@@ -80,6 +80,16 @@ def test_parity_gemma_window_donors_softcap():
     assert_same(got, want)
 
 
+def test_single_token_prompt():
+    """A one-row prompt pass takes the single-row attention path with a host
+    position (both families)."""
+    from iris_b200.shapes import parity_gemma, parity_mistral
+    for cfg in (parity_mistral(), parity_gemma()):
+        prompt = seeded_prompt(13, 1, cfg.vocab)
+        _, _, _, got, want = run_both(cfg, 13, prompt, 5)
+        assert_same(got, want)
+
+
 def test_long_prompt_crosses_device_ranges():
     """A 300-token prompt is processed as two device ranges (256 + 44)."""
     from iris_b200.shapes import parity_mistral
