@@ -281,10 +281,10 @@ cudaError_t prepare_layer_kernels() {
 // ---------------------------------------------------------------------------
 
 __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t cols,
-                             const uint32_t* ids, int32_t scale, int has_scale, int32_t* out) {
+                             uint32_t spitch, const uint32_t* ids, int32_t scale, int has_scale, int32_t* out) {
   uint32_t t = blockIdx.x, id = ids[t];
   const int8_t* row = q + (size_t)id * cols;
-  const uint16_t* srow = s + (size_t)id * (cols / 32);
+  const uint16_t* srow = s + (size_t)id * spitch;
   for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
     int32_t m, e;
     q8_scale_parts(srow[i >> 5], &m, &e);
@@ -297,7 +297,8 @@ __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __res
 cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32_t tokens,
                          int has_scale, int32_t scale, int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, d_ids, scale, has_scale, out);
+  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, embed->spitch, d_ids, scale, has_scale,
+                                      out);
   return cudaGetLastError();
 }
 
@@ -486,7 +487,7 @@ cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const i
 }
 
 __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, const uint16_t* es,
-                                   uint32_t ecols, const uint32_t* ids, const int32_t* ple_norm,
+                                   uint32_t ecols, uint32_t espitch, const uint32_t* ids, const int32_t* ple_norm,
                                    int64_t eps, int32_t projection_scalar, int32_t embedding_scale,
                                    int32_t input_scale, uint32_t L, uint32_t P, int32_t* out) {
   extern __shared__ __align__(16) int32_t row[];  // [P]
@@ -499,7 +500,7 @@ __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, c
   for (uint32_t j = threadIdx.x; j < P; j += blockDim.x) {
     uint32_t col = l * P + j;
     int32_t m, e;
-    q8_scale_parts(es[(size_t)id * (ecols / 32) + (col >> 5)], &m, &e);
+    q8_scale_parts(es[(size_t)id * espitch + (col >> 5)], &m, &e);
     int32_t v = mul_sat(q8_dequant(eq[(size_t)id * ecols + col], m, e), embedding_scale);
     v = add_sat(v, row[j]);
     out[((size_t)t * L + l) * P + j] = mul_sat(v, input_scale);
@@ -513,7 +514,8 @@ cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_
                                int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   dim3 grid(tokens, layers);
-  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->cols, d_ids,
+  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->cols,
+                                              ple_embed->spitch, d_ids,
                                               ple_norm, eps, projection_scalar, embedding_scale,
                                               input_scale, layers, P, out);
   return cudaGetLastError();

@@ -244,6 +244,7 @@ ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
   ProductArgs a{};
   a.q = w->q;
   a.s = w->s;
+  a.spitch = w->spitch;
   a.rows = w->rows;
   a.cols = w->cols;
   a.tokens = tokens;

@@ -37,7 +37,7 @@ namespace iris {
 
 __global__ void repack_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t rows, uint32_t cols,
                                      uint32_t row_stride, uint32_t row_offset, int8_t* q,
-                                     uint16_t* s, int* bad) {
+                                     uint16_t* s, uint32_t spitch, int* bad) {
   uint32_t nb = cols / 32;
   uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
@@ -46,7 +46,7 @@ __global__ void repack_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t r
   uint16_t bits = (uint16_t)(src[0] | (src[1] << 8));
   if (((bits >> 10) & 0x1f) == 0x1f) atomicExch(bad, 1);
   uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  s[dr * nb + blk] = bits;
+  s[dr * spitch + blk] = bits;
   uint32_t w[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -57,14 +57,14 @@ __global__ void repack_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t r
   dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-__global__ void unpack_blocks_kernel(const int8_t* q, const uint16_t* s, uint32_t rows, uint32_t cols,
-                                     uint32_t row_stride, uint32_t row_offset, uint8_t* raw) {
+__global__ void unpack_blocks_kernel(const int8_t* q, const uint16_t* s, uint32_t spitch, uint32_t rows,
+                                     uint32_t cols, uint32_t row_stride, uint32_t row_offset, uint8_t* raw) {
   uint32_t nb = cols / 32;
   uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
   uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
   uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  uint16_t bits = s[dr * nb + blk];
+  uint16_t bits = s[dr * spitch + blk];
   uint8_t* dst = raw + b * 34;
   dst[0] = (uint8_t)bits;
   dst[1] = (uint8_t)(bits >> 8);
@@ -72,7 +72,7 @@ __global__ void unpack_blocks_kernel(const int8_t* q, const uint16_t* s, uint32_
   for (int i = 0; i < 32; ++i) dst[2 + i] = (uint8_t)src[i];
 }
 
-__global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint64_t seed, uint32_t tensor,
+__global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint32_t spitch, uint64_t seed, uint32_t tensor,
                                 int32_t layer, uint32_t rows, uint32_t cols, uint32_t row_stride,
                                 uint32_t row_offset, int per_block) {
   uint32_t nb = cols / 32;
@@ -80,7 +80,7 @@ __global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint64_t seed, uint32_t 
   if (b >= (uint64_t)rows * nb) return;
   uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
   uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  s[dr * nb + blk] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
+  s[dr * spitch + blk] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
   uint32_t w[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -109,9 +109,11 @@ Q8GpuMatrix* alloc_q8(uint32_t rows, uint32_t cols, cudaError_t* err) {
   }
   m->rows = rows;
   m->cols = cols;
+  m->spitch = q8_scale_pitch(cols);
   m->owns = true;
   *err = cudaMalloc((void**)&m->q, (size_t)rows * cols);
-  if (*err == cudaSuccess) *err = cudaMalloc((void**)&m->s, (size_t)rows * (cols / 32) * 2);
+  if (*err == cudaSuccess) *err = cudaMalloc((void**)&m->s, (size_t)rows * m->spitch * 2);
+  if (*err == cudaSuccess) *err = cudaMemset(m->s, 0, (size_t)rows * m->spitch * 2);
   if (*err != cudaSuccess) {
     free_q8(m);
     return nullptr;
@@ -141,7 +143,7 @@ cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint3
   if (e == cudaSuccess) {
     uint64_t nblk = (uint64_t)rows * (cols / 32);
     repack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(staging, rows, cols, row_stride,
-                                                                  row_offset, dst->q, dst->s, bad);
+                                                                  row_offset, dst->q, dst->s, dst->spitch, bad);
     e = cudaGetLastError();
   }
   int h_bad = 0;
@@ -159,7 +161,7 @@ cudaError_t download_q8_blocks(const Q8GpuMatrix* src, uint8_t* host_blocks, uin
   cudaError_t e = cudaMalloc((void**)&staging, bytes);
   if (e == cudaSuccess) {
     uint64_t nblk = (uint64_t)rows * (cols / 32);
-    unpack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(src->q, src->s, rows, cols,
+    unpack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(src->q, src->s, src->spitch, rows, cols,
                                                                   row_stride, row_offset, staging);
     e = cudaGetLastError();
   }
@@ -173,7 +175,7 @@ cudaError_t synth_q8_rows(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int3
                           int per_block, cudaStream_t stream) {
   uint64_t nblk = (uint64_t)rows * (cols / 32);
   synth_q8_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream>>>(
-      dst->q, dst->s, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
+      dst->q, dst->s, dst->spitch, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
   return cudaGetLastError();
 }
 
@@ -330,9 +332,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a)
   const uint4* P1 = P0 + K / 16;
   const uint4* P2 = P1 + K / 16;
   const uint4* P3 = P2 + K / 16;
-  const uint32_t nchunk = K / 16, nblk = K / 32;
+  const uint32_t nchunk = K / 16;
   const int8_t* wrow = a.q + (size_t)row0 * K;
-  const uint16_t* srow = a.s + (size_t)row0 * nblk;
+  const uint16_t* srow = a.s + (size_t)row0 * a.spitch;
   const uint32_t live = min((uint32_t)R, a.rows - row0);
 
   Acc128 acc[R];
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a)
     for (int r = 0; r < R; ++r) {
       if ((uint32_t)r < live) {
         w[r] = ld_stream_v4(wrow + (size_t)r * K + (size_t)c * 16);
-        sb[r] = ld_stream_u16(srow + (size_t)r * nblk + (c >> 1));
+        sb[r] = ld_stream_u16(srow + (size_t)r * a.spitch + (c >> 1));
       } else {
         w[r] = make_uint4(0, 0, 0, 0);
         sb[r] = 0;
@@ -391,6 +393,233 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a)
 }
 
 // ---------------------------------------------------------------------------
+// Decode GEMV, bulk-copy pipeline: one persistent block an SM
+// ---------------------------------------------------------------------------
+//
+// Each block owns a contiguous range of rows, taken in groups of up to 16
+// rows and, along K, in slices of up to 2048 columns. A producer warp streams
+// every (group, slice) tile - the rows' int8 values and fp16 scale bits -
+// from HBM into a ring of shared-memory stages with cp.async.bulk (TMA,
+// evict-first in L2), completing on the stage's "full" mbarrier. Eight
+// consumer warps, two rows each, run the dp4a byte-plane products against the
+// activation planes held in shared memory and release the stage on its
+// "empty" mbarrier. The activation prologue (planes, or the fused RMSNorm)
+// runs once per block while the first stages are already in flight. Every
+// wait is bounded (about one second): a stalled pipeline records a fault and
+// the kernel returns instead of hanging.
+
+__device__ unsigned int g_fault;
+
+constexpr int kTmaConsumerWarps = 8;
+constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;
+constexpr uint32_t kTmaMaxStages = 4;
+constexpr uint32_t kTmaGroupRows = 2 * kTmaConsumerWarps;
+constexpr uint32_t kTmaSmemBudget = 220 * 1024;
+
+struct GemvPlan {
+  uint32_t kc;              // slice width
+  uint32_t nslices;         // K / kc
+  uint32_t sbytes;          // scale bytes a row contributes to a slice
+  uint32_t grows;           // rows a group (even)
+  uint32_t stages;
+  uint32_t stage_bytes;     // grows * (kc + sbytes), rounded to 128
+  uint32_t planes_bytes;    // 4 K, rounded to 128
+  uint32_t rows_per_block;  // even
+  uint32_t smem;
+  uint32_t grid;
+};
+
+__host__ __device__ inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+bool plan_gemv(uint32_t rows, uint32_t K, uint32_t spitch, int sms, GemvPlan* p) {
+  if (K % 32 || rows == 0) return false;
+  p->kc = K;
+  if (K % 256 == 0)
+    for (uint32_t kc = 2048; kc >= 256; kc /= 2)
+      if (K % kc == 0) { p->kc = kc; break; }
+  p->nslices = K / p->kc;
+  p->sbytes = p->nslices == 1 ? spitch * 2 : p->kc / 16;
+  p->planes_bytes = round_up(4 * K, 128);
+  if (p->planes_bytes >= kTmaSmemBudget) return false;
+  p->grows = kTmaGroupRows;
+  while (true) {
+    p->stage_bytes = round_up(p->grows * (p->kc + p->sbytes), 128);
+    uint32_t fit = (kTmaSmemBudget - p->planes_bytes) / p->stage_bytes;
+    if (fit >= 2) {
+      p->stages = fit < kTmaMaxStages ? fit : kTmaMaxStages;
+      break;
+    }
+    if (p->grows == 2) return false;
+    p->grows -= 2;
+  }
+  p->smem = p->planes_bytes + p->stages * p->stage_bytes;
+  uint32_t pairs = (rows + 1) / 2;
+  uint32_t grid = (uint32_t)sms < pairs ? (uint32_t)sms : pairs;
+  p->rows_per_block = round_up((rows + grid - 1) / grid, 2);
+  p->grid = (rows + p->rows_per_block - 1) / p->rows_per_block;
+  return true;
+}
+
+template <int IN, int EPI>
+__global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs a, GemvPlan p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kTmaMaxStages];
+  __shared__ __align__(8) uint64_t empty[kTmaMaxStages];
+  __shared__ uint64_t red[32];
+  __shared__ int32_t s_scale;
+  const uint32_t K = a.cols;
+  uint8_t* planes = smem;
+  uint8_t* stage0 = smem + p.planes_bytes;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool producer = warp == kTmaConsumerWarps;
+  const uint32_t r_begin = blockIdx.x * p.rows_per_block;
+  const uint32_t r_end = min(a.rows, r_begin + p.rows_per_block);
+  const uint32_t ngroups = r_begin < r_end ? (r_end - r_begin + p.grows - 1) / p.grows : 0;
+  const uint32_t nitems = ngroups * p.nslices;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t st = 0; st < p.stages; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kTmaConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  const uint64_t policy = l2_evict_first_policy();
+  auto issue = [&](uint32_t item) {
+    const uint32_t st = item % p.stages, g = item / p.nslices, sl = item % p.nslices;
+    const uint32_t row0 = r_begin + g * p.grows, nr = min(p.grows, r_end - row0);
+    uint8_t* wdst = stage0 + st * p.stage_bytes;
+    uint8_t* sdst = wdst + p.grows * p.kc;
+    const uint8_t* sbase = (const uint8_t*)a.s;
+    mbar_arrive_expect_tx(&full[st], nr * (p.kc + p.sbytes));
+    if (p.nslices == 1) {  // whole rows: one copy each for values and scales
+      bulk_load(wdst, a.q + (size_t)row0 * K, nr * K, &full[st], policy);
+      bulk_load(sdst, sbase + (size_t)row0 * a.spitch * 2, nr * p.sbytes, &full[st], policy);
+    } else {
+      for (uint32_t r = 0; r < nr; ++r) {
+        bulk_load(wdst + r * p.kc, a.q + (size_t)(row0 + r) * K + (size_t)sl * p.kc, p.kc, &full[st], policy);
+        bulk_load(sdst + r * p.sbytes, sbase + (size_t)(row0 + r) * a.spitch * 2 + (size_t)sl * p.sbytes,
+                  p.sbytes, &full[st], policy);
+      }
+    }
+  };
+
+  // The first stages need no release: issue them before the prologue.
+  const uint32_t first = nitems < p.stages ? nitems : p.stages;
+  if (producer && lane == 0)
+    for (uint32_t item = 0; item < first; ++item) issue(item);
+
+  if (IN == IN_PLANES) {
+    const uint4* src = (const uint4*)a.planes;
+    for (uint32_t i = threadIdx.x; i < K / 4; i += blockDim.x) ((uint4*)planes)[i] = src[i];
+  } else {
+    row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, planes, red, &s_scale);
+  }
+  __syncthreads();
+
+  if (producer) {
+    if (lane == 0) {
+      uint32_t issued = first;
+      bool stalled = false;
+      for (uint32_t item = first; item < nitems; ++item) {
+        const uint32_t st = item % p.stages, use = item / p.stages;
+        if (!mbar_wait_bounded(&empty[st], (use - 1) & 1, &g_fault)) {
+          stalled = true;
+          break;
+        }
+        issue(item);
+        issued = item + 1;
+      }
+      if (stalled)  // let the copies already issued land before the block exits
+        for (uint32_t item = issued > p.stages ? issued - p.stages : 0; item < issued; ++item)
+          mbar_wait_bounded(&full[item % p.stages], (item / p.stages) & 1, &g_fault);
+    }
+    return;
+  }
+
+  const uint4* P0 = (const uint4*)planes;
+  const uint4* P1 = P0 + K / 16;
+  const uint4* P2 = P1 + K / 16;
+  const uint4* P3 = P2 + K / 16;
+  const uint32_t lr0 = 2 * warp, lr1 = lr0 + 1, chunks = p.kc / 16;
+  Acc128 acc0{0, 0}, acc1{0, 0};
+  for (uint32_t item = 0; item < nitems; ++item) {
+    const uint32_t st = item % p.stages, use = item / p.stages;
+    const uint32_t g = item / p.nslices, sl = item % p.nslices;
+    const uint32_t row0 = r_begin + g * p.grows, nr = min(p.grows, r_end - row0);
+    if (!mbar_wait_bounded(&full[st], use & 1, &g_fault)) return;
+    if (lr0 < nr) {
+      const uint8_t* W0 = stage0 + st * p.stage_bytes + lr0 * p.kc;
+      const uint16_t* S0 = (const uint16_t*)(stage0 + st * p.stage_bytes + p.grows * p.kc + lr0 * p.sbytes);
+      const uint32_t cbase = sl * chunks;
+      if (lr1 < nr) {
+        const uint8_t* W1 = W0 + p.kc;
+        const uint16_t* S1 = S0 + p.sbytes / 2;
+        for (uint32_t c = lane; c < chunks; c += 32) {
+          const uint4 p0 = P0[cbase + c], p1 = P1[cbase + c], p2 = P2[cbase + c], p3 = P3[cbase + c];
+          const uint4 w0 = *(const uint4*)(W0 + c * 16), w1 = *(const uint4*)(W1 + c * 16);
+          int32_t m0, e0, m1, e1;
+          q8_scale_parts(S0[c >> 1], &m0, &e0);  // finite: checked at upload
+          q8_scale_parts(S1[c >> 1], &m1, &e1);
+          acc128_add_shifted(acc0, q8_partial16(w0, p0, p1, p2, p3) * m0, e0);
+          acc128_add_shifted(acc1, q8_partial16(w1, p0, p1, p2, p3) * m1, e1);
+        }
+      } else {
+        for (uint32_t c = lane; c < chunks; c += 32) {
+          const uint4 p0 = P0[cbase + c], p1 = P1[cbase + c], p2 = P2[cbase + c], p3 = P3[cbase + c];
+          const uint4 w0 = *(const uint4*)(W0 + c * 16);
+          int32_t m0, e0;
+          q8_scale_parts(S0[c >> 1], &m0, &e0);
+          acc128_add_shifted(acc0, q8_partial16(w0, p0, p1, p2, p3) * m0, e0);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (sl + 1 == p.nslices) {
+      if (lr0 < nr) {
+        acc0 = warp_sum_acc128(acc0);
+        acc1 = warp_sum_acc128(acc1);
+        if (lane == 0) {
+          const uint32_t row = row0 + lr0;
+          const int32_t v0 = acc128_round_q24(acc0);
+          const bool two = lr1 < nr;
+          const int32_t v1 = two ? acc128_round_q24(acc1) : 0;
+          if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+            if (two) epi_pair<EPI>(a, 0, row, v0, v1);
+          } else if (EPI == EPI_LOGITS) {
+            int32_t c0 = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
+            unsigned long long key = best_key(c0, row);
+            if (a.out) a.out[row] = c0;
+            if (two) {
+              int32_t c1 = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
+              if (a.out) a.out[row + 1] = c1;
+              unsigned long long k1 = best_key(c1, row + 1);
+              key = k1 > key ? k1 : key;
+            }
+            atomicMax(a.best, key);
+          } else {
+            epi_single<EPI>(a, 0, row, v0);
+            if (two) epi_single<EPI>(a, 0, row + 1, v1);
+          }
+        }
+      }
+      acc0 = Acc128{0, 0};
+      acc1 = Acc128{0, 0};
+    }
+  }
+}
+
+cudaError_t take_device_fault(uint32_t* fault) {
+  uint32_t zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(fault, g_fault, sizeof(uint32_t));
+  if (e == cudaSuccess && *fault) e = cudaMemcpyToSymbol(g_fault, &zero, sizeof(uint32_t));
+  return e;
+}
+
+// ---------------------------------------------------------------------------
 // Tiled GEMM: 64 rows x 32 tokens a block, 4 rows x 2 tokens a thread
 // ---------------------------------------------------------------------------
 
@@ -421,7 +650,7 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
     } else if (tid < 128 + kTileN) {
       int r = tid - 128;
       uint32_t row = n0 + r;
-      ssc[r] = row < a.rows ? a.s[(size_t)row * nblk + kb] : (uint16_t)0;
+      ssc[r] = row < a.rows ? a.s[(size_t)row * a.spitch + kb] : (uint16_t)0;
     }
     {
       int t = tid >> 3, p = (tid >> 1) & 3, h = tid & 1;
@@ -483,8 +712,26 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
 
 constexpr size_t kGemvMaxSmem = 200 * 1024;  // activations up to 51200 wide
 
+int g_sms = 0;  // multiprocessors of the current device
+
+int device_sms() {
+  if (g_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || g_sms <= 0)
+      g_sms = 148;
+  }
+  return g_sms;
+}
+
 template <int IN, int EPI>
 cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
+  GemvPlan p;
+  if (plan_gemv(a.rows, a.cols, a.spitch, device_sms(), &p)) {
+    q8_gemv_tma_kernel<IN, EPI><<<p.grid, kTmaThreads, p.smem, stream>>>(a, p);
+    return cudaGetLastError();
+  }
+  // Shapes whose tiles do not fit the shared-memory ring: the direct-load GEMV.
   auto kern = q8_gemv_kernel<kGemvRows, IN, EPI>;
   size_t smem = (size_t)a.cols * 4;
   if (smem > kGemvMaxSmem) return cudaErrorInvalidValue;
@@ -494,22 +741,30 @@ cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+template <int IN, int EPI>
+cudaError_t prepare_gemv_pair() {
+  cudaError_t e = cudaFuncSetAttribute(q8_gemv_kernel<kGemvRows, IN, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kTmaSmemBudget);
+  return e;
+}
+
 template <int IN>
 cudaError_t prepare_gemv_in() {
-  const void* kerns[] = {
-      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_STORE>, (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_RESID>,
-      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_QKV_ROPE>,
-      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_SILU_MUL>,
-      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_GELU_MUL>,
-      (const void*)q8_gemv_kernel<kGemvRows, IN, EPI_LOGITS>};
-  for (const void* k : kerns) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem);
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  cudaError_t e = prepare_gemv_pair<IN, EPI_STORE>();
+  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_RESID>();
+  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_QKV_ROPE>();
+  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_SILU_MUL>();
+  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_GELU_MUL>();
+  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_LOGITS>();
+  return e;
 }
 
 cudaError_t prepare_product_kernels() {
+  g_sms = 0;
+  device_sms();
   cudaError_t e = prepare_gemv_in<IN_PLANES>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_NORM>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_RAW>();
@@ -650,7 +905,9 @@ int q8gpu_upload(const int8_t* weights, const int64_t* scales_q24, uint32_t rows
   Q8GpuMatrix* m = alloc_q8(rows, cols, &e);
   if (!m) return (int)e;
   e = cudaMemcpy(m->q, weights, (size_t)rows * cols, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemcpy(m->s, bits.data(), nblk * 2, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy2D(m->s, (size_t)m->spitch * 2, bits.data(), (size_t)(cols / 32) * 2, (size_t)(cols / 32) * 2,
+                     rows, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     free_q8(m);
     return (int)e;
@@ -683,6 +940,7 @@ int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint
   ProductArgs a{};
   a.q = m->q;
   a.s = m->s;
+  a.spitch = m->spitch;
   a.rows = m->rows;
   a.cols = m->cols;
   a.tokens = tokens;
@@ -720,6 +978,7 @@ int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tok
   ProductArgs a{};
   a.q = m->q;
   a.s = m->s;
+  a.spitch = m->spitch;
   a.rows = m->rows;
   a.cols = m->cols;
   a.tokens = tokens;

@@ -6,13 +6,15 @@
 #include "common.cuh"
 
 // Repacked device layout of a Q8_0 matrix: the 34-byte GGUF blocks split into
-// int8 values [rows][cols] (16-byte aligned rows, coalesced 128-bit loads) and
-// fp16 scale bits [rows][cols/32]. 1.0625 bytes a weight, as in Q8_0.
+// int8 values [rows][cols] (16-byte aligned rows, coalesced 128-bit loads and
+// bulk copies) and fp16 scale bits [rows][spitch], spitch = cols/32 rounded
+// up to 8 entries so that every row of scales starts on a 16-byte boundary.
+// 1.0625 bytes a weight, as in Q8_0, for the widths models use.
 struct Q8GpuMatrix {
   int8_t* q;
   uint16_t* s;
-  uint32_t rows, cols;
-  bool owns;  // false for views into a model's fused buffers
+  uint32_t rows, cols, spitch;
+  bool owns;
 };
 
 namespace iris {
@@ -27,10 +29,13 @@ enum EpiMode {
   EPI_LOGITS = 5     // logits (+softcap) and a first-maximum key
 };
 
+__host__ __device__ inline uint32_t q8_scale_pitch(uint32_t cols) { return ((cols / 32 + 7) / 8) * 8; }
+
 struct ProductArgs {
   const int8_t* q;
   const uint16_t* s;
   uint32_t rows, cols, tokens;
+  uint32_t spitch;         // scale entries per row (q8_scale_pitch(cols))
   // input: planes [tokens][4][cols], or raw / to-be-normed int32 [tokens][cols]
   const uint8_t* planes;
   const int32_t* x;
@@ -68,6 +73,10 @@ __host__ __device__ inline int32_t best_key_value(unsigned long long key) {
 __host__ __device__ inline unsigned long long best_key(int32_t v, uint32_t idx) {
   return ((unsigned long long)((uint32_t)v ^ 0x80000000u) << 32) | (0xFFFFFFFFu - idx);
 }
+
+// Non-zero once a kernel gave up a bounded wait (a stalled pipeline); read and
+// cleared by the host.
+cudaError_t take_device_fault(uint32_t* fault);
 
 // Uploads raw Q8_0 blocks into rows [row_offset + i*row_stride] of dst.
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
