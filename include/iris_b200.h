@@ -35,6 +35,7 @@ extern "C" {
 #define IRIS_ERANGE 10003   /* a position past max_positions or the KV capacity */
 #define IRIS_ESTATE 10004   /* call out of order (e.g. decode before prefill) */
 #define IRIS_EWINDOW 10005  /* attention window not covered by the given keys */
+#define IRIS_ESTALL 10006   /* a kernel gave up a bounded wait (pipeline stalled) */
 
 /* ---------------------------------------------------------------------------
  * 1. Drop-in for the reference's q8gpu_* FFI. Same names, signatures and

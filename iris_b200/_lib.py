@@ -14,7 +14,7 @@ import numpy as np
 PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libiris_b200.so"
 
-IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW = 10001, 10002, 10003, 10004, 10005
+IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 10001, 10002, 10003, 10004, 10005, 10006
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
 
 # Tensor kinds (include/iris_b200.h)

@@ -39,159 +39,200 @@ __device__ __forceinline__ uint32_t query_position(const AttnArgs& a) {
 // ---------------------------------------------------------------------------
 // Decode attention
 // ---------------------------------------------------------------------------
+//
+// Grid (heads / hpc, position chunks of kAttnChunk), 256 threads. A block
+// owns hpc query heads of one kv group and 64 consecutive positions of the
+// window [ws, p]. Scores: each warp takes its 8 positions four at a time, 8
+// lanes a position, each lane d/8 contiguous dimensions of the key row
+// (coalesced), reduced over the 8 lanes with shuffles.
 
-constexpr int kAttnThreads = 128;
-constexpr int kMaxGroup = 16;  // query heads per kv head
+constexpr int kAttnThreads = 256;
+constexpr uint32_t kAttnChunk = 64;
+constexpr int kMaxHpc = 4;  // query heads a block
 
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
-  extern __shared__ __align__(16) int32_t q_s[];  // [G][d]
-  __shared__ unsigned long long best_s[kMaxGroup];
+  __shared__ __align__(16) int32_t q_s[kMaxHpc * 256];
+  __shared__ unsigned long long best_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
-  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
-  const uint32_t t0 = ws + c * a.chunk;
+  const uint32_t hpc = a.hpc, G = a.heads / a.kv_heads, h0 = blockIdx.x * hpc, g = h0 / G;
+  const uint32_t c = blockIdx.y, t0 = ws + c * kAttnChunk;
   if (t0 > p) return;
-  for (uint32_t i = threadIdx.x; i < G * a.d; i += blockDim.x) q_s[i] = a.q[g * G * a.d + i];
-  if (threadIdx.x < G) best_s[threadIdx.x] = 0;
+  const uint32_t d = a.d;
+  for (uint32_t i = threadIdx.x; i < hpc * d; i += blockDim.x) q_s[i] = a.q[h0 * d + i];
+  if (threadIdx.x < hpc) best_s[threadIdx.x] = 0;
   __syncthreads();
-  const uint32_t hs = blockDim.x / a.chunk;  // threads sharing a position
-  const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
-  const uint32_t t = t0 + lp;
-  if (t <= p) {
-    const int32_t* krow = a.kcache + (size_t)t * a.kvd + g * a.d;
-    for (uint32_t h = hg; h < G; h += hs) {
-      const int32_t* qh = q_s + h * a.d;
-      int64_t sum = 0;
-      for (uint32_t i = 0; i < a.d; i += 4) {
-        int4 k4 = *(const int4*)(krow + i);
-        int4 q4 = *(const int4*)(qh + i);
-        sum = (int64_t)((uint64_t)sum + (uint64_t)((int64_t)q4.x * k4.x) + (uint64_t)((int64_t)q4.y * k4.y) +
-                        (uint64_t)((int64_t)q4.z * k4.z) + (uint64_t)((int64_t)q4.w * k4.w));
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = lane >> 3, ql = lane & 7;
+  const uint32_t per = d / 8, i0 = ql * per;  // this lane's dimensions
+  for (uint32_t round = 0; round < 2; ++round) {
+    const uint32_t t = t0 + warp * 8 + round * 4 + quad;
+    const bool live = t <= p;
+    const int32_t* krow = a.kcache + (size_t)(live ? t : t0) * a.kvd + g * d + i0;
+    int64_t sum[kMaxHpc] = {0, 0, 0, 0};
+    for (uint32_t i = 0; i < per; i += 4) {
+      const int4 k4 = *(const int4*)(krow + i);
+#pragma unroll
+      for (uint32_t h = 0; h < kMaxHpc; ++h) {
+        if (h < hpc) {
+          const int4 q4 = *(const int4*)(q_s + h * d + i0 + i);
+          sum[h] = (int64_t)((uint64_t)sum[h] + (uint64_t)((int64_t)q4.x * k4.x) +
+                             (uint64_t)((int64_t)q4.y * k4.y) + (uint64_t)((int64_t)q4.z * k4.z) +
+                             (uint64_t)((int64_t)q4.w * k4.w));
+        }
       }
-      int32_t sc = finish_score(sum, a.mode, a.scale_q32);
-      uint32_t hh = g * G + h;
-      a.scores[(size_t)hh * a.cap + t] = sc;
-      atomicMax(&best_s[h], best_key(sc, t));
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < kMaxHpc; ++h) {
+      if (h < hpc) {
+        int64_t v = sum[h];
+        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 4));
+        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 2));
+        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 1));
+        if (ql == 0 && live) {
+          const int32_t sc = finish_score(v, a.mode, a.scale_q32);
+          a.scores[(size_t)(h0 + h) * a.cap + t] = sc;
+          atomicMax(&best_s[h], best_key(sc, t));
+        }
+      }
     }
   }
   __syncthreads();
-  if (threadIdx.x < G) a.chunk_best[(g * G + threadIdx.x) * a.nchunks + c] = best_s[threadIdx.x];
+  if (threadIdx.x < hpc) a.chunk_best[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = best_s[threadIdx.x];
 }
 
-__device__ void group_global_best(const AttnArgs& a, uint32_t g, uint32_t G, uint32_t nact,
-                                  unsigned long long* best_s) {
-  if (threadIdx.x < G) {
+// First maximum of each of the block's heads over the active chunks.
+__device__ void block_global_best(const AttnArgs& a, uint32_t h0, uint32_t nact, unsigned long long* best_s) {
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < a.hpc) {
+    const unsigned long long* cb = a.chunk_best + (size_t)(h0 + warp) * a.nchunks;
     unsigned long long b = 0;
-    const unsigned long long* cb = a.chunk_best + (size_t)(g * G + threadIdx.x) * a.nchunks;
-    for (uint32_t k = 0; k < nact; ++k) b = cb[k] > b ? cb[k] : b;
-    best_s[threadIdx.x] = b;
+    for (uint32_t k = lane; k < nact; k += 32) b = cb[k] > b ? cb[k] : b;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      unsigned long long o = __shfl_xor_sync(0xffffffffu, b, off);
+      b = o > b ? o : b;
+    }
+    if (lane == 0) best_s[warp] = b;
   }
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
-  __shared__ unsigned long long best_s[kMaxGroup];
-  __shared__ unsigned long long sum_s[kMaxGroup];
+  __shared__ unsigned long long best_s[kMaxHpc];
+  __shared__ unsigned long long sum_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
-  const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
-  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
+  const uint32_t n = p - ws + 1, nact = (n + kAttnChunk - 1) / kAttnChunk;
+  const uint32_t h0 = blockIdx.x * a.hpc, c = blockIdx.y;
   if (c >= nact) return;
-  group_global_best(a, g, G, nact, best_s);
-  if (threadIdx.x < G) sum_s[threadIdx.x] = 0;
+  block_global_best(a, h0, nact, best_s);
+  if (threadIdx.x < a.hpc) sum_s[threadIdx.x] = 0;
   __syncthreads();
-  const uint32_t hs = blockDim.x / a.chunk;
-  const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
-  const uint32_t t = ws + c * a.chunk + lp;
-  if (t <= p) {
-    for (uint32_t h = hg; h < G; h += hs) {
-      uint32_t hh = g * G + h;
-      int64_t e = softmax_exp_term_act(a.scores[(size_t)hh * a.cap + t], best_key_value(best_s[h]));
-      a.terms[(size_t)hh * a.cap + t] = e;
-      atomicAdd(&sum_s[h], (unsigned long long)e);
-    }
+  const uint32_t hl = threadIdx.x / kAttnChunk, t = ws + c * kAttnChunk + threadIdx.x % kAttnChunk;
+  uint64_t e = 0;
+  if (hl < a.hpc && t <= p) {
+    const size_t at = (size_t)(h0 + hl) * a.cap + t;
+    e = (uint64_t)softmax_exp_term_act(a.scores[at], best_key_value(best_s[hl]));
+    a.terms[at] = (int64_t)e;
   }
+  // 64 consecutive threads share a head: two warps, one shuffle sum each
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
+  if ((threadIdx.x & 31) == 0 && hl < a.hpc) atomicAdd(&sum_s[hl], e);
   __syncthreads();
-  if (threadIdx.x < G) a.chunk_sum[(g * G + threadIdx.x) * a.nchunks + c] = sum_s[threadIdx.x];
+  if (threadIdx.x < a.hpc) a.chunk_sum[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = sum_s[threadIdx.x];
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
-  extern __shared__ __align__(16) int32_t w_s[];  // [G][chunk]
-  __shared__ unsigned long long best_s[kMaxGroup];
-  __shared__ unsigned long long total_s[kMaxGroup];
-  __shared__ int32_t wsum_s[kMaxGroup];
+  __shared__ int32_t w_s[kMaxHpc * kAttnChunk];
+  __shared__ unsigned long long best_s[kMaxHpc];
+  __shared__ unsigned long long total_s[kMaxHpc];
+  __shared__ int32_t wsum_s[kMaxHpc];
   __shared__ bool last_s;
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
-  const uint32_t n = p - ws + 1, nact = (n + a.chunk - 1) / a.chunk;
-  const uint32_t G = a.heads / a.kv_heads, g = blockIdx.x, c = blockIdx.y;
-  const uint32_t t0 = ws + c * a.chunk;
+  const uint32_t n = p - ws + 1, nact = (n + kAttnChunk - 1) / kAttnChunk;
+  const uint32_t hpc = a.hpc, G = a.heads / a.kv_heads, h0 = blockIdx.x * hpc, g = h0 / G, d = a.d;
+  const uint32_t c = blockIdx.y, t0 = ws + c * kAttnChunk;
   if (c < nact) {
-    if (threadIdx.x < G) {
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < hpc) {
+      const uint64_t* cs = a.chunk_sum + (size_t)(h0 + warp) * a.nchunks;
       uint64_t tot = 0;
-      const uint64_t* cs = a.chunk_sum + (size_t)(g * G + threadIdx.x) * a.nchunks;
-      for (uint32_t k = 0; k < nact; ++k) tot += cs[k];
-      total_s[threadIdx.x] = tot;
-      wsum_s[threadIdx.x] = 0;
-    }
-    __syncthreads();
-    const uint32_t hs = blockDim.x / a.chunk;
-    const uint32_t lp = threadIdx.x % a.chunk, hg = threadIdx.x / a.chunk;
-    const uint32_t t = t0 + lp;
-    for (uint32_t h = hg; h < G; h += hs) {
-      int32_t w = 0;
-      if (t <= p) {
-        w = softmax_weight(a.terms[(size_t)(g * G + h) * a.cap + t], total_s[h]);
-        atomicAdd(&wsum_s[h], w);
+      for (uint32_t k = lane; k < nact; k += 32) tot += cs[k];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, off);
+      if (lane == 0) {
+        total_s[warp] = tot;
+        wsum_s[warp] = 0;
       }
-      w_s[h * a.chunk + lp] = w;
     }
     __syncthreads();
-    const uint32_t live = min(a.chunk, p + 1 - t0);
-    for (uint32_t o = threadIdx.x; o < G * a.d; o += blockDim.x) {
-      uint32_t h = o / a.d, i = o % a.d;
-      const int32_t* vcol = a.vcache + (size_t)t0 * a.kvd + g * a.d + i;
-      const int32_t* wrow = w_s + h * a.chunk;
+    const uint32_t hl = threadIdx.x / kAttnChunk, lp = threadIdx.x % kAttnChunk, t = t0 + lp;
+    if (hl < hpc) {
+      int32_t w = 0;
+      if (t <= p) w = softmax_weight(a.terms[(size_t)(h0 + hl) * a.cap + t], total_s[hl]);
+      w_s[hl * kAttnChunk + lp] = w;
+      int32_t ws_w = w;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ws_w += __shfl_xor_sync(0xffffffffu, ws_w, off);
+      if (lane == 0) atomicAdd(&wsum_s[hl], ws_w);
+    }
+    __syncthreads();
+    const uint32_t live = min(kAttnChunk, p + 1 - t0);
+    for (uint32_t o = threadIdx.x; o < hpc * d; o += blockDim.x) {
+      const uint32_t h = o / d, i = o % d;
+      const int32_t* vcol = a.vcache + (size_t)t0 * a.kvd + g * d + i;
+      const int32_t* wrow = w_s + h * kAttnChunk;
       int64_t acc = 0;
+#pragma unroll 8
       for (uint32_t j = 0; j < live; ++j)
         acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wrow[j] * vcol[(size_t)j * a.kvd]));
-      a.partial[((size_t)c * a.heads + g * G + h) * a.d + i] = acc;
+      a.partial[((size_t)c * a.heads + h0 + h) * d + i] = acc;
     }
-    if (threadIdx.x < G) a.chunk_wsum[(g * G + threadIdx.x) * a.nchunks + c] = wsum_s[threadIdx.x];
+    if (threadIdx.x < hpc) a.chunk_wsum[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = wsum_s[threadIdx.x];
   }
-  // The last block of this kv group combines the chunks.
+  // The last block of this head block combines the chunks.
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[g], 1u) == gridDim.y - 1;
+  if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[blockIdx.x], 1u) == gridDim.y - 1;
   __syncthreads();
   if (!last_s) return;
   __threadfence();
-  group_global_best(a, g, G, nact, best_s);
-  if (threadIdx.x < G) {
+  block_global_best(a, h0, nact, best_s);
+  if (threadIdx.x < hpc) {
     int32_t sw = 0;
-    const int32_t* cw = a.chunk_wsum + (size_t)(g * G + threadIdx.x) * a.nchunks;
+    const int32_t* cw = a.chunk_wsum + (size_t)(h0 + threadIdx.x) * a.nchunks;
     for (uint32_t k = 0; k < nact; ++k) sw += __ldcg(cw + k);
     wsum_s[threadIdx.x] = sub_sat(kOneAct, sw);  // residual (ops.rs:274-276)
   }
   __syncthreads();
-  const uint32_t qd = a.heads * a.d;
-  for (uint32_t o = threadIdx.x; o < G * a.d; o += blockDim.x) {
-    uint32_t h = o / a.d, i = o % a.d, hh = g * G + h;
+  const uint32_t qd = a.heads * d;
+  for (uint32_t o = threadIdx.x; o < hpc * d; o += blockDim.x) {
+    const uint32_t h = o / d, i = o % d, hh = h0 + h;
     int64_t acc = 0;
     for (uint32_t k = 0; k < nact; ++k)
-      acc = (int64_t)((uint64_t)acc + (uint64_t)ldcg_i64(a.partial + ((size_t)k * a.heads + hh) * a.d + i));
-    uint32_t tmax = best_key_token(best_s[h]);
-    acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wsum_s[h] * a.vcache[(size_t)tmax * a.kvd + g * a.d + i]));
-    int32_t v = requantize(acc);
-    put_planes(a.ctx_planes, qd, hh * a.d + i, v);
-    if (a.ctx) a.ctx[hh * a.d + i] = v;
+      acc = (int64_t)((uint64_t)acc + (uint64_t)ldcg_i64(a.partial + ((size_t)k * a.heads + hh) * d + i));
+    const uint32_t tmax = best_key_token(best_s[h]);
+    acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wsum_s[h] * a.vcache[(size_t)tmax * a.kvd + g * d + i]));
+    const int32_t v = requantize(acc);
+    put_planes(a.ctx_planes, qd, hh * d + i, v);
+    if (a.ctx) a.ctx[hh * d + i] = v;
   }
-  if (threadIdx.x == 0) a.counters[g] = 0;
+  if (threadIdx.x == 0) a.counters[blockIdx.x] = 0;
 }
 
+uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads) {
+  uint32_t G = heads / kv_heads, hpc = G < (uint32_t)kMaxHpc ? G : (uint32_t)kMaxHpc;
+  while (hpc > 1 && (G % hpc || heads / hpc < 8)) --hpc;
+  return hpc;
+}
+
+uint32_t attention_chunks(uint32_t cap) { return (cap + kAttnChunk - 1) / kAttnChunk; }
+
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
-  uint32_t G = a.heads / a.kv_heads;
-  if (G > kMaxGroup || a.d % 4 || kAttnThreads % a.chunk) return cudaErrorInvalidValue;
-  dim3 grid(a.kv_heads, a.nchunks);
-  attn_scores_kernel<<<grid, kAttnThreads, G * a.d * 4, s>>>(a);
+  const uint32_t G = a.heads / a.kv_heads;
+  if (a.d % 32 || a.d > 256 || a.hpc == 0 || a.hpc > (uint32_t)kMaxHpc || G % a.hpc) return cudaErrorInvalidValue;
+  dim3 grid(a.heads / a.hpc, a.nchunks);
+  attn_scores_kernel<<<grid, kAttnThreads, 0, s>>>(a);
   attn_exp_kernel<<<grid, kAttnThreads, 0, s>>>(a);
-  attn_out_kernel<<<grid, kAttnThreads, G * a.chunk * 4, s>>>(a);
+  attn_out_kernel<<<grid, kAttnThreads, 0, s>>>(a);
   return cudaGetLastError();
 }
 

@@ -30,9 +30,15 @@ struct AttnArgs {
   uint64_t* chunk_sum;             // [heads][nchunks]
   int32_t* chunk_wsum;             // [heads][nchunks]
   int64_t* partial;                // [nchunks][heads][d]
-  unsigned int* counters;          // [kv_heads], zero between launches
-  uint32_t cap, chunk, nchunks;
+  unsigned int* counters;          // [heads], zero between launches
+  uint32_t cap, nchunks;           // positions held; chunks of 64 positions
+  uint32_t hpc;                    // query heads a block (attention_hpc)
 };
+
+// Query heads a decode-attention block handles, and the chunk count for a
+// cache of `cap` positions (sizes of the scratch arrays above).
+uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads);
+uint32_t attention_chunks(uint32_t cap);
 
 // Decode (one query): three launches split over kv groups x position chunks.
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s);

@@ -137,7 +137,7 @@ struct IrisSession {
   int32_t* chunk_wsum = nullptr;
   int64_t* partial = nullptr;
   unsigned int* counters = nullptr;
-  uint32_t chunk = 0, nchunks = 0;
+  uint32_t nchunks = 0, hpc = 1;
   cudaStream_t stream = nullptr;
   cudaGraphExec_t graph = nullptr;
 };
@@ -188,16 +188,16 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
     if (e == cudaSuccess) e = dalloc(&s->ple_rows, (size_t)R * m->L * m->P);
     if (e == cudaSuccess) e = dalloc(&s->ple_proj, (size_t)R * m->L * m->P);
   }
-  s->chunk = m->kvh >= 4 ? 128 : 32;
-  s->nchunks = (cap + s->chunk - 1) / s->chunk;
+  s->nchunks = attention_chunks(cap);
+  s->hpc = attention_hpc(m->heads, m->kvh);
   if (e == cudaSuccess) e = dalloc(&s->scores, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->terms, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->chunk_best, (size_t)m->heads * s->nchunks);
   if (e == cudaSuccess) e = dalloc(&s->chunk_sum, (size_t)m->heads * s->nchunks);
   if (e == cudaSuccess) e = dalloc(&s->chunk_wsum, (size_t)m->heads * s->nchunks);
   if (e == cudaSuccess) e = dalloc(&s->partial, (size_t)s->nchunks * m->heads * m->d);
-  if (e == cudaSuccess) e = dalloc(&s->counters, m->kvh);
-  if (e == cudaSuccess) e = cudaMemset(s->counters, 0, m->kvh * sizeof(unsigned int));
+  if (e == cudaSuccess) e = dalloc(&s->counters, m->heads);
+  if (e == cudaSuccess) e = cudaMemset(s->counters, 0, m->heads * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemset(s->best, 0, R * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(s->d_pos, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(s->d_step, 0, 4);
@@ -235,8 +235,8 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   a.partial = s->partial;
   a.counters = s->counters;
   a.cap = s->cap;
-  a.chunk = s->chunk;
   a.nchunks = s->nchunks;
+  a.hpc = s->hpc;
   return a;
 }
 
@@ -418,6 +418,14 @@ cudaError_t run_pass(IrisSession* s, uint32_t tokens, const uint32_t* ids_dev, c
   return launch_product(h, IN_NORM, EPI_LOGITS, st, IRIS_PATH_GEMV);
 }
 
+// IRIS_ESTALL when a kernel recorded a given-up wait since the last check.
+int check_fault() {
+  uint32_t fault = 0;
+  cudaError_t e = take_device_fault(&fault);
+  if (e != cudaSuccess) return (int)e;
+  return fault ? IRIS_ESTALL : 0;
+}
+
 int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits, uint32_t* token) {
   IrisModel* m = s->m;
   if (n == 0) return IRIS_EINVAL;
@@ -437,6 +445,8 @@ int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits
   if (e == cudaSuccess) e = launch_fill_u64(s->best, 1, s->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
   if (e != cudaSuccess) return (int)e;
+  int rc = check_fault();
+  if (rc) return rc;
   s->len += n;
   s->has_logits = true;
   uint32_t tok = best_key_token(key);
@@ -904,12 +914,12 @@ int iris_generate(IrisSession* s, const uint32_t* prompt, uint32_t n_prompt, uin
         e = cudaMemcpy(s->d_token, &state[0], 4, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(s->d_pos, &state[1], 4, cudaMemcpyHostToDevice);
         *out_count = count;
-        return (int)e;
+        return e != cudaSuccess ? (int)e : check_fault();
       }
     }
   }
   *out_count = count;
-  return 0;
+  return check_fault();
 }
 
 uint32_t iris_session_length(const IrisSession* s) { return s ? s->len : 0; }
@@ -921,7 +931,9 @@ int iris_session_decode_steps(IrisSession* s, uint32_t steps) {
 
 int iris_session_synchronize(IrisSession* s) {
   if (!s) return IRIS_EINVAL;
-  return (int)cudaStreamSynchronize(s->stream);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return (int)e;
+  return check_fault();
 }
 
 void* iris_session_stream(IrisSession* s) { return s ? (void*)s->stream : nullptr; }

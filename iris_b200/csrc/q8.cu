@@ -396,12 +396,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a)
 // Decode GEMV, bulk-copy pipeline: one persistent block an SM
 // ---------------------------------------------------------------------------
 //
-// Each block owns a contiguous range of rows, taken in groups of up to 16
-// rows and, along K, in slices of up to 2048 columns. A producer warp streams
+// Each block owns a contiguous range of rows, taken in groups of up to 32
+// rows and, along K, in slices of up to 1024 columns. A producer warp streams
 // every (group, slice) tile - the rows' int8 values and fp16 scale bits -
 // from HBM into a ring of shared-memory stages with cp.async.bulk (TMA,
 // evict-first in L2), completing on the stage's "full" mbarrier. Eight
-// consumer warps, two rows each, run the dp4a byte-plane products against the
+// consumer warps, four rows each, run the dp4a byte-plane products against the
 // activation planes held in shared memory and release the stage on its
 // "empty" mbarrier. The activation prologue (planes, or the fused RMSNorm)
 // runs once per block while the first stages are already in flight. Every
@@ -413,7 +413,8 @@ __device__ unsigned int g_fault;
 constexpr int kTmaConsumerWarps = 8;
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;
 constexpr uint32_t kTmaMaxStages = 4;
-constexpr uint32_t kTmaGroupRows = 2 * kTmaConsumerWarps;
+constexpr int kTmaRowsPerWarp = 4;
+constexpr uint32_t kTmaGroupRows = kTmaRowsPerWarp * kTmaConsumerWarps;
 constexpr uint32_t kTmaSmemBudget = 220 * 1024;
 
 struct GemvPlan {
@@ -435,7 +436,7 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t spitch, int sms, GemvPlan* p)
   if (K % 32 || rows == 0) return false;
   p->kc = K;
   if (K % 256 == 0)
-    for (uint32_t kc = 2048; kc >= 256; kc /= 2)
+    for (uint32_t kc = 1024; kc >= 256; kc /= 2)
       if (K % kc == 0) { p->kc = kc; break; }
   p->nslices = K / p->kc;
   p->sbytes = p->nslices == 1 ? spitch * 2 : p->kc / 16;
@@ -543,36 +544,39 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   const uint4* P1 = P0 + K / 16;
   const uint4* P2 = P1 + K / 16;
   const uint4* P3 = P2 + K / 16;
-  const uint32_t lr0 = 2 * warp, lr1 = lr0 + 1, chunks = p.kc / 16;
-  Acc128 acc0{0, 0}, acc1{0, 0};
+  // Each lane takes whole 32-value blocks (two 16-byte chunks, one scale).
+  // Lanes 4-7 of every quarter-warp load the two chunks in the other order,
+  // so that each 8-lane phase of a 128-bit shared load touches 8 different
+  // 16-byte bank groups; the block sum does not depend on the order.
+  const uint32_t lr0 = kTmaRowsPerWarp * warp, blocks = p.kc / 32;
+  const uint32_t swap = (lane >> 2) & 1;
+  Acc128 acc[kTmaRowsPerWarp];
+#pragma unroll
+  for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
   for (uint32_t item = 0; item < nitems; ++item) {
     const uint32_t st = item % p.stages, use = item / p.stages;
     const uint32_t g = item / p.nslices, sl = item % p.nslices;
     const uint32_t row0 = r_begin + g * p.grows, nr = min(p.grows, r_end - row0);
     if (!mbar_wait_bounded(&full[st], use & 1, &g_fault)) return;
     if (lr0 < nr) {
-      const uint8_t* W0 = stage0 + st * p.stage_bytes + lr0 * p.kc;
-      const uint16_t* S0 = (const uint16_t*)(stage0 + st * p.stage_bytes + p.grows * p.kc + lr0 * p.sbytes);
-      const uint32_t cbase = sl * chunks;
-      if (lr1 < nr) {
-        const uint8_t* W1 = W0 + p.kc;
-        const uint16_t* S1 = S0 + p.sbytes / 2;
-        for (uint32_t c = lane; c < chunks; c += 32) {
-          const uint4 p0 = P0[cbase + c], p1 = P1[cbase + c], p2 = P2[cbase + c], p3 = P3[cbase + c];
-          const uint4 w0 = *(const uint4*)(W0 + c * 16), w1 = *(const uint4*)(W1 + c * 16);
-          int32_t m0, e0, m1, e1;
-          q8_scale_parts(S0[c >> 1], &m0, &e0);  // finite: checked at upload
-          q8_scale_parts(S1[c >> 1], &m1, &e1);
-          acc128_add_shifted(acc0, q8_partial16(w0, p0, p1, p2, p3) * m0, e0);
-          acc128_add_shifted(acc1, q8_partial16(w1, p0, p1, p2, p3) * m1, e1);
-        }
-      } else {
-        for (uint32_t c = lane; c < chunks; c += 32) {
-          const uint4 p0 = P0[cbase + c], p1 = P1[cbase + c], p2 = P2[cbase + c], p3 = P3[cbase + c];
-          const uint4 w0 = *(const uint4*)(W0 + c * 16);
-          int32_t m0, e0;
-          q8_scale_parts(S0[c >> 1], &m0, &e0);
-          acc128_add_shifted(acc0, q8_partial16(w0, p0, p1, p2, p3) * m0, e0);
+      const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * p.kc;
+      const uint16_t* S = (const uint16_t*)(stage0 + st * p.stage_bytes + p.grows * p.kc + lr0 * p.sbytes);
+      const uint32_t live = min((uint32_t)kTmaRowsPerWarp, nr - lr0);
+      const uint32_t cbase = sl * (p.kc / 16);
+      for (uint32_t b = lane; b < blocks; b += 32) {
+        const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
+        const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0], pa3 = P3[cbase + c0];
+        const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1], pb3 = P3[cbase + c1];
+#pragma unroll
+        for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+          if ((uint32_t)r < live) {
+            const uint8_t* Wr = W + r * p.kc;
+            const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
+            int32_t m, e;
+            q8_scale_parts(S[r * (p.sbytes / 2) + b], &m, &e);  // finite: checked at upload
+            const int64_t bs = q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
+            acc128_add_shifted(acc[r], bs * m, e);
+          }
         }
       }
     }
@@ -580,34 +584,36 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
     if (lane == 0) mbar_arrive(&empty[st]);
     if (sl + 1 == p.nslices) {
       if (lr0 < nr) {
-        acc0 = warp_sum_acc128(acc0);
-        acc1 = warp_sum_acc128(acc1);
-        if (lane == 0) {
-          const uint32_t row = row0 + lr0;
-          const int32_t v0 = acc128_round_q24(acc0);
-          const bool two = lr1 < nr;
-          const int32_t v1 = two ? acc128_round_q24(acc1) : 0;
-          if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-            if (two) epi_pair<EPI>(a, 0, row, v0, v1);
-          } else if (EPI == EPI_LOGITS) {
-            int32_t c0 = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
-            unsigned long long key = best_key(c0, row);
-            if (a.out) a.out[row] = c0;
-            if (two) {
-              int32_t c1 = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
-              if (a.out) a.out[row + 1] = c1;
-              unsigned long long k1 = best_key(c1, row + 1);
-              key = k1 > key ? k1 : key;
+        const uint32_t live = min((uint32_t)kTmaRowsPerWarp, nr - lr0);
+#pragma unroll
+        for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
+        const uint32_t row = row0 + lr0;
+        if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+#pragma unroll
+          for (int j = 0; j < kTmaRowsPerWarp / 2; ++j)
+            if (lane == (uint32_t)j && (uint32_t)(2 * j + 1) < live)
+              epi_pair<EPI>(a, 0, row + 2 * j, acc128_round_q24(acc[2 * j]), acc128_round_q24(acc[2 * j + 1]));
+        } else if (EPI == EPI_LOGITS) {
+          unsigned long long key = 0;
+#pragma unroll
+          for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+            if ((uint32_t)r < live) {
+              int32_t v = acc128_round_q24(acc[r]);
+              if (a.softcap > 0) v = softcap_act(v, a.softcap);
+              if (lane == (uint32_t)r && a.out) a.out[row + r] = v;
+              const unsigned long long k = best_key(v, row + r);
+              key = k > key ? k : key;
             }
-            atomicMax(a.best, key);
-          } else {
-            epi_single<EPI>(a, 0, row, v0);
-            if (two) epi_single<EPI>(a, 0, row + 1, v1);
           }
+          if (lane == 0) atomicMax(a.best, key);
+        } else {
+#pragma unroll
+          for (int r = 0; r < kTmaRowsPerWarp; ++r)
+            if (lane == (uint32_t)r && (uint32_t)r < live) epi_single<EPI>(a, 0, row + r, acc128_round_q24(acc[r]));
         }
       }
-      acc0 = Acc128{0, 0};
-      acc1 = Acc128{0, 0};
+#pragma unroll
+      for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
     }
   }
 }
@@ -876,6 +882,7 @@ const char* iris_error(int code) {
     case IRIS_ERANGE: return "iris: position out of range";
     case IRIS_ESTATE: return "iris: call out of order";
     case IRIS_EWINDOW: return "iris: attention window not covered by the keys";
+    case IRIS_ESTALL: return "iris: a kernel gave up a bounded wait (stalled pipeline)";
     default: return cudaGetErrorString((cudaError_t)code);
   }
 }
