@@ -322,14 +322,13 @@ cudaError_t prepare_layer_kernels() {
 // ---------------------------------------------------------------------------
 
 __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t cols,
-                             uint32_t spitch, const uint32_t* ids, int32_t scale, int has_scale, int32_t* out) {
+                             uint32_t kc, uint32_t nslices, const uint32_t* ids, int32_t scale, int has_scale,
+                             int32_t* out) {
   uint32_t t = blockIdx.x, id = ids[t];
-  const int8_t* row = q + (size_t)id * cols;
-  const uint16_t* srow = s + (size_t)id * spitch;
   for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
     int32_t m, e;
-    q8_scale_parts(srow[i >> 5], &m, &e);
-    int32_t v = q8_dequant(row[i], m, e);  // dequantize_row, q8.rs:76-91
+    q8_scale_parts(s[q8_scale_offset(kc, nslices, id, i >> 5)], &m, &e);
+    int32_t v = q8_dequant(q[q8_value_offset(kc, nslices, id, i)], m, e);  // dequantize_row, q8.rs:76-91
     if (has_scale) v = mul_sat(v, scale);   // model.rs:316-330 (gemma)
     out[(size_t)t * cols + i] = v;
   }
@@ -338,7 +337,8 @@ __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __res
 cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32_t tokens,
                          int has_scale, int32_t scale, int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, embed->spitch, d_ids, scale, has_scale,
+  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, embed->kc, embed->nslices, d_ids, scale,
+                                      has_scale,
                                       out);
   return cudaGetLastError();
 }
@@ -528,7 +528,7 @@ cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const i
 }
 
 __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, const uint16_t* es,
-                                   uint32_t ecols, uint32_t espitch, const uint32_t* ids, const int32_t* ple_norm,
+                                   uint32_t ekc, uint32_t enslices, const uint32_t* ids, const int32_t* ple_norm,
                                    int64_t eps, int32_t projection_scalar, int32_t embedding_scale,
                                    int32_t input_scale, uint32_t L, uint32_t P, int32_t* out) {
   extern __shared__ __align__(16) int32_t row[];  // [P]
@@ -541,8 +541,8 @@ __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, c
   for (uint32_t j = threadIdx.x; j < P; j += blockDim.x) {
     uint32_t col = l * P + j;
     int32_t m, e;
-    q8_scale_parts(es[(size_t)id * espitch + (col >> 5)], &m, &e);
-    int32_t v = mul_sat(q8_dequant(eq[(size_t)id * ecols + col], m, e), embedding_scale);
+    q8_scale_parts(es[q8_scale_offset(ekc, enslices, id, col >> 5)], &m, &e);
+    int32_t v = mul_sat(q8_dequant(eq[q8_value_offset(ekc, enslices, id, col)], m, e), embedding_scale);
     v = add_sat(v, row[j]);
     out[((size_t)t * L + l) * P + j] = mul_sat(v, input_scale);
   }
@@ -555,8 +555,8 @@ cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_
                                int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   dim3 grid(tokens, layers);
-  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->cols,
-                                              ple_embed->spitch, d_ids,
+  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->kc,
+                                              ple_embed->nslices, d_ids,
                                               ple_norm, eps, projection_scalar, embedding_scale,
                                               input_scale, layers, P, out);
   return cudaGetLastError();

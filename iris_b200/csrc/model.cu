@@ -240,16 +240,6 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   return a;
 }
 
-ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
-  ProductArgs a{};
-  a.q = w->q;
-  a.s = w->s;
-  a.spitch = w->spitch;
-  a.rows = w->rows;
-  a.cols = w->cols;
-  a.tokens = tokens;
-  return a;
-}
 
 // One mistral-dense layer (mistral/layer.rs:107-270) over `tokens` rows in
 // s->x at positions pos0.. (or *pos_ptr for the decode pass).

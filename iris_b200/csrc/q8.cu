@@ -9,11 +9,11 @@
 // the order in which lanes, warps or blocks combine partial sums never
 // changes a value.
 //
-// Two kernels:
-//  - q8_gemv_kernel: one token (the decode step). Each warp owns R rows and
-//    streams them with 128-bit non-allocating loads; activations sit in
-//    shared memory as byte planes, built either from planes in global memory
-//    or, fused, from the int32 row and its RMSNorm (ops.rs:98-114).
+// Kernels:
+//  - q8_gemv_tma_kernel: one token (the decode step). A persistent block an SM
+//    streams whole weight tiles (q8.cuh) from HBM through a ring of
+//    shared-memory stages with bulk copies (TMA) while eight consumer warps
+//    run the products against activation planes held in shared memory.
 //  - q8_gemm_kernel: many tokens (prefill, the chain's ranges), a 64-row x
 //    32-token tile per block staged through shared memory.
 // Both end in a fused epilogue (residual add, RoPE and K/V store, SiLU/GELU
@@ -32,55 +32,74 @@
 namespace iris {
 
 // ---------------------------------------------------------------------------
-// Upload / download / synthesis
+// Layout: allocation, upload, download, synthesis
 // ---------------------------------------------------------------------------
 
-__global__ void repack_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t rows, uint32_t cols,
-                                     uint32_t row_stride, uint32_t row_offset, int8_t* q,
-                                     uint16_t* s, uint32_t spitch, int* bad) {
-  uint32_t nb = cols / 32;
-  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Natural row-major int8 values and scale bits -> tiled layout.
+__global__ void tile_from_natural_kernel(const int8_t* __restrict__ q_nat, const uint16_t* __restrict__ s_nat,
+                                         uint32_t rows, uint32_t cols, uint32_t kc, uint32_t nslices, int8_t* q,
+                                         uint16_t* s, int* bad) {
+  const uint32_t nb = cols / 32;
+  const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
-  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
-  const uint8_t* src = raw + b * 34;
-  uint16_t bits = (uint16_t)(src[0] | (src[1] << 8));
+  const uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  const uint16_t bits = s_nat[b];
   if (((bits >> 10) & 0x1f) == 0x1f) atomicExch(bad, 1);
-  uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  s[dr * spitch + blk] = bits;
+  s[q8_scale_offset(kc, nslices, r, blk)] = bits;
+  const uint4* src = (const uint4*)(q_nat + (size_t)r * cols + (size_t)blk * 32);
+  uint4* dst = (uint4*)(q + q8_value_offset(kc, nslices, r, blk * 32));
+  dst[0] = src[0];
+  dst[1] = src[1];
+}
+
+// Raw 34-byte Q8_0 blocks -> rows (row_offset + i * row_stride) of the tiles.
+__global__ void tile_from_blocks_kernel(const uint8_t* __restrict__ raw, uint32_t rows, uint32_t cols,
+                                        uint32_t row_stride, uint32_t row_offset, uint32_t kc, uint32_t nslices,
+                                        int8_t* q, uint16_t* s, int* bad) {
+  const uint32_t nb = cols / 32;
+  const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= (uint64_t)rows * nb) return;
+  const uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  const uint8_t* src = raw + b * 34;
+  const uint16_t bits = (uint16_t)(src[0] | (src[1] << 8));
+  if (((bits >> 10) & 0x1f) == 0x1f) atomicExch(bad, 1);
+  const uint32_t dr = r * row_stride + row_offset;
+  s[q8_scale_offset(kc, nslices, dr, blk)] = bits;
   uint32_t w[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) |
-           ((uint32_t)src[4 + 4 * i] << 16) | ((uint32_t)src[5 + 4 * i] << 24);
-  uint4* dst = (uint4*)(q + dr * cols + (uint64_t)blk * 32);
+    w[i] = (uint32_t)src[2 + 4 * i] | ((uint32_t)src[3 + 4 * i] << 8) | ((uint32_t)src[4 + 4 * i] << 16) |
+           ((uint32_t)src[5 + 4 * i] << 24);
+  uint4* dst = (uint4*)(q + q8_value_offset(kc, nslices, dr, blk * 32));
   dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
   dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-__global__ void unpack_blocks_kernel(const int8_t* q, const uint16_t* s, uint32_t spitch, uint32_t rows,
-                                     uint32_t cols, uint32_t row_stride, uint32_t row_offset, uint8_t* raw) {
-  uint32_t nb = cols / 32;
-  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void blocks_from_tile_kernel(const int8_t* q, const uint16_t* s, uint32_t kc, uint32_t nslices,
+                                        uint32_t rows, uint32_t cols, uint32_t row_stride, uint32_t row_offset,
+                                        uint8_t* raw) {
+  const uint32_t nb = cols / 32;
+  const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
-  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
-  uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  uint16_t bits = s[dr * spitch + blk];
+  const uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  const uint32_t dr = r * row_stride + row_offset;
+  const uint16_t bits = s[q8_scale_offset(kc, nslices, dr, blk)];
   uint8_t* dst = raw + b * 34;
   dst[0] = (uint8_t)bits;
   dst[1] = (uint8_t)(bits >> 8);
-  const int8_t* src = q + dr * cols + (uint64_t)blk * 32;
+  const int8_t* src = q + q8_value_offset(kc, nslices, dr, blk * 32);
   for (int i = 0; i < 32; ++i) dst[2 + i] = (uint8_t)src[i];
 }
 
-__global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint32_t spitch, uint64_t seed, uint32_t tensor,
-                                int32_t layer, uint32_t rows, uint32_t cols, uint32_t row_stride,
+__global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint32_t kc, uint32_t nslices, uint64_t seed,
+                                uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols, uint32_t row_stride,
                                 uint32_t row_offset, int per_block) {
-  uint32_t nb = cols / 32;
-  uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t nb = cols / 32;
+  const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
-  uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
-  uint64_t dr = (uint64_t)r * row_stride + row_offset;
-  s[dr * spitch + blk] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
+  const uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
+  const uint32_t dr = r * row_stride + row_offset;
+  s[q8_scale_offset(kc, nslices, dr, blk)] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
   uint32_t w[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -90,7 +109,7 @@ __global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint32_t spitch, uint64_
       v |= (uint32_t)(uint8_t)synth_q(seed, tensor, layer, r, blk * 32 + i * 4 + j, cols) << (8 * j);
     w[i] = v;
   }
-  uint4* dst = (uint4*)(q + dr * cols + (uint64_t)blk * 32);
+  uint4* dst = (uint4*)(q + q8_value_offset(kc, nslices, dr, blk * 32));
   dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
   dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
@@ -109,11 +128,15 @@ Q8GpuMatrix* alloc_q8(uint32_t rows, uint32_t cols, cudaError_t* err) {
   }
   m->rows = rows;
   m->cols = cols;
-  m->spitch = q8_scale_pitch(cols);
+  m->kc = q8_slice_cols(cols);
+  m->nslices = cols / m->kc;
+  m->groups = (rows + kQ8TileRows - 1) / kQ8TileRows;
   m->owns = true;
-  *err = cudaMalloc((void**)&m->q, (size_t)rows * cols);
-  if (*err == cudaSuccess) *err = cudaMalloc((void**)&m->s, (size_t)rows * m->spitch * 2);
-  if (*err == cudaSuccess) *err = cudaMemset(m->s, 0, (size_t)rows * m->spitch * 2);
+  const size_t padded = (size_t)m->groups * kQ8TileRows;
+  *err = cudaMalloc((void**)&m->q, padded * cols);
+  if (*err == cudaSuccess) *err = cudaMemset(m->q, 0, padded * cols);
+  if (*err == cudaSuccess) *err = cudaMalloc((void**)&m->s, padded * (cols / 32) * 2);
+  if (*err == cudaSuccess) *err = cudaMemset(m->s, 0, padded * (cols / 32) * 2);
   if (*err != cudaSuccess) {
     free_q8(m);
     return nullptr;
@@ -130,6 +153,18 @@ void free_q8(Q8GpuMatrix* m) {
   std::free(m);
 }
 
+ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
+  ProductArgs a{};
+  a.q = w->q;
+  a.s = w->s;
+  a.rows = w->rows;
+  a.cols = w->cols;
+  a.kc = w->kc;
+  a.nslices = w->nslices;
+  a.tokens = tokens;
+  return a;
+}
+
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
                              uint32_t cols, uint32_t row_stride, uint32_t row_offset,
                              int* bad_scale) {
@@ -142,8 +177,8 @@ cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint3
   if (e == cudaSuccess) e = cudaMemcpy(staging, host_blocks, bytes, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) {
     uint64_t nblk = (uint64_t)rows * (cols / 32);
-    repack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(staging, rows, cols, row_stride,
-                                                                  row_offset, dst->q, dst->s, dst->spitch, bad);
+    tile_from_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(staging, rows, cols, row_stride, row_offset,
+                                                                     dst->kc, dst->nslices, dst->q, dst->s, bad);
     e = cudaGetLastError();
   }
   int h_bad = 0;
@@ -161,8 +196,8 @@ cudaError_t download_q8_blocks(const Q8GpuMatrix* src, uint8_t* host_blocks, uin
   cudaError_t e = cudaMalloc((void**)&staging, bytes);
   if (e == cudaSuccess) {
     uint64_t nblk = (uint64_t)rows * (cols / 32);
-    unpack_blocks_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(src->q, src->s, src->spitch, rows, cols,
-                                                                  row_stride, row_offset, staging);
+    blocks_from_tile_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(src->q, src->s, src->kc, src->nslices, rows,
+                                                                     cols, row_stride, row_offset, staging);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaMemcpy(host_blocks, staging, bytes, cudaMemcpyDeviceToHost);
@@ -175,7 +210,7 @@ cudaError_t synth_q8_rows(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int3
                           int per_block, cudaStream_t stream) {
   uint64_t nblk = (uint64_t)rows * (cols / 32);
   synth_q8_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream>>>(
-      dst->q, dst->s, dst->spitch, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
+      dst->q, dst->s, dst->kc, dst->nslices, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
   return cudaGetLastError();
 }
 
@@ -305,159 +340,51 @@ __device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uin
 }
 
 // ---------------------------------------------------------------------------
-// Decode GEMV: one token, R rows a warp
-// ---------------------------------------------------------------------------
-
-constexpr int kGemvWarps = 4;
-constexpr int kGemvRows = 4;  // rows a warp (even: paired epilogues)
-
-template <int R, int IN, int EPI>
-__global__ void __launch_bounds__(kGemvWarps * 32) q8_gemv_kernel(ProductArgs a) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint64_t red[32];
-  __shared__ int32_t s_scale;
-  const uint32_t K = a.cols;
-  if (IN == IN_PLANES) {
-    const uint4* src = (const uint4*)a.planes;
-    for (uint32_t i = threadIdx.x; i < K / 4; i += blockDim.x) ((uint4*)smem)[i] = src[i];
-  } else {
-    row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, smem, red, &s_scale);
-  }
-  __syncthreads();
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t row0 = (blockIdx.x * kGemvWarps + warp) * R;
-  if (row0 >= a.rows) return;
-  const uint4* P0 = (const uint4*)smem;
-  const uint4* P1 = P0 + K / 16;
-  const uint4* P2 = P1 + K / 16;
-  const uint4* P3 = P2 + K / 16;
-  const uint32_t nchunk = K / 16;
-  const int8_t* wrow = a.q + (size_t)row0 * K;
-  const uint16_t* srow = a.s + (size_t)row0 * a.spitch;
-  const uint32_t live = min((uint32_t)R, a.rows - row0);
-
-  Acc128 acc[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = Acc128{0, 0};
-
-#pragma unroll 2
-  for (uint32_t c = lane; c < nchunk; c += 32) {
-    uint4 w[R];
-    uint16_t sb[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if ((uint32_t)r < live) {
-        w[r] = ld_stream_v4(wrow + (size_t)r * K + (size_t)c * 16);
-        sb[r] = ld_stream_u16(srow + (size_t)r * a.spitch + (c >> 1));
-      } else {
-        w[r] = make_uint4(0, 0, 0, 0);
-        sb[r] = 0;
-      }
-    }
-    uint4 p0 = P0[c], p1 = P1[c], p2 = P2[c], p3 = P3[c];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      int64_t part = q8_partial16(w[r], p0, p1, p2, p3);
-      int32_t m, e;
-      q8_scale_parts(sb[r], &m, &e);  // finite: checked at upload
-      acc128_add_shifted(acc[r], part * m, e);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = warp_sum_acc128(acc[r]);
-
-  if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-#pragma unroll
-    for (int j = 0; j < R / 2; ++j)
-      if (lane == j && (uint32_t)(2 * j + 1) < live)
-        epi_pair<EPI>(a, 0, row0 + 2 * j, acc128_round_q24(acc[2 * j]), acc128_round_q24(acc[2 * j + 1]));
-  } else if (EPI == EPI_LOGITS) {
-    unsigned long long key = 0;
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      if ((uint32_t)r < live) {
-        int32_t v = acc128_round_q24(acc[r]);
-        if (a.softcap > 0) v = softcap_act(v, a.softcap);
-        if (lane == r && a.out) a.out[row0 + r] = v;
-        unsigned long long k = best_key(v, row0 + r);
-        key = k > key ? k : key;
-      }
-    }
-    if (lane == 0) atomicMax(a.best, key);
-  } else {
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-      if (lane == r && (uint32_t)r < live) epi_single<EPI>(a, 0, row0 + r, acc128_round_q24(acc[r]));
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Decode GEMV, bulk-copy pipeline: one persistent block an SM
 // ---------------------------------------------------------------------------
 //
-// Each block owns a contiguous range of rows, taken in groups of up to 32
-// rows and, along K, in slices of up to 1024 columns. A producer warp streams
-// every (group, slice) tile - the rows' int8 values and fp16 scale bits -
-// from HBM into a ring of shared-memory stages with cp.async.bulk (TMA,
-// evict-first in L2), completing on the stage's "full" mbarrier. Eight
-// consumer warps, four rows each, run the dp4a byte-plane products against the
-// activation planes held in shared memory and release the stage on its
-// "empty" mbarrier. The activation prologue (planes, or the fused RMSNorm)
-// runs once per block while the first stages are already in flight. Every
-// wait is bounded (about one second): a stalled pipeline records a fault and
-// the kernel returns instead of hanging.
+// A block owns a contiguous range of tile groups (16 rows each). A producer
+// warp streams every tile of its range - 16 rows x kc values and their scale
+// bits, two contiguous runs - from HBM into a ring of shared-memory stages
+// with cp.async.bulk (TMA, evict-first in L2), completing on the stage's
+// "full" mbarrier. Eight consumer warps, two rows each, run the dp4a
+// byte-plane products against the activation planes held in shared memory
+// and release the stage on its "empty" mbarrier. The activation prologue
+// (planes, or the fused RMSNorm) runs once per block while the first stages
+// are already in flight. Every wait is bounded (about one second): a stalled
+// pipeline records a fault and the kernel returns instead of hanging.
 
 __device__ unsigned int g_fault;
 
 constexpr int kTmaConsumerWarps = 8;
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;
-constexpr uint32_t kTmaMaxStages = 4;
-constexpr int kTmaRowsPerWarp = 4;
-constexpr uint32_t kTmaGroupRows = kTmaRowsPerWarp * kTmaConsumerWarps;
+constexpr int kTmaRowsPerWarp = kQ8TileRows / kTmaConsumerWarps;  // 2
+constexpr uint32_t kTmaMaxStages = 8;
 constexpr uint32_t kTmaSmemBudget = 220 * 1024;
 
 struct GemvPlan {
-  uint32_t kc;              // slice width
-  uint32_t nslices;         // K / kc
-  uint32_t sbytes;          // scale bytes a row contributes to a slice
-  uint32_t grows;           // rows a group (even)
   uint32_t stages;
-  uint32_t stage_bytes;     // grows * (kc + sbytes), rounded to 128
-  uint32_t planes_bytes;    // 4 K, rounded to 128
-  uint32_t rows_per_block;  // even
+  uint32_t stage_bytes;      // tile values (16 kc) + tile scales (kc), rounded to 128
+  uint32_t planes_bytes;     // 4 K, rounded to 128
+  uint32_t groups_per_block;
   uint32_t smem;
   uint32_t grid;
 };
 
 __host__ __device__ inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
 
-bool plan_gemv(uint32_t rows, uint32_t K, uint32_t spitch, int sms, GemvPlan* p) {
+bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, GemvPlan* p) {
   if (K % 32 || rows == 0) return false;
-  p->kc = K;
-  if (K % 256 == 0)
-    for (uint32_t kc = 1024; kc >= 256; kc /= 2)
-      if (K % kc == 0) { p->kc = kc; break; }
-  p->nslices = K / p->kc;
-  p->sbytes = p->nslices == 1 ? spitch * 2 : p->kc / 16;
   p->planes_bytes = round_up(4 * K, 128);
-  if (p->planes_bytes >= kTmaSmemBudget) return false;
-  p->grows = kTmaGroupRows;
-  while (true) {
-    p->stage_bytes = round_up(p->grows * (p->kc + p->sbytes), 128);
-    uint32_t fit = (kTmaSmemBudget - p->planes_bytes) / p->stage_bytes;
-    if (fit >= 2) {
-      p->stages = fit < kTmaMaxStages ? fit : kTmaMaxStages;
-      break;
-    }
-    if (p->grows == 2) return false;
-    p->grows -= 2;
-  }
+  p->stage_bytes = round_up(kQ8TileRows * kc + kc, 128);
+  if (p->planes_bytes + 2 * p->stage_bytes > kTmaSmemBudget) return false;
+  uint32_t fit = (kTmaSmemBudget - p->planes_bytes) / p->stage_bytes;
+  p->stages = fit < kTmaMaxStages ? fit : kTmaMaxStages;
   p->smem = p->planes_bytes + p->stages * p->stage_bytes;
-  uint32_t pairs = (rows + 1) / 2;
-  uint32_t grid = (uint32_t)sms < pairs ? (uint32_t)sms : pairs;
-  p->rows_per_block = round_up((rows + grid - 1) / grid, 2);
-  p->grid = (rows + p->rows_per_block - 1) / p->rows_per_block;
+  const uint32_t groups = (rows + kQ8TileRows - 1) / kQ8TileRows;
+  const uint32_t grid = (uint32_t)sms < groups ? (uint32_t)sms : groups;
+  p->groups_per_block = (groups + grid - 1) / grid;
+  p->grid = (groups + p->groups_per_block - 1) / p->groups_per_block;
   return true;
 }
 
@@ -468,15 +395,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   __shared__ __align__(8) uint64_t empty[kTmaMaxStages];
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
-  const uint32_t K = a.cols;
+  const uint32_t K = a.cols, kc = a.kc, S = a.nslices;
   uint8_t* planes = smem;
   uint8_t* stage0 = smem + p.planes_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool producer = warp == kTmaConsumerWarps;
-  const uint32_t r_begin = blockIdx.x * p.rows_per_block;
-  const uint32_t r_end = min(a.rows, r_begin + p.rows_per_block);
-  const uint32_t ngroups = r_begin < r_end ? (r_end - r_begin + p.grows - 1) / p.grows : 0;
-  const uint32_t nitems = ngroups * p.nslices;
+  const uint32_t groups = (a.rows + kQ8TileRows - 1) / kQ8TileRows;
+  const uint32_t g_begin = blockIdx.x * p.groups_per_block;
+  const uint32_t g_end = min(groups, g_begin + p.groups_per_block);
+  const uint32_t nitems = g_begin < g_end ? (g_end - g_begin) * S : 0;
 
   if (threadIdx.x == 0) {
     for (uint32_t st = 0; st < p.stages; ++st) {
@@ -488,23 +415,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   __syncthreads();
 
   const uint64_t policy = l2_evict_first_policy();
+  // Item i is tile (g_begin + i / S, i % S): tiles of a range are consecutive
+  // in memory, so item i starts at tile index g_begin * S + i.
   auto issue = [&](uint32_t item) {
-    const uint32_t st = item % p.stages, g = item / p.nslices, sl = item % p.nslices;
-    const uint32_t row0 = r_begin + g * p.grows, nr = min(p.grows, r_end - row0);
-    uint8_t* wdst = stage0 + st * p.stage_bytes;
-    uint8_t* sdst = wdst + p.grows * p.kc;
-    const uint8_t* sbase = (const uint8_t*)a.s;
-    mbar_arrive_expect_tx(&full[st], nr * (p.kc + p.sbytes));
-    if (p.nslices == 1) {  // whole rows: one copy each for values and scales
-      bulk_load(wdst, a.q + (size_t)row0 * K, nr * K, &full[st], policy);
-      bulk_load(sdst, sbase + (size_t)row0 * a.spitch * 2, nr * p.sbytes, &full[st], policy);
-    } else {
-      for (uint32_t r = 0; r < nr; ++r) {
-        bulk_load(wdst + r * p.kc, a.q + (size_t)(row0 + r) * K + (size_t)sl * p.kc, p.kc, &full[st], policy);
-        bulk_load(sdst + r * p.sbytes, sbase + (size_t)(row0 + r) * a.spitch * 2 + (size_t)sl * p.sbytes,
-                  p.sbytes, &full[st], policy);
-      }
-    }
+    const uint32_t st = item % p.stages;
+    const size_t tile = (size_t)g_begin * S + item;
+    uint8_t* dst = stage0 + st * p.stage_bytes;
+    mbar_arrive_expect_tx(&full[st], kQ8TileRows * kc + kc);
+    bulk_load(dst, a.q + tile * kQ8TileRows * kc, kQ8TileRows * kc, &full[st], policy);
+    bulk_load(dst + kQ8TileRows * kc, (const uint8_t*)a.s + tile * kc, kc, &full[st], policy);
   };
 
   // The first stages need no release: issue them before the prologue.
@@ -548,68 +467,60 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   // Lanes 4-7 of every quarter-warp load the two chunks in the other order,
   // so that each 8-lane phase of a 128-bit shared load touches 8 different
   // 16-byte bank groups; the block sum does not depend on the order.
-  const uint32_t lr0 = kTmaRowsPerWarp * warp, blocks = p.kc / 32;
-  const uint32_t swap = (lane >> 2) & 1;
+  const uint32_t lr0 = kTmaRowsPerWarp * warp, blocks = kc / 32, swap = (lane >> 2) & 1;
   Acc128 acc[kTmaRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
   for (uint32_t item = 0; item < nitems; ++item) {
-    const uint32_t st = item % p.stages, use = item / p.stages;
-    const uint32_t g = item / p.nslices, sl = item % p.nslices;
-    const uint32_t row0 = r_begin + g * p.grows, nr = min(p.grows, r_end - row0);
+    const uint32_t st = item % p.stages, use = item / p.stages, sl = item % S;
+    const uint32_t row0 = (g_begin + item / S) * kQ8TileRows;
     if (!mbar_wait_bounded(&full[st], use & 1, &g_fault)) return;
-    if (lr0 < nr) {
-      const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * p.kc;
-      const uint16_t* S = (const uint16_t*)(stage0 + st * p.stage_bytes + p.grows * p.kc + lr0 * p.sbytes);
-      const uint32_t live = min((uint32_t)kTmaRowsPerWarp, nr - lr0);
-      const uint32_t cbase = sl * (p.kc / 16);
-      for (uint32_t b = lane; b < blocks; b += 32) {
-        const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
-        const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0], pa3 = P3[cbase + c0];
-        const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1], pb3 = P3[cbase + c1];
+    const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * kc;
+    const uint16_t* Sc = (const uint16_t*)(stage0 + st * p.stage_bytes + kQ8TileRows * kc) + lr0 * blocks;
+    const uint32_t cbase = sl * (kc / 16);
+#pragma unroll 2
+    for (uint32_t b = lane; b < blocks; b += 32) {
+      const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
+      const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0], pa3 = P3[cbase + c0];
+      const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1], pb3 = P3[cbase + c1];
 #pragma unroll
-        for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-          if ((uint32_t)r < live) {
-            const uint8_t* Wr = W + r * p.kc;
-            const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
-            int32_t m, e;
-            q8_scale_parts(S[r * (p.sbytes / 2) + b], &m, &e);  // finite: checked at upload
-            const int64_t bs = q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
-            acc128_add_shifted(acc[r], bs * m, e);
-          }
-        }
+      for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+        const uint8_t* Wr = W + r * kc;
+        const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
+        int32_t m, e;
+        q8_scale_parts(Sc[r * blocks + b], &m, &e);  // finite: checked at upload (padding rows: 0)
+        const int64_t bs = q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
+        acc128_add_shifted(acc[r], bs * m, e);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
-    if (sl + 1 == p.nslices) {
-      if (lr0 < nr) {
-        const uint32_t live = min((uint32_t)kTmaRowsPerWarp, nr - lr0);
+    if (sl + 1 == S) {
+      const uint32_t row = row0 + lr0;
+      if (row < a.rows) {
+        const uint32_t live = min((uint32_t)kTmaRowsPerWarp, a.rows - row);
 #pragma unroll
         for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
-        const uint32_t row = row0 + lr0;
-        if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-#pragma unroll
-          for (int j = 0; j < kTmaRowsPerWarp / 2; ++j)
-            if (lane == (uint32_t)j && (uint32_t)(2 * j + 1) < live)
-              epi_pair<EPI>(a, 0, row + 2 * j, acc128_round_q24(acc[2 * j]), acc128_round_q24(acc[2 * j + 1]));
-        } else if (EPI == EPI_LOGITS) {
-          unsigned long long key = 0;
-#pragma unroll
-          for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-            if ((uint32_t)r < live) {
-              int32_t v = acc128_round_q24(acc[r]);
-              if (a.softcap > 0) v = softcap_act(v, a.softcap);
-              if (lane == (uint32_t)r && a.out) a.out[row + r] = v;
-              const unsigned long long k = best_key(v, row + r);
-              key = k > key ? k : key;
+        if (lane == 0) {
+          const int32_t v0 = acc128_round_q24(acc[0]);
+          const int32_t v1 = live > 1 ? acc128_round_q24(acc[1]) : 0;
+          if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+            if (live > 1) epi_pair<EPI>(a, 0, row, v0, v1);
+          } else if (EPI == EPI_LOGITS) {
+            const int32_t c0v = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
+            unsigned long long key = best_key(c0v, row);
+            if (a.out) a.out[row] = c0v;
+            if (live > 1) {
+              const int32_t c1v = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
+              if (a.out) a.out[row + 1] = c1v;
+              const unsigned long long k1 = best_key(c1v, row + 1);
+              key = k1 > key ? k1 : key;
             }
+            atomicMax(a.best, key);
+          } else {
+            epi_single<EPI>(a, 0, row, v0);
+            if (live > 1) epi_single<EPI>(a, 0, row + 1, v1);
           }
-          if (lane == 0) atomicMax(a.best, key);
-        } else {
-#pragma unroll
-          for (int r = 0; r < kTmaRowsPerWarp; ++r)
-            if (lane == (uint32_t)r && (uint32_t)r < live) epi_single<EPI>(a, 0, row + r, acc128_round_q24(acc[r]));
         }
       }
 #pragma unroll
@@ -650,13 +561,13 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
     if (tid < 128) {
       int r = tid >> 1, h = tid & 1;
       uint32_t row = n0 + r;
-      uint4 v = row < a.rows ? ld_stream_v4(a.q + (size_t)row * K + kb * 32 + h * 16)
+      uint4 v = row < a.rows ? ld_stream_v4(a.q + q8_value_offset(a.kc, a.nslices, row, kb * 32) + h * 16)
                              : make_uint4(0, 0, 0, 0);
       *(uint4*)(sw + r * kWPitch + h * 16) = v;
     } else if (tid < 128 + kTileN) {
       int r = tid - 128;
       uint32_t row = n0 + r;
-      ssc[r] = row < a.rows ? a.s[(size_t)row * a.spitch + kb] : (uint16_t)0;
+      ssc[r] = row < a.rows ? a.s[q8_scale_offset(a.kc, a.nslices, row, kb)] : (uint16_t)0;
     }
     {
       int t = tid >> 3, p = (tid >> 1) & 3, h = tid & 1;
@@ -716,8 +627,6 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
 // Launchers
 // ---------------------------------------------------------------------------
 
-constexpr size_t kGemvMaxSmem = 200 * 1024;  // activations up to 51200 wide
-
 int g_sms = 0;  // multiprocessors of the current device
 
 int device_sms() {
@@ -733,38 +642,25 @@ int device_sms() {
 template <int IN, int EPI>
 cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
   GemvPlan p;
-  if (plan_gemv(a.rows, a.cols, a.spitch, device_sms(), &p)) {
-    q8_gemv_tma_kernel<IN, EPI><<<p.grid, kTmaThreads, p.smem, stream>>>(a, p);
-    return cudaGetLastError();
-  }
-  // Shapes whose tiles do not fit the shared-memory ring: the direct-load GEMV.
-  auto kern = q8_gemv_kernel<kGemvRows, IN, EPI>;
-  size_t smem = (size_t)a.cols * 4;
-  if (smem > kGemvMaxSmem) return cudaErrorInvalidValue;
-  unsigned rows_per_block = kGemvWarps * kGemvRows;
-  unsigned grid = (a.rows + rows_per_block - 1) / rows_per_block;
-  kern<<<grid, kGemvWarps * 32, smem, stream>>>(a);
+  if (!plan_gemv(a.rows, a.cols, a.kc, device_sms(), &p)) return cudaErrorInvalidValue;
+  q8_gemv_tma_kernel<IN, EPI><<<p.grid, kTmaThreads, p.smem, stream>>>(a, p);
   return cudaGetLastError();
 }
 
 template <int IN, int EPI>
-cudaError_t prepare_gemv_pair() {
-  cudaError_t e = cudaFuncSetAttribute(q8_gemv_kernel<kGemvRows, IN, EPI>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemvMaxSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kTmaSmemBudget);
-  return e;
+cudaError_t prepare_gemv_one() {
+  return cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kTmaSmemBudget);
 }
 
 template <int IN>
 cudaError_t prepare_gemv_in() {
-  cudaError_t e = prepare_gemv_pair<IN, EPI_STORE>();
-  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_RESID>();
-  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_QKV_ROPE>();
-  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_SILU_MUL>();
-  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_GELU_MUL>();
-  if (e == cudaSuccess) e = prepare_gemv_pair<IN, EPI_LOGITS>();
+  cudaError_t e = prepare_gemv_one<IN, EPI_STORE>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_RESID>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_QKV_ROPE>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_SILU_MUL>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_GELU_MUL>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_LOGITS>();
   return e;
 }
 
@@ -802,7 +698,7 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
   ProductArgs a = a0;
   if (a.out_stride == 0) a.out_stride = a.rows;
   if (a.tokens == 0 || a.rows == 0) return cudaSuccess;
-  if (a.cols == 0 || a.cols % 32) return cudaErrorInvalidValue;
+  if (a.cols == 0 || a.cols % 32 || a.kc == 0) return cudaErrorInvalidValue;
   bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
   if (gemv) {
     if (a.tokens != 1) return cudaErrorInvalidValue;
@@ -911,10 +807,24 @@ int q8gpu_upload(const int8_t* weights, const int64_t* scales_q24, uint32_t rows
   cudaError_t e;
   Q8GpuMatrix* m = alloc_q8(rows, cols, &e);
   if (!m) return (int)e;
-  e = cudaMemcpy(m->q, weights, (size_t)rows * cols, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess)
-    e = cudaMemcpy2D(m->s, (size_t)m->spitch * 2, bits.data(), (size_t)(cols / 32) * 2, (size_t)(cols / 32) * 2,
-                     rows, cudaMemcpyHostToDevice);
+  int8_t* q_nat = nullptr;
+  uint16_t* s_nat = nullptr;
+  int* bad = nullptr;
+  e = cudaMalloc((void**)&q_nat, (size_t)rows * cols);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&s_nat, nblk * 2);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&bad, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(bad, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpy(q_nat, weights, (size_t)rows * cols, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(s_nat, bits.data(), nblk * 2, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) {
+    tile_from_natural_kernel<<<(unsigned)((nblk + 255) / 256), 256>>>(q_nat, s_nat, rows, cols, m->kc, m->nslices,
+                                                                      m->q, m->s, bad);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(q_nat);
+  cudaFree(s_nat);
+  cudaFree(bad);
   if (e != cudaSuccess) {
     free_q8(m);
     return (int)e;
@@ -944,13 +854,7 @@ int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint
                                 int32_t* d_out, void* stream, int path) {
   if (!m || tokens == 0) return tokens == 0 ? 0 : IRIS_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;
-  ProductArgs a{};
-  a.q = m->q;
-  a.s = m->s;
-  a.spitch = m->spitch;
-  a.rows = m->rows;
-  a.cols = m->cols;
-  a.tokens = tokens;
+  ProductArgs a = product_args(m, tokens);
   a.out = d_out;
   bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
   if (gemv) {
@@ -982,13 +886,7 @@ int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tok
   if (e == cudaSuccess && tokens > 1) e = reserve(&g_planes, &g_planes_bytes, act_bytes);
   if (e == cudaSuccess) e = cudaMemcpy(g_act, activations, act_bytes, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return (int)e;
-  ProductArgs a{};
-  a.q = m->q;
-  a.s = m->s;
-  a.spitch = m->spitch;
-  a.rows = m->rows;
-  a.cols = m->cols;
-  a.tokens = tokens;
+  ProductArgs a = product_args(m, tokens);
   a.out = g_out;
   if (tokens == 1) {
     a.x = g_act;

@@ -5,19 +5,51 @@
 
 #include "common.cuh"
 
-// Repacked device layout of a Q8_0 matrix: the 34-byte GGUF blocks split into
-// int8 values [rows][cols] (16-byte aligned rows, coalesced 128-bit loads and
-// bulk copies) and fp16 scale bits [rows][spitch], spitch = cols/32 rounded
-// up to 8 entries so that every row of scales starts on a 16-byte boundary.
-// 1.0625 bytes a weight, as in Q8_0, for the widths models use.
+// Device layout of a Q8_0 matrix, chosen for the products that stream it.
+//
+// The 34-byte GGUF blocks are split into int8 values and fp16 scale bits, and
+// both are stored tile by tile: a tile is kQ8TileRows consecutive rows times
+// kc consecutive columns (a "slice", kc a multiple of 32 dividing cols), and
+// the tiles of a matrix follow each other group-major, slice-minor:
+//
+//   values: tile (g, s) at ((g * nslices + s) * kQ8TileRows) * kc bytes,
+//           row r of the tile at + r * kc, column c of the slice at + c;
+//   scales: tile (g, s) at ((g * nslices + s) * kQ8TileRows) * (kc / 32)
+//           entries, row r at + r * (kc / 32), block b of the slice at + b.
+//
+// So every tile is one contiguous run of values (16 kc bytes) and one of
+// scales (kc bytes): the decode GEMV moves a tile with two bulk copies. The
+// rows are padded to a whole tile group with zeros. 1.0625 bytes a weight.
+constexpr uint32_t kQ8TileRows = 16;
+
 struct Q8GpuMatrix {
   int8_t* q;
   uint16_t* s;
-  uint32_t rows, cols, spitch;
+  uint32_t rows, cols;
+  uint32_t kc, nslices, groups;
   bool owns;
 };
 
 namespace iris {
+
+// Slice width for a matrix of `cols` columns (cols a multiple of 32).
+__host__ __device__ inline uint32_t q8_slice_cols(uint32_t cols) {
+  if (cols % 2048 == 0) return 2048;
+  if (cols % 1024 == 0) return 1024;
+  if (cols <= 2048) return cols;
+  for (uint32_t kc = 2048; kc >= 32; kc -= 32)
+    if (cols % kc == 0) return kc;
+  return 32;
+}
+__host__ __device__ inline size_t q8_value_offset(uint32_t kc, uint32_t nslices, uint32_t row, uint32_t col) {
+  size_t tile = (size_t)(row / kQ8TileRows) * nslices + col / kc;
+  return (tile * kQ8TileRows + row % kQ8TileRows) * kc + col % kc;
+}
+__host__ __device__ inline size_t q8_scale_offset(uint32_t kc, uint32_t nslices, uint32_t row, uint32_t block) {
+  const uint32_t bps = kc / 32;
+  size_t tile = (size_t)(row / kQ8TileRows) * nslices + block / bps;
+  return (tile * kQ8TileRows + row % kQ8TileRows) * bps + block % bps;
+}
 
 enum InMode { IN_PLANES = 0, IN_NORM = 1, IN_RAW = 2 };
 enum EpiMode {
@@ -29,13 +61,11 @@ enum EpiMode {
   EPI_LOGITS = 5     // logits (+softcap) and a first-maximum key
 };
 
-__host__ __device__ inline uint32_t q8_scale_pitch(uint32_t cols) { return ((cols / 32 + 7) / 8) * 8; }
-
 struct ProductArgs {
   const int8_t* q;
   const uint16_t* s;
   uint32_t rows, cols, tokens;
-  uint32_t spitch;         // scale entries per row (q8_scale_pitch(cols))
+  uint32_t kc, nslices;    // tile layout of q and s
   // input: planes [tokens][4][cols], or raw / to-be-normed int32 [tokens][cols]
   const uint8_t* planes;
   const int32_t* x;
@@ -55,6 +85,8 @@ struct ProductArgs {
   unsigned long long* best;  // first-maximum key per token
   int32_t softcap;
 };
+
+ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);
 
 // Launches the product over args.tokens tokens: the decode GEMV for one token,
 // the tiled GEMM otherwise (path forces one of them).
