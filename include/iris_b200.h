@@ -189,6 +189,10 @@ uint32_t iris_session_graph_kernels(IrisSession* session);
  * (which: 0 = fused q|k|v, 1 = o, 2 = gate|up, 3 = down, 4 = head) with the
  * session's current activations; the result is discarded. For timing. */
 int iris_session_product(IrisSession* session, uint32_t layer, int which);
+/* Launches one single-query attention of layer `layer` on the session's
+ * stream: the last held position attends over the positions before it, with
+ * the session's current query rows; the context is discarded. For timing. */
+int iris_session_attention(IrisSession* session, uint32_t layer);
 /* Reads count K/V rows of one layer starting at position first
  * (kv_heads*head_dim values each). For a gemma sliding layer these are the
  * positions the window still holds. */

@@ -85,6 +85,7 @@ SIGNATURES = {
     "iris_session_stream": (vp, [vp]),
     "iris_session_graph_kernels": (C.c_uint32, [vp]),
     "iris_session_product": (C.c_int, [vp, C.c_uint32, C.c_int]),
+    "iris_session_attention": (C.c_int, [vp, C.c_uint32]),
     "iris_session_get_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i32p, i32p]),
     "iris_session_free": (None, [vp]),
     "iris_mistral_layer_range": (C.c_int, [vp, C.c_uint32, i32p, C.c_uint32, C.c_uint32, i32p, i32p,

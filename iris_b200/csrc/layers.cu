@@ -8,10 +8,11 @@
 //      chunk sums (exact: every term is at most 2^32, so the i64 sum of fewer
 //      than 2^31 terms cannot saturate);
 //   3. weights requantize((term << 32) / sum) (ties to even), the chunk's
-//      weighted value sums (wrapping i64, order-free) and weight sums; the
-//      last block adds the residual 1.0 - sum(weights) times the first
-//      maximum's value row (the same as adding it to that weight first,
-//      since no weight saturates) and requantizes.
+//      weighted value sums and weight sums added atomically into per-head
+//      totals (wrapping i64, order-free); the last block adds the residual
+//      1.0 - sum(weights) times the first maximum's value row (the same as
+//      adding it to that weight first, since no weight saturates) and
+//      requantizes.
 #include <cuda_runtime.h>
 
 #include "layers.cuh"
@@ -175,6 +176,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
       if (lane == 0) atomicAdd(&wsum_s[hl], ws_w);
     }
     __syncthreads();
+    // This chunk's weighted value sums go straight into the head's running
+    // total: wrapping 64-bit addition is exact in any order.
     const uint32_t live = min(kAttnChunk, p + 1 - t0);
     for (uint32_t o = threadIdx.x; o < hpc * d; o += blockDim.x) {
       const uint32_t h = o / d, i = o % d;
@@ -184,11 +187,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
 #pragma unroll 8
       for (uint32_t j = 0; j < live; ++j)
         acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wrow[j] * vcol[(size_t)j * a.kvd]));
-      a.partial[((size_t)c * a.heads + h0 + h) * d + i] = acc;
+      atomicAdd((unsigned long long*)(a.acc + (size_t)(h0 + h) * d + i), (unsigned long long)acc);
     }
-    if (threadIdx.x < hpc) a.chunk_wsum[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = wsum_s[threadIdx.x];
+    if (threadIdx.x < hpc) atomicAdd(a.wsum + h0 + threadIdx.x, wsum_s[threadIdx.x]);
   }
-  // The last block of this head block combines the chunks.
+  // The last block of this head block finishes the heads and clears the totals.
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) last_s = atomicAdd(&a.counters[blockIdx.x], 1u) == gridDim.y - 1;
@@ -196,19 +199,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
   if (!last_s) return;
   __threadfence();
   block_global_best(a, h0, nact, best_s);
-  if (threadIdx.x < hpc) {
-    int32_t sw = 0;
-    const int32_t* cw = a.chunk_wsum + (size_t)(h0 + threadIdx.x) * a.nchunks;
-    for (uint32_t k = 0; k < nact; ++k) sw += __ldcg(cw + k);
-    wsum_s[threadIdx.x] = sub_sat(kOneAct, sw);  // residual (ops.rs:274-276)
-  }
+  if (threadIdx.x < hpc)  // residual 1.0 - sum of weights (ops.rs:274-276)
+    wsum_s[threadIdx.x] = sub_sat(kOneAct, (int32_t)atomicExch((unsigned int*)(a.wsum + h0 + threadIdx.x), 0u));
   __syncthreads();
   const uint32_t qd = a.heads * d;
   for (uint32_t o = threadIdx.x; o < hpc * d; o += blockDim.x) {
     const uint32_t h = o / d, i = o % d, hh = h0 + h;
-    int64_t acc = 0;
-    for (uint32_t k = 0; k < nact; ++k)
-      acc = (int64_t)((uint64_t)acc + (uint64_t)ldcg_i64(a.partial + ((size_t)k * a.heads + hh) * d + i));
+    int64_t acc = (int64_t)atomicExch((unsigned long long*)(a.acc + (size_t)hh * d + i), 0ull);
     const uint32_t tmax = best_key_token(best_s[h]);
     acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wsum_s[h] * a.vcache[(size_t)tmax * a.kvd + g * d + i]));
     const int32_t v = requantize(acc);

@@ -28,8 +28,8 @@ struct AttnArgs {
   int64_t* terms;                  // [heads][cap]
   unsigned long long* chunk_best;  // [heads][nchunks]
   uint64_t* chunk_sum;             // [heads][nchunks]
-  int32_t* chunk_wsum;             // [heads][nchunks]
-  int64_t* partial;                // [nchunks][heads][d]
+  int32_t* wsum;                   // [heads], zero between launches
+  int64_t* acc;                    // [heads][d], zero between launches
   unsigned int* counters;          // [heads], zero between launches
   uint32_t cap, nchunks;           // positions held; chunks of 64 positions
   uint32_t hpc;                    // query heads a block (attention_hpc)

@@ -134,8 +134,8 @@ struct IrisSession {
   int64_t* terms = nullptr;
   unsigned long long* chunk_best = nullptr;
   uint64_t* chunk_sum = nullptr;
-  int32_t* chunk_wsum = nullptr;
-  int64_t* partial = nullptr;
+  int32_t* wsum = nullptr;
+  int64_t* acc = nullptr;
   unsigned int* counters = nullptr;
   uint32_t nchunks = 0, hpc = 1;
   cudaStream_t stream = nullptr;
@@ -151,8 +151,8 @@ void free_session(IrisSession* s) {
   if (s->graph) cudaGraphExecDestroy(s->graph);
   void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
-                  s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->chunk_wsum,
-                  s->partial, s->counters};
+                  s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
+                  s->acc, s->counters};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -194,8 +194,10 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   if (e == cudaSuccess) e = dalloc(&s->terms, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->chunk_best, (size_t)m->heads * s->nchunks);
   if (e == cudaSuccess) e = dalloc(&s->chunk_sum, (size_t)m->heads * s->nchunks);
-  if (e == cudaSuccess) e = dalloc(&s->chunk_wsum, (size_t)m->heads * s->nchunks);
-  if (e == cudaSuccess) e = dalloc(&s->partial, (size_t)s->nchunks * m->heads * m->d);
+  if (e == cudaSuccess) e = dalloc(&s->wsum, m->heads);
+  if (e == cudaSuccess) e = dalloc(&s->acc, (size_t)m->heads * m->d);
+  if (e == cudaSuccess) e = cudaMemset(s->wsum, 0, m->heads * sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaMemset(s->acc, 0, (size_t)m->heads * m->d * sizeof(int64_t));
   if (e == cudaSuccess) e = dalloc(&s->counters, m->heads);
   if (e == cudaSuccess) e = cudaMemset(s->counters, 0, m->heads * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemset(s->best, 0, R * sizeof(unsigned long long));
@@ -231,8 +233,8 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   a.terms = s->terms;
   a.chunk_best = s->chunk_best;
   a.chunk_sum = s->chunk_sum;
-  a.chunk_wsum = s->chunk_wsum;
-  a.partial = s->partial;
+  a.wsum = s->wsum;
+  a.acc = s->acc;
   a.counters = s->counters;
   a.cap = s->cap;
   a.nchunks = s->nchunks;
@@ -949,6 +951,12 @@ uint32_t iris_session_graph_kernels(IrisSession* s) {
   }
   cudaGraphDestroy(g);
   return kernels;
+}
+
+int iris_session_attention(IrisSession* s, uint32_t layer) {
+  if (!s || layer >= s->m->L || s->len == 0) return IRIS_EINVAL;
+  AttnArgs a = attn_args(s, layer, nullptr, s->len - 1);
+  return (int)launch_attention_decode(a, s->stream);
 }
 
 int iris_session_product(IrisSession* s, uint32_t layer, int which) {

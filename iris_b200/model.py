@@ -242,6 +242,10 @@ class Session:
     def product(self, layer: int, which: int) -> None:
         check(lib().iris_session_product(self._h, layer, which), "iris_session_product")
 
+    def attention(self, layer: int) -> None:
+        """Launches one single-query attention of `layer` (for timing)."""
+        check(lib().iris_session_attention(self._h, layer), "iris_session_attention")
+
     def kv(self, layer: int, first: int, count: int):
         kvd = self.model.cfg.kv_heads * self.model.cfg.head_dim
         k = np.empty((count, kvd), np.int32)
