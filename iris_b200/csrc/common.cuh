@@ -132,6 +132,31 @@ __device__ __forceinline__ int64_t q8_partial16(uint4 w, uint4 p0, uint4 p1, uin
   return (int64_t)(s0 + s1 * 256) + ((int64_t)(s2 + s3 * 256) << 16);
 }
 
+// Three planes suffice when |a| < 2^23: a = b0 + 2^8 b1 + 2^16 b2 with b2 the
+// signed byte a >> 16, which is byte 2 of a (byte 3 is its sign extension).
+__device__ __forceinline__ bool fits_three_planes(int32_t a) { return a >= -(1 << 23) && a < (1 << 23); }
+// Every byte of plane 3 is the sign extension of the same value's plane-2 byte.
+__device__ __forceinline__ bool planes_sign_extended(uint32_t p2, uint32_t p3) {
+  // per byte: 0xFF where the plane-2 byte is negative, else 0x00
+  uint32_t ext = ((p2 >> 7) & 0x01010101u) * 0xFFu;
+  return p3 == ext;
+}
+__device__ __forceinline__ int64_t q8_partial16_three(uint4 w, uint4 p0, uint4 p1, uint4 p2) {
+  int s0 = dp4a_su(w.x, p0.x, 0);
+  s0 = dp4a_su(w.y, p0.y, s0);
+  s0 = dp4a_su(w.z, p0.z, s0);
+  s0 = dp4a_su(w.w, p0.w, s0);
+  int s1 = dp4a_su(w.x, p1.x, 0);
+  s1 = dp4a_su(w.y, p1.y, s1);
+  s1 = dp4a_su(w.z, p1.z, s1);
+  s1 = dp4a_su(w.w, p1.w, s1);
+  int s2 = dp4a_ss(w.x, p2.x, 0);
+  s2 = dp4a_ss(w.y, p2.y, s2);
+  s2 = dp4a_ss(w.z, p2.z, s2);
+  s2 = dp4a_ss(w.w, p2.w, s2);
+  return (int64_t)(s0 + s1 * 256) + ((int64_t)s2 << 16);
+}
+
 // Warp-wide sum of a 128-bit accumulator (every lane ends with the total).
 __device__ __forceinline__ Acc128 warp_sum_acc128(Acc128 a) {
 #pragma unroll

@@ -51,53 +51,81 @@ constexpr int kAttnThreads = 256;
 constexpr uint32_t kAttnChunk = 64;
 constexpr int kMaxHpc = 4;  // query heads a block
 
-__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
-  __shared__ __align__(16) int32_t q_s[kMaxHpc * 256];
-  __shared__ unsigned long long best_s[kMaxHpc];
-  const uint32_t p = query_position(a), ws = window_start(p, a.window);
-  const uint32_t hpc = a.hpc, G = a.heads / a.kv_heads, h0 = blockIdx.x * hpc, g = h0 / G;
-  const uint32_t c = blockIdx.y, t0 = ws + c * kAttnChunk;
-  if (t0 > p) return;
-  const uint32_t d = a.d;
-  for (uint32_t i = threadIdx.x; i < hpc * d; i += blockDim.x) q_s[i] = a.q[h0 * d + i];
-  if (threadIdx.x < hpc) best_s[threadIdx.x] = 0;
-  __syncthreads();
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = lane >> 3, ql = lane & 7;
-  const uint32_t per = d / 8, i0 = ql * per;  // this lane's dimensions
-  for (uint32_t round = 0; round < 2; ++round) {
-    const uint32_t t = t0 + warp * 8 + round * 4 + quad;
-    const bool live = t <= p;
-    const int32_t* krow = a.kcache + (size_t)(live ? t : t0) * a.kvd + g * d + i0;
-    int64_t sum[kMaxHpc] = {0, 0, 0, 0};
-    for (uint32_t i = 0; i < per; i += 4) {
-      const int4 k4 = *(const int4*)(krow + i);
+template <uint32_t PER, uint32_t HPC>
+__device__ __forceinline__ void attn_scores_body(const AttnArgs& a, uint32_t p, uint32_t t0, uint32_t h0, uint32_t g,
+                                                 unsigned long long* best_s) {
+  const uint32_t d = a.d, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = lane >> 3, ql = lane & 7;
+  const uint32_t i0 = ql * PER;  // this lane's dimensions
+  int32_t q[HPC][PER];
 #pragma unroll
-      for (uint32_t h = 0; h < kMaxHpc; ++h) {
-        if (h < hpc) {
-          const int4 q4 = *(const int4*)(q_s + h * d + i0 + i);
-          sum[h] = (int64_t)((uint64_t)sum[h] + (uint64_t)((int64_t)q4.x * k4.x) +
-                             (uint64_t)((int64_t)q4.y * k4.y) + (uint64_t)((int64_t)q4.z * k4.z) +
-                             (uint64_t)((int64_t)q4.w * k4.w));
-        }
-      }
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < PER; i += 4) {
+      const int4 v = *(const int4*)(a.q + (size_t)(h0 + h) * d + i0 + i);
+      q[h][i] = v.x;
+      q[h][i + 1] = v.y;
+      q[h][i + 2] = v.z;
+      q[h][i + 3] = v.w;
     }
+  // both rounds' key segments first: eight positions a warp, four at a time
+  int4 k[2][PER / 4];
+  uint32_t t[2];
 #pragma unroll
-    for (uint32_t h = 0; h < kMaxHpc; ++h) {
-      if (h < hpc) {
-        int64_t v = sum[h];
-        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 4));
-        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 2));
-        v = (int64_t)((uint64_t)v + (uint64_t)__shfl_xor_sync(0xffffffffu, v, 1));
-        if (ql == 0 && live) {
-          const int32_t sc = finish_score(v, a.mode, a.scale_q32);
-          a.scores[(size_t)(h0 + h) * a.cap + t] = sc;
-          atomicMax(&best_s[h], best_key(sc, t));
-        }
+  for (uint32_t r = 0; r < 2; ++r) {
+    t[r] = t0 + warp * 8 + r * 4 + quad;
+    const int32_t* krow = a.kcache + (size_t)(t[r] <= p ? t[r] : t0) * a.kvd + g * d + i0;
+#pragma unroll
+    for (uint32_t i = 0; i < PER / 4; ++i) k[r][i] = *(const int4*)(krow + 4 * i);
+  }
+#pragma unroll
+  for (uint32_t r = 0; r < 2; ++r) {
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      uint64_t sum = 0;
+#pragma unroll
+      for (uint32_t i = 0; i < PER / 4; ++i) {
+        sum += (uint64_t)((int64_t)q[h][4 * i] * k[r][i].x) + (uint64_t)((int64_t)q[h][4 * i + 1] * k[r][i].y) +
+               (uint64_t)((int64_t)q[h][4 * i + 2] * k[r][i].z) + (uint64_t)((int64_t)q[h][4 * i + 3] * k[r][i].w);
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      if (ql == 0 && t[r] <= p) {
+        const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
+        a.scores[(size_t)(h0 + h) * a.cap + t[r]] = sc;
+        atomicMax(&best_s[h], best_key(sc, t[r]));
       }
     }
   }
+}
+
+template <uint32_t PER, uint32_t HPC>
+__global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
+  __shared__ unsigned long long best_s[kMaxHpc];
+  const uint32_t p = query_position(a), ws = window_start(p, a.window);
+  const uint32_t G = a.heads / a.kv_heads, h0 = blockIdx.x * HPC, g = h0 / G;
+  const uint32_t c = blockIdx.y, t0 = ws + c * kAttnChunk;
+  if (t0 > p) return;
+  if (threadIdx.x < HPC) best_s[threadIdx.x] = 0;
   __syncthreads();
-  if (threadIdx.x < hpc) a.chunk_best[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = best_s[threadIdx.x];
+  attn_scores_body<PER, HPC>(a, p, t0, h0, g, best_s);
+  __syncthreads();
+  if (threadIdx.x < HPC) a.chunk_best[(size_t)(h0 + threadIdx.x) * a.nchunks + c] = best_s[threadIdx.x];
+}
+
+cudaError_t launch_attn_scores(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+  const uint32_t per = a.d / 8;
+#define IRIS_SCORES(PER, HPC)                                               \
+  if (per == PER && a.hpc == HPC) {                                         \
+    attn_scores_kernel<PER, HPC><<<grid, kAttnThreads, 0, s>>>(a);          \
+    return cudaGetLastError();                                              \
+  }
+  IRIS_SCORES(4, 1) IRIS_SCORES(4, 2) IRIS_SCORES(4, 4)
+  IRIS_SCORES(8, 1) IRIS_SCORES(8, 2) IRIS_SCORES(8, 4)
+  IRIS_SCORES(16, 1) IRIS_SCORES(16, 2) IRIS_SCORES(16, 4)
+  IRIS_SCORES(32, 1) IRIS_SCORES(32, 2)
+#undef IRIS_SCORES
+  return cudaErrorInvalidValue;
 }
 
 // First maximum of each of the block's heads over the active chunks.
@@ -178,16 +206,23 @@ __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
     __syncthreads();
     // This chunk's weighted value sums go straight into the head's running
     // total: wrapping 64-bit addition is exact in any order.
+    // Thread: one dimension i for every head of the block, over the chunk's
+    // positions j = pg, pg + npg, ... (each value row element read once).
     const uint32_t live = min(kAttnChunk, p + 1 - t0);
-    for (uint32_t o = threadIdx.x; o < hpc * d; o += blockDim.x) {
-      const uint32_t h = o / d, i = o % d;
+    const uint32_t npg = blockDim.x / d, pg = threadIdx.x / d, i = threadIdx.x % d;
+    if (pg < npg) {
       const int32_t* vcol = a.vcache + (size_t)t0 * a.kvd + g * d + i;
-      const int32_t* wrow = w_s + h * kAttnChunk;
-      int64_t acc = 0;
+      uint64_t acc[kMaxHpc] = {0, 0, 0, 0};
 #pragma unroll 8
-      for (uint32_t j = 0; j < live; ++j)
-        acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)wrow[j] * vcol[(size_t)j * a.kvd]));
-      atomicAdd((unsigned long long*)(a.acc + (size_t)(h0 + h) * d + i), (unsigned long long)acc);
+      for (uint32_t j = pg; j < live; j += npg) {
+        const int64_t v = vcol[(size_t)j * a.kvd];
+#pragma unroll
+        for (uint32_t h = 0; h < kMaxHpc; ++h)
+          if (h < hpc) acc[h] += (uint64_t)((int64_t)w_s[h * kAttnChunk + j] * v);
+      }
+#pragma unroll
+      for (uint32_t h = 0; h < kMaxHpc; ++h)
+        if (h < hpc) atomicAdd((unsigned long long*)(a.acc + (size_t)(h0 + h) * d + i), (unsigned long long)acc[h]);
     }
     if (threadIdx.x < hpc) atomicAdd(a.wsum + h0 + threadIdx.x, wsum_s[threadIdx.x]);
   }
@@ -225,9 +260,12 @@ uint32_t attention_chunks(uint32_t cap) { return (cap + kAttnChunk - 1) / kAttnC
 
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
   const uint32_t G = a.heads / a.kv_heads;
-  if (a.d % 32 || a.d > 256 || a.hpc == 0 || a.hpc > (uint32_t)kMaxHpc || G % a.hpc) return cudaErrorInvalidValue;
+  if (a.d % 32 || a.d > 256 || a.hpc == 0 || a.hpc > (uint32_t)kMaxHpc || G % a.hpc ||
+      (a.d == 256 && a.hpc > 2))
+    return cudaErrorInvalidValue;
   dim3 grid(a.heads / a.hpc, a.nchunks);
-  attn_scores_kernel<<<grid, kAttnThreads, 0, s>>>(a);
+  cudaError_t e = launch_attn_scores(a, grid, s);
+  if (e != cudaSuccess) return e;
   attn_exp_kernel<<<grid, kAttnThreads, 0, s>>>(a);
   attn_out_kernel<<<grid, kAttnThreads, 0, s>>>(a);
   return cudaGetLastError();

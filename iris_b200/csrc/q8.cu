@@ -243,7 +243,7 @@ __device__ uint64_t block_sum_sat(uint64_t v, uint64_t* red) {
 // Builds the byte planes of one K-wide row into `planes` (shared or global),
 // RMS-normalising first when norm_w is given (ops.rs:98-114: two mul_sat per
 // value, by the inverse-RMS scale and then by the weight).
-__device__ void row_to_planes(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
+__device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
                               int64_t eps, uint32_t K, uint8_t* planes, uint64_t* red,
                               int32_t* s_scale) {
   int32_t scale = 0;
@@ -261,6 +261,7 @@ __device__ void row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
     __syncthreads();
     scale = *s_scale;
   }
+  int wide = 0;
   for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
     int4 v = *(const int4*)(x + i);
     if (norm_w) {
@@ -270,8 +271,10 @@ __device__ void row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
       v.z = mul_sat(mul_sat(v.z, scale), w.z);
       v.w = mul_sat(mul_sat(v.w, scale), w.w);
     }
+    wide |= !fits_three_planes(v.x) | !fits_three_planes(v.y) | !fits_three_planes(v.z) | !fits_three_planes(v.w);
     put_planes4(planes, K, i, v);
   }
+  return __syncthreads_or(wide) != 0;
 }
 
 __global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
@@ -347,20 +350,23 @@ __device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uin
 // warp streams every tile of its range - 16 rows x kc values and their scale
 // bits, two contiguous runs - from HBM into a ring of shared-memory stages
 // with cp.async.bulk (TMA, evict-first in L2), completing on the stage's
-// "full" mbarrier. Eight consumer warps, two rows each, run the dp4a
-// byte-plane products against the activation planes held in shared memory
-// and release the stage on its "empty" mbarrier. The activation prologue
+// "full" mbarrier. Sixteen consumer warps - two rows and half of the slice's
+// blocks each - run the dp4a byte-plane products against the activation
+// planes held in shared memory (three planes when every activation fits in
+// +-2^23, else four) and release the stage on its "empty" mbarrier; at the
+// end of a tile group the two halves of each row meet in shared memory. The activation prologue
 // (planes, or the fused RMSNorm) runs once per block while the first stages
 // are already in flight. Every wait is bounded (about one second): a stalled
 // pipeline records a fault and the kernel returns instead of hanging.
 
 __device__ unsigned int g_fault;
 
-constexpr int kTmaConsumerWarps = 8;
+constexpr int kTmaConsumerWarps = 16;
 constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;
-constexpr int kTmaRowsPerWarp = kQ8TileRows / kTmaConsumerWarps;  // 2
+constexpr int kTmaRowsPerWarp = 2;
 constexpr uint32_t kTmaMaxStages = 8;
 constexpr uint32_t kTmaSmemBudget = 220 * 1024;
+constexpr uint32_t kConsumerThreads = kTmaConsumerWarps * 32;
 
 struct GemvPlan {
   uint32_t stages;
@@ -388,6 +394,45 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, GemvPlan* p) {
   return true;
 }
 
+// One warp's share of a tile: two rows, blocks [b0, b1) of the slice. Each
+// lane takes whole 32-value blocks (two 16-byte chunks, one scale); lanes
+// 4-7 of every quarter-warp load the two chunks in the other order, so that
+// each 8-lane phase of a 128-bit shared load touches 8 different 16-byte bank
+// groups (the block sum does not depend on the order).
+template <bool kThree>
+__device__ __forceinline__ void gemv_tile_rows(const uint8_t* __restrict__ W, const uint16_t* __restrict__ Sc,
+                                               const uint4* __restrict__ P0, const uint4* __restrict__ P1,
+                                               const uint4* __restrict__ P2, const uint4* __restrict__ P3,
+                                               uint32_t kc, uint32_t cbase, uint32_t b0, uint32_t b1,
+                                               uint32_t lane, Acc128* acc) {
+  const uint32_t blocks = kc / 32, swap = (lane >> 2) & 1;
+#pragma unroll 2
+  for (uint32_t b = b0 + lane; b < b1; b += 32) {
+    const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
+    const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
+    const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1];
+    uint4 pa3, pb3;
+    if (!kThree) {
+      pa3 = P3[cbase + c0];
+      pb3 = P3[cbase + c1];
+    }
+#pragma unroll
+    for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+      const uint8_t* Wr = W + r * kc;
+      const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
+      int32_t m, e;
+      q8_scale_parts(Sc[r * blocks + b], &m, &e);  // finite: checked at upload (padding rows: 0)
+      const int64_t bs = kThree ? q8_partial16_three(wa, pa0, pa1, pa2) + q8_partial16_three(wb, pb0, pb1, pb2)
+                                : q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
+      acc128_add_shifted(acc[r], bs * m, e);
+    }
+  }
+}
+
+__device__ __forceinline__ void consumer_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerThreads) : "memory");
+}
+
 template <int IN, int EPI>
 __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs a, GemvPlan p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -395,6 +440,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   __shared__ __align__(8) uint64_t empty[kTmaMaxStages];
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
+  __shared__ Acc128 half_sums[2][kQ8TileRows];  // second-half sums, by group parity
   const uint32_t K = a.cols, kc = a.kc, S = a.nslices;
   uint8_t* planes = smem;
   uint8_t* stage0 = smem + p.planes_bytes;
@@ -415,8 +461,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   __syncthreads();
 
   const uint64_t policy = l2_evict_first_policy();
-  // Item i is tile (g_begin + i / S, i % S): tiles of a range are consecutive
-  // in memory, so item i starts at tile index g_begin * S + i.
+  // Item i is tile (g_begin + i / S, i % S): the tiles of a range are
+  // consecutive in memory, so item i is tile index g_begin * S + i.
   auto issue = [&](uint32_t item) {
     const uint32_t st = item % p.stages;
     const size_t tile = (size_t)g_begin * S + item;
@@ -431,13 +477,24 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   if (producer && lane == 0)
     for (uint32_t item = 0; item < first; ++item) issue(item);
 
+  // Activation planes; `wide` when some value needs the fourth plane.
+  bool wide;
   if (IN == IN_PLANES) {
     const uint4* src = (const uint4*)a.planes;
-    for (uint32_t i = threadIdx.x; i < K / 4; i += blockDim.x) ((uint4*)planes)[i] = src[i];
+    int w = 0;
+    for (uint32_t i = threadIdx.x; i < K / 16; i += blockDim.x) {
+      const uint4 v0 = src[i], v1 = src[K / 16 + i], v2 = src[2 * (K / 16) + i], v3 = src[3 * (K / 16) + i];
+      ((uint4*)planes)[i] = v0;
+      ((uint4*)planes)[K / 16 + i] = v1;
+      ((uint4*)planes)[2 * (K / 16) + i] = v2;
+      ((uint4*)planes)[3 * (K / 16) + i] = v3;
+      w |= !planes_sign_extended(v2.x, v3.x) | !planes_sign_extended(v2.y, v3.y) |
+           !planes_sign_extended(v2.z, v3.z) | !planes_sign_extended(v2.w, v3.w);
+    }
+    wide = __syncthreads_or(w) != 0;
   } else {
-    row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, planes, red, &s_scale);
+    wide = row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, planes, red, &s_scale);
   }
-  __syncthreads();
 
   if (producer) {
     if (lane == 0) {
@@ -463,66 +520,60 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   const uint4* P1 = P0 + K / 16;
   const uint4* P2 = P1 + K / 16;
   const uint4* P3 = P2 + K / 16;
-  // Each lane takes whole 32-value blocks (two 16-byte chunks, one scale).
-  // Lanes 4-7 of every quarter-warp load the two chunks in the other order,
-  // so that each 8-lane phase of a 128-bit shared load touches 8 different
-  // 16-byte bank groups; the block sum does not depend on the order.
-  const uint32_t lr0 = kTmaRowsPerWarp * warp, blocks = kc / 32, swap = (lane >> 2) & 1;
+  // Warp w: rows 2 (w % 8) and 2 (w % 8) + 1 of each tile, blocks of the
+  // slice's first half (w < 8) or second half (w >= 8).
+  const uint32_t pair = warp % (kTmaConsumerWarps / 2), half = warp / (kTmaConsumerWarps / 2);
+  const uint32_t lr0 = kTmaRowsPerWarp * pair, blocks = kc / 32, mid = (blocks + 1) / 2;
+  const uint32_t b0 = half ? mid : 0, b1 = half ? blocks : mid;
   Acc128 acc[kTmaRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
+  uint32_t parity = 0;
+  bool stalled = false;  // after a given-up wait: keep pace with the barriers, skip the waits
   for (uint32_t item = 0; item < nitems; ++item) {
     const uint32_t st = item % p.stages, use = item / p.stages, sl = item % S;
-    const uint32_t row0 = (g_begin + item / S) * kQ8TileRows;
-    if (!mbar_wait_bounded(&full[st], use & 1, &g_fault)) return;
+    if (!stalled && !mbar_wait_bounded(&full[st], use & 1, &g_fault)) stalled = true;
     const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * kc;
     const uint16_t* Sc = (const uint16_t*)(stage0 + st * p.stage_bytes + kQ8TileRows * kc) + lr0 * blocks;
     const uint32_t cbase = sl * (kc / 16);
-#pragma unroll 2
-    for (uint32_t b = lane; b < blocks; b += 32) {
-      const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
-      const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0], pa3 = P3[cbase + c0];
-      const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1], pb3 = P3[cbase + c1];
-#pragma unroll
-      for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-        const uint8_t* Wr = W + r * kc;
-        const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
-        int32_t m, e;
-        q8_scale_parts(Sc[r * blocks + b], &m, &e);  // finite: checked at upload (padding rows: 0)
-        const int64_t bs = q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
-        acc128_add_shifted(acc[r], bs * m, e);
-      }
-    }
+    if (wide) gemv_tile_rows<false>(W, Sc, P0, P1, P2, P3, kc, cbase, b0, b1, lane, acc);
+    else gemv_tile_rows<true>(W, Sc, P0, P1, P2, P3, kc, cbase, b0, b1, lane, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (sl + 1 == S) {
-      const uint32_t row = row0 + lr0;
-      if (row < a.rows) {
-        const uint32_t live = min((uint32_t)kTmaRowsPerWarp, a.rows - row);
 #pragma unroll
-        for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
-        if (lane == 0) {
-          const int32_t v0 = acc128_round_q24(acc[0]);
-          const int32_t v1 = live > 1 ? acc128_round_q24(acc[1]) : 0;
-          if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-            if (live > 1) epi_pair<EPI>(a, 0, row, v0, v1);
-          } else if (EPI == EPI_LOGITS) {
-            const int32_t c0v = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
-            unsigned long long key = best_key(c0v, row);
-            if (a.out) a.out[row] = c0v;
-            if (live > 1) {
-              const int32_t c1v = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
-              if (a.out) a.out[row + 1] = c1v;
-              const unsigned long long k1 = best_key(c1v, row + 1);
-              key = k1 > key ? k1 : key;
-            }
-            atomicMax(a.best, key);
-          } else {
-            epi_single<EPI>(a, 0, row, v0);
-            if (live > 1) epi_single<EPI>(a, 0, row + 1, v1);
+      for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
+      if (half && lane == 0) {
+        half_sums[parity][lr0] = acc[0];
+        half_sums[parity][lr0 + 1] = acc[1];
+      }
+      consumer_barrier();
+      const uint32_t row = (g_begin + item / S) * kQ8TileRows + lr0;
+      if (!half && lane == 0 && row < a.rows) {
+        acc128_add(acc[0], half_sums[parity][lr0].lo, half_sums[parity][lr0].hi);
+        acc128_add(acc[1], half_sums[parity][lr0 + 1].lo, half_sums[parity][lr0 + 1].hi);
+        const bool two = row + 1 < a.rows;
+        const int32_t v0 = acc128_round_q24(acc[0]);
+        const int32_t v1 = two ? acc128_round_q24(acc[1]) : 0;
+        if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+          if (two) epi_pair<EPI>(a, 0, row, v0, v1);
+        } else if (EPI == EPI_LOGITS) {
+          const int32_t c0v = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
+          unsigned long long key = best_key(c0v, row);
+          if (a.out) a.out[row] = c0v;
+          if (two) {
+            const int32_t c1v = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
+            if (a.out) a.out[row + 1] = c1v;
+            const unsigned long long k1 = best_key(c1v, row + 1);
+            key = k1 > key ? k1 : key;
           }
+          atomicMax(a.best, key);
+        } else {
+          epi_single<EPI>(a, 0, row, v0);
+          if (two) epi_single<EPI>(a, 0, row + 1, v1);
         }
       }
+      parity ^= 1;
 #pragma unroll
       for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
     }
