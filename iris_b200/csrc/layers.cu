@@ -13,6 +13,7 @@
 //      1.0 - sum(weights) times the first maximum's value row (the same as
 //      adding it to that weight first, since no weight saturates) and
 //      requantizes.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include "layers.cuh"
@@ -258,11 +259,251 @@ uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads) {
 
 uint32_t attention_chunks(uint32_t cap) { return (cap + kAttnChunk - 1) / kAttnChunk; }
 
+uint32_t attention_cluster_hpc(uint32_t heads, uint32_t kv_heads, uint32_t d) {
+  uint32_t G = heads / kv_heads, hpc = G < (uint32_t)kMaxHpc ? G : (uint32_t)kMaxHpc;
+  if (d == 256 && hpc > 2) hpc = 2;
+  while (hpc > 1 && (G % hpc || heads / hpc < 16)) --hpc;
+  return hpc;
+}
+
+// ---------------------------------------------------------------------------
+// Decode attention in one launch: a thread-block cluster a head block
+// ---------------------------------------------------------------------------
+//
+// A cluster of kClusterCtas blocks owns hpc query heads of one kv group; block
+// rank r takes the r-th of kClusterCtas contiguous ranges of the window
+// [ws, p]. The three dependent steps of attention_softmax meet through
+// distributed shared memory (cluster barriers, no global atomics):
+//   1. scores of the block's positions (kept in the scores scratch) and the
+//      block's first maximum a head; cluster barrier; every block takes the
+//      maximum over the cluster;
+//   2. exp terms against it (terms scratch) and their sum a head; cluster
+//      barrier; every block takes the total over the cluster;
+//   3. weights (written over the scores), their sum a head, and the wrapping
+//      weighted value sums of the block's positions; cluster barrier; block
+//      r finishes its share of the head dimensions: the sum over the cluster
+//      plus (1.0 - sum of weights) times the first maximum's value, then
+//      requantize and write the context planes.
+
+constexpr uint32_t kClusterCtas = 8;
+constexpr uint32_t kClusterWarps = kAttnThreads / 32;
+
+template <uint32_t PER, uint32_t HPC>
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kAttnThreads)
+    attn_cluster_kernel(AttnArgs a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  constexpr uint32_t D = PER * 8;
+  extern __shared__ __align__(16) int64_t wpart[];  // [kClusterWarps][HPC][D], then part [HPC][D]
+  int64_t* part = wpart + kClusterWarps * HPC * D;
+  __shared__ unsigned long long best_s[HPC];
+  __shared__ unsigned long long sum_s[HPC];
+  __shared__ int32_t wsum_s[HPC];
+  __shared__ unsigned long long gbest_s[HPC];
+  __shared__ unsigned long long gtotal_s[HPC];
+  __shared__ int32_t resid_s[HPC];
+
+  const uint32_t rank = cluster.block_rank();
+  const uint32_t hb = blockIdx.x / kClusterCtas, h0 = hb * HPC, G = a.heads / a.kv_heads, g = h0 / G;
+  const uint32_t p = query_position(a), ws = window_start(p, a.window), n = p - ws + 1;
+  const uint32_t span = (n + kClusterCtas - 1) / kClusterCtas;
+  const uint32_t r0 = ws + rank * span, r1 = min(p + 1, r0 + span);  // may be empty
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = lane >> 3, ql = lane & 7;
+  if (threadIdx.x < HPC) {
+    best_s[threadIdx.x] = 0;
+    sum_s[threadIdx.x] = 0;
+    wsum_s[threadIdx.x] = 0;
+  }
+  __syncthreads();
+
+  // ---- 1. scores: 8 lanes a position, 4 positions a warp at a time
+  {
+    const uint32_t i0 = ql * PER;
+    int32_t q[HPC][PER];
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+      for (uint32_t i = 0; i < PER; i += 4) {
+        const int4 v = *(const int4*)(a.q + (size_t)(h0 + h) * D + i0 + i);
+        q[h][i] = v.x;
+        q[h][i + 1] = v.y;
+        q[h][i + 2] = v.z;
+        q[h][i + 3] = v.w;
+      }
+    unsigned long long best[HPC];
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
+    for (uint32_t base = r0; base < r1; base += kClusterWarps * 4) {
+      const uint32_t t = base + warp * 4 + quad;
+      const bool live = t < r1;
+      const int32_t* krow = a.kcache + (size_t)(live ? t : r0) * a.kvd + g * D + i0;
+      int4 k[PER / 4];
+#pragma unroll
+      for (uint32_t i = 0; i < PER / 4; ++i) k[i] = *(const int4*)(krow + 4 * i);
+#pragma unroll
+      for (uint32_t h = 0; h < HPC; ++h) {
+        uint64_t sum = 0;
+#pragma unroll
+        for (uint32_t i = 0; i < PER / 4; ++i)
+          sum += (uint64_t)((int64_t)q[h][4 * i] * k[i].x) + (uint64_t)((int64_t)q[h][4 * i + 1] * k[i].y) +
+                 (uint64_t)((int64_t)q[h][4 * i + 2] * k[i].z) + (uint64_t)((int64_t)q[h][4 * i + 3] * k[i].w);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (ql == 0 && live) {
+          const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
+          a.scores[(size_t)(h0 + h) * a.cap + t] = sc;
+          const unsigned long long key = best_key(sc, t);
+          best[h] = key > best[h] ? key : best[h];
+        }
+      }
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+      if (ql == 0 && best[h]) atomicMax(&best_s[h], best[h]);
+  }
+  cluster.sync();
+  if (threadIdx.x < HPC) {
+    unsigned long long b = 0;
+    for (uint32_t r = 0; r < kClusterCtas; ++r) {
+      const unsigned long long v = *cluster.map_shared_rank(&best_s[threadIdx.x], r);
+      b = v > b ? v : b;
+    }
+    gbest_s[threadIdx.x] = b;
+  }
+  __syncthreads();
+
+  // ---- 2. exp terms and their sums
+  const uint32_t cnt = r1 > r0 ? r1 - r0 : 0;
+  for (uint32_t idx = threadIdx.x; idx < HPC * cnt; idx += blockDim.x) {
+    const uint32_t h = idx / cnt, t = r0 + idx % cnt;
+    const size_t at = (size_t)(h0 + h) * a.cap + t;
+    const int64_t e = softmax_exp_term_act(a.scores[at], best_key_value(gbest_s[h]));
+    a.terms[at] = e;
+    atomicAdd(&sum_s[h], (unsigned long long)e);
+  }
+  cluster.sync();
+  if (threadIdx.x < HPC) {
+    unsigned long long tot = 0;
+    for (uint32_t r = 0; r < kClusterCtas; ++r) tot += *cluster.map_shared_rank(&sum_s[threadIdx.x], r);
+    gtotal_s[threadIdx.x] = tot;
+  }
+  __syncthreads();
+
+  // ---- 3. weights (over the scores), weight sums, weighted value sums
+  for (uint32_t idx = threadIdx.x; idx < HPC * cnt; idx += blockDim.x) {
+    const uint32_t h = idx / cnt, t = r0 + idx % cnt;
+    const size_t at = (size_t)(h0 + h) * a.cap + t;
+    const int32_t w = softmax_weight(a.terms[at], gtotal_s[h]);
+    a.scores[at] = w;
+    atomicAdd(&wsum_s[h], w);
+  }
+  __syncthreads();
+  {
+    // warp w: positions r0 + w, r0 + w + kClusterWarps, ...; lane: 4 dims at a time
+    uint64_t acc[HPC][(D + 127) / 128][4];
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+      for (uint32_t c = 0; c < (D + 127) / 128; ++c)
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) acc[h][c][j] = 0;
+#pragma unroll 4
+    for (uint32_t t = r0 + warp; t < r1; t += kClusterWarps) {
+      const int32_t* vrow = a.vcache + (size_t)t * a.kvd + g * D;
+#pragma unroll
+      for (uint32_t c = 0; c < (D + 127) / 128; ++c) {
+        const uint32_t dim = c * 128 + 4 * lane;
+        if (dim < D) {
+          const int4 v = *(const int4*)(vrow + dim);
+#pragma unroll
+          for (uint32_t h = 0; h < HPC; ++h) {
+            const int64_t w = a.scores[(size_t)(h0 + h) * a.cap + t];
+            acc[h][c][0] += (uint64_t)(w * v.x);
+            acc[h][c][1] += (uint64_t)(w * v.y);
+            acc[h][c][2] += (uint64_t)(w * v.z);
+            acc[h][c][3] += (uint64_t)(w * v.w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+      for (uint32_t c = 0; c < (D + 127) / 128; ++c) {
+        const uint32_t dim = c * 128 + 4 * lane;
+        if (dim < D)
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) wpart[(warp * HPC + h) * D + dim + j] = (int64_t)acc[h][c][j];
+      }
+  }
+  __syncthreads();
+  for (uint32_t o = threadIdx.x; o < HPC * D; o += blockDim.x) {
+    uint64_t s = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < kClusterWarps; ++w) s += (uint64_t)wpart[w * HPC * D + o];
+    part[o] = (int64_t)s;
+  }
+  cluster.sync();
+
+  // ---- 4. block `rank` finishes outputs [rank * share, (rank + 1) * share)
+  if (threadIdx.x < HPC) {
+    int32_t sw = 0;
+    for (uint32_t r = 0; r < kClusterCtas; ++r) sw += *cluster.map_shared_rank(&wsum_s[threadIdx.x], r);
+    resid_s[threadIdx.x] = sub_sat(kOneAct, sw);  // residual (ops.rs:274-276)
+  }
+  __syncthreads();
+  const uint32_t share = (HPC * D + kClusterCtas - 1) / kClusterCtas, qd = a.heads * D;
+  for (uint32_t o = rank * share + threadIdx.x; o < min(HPC * D, (rank + 1) * share); o += blockDim.x) {
+    const uint32_t h = o / D, i = o % D, hh = h0 + h;
+    uint64_t s = 0;
+    for (uint32_t r = 0; r < kClusterCtas; ++r) s += (uint64_t)*cluster.map_shared_rank(&part[o], r);
+    const uint32_t tmax = best_key_token(gbest_s[h]);
+    s += (uint64_t)((int64_t)resid_s[h] * a.vcache[(size_t)tmax * a.kvd + g * D + i]);
+    const int32_t v = requantize((int64_t)s);
+    put_planes(a.ctx_planes, qd, hh * D + i, v);
+    if (a.ctx) a.ctx[hh * D + i] = v;
+  }
+  cluster.sync();  // the other blocks may still be reading this block's shared memory
+}
+
+cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s) {
+  const uint32_t per = a.d / 8;
+  dim3 grid(kClusterCtas * (a.heads / a.hpc));
+  const size_t smem = (size_t)(kClusterWarps + 1) * a.hpc * a.d * sizeof(int64_t);
+#define IRIS_CLUSTER(PER, HPC)                                                  \
+  if (per == PER && a.hpc == HPC) {                                             \
+    attn_cluster_kernel<PER, HPC><<<grid, kAttnThreads, smem, s>>>(a);          \
+    return cudaGetLastError();                                                  \
+  }
+  IRIS_CLUSTER(4, 1) IRIS_CLUSTER(4, 2) IRIS_CLUSTER(4, 4)
+  IRIS_CLUSTER(8, 1) IRIS_CLUSTER(8, 2) IRIS_CLUSTER(8, 4)
+  IRIS_CLUSTER(16, 1) IRIS_CLUSTER(16, 2) IRIS_CLUSTER(16, 4)
+  IRIS_CLUSTER(32, 1) IRIS_CLUSTER(32, 2)
+#undef IRIS_CLUSTER
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t prepare_attention_cluster_kernels() {
+  cudaError_t e = cudaSuccess;
+#define IRIS_CLUSTER_ATTR(PER, HPC)                                                                          \
+  if (e == cudaSuccess)                                                                                      \
+    e = cudaFuncSetAttribute(attn_cluster_kernel<PER, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                             (int)((kClusterWarps + 1) * HPC * PER * 8 * sizeof(int64_t)));
+  IRIS_CLUSTER_ATTR(4, 1) IRIS_CLUSTER_ATTR(4, 2) IRIS_CLUSTER_ATTR(4, 4)
+  IRIS_CLUSTER_ATTR(8, 1) IRIS_CLUSTER_ATTR(8, 2) IRIS_CLUSTER_ATTR(8, 4)
+  IRIS_CLUSTER_ATTR(16, 1) IRIS_CLUSTER_ATTR(16, 2) IRIS_CLUSTER_ATTR(16, 4)
+  IRIS_CLUSTER_ATTR(32, 1) IRIS_CLUSTER_ATTR(32, 2)
+#undef IRIS_CLUSTER_ATTR
+  return e;
+}
+
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
   const uint32_t G = a.heads / a.kv_heads;
   if (a.d % 32 || a.d > 256 || a.hpc == 0 || a.hpc > (uint32_t)kMaxHpc || G % a.hpc ||
       (a.d == 256 && a.hpc > 2))
     return cudaErrorInvalidValue;
+  if (a.cluster) return launch_attention_cluster(a, s);
   dim3 grid(a.heads / a.hpc, a.nchunks);
   cudaError_t e = launch_attn_scores(a, grid, s);
   if (e != cudaSuccess) return e;
@@ -349,7 +590,9 @@ cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_
 }
 
 cudaError_t prepare_layer_kernels() {
-  return cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  if (e == cudaSuccess) e = prepare_attention_cluster_kernels();
+  return e;
 }
 
 // ---------------------------------------------------------------------------

@@ -33,12 +33,15 @@ struct AttnArgs {
   unsigned int* counters;          // [heads], zero between launches
   uint32_t cap, nchunks;           // positions held; chunks of 64 positions
   uint32_t hpc;                    // query heads a block (attention_hpc)
+  int cluster;                     // decode: one cluster launch (else three launches)
 };
 
 // Query heads a decode-attention block handles, and the chunk count for a
 // cache of `cap` positions (sizes of the scratch arrays above).
 uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads);
 uint32_t attention_chunks(uint32_t cap);
+// Query heads a block of the one-launch (cluster) decode attention.
+uint32_t attention_cluster_hpc(uint32_t heads, uint32_t kv_heads, uint32_t d);
 
 // Decode (one query): three launches split over kv groups x position chunks.
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s);
