@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "detnum.cuh"
 
 namespace iris {
@@ -21,6 +23,33 @@ namespace iris {
     cudaError_t _e = (expr);                     \
     if (_e != cudaSuccess) return (int)_e;       \
   } while (0)
+
+// ---- programmatic dependent launch ------------------------------------------
+//
+// Kernels on the inference path are launched with programmatic stream
+// serialization: kernel N+1 may be scheduled while kernel N finishes. Every
+// such kernel calls pdl_trigger() first (its successor may launch once all of
+// its blocks have started) and pdl_wait() before it reads anything an earlier
+// kernel wrote or writes anything an earlier kernel may still read; only reads
+// of immutable data (weights) may precede pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 __device__ __forceinline__ int dp4a_su(uint32_t w_s8, uint32_t a_u8, int c) {
   int d;

@@ -102,6 +102,8 @@ __device__ __forceinline__ void attn_scores_body(const AttnArgs& a, uint32_t p, 
 
 template <uint32_t PER, uint32_t HPC>
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ unsigned long long best_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
   const uint32_t G = a.heads / a.kv_heads, h0 = blockIdx.x * HPC, g = h0 / G;
@@ -118,7 +120,8 @@ cudaError_t launch_attn_scores(const AttnArgs& a, dim3 grid, cudaStream_t s) {
   const uint32_t per = a.d / 8;
 #define IRIS_SCORES(PER, HPC)                                               \
   if (per == PER && a.hpc == HPC) {                                         \
-    attn_scores_kernel<PER, HPC><<<grid, kAttnThreads, 0, s>>>(a);          \
+    cudaError_t e_ = launch_k(attn_scores_kernel<PER, HPC>, grid, dim3(kAttnThreads), 0, s, a); \
+    if (e_ != cudaSuccess) return e_;          \
     return cudaGetLastError();                                              \
   }
   IRIS_SCORES(4, 1) IRIS_SCORES(4, 2) IRIS_SCORES(4, 4)
@@ -146,6 +149,8 @@ __device__ void block_global_best(const AttnArgs& a, uint32_t h0, uint32_t nact,
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ unsigned long long best_s[kMaxHpc];
   __shared__ unsigned long long sum_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
@@ -171,6 +176,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ int32_t w_s[kMaxHpc * kAttnChunk];
   __shared__ unsigned long long best_s[kMaxHpc];
   __shared__ unsigned long long total_s[kMaxHpc];
@@ -291,6 +298,8 @@ constexpr uint32_t kClusterWarps = kAttnThreads / 32;
 template <uint32_t PER, uint32_t HPC>
 __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kAttnThreads)
     attn_cluster_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   constexpr uint32_t D = PER * 8;
@@ -473,7 +482,8 @@ cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s) {
   const size_t smem = (size_t)(kClusterWarps + 1) * a.hpc * a.d * sizeof(int64_t);
 #define IRIS_CLUSTER(PER, HPC)                                                  \
   if (per == PER && a.hpc == HPC) {                                             \
-    attn_cluster_kernel<PER, HPC><<<grid, kAttnThreads, smem, s>>>(a);          \
+    cudaError_t e_ = launch_k(attn_cluster_kernel<PER, HPC>, grid, dim3(kAttnThreads), smem, s, a); \
+    if (e_ != cudaSuccess) return e_;          \
     return cudaGetLastError();                                                  \
   }
   IRIS_CLUSTER(4, 1) IRIS_CLUSTER(4, 2) IRIS_CLUSTER(4, 4)
@@ -507,9 +517,9 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
   dim3 grid(a.heads / a.hpc, a.nchunks);
   cudaError_t e = launch_attn_scores(a, grid, s);
   if (e != cudaSuccess) return e;
-  attn_exp_kernel<<<grid, kAttnThreads, 0, s>>>(a);
-  attn_out_kernel<<<grid, kAttnThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  e = launch_k(attn_exp_kernel, grid, dim3(kAttnThreads), 0, s, a);
+  if (e != cudaSuccess) return e;
+  return launch_k(attn_out_kernel, grid, dim3(kAttnThreads), 0, s, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -517,6 +527,8 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ unsigned long long best_s, total_s;
   __shared__ int32_t wsum_s;
@@ -585,8 +597,7 @@ cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_
   size_t smem = ((a.d * 4 + 15) & ~15u) + (size_t)max_visible * 12;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   dim3 grid(tokens, a.heads);
-  attn_prefill_kernel<<<grid, kAttnThreads, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_k(attn_prefill_kernel, grid, dim3(kAttnThreads), smem, s, a);
 }
 
 cudaError_t prepare_layer_kernels() {
@@ -602,6 +613,8 @@ cudaError_t prepare_layer_kernels() {
 __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t cols,
                              uint32_t kc, uint32_t nslices, const uint32_t* ids, int32_t scale, int has_scale,
                              int32_t* out) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t t = blockIdx.x, id = ids[t];
   for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
     int32_t m, e;
@@ -615,24 +628,25 @@ __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __res
 cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32_t tokens,
                          int has_scale, int32_t scale, int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  embed_kernel<<<tokens, 256, 0, s>>>(embed->q, embed->s, embed->cols, embed->kc, embed->nslices, d_ids, scale,
-                                      has_scale,
-                                      out);
-  return cudaGetLastError();
+  return launch_k(embed_kernel, dim3(tokens), dim3(256), 0, s, (const int8_t*)embed->q, (const uint16_t*)embed->s,
+                  embed->cols, embed->kc, embed->nslices, d_ids, scale, has_scale, out);
 }
 
 __global__ void fill_u64_kernel(unsigned long long* p, uint32_t n) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = 0;
 }
 cudaError_t launch_fill_u64(unsigned long long* p, uint32_t n, cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  fill_u64_kernel<<<(n + 255) / 256, 256, 0, s>>>(p, n);
-  return cudaGetLastError();
+  return launch_k(fill_u64_kernel, dim3((n + 255) / 256), dim3(256), 0, s, p, n);
 }
 
 __global__ void decode_finish_kernel(unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
                                      uint32_t* d_step, uint32_t* history, uint32_t cap) {
+  pdl_trigger();
+  pdl_wait();
   uint32_t tok = best_key_token(*best);  // first maximum (generation.rs:25-58)
   *d_token = tok;
   *best = 0;
@@ -644,9 +658,8 @@ __global__ void decode_finish_kernel(unsigned long long* best, uint32_t* d_token
 cudaError_t launch_decode_finish(const unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
                                  uint32_t* d_step, uint32_t* history, uint32_t history_cap,
                                  cudaStream_t s) {
-  decode_finish_kernel<<<1, 1, 0, s>>>((unsigned long long*)best, d_token, d_pos, d_step, history,
-                                       history_cap);
-  return cudaGetLastError();
+  return launch_k(decode_finish_kernel, dim3(1), dim3(1), 0, s, (unsigned long long*)best, d_token, d_pos, d_step,
+                  history, history_cap);
 }
 
 // ---------------------------------------------------------------------------
@@ -678,6 +691,8 @@ __device__ void block_rms_norm(int32_t* v, uint32_t n, const int32_t* w, int64_t
 }
 
 __global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) int32_t hv[];  // [d]
   __shared__ uint64_t red[32];
   const uint32_t tok = blockIdx.x, which = blockIdx.y, d = a.d;
@@ -713,13 +728,14 @@ __global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
 cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   dim3 grid(tokens, a.heads + 2 * a.kv_heads);
-  gemma_qkv_finish_kernel<<<grid, 128, a.d * 4, s>>>(a);
-  return cudaGetLastError();
+  return launch_k(gemma_qkv_finish_kernel, grid, dim3(128), a.d * 4, s, a);
 }
 
 __global__ void gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
                                        const int32_t* w_pre_ffw, int64_t eps, uint32_t H,
                                        uint8_t* planes) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) int32_t row[];  // [H]
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x;
@@ -740,12 +756,14 @@ cudaError_t launch_gemma_post_attn(const int32_t* o, int32_t* x, const int32_t* 
                                    const int32_t* w_pre_ffw, int64_t eps, uint32_t tokens,
                                    uint32_t hidden, uint8_t* planes, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  gemma_post_attn_kernel<<<tokens, 256, hidden * 4, s>>>(o, x, w_post_attn, w_pre_ffw, eps, hidden, planes);
-  return cudaGetLastError();
+  return launch_k(gemma_post_attn_kernel, dim3(tokens), dim3(256), hidden * 4, s, o, x, w_post_attn, w_pre_ffw, eps,
+                  hidden, planes);
 }
 
 __global__ void gemma_norm_add_kernel(const int32_t* v_in, const int32_t* add, const int32_t* w,
                                       int64_t eps, int32_t scalar, uint32_t H, int32_t* out) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) int32_t row[];
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x;
@@ -763,22 +781,24 @@ cudaError_t launch_gemma_post_ffw(const int32_t* ff, const int32_t* x, const int
                                   int64_t eps, uint32_t tokens, uint32_t hidden, int32_t* xs,
                                   cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  gemma_norm_add_kernel<<<tokens, 256, hidden * 4, s>>>(ff, x, w_post_ffw, eps, 0, hidden, xs);
-  return cudaGetLastError();
+  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(256), hidden * 4, s, ff, x, w_post_ffw, eps, (int32_t)0,
+                  hidden, xs);
 }
 
 cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const int32_t* w_ple_post,
                                 int64_t eps, int32_t layer_scalar, uint32_t tokens, uint32_t hidden,
                                 int32_t* x_out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  gemma_norm_add_kernel<<<tokens, 256, hidden * 4, s>>>(proj, xs, w_ple_post, eps, layer_scalar, hidden, x_out);
-  return cudaGetLastError();
+  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(256), hidden * 4, s, proj, xs, w_ple_post, eps,
+                  layer_scalar, hidden, x_out);
 }
 
 // Warp per (token, row) dense product.
 __global__ void dense_kernel(const int32_t* __restrict__ w, uint32_t rows, uint32_t cols,
                              const int32_t* __restrict__ in, uint32_t in_stride, uint32_t tokens,
                              int32_t* out, uint32_t out_stride, const int32_t* gate, uint32_t gate_stride) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows * tokens) return;
   const uint32_t t = warp / rows, r = warp % rows;
@@ -800,15 +820,16 @@ cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const i
                          const int32_t* gelu_gate, uint32_t gate_stride, cudaStream_t s) {
   uint64_t warps = (uint64_t)rows * tokens;
   if (warps == 0) return cudaSuccess;
-  dense_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(w, rows, cols, in, in_stride, tokens, out,
-                                                           out_stride, gelu_gate, gate_stride);
-  return cudaGetLastError();
+  return launch_k(dense_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, w, rows, cols, in, in_stride, tokens,
+                  out, out_stride, gelu_gate, gate_stride);
 }
 
 __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, const uint16_t* es,
                                    uint32_t ekc, uint32_t enslices, const uint32_t* ids, const int32_t* ple_norm,
                                    int64_t eps, int32_t projection_scalar, int32_t embedding_scale,
                                    int32_t input_scale, uint32_t L, uint32_t P, int32_t* out) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) int32_t row[];  // [P]
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x, l = blockIdx.y, id = ids[t];
@@ -833,11 +854,9 @@ cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_
                                int32_t* out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   dim3 grid(tokens, layers);
-  ple_prepare_kernel<<<grid, 128, P * 4, s>>>(projected, ple_embed->q, ple_embed->s, ple_embed->kc,
-                                              ple_embed->nslices, d_ids,
-                                              ple_norm, eps, projection_scalar, embedding_scale,
-                                              input_scale, layers, P, out);
-  return cudaGetLastError();
+  return launch_k(ple_prepare_kernel, grid, dim3(128), P * 4, s, projected, (const int8_t*)ple_embed->q,
+                  (const uint16_t*)ple_embed->s, ple_embed->kc, ple_embed->nslices, d_ids, ple_norm, eps,
+                  projection_scalar, embedding_scale, input_scale, layers, P, out);
 }
 
 }  // namespace iris

@@ -238,8 +238,8 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   a.counters = s->counters;
   a.cap = s->cap;
   a.nchunks = s->nchunks;
-  a.hpc = attention_cluster_hpc(m->heads, m->kvh, m->d);
-  a.cluster = 1;
+  a.hpc = s->hpc;
+  a.cluster = 0;
   return a;
 }
 

@@ -279,6 +279,8 @@ __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
 
 __global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
                               int64_t eps, uint32_t K, uint8_t* planes) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
   uint32_t t = blockIdx.x;
@@ -288,8 +290,7 @@ __global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __re
 cudaError_t launch_planes(const int32_t* x, const int32_t* norm_w, int64_t eps, uint32_t tokens,
                           uint32_t cols, uint8_t* planes, cudaStream_t stream) {
   if (tokens == 0) return cudaSuccess;
-  planes_kernel<<<tokens, 256, 0, stream>>>(x, norm_w, eps, cols, planes);
-  return cudaGetLastError();
+  return launch_k(planes_kernel, dim3(tokens), dim3(256), 0, stream, x, norm_w, eps, cols, planes);
 }
 
 // ---------------------------------------------------------------------------
@@ -473,9 +474,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   };
 
   // The first stages need no release: issue them before the prologue.
+  // Weights never change: the first stages stream while the previous kernel
+  // of the stream finishes; the activations are read only after pdl_wait().
+  pdl_trigger();
   const uint32_t first = nitems < p.stages ? nitems : p.stages;
   if (producer && lane == 0)
     for (uint32_t item = 0; item < first; ++item) issue(item);
+  pdl_wait();
 
   // Activation planes; `wide` when some value needs the fourth plane.
   bool wide;
@@ -595,6 +600,8 @@ constexpr int kTileN = 64, kTileM = 32, kWPitch = 48;
 
 template <int EPI>
 __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ __align__(16) uint8_t sw[kTileN * kWPitch];
   __shared__ uint16_t ssc[kTileN];
   __shared__ __align__(16) uint8_t sp[kTileM * 4 * 32];
@@ -694,8 +701,7 @@ template <int IN, int EPI>
 cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
   GemvPlan p;
   if (!plan_gemv(a.rows, a.cols, a.kc, device_sms(), &p)) return cudaErrorInvalidValue;
-  q8_gemv_tma_kernel<IN, EPI><<<p.grid, kTmaThreads, p.smem, stream>>>(a, p);
-  return cudaGetLastError();
+  return launch_k(q8_gemv_tma_kernel<IN, EPI>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, a, p);
 }
 
 template <int IN, int EPI>
@@ -727,8 +733,7 @@ cudaError_t prepare_product_kernels() {
 template <int EPI>
 cudaError_t launch_gemm(const ProductArgs& a, cudaStream_t stream) {
   dim3 grid((a.rows + kTileN - 1) / kTileN, (a.tokens + kTileM - 1) / kTileM);
-  q8_gemm_kernel<EPI><<<grid, 256, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_k(q8_gemm_kernel<EPI>, grid, dim3(256), 0, stream, a);
 }
 
 template <int IN>
