@@ -36,6 +36,7 @@ extern "C" {
 #define IRIS_ESTATE 10004   /* call out of order (e.g. decode before prefill) */
 #define IRIS_EWINDOW 10005  /* attention window not covered by the given keys */
 #define IRIS_ESTALL 10006   /* a kernel gave up a bounded wait (pipeline stalled) */
+#define IRIS_ESCRATCH 10007 /* input larger than a fixed scratch array */
 
 /* ---------------------------------------------------------------------------
  * 1. Drop-in for the reference's q8gpu_* FFI. Same names, signatures and
@@ -80,6 +81,17 @@ int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_acti
 #define IRIS_PATH_AUTO 0
 #define IRIS_PATH_GEMV 1
 #define IRIS_PATH_GEMM 2
+/* No counterpart in the reference. The same product as
+ * iris_q8_product_device, allocating nothing: the GEMM path's byte planes
+ * live in a fixed 16 MiB device array, so tokens > 1 needs
+ * tokens * cols * 4 <= 16 MiB (else IRIS_ESCRATCH, nothing launched); one
+ * token needs no scratch. The first call on each device looks the array's
+ * address up (make it before any stream capture begins). Nothing must start
+ * at zero. Asynchronous and not synchronized: calls in flight at the same time
+ * on one device (other streams or host threads) share the array and race;
+ * calls on one stream are ordered. */
+int iris_q8_product_device_noalloc(const Q8GpuMatrix* matrix, const int32_t* d_activations,
+                                   uint32_t tokens, int32_t* d_out, void* stream);
 
 /* ---------------------------------------------------------------------------
  * 3. Device-resident models, sessions and the decode loop.

@@ -15,6 +15,8 @@ PKG = Path(__file__).resolve().parent
 LIB_PATH = PKG / "libiris_b200.so"
 
 IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 10001, 10002, 10003, 10004, 10005, 10006
+IRIS_ESCRATCH = 10007
+NOALLOC_PLANES_BYTES = 16 << 20
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
 
 # Tensor kinds (include/iris_b200.h)
@@ -65,6 +67,7 @@ SIGNATURES = {
     "iris_q8_upload_blocks": (C.c_int, [u8p, C.c_uint32, C.c_uint32, C.POINTER(vp)]),
     "iris_q8_product_device": (C.c_int, [vp, vp, C.c_uint32, vp, vp]),
     "iris_q8_product_device_path": (C.c_int, [vp, vp, C.c_uint32, vp, vp, C.c_int]),
+    "iris_q8_product_device_noalloc": (C.c_int, [vp, vp, C.c_uint32, vp, vp]),
     "iris_model_create_mistral": (C.c_int, [C.POINTER(MistralShape), C.POINTER(vp)]),
     "iris_model_create_gemma": (C.c_int, [C.POINTER(GemmaShape), C.POINTER(vp)]),
     "iris_model_set_q8": (C.c_int, [vp, C.c_int, C.c_int32, u8p, C.c_uint64]),

@@ -835,6 +835,8 @@ const char* iris_error(int code) {
     case IRIS_ESTATE: return "iris: call out of order";
     case IRIS_EWINDOW: return "iris: attention window not covered by the keys";
     case IRIS_ESTALL: return "iris: a kernel gave up a bounded wait (stalled pipeline)";
+    case IRIS_ESCRATCH:
+      return "iris: input larger than the fixed no-alloc scratch (tokens * cols * 4 must be <= 16 MiB)";
     default: return cudaGetErrorString((cudaError_t)code);
   }
 }
@@ -930,6 +932,57 @@ int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint
 int iris_q8_product_device(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
                            int32_t* d_out, void* stream) {
   return iris_q8_product_device_path(m, d_act, tokens, d_out, stream, IRIS_PATH_AUTO);
+}
+
+// ---- the product without allocation -----------------------------------------
+//
+// The byte planes of the GEMM path live in a fixed device array instead of
+// the grown-on-demand scratch above. Its address is looked up once per device
+// (cudaGetSymbolAddress with that device current) by the first call made on
+// it. Every byte a call reads is written earlier in the same call, so nothing
+// needs to start at zero. Calls in flight at the same time on one device
+// (other streams, other host threads) share the array and race; calls queued
+// on one stream are ordered and do not.
+constexpr size_t kNoAllocPlanesBytes = (size_t)16 << 20;  // tokens * cols * 4 at most
+static __device__ __align__(256) uint8_t g_noalloc_planes[kNoAllocPlanesBytes];
+constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_noalloc_mutex;
+static uint8_t* g_noalloc_addr[kNoAllocMaxDevices];
+
+static cudaError_t noalloc_planes(uint8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_planes);
+    if (e != cudaSuccess) return e;
+    g_noalloc_addr[dev] = (uint8_t*)p;
+  }
+  *out = g_noalloc_addr[dev];
+  return cudaSuccess;
+}
+
+int iris_q8_product_device_noalloc(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
+                                   int32_t* d_out, void* stream) {
+  if (!m) return IRIS_EINVAL;
+  if (tokens > 1 && (uint64_t)tokens * m->cols * 4 > kNoAllocPlanesBytes) return IRIS_ESCRATCH;
+  uint8_t* planes = nullptr;
+  cudaError_t e = noalloc_planes(&planes);
+  if (e != cudaSuccess || tokens == 0) return (int)e;
+  cudaStream_t s = (cudaStream_t)stream;
+  ProductArgs a = product_args(m, tokens);
+  a.out = d_out;
+  if (tokens == 1) {
+    a.x = d_act;
+    return (int)launch_product(a, IN_RAW, EPI_STORE, s, IRIS_PATH_GEMV);
+  }
+  e = launch_planes(d_act, nullptr, 0, tokens, m->cols, planes, s);
+  a.planes = planes;
+  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, IRIS_PATH_GEMM);
+  return (int)e;
 }
 
 int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tokens, int32_t* out) {
