@@ -205,12 +205,32 @@ int iris_session_product(IrisSession* session, uint32_t layer, int which);
  * stream: the last held position attends over the positions before it, with
  * the session's current query rows; the context is discarded. For timing. */
 int iris_session_attention(IrisSession* session, uint32_t layer);
+/* Selects the decode attention kernels of a session: IRIS_ATTN_AUTO (one
+ * thread-block-cluster launch where the device and shape allow it) or
+ * IRIS_ATTN_SPLIT (three launches over position chunks). Both give the same
+ * values; the captured decode pass is rebuilt. */
+int iris_session_set_attention(IrisSession* session, int mode);
+#define IRIS_ATTN_AUTO 0
+#define IRIS_ATTN_SPLIT 1
+/* Tuning hook: an explicit one-launch decode attention shape - blocks a
+ * cluster (4, 8 or 16), query heads a block (1, 2 or 4, dividing the group)
+ * and shared-memory tile buffers a block (2..12). IRIS_EINVAL when the shape
+ * does not fit the model, the capacity or the device. */
+int iris_session_set_attention_shape(IrisSession* session, uint32_t cluster, uint32_t hpc, uint32_t ring);
 /* Reads count K/V rows of one layer starting at position first
  * (kv_heads*head_dim values each). For a gemma sliding layer these are the
  * positions the window still holds. */
 int iris_session_get_kv(const IrisSession* session, uint32_t layer, uint32_t first, uint32_t count,
                         int32_t* k, int32_t* v);
 void iris_session_free(IrisSession* session);
+
+/* Stream capture for replaying a sequence of this library's launches as one
+ * CUDA graph (timing, serving loops). Between begin and end, launches on
+ * `stream` (cudaStream_t as void*) from this thread are recorded, not run. */
+int iris_capture_begin(void* stream);
+int iris_capture_end(void* stream, void** graph_exec);
+int iris_graph_launch(void* graph_exec, void* stream);
+void iris_graph_free(void* graph_exec);
 
 /* ---------------------------------------------------------------------------
  * 4. The teacher-forced chain stage: one layer over one range of rows

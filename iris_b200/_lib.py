@@ -18,6 +18,7 @@ IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 
 IRIS_ESCRATCH = 10007
 NOALLOC_PLANES_BYTES = 16 << 20
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
+ATTN_AUTO, ATTN_SPLIT = 0, 1
 
 # Tensor kinds (include/iris_b200.h)
 T = dict(EMBED=0, HEAD=1, FINAL_NORM=2, W_Q=3, W_K=4, W_V=5, W_O=6, W_GATE=7, W_UP=8, W_DOWN=9,
@@ -89,8 +90,14 @@ SIGNATURES = {
     "iris_session_graph_kernels": (C.c_uint32, [vp]),
     "iris_session_product": (C.c_int, [vp, C.c_uint32, C.c_int]),
     "iris_session_attention": (C.c_int, [vp, C.c_uint32]),
+    "iris_session_set_attention": (C.c_int, [vp, C.c_int]),
+    "iris_session_set_attention_shape": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32]),
     "iris_session_get_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i32p, i32p]),
     "iris_session_free": (None, [vp]),
+    "iris_capture_begin": (C.c_int, [vp]),
+    "iris_capture_end": (C.c_int, [vp, C.POINTER(vp)]),
+    "iris_graph_launch": (C.c_int, [vp, vp]),
+    "iris_graph_free": (None, [vp]),
     "iris_mistral_layer_range": (C.c_int, [vp, C.c_uint32, i32p, C.c_uint32, C.c_uint32, i32p, i32p,
                                            i32p, i32p, i32p]),
     "iris_synth_q8": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.c_int, u8p]),

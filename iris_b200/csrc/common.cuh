@@ -109,14 +109,27 @@ __device__ __forceinline__ uint64_t global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// try_wait that may suspend the thread for up to 20 us while the phase is
+// incomplete (it resumes as soon as the phase completes), so that waiting
+// warps do not take issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
 // Waits for the phase of `bar` with the given parity to complete, giving up
 // after about one second; a give-up is recorded in *fault.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned int* fault) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 0 && global_ns() - t0 > 1000000000ull) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if ((i & 15) == 0 && global_ns() - t0 > 1000000000ull) {
       atomicOr(fault, 1u);
       return false;
     }
@@ -207,6 +220,25 @@ __device__ __forceinline__ uint64_t warp_sum_sat_nonneg(uint64_t v) {
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) v = add_sat_nonneg(v, __shfl_xor_sync(0xffffffffu, v, off));
   return v;
+}
+
+// inv_sqrt_acc (ops.rs:722-771) by a warp: the largest c with c^2 x <= 2^64
+// is found five bits a round (lane j tests the next five bits = j; the
+// predicate falls with c, so the lanes that pass are a prefix), then the same
+// tie-break. Every lane passes the same x and gets the same value.
+__device__ __forceinline__ int32_t inv_sqrt_acc_warp(int64_t xs) {
+  if (xs <= 0) return INT32_MAX;
+  const uint64_t x = (uint64_t)xs;
+  if (inv_sqrt_le_target((uint32_t)INT32_MAX, x)) return INT32_MAX;
+  const uint32_t lane = threadIdx.x & 31;
+  uint32_t base = 0;  // c^2 x <= 2^64 holds at base
+#pragma unroll
+  for (int shift = 26; shift >= 1; shift -= 5) {
+    const uint32_t ok = __ballot_sync(0xffffffffu, inv_sqrt_le_target(base + (lane << shift), x));
+    base += (uint32_t)(__popc(ok) - 1) << shift;
+  }
+  if (inv_sqrt_le_target(base + 1, x)) base += 1;
+  return inv_sqrt_pick(base, x);
 }
 
 // Writes one activation into the four planes of a K-wide row.

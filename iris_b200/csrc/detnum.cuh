@@ -124,18 +124,10 @@ IRIS_HD bool inv_sqrt_le_target(uint32_t c, uint64_t x) {  // c^2 * x <= 2^64
   uint64_t lo = sq * x, hi = mulhi_u64(sq, x);
   return hi == 0 || (hi == 1 && lo == 0);
 }
-IRIS_HD int32_t inv_sqrt_acc(int64_t xs) {
-  if (xs <= 0) return INT32_MAX;  // only 0 reaches here: eps and squares are >= 0
-  uint64_t x = (uint64_t)xs;
-  const uint32_t max_bits = (uint32_t)INT32_MAX;
-  if (inv_sqrt_le_target(max_bits, x)) return INT32_MAX;
-  uint32_t low = 0, high = max_bits;
-  while (low < high) {
-    uint32_t mid = low + ((high - low + 1) >> 1);
-    if (inv_sqrt_le_target(mid, x)) low = mid;
-    else high = mid - 1;
-  }
-  uint32_t lower = low, upper = low + 1;  // low < max_bits here
+// The tie-break of inv_sqrt_acc between low (the largest c with c^2 x <= 2^64,
+// below i32::MAX) and low + 1.
+IRIS_HD int32_t inv_sqrt_pick(uint32_t low, uint64_t x) {
+  uint32_t lower = low, upper = low + 1;
   // errors |c^2 x - 2^64| as 128-bit (hi, lo) pairs
   uint64_t sq_l = (uint64_t)lower * lower, sq_u = (uint64_t)upper * upper;
   uint64_t l_lo = sq_l * x, l_hi = mulhi_u64(sq_l, x);  // <= 2^64
@@ -152,6 +144,19 @@ IRIS_HD int32_t inv_sqrt_acc(int64_t xs) {
   else if (u_less) r = upper;
   else r = (lower & 1) == 0 ? lower : upper;
   return (int32_t)r;
+}
+IRIS_HD int32_t inv_sqrt_acc(int64_t xs) {
+  if (xs <= 0) return INT32_MAX;  // only 0 reaches here: eps and squares are >= 0
+  uint64_t x = (uint64_t)xs;
+  const uint32_t max_bits = (uint32_t)INT32_MAX;
+  if (inv_sqrt_le_target(max_bits, x)) return INT32_MAX;
+  uint32_t low = 0, high = max_bits;
+  while (low < high) {
+    uint32_t mid = low + ((high - low + 1) >> 1);
+    if (inv_sqrt_le_target(mid, x)) low = mid;
+    else high = mid - 1;
+  }
+  return inv_sqrt_pick(low, x);
 }
 // rms_norm_scale (ops.rs:409-428) from the saturated sum of squares.
 IRIS_HD int32_t rms_scale_from_sumsq(uint64_t sumsq_sat, uint32_t n, int64_t eps) {
@@ -324,6 +329,30 @@ IRIS_HD int32_t softmax_weight(int64_t term, uint64_t sum) {
     uint64_t q0 = UINT64_MAX / sum, r0 = UINT64_MAX - q0 * sum;
     if (r0 + 1 == sum) { q = q0 + 1; r = 0; }
     else { q = q0; r = r0 + 1; }
+  }
+  uint64_t other = sum - r;
+  if (r > other) q += 1;
+  else if (r == other) q += (q & 1);
+  return requantize((int64_t)q);
+}
+
+// softmax_weight with the divisor's reciprocal inv = floor((2^64 - 1) / sum)
+// computed once for every weight of a head. For n = term * 2^32 < 2^64,
+// floor(n * inv / 2^64) is q, q - 1 or q - 2 (q = floor(n / sum)), so two
+// exact corrections give the same quotient and remainder as the division;
+// sum < 2^62 keeps n - q_est * sum < 3 sum inside 64 bits.
+IRIS_HD int32_t softmax_weight_inv(int64_t term, uint64_t sum, uint64_t inv) {
+  uint64_t q, r;
+  if (term < kOneAcc) {
+    const uint64_t n = (uint64_t)term << 32;
+    q = mulhi_u64(n, inv);
+    r = n - q * sum;
+    if (r >= sum) { q += 1; r -= sum; }
+    if (r >= sum) { q += 1; r -= sum; }
+  } else {  // dividend 2^64 = (2^64 - 1) + 1
+    const uint64_t r0 = UINT64_MAX - inv * sum;
+    if (r0 + 1 == sum) { q = inv + 1; r = 0; }
+    else { q = inv; r = r0 + 1; }
   }
   uint64_t other = sum - r;
   if (r > other) q += 1;

@@ -266,226 +266,372 @@ uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads) {
 
 uint32_t attention_chunks(uint32_t cap) { return (cap + kAttnChunk - 1) / kAttnChunk; }
 
-uint32_t attention_cluster_hpc(uint32_t heads, uint32_t kv_heads, uint32_t d) {
-  uint32_t G = heads / kv_heads, hpc = G < (uint32_t)kMaxHpc ? G : (uint32_t)kMaxHpc;
-  if (d == 256 && hpc > 2) hpc = 2;
-  while (hpc > 1 && (G % hpc || heads / hpc < 16)) --hpc;
-  return hpc;
-}
-
 // ---------------------------------------------------------------------------
 // Decode attention in one launch: a thread-block cluster a head block
 // ---------------------------------------------------------------------------
 //
-// A cluster of kClusterCtas blocks owns hpc query heads of one kv group; block
-// rank r takes the r-th of kClusterCtas contiguous ranges of the window
-// [ws, p]. The three dependent steps of attention_softmax meet through
-// distributed shared memory (cluster barriers, no global atomics):
-//   1. scores of the block's positions (kept in the scores scratch) and the
-//      block's first maximum a head; cluster barrier; every block takes the
-//      maximum over the cluster;
-//   2. exp terms against it (terms scratch) and their sum a head; cluster
-//      barrier; every block takes the total over the cluster;
-//   3. weights (written over the scores), their sum a head, and the wrapping
-//      weighted value sums of the block's positions; cluster barrier; block
-//      r finishes its share of the head dimensions: the sum over the cluster
-//      plus (1.0 - sum of weights) times the first maximum's value, then
-//      requantize and write the context planes.
+// A cluster of C blocks (16 where the device allows it, else 8) owns HPC
+// query heads of one kv group; block rank r takes the r-th of C contiguous
+// ranges of the window [ws, p]. The block's key rows and then its value rows
+// stream as one sequence of 32-position tiles through a ring of shared-memory
+// buffers with cp.async: all of them are in flight from the start when the
+// ring holds them, and the HPC query heads share every key and value read.
+// The three dependent steps of attention_softmax (ops.rs:233-261) meet
+// through distributed shared memory:
+//   1. scores of the block's positions and the block's first maximum a head;
+//      cluster barrier; every block takes the maximum over the cluster;
+//   2. exp terms against it (kept) and their sum a head; cluster barrier;
+//      every block takes the total over the cluster;
+//   3. weights (one reciprocal a head, softmax_weight_inv), their sum a head,
+//      and the wrapping weighted value sums of the block's positions;
+//      cluster barrier; block r finishes its share of the head dimensions:
+//      the sum over the cluster plus (1.0 - sum of weights) times the first
+//      maximum's value row (ops.rs:274-276), requantized into the context
+//      planes.
+// Every block passes every cluster barrier, also one with no positions.
 
-constexpr uint32_t kClusterCtas = 8;
-constexpr uint32_t kClusterWarps = kAttnThreads / 32;
+constexpr uint32_t kCThreads = 512;   // 16 warps
+constexpr uint32_t kTileP = 32;       // positions a tile (= 8 warps x 4 positions)
+constexpr uint32_t kMaxRing = 12;     // tile buffers at most
+constexpr size_t kClusterSmemMax = 200 * 1024;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most n of this thread's committed groups are pending.
+__device__ __forceinline__ void cp_async_wait_pending(uint32_t n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    case 7: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+    case 8: asm volatile("cp.async.wait_group 8;" ::: "memory"); break;
+    case 9: asm volatile("cp.async.wait_group 9;" ::: "memory"); break;
+    case 10: asm volatile("cp.async.wait_group 10;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 11;" ::: "memory"); break;
+  }
+}
+
+// acc += a * b, the 32 x 32 -> 64-bit product added with 64-bit wraparound
+// (one multiply-add).
+__device__ __forceinline__ void mac_wide(int64_t& acc, int32_t a, int32_t b) {
+  asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+}
+
+// The 16-byte pieces this thread copies of every [kTileP][D] tile: piece c =
+// tid + j kCThreads is row c / (D/4), column piece c % (D/4). Offsets are
+// fixed for the kernel; a tile only moves the base position.
+template <uint32_t D>
+struct TileCopier {
+  static constexpr uint32_t kPieces = (kTileP * D / 4 + kCThreads - 1) / kCThreads;
+  uint32_t row[kPieces], soff[kPieces];
+  size_t goff[kPieces];
+  __device__ TileCopier(uint32_t kvd, uint32_t g) {
+#pragma unroll
+    for (uint32_t j = 0; j < kPieces; ++j) {
+      const uint32_t c = threadIdx.x + j * kCThreads, r = c / (D / 4), piece = c % (D / 4);
+      row[j] = c < kTileP * D / 4 ? r : kTileP;  // kTileP: no piece
+      soff[j] = r * D + 4 * piece;
+      goff[j] = (size_t)r * kvd + g * D + 4 * piece;
+    }
+  }
+  // Rows [t0, min(t0 + kTileP, r1)) of the cache into buf.
+  __device__ __forceinline__ void load(int32_t* buf, const int32_t* cache, uint32_t kvd, uint32_t t0,
+                                       uint32_t r1) const {
+    const int32_t* base = cache + (size_t)t0 * kvd;
+#pragma unroll
+    for (uint32_t j = 0; j < kPieces; ++j)
+      if (row[j] < kTileP && t0 + row[j] < r1) cp_async16(buf + soff[j], base + goff[j]);
+  }
+};
+
+// Warp-wide sums over the lanes that share lane % HPC; lane h < HPC ends with
+// the sum of head h's lanes.
+template <uint32_t HPC, typename T>
+__device__ __forceinline__ T head_lane_sum(T v) {
+#pragma unroll
+  for (uint32_t off = 16; off >= HPC; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
 
 template <uint32_t PER, uint32_t HPC>
-__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kAttnThreads)
-    attn_cluster_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnArgs a) {
   pdl_trigger();
   pdl_wait();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
-  constexpr uint32_t D = PER * 8;
-  extern __shared__ __align__(16) int64_t wpart[];  // [kClusterWarps][HPC][D], then part [HPC][D]
-  int64_t* part = wpart + kClusterWarps * HPC * D;
-  __shared__ unsigned long long best_s[HPC];
-  __shared__ unsigned long long sum_s[HPC];
-  __shared__ int32_t wsum_s[HPC];
-  __shared__ unsigned long long gbest_s[HPC];
-  __shared__ unsigned long long gtotal_s[HPC];
-  __shared__ int32_t resid_s[HPC];
+  constexpr uint32_t D = PER * 8, NH = kCThreads / D;
+  constexpr uint32_t HG = HPC >= 2 ? 2 : 1, HH = HPC / HG;  // warp groups of the score step, heads each
+  constexpr uint32_t tile_ints = kTileP * D;
+  const uint32_t ring = a.ring, span_a = a.span;      // span_a even
+  extern __shared__ __align__(16) int32_t dsm[];
+  int32_t* tiles = dsm;                               // [ring][kTileP][D]
+  uint64_t* tm = (uint64_t*)(tiles + ring * tile_ints);  // [span][HPC] exp terms
+  int32_t* sw = (int32_t*)(tm + span_a * HPC);        // [span][HPC] scores, then weights
+  int64_t* part = (int64_t*)(sw + span_a * HPC);      // [HPC][D]
+  __shared__ unsigned long long best_s[HPC], sum_s[HPC], gbest_s[HPC], gtotal_s[HPC], ginv_s[HPC];
+  __shared__ int32_t wsum_s[HPC], resid_s[HPC];
 
-  const uint32_t rank = cluster.block_rank();
-  const uint32_t hb = blockIdx.x / kClusterCtas, h0 = hb * HPC, G = a.heads / a.kv_heads, g = h0 / G;
+  const uint32_t C = cluster.num_blocks(), rank = cluster.block_rank();
+  const uint32_t h0 = (blockIdx.x / C) * HPC, G = a.heads / a.kv_heads, g = h0 / G;
   const uint32_t p = query_position(a), ws = window_start(p, a.window), n = p - ws + 1;
-  const uint32_t span = (n + kClusterCtas - 1) / kClusterCtas;
-  const uint32_t r0 = ws + rank * span, r1 = min(p + 1, r0 + span);  // may be empty
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, quad = lane >> 3, ql = lane & 7;
-  if (threadIdx.x < HPC) {
-    best_s[threadIdx.x] = 0;
-    sum_s[threadIdx.x] = 0;
-    wsum_s[threadIdx.x] = 0;
-  }
-  __syncthreads();
+  const uint32_t span = (n + C - 1) / C;
+  const uint32_t r0 = min(p + 1, ws + rank * span), r1 = min(p + 1, r0 + span);
+  const uint32_t cnt = r1 - r0, ntiles = (cnt + kTileP - 1) / kTileP, nitems = 2 * ntiles;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quad = lane >> 3, ql = lane & 7;
 
-  // ---- 1. scores: 8 lanes a position, 4 positions a warp at a time
-  {
-    const uint32_t i0 = ql * PER;
-    int32_t q[HPC][PER];
+  // item i < ntiles: key tile i; item ntiles + i: value tile i. One commit
+  // group an item, issued in order; item i uses buffer i % ring.
+  const TileCopier<D> copier(a.kvd, g);
+  uint32_t issued = 0;
+  auto issue_upto = [&](uint32_t limit) {
+    limit = min(limit, nitems);
+    for (; issued < limit; ++issued) {
+      const bool key = issued < ntiles;
+      const uint32_t t0 = r0 + (key ? issued : issued - ntiles) * kTileP;
+      copier.load(tiles + (issued % ring) * tile_ints, key ? a.kcache : a.vcache, a.kvd, t0, r1);
+      cp_async_commit();
+    }
+  };
+  // Before consuming item i: its group has landed for every thread, and
+  // every thread is done with item i - 1, whose buffer item i - 1 + ring
+  // then takes.
+  auto acquire = [&](uint32_t i) {
+    cp_async_wait_pending(issued - (i + 1));
+    __syncthreads();
+    if (i >= 1) issue_upto(i - 1 + ring + 1);
+  };
+  issue_upto(ring);
+
+  for (uint32_t i = tid; i < HPC * D; i += kCThreads) part[i] = 0;
+  if (tid < HPC) {
+    best_s[tid] = 0;
+    sum_s[tid] = 0;
+    wsum_s[tid] = 0;
+  }
+
+  // ---- 1. scores: warp group wg (of HG) takes heads [wg HH, wg HH + HH); 8
+  // lanes a position, lane ql holding the 16-byte pieces ql, ql + 8, ...
+  const uint32_t wg = warp / 8, wl = warp % 8, hb = wg * HH;
+  const bool scoring = wg < HG;
+  int4 q[HH][PER / 4];
 #pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h)
+  for (uint32_t h = 0; h < HH; ++h)
 #pragma unroll
-      for (uint32_t i = 0; i < PER; i += 4) {
-        const int4 v = *(const int4*)(a.q + (size_t)(h0 + h) * D + i0 + i);
-        q[h][i] = v.x;
-        q[h][i + 1] = v.y;
-        q[h][i + 2] = v.z;
-        q[h][i + 3] = v.w;
+    for (uint32_t i = 0; i < PER / 4; ++i)
+      q[h][i] = scoring ? *(const int4*)(a.q + (size_t)(h0 + hb + h) * D + 4 * (ql + 8 * i)) : make_int4(0, 0, 0, 0);
+  unsigned long long best[HH];
+#pragma unroll
+  for (uint32_t h = 0; h < HH; ++h) best[h] = 0;
+  for (uint32_t k = 0; k < ntiles; ++k) {
+    acquire(k);
+    if (!scoring) continue;
+    const uint32_t tl = wl * 4 + quad, t = r0 + k * kTileP + tl;
+    const int32_t* krow = tiles + (k % ring) * tile_ints + tl * D;
+    int4 kv[PER / 4];
+#pragma unroll
+    for (uint32_t i = 0; i < PER / 4; ++i) kv[i] = *(const int4*)(krow + 4 * (ql + 8 * i));
+#pragma unroll
+    for (uint32_t h = 0; h < HH; ++h) {
+      int64_t c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+#pragma unroll
+      for (uint32_t i = 0; i < PER / 4; ++i) {
+        mac_wide(c0, q[h][i].x, kv[i].x);
+        mac_wide(c1, q[h][i].y, kv[i].y);
+        mac_wide(c2, q[h][i].z, kv[i].z);
+        mac_wide(c3, q[h][i].w, kv[i].w);
       }
-    unsigned long long best[HPC];
-#pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
-    for (uint32_t base = r0; base < r1; base += kClusterWarps * 4) {
-      const uint32_t t = base + warp * 4 + quad;
-      const bool live = t < r1;
-      const int32_t* krow = a.kcache + (size_t)(live ? t : r0) * a.kvd + g * D + i0;
-      int4 k[PER / 4];
-#pragma unroll
-      for (uint32_t i = 0; i < PER / 4; ++i) k[i] = *(const int4*)(krow + 4 * i);
-#pragma unroll
-      for (uint32_t h = 0; h < HPC; ++h) {
-        uint64_t sum = 0;
-#pragma unroll
-        for (uint32_t i = 0; i < PER / 4; ++i)
-          sum += (uint64_t)((int64_t)q[h][4 * i] * k[i].x) + (uint64_t)((int64_t)q[h][4 * i + 1] * k[i].y) +
-                 (uint64_t)((int64_t)q[h][4 * i + 2] * k[i].z) + (uint64_t)((int64_t)q[h][4 * i + 3] * k[i].w);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        if (ql == 0 && live) {
-          const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
-          a.scores[(size_t)(h0 + h) * a.cap + t] = sc;
-          const unsigned long long key = best_key(sc, t);
-          best[h] = key > best[h] ? key : best[h];
-        }
+      uint64_t sum = (uint64_t)c0 + (uint64_t)c1 + (uint64_t)c2 + (uint64_t)c3;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      if (ql == 0 && t < r1) {
+        const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
+        sw[(t - r0) * HPC + hb + h] = sc;
+        const unsigned long long key = best_key(sc, t);
+        best[h] = key > best[h] ? key : best[h];
       }
     }
-#pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h)
-      if (ql == 0 && best[h]) atomicMax(&best_s[h], best[h]);
   }
+#pragma unroll
+  for (uint32_t h = 0; h < HH; ++h)
+    if (scoring && ql == 0 && best[h]) atomicMax(&best_s[hb + h], best[h]);
   cluster.sync();
-  if (threadIdx.x < HPC) {
+  if (tid < HPC) {
     unsigned long long b = 0;
-    for (uint32_t r = 0; r < kClusterCtas; ++r) {
-      const unsigned long long v = *cluster.map_shared_rank(&best_s[threadIdx.x], r);
+    for (uint32_t r = 0; r < C; ++r) {
+      const unsigned long long v = *cluster.map_shared_rank(&best_s[tid], r);
       b = v > b ? v : b;
     }
-    gbest_s[threadIdx.x] = b;
+    gbest_s[tid] = b;
   }
   __syncthreads();
 
-  // ---- 2. exp terms and their sums
-  const uint32_t cnt = r1 > r0 ? r1 - r0 : 0;
-  for (uint32_t idx = threadIdx.x; idx < HPC * cnt; idx += blockDim.x) {
-    const uint32_t h = idx / cnt, t = r0 + idx % cnt;
-    const size_t at = (size_t)(h0 + h) * a.cap + t;
-    const int64_t e = softmax_exp_term_act(a.scores[at], best_key_value(gbest_s[h]));
-    a.terms[at] = e;
-    atomicAdd(&sum_s[h], (unsigned long long)e);
+  // ---- 2. exp terms against the global first maximum (kept), and their sums.
+  // Element e = position * HPC + head: thread tid always meets head tid % HPC.
+  const uint32_t my_h = tid % HPC;
+  {
+    const int32_t mx = best_key_value(gbest_s[my_h]);
+    uint64_t e = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kCThreads) {
+      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
+      tm[el] = term;
+      e += term;
+    }
+    e = head_lane_sum<HPC>(e);
+    if (lane < HPC && e) atomicAdd(&sum_s[lane], (unsigned long long)e);
   }
   cluster.sync();
-  if (threadIdx.x < HPC) {
+  if (tid < HPC) {
     unsigned long long tot = 0;
-    for (uint32_t r = 0; r < kClusterCtas; ++r) tot += *cluster.map_shared_rank(&sum_s[threadIdx.x], r);
-    gtotal_s[threadIdx.x] = tot;
+    for (uint32_t r = 0; r < C; ++r) tot += *cluster.map_shared_rank(&sum_s[tid], r);
+    gtotal_s[tid] = tot;
+    ginv_s[tid] = UINT64_MAX / tot;  // tot >= 2^32: the first maximum's term is 2^32
   }
   __syncthreads();
 
-  // ---- 3. weights (over the scores), weight sums, weighted value sums
-  for (uint32_t idx = threadIdx.x; idx < HPC * cnt; idx += blockDim.x) {
-    const uint32_t h = idx / cnt, t = r0 + idx % cnt;
-    const size_t at = (size_t)(h0 + h) * a.cap + t;
-    const int32_t w = softmax_weight(a.terms[at], gtotal_s[h]);
-    a.scores[at] = w;
-    atomicAdd(&wsum_s[h], w);
-  }
-  __syncthreads();
+  // ---- 3. weights over the scores and their sums, then the value sums
   {
-    // warp w: positions r0 + w, r0 + w + kClusterWarps, ...; lane: 4 dims at a time
-    uint64_t acc[HPC][(D + 127) / 128][4];
-#pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h)
-#pragma unroll
-      for (uint32_t c = 0; c < (D + 127) / 128; ++c)
-#pragma unroll
-        for (uint32_t j = 0; j < 4; ++j) acc[h][c][j] = 0;
-#pragma unroll 4
-    for (uint32_t t = r0 + warp; t < r1; t += kClusterWarps) {
-      const int32_t* vrow = a.vcache + (size_t)t * a.kvd + g * D;
-#pragma unroll
-      for (uint32_t c = 0; c < (D + 127) / 128; ++c) {
-        const uint32_t dim = c * 128 + 4 * lane;
-        if (dim < D) {
-          const int4 v = *(const int4*)(vrow + dim);
-#pragma unroll
-          for (uint32_t h = 0; h < HPC; ++h) {
-            const int64_t w = a.scores[(size_t)(h0 + h) * a.cap + t];
-            acc[h][c][0] += (uint64_t)(w * v.x);
-            acc[h][c][1] += (uint64_t)(w * v.y);
-            acc[h][c][2] += (uint64_t)(w * v.z);
-            acc[h][c][3] += (uint64_t)(w * v.w);
-          }
-        }
-      }
+    const uint64_t tot = gtotal_s[my_h], inv = ginv_s[my_h];
+    int32_t wsum = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kCThreads) {
+      const int32_t w = softmax_weight_inv((int64_t)tm[el], tot, inv);
+      sw[el] = w;
+      wsum += w;
     }
+    wsum = head_lane_sum<HPC>(wsum);
+    if (lane < HPC && wsum) atomicAdd(&wsum_s[lane], wsum);
+  }
+  const uint32_t dim = tid % D, hv = tid / D;
+  int64_t acc[HPC];
 #pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h)
-#pragma unroll
-      for (uint32_t c = 0; c < (D + 127) / 128; ++c) {
-        const uint32_t dim = c * 128 + 4 * lane;
-        if (dim < D)
-#pragma unroll
-          for (uint32_t j = 0; j < 4; ++j) wpart[(warp * HPC + h) * D + dim + j] = (int64_t)acc[h][c][j];
+  for (uint32_t h = 0; h < HPC; ++h) acc[h] = 0;
+  for (uint32_t k = 0; k < ntiles; ++k) {
+    acquire(ntiles + k);  // also orders the weights above before their reads
+    const int32_t* buf = tiles + ((ntiles + k) % ring) * tile_ints;
+    const uint32_t base = k * kTileP, rows = min(kTileP, cnt - base);
+#pragma unroll 4
+    for (uint32_t r = hv; r < rows; r += NH) {
+      const int32_t v = buf[r * D + dim];
+      int32_t w[HPC];
+      if (HPC == 4) {
+        const int4 w4 = *(const int4*)(sw + (base + r) * HPC);
+        w[0] = w4.x, w[1] = w4.y, w[2 % HPC] = w4.z, w[3 % HPC] = w4.w;
+      } else if (HPC == 2) {
+        const int2 w2 = *(const int2*)(sw + (base + r) * HPC);
+        w[0] = w2.x, w[1 % HPC] = w2.y;
+      } else {
+        w[0] = sw[base + r];
       }
-  }
-  __syncthreads();
-  for (uint32_t o = threadIdx.x; o < HPC * D; o += blockDim.x) {
-    uint64_t s = 0;
 #pragma unroll
-    for (uint32_t w = 0; w < kClusterWarps; ++w) s += (uint64_t)wpart[w * HPC * D + o];
-    part[o] = (int64_t)s;
+      for (uint32_t h = 0; h < HPC; ++h) mac_wide(acc[h], w[h], v);
+    }
   }
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+    if (acc[h]) atomicAdd((unsigned long long*)&part[h * D + dim], (unsigned long long)acc[h]);
   cluster.sync();
 
   // ---- 4. block `rank` finishes outputs [rank * share, (rank + 1) * share)
-  if (threadIdx.x < HPC) {
-    int32_t sw = 0;
-    for (uint32_t r = 0; r < kClusterCtas; ++r) sw += *cluster.map_shared_rank(&wsum_s[threadIdx.x], r);
-    resid_s[threadIdx.x] = sub_sat(kOneAct, sw);  // residual (ops.rs:274-276)
+  if (tid < HPC) {
+    int32_t total_w = 0;
+    for (uint32_t r = 0; r < C; ++r) total_w += *cluster.map_shared_rank(&wsum_s[tid], r);
+    resid_s[tid] = sub_sat(kOneAct, total_w);  // residual (ops.rs:274-276)
   }
   __syncthreads();
-  const uint32_t share = (HPC * D + kClusterCtas - 1) / kClusterCtas, qd = a.heads * D;
-  for (uint32_t o = rank * share + threadIdx.x; o < min(HPC * D, (rank + 1) * share); o += blockDim.x) {
+  const uint32_t share = (HPC * D + C - 1) / C, qd = a.heads * D;
+  for (uint32_t o = rank * share + tid; o < min(HPC * D, (rank + 1) * share); o += kCThreads) {
     const uint32_t h = o / D, i = o % D, hh = h0 + h;
     uint64_t s = 0;
-    for (uint32_t r = 0; r < kClusterCtas; ++r) s += (uint64_t)*cluster.map_shared_rank(&part[o], r);
+    for (uint32_t r = 0; r < C; ++r) s += (uint64_t)*cluster.map_shared_rank(&part[o], r);
     const uint32_t tmax = best_key_token(gbest_s[h]);
     s += (uint64_t)((int64_t)resid_s[h] * a.vcache[(size_t)tmax * a.kvd + g * D + i]);
     const int32_t v = requantize((int64_t)s);
     put_planes(a.ctx_planes, qd, hh * D + i, v);
     if (a.ctx) a.ctx[hh * D + i] = v;
   }
-  cluster.sync();  // the other blocks may still be reading this block's shared memory
+  cluster.sync();  // every block's shared memory stays until all have read it
 }
+
+// Shared memory of one block of the one-launch decode attention.
+size_t cluster_smem_bytes(uint32_t d, uint32_t hpc, uint32_t span, uint32_t ring) {
+  return (size_t)ring * kTileP * d * 4 + (size_t)span * hpc * 12 + (size_t)hpc * d * 8;
+}
+
+// Whether (cluster c, hpc, ring) is a valid one-launch shape for the model
+// and cache capacity, with every cluster resident at once; sets *span.
+int cluster_fits(uint32_t d, uint32_t hpc, uint32_t c, size_t smem);
+bool attention_cluster_shape_ok(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t c,
+                                uint32_t hpc, uint32_t ring, uint32_t* span) {
+  const uint32_t G = heads / kv_heads;
+  if (d % 32 || d > 256 || hpc == 0 || hpc > 4 || (hpc & (hpc - 1)) || G % hpc || hpc * d > 512) return false;
+  if (c != 4 && c != 8 && c != 16) return false;
+  if (ring < 2 || ring > kMaxRing) return false;
+  const uint32_t sp = (((cap + c - 1) / c) + 1) & ~1u;
+  const size_t smem = cluster_smem_bytes(d, hpc, sp, ring);
+  if (smem > kClusterSmemMax) return false;
+  if (cluster_fits(d, hpc, c, smem) < (int)(heads / hpc)) return false;
+  *span = sp;
+  return true;
+}
+
+// Query heads a block and blocks a cluster of the one-launch decode attention
+// (0 blocks: the shape is served by the three-launch path), the positions a
+// block at most and the tile buffers of its ring: the first shape of a
+// preference list whose clusters are all resident at once. Six buffers a
+// block (about 100 KB for d = 128) keep enough reads in flight and let two
+// blocks share a multiprocessor.
+void attention_cluster_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t* hpc,
+                            uint32_t* cluster, uint32_t* span, uint32_t* ring) {
+  const uint32_t G = heads / kv_heads;
+  uint32_t hmax = 4;
+  while (hmax > 1 && (G % hmax || hmax * d > 512)) hmax >>= 1;
+  const uint32_t hhalf = hmax > 1 ? hmax / 2 : 1;
+  const uint32_t shapes[4][2] = {{16, hmax}, {16, hhalf}, {8, hhalf}, {8, hmax}};
+  *hpc = hmax;
+  *cluster = 0;
+  *span = 0;
+  *ring = 0;
+  for (const auto& sh : shapes) {
+    const uint32_t sp = (((cap + sh[0] - 1) / sh[0]) + 1) & ~1u;
+    uint32_t rg = 2 * ((sp + kTileP - 1) / kTileP);  // every key and value tile of a block
+    rg = rg < 6 ? rg : 6;
+    rg = rg < 2 ? 2 : rg;
+    uint32_t got = 0;
+    if (!attention_cluster_shape_ok(heads, kv_heads, d, cap, sh[0], sh[1], rg, &got)) continue;
+    *hpc = sh[1];
+    *cluster = sh[0];
+    *span = got;
+    *ring = rg;
+    return;
+  }
+}
+
+size_t attention_cluster_smem(const AttnArgs& a) { return cluster_smem_bytes(a.d, a.chpc, a.span, a.ring); }
 
 cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s) {
   const uint32_t per = a.d / 8;
-  dim3 grid(kClusterCtas * (a.heads / a.hpc));
-  const size_t smem = (size_t)(kClusterWarps + 1) * a.hpc * a.d * sizeof(int64_t);
-#define IRIS_CLUSTER(PER, HPC)                                                  \
-  if (per == PER && a.hpc == HPC) {                                             \
-    cudaError_t e_ = launch_k(attn_cluster_kernel<PER, HPC>, grid, dim3(kAttnThreads), smem, s, a); \
-    if (e_ != cudaSuccess) return e_;          \
-    return cudaGetLastError();                                                  \
-  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.cluster * (a.heads / a.chpc));
+  cfg.blockDim = dim3(kCThreads);
+  cfg.dynamicSmemBytes = attention_cluster_smem(a);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+#define IRIS_CLUSTER(PER, HPC) \
+  if (per == PER && a.chpc == HPC) return cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel<PER, HPC>, a);
   IRIS_CLUSTER(4, 1) IRIS_CLUSTER(4, 2) IRIS_CLUSTER(4, 4)
   IRIS_CLUSTER(8, 1) IRIS_CLUSTER(8, 2) IRIS_CLUSTER(8, 4)
   IRIS_CLUSTER(16, 1) IRIS_CLUSTER(16, 2) IRIS_CLUSTER(16, 4)
@@ -494,12 +640,51 @@ cudaError_t launch_attention_cluster(const AttnArgs& a, cudaStream_t s) {
   return cudaErrorInvalidValue;
 }
 
+template <uint32_t PER, uint32_t HPC>
+cudaError_t prepare_cluster_one() {
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_cluster_kernel<PER, HPC>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kClusterSmemMax);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_decode_cluster_kernel<PER, HPC>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                             1);
+  return e;
+}
+
+// Clusters of c blocks of the (d / 8, hpc) instantiation with `smem` bytes
+// of shared memory that the device runs at once (0 when it runs none).
+int cluster_fits(uint32_t d, uint32_t hpc, uint32_t c, size_t smem) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(c * 64);
+  cfg.blockDim = dim3(kCThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = c;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  const uint32_t per = d / 8;
+#define IRIS_FITS(PER, HPC) \
+  if (per == PER && hpc == HPC) e = cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel<PER, HPC>, &cfg);
+  IRIS_FITS(4, 1) IRIS_FITS(4, 2) IRIS_FITS(4, 4)
+  IRIS_FITS(8, 1) IRIS_FITS(8, 2) IRIS_FITS(8, 4)
+  IRIS_FITS(16, 1) IRIS_FITS(16, 2) IRIS_FITS(16, 4)
+  IRIS_FITS(32, 1) IRIS_FITS(32, 2)
+#undef IRIS_FITS
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // a refused query leaves no error behind
+    return 0;
+  }
+  return n;
+}
+
 cudaError_t prepare_attention_cluster_kernels() {
   cudaError_t e = cudaSuccess;
-#define IRIS_CLUSTER_ATTR(PER, HPC)                                                                          \
-  if (e == cudaSuccess)                                                                                      \
-    e = cudaFuncSetAttribute(attn_cluster_kernel<PER, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
-                             (int)((kClusterWarps + 1) * HPC * PER * 8 * sizeof(int64_t)));
+#define IRIS_CLUSTER_ATTR(PER, HPC) \
+  if (e == cudaSuccess) e = prepare_cluster_one<PER, HPC>();
   IRIS_CLUSTER_ATTR(4, 1) IRIS_CLUSTER_ATTR(4, 2) IRIS_CLUSTER_ATTR(4, 4)
   IRIS_CLUSTER_ATTR(8, 1) IRIS_CLUSTER_ATTR(8, 2) IRIS_CLUSTER_ATTR(8, 4)
   IRIS_CLUSTER_ATTR(16, 1) IRIS_CLUSTER_ATTR(16, 2) IRIS_CLUSTER_ATTR(16, 4)

@@ -33,17 +33,29 @@ struct AttnArgs {
   unsigned int* counters;          // [heads], zero between launches
   uint32_t cap, nchunks;           // positions held; chunks of 64 positions
   uint32_t hpc;                    // query heads a block (attention_hpc)
-  int cluster;                     // decode: one cluster launch (else three launches)
+  // one-launch decode (attention_cluster_plan): blocks a cluster (0 = the
+  // three-launch path), query heads a block, positions a block at most
+  // (even), tile buffers a block
+  uint32_t cluster, chpc, span, ring;
 };
 
 // Query heads a decode-attention block handles, and the chunk count for a
 // cache of `cap` positions (sizes of the scratch arrays above).
 uint32_t attention_hpc(uint32_t heads, uint32_t kv_heads);
 uint32_t attention_chunks(uint32_t cap);
-// Query heads a block of the one-launch (cluster) decode attention.
-uint32_t attention_cluster_hpc(uint32_t heads, uint32_t kv_heads, uint32_t d);
+// The one-launch (thread-block cluster) decode attention for a cache of `cap`
+// positions: query heads a block, blocks a cluster (0 when the shape needs
+// the three-launch path), positions a block at most and tile buffers a block.
+void attention_cluster_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t* hpc,
+                            uint32_t* cluster, uint32_t* span, uint32_t* ring);
 
-// Decode (one query): three launches split over kv groups x position chunks.
+// Checks an explicit one-launch shape (blocks a cluster, query heads a block,
+// tile buffers a block) for the model and capacity; sets *span.
+bool attention_cluster_shape_ok(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t cluster,
+                                uint32_t hpc, uint32_t ring, uint32_t* span);
+
+// Decode (one query): one cluster launch when a.cluster is set, else three
+// launches split over kv groups x position chunks.
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s);
 // Many queries at positions pos0.. (prefill, chain ranges): one block a
 // (query, head). max_visible bounds the shared memory.

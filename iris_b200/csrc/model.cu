@@ -138,6 +138,11 @@ struct IrisSession {
   int64_t* acc = nullptr;
   unsigned int* counters = nullptr;
   uint32_t nchunks = 0, hpc = 1;
+  uint32_t cluster = 0, chpc = 1, span = 0, ring = 0;  // one-launch decode attention
+  // decode GEMV split scratch (zero between launches)
+  unsigned long long* split_acc = nullptr;
+  unsigned int* split_count = nullptr;
+  uint32_t split_groups = 0;
   cudaStream_t stream = nullptr;
   cudaGraphExec_t graph = nullptr;
 };
@@ -152,7 +157,7 @@ void free_session(IrisSession* s) {
   void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
-                  s->acc, s->counters};
+                  s->acc, s->counters, s->split_acc, s->split_count};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -190,6 +195,7 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   }
   s->nchunks = attention_chunks(cap);
   s->hpc = attention_hpc(m->heads, m->kvh);
+  attention_cluster_plan(m->heads, m->kvh, m->d, cap, &s->chpc, &s->cluster, &s->span, &s->ring);
   if (e == cudaSuccess) e = dalloc(&s->scores, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->terms, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->chunk_best, (size_t)m->heads * s->nchunks);
@@ -200,6 +206,12 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   if (e == cudaSuccess) e = cudaMemset(s->acc, 0, (size_t)m->heads * m->d * sizeof(int64_t));
   if (e == cudaSuccess) e = dalloc(&s->counters, m->heads);
   if (e == cudaSuccess) e = cudaMemset(s->counters, 0, m->heads * sizeof(unsigned int));
+  s->split_groups = (std::max({m->qd + 2 * m->kvd, m->H, 2 * m->F, m->V}) + kQ8TileRows - 1) / kQ8TileRows;
+  if (e == cudaSuccess) e = dalloc(&s->split_acc, (size_t)s->split_groups * kQ8TileRows * 2);
+  if (e == cudaSuccess) e = dalloc(&s->split_count, s->split_groups);
+  if (e == cudaSuccess)
+    e = cudaMemset(s->split_acc, 0, (size_t)s->split_groups * kQ8TileRows * 2 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(s->split_count, 0, s->split_groups * sizeof(unsigned int));
   if (e == cudaSuccess) e = cudaMemset(s->best, 0, R * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(s->d_pos, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(s->d_step, 0, 4);
@@ -209,6 +221,15 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   }
   *out = s;
   return 0;
+}
+
+// Product arguments with the session's GEMV split scratch.
+ProductArgs session_product_args(IrisSession* s, const Q8GpuMatrix* w, uint32_t tokens) {
+  ProductArgs a = product_args(w, tokens);
+  a.split_acc = s->split_acc;
+  a.split_count = s->split_count;
+  a.split_groups = s->split_groups;
+  return a;
 }
 
 AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t pos0) {
@@ -239,7 +260,10 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   a.cap = s->cap;
   a.nchunks = s->nchunks;
   a.hpc = s->hpc;
-  a.cluster = 0;
+  a.cluster = s->cluster;
+  a.chpc = s->chpc;
+  a.span = s->span;
+  a.ring = s->ring;
   return a;
 }
 
@@ -254,7 +278,7 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   cudaError_t e = cudaSuccess;
   bool one = tokens == 1;
   // n = rms_norm(x); q, k, v = W n; rope(q), rope(k); k, v to the cache
-  ProductArgs a = product_args(L.qkv, tokens);
+  ProductArgs a = session_product_args(s, L.qkv, tokens);
   a.out = s->q;
   a.out_stride = m->qd;
   a.freqs = m->freqs;
@@ -281,14 +305,14 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, pos0 + tokens, st);
   if (e != cudaSuccess) return e;
   // x = x + W_o ctx
-  ProductArgs o = product_args(L.o, tokens);
+  ProductArgs o = session_product_args(s, L.o, tokens);
   o.planes = s->planes;
   o.out = s->x;
   o.resid = s->x;
   e = launch_product(o, IN_PLANES, EPI_RESID, st);
   if (e != cudaSuccess) return e;
   // g = silu(W_gate m) * (W_up m), m = rms_norm(x)
-  ProductArgs g = product_args(L.gu, tokens);
+  ProductArgs g = session_product_args(s, L.gu, tokens);
   g.out_planes = s->planes2;
   if (one) {
     g.x = s->x;
@@ -302,7 +326,7 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   }
   if (e != cudaSuccess) return e;
   // x = x + W_down g
-  ProductArgs dn = product_args(L.down, tokens);
+  ProductArgs dn = session_product_args(s, L.down, tokens);
   dn.planes = s->planes2;
   dn.out = s->x;
   dn.resid = s->x;
@@ -317,7 +341,7 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   cudaStream_t st = s->stream;
   cudaError_t e;
   bool one = tokens == 1;
-  ProductArgs a = product_args(L.qkv, tokens);
+  ProductArgs a = session_product_args(s, L.qkv, tokens);
   a.out = s->qkv;
   if (one) {
     a.x = s->x;
@@ -352,19 +376,19 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   uint32_t max_vis = L.window ? std::min(L.window, pos0 + tokens) : pos0 + tokens;
   e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, max_vis, st);
   if (e != cudaSuccess) return e;
-  ProductArgs o = product_args(L.o, tokens);
+  ProductArgs o = session_product_args(s, L.o, tokens);
   o.planes = s->planes;
   o.out = s->tmp;
   e = launch_product(o, IN_PLANES, EPI_STORE, st);
   if (e == cudaSuccess)
     e = launch_gemma_post_attn(s->tmp, s->x, L.norm_post_attn, L.norm_ffn, m->eps, tokens, m->H, s->planes, st);
   if (e != cudaSuccess) return e;
-  ProductArgs g = product_args(L.gu, tokens);
+  ProductArgs g = session_product_args(s, L.gu, tokens);
   g.planes = s->planes;
   g.out_planes = s->planes2;
   e = launch_product(g, IN_PLANES, EPI_GELU_MUL, st);
   if (e != cudaSuccess) return e;
-  ProductArgs dn = product_args(L.down, tokens);
+  ProductArgs dn = session_product_args(s, L.down, tokens);
   dn.planes = s->planes2;
   dn.out = s->tmp;
   e = launch_product(dn, IN_PLANES, EPI_STORE, st);
@@ -401,7 +425,7 @@ cudaError_t run_pass(IrisSession* s, uint32_t tokens, const uint32_t* ids_dev, c
   }
   if (!head) return cudaSuccess;
   // head: rms_norm(final) -> dot_row over the vocabulary -> softcap -> first max
-  ProductArgs h = product_args(m->head, 1);
+  ProductArgs h = session_product_args(s, m->head, 1);
   h.x = s->x + (size_t)(tokens - 1) * m->H;
   h.norm_w = m->final_norm;
   h.eps = m->eps;
@@ -960,12 +984,41 @@ int iris_session_attention(IrisSession* s, uint32_t layer) {
   return (int)launch_attention_decode(a, s->stream);
 }
 
+static int rebuild_graph_later(IrisSession* s) {
+  if (!s->graph) return 0;
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return (int)e;
+  cudaGraphExecDestroy(s->graph);
+  s->graph = nullptr;
+  return 0;
+}
+
+int iris_session_set_attention(IrisSession* s, int mode) {
+  if (!s || (mode != IRIS_ATTN_AUTO && mode != IRIS_ATTN_SPLIT)) return IRIS_EINVAL;
+  IrisModel* m = s->m;
+  if (mode == IRIS_ATTN_SPLIT) s->cluster = 0;
+  else attention_cluster_plan(m->heads, m->kvh, m->d, s->cap, &s->chpc, &s->cluster, &s->span, &s->ring);
+  return rebuild_graph_later(s);
+}
+
+int iris_session_set_attention_shape(IrisSession* s, uint32_t cluster, uint32_t hpc, uint32_t ring) {
+  if (!s) return IRIS_EINVAL;
+  IrisModel* m = s->m;
+  uint32_t span = 0;
+  if (!attention_cluster_shape_ok(m->heads, m->kvh, m->d, s->cap, cluster, hpc, ring, &span)) return IRIS_EINVAL;
+  s->cluster = cluster;
+  s->chpc = hpc;
+  s->ring = ring;
+  s->span = span;
+  return rebuild_graph_later(s);
+}
+
 int iris_session_product(IrisSession* s, uint32_t layer, int which) {
   if (!s || layer >= s->m->L || which < 0 || which > 4) return IRIS_EINVAL;
   IrisModel* m = s->m;
   const LayerDev& L = m->layers[layer];
   const Q8GpuMatrix* w = which == 0 ? L.qkv : which == 1 ? L.o : which == 2 ? L.gu : which == 3 ? L.down : m->head;
-  ProductArgs a = product_args(w, 1);
+  ProductArgs a = session_product_args(s, w, 1);
   if (which == 1 || which == 3) {  // inputs from byte planes, as in the pass
     a.planes = which == 1 ? s->planes : s->planes2;
     a.out = s->tmp;
@@ -998,6 +1051,33 @@ int iris_session_get_kv(const IrisSession* s, uint32_t layer, uint32_t first, ui
 }
 
 void iris_session_free(IrisSession* s) { free_session(s); }
+
+int iris_capture_begin(void* stream) {
+  if (!stream) return IRIS_EINVAL;  // the legacy default stream cannot be captured
+  return (int)cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal);
+}
+
+int iris_capture_end(void* stream, void** graph_exec) {
+  if (!stream || !graph_exec) return IRIS_EINVAL;
+  *graph_exec = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture((cudaStream_t)stream, &g);
+  if (e != cudaSuccess) return (int)e;
+  cudaGraphExec_t x = nullptr;
+  e = cudaGraphInstantiate(&x, g, 0);
+  cudaGraphDestroy(g);
+  if (e == cudaSuccess) *graph_exec = (void*)x;
+  return (int)e;
+}
+
+int iris_graph_launch(void* graph_exec, void* stream) {
+  if (!graph_exec) return IRIS_EINVAL;
+  return (int)cudaGraphLaunch((cudaGraphExec_t)graph_exec, (cudaStream_t)stream);
+}
+
+void iris_graph_free(void* graph_exec) {
+  if (graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
+}
 
 int iris_mistral_layer_range(IrisModel* m, uint32_t layer, const int32_t* rows_in, uint32_t n, uint32_t start,
                              const int32_t* prior_k, const int32_t* prior_v, int32_t* rows_out, int32_t* own_k,

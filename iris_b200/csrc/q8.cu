@@ -12,8 +12,9 @@
 // Kernels:
 //  - q8_gemv_tma_kernel: one token (the decode step). A persistent block an SM
 //    streams whole weight tiles (q8.cuh) from HBM through a ring of
-//    shared-memory stages with bulk copies (TMA) while eight consumer warps
-//    run the products against activation planes held in shared memory.
+//    shared-memory stages with bulk copies (TMA) while sixteen consumer warps
+//    run the products against activation planes held in shared memory and an
+//    epilogue warp rounds and finishes the rows.
 //  - q8_gemm_kernel: many tokens (prefill, the chain's ranges), a 64-row x
 //    32-token tile per block staged through shared memory.
 // Both end in a fused epilogue (residual add, RoPE and K/V store, SiLU/GELU
@@ -256,8 +257,11 @@ __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.z * v.z));
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.w * v.w));
     }
-    uint64_t total = block_sum_sat(ss, red);
-    if (threadIdx.x == 0) *s_scale = rms_scale_from_sumsq(total, K, eps);
+    uint64_t total = block_sum_sat(ss, red);  // in every lane of warp 0
+    if (threadIdx.x < 32) {  // rms_scale_from_sumsq with the warp-parallel inverse square root
+      const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), eps));
+      if (threadIdx.x == 0) *s_scale = sc;
+    }
     __syncthreads();
     scale = *s_scale;
   }
@@ -347,41 +351,56 @@ __device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uin
 // Decode GEMV, bulk-copy pipeline: one persistent block an SM
 // ---------------------------------------------------------------------------
 //
-// A block owns a contiguous range of tile groups (16 rows each). A producer
-// warp streams every tile of its range - 16 rows x kc values and their scale
-// bits, two contiguous runs - from HBM into a ring of shared-memory stages
-// with cp.async.bulk (TMA, evict-first in L2), completing on the stage's
-// "full" mbarrier. Sixteen consumer warps - two rows and half of the slice's
-// blocks each - run the dp4a byte-plane products against the activation
-// planes held in shared memory (three planes when every activation fits in
-// +-2^23, else four) and release the stage on its "empty" mbarrier; at the
-// end of a tile group the two halves of each row meet in shared memory. The activation prologue
-// (planes, or the fused RMSNorm) runs once per block while the first stages
-// are already in flight. Every wait is bounded (about one second): a stalled
-// pipeline records a fault and the kernel returns instead of hanging.
+// The matrix's tiles (16 rows x kc values, tile (g, s) at index g * S + s)
+// are the work items. A block owns a contiguous range of items; three warp
+// roles run concurrently:
+//   - a producer warp streams every tile of the range - two contiguous runs,
+//     values and scale bits - from HBM into a ring of shared-memory stages
+//     with cp.async.bulk (TMA, evict-first in L2), completing on the stage's
+//     "full" mbarrier;
+//   - sixteen consumer warps - two rows and half of the slice's blocks each -
+//     run the dp4a byte-plane products against the activation planes held in
+//     shared memory (three planes when every activation fits in +-2^23, else
+//     four), release the stage on its "empty" mbarrier and, at the end of a
+//     tile group, leave their exact 128-bit row sums in a slot of a small
+//     ring for
+//   - an epilogue warp, which adds the two halves of each row, rounds once
+//     (q8.rs:69-71) and applies the epilogue, off the consumers' path.
+// With split scratch (stream-K), ranges are even item counts and may start
+// or end inside a tile group: the blocks sharing a group add their partial
+// 128-bit sums into the scratch with 64-bit atomics (wrapping 128-bit
+// addition, exact in any order) and the block completing the group's slice
+// count rounds it. Without it, ranges are whole tile groups.
+// The activation prologue (planes, or the fused RMSNorm) runs once per block
+// while the first stages are already in flight. Every wait is bounded (about
+// one second): a stalled pipeline records a fault and the kernel returns
+// instead of hanging.
 
 __device__ unsigned int g_fault;
 
 constexpr int kTmaConsumerWarps = 16;
-constexpr int kTmaThreads = (kTmaConsumerWarps + 1) * 32;
+constexpr int kTmaEpilogueWarp = kTmaConsumerWarps + 1;
+constexpr int kTmaThreads = (kTmaConsumerWarps + 2) * 32;
 constexpr int kTmaRowsPerWarp = 2;
 constexpr uint32_t kTmaMaxStages = 8;
+constexpr uint32_t kTmaSlots = 4;  // tile groups between the consumers and the epilogue warp
 constexpr uint32_t kTmaSmemBudget = 220 * 1024;
-constexpr uint32_t kConsumerThreads = kTmaConsumerWarps * 32;
 
 struct GemvPlan {
   uint32_t stages;
   uint32_t stage_bytes;      // tile values (16 kc) + tile scales (kc), rounded to 128
   uint32_t planes_bytes;     // 4 K, rounded to 128
-  uint32_t groups_per_block;
+  uint32_t items;            // tiles of the matrix: groups * nslices
+  uint32_t groups_per_block; // whole-group ranges (split == 0)
+  uint32_t split;            // even item ranges through the split scratch
   uint32_t smem;
   uint32_t grid;
 };
 
 __host__ __device__ inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
 
-bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, GemvPlan* p) {
-  if (K % 32 || rows == 0) return false;
+bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, bool split, GemvPlan* p) {
+  if (K % 32 || rows == 0 || kc == 0) return false;
   p->planes_bytes = round_up(4 * K, 128);
   p->stage_bytes = round_up(kQ8TileRows * kc + kc, 128);
   if (p->planes_bytes + 2 * p->stage_bytes > kTmaSmemBudget) return false;
@@ -389,49 +408,111 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, GemvPlan* p) {
   p->stages = fit < kTmaMaxStages ? fit : kTmaMaxStages;
   p->smem = p->planes_bytes + p->stages * p->stage_bytes;
   const uint32_t groups = (rows + kQ8TileRows - 1) / kQ8TileRows;
-  const uint32_t grid = (uint32_t)sms < groups ? (uint32_t)sms : groups;
-  p->groups_per_block = (groups + grid - 1) / grid;
-  p->grid = (groups + p->groups_per_block - 1) / p->groups_per_block;
+  p->items = groups * (K / kc);
+  p->split = split ? 1 : 0;
+  if (split) {
+    p->grid = (uint32_t)sms < p->items ? (uint32_t)sms : p->items;
+    p->groups_per_block = 0;
+  } else {
+    const uint32_t grid = (uint32_t)sms < groups ? (uint32_t)sms : groups;
+    p->groups_per_block = (groups + grid - 1) / grid;
+    p->grid = (groups + p->groups_per_block - 1) / p->groups_per_block;
+  }
   return true;
 }
 
-// One warp's share of a tile: two rows, blocks [b0, b1) of the slice. Each
-// lane takes whole 32-value blocks (two 16-byte chunks, one scale); lanes
-// 4-7 of every quarter-warp load the two chunks in the other order, so that
-// each 8-lane phase of a 128-bit shared load touches 8 different 16-byte bank
-// groups (the block sum does not depend on the order).
-template <bool kThree>
-__device__ __forceinline__ void gemv_tile_rows(const uint8_t* __restrict__ W, const uint16_t* __restrict__ Sc,
-                                               const uint4* __restrict__ P0, const uint4* __restrict__ P1,
-                                               const uint4* __restrict__ P2, const uint4* __restrict__ P3,
-                                               uint32_t kc, uint32_t cbase, uint32_t b0, uint32_t b1,
-                                               uint32_t lane, Acc128* acc) {
+// One warp's share of a tile: two rows, one 32-value block b of the slice a
+// lane (a half slice is at most 32 blocks). The lane first copies its weights
+// and scale bits out of the stage into registers, so that the warp can release
+// the stage before the products run and the producer refills it at once.
+// Lanes 4-7 of every quarter-warp take the two 16-byte chunks in the other
+// order, so that each 8-lane phase of a 128-bit shared load touches 8
+// different 16-byte bank groups (the block sum does not depend on the order).
+struct RowBlocks {
+  uint4 wa[kTmaRowsPerWarp], wb[kTmaRowsPerWarp];
+  uint16_t sc[kTmaRowsPerWarp];
+};
+
+__device__ __forceinline__ void gemv_take_rows(const uint8_t* __restrict__ W, const uint16_t* __restrict__ Sc,
+                                               uint32_t kc, uint32_t b, uint32_t lane, RowBlocks& rb) {
   const uint32_t blocks = kc / 32, swap = (lane >> 2) & 1;
-#pragma unroll 2
-  for (uint32_t b = b0 + lane; b < b1; b += 32) {
-    const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
-    const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
-    const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1];
-    uint4 pa3, pb3;
-    if (!kThree) {
-      pa3 = P3[cbase + c0];
-      pb3 = P3[cbase + c1];
-    }
+  const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
 #pragma unroll
-    for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-      const uint8_t* Wr = W + r * kc;
-      const uint4 wa = *(const uint4*)(Wr + c0 * 16), wb = *(const uint4*)(Wr + c1 * 16);
-      int32_t m, e;
-      q8_scale_parts(Sc[r * blocks + b], &m, &e);  // finite: checked at upload (padding rows: 0)
-      const int64_t bs = kThree ? q8_partial16_three(wa, pa0, pa1, pa2) + q8_partial16_three(wb, pb0, pb1, pb2)
-                                : q8_partial16(wa, pa0, pa1, pa2, pa3) + q8_partial16(wb, pb0, pb1, pb2, pb3);
-      acc128_add_shifted(acc[r], bs * m, e);
-    }
+  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+    rb.wa[r] = *(const uint4*)(W + r * kc + c0 * 16);
+    rb.wb[r] = *(const uint4*)(W + r * kc + c1 * 16);
+    rb.sc[r] = Sc[r * blocks + b];
   }
 }
 
-__device__ __forceinline__ void consumer_barrier() {
-  asm volatile("bar.sync 1, %0;" ::"r"(kConsumerThreads) : "memory");
+template <bool kThree>
+__device__ __forceinline__ void gemv_rows_product(const RowBlocks& rb, const uint4* __restrict__ P0,
+                                                  const uint4* __restrict__ P1, const uint4* __restrict__ P2,
+                                                  const uint4* __restrict__ P3, uint32_t cbase, uint32_t b,
+                                                  uint32_t lane, Acc128* acc) {
+  const uint32_t swap = (lane >> 2) & 1;
+  const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
+  const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
+  const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1];
+  uint4 pa3, pb3;
+  if (!kThree) {
+    pa3 = P3[cbase + c0];
+    pb3 = P3[cbase + c1];
+  }
+#pragma unroll
+  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+    int32_t m, e;
+    q8_scale_parts(rb.sc[r], &m, &e);  // finite: checked at upload (padding rows: 0)
+    const int64_t bs = kThree ? q8_partial16_three(rb.wa[r], pa0, pa1, pa2) + q8_partial16_three(rb.wb[r], pb0, pb1, pb2)
+                              : q8_partial16(rb.wa[r], pa0, pa1, pa2, pa3) + q8_partial16(rb.wb[r], pb0, pb1, pb2, pb3);
+    acc128_add_shifted(acc[r], bs * m, e);
+  }
+}
+
+// Item range [*ib, *ie) of block b.
+__device__ __forceinline__ void gemv_range(const GemvPlan& p, uint32_t S, uint32_t groups, uint32_t b,
+                                           uint32_t* ib, uint32_t* ie) {
+  if (p.split) {
+    *ib = (uint32_t)((uint64_t)b * p.items / p.grid);
+    *ie = (uint32_t)((uint64_t)(b + 1) * p.items / p.grid);
+  } else {
+    const uint32_t g0 = b * p.groups_per_block, g1 = min(groups, g0 + p.groups_per_block);
+    *ib = g0 * S;
+    *ie = g0 < g1 ? g1 * S : g0 * S;
+  }
+}
+
+// Exact 128-bit addition into the split scratch (two 64-bit words a row).
+__device__ __forceinline__ void atomic_add_acc128(unsigned long long* dst, Acc128 v) {
+  const unsigned long long old = atomicAdd(dst, (unsigned long long)v.lo);
+  const unsigned long long carry = old + v.lo < old ? 1ull : 0ull;
+  atomicAdd(dst + 1, (unsigned long long)v.hi + carry);
+}
+
+// The epilogue of one finished tile group: lane l < 16 holds the rounded value
+// of row g * 16 + l.
+template <int EPI>
+__device__ __forceinline__ void gemv_group_epilogue(const ProductArgs& a, uint32_t g, int32_t v, uint32_t lane,
+                                                    unsigned long long* best) {
+  const uint32_t row0 = g * kQ8TileRows;
+  if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+    // pairs (2j, 2j + 1): lane j < 8 takes pair j
+    const int32_t v0 = __shfl_sync(0xffffffffu, v, (2 * lane) & 31);
+    const int32_t v1 = __shfl_sync(0xffffffffu, v, (2 * lane + 1) & 31);
+    const uint32_t row = row0 + 2 * lane;
+    if (lane < kQ8TileRows / 2 && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
+  } else if (EPI == EPI_LOGITS) {
+    const uint32_t row = row0 + lane;
+    if (lane < kQ8TileRows && row < a.rows) {
+      const int32_t c = a.softcap > 0 ? softcap_act(v, a.softcap) : v;
+      if (a.out) a.out[row] = c;
+      const unsigned long long key = best_key(c, row);
+      *best = key > *best ? key : *best;
+    }
+  } else {
+    const uint32_t row = row0 + lane;
+    if (lane < kQ8TileRows && row < a.rows) epi_single<EPI>(a, 0, row, v);
+  }
 }
 
 template <int IN, int EPI>
@@ -439,47 +520,50 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kTmaMaxStages];
   __shared__ __align__(8) uint64_t empty[kTmaMaxStages];
+  __shared__ __align__(8) uint64_t slot_full[kTmaSlots];
+  __shared__ __align__(8) uint64_t slot_empty[kTmaSlots];
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
-  __shared__ Acc128 half_sums[2][kQ8TileRows];  // second-half sums, by group parity
+  __shared__ Acc128 slot_sums[kTmaSlots][2][kQ8TileRows];  // [slot][half][row of the tile]
   const uint32_t K = a.cols, kc = a.kc, S = a.nslices;
   uint8_t* planes = smem;
   uint8_t* stage0 = smem + p.planes_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool producer = warp == kTmaConsumerWarps;
   const uint32_t groups = (a.rows + kQ8TileRows - 1) / kQ8TileRows;
-  const uint32_t g_begin = blockIdx.x * p.groups_per_block;
-  const uint32_t g_end = min(groups, g_begin + p.groups_per_block);
-  const uint32_t nitems = g_begin < g_end ? (g_end - g_begin) * S : 0;
+  uint32_t ib, ie;
+  gemv_range(p, S, groups, blockIdx.x, &ib, &ie);
+  const uint32_t nitems = ie - ib;
 
   if (threadIdx.x == 0) {
     for (uint32_t st = 0; st < p.stages; ++st) {
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], kTmaConsumerWarps);
     }
+    for (uint32_t sl = 0; sl < kTmaSlots; ++sl) {
+      mbar_init(&slot_full[sl], kTmaConsumerWarps);
+      mbar_init(&slot_empty[sl], 1);
+    }
     mbar_fence_init();
   }
   __syncthreads();
 
   const uint64_t policy = l2_evict_first_policy();
-  // Item i is tile (g_begin + i / S, i % S): the tiles of a range are
-  // consecutive in memory, so item i is tile index g_begin * S + i.
-  auto issue = [&](uint32_t item) {
-    const uint32_t st = item % p.stages;
-    const size_t tile = (size_t)g_begin * S + item;
+  // Item k of the range is tile ib + k: the tiles of a range are consecutive.
+  auto issue = [&](uint32_t item, uint32_t st) {
+    const size_t tile = (size_t)ib + item;
     uint8_t* dst = stage0 + st * p.stage_bytes;
     mbar_arrive_expect_tx(&full[st], kQ8TileRows * kc + kc);
     bulk_load(dst, a.q + tile * kQ8TileRows * kc, kQ8TileRows * kc, &full[st], policy);
     bulk_load(dst + kQ8TileRows * kc, (const uint8_t*)a.s + tile * kc, kc, &full[st], policy);
   };
 
-  // The first stages need no release: issue them before the prologue.
   // Weights never change: the first stages stream while the previous kernel
   // of the stream finishes; the activations are read only after pdl_wait().
   pdl_trigger();
   const uint32_t first = nitems < p.stages ? nitems : p.stages;
   if (producer && lane == 0)
-    for (uint32_t item = 0; item < first; ++item) issue(item);
+    for (uint32_t item = 0; item < first; ++item) issue(item, item);
   pdl_wait();
 
   // Activation planes; `wide` when some value needs the fourth plane.
@@ -503,16 +587,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
 
   if (producer) {
     if (lane == 0) {
-      uint32_t issued = first;
+      uint32_t issued = first, st = 0, phase = 0;  // stage of item `first`, parity of its release
       bool stalled = false;
       for (uint32_t item = first; item < nitems; ++item) {
-        const uint32_t st = item % p.stages, use = item / p.stages;
-        if (!mbar_wait_bounded(&empty[st], (use - 1) & 1, &g_fault)) {
+        if (!mbar_wait_bounded(&empty[st], phase, &g_fault)) {
           stalled = true;
           break;
         }
-        issue(item);
+        issue(item, st);
         issued = item + 1;
+        if (++st == p.stages) {
+          st = 0;
+          phase ^= 1;
+        }
       }
       if (stalled)  // let the copies already issued land before the block exits
         for (uint32_t item = issued > p.stages ? issued - p.stages : 0; item < issued; ++item)
@@ -521,64 +608,99 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
     return;
   }
 
+  const uint32_t gfirst = ib / S, ngroups = nitems ? (ie - 1) / S - gfirst + 1 : 0;
+  if (warp == kTmaEpilogueWarp) {
+    unsigned long long best = 0;
+    for (uint32_t j = 0; j < ngroups; ++j) {
+      const uint32_t sl = j % kTmaSlots, g = gfirst + j;
+      if (!mbar_wait_bounded(&slot_full[sl], (j / kTmaSlots) & 1, &g_fault)) return;
+      Acc128 v = Acc128{0, 0};
+      if (lane < kQ8TileRows) {
+        v = slot_sums[sl][0][lane];
+        if (kTmaConsumerWarps == 16) acc128_add(v, slot_sums[sl][1][lane].lo, slot_sums[sl][1][lane].hi);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&slot_empty[sl]);
+      const uint32_t lo = max(ib, g * S), hi = min(ie, (g + 1) * S);
+      if (hi - lo < S) {  // a share of a group split between blocks
+        unsigned long long* acc = a.split_acc + (size_t)g * kQ8TileRows * 2;
+        if (lane < kQ8TileRows) atomic_add_acc128(acc + 2 * lane, v);
+        __threadfence();
+        __syncwarp();
+        uint32_t done = 0;
+        if (lane == 0) done = atomicAdd(a.split_count + g, hi - lo) + (hi - lo) == S;
+        if (!__shfl_sync(0xffffffffu, done, 0)) continue;
+        __threadfence();
+        if (lane < kQ8TileRows) {
+          v.lo = (uint64_t)__ldcg(acc + 2 * lane);
+          v.hi = (int64_t)__ldcg(acc + 2 * lane + 1);
+          acc[2 * lane] = 0;
+          acc[2 * lane + 1] = 0;
+        }
+        if (lane == 0) a.split_count[g] = 0;
+      }
+      gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
+    }
+    if (EPI == EPI_LOGITS) {
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+        best = o > best ? o : best;
+      }
+      if (lane == 0 && best) atomicMax(a.best, best);
+    }
+    return;
+  }
+
   const uint4* P0 = (const uint4*)planes;
   const uint4* P1 = P0 + K / 16;
   const uint4* P2 = P1 + K / 16;
   const uint4* P3 = P2 + K / 16;
-  // Warp w: rows 2 (w % 8) and 2 (w % 8) + 1 of each tile, blocks of the
-  // slice's first half (w < 8) or second half (w >= 8).
-  const uint32_t pair = warp % (kTmaConsumerWarps / 2), half = warp / (kTmaConsumerWarps / 2);
-  const uint32_t lr0 = kTmaRowsPerWarp * pair, blocks = kc / 32, mid = (blocks + 1) / 2;
+  // Warp w: rows 2 (w % 8) and 2 (w % 8) + 1 of each tile; with sixteen
+  // consumer warps, blocks of the slice's first half (w < 8) or second half
+  // (w >= 8), with eight the whole slice.
+  constexpr uint32_t kHalves = kTmaConsumerWarps / 8;
+  static_assert(kHalves == 2, "a lane takes one block a row: 2048-value slices need two halves");
+  const uint32_t pair = warp % 8, half = warp / 8;
+  const uint32_t lr0 = kTmaRowsPerWarp * pair, blocks = kc / 32, mid = kHalves == 2 ? (blocks + 1) / 2 : blocks;
   const uint32_t b0 = half ? mid : 0, b1 = half ? blocks : mid;
   Acc128 acc[kTmaRowsPerWarp];
 #pragma unroll
   for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
-  uint32_t parity = 0;
+  uint32_t j = 0;        // tile groups finished
   bool stalled = false;  // after a given-up wait: keep pace with the barriers, skip the waits
+  // stage, its fill parity and the slice of the current item, kept without divisions
+  uint32_t st = 0, phase = 0, sl = ib % S;
   for (uint32_t item = 0; item < nitems; ++item) {
-    const uint32_t st = item % p.stages, use = item / p.stages, sl = item % S;
-    if (!stalled && !mbar_wait_bounded(&full[st], use & 1, &g_fault)) stalled = true;
+    if (!stalled && !mbar_wait_bounded(&full[st], phase, &g_fault)) stalled = true;
     const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * kc;
     const uint16_t* Sc = (const uint16_t*)(stage0 + st * p.stage_bytes + kQ8TileRows * kc) + lr0 * blocks;
-    const uint32_t cbase = sl * (kc / 16);
-    if (wide) gemv_tile_rows<false>(W, Sc, P0, P1, P2, P3, kc, cbase, b0, b1, lane, acc);
-    else gemv_tile_rows<true>(W, Sc, P0, P1, P2, P3, kc, cbase, b0, b1, lane, acc);
+    const uint32_t cbase = sl * (kc / 16), b = b0 + lane;
+    RowBlocks rb;
+    if (b < b1) gemv_take_rows(W, Sc, kc, b, lane, rb);
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (sl + 1 == S) {
+    if (lane == 0) mbar_arrive(&empty[st]);  // the stage is in registers: refill it
+    if (++st == p.stages) {
+      st = 0;
+      phase ^= 1;
+    }
+    if (b < b1) {
+      if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, acc);
+      else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, acc);
+    }
+    if (++sl == S) sl = 0;
+    if (sl == 0 || item + 1 == nitems) {
 #pragma unroll
       for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
-      if (half && lane == 0) {
-        half_sums[parity][lr0] = acc[0];
-        half_sums[parity][lr0 + 1] = acc[1];
+      const uint32_t slot = j % kTmaSlots;
+      if (j >= kTmaSlots && !stalled && !mbar_wait_bounded(&slot_empty[slot], (j / kTmaSlots - 1) & 1, &g_fault))
+        stalled = true;
+      if (lane == 0) {
+        slot_sums[slot][half][lr0] = acc[0];
+        slot_sums[slot][half][lr0 + 1] = acc[1];
+        mbar_arrive(&slot_full[slot]);
       }
-      consumer_barrier();
-      const uint32_t row = (g_begin + item / S) * kQ8TileRows + lr0;
-      if (!half && lane == 0 && row < a.rows) {
-        acc128_add(acc[0], half_sums[parity][lr0].lo, half_sums[parity][lr0].hi);
-        acc128_add(acc[1], half_sums[parity][lr0 + 1].lo, half_sums[parity][lr0 + 1].hi);
-        const bool two = row + 1 < a.rows;
-        const int32_t v0 = acc128_round_q24(acc[0]);
-        const int32_t v1 = two ? acc128_round_q24(acc[1]) : 0;
-        if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-          if (two) epi_pair<EPI>(a, 0, row, v0, v1);
-        } else if (EPI == EPI_LOGITS) {
-          const int32_t c0v = a.softcap > 0 ? softcap_act(v0, a.softcap) : v0;
-          unsigned long long key = best_key(c0v, row);
-          if (a.out) a.out[row] = c0v;
-          if (two) {
-            const int32_t c1v = a.softcap > 0 ? softcap_act(v1, a.softcap) : v1;
-            if (a.out) a.out[row + 1] = c1v;
-            const unsigned long long k1 = best_key(c1v, row + 1);
-            key = k1 > key ? k1 : key;
-          }
-          atomicMax(a.best, key);
-        } else {
-          epi_single<EPI>(a, 0, row, v0);
-          if (two) epi_single<EPI>(a, 0, row + 1, v1);
-        }
-      }
-      parity ^= 1;
+      ++j;
 #pragma unroll
       for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
     }
@@ -700,7 +822,9 @@ int device_sms() {
 template <int IN, int EPI>
 cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
   GemvPlan p;
-  if (!plan_gemv(a.rows, a.cols, a.kc, device_sms(), &p)) return cudaErrorInvalidValue;
+  const uint32_t groups = (a.rows + kQ8TileRows - 1) / kQ8TileRows;
+  const bool split = a.split_acc && a.split_count && groups <= a.split_groups;
+  if (!plan_gemv(a.rows, a.cols, a.kc, device_sms(), split, &p)) return cudaErrorInvalidValue;
   return launch_k(q8_gemv_tma_kernel<IN, EPI>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, a, p);
 }
 

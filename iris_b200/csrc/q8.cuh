@@ -84,6 +84,11 @@ struct ProductArgs {
   uint32_t pos0;           // position of token 0 when pos_ptr is NULL
   unsigned long long* best;  // first-maximum key per token
   int32_t softcap;
+  // Decode GEMV split scratch (optional): 2 words a row and a slice count a
+  // tile group for split_groups groups, all zero between launches.
+  unsigned long long* split_acc;
+  unsigned int* split_count;
+  uint32_t split_groups;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);

@@ -5,11 +5,15 @@
   python -m iris_b200.microbench attention [--context 2560 --layers 1]
       one single-query attention over a mistral-7b-shaped cache;
   python -m iris_b200.microbench gemm [--rows 6144 --cols 4096 --tokens 256]
-      the many-token product.
+      the many-token product;
+  python -m iris_b200.microbench product [--product 2 --layers 2]
+      one of the decode pass's own products (0 q|k|v, 1 o, 2 gate|up,
+      3 down, 4 head) of a mistral-7b-shaped session, layer after layer.
 
 Each prints one JSON line (average device time a launch, bytes or ops a
-launch, the implied rate). Inputs are seeded synthetic values; timings use
-CUDA events on the stream the kernels run on.
+launch, the implied rate). Inputs are seeded synthetic values; the launches
+are captured into a CUDA graph and timed with CUDA events around one replay
+on the stream they run on.
 """
 from __future__ import annotations
 
@@ -30,6 +34,35 @@ def _events(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
+def device_us(torch, stream, launches, iters):
+    """Average device time of launches(i) over i < iters: the launches are
+    captured into one CUDA graph on `stream` (through the library's own
+    capture entry points) and replayed, so host launch overhead does not
+    enter the figure."""
+    from iris_b200 import _lib
+    L = _lib.lib()
+    sp = C.c_void_p(stream.cuda_stream)
+    _lib.check(L.iris_capture_begin(sp), "iris_capture_begin")
+    try:
+        for i in range(iters):
+            launches(i)
+    finally:
+        g = C.c_void_p()
+        end = L.iris_capture_end(sp, C.byref(g))
+    _lib.check(end, "iris_capture_end")
+    try:
+        _lib.check(L.iris_graph_launch(g, sp), "iris_graph_launch")
+        stream.synchronize()
+        e0, e1 = _events(torch)
+        e0.record(stream)
+        _lib.check(L.iris_graph_launch(g, sp), "iris_graph_launch")
+        e1.record(stream)
+        stream.synchronize()
+    finally:
+        L.iris_graph_free(g)
+    return e0.elapsed_time(e1) * 1e3 / iters
+
+
 def gemv(args):
     import torch
     from iris_b200 import _lib
@@ -43,19 +76,14 @@ def gemv(args):
         mats.append(h)
     x = torch.randint(-(1 << 20), 1 << 20, (1, args.cols), dtype=torch.int32, device="cuda")
     out = torch.empty((1, args.rows), dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
     run = lambda h: _lib.check(L.iris_q8_product_device_path(h, x.data_ptr(), 1, out.data_ptr(), stream.cuda_stream,
                                                              _lib.PATH_GEMV), "gemv")
     for h in mats:
         run(h)
     torch.cuda.synchronize()
-    e0, e1 = _events(torch)
-    e0.record(stream)
-    for i in range(args.iters):
-        run(mats[i % len(mats)])
-    e1.record(stream)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / args.iters
+    us = device_us(torch, stream, lambda i: run(mats[i % len(mats)]), args.iters)
     nbytes = args.rows * args.cols * 34 // 32 + 4 * args.cols + 4 * args.rows
     for h in mats:
         L.q8gpu_free(h)
@@ -73,20 +101,19 @@ def attention(args):
     sess = model.session(args.context + 8)
     prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab, size=args.context).tolist()
     sess.prefill(prompt)
+    sess.set_attention(args.attn)
+    if args.shape:
+        c, h, r = (int(v) for v in args.shape.split(","))
+        sess.set_attention_shape(c, h, r)
     stream = torch.cuda.ExternalStream(sess.stream_ptr)
     for _ in range(3):
         sess.attention(0)
     sess.synchronize()
-    e0, e1 = _events(torch)
-    e0.record(stream)
-    for i in range(args.iters):
-        sess.attention(i % args.layers)
-    e1.record(stream)
-    sess.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / args.iters
+    us = device_us(torch, stream, lambda i: sess.attention(i % args.layers), args.iters)
     kvd = cfg.kv_heads * cfg.head_dim
     nbytes = 2 * args.context * kvd * 4
-    return {"kernel": "attn_scores+attn_exp+attn_out (decode)", "context": args.context, "us_per_attention": us,
+    kernel = "attn_decode_cluster_kernel" if args.attn == "auto" else "attn_scores+attn_exp+attn_out"
+    return {"kernel": kernel, "attn": args.attn, "shape": args.shape, "context": args.context, "us_per_attention": us,
             "kv_bytes": nbytes, "GB_s": nbytes / us / 1e3}
 
 
@@ -100,39 +127,64 @@ def gemm(args):
     _lib.check(L.iris_q8_upload_blocks(_lib.ptr(blocks, C.c_uint8), args.rows, args.cols, C.byref(h)), "upload")
     x = torch.randint(-(1 << 20), 1 << 20, (args.tokens, args.cols), dtype=torch.int32, device="cuda")
     out = torch.empty((args.tokens, args.rows), dtype=torch.int32, device="cuda")
-    stream = torch.cuda.current_stream()
-    run = lambda: _lib.check(L.iris_q8_product_device_path(h, x.data_ptr(), args.tokens, out.data_ptr(),
-                                                           stream.cuda_stream, _lib.PATH_GEMM), "gemm")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    # the no-alloc entry point: the tiled GEMM path without a synchronisation
+    run = lambda: _lib.check(L.iris_q8_product_device_noalloc(h, x.data_ptr(), args.tokens, out.data_ptr(),
+                                                              stream.cuda_stream), "gemm")
     run()
     torch.cuda.synchronize()
-    e0, e1 = _events(torch)
-    e0.record(stream)
-    for _ in range(args.iters):
-        run()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / args.iters
+    us = device_us(torch, stream, lambda i: run(), args.iters)
     ops = 2 * args.rows * args.cols * args.tokens
     L.q8gpu_free(h)
     return {"kernel": "planes_kernel + q8_gemm_kernel<EPI_STORE>", "rows": args.rows, "cols": args.cols,
             "tokens": args.tokens, "us_per_launch": us, "TOPS": ops / us / 1e6}
 
 
+def product(args):
+    import torch
+    from iris_b200.model import DeviceModel
+    from iris_b200.shapes import mistral_7b
+    cfg = mistral_7b()
+    cfg = type(cfg)(**{**cfg.__dict__, "layers": args.layers})
+    model = DeviceModel(cfg, seed=args.seed)
+    sess = model.session(64)
+    sess.prefill(np.random.default_rng(args.seed).integers(0, cfg.vocab, size=16).tolist())
+    stream = torch.cuda.ExternalStream(sess.stream_ptr)
+    for l in range(args.layers):
+        sess.product(l, args.product_which)
+    sess.synchronize()
+    us = device_us(torch, stream, lambda i: sess.product(i % args.layers, args.product_which), args.iters)
+    H, F, qd, kvd, V = cfg.hidden, cfg.ffn, cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.vocab
+    rows, cols, outb = {0: (qd + 2 * kvd, H, 4 * (qd + 2 * kvd)), 1: (H, qd, 4 * H), 2: (2 * F, H, 4 * F),
+                        3: (H, F, 4 * H), 4: (V, H, 4 * V)}[args.product_which]
+    nbytes = rows * cols * 34 // 32 + 4 * cols + outb
+    sess.close()
+    model.close()
+    names = {0: "IN_NORM, EPI_STORE", 1: "IN_PLANES, EPI_STORE", 2: "IN_NORM, EPI_SILU_MUL",
+             3: "IN_PLANES, EPI_STORE", 4: "IN_NORM, EPI_LOGITS"}
+    return {"kernel": f"q8_gemv_tma_kernel<{names[args.product_which]}>", "rows": rows, "cols": cols,
+            "us_per_launch": us, "bytes_per_launch": nbytes, "GB_s": nbytes / us / 1e3}
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["gemv", "attention", "gemm"])
+    p.add_argument("which", choices=["gemv", "attention", "gemm", "product"])
+    p.add_argument("--product", type=int, default=2, dest="product_which")
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
     p.add_argument("--tokens", type=int, default=256)
     p.add_argument("--copies", type=int, default=1)
     p.add_argument("--context", type=int, default=2560)
     p.add_argument("--layers", type=int, default=1)
+    p.add_argument("--attn", choices=["auto", "split"], default="auto")
+    p.add_argument("--shape", default="", help="cluster,hpc,ring of the one-launch attention")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--seed", type=int, default=7)
     args = p.parse_args()
     from iris_b200 import build
     build.build()
-    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm}[args.which](args)), flush=True)
+    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product}[args.which](args)), flush=True)
 
 
 if __name__ == "__main__":

@@ -246,6 +246,14 @@ class Session:
         """Launches one single-query attention of `layer` (for timing)."""
         check(lib().iris_session_attention(self._h, layer), "iris_session_attention")
 
+    def set_attention(self, mode: str) -> None:
+        """'auto' (one cluster launch where possible) or 'split' (three launches)."""
+        check(lib().iris_session_set_attention(self._h, {"auto": 0, "split": 1}[mode]), "iris_session_set_attention")
+
+    def set_attention_shape(self, cluster: int, hpc: int, ring: int) -> None:
+        """Explicit one-launch decode attention shape (tuning)."""
+        check(lib().iris_session_set_attention_shape(self._h, cluster, hpc, ring), "iris_session_set_attention_shape")
+
     def kv(self, layer: int, first: int, count: int):
         kvd = self.model.cfg.kv_heads * self.model.cfg.head_dim
         k = np.empty((count, kvd), np.int32)

@@ -25,6 +25,9 @@ int32_t shim_scaled_score(const int32_t* q, const int32_t* k, uint32_t n, uint32
 }
 int64_t shim_exp_term(int32_t logit, int32_t mx) { return softmax_exp_term_act(logit, mx); }
 int32_t shim_softmax_weight(int64_t term, uint64_t sum) { return softmax_weight(term, sum); }
+int32_t shim_softmax_weight_inv(int64_t term, uint64_t sum) {
+  return softmax_weight_inv(term, sum, UINT64_MAX / sum);
+}
 int32_t shim_tanh(int32_t x) { return tanh_act(x); }
 int32_t shim_gelu(int32_t x) { return gelu_tanh(x); }
 int32_t shim_softcap(int32_t x, int32_t c) { return softcap_act(x, c); }

@@ -40,6 +40,7 @@ def S(tmp_path_factory):
         "shim_scaled_score": (C.c_int32, [i32p, i32p, C.c_uint32, C.c_uint32]),
         "shim_exp_term": (C.c_int64, [C.c_int32, C.c_int32]),
         "shim_softmax_weight": (C.c_int32, [C.c_int64, C.c_uint64]),
+        "shim_softmax_weight_inv": (C.c_int32, [C.c_int64, C.c_uint64]),
         "shim_tanh": (C.c_int32, [C.c_int32]),
         "shim_gelu": (C.c_int32, [C.c_int32]),
         "shim_softcap": (C.c_int32, [C.c_int32, C.c_int32]),
@@ -135,9 +136,24 @@ def test_softmax_pieces(S, L):
         terms = [S.shim_exp_term(int(x), mx) for x in logits]
         total = sum(terms)
         mine = [S.shim_softmax_weight(t, total) for t in terms]
+        assert [S.shim_softmax_weight_inv(t, total) for t in terms] == mine
         first = int(np.argmax(logits))
         mine[first] += 65536 - sum(mine)
         assert mine == w.tolist()
+
+
+def test_softmax_weight_by_reciprocal(S):
+    """The device's reciprocal form of the weight division equals the plain
+    division for every term in [0, 2^32] and sums in [2^32, 2^62)."""
+    rng = np.random.default_rng(12)
+    sums = [2**32, 2**32 + 1, 2**33 - 1, 3 << 31, 2**44 + 12345, 2**61 + 7, 2**62 - 1]
+    sums += [int(x) for x in rng.integers(2**32, 2**40, size=300)]
+    sums += [int(x) for x in rng.integers(2**32, 2**62, size=300)]
+    for total in sums:
+        terms = [0, 1, 2**32, 2**32 - 1, 2**31, total % 2**32]
+        terms += [int(x) for x in rng.integers(0, 2**32 + 1, size=40)]
+        for t in terms:
+            assert S.shim_softmax_weight_inv(t, total) == S.shim_softmax_weight(t, total), (t, total)
 
 
 def test_gemma_functions(S, L):

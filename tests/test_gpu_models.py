@@ -25,12 +25,13 @@ def seeded_prompt(seed, n, vocab):
     return np.random.default_rng(seed).integers(0, vocab, size=n).tolist()
 
 
-def run_both(cfg, seed, prompt, steps, per_block=False, eos=()):
+def run_both(cfg, seed, prompt, steps, per_block=False, eos=(), attn="auto"):
     from iris_b200.model import DeviceModel, synth_host_weights
     from oracle.models import OracleModel
     w = synth_host_weights(cfg, seed, per_block)
     dm = DeviceModel(cfg, weights=w)
     sess = dm.session(len(prompt) + steps + 8)
+    sess.set_attention(attn)
     got = sess.generate(prompt, steps, eos, want_logits=True)
     want = OracleModel(cfg, w).generate(prompt, steps, eos)
     return dm, sess, w, got, want
@@ -88,6 +89,26 @@ def test_single_token_prompt():
         prompt = seeded_prompt(13, 1, cfg.vocab)
         _, _, _, got, want = run_both(cfg, 13, prompt, 5)
         assert_same(got, want)
+
+
+def test_three_launch_decode_attention():
+    """The split (three-launch) decode attention, kept for shapes the cluster
+    kernel does not serve, on both families."""
+    from iris_b200.shapes import parity_gemma, parity_mistral
+    for cfg, seed in ((parity_mistral(), 21), (parity_gemma(), 22)):
+        prompt = seeded_prompt(seed, 23, cfg.vocab)
+        _, _, _, got, want = run_both(cfg, seed, prompt, 9, attn="split")
+        assert_same(got, want)
+
+
+def test_long_context_spans_several_tiles_a_block():
+    """1100 positions: every block of a 16-block cluster streams several
+    32-position key and value tiles."""
+    from iris_b200.shapes import parity_mistral
+    cfg = parity_mistral()
+    prompt = seeded_prompt(31, 1100, cfg.vocab)
+    _, _, _, got, want = run_both(cfg, 31, prompt, 4)
+    assert_same(got, want)
 
 
 def test_long_prompt_crosses_device_ranges():
