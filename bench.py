@@ -96,6 +96,19 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def profiled_traffic():
+    """DRAM bytes (read + write) a launch of the roofline kernel moved in its
+    committed ncu capture (profiles/q8_gemv_gate_up_28672x4096.md), or None."""
+    path = ROOT / "profiles" / "q8_gemv_gate_up_28672x4096.md"
+    try:
+        for line in path.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
 def algorithmic_bytes_per_step(cfg, context_positions):
     """Bytes a decode pass must move: every Q8_0 weight once (34 bytes per 32
     weights), the norm vectors, the embedding row, the K/V rows it reads and
@@ -313,8 +326,9 @@ def main():
                    "global_batch": world, "parallelism": f"replicas x{world}" if world > 1 else "single",
                    "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
-                     "kernel": "q8_gemv_kernel<IN_NORM, EPI_SILU_MUL> (fused gate|up, 28672x4096)",
+                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "algorithmic_bytes": gemv_bytes,
+                     "kernel": "q8_gemv_tma_kernel<IN_NORM, EPI_SILU_MUL> (fused gate|up, 28672x4096)",
                      "peak_kind": peak_kind},
         "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
                           "bytes_per_step": step_bytes},

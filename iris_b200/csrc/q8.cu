@@ -247,15 +247,34 @@ __device__ uint64_t block_sum_sat(uint64_t v, uint64_t* red) {
 __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
                               int64_t eps, uint32_t K, uint8_t* planes, uint64_t* red,
                               int32_t* s_scale) {
+  // Rows of up to kHeld values a thread are held in registers, the values and
+  // the norm weights loaded together: one pass over global memory.
+  constexpr uint32_t kHeld = 2;  // int4 pieces a thread
+  const uint32_t step = blockDim.x * 4;
+  const bool held = K <= kHeld * step;
+  int4 xv[kHeld], wv[kHeld];
+  if (held) {
+#pragma unroll
+    for (uint32_t j = 0; j < kHeld; ++j) {
+      const uint32_t i = threadIdx.x * 4 + j * step;
+      xv[j] = i < K ? *(const int4*)(x + i) : make_int4(0, 0, 0, 0);
+      wv[j] = i < K && norm_w ? *(const int4*)(norm_w + i) : make_int4(0, 0, 0, 0);
+    }
+  }
   int32_t scale = 0;
   if (norm_w) {
     uint64_t ss = 0;
-    for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
-      int4 v = *(const int4*)(x + i);
+    auto square_sum = [&](int4 v) {
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.x * v.x));
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.y * v.y));
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.z * v.z));
       ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.w * v.w));
+    };
+    if (held) {
+#pragma unroll
+      for (uint32_t j = 0; j < kHeld; ++j) square_sum(xv[j]);
+    } else {
+      for (uint32_t i = threadIdx.x * 4; i < K; i += step) square_sum(*(const int4*)(x + i));
     }
     uint64_t total = block_sum_sat(ss, red);  // in every lane of warp 0
     if (threadIdx.x < 32) {  // rms_scale_from_sumsq with the warp-parallel inverse square root
@@ -266,10 +285,8 @@ __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
     scale = *s_scale;
   }
   int wide = 0;
-  for (uint32_t i = threadIdx.x * 4; i < K; i += blockDim.x * 4) {
-    int4 v = *(const int4*)(x + i);
+  auto emit = [&](int4 v, int4 w, uint32_t i) {
     if (norm_w) {
-      int4 w = *(const int4*)(norm_w + i);
       v.x = mul_sat(mul_sat(v.x, scale), w.x);
       v.y = mul_sat(mul_sat(v.y, scale), w.y);
       v.z = mul_sat(mul_sat(v.z, scale), w.z);
@@ -277,6 +294,16 @@ __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
     }
     wide |= !fits_three_planes(v.x) | !fits_three_planes(v.y) | !fits_three_planes(v.z) | !fits_three_planes(v.w);
     put_planes4(planes, K, i, v);
+  };
+  if (held) {
+#pragma unroll
+    for (uint32_t j = 0; j < kHeld; ++j) {
+      const uint32_t i = threadIdx.x * 4 + j * step;
+      if (i < K) emit(xv[j], wv[j], i);
+    }
+  } else {
+    for (uint32_t i = threadIdx.x * 4; i < K; i += step)
+      emit(*(const int4*)(x + i), norm_w ? *(const int4*)(norm_w + i) : make_int4(0, 0, 0, 0), i);
   }
   return __syncthreads_or(wide) != 0;
 }

@@ -6,6 +6,11 @@
       one single-query attention over a mistral-7b-shaped cache;
   python -m iris_b200.microbench gemm [--rows 6144 --cols 4096 --tokens 256]
       the many-token product;
+  python -m iris_b200.microbench sweep
+      the Q8 sweep (M in 1, 16, 128, 2048 x (N, K) pairs): this library's
+      device products, and both this library's and the reference's
+      q8gpu_product (host buffers in and out) when oracle/_ref holds the
+      reference kernel;
   python -m iris_b200.microbench product [--product 2 --layers 2]
       one of the decode pass's own products (0 q|k|v, 1 o, 2 gate|up,
       3 down, 4 head) of a mistral-7b-shaped session, layer after layer.
@@ -167,9 +172,89 @@ def product(args):
             "us_per_launch": us, "bytes_per_launch": nbytes, "GB_s": nbytes / us / 1e3}
 
 
+def sweep(args):
+    """Q8 sweep: one JSON line a (M, N, K). `device_us`: this library's
+    product on device buffers (GEMV for M = 1, tiled GEMM otherwise);
+    `host_us` / `ref_host_us`: q8gpu_product of this library / of the
+    reference's kernel with host activations and outputs (copies included)."""
+    import time
+    import torch
+    from iris_b200 import _lib
+    from oracle import oracle
+    L = _lib.lib()
+    _lib.check(L.q8gpu_init(), "q8gpu_init")
+    ref = oracle.reference_q8()
+    if ref is not None:
+        assert ref.q8gpu_init() == 0
+    rng = np.random.default_rng(args.seed)
+    lines = []
+    for n, k in [(2048, 2048), (16384, 2048), (4096, 4096), (14336, 4096)]:
+        nb = n * k // 32
+        bits = (rng.integers(0, 64, size=nb) + 0x2400).astype(np.int64)  # finite positive scales
+        ex, man = (bits >> 10) & 0x1F, bits & 0x3FF
+        scales = ((1024 + man) << np.maximum(ex - 1, 0)).astype(np.int64)
+        weights = rng.integers(-127, 128, size=n * k).astype(np.int8)
+        h = C.c_void_p()
+        _lib.check(L.q8gpu_upload(weights.ctypes.data_as(C.POINTER(C.c_int8)), _lib.ptr(scales, C.c_int64), n, k,
+                                  C.byref(h)), "upload")
+        hr = C.c_void_p()
+        if ref is not None:
+            assert ref.q8gpu_upload(weights.ctypes.data_as(C.POINTER(C.c_int8)),
+                                    scales.ctypes.data_as(C.POINTER(C.c_int64)), n, k, C.byref(hr)) == 0
+        for m in [1, 16, 128, 2048]:
+            acts = rng.integers(-(1 << 20), 1 << 20, size=(m, k)).astype(np.int32)
+            x = torch.from_numpy(acts).cuda()
+            out = torch.empty((m, n), dtype=torch.int32, device="cuda")
+            stream = torch.cuda.Stream()
+            torch.cuda.synchronize()
+            iters = max(2, min(args.iters, int(2e9 / (2 * m * n * k)) + 2))
+            if m * k * 4 <= _lib.NOALLOC_PLANES_BYTES:  # captured: no host launch overhead
+                run = lambda i: _lib.check(L.iris_q8_product_device_noalloc(h, x.data_ptr(), m, out.data_ptr(),
+                                                                            stream.cuda_stream), "product")
+                run(0)
+                stream.synchronize()
+                dev = device_us(torch, stream, run, iters)
+            else:  # large M: the GEMM dominates the eager call
+                run = lambda: _lib.check(L.iris_q8_product_device(h, x.data_ptr(), m, out.data_ptr(),
+                                                                  stream.cuda_stream), "product")
+                run()
+                stream.synchronize()
+                e0, e1 = _events(torch)
+                e0.record(stream)
+                for _ in range(iters):
+                    run()
+                e1.record(stream)
+                stream.synchronize()
+                dev = e0.elapsed_time(e1) * 1e3 / iters
+            host_out = np.empty(m * n, np.int32)
+            def host_time(lib, handle):
+                lib.q8gpu_product(handle, _lib.ptr(acts, C.c_int32), m, _lib.ptr(host_out, C.c_int32))
+                reps = max(1, min(5, int(5e8 / (2 * m * n * k)) + 1))
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    rc = lib.q8gpu_product(handle, _lib.ptr(acts, C.c_int32), m, _lib.ptr(host_out, C.c_int32))
+                    assert rc == 0, rc
+                return (time.perf_counter() - t0) / reps * 1e6
+            mine_host = host_time(L, h)
+            mine_vals = host_out.copy()
+            line = {"m": m, "n": n, "k": k, "device_us": dev, "host_us": mine_host,
+                    "bytes": n * k * 34 // 32 + 4 * m * k + 4 * m * n, "ops": 2 * m * n * k}
+            line["GB_s"] = line["bytes"] / dev / 1e3
+            line["TOPS"] = line["ops"] / dev / 1e6
+            if ref is not None:
+                line["ref_host_us"] = host_time(ref, hr)
+                line["equal_to_reference"] = bool(np.array_equal(mine_vals, host_out))
+            lines.append(line)
+            print(json.dumps(line), flush=True)
+        L.q8gpu_free(h)
+        if ref is not None:
+            ref.q8gpu_free(hr)
+    return {"sweep": len(lines)}
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["gemv", "attention", "gemm", "product"])
+    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep"])
     p.add_argument("--product", type=int, default=2, dest="product_which")
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
@@ -184,7 +269,7 @@ def main():
     args = p.parse_args()
     from iris_b200 import build
     build.build()
-    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product}[args.which](args)), flush=True)
+    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep}[args.which](args)), flush=True)
 
 
 if __name__ == "__main__":

@@ -16,6 +16,11 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "liboracle.so"
+# The reference's GPU product kernel, built unchanged from its own source
+# where the reference checkout is present (oracle/Makefile, _ref/ target).
+REF_Q8_SOURCE = Path(os.environ.get("IRIS_REFERENCE", "/root/reference")) / \
+    "crates/inference/kernels/cuda/q8_product.cu"
+REF_Q8_LIB = HERE / "_ref" / "libq8ref.so"
 
 i32p = C.POINTER(C.c_int32)
 i64p = C.POINTER(C.c_int64)
@@ -72,13 +77,37 @@ class Keys(C.Structure):
     _fields_ = [("n", C.c_size_t), ("positions", u32p), ("k", i32p), ("v", i32p)]
 
 
-def build(force: bool = False) -> Path:
-    """Compile liboracle.so with the committed Makefile (g++, seconds)."""
+def build(force: bool = False, reference: bool = False) -> Path:
+    """Compile liboracle.so with the committed Makefile (g++, seconds); with
+    `reference`, also the reference's own GPU product kernel into _ref/ when
+    the reference checkout is present (nvcc). Tests and the GPU box only use
+    the prebuilt _ref/ file."""
     sources = [HERE / n for n in ("det_num.cc", "layers.cc", "det_num.h", "oracle_abi.h")]
     if force or not LIB_PATH.exists() or any(
             s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in sources):
         subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
+    if reference and REF_Q8_SOURCE.exists() and (force or not REF_Q8_LIB.exists()):
+        subprocess.run(["make", "-s", "-C", str(HERE), "_ref/libq8ref.so"], check=True)
     return LIB_PATH
+
+
+def reference_q8():
+    """The reference's q8gpu_* library (crates/inference/kernels/cuda/
+    q8_product.cu built unchanged for sm_100a), or None when it was not built."""
+    if not REF_Q8_LIB.exists():
+        return None
+    L = C.CDLL(str(REF_Q8_LIB))
+    vp = C.c_void_p
+    L.q8gpu_init.restype = C.c_int
+    L.q8gpu_upload.restype = C.c_int
+    L.q8gpu_upload.argtypes = [C.POINTER(C.c_int8), C.POINTER(C.c_int64), C.c_uint32, C.c_uint32, C.POINTER(vp)]
+    L.q8gpu_product.restype = C.c_int
+    L.q8gpu_product.argtypes = [vp, C.POINTER(C.c_int32), C.c_uint32, C.POINTER(C.c_int32)]
+    L.q8gpu_free.restype = None
+    L.q8gpu_free.argtypes = [vp]
+    L.q8gpu_error.restype = C.c_char_p
+    L.q8gpu_error.argtypes = [C.c_int]
+    return L
 
 
 _lib = None
