@@ -4,8 +4,12 @@ Tests marked `gpu` need a CUDA device and the built libiris_b200.so; the rest
 run on a CPU-only machine (oracle known-answer tests, host logic, the C-ABI
 symbol check, and multi-process gloo tests).
 """
+import ctypes as C
 import os
+import subprocess
 import sys
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
@@ -14,3 +18,37 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built CUDA library")
+
+
+@pytest.fixture(scope="session")
+def detnum_shim(tmp_path_factory):
+    """iris_b200/csrc/detnum.cuh compiled as host C++ (tests/native/detnum_shim.cc)."""
+    out = tmp_path_factory.mktemp("shim") / "libdetnum_shim.so"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-o", str(out),
+                    os.path.join(ROOT, "tests", "native", "detnum_shim.cc")], check=True)
+    L = C.CDLL(str(out))
+    i32p, i64p = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
+    sig = {
+        "shim_requantize": (C.c_int32, [C.c_int64]),
+        "shim_mul_sat": (C.c_int32, [C.c_int32, C.c_int32]),
+        "shim_div_act": (C.c_int32, [C.c_int32, C.c_int32]),
+        "shim_inv_sqrt_acc": (C.c_int32, [C.c_int64]),
+        "shim_rms_scale": (C.c_int32, [i32p, C.c_uint32, C.c_int64]),
+        "shim_silu": (C.c_int32, [C.c_int32]),
+        "shim_sin_cos_q30": (None, [C.c_int64, i64p, i64p]),
+        "shim_sin_cos_acc": (None, [C.c_int64, i32p, i32p]),
+        "shim_scaled_score": (C.c_int32, [i32p, i32p, C.c_uint32, C.c_uint32]),
+        "shim_exp_term": (C.c_int64, [C.c_int32, C.c_int32]),
+        "shim_softmax_weight": (C.c_int32, [C.c_int64, C.c_uint64]),
+        "shim_softmax_weight_inv": (C.c_int32, [C.c_int64, C.c_uint64]),
+        "shim_tanh": (C.c_int32, [C.c_int32]),
+        "shim_gelu": (C.c_int32, [C.c_int32]),
+        "shim_softcap": (C.c_int32, [C.c_int32, C.c_int32]),
+        "shim_q8_dot": (C.c_int32, [i32p, C.POINTER(C.c_uint8), C.c_uint32]),
+        "shim_q8_dequant": (C.c_int32, [C.c_int8, C.c_uint16]),
+        "shim_rotate_half": (None, [i32p, i32p, C.c_int64, C.c_uint32]),
+    }
+    for name, (res, args) in sig.items():
+        getattr(L, name).restype = res
+        getattr(L, name).argtypes = args
+    return L
