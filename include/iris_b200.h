@@ -206,12 +206,15 @@ int iris_session_product(IrisSession* session, uint32_t layer, int which);
  * the session's current query rows; the context is discarded. For timing. */
 int iris_session_attention(IrisSession* session, uint32_t layer);
 /* Selects the decode attention kernels of a session: IRIS_ATTN_AUTO (one
- * thread-block-cluster launch where the device and shape allow it) or
- * IRIS_ATTN_SPLIT (three launches over position chunks). Both give the same
- * values; the captured decode pass is rebuilt. */
+ * launch over the whole GPU where the shape and capacity allow it, else one
+ * thread-block-cluster launch, else three launches), IRIS_ATTN_SPLIT (three
+ * launches over position chunks) or IRIS_ATTN_CLUSTER (the cluster launch
+ * where possible). All give the same values; the captured decode pass is
+ * rebuilt. */
 int iris_session_set_attention(IrisSession* session, int mode);
 #define IRIS_ATTN_AUTO 0
 #define IRIS_ATTN_SPLIT 1
+#define IRIS_ATTN_CLUSTER 2
 /* Tuning hook: an explicit one-launch decode attention shape - blocks a
  * cluster (4, 8 or 16), query heads a block (1, 2 or 4, dividing the group)
  * and shared-memory tile buffers a block (2..12). IRIS_EINVAL when the shape

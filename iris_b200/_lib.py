@@ -18,7 +18,7 @@ IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 
 IRIS_ESCRATCH = 10007
 NOALLOC_PLANES_BYTES = 16 << 20
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
-ATTN_AUTO, ATTN_SPLIT = 0, 1
+ATTN_AUTO, ATTN_SPLIT, ATTN_CLUSTER = 0, 1, 2
 
 # Tensor kinds (include/iris_b200.h)
 T = dict(EMBED=0, HEAD=1, FINAL_NORM=2, W_Q=3, W_K=4, W_V=5, W_O=6, W_GATE=7, W_UP=8, W_DOWN=9,

@@ -558,6 +558,306 @@ __global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnA
   cluster.sync();  // every block's shared memory stays until all have read it
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention in one launch over the whole GPU
+// ---------------------------------------------------------------------------
+//
+// A head group (HPC query heads of one kv group) is split over `chunks`
+// blocks, about one block a multiprocessor over all groups; block r takes the
+// r-th contiguous range of the window [ws, p] and copies all of its key rows
+// and value rows into shared memory with cp.async at its start (two commit
+// groups), so the whole cache read of the step is in flight at once. The
+// three dependent steps of attention_softmax (ops.rs:233-261) meet through
+// global memory: first-maximum keys (atomicMax), sums of exp terms and of
+// weights, and the wrapping weighted value sums (atomicAdd) of the group,
+// with a bounded arrival barrier a step. After the last step every block
+// finishes its share of the group's outputs; the group's last block clears
+// the exchange words for the next launch. The blocks of a launch must be
+// resident together (the plan checks the occupancy); a barrier that waits
+// about a second records a fault instead of hanging.
+
+constexpr uint32_t kGThreads = 256;
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Arrival barrier of one head group: returns once *bar reaches target.
+__device__ __forceinline__ void group_barrier(unsigned int* bar, unsigned int target, unsigned int* fault) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    if (ld_acquire_u32(bar) < target) {
+      const uint64_t t0 = global_ns();
+      for (uint32_t i = 1;; ++i) {
+        __nanosleep(100);
+        if (ld_acquire_u32(bar) >= target) break;
+        if ((i & 63) == 0 && global_ns() - t0 > 1000000000ull) {
+          if (fault) atomicOr(fault, 1u);
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+}
+
+template <uint32_t PER, uint32_t HPC>
+__global__ void __launch_bounds__(kGThreads) attn_decode_grid_kernel(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr uint32_t D = PER * 8, NH = kGThreads / D, kWarps = kGThreads / 32;
+  const uint32_t span_a = a.gspan;                   // even
+  extern __shared__ __align__(16) int32_t gsm[];
+  int32_t* ks = gsm;                                  // [span][D]
+  int32_t* vs = ks + span_a * D;                      // [span][D]
+  uint64_t* tm = (uint64_t*)(vs + span_a * D);        // [span][HPC] exp terms
+  int32_t* sw = (int32_t*)(tm + span_a * HPC);        // [span][HPC] scores, then weights
+  __shared__ unsigned long long best_s[HPC], sum_s[HPC], gbest_s[HPC], gtot_s[HPC], ginv_s[HPC];
+  __shared__ int32_t wsum_s[HPC], resid_s[HPC];
+
+  const uint32_t chunks = a.chunks, grp = blockIdx.x / chunks, rank = blockIdx.x % chunks;
+  const uint32_t h0 = grp * HPC, G = a.heads / a.kv_heads, g = h0 / G;
+  const uint32_t p = query_position(a), ws = window_start(p, a.window), n = p - ws + 1;
+  const uint32_t span = (n + chunks - 1) / chunks;
+  const uint32_t r0 = min(p + 1, ws + rank * span), r1 = min(p + 1, r0 + span), cnt = r1 - r0;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quad = lane >> 3, ql = lane & 7;
+  unsigned int* bar = a.gbar + 2 * grp;
+
+  // every key row, then every value row of the block's range
+  for (uint32_t c = tid; c < cnt * (D / 4); c += kGThreads) {
+    const uint32_t r = c / (D / 4), j = c % (D / 4);
+    cp_async16(ks + r * D + 4 * j, a.kcache + (size_t)(r0 + r) * a.kvd + g * D + 4 * j);
+  }
+  cp_async_commit();
+  for (uint32_t c = tid; c < cnt * (D / 4); c += kGThreads) {
+    const uint32_t r = c / (D / 4), j = c % (D / 4);
+    cp_async16(vs + r * D + 4 * j, a.vcache + (size_t)(r0 + r) * a.kvd + g * D + 4 * j);
+  }
+  cp_async_commit();
+  if (tid < HPC) {
+    best_s[tid] = 0;
+    sum_s[tid] = 0;
+    wsum_s[tid] = 0;
+  }
+  int4 q[HPC][PER / 4];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < PER / 4; ++i) q[h][i] = *(const int4*)(a.q + (size_t)(h0 + h) * D + 4 * (ql + 8 * i));
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+  __syncthreads();  // every key row has landed
+
+  // ---- 1. scores: 8 lanes a position, four positions a warp at a time
+  unsigned long long best[HPC];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
+  for (uint32_t base = 0; base < cnt; base += kWarps * 4) {
+    const uint32_t tl = base + warp * 4 + quad;
+    const bool live = tl < cnt;
+    const int32_t* krow = ks + (live ? tl : 0) * D;
+    int4 kv[PER / 4];
+#pragma unroll
+    for (uint32_t i = 0; i < PER / 4; ++i) kv[i] = *(const int4*)(krow + 4 * (ql + 8 * i));
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      int64_t c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+#pragma unroll
+      for (uint32_t i = 0; i < PER / 4; ++i) {
+        mac_wide(c0, q[h][i].x, kv[i].x);
+        mac_wide(c1, q[h][i].y, kv[i].y);
+        mac_wide(c2, q[h][i].z, kv[i].z);
+        mac_wide(c3, q[h][i].w, kv[i].w);
+      }
+      uint64_t sum = (uint64_t)c0 + (uint64_t)c1 + (uint64_t)c2 + (uint64_t)c3;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      if (ql == 0 && live) {
+        const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
+        sw[tl * HPC + h] = sc;
+        const unsigned long long key = best_key(sc, r0 + tl);
+        best[h] = key > best[h] ? key : best[h];
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+    if (ql == 0 && best[h]) atomicMax(&best_s[h], best[h]);
+  __syncthreads();
+  if (tid < HPC && best_s[tid]) atomicMax(a.gbest + h0 + tid, best_s[tid]);
+  group_barrier(bar, chunks, a.fault);
+  if (tid < HPC) gbest_s[tid] = __ldcg(a.gbest + h0 + tid);
+  __syncthreads();
+
+  // ---- 2. exp terms against the group's first maximum (kept), their sums.
+  // Element e = position * HPC + head: thread tid always meets head tid % HPC.
+  const uint32_t my_h = tid % HPC;
+  {
+    const int32_t mx = best_key_value(gbest_s[my_h]);
+    uint64_t e = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kGThreads) {
+      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
+      tm[el] = term;
+      e += term;
+    }
+    e = head_lane_sum<HPC>(e);
+    if (lane < HPC && e) atomicAdd(&sum_s[lane], (unsigned long long)e);
+  }
+  __syncthreads();
+  if (tid < HPC && sum_s[tid]) atomicAdd(a.gsum + h0 + tid, sum_s[tid]);
+  group_barrier(bar, 2 * chunks, a.fault);
+  if (tid < HPC) {
+    const unsigned long long tot = __ldcg(a.gsum + h0 + tid);
+    gtot_s[tid] = tot;
+    ginv_s[tid] = tot ? UINT64_MAX / tot : 0;  // tot >= 2^32 after a complete exchange
+  }
+  __syncthreads();
+
+  // ---- 3. weights over the scores and their sums, then the value sums
+  {
+    const uint64_t tot = gtot_s[my_h], inv = ginv_s[my_h];
+    int32_t wsum = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kGThreads) {
+      const int32_t w = tot ? softmax_weight_inv((int64_t)tm[el], tot, inv) : 0;
+      sw[el] = w;
+      wsum += w;
+    }
+    wsum = head_lane_sum<HPC>(wsum);
+    if (lane < HPC && wsum) atomicAdd(&wsum_s[lane], wsum);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // every value row has landed; the weights are written
+  if (tid < HPC && wsum_s[tid]) atomicAdd(a.wsum + h0 + tid, wsum_s[tid]);
+  {
+    const uint32_t dim = tid % D, hv = tid / D;
+    int64_t acc[HPC];
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) acc[h] = 0;
+#pragma unroll 4
+    for (uint32_t r = hv; r < cnt; r += NH) {
+      const int32_t v = vs[r * D + dim];
+      int32_t w[HPC];
+      if (HPC == 4) {
+        const int4 w4 = *(const int4*)(sw + r * HPC);
+        w[0] = w4.x, w[1] = w4.y, w[2 % HPC] = w4.z, w[3 % HPC] = w4.w;
+      } else if (HPC == 2) {
+        const int2 w2 = *(const int2*)(sw + r * HPC);
+        w[0] = w2.x, w[1 % HPC] = w2.y;
+      } else {
+        w[0] = sw[r];
+      }
+#pragma unroll
+      for (uint32_t h = 0; h < HPC; ++h) mac_wide(acc[h], w[h], v);
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+      if (acc[h]) atomicAdd((unsigned long long*)(a.acc + (size_t)(h0 + h) * D + dim), (unsigned long long)acc[h]);
+  }
+  group_barrier(bar, 3 * chunks, a.fault);
+
+  // ---- 4. block `rank` finishes outputs [rank * share, (rank + 1) * share)
+  if (tid < HPC) resid_s[tid] = sub_sat(kOneAct, (int32_t)__ldcg((const int*)(a.wsum + h0 + tid)));  // ops.rs:274-276
+  __syncthreads();
+  const uint32_t share = (HPC * D + chunks - 1) / chunks, qd = a.heads * D;
+  for (uint32_t o = rank * share + tid; o < min(HPC * D, (rank + 1) * share); o += kGThreads) {
+    const uint32_t h = o / D, i = o % D, hh = h0 + h;
+    uint64_t s = (uint64_t)atomicExch((unsigned long long*)(a.acc + (size_t)hh * D + i), 0ull);
+    const uint32_t tmax = best_key_token(gbest_s[h]);
+    s += (uint64_t)((int64_t)resid_s[h] * a.vcache[(size_t)tmax * a.kvd + g * D + i]);
+    const int32_t v = requantize((int64_t)s);
+    put_planes(a.ctx_planes, qd, hh * D + i, v);
+    if (a.ctx) a.ctx[hh * D + i] = v;
+  }
+  // the group's last block clears its exchange words for the next launch
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(bar + 1, 1u) == chunks - 1) {
+      __threadfence();
+      for (uint32_t h = 0; h < HPC; ++h) {
+        a.gbest[h0 + h] = 0;
+        a.gsum[h0 + h] = 0;
+        a.wsum[h0 + h] = 0;
+      }
+      bar[0] = 0;
+      bar[1] = 0;
+      __threadfence();
+    }
+  }
+}
+
+size_t attention_grid_smem(uint32_t d, uint32_t hpc, uint32_t span) {
+  return (size_t)span * d * 8 + (size_t)span * hpc * 12;
+}
+
+int grid_blocks_per_sm(uint32_t d, uint32_t hpc, size_t smem) {
+  int n = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  const uint32_t per = d / 8;
+#define IRIS_GFITS(PER, HPC) \
+  if (per == PER && hpc == HPC) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, attn_decode_grid_kernel<PER, HPC>, kGThreads, smem);
+  IRIS_GFITS(4, 1) IRIS_GFITS(4, 2) IRIS_GFITS(4, 4)
+  IRIS_GFITS(8, 1) IRIS_GFITS(8, 2) IRIS_GFITS(8, 4)
+  IRIS_GFITS(16, 1) IRIS_GFITS(16, 2) IRIS_GFITS(16, 4)
+  IRIS_GFITS(32, 1) IRIS_GFITS(32, 2)
+#undef IRIS_GFITS
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+void attention_grid_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t* hpc,
+                         uint32_t* chunks, uint32_t* span) {
+  const uint32_t G = heads / kv_heads;
+  uint32_t h = 4;
+  while (h > 1 && (G % h || h * d > 512)) h >>= 1;
+  *hpc = h;
+  *chunks = 0;
+  *span = 0;
+  if (d % 32 || d > 256 || (d == 256 && h > 2)) return;
+  int sms = 0, dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return;
+  const uint32_t groups = heads / h;
+  const uint32_t c = (uint32_t)sms / groups;
+  if (c < 2) return;
+  const uint32_t sp = (((cap + c - 1) / c) + 1) & ~1u;
+  const size_t smem = attention_grid_smem(d, h, sp);
+  if (smem > kClusterSmemMax) return;
+  // every block of the launch must be resident at once
+  if ((uint64_t)grid_blocks_per_sm(d, h, smem) * (uint32_t)sms < (uint64_t)groups * c) return;
+  *chunks = c;
+  *span = sp;
+}
+
+cudaError_t launch_attention_grid(const AttnArgs& a, cudaStream_t s) {
+  const uint32_t per = a.d / 8;
+  const dim3 grid(a.chunks * (a.heads / a.ghpc));
+  const size_t smem = attention_grid_smem(a.d, a.ghpc, a.gspan);
+#define IRIS_GRID(PER, HPC) \
+  if (per == PER && a.ghpc == HPC) return launch_k(attn_decode_grid_kernel<PER, HPC>, grid, dim3(kGThreads), smem, s, a);
+  IRIS_GRID(4, 1) IRIS_GRID(4, 2) IRIS_GRID(4, 4)
+  IRIS_GRID(8, 1) IRIS_GRID(8, 2) IRIS_GRID(8, 4)
+  IRIS_GRID(16, 1) IRIS_GRID(16, 2) IRIS_GRID(16, 4)
+  IRIS_GRID(32, 1) IRIS_GRID(32, 2)
+#undef IRIS_GRID
+  return cudaErrorInvalidValue;
+}
+
+template <uint32_t PER, uint32_t HPC>
+cudaError_t prepare_grid_one() {
+  return cudaFuncSetAttribute(attn_decode_grid_kernel<PER, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kClusterSmemMax);
+}
+
 // Shared memory of one block of the one-launch decode attention.
 size_t cluster_smem_bytes(uint32_t d, uint32_t hpc, uint32_t span, uint32_t ring) {
   return (size_t)ring * kTileP * d * 4 + (size_t)span * hpc * 12 + (size_t)hpc * d * 8;
@@ -690,6 +990,13 @@ cudaError_t prepare_attention_cluster_kernels() {
   IRIS_CLUSTER_ATTR(16, 1) IRIS_CLUSTER_ATTR(16, 2) IRIS_CLUSTER_ATTR(16, 4)
   IRIS_CLUSTER_ATTR(32, 1) IRIS_CLUSTER_ATTR(32, 2)
 #undef IRIS_CLUSTER_ATTR
+#define IRIS_GRID_ATTR(PER, HPC) \
+  if (e == cudaSuccess) e = prepare_grid_one<PER, HPC>();
+  IRIS_GRID_ATTR(4, 1) IRIS_GRID_ATTR(4, 2) IRIS_GRID_ATTR(4, 4)
+  IRIS_GRID_ATTR(8, 1) IRIS_GRID_ATTR(8, 2) IRIS_GRID_ATTR(8, 4)
+  IRIS_GRID_ATTR(16, 1) IRIS_GRID_ATTR(16, 2) IRIS_GRID_ATTR(16, 4)
+  IRIS_GRID_ATTR(32, 1) IRIS_GRID_ATTR(32, 2)
+#undef IRIS_GRID_ATTR
   return e;
 }
 
@@ -698,6 +1005,7 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
   if (a.d % 32 || a.d > 256 || a.hpc == 0 || a.hpc > (uint32_t)kMaxHpc || G % a.hpc ||
       (a.d == 256 && a.hpc > 2))
     return cudaErrorInvalidValue;
+  if (a.chunks) return launch_attention_grid(a, s);
   if (a.cluster) return launch_attention_cluster(a, s);
   dim3 grid(a.heads / a.hpc, a.nchunks);
   cudaError_t e = launch_attn_scores(a, grid, s);

@@ -37,6 +37,14 @@ struct AttnArgs {
   // three-launch path), query heads a block, positions a block at most
   // (even), tile buffers a block
   uint32_t cluster, chpc, span, ring;
+  // one-launch decode over the whole GPU (attention_grid_plan): blocks a head
+  // group (0 = not used), positions a block at most (even), the group
+  // exchange words (zero between launches) and the fault word
+  uint32_t chunks, ghpc, gspan;
+  unsigned long long* gbest;  // [heads] first-maximum keys
+  unsigned long long* gsum;   // [heads] sums of exp terms
+  unsigned int* gbar;         // [2 * heads]: arrivals, then finished blocks, a head group
+  unsigned int* fault;
 };
 
 // Query heads a decode-attention block handles, and the chunk count for a
@@ -48,6 +56,12 @@ uint32_t attention_chunks(uint32_t cap);
 // the three-launch path), positions a block at most and tile buffers a block.
 void attention_cluster_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t* hpc,
                             uint32_t* cluster, uint32_t* span, uint32_t* ring);
+
+// The whole-GPU decode attention for a cache of `cap` positions: query heads
+// a block, blocks a head group (0 when the shape or capacity needs another
+// path) and positions a block at most.
+void attention_grid_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t cap, uint32_t* hpc,
+                         uint32_t* chunks, uint32_t* span);
 
 // Checks an explicit one-launch shape (blocks a cluster, query heads a block,
 // tile buffers a block) for the model and capacity; sets *span.

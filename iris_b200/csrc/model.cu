@@ -138,7 +138,11 @@ struct IrisSession {
   int64_t* acc = nullptr;
   unsigned int* counters = nullptr;
   uint32_t nchunks = 0, hpc = 1;
-  uint32_t cluster = 0, chpc = 1, span = 0, ring = 0;  // one-launch decode attention
+  uint32_t cluster = 0, chpc = 1, span = 0, ring = 0;  // one-launch cluster decode attention
+  uint32_t chunks = 0, ghpc = 1, gspan = 0;               // one-launch whole-GPU decode attention
+  unsigned long long *gbest = nullptr, *gsum = nullptr;
+  unsigned int* gbar = nullptr;
+  unsigned int* fault = nullptr;
   // decode GEMV split scratch (zero between launches)
   unsigned long long* split_acc = nullptr;
   unsigned int* split_count = nullptr;
@@ -157,7 +161,7 @@ void free_session(IrisSession* s) {
   void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
-                  s->acc, s->counters, s->split_acc, s->split_count};
+                  s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -196,6 +200,14 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   s->nchunks = attention_chunks(cap);
   s->hpc = attention_hpc(m->heads, m->kvh);
   attention_cluster_plan(m->heads, m->kvh, m->d, cap, &s->chpc, &s->cluster, &s->span, &s->ring);
+  attention_grid_plan(m->heads, m->kvh, m->d, cap, &s->ghpc, &s->chunks, &s->gspan);
+  s->fault = device_fault_word();
+  if (e == cudaSuccess) e = dalloc(&s->gbest, m->heads);
+  if (e == cudaSuccess) e = dalloc(&s->gsum, m->heads);
+  if (e == cudaSuccess) e = dalloc(&s->gbar, 2 * m->heads);
+  if (e == cudaSuccess) e = cudaMemset(s->gbest, 0, m->heads * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(s->gsum, 0, m->heads * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(s->gbar, 0, 2 * m->heads * sizeof(unsigned int));
   if (e == cudaSuccess) e = dalloc(&s->scores, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->terms, (size_t)m->heads * cap);
   if (e == cudaSuccess) e = dalloc(&s->chunk_best, (size_t)m->heads * s->nchunks);
@@ -264,6 +276,13 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
   a.chpc = s->chpc;
   a.span = s->span;
   a.ring = s->ring;
+  a.chunks = s->chunks;
+  a.ghpc = s->ghpc;
+  a.gspan = s->gspan;
+  a.gbest = s->gbest;
+  a.gsum = s->gsum;
+  a.gbar = s->gbar;
+  a.fault = s->fault;
   return a;
 }
 
@@ -994,10 +1013,13 @@ static int rebuild_graph_later(IrisSession* s) {
 }
 
 int iris_session_set_attention(IrisSession* s, int mode) {
-  if (!s || (mode != IRIS_ATTN_AUTO && mode != IRIS_ATTN_SPLIT)) return IRIS_EINVAL;
+  if (!s || mode < IRIS_ATTN_AUTO || mode > IRIS_ATTN_CLUSTER) return IRIS_EINVAL;
   IrisModel* m = s->m;
-  if (mode == IRIS_ATTN_SPLIT) s->cluster = 0;
-  else attention_cluster_plan(m->heads, m->kvh, m->d, s->cap, &s->chpc, &s->cluster, &s->span, &s->ring);
+  s->chunks = 0;
+  s->cluster = 0;
+  if (mode != IRIS_ATTN_SPLIT)
+    attention_cluster_plan(m->heads, m->kvh, m->d, s->cap, &s->chpc, &s->cluster, &s->span, &s->ring);
+  if (mode == IRIS_ATTN_AUTO) attention_grid_plan(m->heads, m->kvh, m->d, s->cap, &s->ghpc, &s->chunks, &s->gspan);
   return rebuild_graph_later(s);
 }
 
@@ -1010,6 +1032,7 @@ int iris_session_set_attention_shape(IrisSession* s, uint32_t cluster, uint32_t 
   s->chpc = hpc;
   s->ring = ring;
   s->span = span;
+  s->chunks = 0;
   return rebuild_graph_later(s);
 }
 

@@ -734,6 +734,18 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   }
 }
 
+unsigned int* device_fault_word() {
+  static unsigned int* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_fault) != cudaSuccess) return nullptr;
+    addr[dev] = (unsigned int*)p;
+  }
+  return addr[dev];
+}
+
 cudaError_t take_device_fault(uint32_t* fault) {
   uint32_t zero = 0;
   cudaError_t e = cudaMemcpyFromSymbol(fault, g_fault, sizeof(uint32_t));

@@ -114,6 +114,9 @@ __host__ __device__ inline unsigned long long best_key(int32_t v, uint32_t idx) 
 // Non-zero once a kernel gave up a bounded wait (a stalled pipeline); read and
 // cleared by the host.
 cudaError_t take_device_fault(uint32_t* fault);
+// Device address of that fault word (kernels of other files record into it);
+// looked up once per device, before any stream capture.
+unsigned int* device_fault_word();
 
 // Uploads raw Q8_0 blocks into rows [row_offset + i*row_stride] of dst.
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,

@@ -117,7 +117,8 @@ def attention(args):
     us = device_us(torch, stream, lambda i: sess.attention(i % args.layers), args.iters)
     kvd = cfg.kv_heads * cfg.head_dim
     nbytes = 2 * args.context * kvd * 4
-    kernel = "attn_decode_cluster_kernel" if args.attn == "auto" else "attn_scores+attn_exp+attn_out"
+    kernel = {"auto": "attn_decode_grid_kernel (where planned)", "cluster": "attn_decode_cluster_kernel",
+              "split": "attn_scores+attn_exp+attn_out"}[args.attn]
     return {"kernel": kernel, "attn": args.attn, "shape": args.shape, "context": args.context, "us_per_attention": us,
             "kv_bytes": nbytes, "GB_s": nbytes / us / 1e3}
 
@@ -262,7 +263,7 @@ def main():
     p.add_argument("--copies", type=int, default=1)
     p.add_argument("--context", type=int, default=2560)
     p.add_argument("--layers", type=int, default=1)
-    p.add_argument("--attn", choices=["auto", "split"], default="auto")
+    p.add_argument("--attn", choices=["auto", "split", "cluster"], default="auto")
     p.add_argument("--shape", default="", help="cluster,hpc,ring of the one-launch attention")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--seed", type=int, default=7)

@@ -247,8 +247,10 @@ class Session:
         check(lib().iris_session_attention(self._h, layer), "iris_session_attention")
 
     def set_attention(self, mode: str) -> None:
-        """'auto' (one cluster launch where possible) or 'split' (three launches)."""
-        check(lib().iris_session_set_attention(self._h, {"auto": 0, "split": 1}[mode]), "iris_session_set_attention")
+        """'auto' (whole-GPU launch, else cluster, else split), 'split' (three
+        launches) or 'cluster' (the cluster launch where possible)."""
+        check(lib().iris_session_set_attention(self._h, {"auto": 0, "split": 1, "cluster": 2}[mode]),
+              "iris_session_set_attention")
 
     def set_attention_shape(self, cluster: int, hpc: int, ring: int) -> None:
         """Explicit one-launch decode attention shape (tuning)."""

@@ -101,14 +101,26 @@ def test_three_launch_decode_attention():
         assert_same(got, want)
 
 
-def test_long_context_spans_several_tiles_a_block():
-    """1100 positions: every block of a 16-block cluster streams several
-    32-position key and value tiles."""
+def test_cluster_decode_attention():
+    """The thread-block-cluster decode attention (the path for capacities the
+    whole-GPU launch does not hold), on both families."""
+    from iris_b200.shapes import parity_gemma, parity_mistral
+    for cfg, seed in ((parity_mistral(), 23), (parity_gemma(), 24)):
+        prompt = seeded_prompt(seed, 45, cfg.vocab)
+        _, _, _, got, want = run_both(cfg, seed, prompt, 7, attn="cluster")
+        assert_same(got, want)
+
+
+def test_long_context_attention():
+    """1100 positions: the whole-GPU launch holds tens of positions a block,
+    and every block of a cluster streams several 32-position key and value
+    tiles."""
     from iris_b200.shapes import parity_mistral
     cfg = parity_mistral()
     prompt = seeded_prompt(31, 1100, cfg.vocab)
-    _, _, _, got, want = run_both(cfg, 31, prompt, 4)
-    assert_same(got, want)
+    for attn in ("auto", "cluster"):
+        _, _, _, got, want = run_both(cfg, 31, prompt, 4, attn=attn)
+        assert_same(got, want)
 
 
 def test_long_prompt_crosses_device_ranges():
