@@ -28,10 +28,13 @@ namespace iris {
 //
 // Kernels on the inference path are launched with programmatic stream
 // serialization: kernel N+1 may be scheduled while kernel N finishes. Every
-// such kernel calls pdl_trigger() first (its successor may launch once all of
-// its blocks have started) and pdl_wait() before it reads anything an earlier
-// kernel wrote or writes anything an earlier kernel may still read; only reads
-// of immutable data (weights) may precede pdl_wait().
+// such kernel calls pdl_wait() before it reads anything its predecessor wrote
+// or writes anything an earlier kernel may still read, and pdl_trigger()
+// right after it (its successor may then launch). So when a kernel starts,
+// every kernel before its predecessor has completed: work placed before
+// pdl_wait() may read data written two or more kernels earlier (the decode
+// position, cached K/V rows of earlier positions) and immutable data
+// (weights).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -102,8 +102,8 @@ __device__ __forceinline__ void attn_scores_body(const AttnArgs& a, uint32_t p, 
 
 template <uint32_t PER, uint32_t HPC>
 __global__ void __launch_bounds__(kAttnThreads) attn_scores_kernel(AttnArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ unsigned long long best_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
   const uint32_t G = a.heads / a.kv_heads, h0 = blockIdx.x * HPC, g = h0 / G;
@@ -149,8 +149,8 @@ __device__ void block_global_best(const AttnArgs& a, uint32_t h0, uint32_t nact,
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ unsigned long long best_s[kMaxHpc];
   __shared__ unsigned long long sum_s[kMaxHpc];
   const uint32_t p = query_position(a), ws = window_start(p, a.window);
@@ -176,8 +176,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_exp_kernel(AttnArgs a) {
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_out_kernel(AttnArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ int32_t w_s[kMaxHpc * kAttnChunk];
   __shared__ unsigned long long best_s[kMaxHpc];
   __shared__ unsigned long long total_s[kMaxHpc];
@@ -361,8 +361,8 @@ __device__ __forceinline__ T head_lane_sum(T v) {
 
 template <uint32_t PER, uint32_t HPC>
 __global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   constexpr uint32_t D = PER * 8, NH = kCThreads / D;
@@ -570,8 +570,8 @@ __global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnA
 // three dependent steps of attention_softmax (ops.rs:233-261) meet through
 // global memory: first-maximum keys (atomicMax), sums of exp terms and of
 // weights, and the wrapping weighted value sums (atomicAdd) of the group,
-// with a bounded arrival barrier a step. After the last step every block
-// finishes its share of the group's outputs; the group's last block clears
+// with a bounded arrival barrier after the first two steps. The group's last
+// block to add its value sums finishes every output of the group and clears
 // the exchange words for the next launch. The blocks of a launch must be
 // resident together (the plan checks the occupancy); a barrier that waits
 // about a second records a fault instead of hanging.
@@ -584,32 +584,39 @@ __device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
   return v;
 }
 
-// Arrival barrier of one head group: returns once *bar reaches target.
+__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Arrival barrier of one head group: returns once *bar reaches target. The
+// block's earlier global atomics are published by the release arrival (after
+// the block barrier) and seen by the acquire loads of the other blocks.
 __device__ __forceinline__ void group_barrier(unsigned int* bar, unsigned int target, unsigned int* fault) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1u);
+    red_add_release(bar, 1u);
     if (ld_acquire_u32(bar) < target) {
       const uint64_t t0 = global_ns();
       for (uint32_t i = 1;; ++i) {
-        __nanosleep(100);
+        __nanosleep(32);
         if (ld_acquire_u32(bar) >= target) break;
-        if ((i & 63) == 0 && global_ns() - t0 > 1000000000ull) {
+        if ((i & 255) == 0 && global_ns() - t0 > 1000000000ull) {
           if (fault) atomicOr(fault, 1u);
           break;
         }
       }
     }
-    __threadfence();
   }
   __syncthreads();
 }
 
 template <uint32_t PER, uint32_t HPC>
 __global__ void __launch_bounds__(kGThreads) attn_decode_grid_kernel(AttnArgs a) {
-  pdl_trigger();
-  pdl_wait();
   constexpr uint32_t D = PER * 8, NH = kGThreads / D, kWarps = kGThreads / 32;
   const uint32_t span_a = a.gspan;                   // even
   extern __shared__ __align__(16) int32_t gsm[];
@@ -626,19 +633,30 @@ __global__ void __launch_bounds__(kGThreads) attn_decode_grid_kernel(AttnArgs a)
   const uint32_t span = (n + chunks - 1) / chunks;
   const uint32_t r0 = min(p + 1, ws + rank * span), r1 = min(p + 1, r0 + span), cnt = r1 - r0;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, quad = lane >> 3, ql = lane & 7;
-  unsigned int* bar = a.gbar + 2 * grp;
+  unsigned int* bar = a.gbar + grp;
 
-  // every key row, then every value row of the block's range
-  for (uint32_t c = tid; c < cnt * (D / 4); c += kGThreads) {
+  // Every key row, then every value row of the block's range, except the
+  // query's own position: those rows were written by earlier passes, so they
+  // stream while the q|k|v product that precedes this kernel finishes (the
+  // decode position was written two or more kernels earlier).
+  const uint32_t held = cnt - (cnt && r1 == p + 1 ? 1u : 0u);  // rows before position p
+  for (uint32_t c = tid; c < held * (D / 4); c += kGThreads) {
     const uint32_t r = c / (D / 4), j = c % (D / 4);
     cp_async16(ks + r * D + 4 * j, a.kcache + (size_t)(r0 + r) * a.kvd + g * D + 4 * j);
   }
   cp_async_commit();
-  for (uint32_t c = tid; c < cnt * (D / 4); c += kGThreads) {
+  for (uint32_t c = tid; c < held * (D / 4); c += kGThreads) {
     const uint32_t r = c / (D / 4), j = c % (D / 4);
     cp_async16(vs + r * D + 4 * j, a.vcache + (size_t)(r0 + r) * a.kvd + g * D + 4 * j);
   }
   cp_async_commit();
+  pdl_wait();
+  pdl_trigger();
+  if (held < cnt)  // position p: this pass's key and value rows
+    for (uint32_t j = tid; j < D / 4; j += kGThreads) {
+      *(int4*)(ks + held * D + 4 * j) = *(const int4*)(a.kcache + (size_t)p * a.kvd + g * D + 4 * j);
+      *(int4*)(vs + held * D + 4 * j) = *(const int4*)(a.vcache + (size_t)p * a.kvd + g * D + 4 * j);
+    }
   if (tid < HPC) {
     best_s[tid] = 0;
     sum_s[tid] = 0;
@@ -758,37 +776,33 @@ __global__ void __launch_bounds__(kGThreads) attn_decode_grid_kernel(AttnArgs a)
     for (uint32_t h = 0; h < HPC; ++h)
       if (acc[h]) atomicAdd((unsigned long long*)(a.acc + (size_t)(h0 + h) * D + dim), (unsigned long long)acc[h]);
   }
-  group_barrier(bar, 3 * chunks, a.fault);
-
-  // ---- 4. block `rank` finishes outputs [rank * share, (rank + 1) * share)
+  // ---- 4. the group's last block to add its sums finishes every output of
+  // the group and clears the exchange words for the next launch
+  __shared__ bool last_s;
+  __syncthreads();
+  if (tid == 0) last_s = atom_add_acq_rel(bar, 1u) == 3 * chunks - 1;
+  __syncthreads();
+  if (!last_s) return;
   if (tid < HPC) resid_s[tid] = sub_sat(kOneAct, (int32_t)__ldcg((const int*)(a.wsum + h0 + tid)));  // ops.rs:274-276
   __syncthreads();
-  const uint32_t share = (HPC * D + chunks - 1) / chunks, qd = a.heads * D;
-  for (uint32_t o = rank * share + tid; o < min(HPC * D, (rank + 1) * share); o += kGThreads) {
+  const uint32_t qd = a.heads * D;
+  for (uint32_t o = tid; o < HPC * D; o += kGThreads) {
     const uint32_t h = o / D, i = o % D, hh = h0 + h;
-    uint64_t s = (uint64_t)atomicExch((unsigned long long*)(a.acc + (size_t)hh * D + i), 0ull);
+    uint64_t* accp = (uint64_t*)(a.acc + (size_t)hh * D + i);
+    uint64_t s = (uint64_t)__ldcg((const unsigned long long*)accp);
+    *accp = 0;
     const uint32_t tmax = best_key_token(gbest_s[h]);
     s += (uint64_t)((int64_t)resid_s[h] * a.vcache[(size_t)tmax * a.kvd + g * D + i]);
     const int32_t v = requantize((int64_t)s);
     put_planes(a.ctx_planes, qd, hh * D + i, v);
     if (a.ctx) a.ctx[hh * D + i] = v;
   }
-  // the group's last block clears its exchange words for the next launch
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    if (atomicAdd(bar + 1, 1u) == chunks - 1) {
-      __threadfence();
-      for (uint32_t h = 0; h < HPC; ++h) {
-        a.gbest[h0 + h] = 0;
-        a.gsum[h0 + h] = 0;
-        a.wsum[h0 + h] = 0;
-      }
-      bar[0] = 0;
-      bar[1] = 0;
-      __threadfence();
-    }
+  if (tid < HPC) {
+    a.gbest[h0 + tid] = 0;
+    a.gsum[h0 + tid] = 0;
+    a.wsum[h0 + tid] = 0;
   }
+  if (tid == 0) bar[0] = 0;
 }
 
 size_t attention_grid_smem(uint32_t d, uint32_t hpc, uint32_t span) {
@@ -1020,8 +1034,8 @@ cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s) {
 // ---------------------------------------------------------------------------
 
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ unsigned long long best_s, total_s;
   __shared__ int32_t wsum_s;
@@ -1106,8 +1120,8 @@ cudaError_t prepare_layer_kernels() {
 __global__ void embed_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t cols,
                              uint32_t kc, uint32_t nslices, const uint32_t* ids, int32_t scale, int has_scale,
                              int32_t* out) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   uint32_t t = blockIdx.x, id = ids[t];
   for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
     int32_t m, e;
@@ -1126,8 +1140,8 @@ cudaError_t launch_embed(const Q8GpuMatrix* embed, const uint32_t* d_ids, uint32
 }
 
 __global__ void fill_u64_kernel(unsigned long long* p, uint32_t n) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) p[i] = 0;
 }
@@ -1138,8 +1152,8 @@ cudaError_t launch_fill_u64(unsigned long long* p, uint32_t n, cudaStream_t s) {
 
 __global__ void decode_finish_kernel(unsigned long long* best, uint32_t* d_token, uint32_t* d_pos,
                                      uint32_t* d_step, uint32_t* history, uint32_t cap) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   uint32_t tok = best_key_token(*best);  // first maximum (generation.rs:25-58)
   *d_token = tok;
   *best = 0;
@@ -1184,8 +1198,8 @@ __device__ void block_rms_norm(int32_t* v, uint32_t n, const int32_t* w, int64_t
 }
 
 __global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) int32_t hv[];  // [d]
   __shared__ uint64_t red[32];
   const uint32_t tok = blockIdx.x, which = blockIdx.y, d = a.d;
@@ -1227,8 +1241,8 @@ cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cud
 __global__ void gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
                                        const int32_t* w_pre_ffw, int64_t eps, uint32_t H,
                                        uint8_t* planes) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) int32_t row[];  // [H]
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x;
@@ -1255,8 +1269,8 @@ cudaError_t launch_gemma_post_attn(const int32_t* o, int32_t* x, const int32_t* 
 
 __global__ void gemma_norm_add_kernel(const int32_t* v_in, const int32_t* add, const int32_t* w,
                                       int64_t eps, int32_t scalar, uint32_t H, int32_t* out) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) int32_t row[];
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x;
@@ -1290,8 +1304,8 @@ cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const in
 __global__ void dense_kernel(const int32_t* __restrict__ w, uint32_t rows, uint32_t cols,
                              const int32_t* __restrict__ in, uint32_t in_stride, uint32_t tokens,
                              int32_t* out, uint32_t out_stride, const int32_t* gate, uint32_t gate_stride) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   const uint32_t warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= rows * tokens) return;
   const uint32_t t = warp / rows, r = warp % rows;
@@ -1321,8 +1335,8 @@ __global__ void ple_prepare_kernel(const int32_t* projected, const int8_t* eq, c
                                    uint32_t ekc, uint32_t enslices, const uint32_t* ids, const int32_t* ple_norm,
                                    int64_t eps, int32_t projection_scalar, int32_t embedding_scale,
                                    int32_t input_scale, uint32_t L, uint32_t P, int32_t* out) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) int32_t row[];  // [P]
   __shared__ uint64_t red[32];
   const uint32_t t = blockIdx.x, l = blockIdx.y, id = ids[t];

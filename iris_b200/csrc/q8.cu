@@ -310,8 +310,8 @@ __device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __re
 
 __global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
                               int64_t eps, uint32_t K, uint8_t* planes) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
   uint32_t t = blockIdx.x;
@@ -587,11 +587,11 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
 
   // Weights never change: the first stages stream while the previous kernel
   // of the stream finishes; the activations are read only after pdl_wait().
-  pdl_trigger();
   const uint32_t first = nitems < p.stages ? nitems : p.stages;
   if (producer && lane == 0)
     for (uint32_t item = 0; item < first; ++item) issue(item, item);
   pdl_wait();
+  pdl_trigger();
 
   // Activation planes; `wide` when some value needs the fourth plane.
   bool wide;
@@ -761,8 +761,8 @@ constexpr int kTileN = 64, kTileM = 32, kWPitch = 48;
 
 template <int EPI>
 __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) uint8_t sw[kTileN * kWPitch];
   __shared__ uint16_t ssc[kTileN];
   __shared__ __align__(16) uint8_t sp[kTileM * 4 * 32];
