@@ -841,15 +841,19 @@ void attention_grid_plan(uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     return;
   const uint32_t groups = heads / h;
-  const uint32_t c = (uint32_t)sms / groups;
-  if (c < 2) return;
-  const uint32_t sp = (((cap + c - 1) / c) + 1) & ~1u;
-  const size_t smem = attention_grid_smem(d, h, sp);
-  if (smem > kClusterSmemMax) return;
-  // every block of the launch must be resident at once
-  if ((uint64_t)grid_blocks_per_sm(d, h, smem) * (uint32_t)sms < (uint64_t)groups * c) return;
-  *chunks = c;
-  *span = sp;
+  // two blocks a multiprocessor where they fit (shorter serial work a block),
+  // else one; every block of the launch must be resident at once
+  for (uint32_t per_sm = 2; per_sm >= 1; --per_sm) {
+    const uint32_t c = per_sm * (uint32_t)sms / groups;
+    if (c < 2) continue;
+    const uint32_t sp = (((cap + c - 1) / c) + 1) & ~1u;
+    const size_t smem = attention_grid_smem(d, h, sp);
+    if (smem > kClusterSmemMax) continue;
+    if ((uint64_t)grid_blocks_per_sm(d, h, smem) * (uint32_t)sms < (uint64_t)groups * c) continue;
+    *chunks = c;
+    *span = sp;
+    return;
+  }
 }
 
 cudaError_t launch_attention_grid(const AttnArgs& a, cudaStream_t s) {
