@@ -420,6 +420,7 @@ struct GemvPlan {
   uint32_t items;            // tiles of the matrix: groups * nslices
   uint32_t groups_per_block; // whole-group ranges (split == 0)
   uint32_t split;            // even item ranges through the split scratch
+  int32_t e_fast;            // largest scale exponent of the 64-bit accumulator (-1: none)
   uint32_t smem;
   uint32_t grid;
 };
@@ -436,6 +437,12 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, bool split, Gemv
   p->smem = p->planes_bytes + p->stages * p->stage_bytes;
   const uint32_t groups = (rows + kQ8TileRows - 1) / kQ8TileRows;
   p->items = groups * (K / kc);
+  // a lane adds one term a slice to each row: S terms below 2^(46.1 + e)
+  // stay below 2^62 for e <= 15 - ceil(log2 S)
+  const uint32_t S = K / kc;
+  uint32_t lg = 0;
+  while ((1u << lg) < S) ++lg;
+  p->e_fast = 15 - (int32_t)lg;
   p->split = split ? 1 : 0;
   if (split) {
     p->grid = (uint32_t)sms < p->items ? (uint32_t)sms : p->items;
@@ -472,11 +479,18 @@ __device__ __forceinline__ void gemv_take_rows(const uint8_t* __restrict__ W, co
   }
 }
 
+// The exact block sums of one lane's block for its two rows, times the
+// scales, into the row accumulators. Three planes (|a| < 2^23): one dp4a
+// chain a plane over the whole block (|s0|, |s1| < 2^20, |s2| < 2^19), then
+// p = (s0 + 256 s1) m + 2^16 (s2 m) with |p| < 2^46.1; a term p 2^e with
+// e <= e_fast goes to a 64-bit accumulator (the plan bounds the terms a lane
+// adds for a row so that their sum stays below 2^62), any other to the
+// 128-bit one. Four planes: the 128-bit path throughout.
 template <bool kThree>
 __device__ __forceinline__ void gemv_rows_product(const RowBlocks& rb, const uint4* __restrict__ P0,
                                                   const uint4* __restrict__ P1, const uint4* __restrict__ P2,
                                                   const uint4* __restrict__ P3, uint32_t cbase, uint32_t b,
-                                                  uint32_t lane, Acc128* acc) {
+                                                  uint32_t lane, int32_t e_fast, Acc128* acc, int64_t* fast) {
   const uint32_t swap = (lane >> 2) & 1;
   const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
   const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
@@ -490,9 +504,23 @@ __device__ __forceinline__ void gemv_rows_product(const RowBlocks& rb, const uin
   for (int r = 0; r < kTmaRowsPerWarp; ++r) {
     int32_t m, e;
     q8_scale_parts(rb.sc[r], &m, &e);  // finite: checked at upload (padding rows: 0)
-    const int64_t bs = kThree ? q8_partial16_three(rb.wa[r], pa0, pa1, pa2) + q8_partial16_three(rb.wb[r], pb0, pb1, pb2)
-                              : q8_partial16(rb.wa[r], pa0, pa1, pa2, pa3) + q8_partial16(rb.wb[r], pb0, pb1, pb2, pb3);
-    acc128_add_shifted(acc[r], bs * m, e);
+    if (kThree) {
+      const uint4 wa = rb.wa[r], wb = rb.wb[r];
+      int s0 = dp4a_su(wa.x, pa0.x, 0), s1 = dp4a_su(wa.x, pa1.x, 0), s2 = dp4a_ss(wa.x, pa2.x, 0);
+      s0 = dp4a_su(wa.y, pa0.y, s0), s1 = dp4a_su(wa.y, pa1.y, s1), s2 = dp4a_ss(wa.y, pa2.y, s2);
+      s0 = dp4a_su(wa.z, pa0.z, s0), s1 = dp4a_su(wa.z, pa1.z, s1), s2 = dp4a_ss(wa.z, pa2.z, s2);
+      s0 = dp4a_su(wa.w, pa0.w, s0), s1 = dp4a_su(wa.w, pa1.w, s1), s2 = dp4a_ss(wa.w, pa2.w, s2);
+      s0 = dp4a_su(wb.x, pb0.x, s0), s1 = dp4a_su(wb.x, pb1.x, s1), s2 = dp4a_ss(wb.x, pb2.x, s2);
+      s0 = dp4a_su(wb.y, pb0.y, s0), s1 = dp4a_su(wb.y, pb1.y, s1), s2 = dp4a_ss(wb.y, pb2.y, s2);
+      s0 = dp4a_su(wb.z, pb0.z, s0), s1 = dp4a_su(wb.z, pb1.z, s1), s2 = dp4a_ss(wb.z, pb2.z, s2);
+      s0 = dp4a_su(wb.w, pb0.w, s0), s1 = dp4a_su(wb.w, pb1.w, s1), s2 = dp4a_ss(wb.w, pb2.w, s2);
+      const int64_t p = (int64_t)(s0 + s1 * 256) * m + ((int64_t)(s2 * m) << 16);
+      if (e <= e_fast) fast[r] += (int64_t)((uint64_t)p << e);
+      else acc128_add_shifted(acc[r], p, e);
+    } else {
+      const int64_t bs = q8_partial16(rb.wa[r], pa0, pa1, pa2, pa3) + q8_partial16(rb.wb[r], pb0, pb1, pb2, pb3);
+      acc128_add_shifted(acc[r], bs * m, e);
+    }
   }
 }
 
@@ -692,8 +720,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   const uint32_t lr0 = kTmaRowsPerWarp * pair, blocks = kc / 32, mid = kHalves == 2 ? (blocks + 1) / 2 : blocks;
   const uint32_t b0 = half ? mid : 0, b1 = half ? blocks : mid;
   Acc128 acc[kTmaRowsPerWarp];
+  int64_t fast[kTmaRowsPerWarp];
 #pragma unroll
-  for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
+  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+    acc[r] = Acc128{0, 0};
+    fast[r] = 0;
+  }
   uint32_t j = 0;        // tile groups finished
   bool stalled = false;  // after a given-up wait: keep pace with the barriers, skip the waits
   // stage, its fill parity and the slice of the current item, kept without divisions
@@ -712,13 +744,17 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
       phase ^= 1;
     }
     if (b < b1) {
-      if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, acc);
-      else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, acc);
+      if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, p.e_fast, acc, fast);
+      else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, p.e_fast, acc, fast);
     }
     if (++sl == S) sl = 0;
     if (sl == 0 || item + 1 == nitems) {
 #pragma unroll
-      for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = warp_sum_acc128(acc[r]);
+      for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+        acc128_add(acc[r], (uint64_t)fast[r], fast[r] >> 63);
+        acc[r] = warp_sum_acc128(acc[r]);
+        fast[r] = 0;
+      }
       const uint32_t slot = j % kTmaSlots;
       if (j >= kTmaSlots && !stalled && !mbar_wait_bounded(&slot_empty[slot], (j / kTmaSlots - 1) & 1, &g_fault))
         stalled = true;
