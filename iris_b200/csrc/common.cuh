@@ -138,6 +138,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
   }
 }
+// 16-byte asynchronous global -> shared copy (cp.async) and its commit.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
 // L2 policy for data read once per pass (weights): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;
@@ -152,6 +158,12 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
       ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
+}
+
+// acc += a * b, the 32 x 32 -> 64-bit product added with 64-bit wraparound
+// (one multiply-add).
+__device__ __forceinline__ void mac_wide(int64_t& acc, int32_t a, int32_t b) {
+  asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
 }
 
 // Sixteen weights (one uint4) against the four planes of the same sixteen

@@ -295,10 +295,6 @@ constexpr uint32_t kTileP = 32;       // positions a tile (= 8 warps x 4 positio
 constexpr uint32_t kMaxRing = 12;     // tile buffers at most
 constexpr size_t kClusterSmemMax = 200 * 1024;
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Waits until at most n of this thread's committed groups are pending.
 __device__ __forceinline__ void cp_async_wait_pending(uint32_t n) {
   switch (n) {
@@ -315,12 +311,6 @@ __device__ __forceinline__ void cp_async_wait_pending(uint32_t n) {
     case 10: asm volatile("cp.async.wait_group 10;" ::: "memory"); break;
     default: asm volatile("cp.async.wait_group 11;" ::: "memory"); break;
   }
-}
-
-// acc += a * b, the 32 x 32 -> 64-bit product added with 64-bit wraparound
-// (one multiply-add).
-__device__ __forceinline__ void mac_wide(int64_t& acc, int32_t a, int32_t b) {
-  asm("mad.wide.s32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
 }
 
 // The 16-byte pieces this thread copies of every [kTileP][D] tile: piece c =

@@ -879,6 +879,202 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Tiled GEMM on the tensor cores (mma.sync, int8): 128 rows x 16 tokens a block
+// ---------------------------------------------------------------------------
+//
+// Eight warps, each 16 rows x 16 tokens (two 8-token tiles). A stage holds
+// four 32-value blocks (128 columns) of the block's rows (weights and scale
+// bits) and of its tokens' four activation planes, staged through a
+// three-stage cp.async ring (16-byte pieces, XOR-swizzled by row so that the
+// ldmatrix reads are free of bank conflicts). For every 32-value block and
+// 8-token tile a warp runs four m16n8k32 MMAs (s8 weights against the u8
+// planes 0-2 and the s8 plane 3), whose exact int32 results are the block's
+// plane sums s0..s3 for each (row, token). The block sum is
+// (s0 + 256 s1) + 2^16 (s2 + 256 s3); times the block's Q.24 scale m 2^e it
+// is accumulated exactly:
+//   - e <= 12: m 2^e fits 23 bits, so (s0 + 256 s1) m 2^e and
+//     (s2 + 256 s3) m 2^e are 32 x 32 -> 64-bit multiply-adds into two int64
+//     accumulators (weights 1 and 2^16) that cannot overflow for up to 2048
+//     blocks (|term| < 2^51);
+//   - larger exponents: the 64-bit product shifted into a 128-bit
+//     accumulator.
+// The three are added in 128 bits at the end and rounded once (q8.rs:69-71).
+
+constexpr int kMmaRows = 128, kMmaTok = 16, kMmaKB = 4, kMmaStages = 3, kMmaThreads = 256;
+constexpr int kMmaNT = kMmaTok / 8;  // 8-token tiles a warp
+constexpr uint32_t kMmaAStage = kMmaRows * kMmaKB * 32;     // weight bytes a stage
+constexpr uint32_t kMmaSStage = kMmaRows * kMmaKB * 2;      // scale bytes a stage
+constexpr uint32_t kMmaBStage = kMmaTok * 4 * kMmaKB * 32;  // plane bytes a stage
+constexpr uint32_t kMmaStageBytes = kMmaAStage + kMmaSStage + kMmaBStage;
+constexpr uint32_t kMmaSmem = kMmaStages * kMmaStageBytes;
+constexpr int32_t kMmaEFast = 12;
+
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8_zfill(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4(uint32_t* r, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_addr(p)));
+}
+// D = A (16x32 s8, rows) x B (32x8, columns), zero accumulator; B u8 or s8.
+template <bool kSignedB>
+__device__ __forceinline__ void mma_i8(int32_t* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  if (kSignedB)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+// One stage: weights, scale bits and planes of blocks [kb0, kb0 + 4).
+__device__ __forceinline__ void mma_load_stage(const ProductArgs& a, uint8_t* st, uint32_t n0, uint32_t m0,
+                                               uint32_t kb0, uint32_t nblk) {
+  uint8_t* As = st;
+  uint8_t* Ss = st + kMmaAStage;
+  uint8_t* Bs = st + kMmaAStage + kMmaSStage;
+  const uint32_t tid = threadIdx.x, K = a.cols;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // 128 rows x 8 pieces
+    const uint32_t id = tid + i * kMmaThreads, row = id >> 3, c = id & 7, kb = kb0 + (c >> 1);
+    const bool ok = n0 + row < a.rows && kb < nblk;
+    const int8_t* src = ok ? a.q + q8_value_offset(a.kc, a.nslices, n0 + row, kb * 32) + (c & 1) * 16 : a.q;
+    cp_async16_zfill(As + row * 128 + ((c ^ (row & 7)) << 4), src, ok ? 16u : 0u);
+  }
+  if (tid < kMmaRows) {  // the stage's four blocks are consecutive in one slice
+    const uint32_t row = tid;
+    const bool ok = n0 + row < a.rows && kb0 < nblk;
+    const uint16_t* src = ok ? a.s + q8_scale_offset(a.kc, a.nslices, n0 + row, kb0) : a.s;
+    cp_async8_zfill(Ss + row * 8, src, ok ? 8u : 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < kMmaTok * 32 / kMmaThreads; ++i) {  // tokens x 4 planes x 8 pieces
+    const uint32_t id = tid + i * kMmaThreads, tok = id >> 5, pl = (id >> 3) & 3, c = id & 7;
+    const bool ok = m0 + tok < a.tokens && kb0 + (c >> 1) < nblk;
+    const uint8_t* src =
+        ok ? a.planes + (size_t)(m0 + tok) * 4 * K + (size_t)pl * K + (size_t)kb0 * 32 + c * 16 : a.planes;
+    cp_async16_zfill(Bs + (tok * 4 + pl) * 128 + ((c ^ (tok & 7)) << 4), src, ok ? 16u : 0u);
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs a) {
+  extern __shared__ __align__(128) uint8_t mma_smem[];
+  // token tiles vary fastest, so the blocks sharing a weight tile run together (L2 reuse)
+  const uint32_t n0 = blockIdx.y * kMmaRows, m0 = blockIdx.x * kMmaTok, nblk = a.cols / 32;
+  const uint32_t nst = (nblk + kMmaKB - 1) / kMmaKB;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  pdl_wait();
+  pdl_trigger();
+
+  int64_t alo[kMmaNT][4], ahi[kMmaNT][4];  // [8-token tile][d index]: (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1)
+  Acc128 slow[kMmaNT][4];
+#pragma unroll
+  for (int nt = 0; nt < kMmaNT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      alo[nt][i] = 0;
+      ahi[nt][i] = 0;
+      slow[nt][i] = Acc128{0, 0};
+    }
+
+#pragma unroll
+  for (int s = 0; s < kMmaStages - 1; ++s) {
+    if ((uint32_t)s < nst) mma_load_stage(a, mma_smem + s * kMmaStageBytes, n0, m0, s * kMmaKB, nblk);
+    cp_async_commit();
+  }
+  for (uint32_t st = 0; st < nst; ++st) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kMmaStages - 2) : "memory");
+    __syncthreads();  // stage st has landed for every thread; stage st - 1 is consumed
+    {
+      const uint32_t nx = st + kMmaStages - 1;
+      if (nx < nst) mma_load_stage(a, mma_smem + (nx % kMmaStages) * kMmaStageBytes, n0, m0, nx * kMmaKB, nblk);
+      cp_async_commit();
+    }
+    const uint8_t* As = mma_smem + (st % kMmaStages) * kMmaStageBytes;
+    const uint16_t* Ss = (const uint16_t*)(As + kMmaAStage);
+    const uint8_t* Bs = As + kMmaAStage + kMmaSStage;
+#pragma unroll
+    for (int kb = 0; kb < kMmaKB; ++kb) {
+      uint32_t af[4];
+      {
+        const uint32_t row = 16 * warp + ((lane >> 3) & 1) * 8 + (lane & 7), c = 2 * kb + (lane >> 4);
+        ldmatrix_x4(af, As + row * 128 + ((c ^ (row & 7)) << 4));
+      }
+      int32_t m[2], e[2], mp[2];
+      bool fast[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const uint16_t bits = Ss[(16 * warp + g + 8 * r) * 4 + kb];
+        q8_scale_parts(bits, &m[r], &e[r]);  // finite: checked at upload (padding: 0)
+        fast[r] = e[r] <= kMmaEFast;
+        mp[r] = fast[r] ? m[r] * (1 << e[r]) : 0;
+      }
+#pragma unroll
+      for (int nt = 0; nt < kMmaNT; ++nt) {
+        uint32_t b01[4], b23[4];
+        {
+          const uint32_t j = lane >> 3, tok = 8 * nt + (lane & 7), c = 2 * kb + (j & 1);
+          const uint32_t pl = j >> 1;
+          ldmatrix_x4(b01, Bs + (tok * 4 + pl) * 128 + ((c ^ (tok & 7)) << 4));
+          ldmatrix_x4(b23, Bs + (tok * 4 + 2 + pl) * 128 + ((c ^ (tok & 7)) << 4));
+        }
+        int32_t d0[4], d1[4], d2[4], d3[4];
+        mma_i8<false>(d0, af, b01[0], b01[1]);
+        mma_i8<false>(d1, af, b01[2], b01[3]);
+        mma_i8<false>(d2, af, b23[0], b23[1]);
+        mma_i8<true>(d3, af, b23[2], b23[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = i >> 1;
+          const int32_t lo = d0[i] + d1[i] * 256, hi = d2[i] + d3[i] * 256;
+          if (fast[r]) {
+            mac_wide(alo[nt][i], lo, mp[r]);
+            mac_wide(ahi[nt][i], hi, mp[r]);
+          } else {
+            const int64_t p = (int64_t)lo * m[r] + (int64_t)((uint64_t)((int64_t)hi * m[r]) << 16);
+            acc128_add_shifted(slow[nt][i], p, e[r]);
+          }
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int nt = 0; nt < kMmaNT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      Acc128 tot = slow[nt][i];
+      acc128_add(tot, (uint64_t)alo[nt][i], alo[nt][i] >> 63);
+      acc128_add(tot, (uint64_t)ahi[nt][i] << 16, ahi[nt][i] >> 48);
+      int32_t v = acc128_round_q24(tot);
+      const uint32_t row = n0 + 16 * warp + g + 8 * (i >> 1), tok = m0 + 8 * nt + 2 * t + (i & 1);
+      if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+        const int32_t partner = __shfl_xor_sync(0xffffffffu, v, 4);  // row ^ 1, same token
+        if ((g & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
+      } else if (EPI == EPI_LOGITS) {
+        if (tok < a.tokens && row < a.rows) {
+          if (a.softcap > 0) v = softcap_act(v, a.softcap);
+          if (a.out) a.out[(size_t)tok * a.out_stride + row] = v;
+          atomicMax(a.best + tok, best_key(v, row));
+        }
+      } else if (tok < a.tokens && row < a.rows) {
+        epi_single<EPI>(a, tok, row, v);
+      }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
 
@@ -920,9 +1116,23 @@ cudaError_t prepare_gemv_in() {
   return e;
 }
 
+template <int EPI>
+cudaError_t prepare_mma_one() {
+  return cudaFuncSetAttribute(q8_gemm_mma_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMmaSmem);
+}
+
 cudaError_t prepare_product_kernels() {
   g_sms = 0;
   device_sms();
+  {
+    cudaError_t e = prepare_mma_one<EPI_STORE>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_RESID>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_QKV_ROPE>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_SILU_MUL>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_GELU_MUL>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_LOGITS>();
+    if (e != cudaSuccess) return e;
+  }
   cudaError_t e = prepare_gemv_in<IN_PLANES>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_NORM>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_RAW>();
@@ -931,6 +1141,12 @@ cudaError_t prepare_product_kernels() {
 
 template <int EPI>
 cudaError_t launch_gemm(const ProductArgs& a, cudaStream_t stream) {
+  // the tensor-core GEMM: whole 4-block stages inside each slice, and at most
+  // 2048 blocks a row for its 64-bit accumulators
+  if (a.cols % (32 * kMmaKB) == 0 && (a.kc / 32) % kMmaKB == 0 && a.cols / 32 <= 2048) {
+    dim3 grid((a.tokens + kMmaTok - 1) / kMmaTok, (a.rows + kMmaRows - 1) / kMmaRows);
+    return launch_k(q8_gemm_mma_kernel<EPI>, grid, dim3(kMmaThreads), kMmaSmem, stream, a);
+  }
   dim3 grid((a.rows + kTileN - 1) / kTileN, (a.tokens + kTileM - 1) / kTileM);
   return launch_k(q8_gemm_kernel<EPI>, grid, dim3(256), 0, stream, a);
 }
