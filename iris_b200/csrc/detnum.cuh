@@ -177,6 +177,15 @@ IRIS_HD bool q8_scale_parts(uint16_t bits, int32_t* m, int32_t* e) {
   return true;
 }
 
+// q8_scale_parts for bits already known to be finite (checked at upload):
+// branch-free.
+IRIS_HD void q8_scale_parts_finite(uint16_t bits, int32_t* m, int32_t* e) {
+  const uint32_t ex = (bits >> 10) & 0x1f, man = bits & 0x3ff;
+  const int32_t mag = (int32_t)(man | (ex ? 0x400u : 0u));
+  *e = ex ? (int32_t)ex - 1 : 0;
+  *m = (bits & 0x8000) ? -mag : mag;
+}
+
 // 128-bit two's-complement accumulator of Q8 partial products.
 struct Acc128 {
   uint64_t lo;

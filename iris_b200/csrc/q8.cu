@@ -906,7 +906,7 @@ constexpr uint32_t kMmaAStage = kMmaRows * kMmaKB * 32;     // weight bytes a st
 constexpr uint32_t kMmaSStage = kMmaRows * kMmaKB * 2;      // scale bytes a stage
 constexpr uint32_t kMmaBStage = kMmaTok * 4 * kMmaKB * 32;  // plane bytes a stage
 constexpr uint32_t kMmaStageBytes = kMmaAStage + kMmaSStage + kMmaBStage;
-constexpr uint32_t kMmaSmem = kMmaStages * kMmaStageBytes;
+constexpr uint32_t kMmaSmem = kMmaStages * kMmaStageBytes + kMmaRows * kMmaTok * sizeof(Acc128);
 constexpr int32_t kMmaEFast = 12;
 
 __device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t bytes) {
@@ -937,33 +937,57 @@ __device__ __forceinline__ void mma_i8(int32_t* d, const uint32_t* a, uint32_t b
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-// One stage: weights, scale bits and planes of blocks [kb0, kb0 + 4).
-__device__ __forceinline__ void mma_load_stage(const ProductArgs& a, uint8_t* st, uint32_t n0, uint32_t m0,
-                                               uint32_t kb0, uint32_t nblk) {
+// The global offsets a thread copies from, split into a part fixed for the
+// block (its rows and tokens) and a part that moves with the stage, so that a
+// stage costs no divisions. A stage's four blocks lie in one slice.
+struct MmaCopier {
+  uint32_t a_row[4];  // value offset of piece i's row in slice 0, or ~0u outside the matrix
+  uint32_t s_row;     // scale offset of the thread's row (threads < kMmaRows), or ~0u
+  uint32_t b_tok[kMmaTok * 32 / kMmaThreads];  // plane offset of piece i's token at column 0, or ~0u
+};
+
+__device__ __forceinline__ void mma_copier_init(const ProductArgs& a, uint32_t n0, uint32_t m0, MmaCopier& cp) {
+  const uint32_t tid = threadIdx.x, bps = a.kc / 32;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t row = n0 + ((tid + i * kMmaThreads) >> 3);
+    cp.a_row[i] = row < a.rows ? (uint32_t)q8_value_offset(a.kc, a.nslices, row, 0) : ~0u;
+  }
+  cp.s_row = tid < kMmaRows && n0 + tid < a.rows ? (uint32_t)q8_scale_offset(a.kc, a.nslices, n0 + tid, 0) : ~0u;
+  (void)bps;
+#pragma unroll
+  for (int i = 0; i < kMmaTok * 32 / kMmaThreads; ++i) {
+    const uint32_t id = tid + i * kMmaThreads, tok = m0 + (id >> 5), pl = (id >> 3) & 3;
+    cp.b_tok[i] = tok < a.tokens ? tok * 4 * a.cols + pl * a.cols : ~0u;
+  }
+}
+
+// One stage: weights, scale bits and planes of blocks [kb0, kb0 + 4) of slice
+// sl (block bi = kb0 - sl * kc / 32 within it).
+__device__ __forceinline__ void mma_load_stage(const ProductArgs& a, const MmaCopier& cp, uint8_t* st, uint32_t kb0,
+                                               uint32_t sl, uint32_t bi) {
   uint8_t* As = st;
   uint8_t* Ss = st + kMmaAStage;
   uint8_t* Bs = st + kMmaAStage + kMmaSStage;
-  const uint32_t tid = threadIdx.x, K = a.cols;
+  const uint32_t tid = threadIdx.x, c = tid & 7;
+  const uint32_t a_stage = sl * kQ8TileRows * a.kc + bi * 32 + (c >> 1) * 32 + (c & 1) * 16;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {  // 128 rows x 8 pieces
-    const uint32_t id = tid + i * kMmaThreads, row = id >> 3, c = id & 7, kb = kb0 + (c >> 1);
-    const bool ok = n0 + row < a.rows && kb < nblk;
-    const int8_t* src = ok ? a.q + q8_value_offset(a.kc, a.nslices, n0 + row, kb * 32) + (c & 1) * 16 : a.q;
-    cp_async16_zfill(As + row * 128 + ((c ^ (row & 7)) << 4), src, ok ? 16u : 0u);
+  for (int i = 0; i < 4; ++i) {  // 128 rows x 8 pieces: row (tid >> 3) + 32 i, piece c
+    const uint32_t row = (tid >> 3) + 32 * i;
+    const bool ok = cp.a_row[i] != ~0u;
+    cp_async16_zfill(As + row * 128 + ((c ^ (row & 7)) << 4), ok ? a.q + cp.a_row[i] + a_stage : a.q, ok ? 16u : 0u);
   }
-  if (tid < kMmaRows) {  // the stage's four blocks are consecutive in one slice
-    const uint32_t row = tid;
-    const bool ok = n0 + row < a.rows && kb0 < nblk;
-    const uint16_t* src = ok ? a.s + q8_scale_offset(a.kc, a.nslices, n0 + row, kb0) : a.s;
-    cp_async8_zfill(Ss + row * 8, src, ok ? 8u : 0u);
+  if (tid < kMmaRows) {
+    const bool ok = cp.s_row != ~0u;
+    const uint16_t* src = ok ? a.s + cp.s_row + sl * kQ8TileRows * (a.kc / 32) + bi : a.s;
+    cp_async8_zfill(Ss + tid * 8, src, ok ? 8u : 0u);
   }
 #pragma unroll
   for (int i = 0; i < kMmaTok * 32 / kMmaThreads; ++i) {  // tokens x 4 planes x 8 pieces
-    const uint32_t id = tid + i * kMmaThreads, tok = id >> 5, pl = (id >> 3) & 3, c = id & 7;
-    const bool ok = m0 + tok < a.tokens && kb0 + (c >> 1) < nblk;
-    const uint8_t* src =
-        ok ? a.planes + (size_t)(m0 + tok) * 4 * K + (size_t)pl * K + (size_t)kb0 * 32 + c * 16 : a.planes;
-    cp_async16_zfill(Bs + (tok * 4 + pl) * 128 + ((c ^ (tok & 7)) << 4), src, ok ? 16u : 0u);
+    const uint32_t id = tid + i * kMmaThreads, tok = id >> 5, pl = (id >> 3) & 3;
+    const bool ok = cp.b_tok[i] != ~0u;
+    cp_async16_zfill(Bs + (tok * 4 + pl) * 128 + ((c ^ (tok & 7)) << 4),
+                     ok ? a.planes + cp.b_tok[i] + kb0 * 32 + c * 16 : a.planes, ok ? 16u : 0u);
   }
 }
 
@@ -978,19 +1002,35 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
   pdl_trigger();
 
   int64_t alo[kMmaNT][4], ahi[kMmaNT][4];  // [8-token tile][d index]: (g, 2t) (g, 2t+1) (g+8, 2t) (g+8, 2t+1)
-  Acc128 slow[kMmaNT][4];
 #pragma unroll
   for (int nt = 0; nt < kMmaNT; ++nt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       alo[nt][i] = 0;
       ahi[nt][i] = 0;
-      slow[nt][i] = Acc128{0, 0};
     }
+  // 128-bit accumulators of the rare blocks with a scale exponent above
+  // kMmaEFast: [row][token] of the block tile, each owned by one thread
+  Acc128* slow_s = (Acc128*)(mma_smem + kMmaStages * kMmaStageBytes);
+  for (uint32_t i = tid; i < kMmaRows * kMmaTok; i += kMmaThreads) slow_s[i] = Acc128{0, 0};
+  bool any_slow_seen = false;
 
+  MmaCopier cp;
+  mma_copier_init(a, n0, m0, cp);
+  const uint32_t bps = a.kc / 32;
+  uint32_t ld_kb = 0, ld_sl = 0, ld_bi = 0;  // next stage to load: first block, its slice and place there
+  auto load_next = [&](uint32_t buf) {
+    mma_load_stage(a, cp, mma_smem + buf * kMmaStageBytes, ld_kb, ld_sl, ld_bi);
+    ld_kb += kMmaKB;
+    ld_bi += kMmaKB;
+    if (ld_bi == bps) {
+      ld_bi = 0;
+      ++ld_sl;
+    }
+  };
 #pragma unroll
   for (int s = 0; s < kMmaStages - 1; ++s) {
-    if ((uint32_t)s < nst) mma_load_stage(a, mma_smem + s * kMmaStageBytes, n0, m0, s * kMmaKB, nblk);
+    if ((uint32_t)s < nst) load_next(s);
     cp_async_commit();
   }
   for (uint32_t st = 0; st < nst; ++st) {
@@ -998,7 +1038,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
     __syncthreads();  // stage st has landed for every thread; stage st - 1 is consumed
     {
       const uint32_t nx = st + kMmaStages - 1;
-      if (nx < nst) mma_load_stage(a, mma_smem + (nx % kMmaStages) * kMmaStageBytes, n0, m0, nx * kMmaKB, nblk);
+      if (nx < nst) load_next(nx % kMmaStages);
       cp_async_commit();
     }
     const uint8_t* As = mma_smem + (st % kMmaStages) * kMmaStageBytes;
@@ -1016,10 +1056,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const uint16_t bits = Ss[(16 * warp + g + 8 * r) * 4 + kb];
-        q8_scale_parts(bits, &m[r], &e[r]);  // finite: checked at upload (padding: 0)
+        q8_scale_parts_finite(bits, &m[r], &e[r]);  // checked at upload (padding: 0)
         fast[r] = e[r] <= kMmaEFast;
-        mp[r] = fast[r] ? m[r] * (1 << e[r]) : 0;
+        mp[r] = fast[r] ? m[r] * (1 << e[r]) : 0;  // 0: the block goes the 128-bit way
       }
+      const bool any_slow = __any_sync(0xffffffffu, !fast[0] || !fast[1]);
 #pragma unroll
       for (int nt = 0; nt < kMmaNT; ++nt) {
         uint32_t b01[4], b23[4];
@@ -1036,14 +1077,21 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
         mma_i8<true>(d3, af, b23[2], b23[3]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int r = i >> 1;
           const int32_t lo = d0[i] + d1[i] * 256, hi = d2[i] + d3[i] * 256;
-          if (fast[r]) {
-            mac_wide(alo[nt][i], lo, mp[r]);
-            mac_wide(ahi[nt][i], hi, mp[r]);
-          } else {
-            const int64_t p = (int64_t)lo * m[r] + (int64_t)((uint64_t)((int64_t)hi * m[r]) << 16);
-            acc128_add_shifted(slow[nt][i], p, e[r]);
+          mac_wide(alo[nt][i], lo, mp[i >> 1]);
+          mac_wide(ahi[nt][i], hi, mp[i >> 1]);
+        }
+        if (any_slow) {  // rare: a scale exponent above kMmaEFast somewhere in the warp
+          any_slow_seen = true;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int r = i >> 1;
+            if (!fast[r]) {
+              const int32_t lo = d0[i] + d1[i] * 256, hi = d2[i] + d3[i] * 256;
+              const int64_t p = (int64_t)lo * m[r] + (int64_t)((uint64_t)((int64_t)hi * m[r]) << 16);
+              Acc128& sa = slow_s[(16 * warp + g + 8 * r) * kMmaTok + 8 * nt + 2 * t + (i & 1)];
+              acc128_add_shifted(sa, p, e[r]);
+            }
           }
         }
       }
@@ -1054,7 +1102,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
   for (int nt = 0; nt < kMmaNT; ++nt)
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      Acc128 tot = slow[nt][i];
+      Acc128 tot = any_slow_seen ? slow_s[(16 * warp + g + 8 * (i >> 1)) * kMmaTok + 8 * nt + 2 * t + (i & 1)]
+                                 : Acc128{0, 0};
       acc128_add(tot, (uint64_t)alo[nt][i], alo[nt][i] >> 63);
       acc128_add(tot, (uint64_t)ahi[nt][i] << 16, ahi[nt][i] >> 48);
       int32_t v = acc128_round_q24(tot);
@@ -1143,7 +1192,9 @@ template <int EPI>
 cudaError_t launch_gemm(const ProductArgs& a, cudaStream_t stream) {
   // the tensor-core GEMM: whole 4-block stages inside each slice, and at most
   // 2048 blocks a row for its 64-bit accumulators
-  if (a.cols % (32 * kMmaKB) == 0 && (a.kc / 32) % kMmaKB == 0 && a.cols / 32 <= 2048) {
+  // (and 32-bit copy offsets)
+  if (a.cols % (32 * kMmaKB) == 0 && (a.kc / 32) % kMmaKB == 0 && a.cols / 32 <= 2048 &&
+      (uint64_t)((a.rows + 15) / 16 * 16) * a.cols < (1ull << 32) && (uint64_t)a.tokens * 4 * a.cols < (1ull << 32)) {
     dim3 grid((a.tokens + kMmaTok - 1) / kMmaTok, (a.rows + kMmaRows - 1) / kMmaRows);
     return launch_k(q8_gemm_mma_kernel<EPI>, grid, dim3(kMmaThreads), kMmaSmem, stream, a);
   }
