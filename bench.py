@@ -12,8 +12,9 @@ the 126 MB L2), so no flush is needed between steps.
   python bench.py [--gpus N --steps K --warmup W]      this framework
   python bench.py --impl reference ...                 the CPU reference path
 
-With N > 1 (torchrun), every rank decodes its own seeded sequence
-(independent claims, no collective on the data path): weak scaling.
+With N > 1 (torchrun), the one sequence is decoded by an N-way
+tensor-parallel model (kv groups, FFN rows and vocabulary split; the
+row-parallel products' exact partial sums summed over NCCL): strong scaling.
 """
 from __future__ import annotations
 
@@ -242,8 +243,16 @@ def main():
     _lib.check(_lib.lib().q8gpu_init(), "q8gpu_init")
 
     cfg = mistral_7b()
-    seed = args.seed + rank
-    model = DeviceModel(cfg, seed=seed)
+    seed = args.seed
+    if world > 1:
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        idt = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(_lib.tp_unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        model = DeviceModel(cfg, seed=seed, tp=(rank, world, bytes(idt.cpu().numpy().tobytes())))
+    else:
+        model = DeviceModel(cfg, seed=seed)
     e2e_steps = args.steps
     cap = args.prompt + args.warmup + args.steps + e2e_steps + 8
     sess = model.session(cap)
@@ -275,7 +284,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
         dist.barrier()
-    value = world * args.steps / (ms / 1e3)
+    value = args.steps / (ms / 1e3)  # one sequence (tensor-parallel over the N GPUs)
     ms_per_step = ms / args.steps
 
     # e2e through the C-ABI decode call: host token in, host token out, per step
@@ -290,7 +299,7 @@ def main():
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * e2e_steps / e2e_s
+    e2e_value = e2e_steps / e2e_s
 
     # roofline of the dominant kernel: the decode GEMV over the fused gate|up
     # matrix (28672 x 4096 Q8_0), one launch per layer (32 distinct 125 MB
@@ -307,31 +316,32 @@ def main():
     e1.record(stream)
     sess.synchronize()
     gemv_ms = e0.elapsed_time(e1) / (reps * cfg.layers)
-    n_rows, k = 2 * cfg.ffn, cfg.hidden
+    n_rows, k = 2 * cfg.ffn // world, cfg.hidden  # this rank's gate|up shard
     gemv_bytes = n_rows * k * 34 // 32 + 4 * k + (n_rows // 2) * 4  # weights + activation row + gated output
     peak, peak_kind = peaks()
     achieved = gemv_bytes / (gemv_ms / 1e3) / 1e9
     mean_ctx = ctx0 + (args.steps - 1) / 2.0 + 1
     step_bytes = algorithmic_bytes_per_step(cfg, mean_ctx)
-    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9
+    step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9  # all ranks' bytes
 
     kernels = sess.kernels_per_pass
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "int64",
         "data": "synthetic (seeded Q8_0 weights, seeded prompt tokens)",
         "config": {"workload": "mistral-7b-arch greedy decode after a 2048-token prompt (BASELINE config 4)",
                    "model": "mistral-7b-arch", "prompt": args.prompt, "context_at_start": ctx0,
-                   "global_batch": world, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                   "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(),
                      "algorithmic_bytes": gemv_bytes,
                      "kernel": "q8_gemv_tma_kernel<IN_NORM, EPI_SILU_MUL> (fused gate|up, 28672x4096)",
                      "peak_kind": peak_kind},
-        "step_roofline": {"achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
-                          "bytes_per_step": step_bytes},
+        "step_roofline": {"achieved": step_gbs, "peak": peak * world, "unit": "GB/s",
+                          "frac": step_gbs / (peak * world), "bytes_per_step": step_bytes},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
                 "api": "iris_session_decode (host token id in, host token id out)"},
         "gpu_launches": kernels * args.steps,

@@ -146,6 +146,19 @@ enum {
 
 int iris_model_create_mistral(const IrisMistralShape* shape, IrisModel** out);
 int iris_model_create_gemma(const IrisGemmaShape* shape, IrisModel** out);
+/* No counterpart in the reference (its tensor-parallel plan). Rank `rank` of a
+ * `world`-way tensor-parallel mistral-dense model: kv groups, FFN rows and
+ * vocabulary split evenly (kv_heads, ffn / 32 and vocab divisible by world;
+ * no tied head), the row-parallel o and down products exchanging exact
+ * partial sums over NCCL (communicator from the 128-byte id of
+ * iris_tp_unique_id, the same on every rank). Every rank makes the same calls
+ * in the same order; tensors are synthesized on the device
+ * (iris_model_synthesize); logits, tokens and positions are the whole
+ * model's. */
+int iris_model_create_mistral_tp(const IrisMistralShape* shape, uint32_t rank, uint32_t world,
+                                 const uint8_t* nccl_id, IrisModel** out);
+/* A fresh NCCL unique id (128 bytes) for iris_model_create_mistral_tp. */
+int iris_tp_unique_id(uint8_t* out);
 /* Uploads one Q8_0 tensor (layer = -1 for model-level tensors). */
 int iris_model_set_q8(IrisModel* model, int tensor, int32_t layer, const uint8_t* blocks,
                       uint64_t bytes);
@@ -252,6 +265,11 @@ int iris_mistral_layer_range(IrisModel* model, uint32_t layer, const int32_t* ro
  * ------------------------------------------------------------------------- */
 int iris_synth_q8(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,
                   int per_block_scales, uint8_t* blocks);
+/* Rows [row0, row0 + rows) x columns [col0, col0 + cols) of the synthetic
+ * tensor with full_cols columns (a tensor-parallel shard), as Q8_0 blocks. */
+int iris_synth_q8_block(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,
+                        uint32_t row0, uint32_t col0, uint32_t full_cols, int per_block_scales,
+                        uint8_t* blocks);
 int iris_synth_values(uint64_t seed, uint32_t tensor, int32_t layer, uint64_t count, uint32_t fan_in,
                       int32_t* values);
 

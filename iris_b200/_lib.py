@@ -71,6 +71,10 @@ SIGNATURES = {
     "iris_q8_product_device_noalloc": (C.c_int, [vp, vp, C.c_uint32, vp, vp]),
     "iris_model_create_mistral": (C.c_int, [C.POINTER(MistralShape), C.POINTER(vp)]),
     "iris_model_create_gemma": (C.c_int, [C.POINTER(GemmaShape), C.POINTER(vp)]),
+    "iris_model_create_mistral_tp": (C.c_int, [C.POINTER(MistralShape), C.c_uint32, C.c_uint32, u8p, C.POINTER(vp)]),
+    "iris_tp_unique_id": (C.c_int, [u8p]),
+    "iris_synth_q8_block": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.c_uint32,
+                                      C.c_uint32, C.c_uint32, C.c_int, u8p]),
     "iris_model_set_q8": (C.c_int, [vp, C.c_int, C.c_int32, u8p, C.c_uint64]),
     "iris_model_set_values": (C.c_int, [vp, C.c_int, C.c_int32, i32p, C.c_uint64]),
     "iris_model_synthesize": (C.c_int, [vp, C.c_uint64, C.c_int]),
@@ -122,6 +126,21 @@ def lib() -> C.CDLL:
             f.argtypes = args
         _lib = L
     return _lib
+
+
+def tp_unique_id() -> bytes:
+    """A fresh NCCL unique id (128 bytes) for a tensor-parallel model."""
+    out = np.zeros(128, np.uint8)
+    check(lib().iris_tp_unique_id(ptr(out, C.c_uint8)), "iris_tp_unique_id")
+    return out.tobytes()
+
+
+def synth_q8_block(seed: int, tensor: int, layer: int, rows: int, cols: int, row0: int, col0: int,
+                   full_cols: int, per_block: bool = False) -> np.ndarray:
+    out = np.empty(rows * (cols // 32) * 34, np.uint8)
+    check(lib().iris_synth_q8_block(seed, tensor, layer, rows, cols, row0, col0, full_cols, int(per_block),
+                                    ptr(out, C.c_uint8)), "iris_synth_q8_block")
+    return out
 
 
 def error_string(code: int) -> str:

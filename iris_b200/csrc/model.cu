@@ -23,6 +23,7 @@
 
 #include "../../include/iris_b200.h"
 #include "layers.cuh"
+#include "tp.cuh"
 #include "synth.cuh"
 
 using namespace iris;
@@ -116,6 +117,11 @@ struct IrisModel {
   std::vector<LayerDev> layers;
   uint64_t weight_bytes = 0;
   IrisSession* scratch = nullptr;  // for the chain-stage entry point
+  // tensor parallelism: this rank's share of heads, kv heads, FFN rows and
+  // vocabulary (the dimensions above are the local ones), the full
+  // vocabulary (embedding table, token ids) and the NCCL communicator
+  uint32_t tp_rank = 0, tp_world = 1, Vfull = 0;
+  void* comm = nullptr;
 };
 
 struct IrisSession {
@@ -143,6 +149,8 @@ struct IrisSession {
   unsigned long long *gbest = nullptr, *gsum = nullptr;
   unsigned int* gbar = nullptr;
   unsigned int* fault = nullptr;
+  int64_t* partial = nullptr;     // tensor parallelism: [kMaxRows][H][4] limbs
+  int32_t* logits_full = nullptr; // tensor parallelism: the gathered vocabulary
   // decode GEMV split scratch (zero between launches)
   unsigned long long* split_acc = nullptr;
   unsigned int* split_count = nullptr;
@@ -161,7 +169,7 @@ void free_session(IrisSession* s) {
   void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
-                  s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar};
+                  s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -185,6 +193,10 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   if (e == cudaSuccess) e = dalloc(&s->planes, (size_t)R * 4 * wide);
   if (e == cudaSuccess) e = dalloc(&s->planes2, (size_t)R * 4 * wide);
   if (e == cudaSuccess) e = dalloc(&s->logits, (size_t)m->V);
+  if (m->tp_world > 1) {
+    if (e == cudaSuccess) e = dalloc(&s->partial, (size_t)R * m->H * 4);
+    if (e == cudaSuccess) e = dalloc(&s->logits_full, (size_t)m->Vfull);
+  }
   if (e == cudaSuccess) e = dalloc(&s->best, R);
   if (e == cudaSuccess) e = dalloc(&s->d_ids, R);
   if (e == cudaSuccess) e = dalloc(&s->d_pos, 1);
@@ -289,6 +301,23 @@ AttnArgs attn_args(IrisSession* s, uint32_t l, const uint32_t* pos_ptr, uint32_t
 
 // One mistral-dense layer (mistral/layer.rs:107-270) over `tokens` rows in
 // s->x at positions pos0.. (or *pos_ptr for the decode pass).
+// x = x + W in (in as byte planes): one product, or with tensor parallelism
+// the rank's columns as exact partial sums, their sum over the ranks, then
+// one rounding and the residual.
+cudaError_t row_parallel_resid(IrisSession* s, ProductArgs a, uint32_t tokens) {
+  IrisModel* m = s->m;
+  if (m->tp_world == 1) {
+    a.out = s->x;
+    a.resid = s->x;
+    return launch_product(a, IN_PLANES, EPI_RESID, s->stream);
+  }
+  a.partial = s->partial;
+  cudaError_t e = launch_product(a, IN_PLANES, EPI_PARTIAL, s->stream);
+  if (e == cudaSuccess) e = tp_sum_limbs(m->comm, s->partial, (size_t)tokens * m->H * 4, s->stream);
+  if (e == cudaSuccess) e = launch_tp_finish(s->partial, tokens, m->H, s->x, s->x, s->stream);
+  return e;
+}
+
 cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint32_t* pos_ptr,
                           uint32_t pos0) {
   IrisModel* m = s->m;
@@ -326,9 +355,7 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   // x = x + W_o ctx
   ProductArgs o = session_product_args(s, L.o, tokens);
   o.planes = s->planes;
-  o.out = s->x;
-  o.resid = s->x;
-  e = launch_product(o, IN_PLANES, EPI_RESID, st);
+  e = row_parallel_resid(s, o, tokens);
   if (e != cudaSuccess) return e;
   // g = silu(W_gate m) * (W_up m), m = rms_norm(x)
   ProductArgs g = session_product_args(s, L.gu, tokens);
@@ -347,9 +374,7 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   // x = x + W_down g
   ProductArgs dn = session_product_args(s, L.down, tokens);
   dn.planes = s->planes2;
-  dn.out = s->x;
-  dn.resid = s->x;
-  return launch_product(dn, IN_PLANES, EPI_RESID, st);
+  return row_parallel_resid(s, dn, tokens);
 }
 
 // One gemma-dense layer (prefill_range.rs:307-333, 497-741, 879-957).
@@ -451,7 +476,10 @@ cudaError_t run_pass(IrisSession* s, uint32_t tokens, const uint32_t* ids_dev, c
   h.out = store_logits ? s->logits : nullptr;
   h.best = s->best;
   h.softcap = m->softcap;
-  return launch_product(h, IN_NORM, EPI_LOGITS, st, IRIS_PATH_GEMV);
+  h.row_base = m->tp_rank * m->V;  // vocabulary shard
+  e = launch_product(h, IN_NORM, EPI_LOGITS, st, IRIS_PATH_GEMV);
+  if (e == cudaSuccess && m->tp_world > 1) e = tp_max_keys(m->comm, s->best, 1, st);
+  return e;
 }
 
 // IRIS_ESTALL when a kernel recorded a given-up wait since the last check.
@@ -462,12 +490,24 @@ int check_fault() {
   return fault ? IRIS_ESTALL : 0;
 }
 
+// The last pass's logits (the whole vocabulary) to the host, asynchronously on
+// the session stream; every rank of a tensor-parallel model takes part.
+cudaError_t copy_logits(IrisSession* s, int32_t* host) {
+  IrisModel* m = s->m;
+  if (m->tp_world > 1) {
+    cudaError_t e = tp_gather_i32(m->comm, s->logits, s->logits_full, m->V, s->stream);
+    if (e != cudaSuccess) return e;
+    return cudaMemcpyAsync(host, s->logits_full, (size_t)m->Vfull * 4, cudaMemcpyDeviceToHost, s->stream);
+  }
+  return cudaMemcpyAsync(host, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+}
+
 int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits, uint32_t* token) {
   IrisModel* m = s->m;
   if (n == 0) return IRIS_EINVAL;
   if ((uint64_t)s->len + n > s->cap || (uint64_t)s->len + n > m->max_positions) return IRIS_ERANGE;
   for (uint32_t i = 0; i < n; ++i)
-    if (ids[i] >= m->V) return IRIS_EINVAL;
+    if (ids[i] >= m->Vfull) return IRIS_EINVAL;
   cudaError_t e = cudaSuccess;
   for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
     uint32_t cnt = std::min(kMaxRows, n - r0);
@@ -477,7 +517,7 @@ int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits
   }
   unsigned long long key = 0;
   if (e == cudaSuccess) e = cudaMemcpyAsync(&key, s->best, 8, cudaMemcpyDeviceToHost, s->stream);
-  if (e == cudaSuccess && logits) e = cudaMemcpyAsync(logits, s->logits, (size_t)m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && logits) e = copy_logits(s, logits);
   if (e == cudaSuccess) e = launch_fill_u64(s->best, 1, s->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
   if (e != cudaSuccess) return (int)e;
@@ -539,30 +579,43 @@ int check_model_ready(const IrisModel* m) {
 struct Q8Target {
   Q8GpuMatrix* m;
   uint32_t rows, cols, stride, offset;
+  // the block of the full tensor these rows hold (tensor-parallel shards)
+  uint32_t src_row0 = 0, src_col0 = 0, full_cols = 0;
 };
 
 int q8_target(IrisModel* m, int tensor, int32_t layer, Q8Target* t) {
-  if (tensor == IRIS_T_EMBED) { *t = {m->embed, m->V, m->H, 1, 0}; return 0; }
+  const uint32_t r = m->tp_rank, W = m->tp_world;
+  auto set = [&](Q8GpuMatrix* mat, uint32_t rows, uint32_t cols, uint32_t stride, uint32_t offset, uint32_t row0,
+                 uint32_t col0, uint32_t full_cols) {
+    t->m = mat;
+    t->rows = rows;
+    t->cols = cols;
+    t->stride = stride;
+    t->offset = offset;
+    t->src_row0 = row0;
+    t->src_col0 = col0;
+    t->full_cols = full_cols;
+    return 0;
+  };
+  if (tensor == IRIS_T_EMBED) return set(m->embed, m->Vfull, m->H, 1, 0, 0, 0, m->H);
   if (tensor == IRIS_T_HEAD) {
     if (m->tied) return IRIS_EINVAL;
-    *t = {m->head, m->V, m->H, 1, 0};
-    return 0;
+    return set(m->head, m->V, m->H, 1, 0, r * m->V, 0, m->H);
   }
   if (tensor == IRIS_T_PLE_EMBED) {
     if (m->family != kFamilyGemma) return IRIS_EINVAL;
-    *t = {m->ple_embed, m->V, m->L * m->P, 1, 0};
-    return 0;
+    return set(m->ple_embed, m->V, m->L * m->P, 1, 0, 0, 0, m->L * m->P);
   }
   if (layer < 0 || (uint32_t)layer >= m->L) return IRIS_EINVAL;
   LayerDev& L = m->layers[layer];
   switch (tensor) {
-    case IRIS_T_W_Q: *t = {L.qkv, m->qd, m->H, 1, 0}; return 0;
-    case IRIS_T_W_K: *t = {L.qkv, m->kvd, m->H, 1, m->qd}; return 0;
-    case IRIS_T_W_V: *t = {L.qkv, m->kvd, m->H, 1, m->qd + m->kvd}; return 0;
-    case IRIS_T_W_O: *t = {L.o, m->H, m->qd, 1, 0}; return 0;
-    case IRIS_T_W_GATE: *t = {L.gu, m->F, m->H, 2, 0}; return 0;
-    case IRIS_T_W_UP: *t = {L.gu, m->F, m->H, 2, 1}; return 0;
-    case IRIS_T_W_DOWN: *t = {L.down, m->H, m->F, 1, 0}; return 0;
+    case IRIS_T_W_Q: return set(L.qkv, m->qd, m->H, 1, 0, r * m->qd, 0, m->H);
+    case IRIS_T_W_K: return set(L.qkv, m->kvd, m->H, 1, m->qd, r * m->kvd, 0, m->H);
+    case IRIS_T_W_V: return set(L.qkv, m->kvd, m->H, 1, m->qd + m->kvd, r * m->kvd, 0, m->H);
+    case IRIS_T_W_O: return set(L.o, m->H, m->qd, 1, 0, 0, r * m->qd, W * m->qd);
+    case IRIS_T_W_GATE: return set(L.gu, m->F, m->H, 2, 0, r * m->F, 0, m->H);
+    case IRIS_T_W_UP: return set(L.gu, m->F, m->H, 2, 1, r * m->F, 0, m->H);
+    case IRIS_T_W_DOWN: return set(L.down, m->H, m->F, 1, 0, 0, r * m->F, W * m->F);
   }
   return IRIS_EINVAL;
 }
@@ -604,7 +657,7 @@ int alloc_layers(IrisModel* m) {
     if (r) m->weight_bytes += (uint64_t)rows * cols + (uint64_t)rows * (cols / 32) * 2;
     return r;
   };
-  m->embed = q8(m->V, m->H);
+  m->embed = q8(m->Vfull, m->H);
   m->head = m->tied ? m->embed : q8(m->V, m->H);
   if (e == cudaSuccess) e = dalloc(&m->final_norm, m->H);
   for (uint32_t l = 0; l < m->L; ++l) {
@@ -660,28 +713,39 @@ void iris_model_free(IrisModel* m) {
                     L.ple_post_norm, L.ple_gate, L.ple_proj, L.inv_freq};
     for (void* p : ptrs) cudaFree(p);
   }
+  tp_comm_free(m->comm);
   delete m;
 }
 
-int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
+static int create_mistral(const IrisMistralShape* sh, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
+                          IrisModel** out) {
   *out = nullptr;
   if (!sh || !sh->layers || !sh->hidden || !sh->ffn || !sh->heads || !sh->kv_heads || !sh->head_dim ||
       !sh->vocab || sh->heads % sh->kv_heads || sh->head_dim % 4 || sh->hidden % 32 || sh->ffn % 32 ||
       (sh->heads * sh->head_dim) % 32 || sh->norm_eps < 0 || !sh->rope_inverse_frequencies ||
       sh->heads / sh->kv_heads > 16)
     return IRIS_EINVAL;
+  // a shard: whole kv groups, FFN rows and vocabulary rows in 32-multiples
+  // where they are product columns (o, down); the tied head is not sharded
+  if (world == 0 || rank >= world ||
+      (world > 1 && (sh->kv_heads % world || sh->ffn % (32 * world) || sh->vocab % world || sh->tied_head ||
+                     ((sh->heads / world) * sh->head_dim) % 32 || !nccl_id)))
+    return IRIS_EINVAL;
   for (uint32_t i = 0; i < sh->head_dim / 2; ++i)  // layer.rs:71-78
     if (sh->rope_inverse_frequencies[i] < 0 || sh->rope_inverse_frequencies[i] > ((int64_t)1 << 32))
       return IRIS_EINVAL;
   IrisModel* m = new IrisModel();
   m->family = kFamilyMistral;
+  m->tp_rank = rank;
+  m->tp_world = world;
   m->L = sh->layers;
   m->H = sh->hidden;
-  m->F = sh->ffn;
-  m->heads = sh->heads;
-  m->kvh = sh->kv_heads;
+  m->F = sh->ffn / world;
+  m->heads = sh->heads / world;
+  m->kvh = sh->kv_heads / world;
   m->d = sh->head_dim;
-  m->V = sh->vocab;
+  m->V = sh->vocab / world;
+  m->Vfull = sh->vocab;
   m->max_positions = sh->max_positions;
   m->qd = m->heads * m->d;
   m->kvd = m->kvh * m->d;
@@ -689,7 +753,9 @@ int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
   m->scale_q32 = sh->attention_scale_q32;
   m->tied = sh->tied_head != 0;
   m->layers.resize(m->L);
-  int rc = alloc_layers(m);
+  int rc = 0;
+  if (world > 1) rc = (int)tp_comm_init(&m->comm, rank, world, nccl_id);
+  if (rc == 0) rc = alloc_layers(m);
   if (rc == 0) rc = (int)dalloc(&m->freqs, m->d / 2);
   if (rc == 0)
     rc = (int)cudaMemcpy(m->freqs, sh->rope_inverse_frequencies, (m->d / 2) * 8, cudaMemcpyHostToDevice);
@@ -699,6 +765,17 @@ int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
   }
   *out = m;
   return 0;
+}
+
+int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
+  if (!out) return IRIS_EINVAL;
+  return create_mistral(sh, 0, 1, nullptr, out);
+}
+
+int iris_model_create_mistral_tp(const IrisMistralShape* sh, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
+                                 IrisModel** out) {
+  if (!out) return IRIS_EINVAL;
+  return create_mistral(sh, rank, world, nccl_id, out);
 }
 
 int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
@@ -726,6 +803,7 @@ int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
   m->kvh = sh->kv_heads;
   m->d = sh->head_dim;
   m->V = sh->vocab;
+  m->Vfull = sh->vocab;
   m->P = sh->ple_width;
   m->max_positions = UINT32_MAX;
   m->qd = m->heads * m->d;
@@ -763,7 +841,7 @@ int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
 }
 
 int iris_model_set_q8(IrisModel* m, int tensor, int32_t layer, const uint8_t* blocks, uint64_t bytes) {
-  if (!m || !blocks) return IRIS_EINVAL;
+  if (!m || !blocks || m->tp_world > 1) return IRIS_EINVAL;  // shards are synthesized on the device
   Q8Target t;
   int rc = q8_target(m, tensor, layer, &t);
   if (rc) return rc;
@@ -776,11 +854,11 @@ int iris_model_set_q8(IrisModel* m, int tensor, int32_t layer, const uint8_t* bl
 
 int iris_model_get_q8(const IrisModel* mc, int tensor, int32_t layer, uint8_t* blocks, uint64_t bytes) {
   IrisModel* m = const_cast<IrisModel*>(mc);
-  if (!m || !blocks) return IRIS_EINVAL;
+  if (!m || !blocks || m->tp_world > 1) return IRIS_EINVAL;
   Q8Target t;
   int rc = q8_target(m, tensor, layer, &t);
   if (tensor == IRIS_T_HEAD && m->tied) {
-    t = {m->head, m->V, m->H, 1, 0};
+    t = Q8Target{m->head, m->V, m->H, 1, 0};
     rc = 0;
   }
   if (rc) return rc;
@@ -813,7 +891,8 @@ int iris_model_synthesize(IrisModel* m, uint64_t seed, int per_block) {
   auto q8 = [&](int tensor, int32_t layer) {
     Q8Target t;
     if (e != cudaSuccess || q8_target(m, tensor, layer, &t)) return;
-    e = synth_q8_rows(t.m, seed, (uint32_t)tensor, layer, t.rows, t.cols, t.stride, t.offset, per_block, 0);
+    e = synth_q8_block(t.m, seed, (uint32_t)tensor, layer, t.rows, t.cols, t.src_row0, t.src_col0, t.full_cols,
+                       t.stride, t.offset, per_block, 0);
   };
   auto vals = [&](int tensor, int32_t layer) {
     uint64_t count;
@@ -868,7 +947,7 @@ int iris_session_prefill(IrisSession* s, const uint32_t* ids, uint32_t n, int32_
 
 int iris_session_decode(IrisSession* s, uint32_t token_in, int32_t* logits, uint32_t* token_out) {
   if (!s) return IRIS_EINVAL;
-  if (token_in >= s->m->V) return IRIS_EINVAL;
+  if (token_in >= s->m->Vfull) return IRIS_EINVAL;
   if (!s->has_logits) return IRIS_ESTATE;
   cudaError_t e = cudaMemcpyAsync(s->d_token, &token_in, 4, cudaMemcpyHostToDevice, s->stream);
   if (e != cudaSuccess) return (int)e;
@@ -876,8 +955,7 @@ int iris_session_decode(IrisSession* s, uint32_t token_in, int32_t* logits, uint
   if (rc) return rc;
   uint32_t tok = 0;
   e = cudaMemcpyAsync(&tok, s->d_token, 4, cudaMemcpyDeviceToHost, s->stream);
-  if (e == cudaSuccess && logits)
-    e = cudaMemcpyAsync(logits, s->logits, (size_t)s->m->V * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && logits) e = copy_logits(s, logits);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
   if (e == cudaSuccess && token_out) *token_out = tok;
   return (int)e;
@@ -891,7 +969,7 @@ int iris_generate(IrisSession* s, const uint32_t* prompt, uint32_t n_prompt, uin
   if (max_tokens == 0) return 0;
   int rc = iris_session_reset(s);
   if (rc) return rc;
-  const uint32_t V = s->m->V;
+  const uint32_t V = s->m->Vfull;
   uint32_t tok = 0;
   rc = prefill_ids(s, prompt, n_prompt, out_logits, &tok);
   if (rc) return rc;
@@ -1105,7 +1183,9 @@ void iris_graph_free(void* graph_exec) {
 int iris_mistral_layer_range(IrisModel* m, uint32_t layer, const int32_t* rows_in, uint32_t n, uint32_t start,
                              const int32_t* prior_k, const int32_t* prior_v, int32_t* rows_out, int32_t* own_k,
                              int32_t* own_v) {
-  if (!m || m->family != kFamilyMistral || layer >= m->L || !rows_in || !rows_out) return IRIS_EINVAL;
+  // the chain stage runs whole models (claims are spread data-parallel)
+  if (!m || m->family != kFamilyMistral || layer >= m->L || !rows_in || !rows_out || m->tp_world > 1)
+    return IRIS_EINVAL;
   if (n == 0) return 0;  // layer.rs:117-119: a range with no rows produces nothing
   if ((uint64_t)start + n > m->max_positions) return IRIS_ERANGE;  // layer.rs:121-127
   if (start && (!prior_k || !prior_v)) return IRIS_EINVAL;

@@ -92,22 +92,28 @@ __global__ void blocks_from_tile_kernel(const int8_t* q, const uint16_t* s, uint
   for (int i = 0; i < 32; ++i) dst[2 + i] = (uint8_t)src[i];
 }
 
+// Rows [row0, row0 + rows) x columns [col0, col0 + cols) of the synthetic
+// tensor with full_cols columns, into rows (i * row_stride + row_offset) of
+// dst (a shard of a tensor-parallel model is such a block).
 __global__ void synth_q8_kernel(int8_t* q, uint16_t* s, uint32_t kc, uint32_t nslices, uint64_t seed,
-                                uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols, uint32_t row_stride,
-                                uint32_t row_offset, int per_block) {
+                                uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols, uint32_t row0,
+                                uint32_t col0, uint32_t full_cols, uint32_t row_stride, uint32_t row_offset,
+                                int per_block) {
+  pdl_wait();
+  pdl_trigger();
   const uint32_t nb = cols / 32;
   const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= (uint64_t)rows * nb) return;
   const uint32_t r = (uint32_t)(b / nb), blk = (uint32_t)(b % nb);
-  const uint32_t dr = r * row_stride + row_offset;
-  s[q8_scale_offset(kc, nslices, dr, blk)] = synth_scale_bits(seed, tensor, layer, r, blk, cols, per_block);
+  const uint32_t dr = r * row_stride + row_offset, sr = row0 + r, sblk = col0 / 32 + blk;
+  s[q8_scale_offset(kc, nslices, dr, blk)] = synth_scale_bits(seed, tensor, layer, sr, sblk, full_cols, per_block);
   uint32_t w[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     uint32_t v = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      v |= (uint32_t)(uint8_t)synth_q(seed, tensor, layer, r, blk * 32 + i * 4 + j, cols) << (8 * j);
+      v |= (uint32_t)(uint8_t)synth_q(seed, tensor, layer, sr, sblk * 32 + i * 4 + j, full_cols) << (8 * j);
     w[i] = v;
   }
   uint4* dst = (uint4*)(q + q8_value_offset(kc, nslices, dr, blk * 32));
@@ -209,10 +215,18 @@ cudaError_t download_q8_blocks(const Q8GpuMatrix* src, uint8_t* host_blocks, uin
 cudaError_t synth_q8_rows(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int32_t layer,
                           uint32_t rows, uint32_t cols, uint32_t row_stride, uint32_t row_offset,
                           int per_block, cudaStream_t stream) {
+  return synth_q8_block(dst, seed, tensor, layer, rows, cols, 0, 0, cols, row_stride, row_offset, per_block, stream);
+}
+
+cudaError_t synth_q8_block(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows,
+                           uint32_t cols, uint32_t row0, uint32_t col0, uint32_t full_cols, uint32_t row_stride,
+                           uint32_t row_offset, int per_block, cudaStream_t stream) {
+  if (cols % 32 || col0 % 32) return cudaErrorInvalidValue;
   uint64_t nblk = (uint64_t)rows * (cols / 32);
-  synth_q8_kernel<<<(unsigned)((nblk + 255) / 256), 256, 0, stream>>>(
-      dst->q, dst->s, dst->kc, dst->nslices, seed, tensor, layer, rows, cols, row_stride, row_offset, per_block);
-  return cudaGetLastError();
+  if (nblk == 0) return cudaSuccess;
+  return launch_k(synth_q8_kernel, dim3((unsigned)((nblk + 255) / 256)), dim3(256), 0, stream, dst->q, dst->s,
+                  dst->kc, dst->nslices, seed, tensor, layer, rows, cols, row0, col0, full_cols, row_stride,
+                  row_offset, per_block);
 }
 
 cudaError_t synth_values_dev(int32_t* dst, uint64_t seed, uint32_t tensor, int32_t layer,
@@ -561,7 +575,7 @@ __device__ __forceinline__ void gemv_group_epilogue(const ProductArgs& a, uint32
     if (lane < kQ8TileRows && row < a.rows) {
       const int32_t c = a.softcap > 0 ? softcap_act(v, a.softcap) : v;
       if (a.out) a.out[row] = c;
-      const unsigned long long key = best_key(c, row);
+      const unsigned long long key = best_key(c, row + a.row_base);
       *best = key > *best ? key : *best;
     }
   } else {
@@ -694,7 +708,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
         }
         if (lane == 0) a.split_count[g] = 0;
       }
-      gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
+      if (EPI == EPI_PARTIAL) {
+        const uint32_t row = g * kQ8TileRows + lane;
+        if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, a.partial + (size_t)row * 4);
+      } else {
+        gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
+      }
     }
     if (EPI == EPI_LOGITS) {
 #pragma unroll
@@ -862,14 +881,17 @@ __global__ void __launch_bounds__(256) q8_gemm_kernel(ProductArgs a) {
     for (int i = 0; i < 4; ++i) {
       uint32_t row = n0 + tx + 16 * i;
       int32_t v = acc128_round_q24(acc[i][j]);
-      if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+      if (EPI == EPI_PARTIAL) {
+        if (tok < a.tokens && row < a.rows)
+          limbs_from_acc128(acc[i][j].lo, acc[i][j].hi, a.partial + ((size_t)tok * a.rows + row) * 4);
+      } else if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
         int32_t partner = __shfl_xor_sync(0xffffffffu, v, 1);
         if ((tx & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
       } else if (EPI == EPI_LOGITS) {
         if (tok < a.tokens && row < a.rows) {
           if (a.softcap > 0) v = softcap_act(v, a.softcap);
           if (a.out) a.out[(size_t)tok * a.out_stride + row] = v;
-          atomicMax(a.best + tok, best_key(v, row));
+          atomicMax(a.best + tok, best_key(v, row + a.row_base));
         }
       } else if (tok < a.tokens && row < a.rows) {
         epi_single<EPI>(a, tok, row, v);
@@ -1108,14 +1130,16 @@ __global__ void __launch_bounds__(kMmaThreads, 2) q8_gemm_mma_kernel(ProductArgs
       acc128_add(tot, (uint64_t)ahi[nt][i] << 16, ahi[nt][i] >> 48);
       int32_t v = acc128_round_q24(tot);
       const uint32_t row = n0 + 16 * warp + g + 8 * (i >> 1), tok = m0 + 8 * nt + 2 * t + (i & 1);
-      if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+      if (EPI == EPI_PARTIAL) {
+        if (tok < a.tokens && row < a.rows) limbs_from_acc128(tot.lo, tot.hi, a.partial + ((size_t)tok * a.rows + row) * 4);
+      } else if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
         const int32_t partner = __shfl_xor_sync(0xffffffffu, v, 4);  // row ^ 1, same token
         if ((g & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
       } else if (EPI == EPI_LOGITS) {
         if (tok < a.tokens && row < a.rows) {
           if (a.softcap > 0) v = softcap_act(v, a.softcap);
           if (a.out) a.out[(size_t)tok * a.out_stride + row] = v;
-          atomicMax(a.best + tok, best_key(v, row));
+          atomicMax(a.best + tok, best_key(v, row + a.row_base));
         }
       } else if (tok < a.tokens && row < a.rows) {
         epi_single<EPI>(a, tok, row, v);
@@ -1162,6 +1186,7 @@ cudaError_t prepare_gemv_in() {
   if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_SILU_MUL>();
   if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_GELU_MUL>();
   if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_LOGITS>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN, EPI_PARTIAL>();
   return e;
 }
 
@@ -1180,6 +1205,7 @@ cudaError_t prepare_product_kernels() {
     if (e == cudaSuccess) e = prepare_mma_one<EPI_SILU_MUL>();
     if (e == cudaSuccess) e = prepare_mma_one<EPI_GELU_MUL>();
     if (e == cudaSuccess) e = prepare_mma_one<EPI_LOGITS>();
+    if (e == cudaSuccess) e = prepare_mma_one<EPI_PARTIAL>();
     if (e != cudaSuccess) return e;
   }
   cudaError_t e = prepare_gemv_in<IN_PLANES>();
@@ -1211,6 +1237,7 @@ cudaError_t dispatch_gemv(const ProductArgs& a, EpiMode epi, cudaStream_t s) {
     case EPI_SILU_MUL: return launch_gemv<IN, EPI_SILU_MUL>(a, s);
     case EPI_GELU_MUL: return launch_gemv<IN, EPI_GELU_MUL>(a, s);
     case EPI_LOGITS: return launch_gemv<IN, EPI_LOGITS>(a, s);
+    case EPI_PARTIAL: return launch_gemv<IN, EPI_PARTIAL>(a, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -1239,6 +1266,7 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
     case EPI_SILU_MUL: return launch_gemm<EPI_SILU_MUL>(a, stream);
     case EPI_GELU_MUL: return launch_gemm<EPI_GELU_MUL>(a, stream);
     case EPI_LOGITS: return launch_gemm<EPI_LOGITS>(a, stream);
+    case EPI_PARTIAL: return launch_gemm<EPI_PARTIAL>(a, stream);
   }
   return cudaErrorInvalidValue;
 }
@@ -1474,6 +1502,23 @@ int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tok
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaMemcpy(out, g_out, out_bytes, cudaMemcpyDeviceToHost);
   return (int)e;
+}
+
+int iris_synth_q8_block(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols, uint32_t row0,
+                        uint32_t col0, uint32_t full_cols, int per_block_scales, uint8_t* blocks) {
+  if (cols == 0 || cols % 32 || col0 % 32 || (uint64_t)col0 + cols > full_cols) return IRIS_EINVAL;
+  uint32_t nb = cols / 32;
+  for (uint32_t r = 0; r < rows; ++r)
+    for (uint32_t b = 0; b < nb; ++b) {
+      uint8_t* dst = blocks + ((size_t)r * nb + b) * 34;
+      const uint32_t sr = row0 + r, sb = col0 / 32 + b;
+      uint16_t bits = synth_scale_bits(seed, tensor, layer, sr, sb, full_cols, per_block_scales);
+      dst[0] = (uint8_t)bits;
+      dst[1] = (uint8_t)(bits >> 8);
+      for (uint32_t j = 0; j < 32; ++j)
+        dst[2 + j] = (uint8_t)synth_q(seed, tensor, layer, sr, sb * 32 + j, full_cols);
+    }
+  return 0;
 }
 
 int iris_synth_q8(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,

@@ -58,7 +58,8 @@ enum EpiMode {
   EPI_QKV_ROPE = 2,  // mistral fused q|k|v rows: RoPE q,k; k,v into the cache
   EPI_SILU_MUL = 3,  // interleaved gate|up rows: planes of mul_sat(silu(g), u)
   EPI_GELU_MUL = 4,  // interleaved gate|up rows: planes of mul_sat(gelu(g), u)
-  EPI_LOGITS = 5     // logits (+softcap) and a first-maximum key
+  EPI_LOGITS = 5,    // logits (+softcap) and a first-maximum key
+  EPI_PARTIAL = 6    // the unrounded 128-bit sums as four 32-bit limbs in int64 (tensor parallelism)
 };
 
 struct ProductArgs {
@@ -84,6 +85,8 @@ struct ProductArgs {
   uint32_t pos0;           // position of token 0 when pos_ptr is NULL
   unsigned long long* best;  // first-maximum key per token
   int32_t softcap;
+  uint32_t row_base;         // global index of row 0 in first-maximum keys (vocabulary shards)
+  int64_t* partial;          // EPI_PARTIAL: [tokens][rows][4] limbs
   // Decode GEMV split scratch (optional): 2 words a row and a slice count a
   // tile group for split_groups groups, all zero between launches.
   unsigned long long* split_acc;
@@ -100,6 +103,16 @@ cudaError_t launch_product(const ProductArgs& a, InMode in, EpiMode epi, cudaStr
 // int32 rows -> byte planes (optionally RMS-normalised), one block a token.
 cudaError_t launch_planes(const int32_t* x, const int32_t* norm_w, int64_t eps, uint32_t tokens,
                           uint32_t cols, uint8_t* planes, cudaStream_t stream);
+// The limbs of an unrounded 128-bit row sum (EPI_PARTIAL): bits 0-31, 32-63,
+// 64-95 (unsigned) and 96-127 (signed), each in an int64, so that the sums of
+// up to 2^31 shards' limbs are exact in int64.
+__host__ __device__ inline void limbs_from_acc128(uint64_t lo, int64_t hi, int64_t* l) {
+  l[0] = (int64_t)(lo & 0xffffffffull);
+  l[1] = (int64_t)(lo >> 32);
+  l[2] = (int64_t)((uint64_t)hi & 0xffffffffull);
+  l[3] = hi >> 32;
+}
+
 // Decodes a first-maximum key (value, lowest index) into its token id.
 __host__ __device__ inline uint32_t best_key_token(unsigned long long key) {
   return 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
@@ -129,6 +142,11 @@ cudaError_t download_q8_blocks(const Q8GpuMatrix* src, uint8_t* host_blocks, uin
 cudaError_t synth_q8_rows(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int32_t layer,
                           uint32_t rows, uint32_t cols, uint32_t row_stride, uint32_t row_offset,
                           int per_block, cudaStream_t stream);
+// Rows [row0, row0 + rows) x columns [col0, col0 + cols) of the synthetic
+// tensor with full_cols columns (a tensor-parallel shard).
+cudaError_t synth_q8_block(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows,
+                           uint32_t cols, uint32_t row0, uint32_t col0, uint32_t full_cols, uint32_t row_stride,
+                           uint32_t row_offset, int per_block, cudaStream_t stream);
 cudaError_t synth_values_dev(int32_t* dst, uint64_t seed, uint32_t tensor, int32_t layer,
                              uint64_t count, uint32_t fan_in, cudaStream_t stream);
 Q8GpuMatrix* alloc_q8(uint32_t rows, uint32_t cols, cudaError_t* err);

@@ -1,0 +1,22 @@
+// Tensor parallelism over NCCL (tp.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace iris {
+
+bool tp_available();
+cudaError_t tp_unique_id(uint8_t* out);  // 128 bytes
+cudaError_t tp_comm_init(void** comm, uint32_t rank, uint32_t world, const uint8_t* id);
+void tp_comm_free(void* comm);
+// In-place sums of int64 limbs / maxima of first-maximum keys over the ranks.
+cudaError_t tp_sum_limbs(void* comm, int64_t* limbs, size_t count, cudaStream_t s);
+cudaError_t tp_max_keys(void* comm, unsigned long long* keys, size_t count, cudaStream_t s);
+// Rank-major concatenation of every rank's `count` values.
+cudaError_t tp_gather_i32(void* comm, const int32_t* part, int32_t* full, size_t count, cudaStream_t s);
+// out[t][row] = add_sat(round_q24(sum of limbs), resid[t][row]).
+cudaError_t launch_tp_finish(const int64_t* limbs, uint32_t tokens, uint32_t rows, const int32_t* resid,
+                             int32_t* out, cudaStream_t s);
+
+}  // namespace iris

@@ -74,8 +74,12 @@ class DeviceModel:
     """A model whose weights live in HBM (IrisModel)."""
 
     def __init__(self, cfg, weights: Optional[Dict[Key, np.ndarray]] = None, seed: Optional[int] = None,
-                 per_block: bool = False):
+                 per_block: bool = False, tp: Optional[Tuple[int, int, bytes]] = None):
+        """`tp` = (rank, world, nccl_id): this process's shard of a tensor-parallel
+        mistral-dense model (weights synthesized on the device from `seed`;
+        every rank makes the same calls in the same order)."""
         self.cfg = cfg
+        self.tp = tp
         self._h = C.c_void_p()
         L = lib()
         if cfg.family == "mistral":
@@ -83,7 +87,15 @@ class DeviceModel:
             shape = _lib.MistralShape(cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim,
                                       cfg.vocab, cfg.max_positions, cfg.norm_eps, cfg.scale_q32, int(cfg.tied),
                                       ptr(self._freqs, C.c_int64))
-            check(L.iris_model_create_mistral(C.byref(shape), C.byref(self._h)), "iris_model_create_mistral")
+            if tp is not None and tp[1] > 1:
+                if weights is not None or seed is None:
+                    raise ValueError("tensor-parallel shards are synthesized on the device: give `seed`")
+                rank, world, nccl_id = tp
+                idb = np.frombuffer(bytes(nccl_id), np.uint8).copy()
+                check(L.iris_model_create_mistral_tp(C.byref(shape), rank, world, ptr(idb, C.c_uint8),
+                                                     C.byref(self._h)), "iris_model_create_mistral_tp")
+            else:
+                check(L.iris_model_create_mistral(C.byref(shape), C.byref(self._h)), "iris_model_create_mistral")
         else:
             n = cfg.layers
             self._win = np.array([cfg.window(l) for l in range(n)], np.uint32)

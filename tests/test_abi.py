@@ -100,3 +100,17 @@ def test_against_the_oracle_tables():
     for x in [1e-5, 1e-6, 0.1, 3.0e-8, 30.0, 45.254833995939045, 2 ** -0.5]:
         assert shapes.f32_to_acc(x) == L.oracle_f32_to_acc(x)
         assert shapes.f32_to_act(x) == L.oracle_f32_to_act(x)
+
+
+def test_shard_synthesis_is_a_block_of_the_full_tensor(L):
+    """A tensor-parallel rank synthesizes its rows or columns of each tensor:
+    the blocks equal the corresponding blocks of the full tensor (the shard
+    layout of iris_model_create_mistral_tp)."""
+    from iris_b200 import _lib
+    seed, rows, cols = 77, 48, 256
+    for per_block in (False, True):
+        full = _lib.synth_q8(seed, 9, 3, rows, cols, per_block).reshape(rows, cols // 32, 34)
+        for row0, nrows, col0, ncols in [(0, 48, 0, 256), (16, 16, 0, 256), (0, 48, 128, 128), (8, 24, 64, 96)]:
+            blk = _lib.synth_q8_block(seed, 9, 3, nrows, ncols, row0, col0, cols, per_block)
+            want = full[row0:row0 + nrows, col0 // 32:(col0 + ncols) // 32]
+            assert np.array_equal(blk.reshape(nrows, ncols // 32, 34), want), (row0, nrows, col0, ncols, per_block)

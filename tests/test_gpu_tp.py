@@ -1,0 +1,55 @@
+"""Tensor-parallel decode on two GPUs (iris_model_create_mistral_tp): the
+row-parallel o and down products exchange exact partial sums over NCCL, the
+head's vocabulary shards meet in a first-maximum reduction. Every token and
+every logit of a 2-way model must equal the CPU oracle's on the full model,
+through both decode loops (logits copied each pass; batched graph replays).
+Skipped with fewer than two GPUs."""
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def gpu_count():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("config,seed,prompt_len,steps", [("parity-mistral", 41, 19, 10)])
+def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps):
+    from iris_b200 import _lib, build
+    from iris_b200.model import synth_host_weights
+    from iris_b200.shapes import CONFIGS
+    from oracle import oracle
+    from oracle.models import OracleModel
+    build.build()
+    oracle.build()
+    nccl_id = _lib.tp_unique_id().hex()
+    out = tmp_path / "tp.npz"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, "-m", "iris_b200.tp_worker", "--rank", str(r), "--world", "2",
+                               "--id", nccl_id, "--config", config, "--seed", str(seed), "--prompt-seed", "3",
+                               "--prompt-len", str(prompt_len), "--steps", str(steps), "--out", str(out), "--untied"],
+                              cwd=ROOT, env=env) for r in range(2)]
+    try:
+        codes = [p.wait(timeout=600) for p in procs]
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    assert codes == [0, 0], codes
+    got = np.load(out)
+    cfg = CONFIGS[config]
+    cfg = type(cfg)(**{**cfg.__dict__, "tied": False})  # the head is sharded by vocabulary
+    want_tokens, want_logits = OracleModel(cfg, synth_host_weights(cfg, seed)).generate(got["prompt"].tolist(), steps)
+    assert got["tokens"].tolist() == want_tokens
+    assert got["tokens_graph"].tolist() == want_tokens
+    for p in range(len(want_tokens)):
+        assert np.array_equal(got["logits"][p], want_logits[p]), f"logits of pass {p}"
