@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--seed", type=int, default=0x1215B200)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
+                   help="N > 1: how decode passes exchange partial sums")
     return p.parse_args()
 
 
@@ -251,6 +253,7 @@ def main():
             idt.copy_(torch.frombuffer(bytearray(_lib.tp_unique_id()), dtype=torch.uint8))
         dist.broadcast(idt, 0)
         model = DeviceModel(cfg, seed=seed, tp=(rank, world, bytes(idt.cpu().numpy().tobytes())))
+        model.set_tp_exchange(args.tp_exchange)
     else:
         model = DeviceModel(cfg, seed=seed)
     e2e_steps = args.steps
@@ -334,6 +337,7 @@ def main():
         "config": {"workload": "mistral-7b-arch greedy decode after a 2048-token prompt (BASELINE config 4)",
                    "model": "mistral-7b-arch", "prompt": args.prompt, "context_at_start": ctx0,
                    "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
+                   "tp_exchange": args.tp_exchange if world > 1 else None,
                    "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(),
@@ -346,6 +350,7 @@ def main():
                 "api": "iris_session_decode (host token id in, host token id out)"},
         "gpu_launches": kernels * args.steps,
         "kernels_per_step": kernels,
+        "attention": sess.attention_plan,
         "prefill_tok_s": args.prompt / prefill_s,
         "clocks": clk,
     }

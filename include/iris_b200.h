@@ -159,6 +159,15 @@ int iris_model_create_mistral_tp(const IrisMistralShape* shape, uint32_t rank, u
                                  const uint8_t* nccl_id, IrisModel** out);
 /* A fresh NCCL unique id (128 bytes) for iris_model_create_mistral_tp. */
 int iris_tp_unique_id(uint8_t* out);
+/* How a tensor-parallel model exchanges the partial sums of its one-token
+ * (decode) row-parallel products: IRIS_TP_PEER (default; loads of the peers'
+ * memory over NVLink, world <= 8) or IRIS_TP_NCCL (an NCCL sum). Many-token
+ * passes always use NCCL. Sessions of a tensor-parallel model are used one at
+ * a time; sessions whose captured pass predates a change are rebuilt by the
+ * caller (iris_session_set_attention). */
+int iris_model_set_tp_exchange(IrisModel* model, int mode);
+#define IRIS_TP_PEER 0
+#define IRIS_TP_NCCL 1
 /* Uploads one Q8_0 tensor (layer = -1 for model-level tensors). */
 int iris_model_set_q8(IrisModel* model, int tensor, int32_t layer, const uint8_t* blocks,
                       uint64_t bytes);
@@ -233,6 +242,10 @@ int iris_session_set_attention(IrisSession* session, int mode);
  * and shared-memory tile buffers a block (2..12). IRIS_EINVAL when the shape
  * does not fit the model, the capacity or the device. */
 int iris_session_set_attention_shape(IrisSession* session, uint32_t cluster, uint32_t hpc, uint32_t ring);
+/* The decode attention in use: plan[0] = 3 (whole-GPU launch), 2 (cluster
+ * launch) or 1 (three launches); plan[1] query heads a block; plan[2] blocks
+ * a head group (whole-GPU) or a cluster; plan[3] positions a block at most. */
+int iris_session_attention_plan(const IrisSession* session, uint32_t* plan);
 /* Reads count K/V rows of one layer starting at position first
  * (kv_heads*head_dim values each). For a gemma sliding layer these are the
  * positions the window still holds. */

@@ -73,6 +73,7 @@ SIGNATURES = {
     "iris_model_create_gemma": (C.c_int, [C.POINTER(GemmaShape), C.POINTER(vp)]),
     "iris_model_create_mistral_tp": (C.c_int, [C.POINTER(MistralShape), C.c_uint32, C.c_uint32, u8p, C.POINTER(vp)]),
     "iris_tp_unique_id": (C.c_int, [u8p]),
+    "iris_model_set_tp_exchange": (C.c_int, [vp, C.c_int]),
     "iris_synth_q8_block": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.c_uint32,
                                       C.c_uint32, C.c_uint32, C.c_int, u8p]),
     "iris_model_set_q8": (C.c_int, [vp, C.c_int, C.c_int32, u8p, C.c_uint64]),
@@ -95,6 +96,7 @@ SIGNATURES = {
     "iris_session_product": (C.c_int, [vp, C.c_uint32, C.c_int]),
     "iris_session_attention": (C.c_int, [vp, C.c_uint32]),
     "iris_session_set_attention": (C.c_int, [vp, C.c_int]),
+    "iris_session_attention_plan": (C.c_int, [vp, C.POINTER(C.c_uint32)]),
     "iris_session_set_attention_shape": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32]),
     "iris_session_get_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i32p, i32p]),
     "iris_session_free": (None, [vp]),

@@ -122,6 +122,8 @@ struct IrisModel {
   // vocabulary (embedding table, token ids) and the NCCL communicator
   uint32_t tp_rank = 0, tp_world = 1, Vfull = 0;
   void* comm = nullptr;
+  TpExchange xch{};       // peer-memory exchange of one-token row-parallel products
+  bool xch_nccl = false;  // exchange one-token products over NCCL instead
 };
 
 struct IrisSession {
@@ -310,6 +312,13 @@ cudaError_t row_parallel_resid(IrisSession* s, ProductArgs a, uint32_t tokens) {
     a.out = s->x;
     a.resid = s->x;
     return launch_product(a, IN_PLANES, EPI_RESID, s->stream);
+  }
+  if (tokens == 1 && !m->xch_nccl) {  // one token: the peer-memory exchange
+    a.partial = m->xch.part;
+    a.xepoch = m->xch.epoch;
+    cudaError_t e = launch_product(a, IN_PLANES, EPI_PARTIAL, s->stream);
+    if (e == cudaSuccess) e = launch_tp_p2p_finish(m->xch, m->H, s->x, s->x, s->stream);
+    return e;
   }
   a.partial = s->partial;
   cudaError_t e = launch_product(a, IN_PLANES, EPI_PARTIAL, s->stream);
@@ -713,6 +722,7 @@ void iris_model_free(IrisModel* m) {
                     L.ple_post_norm, L.ple_gate, L.ple_proj, L.inv_freq};
     for (void* p : ptrs) cudaFree(p);
   }
+  if (m->xch.world) tp_exchange_free(&m->xch);
   tp_comm_free(m->comm);
   delete m;
 }
@@ -755,6 +765,7 @@ static int create_mistral(const IrisMistralShape* sh, uint32_t rank, uint32_t wo
   m->layers.resize(m->L);
   int rc = 0;
   if (world > 1) rc = (int)tp_comm_init(&m->comm, rank, world, nccl_id);
+  if (world > 1 && rc == 0) rc = (int)tp_exchange_setup(m->comm, rank, world, m->H, &m->xch, device_fault_word());
   if (rc == 0) rc = alloc_layers(m);
   if (rc == 0) rc = (int)dalloc(&m->freqs, m->d / 2);
   if (rc == 0)
@@ -774,8 +785,14 @@ int iris_model_create_mistral(const IrisMistralShape* sh, IrisModel** out) {
 
 int iris_model_create_mistral_tp(const IrisMistralShape* sh, uint32_t rank, uint32_t world, const uint8_t* nccl_id,
                                  IrisModel** out) {
-  if (!out) return IRIS_EINVAL;
+  if (!out || world > kTpMaxWorld) return IRIS_EINVAL;
   return create_mistral(sh, rank, world, nccl_id, out);
+}
+
+int iris_model_set_tp_exchange(IrisModel* m, int mode) {
+  if (!m || m->tp_world < 2 || (mode != IRIS_TP_PEER && mode != IRIS_TP_NCCL)) return IRIS_EINVAL;
+  m->xch_nccl = mode == IRIS_TP_NCCL;
+  return 0;
 }
 
 int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
@@ -1099,6 +1116,15 @@ int iris_session_set_attention(IrisSession* s, int mode) {
     attention_cluster_plan(m->heads, m->kvh, m->d, s->cap, &s->chpc, &s->cluster, &s->span, &s->ring);
   if (mode == IRIS_ATTN_AUTO) attention_grid_plan(m->heads, m->kvh, m->d, s->cap, &s->ghpc, &s->chunks, &s->gspan);
   return rebuild_graph_later(s);
+}
+
+int iris_session_attention_plan(const IrisSession* s, uint32_t* plan) {
+  if (!s || !plan) return IRIS_EINVAL;
+  plan[0] = s->chunks ? 3 : s->cluster ? 2 : 1;
+  plan[1] = s->chunks ? s->ghpc : s->cluster ? s->chpc : s->hpc;
+  plan[2] = s->chunks ? s->chunks : s->cluster;
+  plan[3] = s->chunks ? s->gspan : s->span;
+  return 0;
 }
 
 int iris_session_set_attention_shape(IrisSession* s, uint32_t cluster, uint32_t hpc, uint32_t ring) {

@@ -679,6 +679,10 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
 
   const uint32_t gfirst = ib / S, ngroups = nitems ? (ie - 1) / S - gfirst + 1 : 0;
   if (warp == kTmaEpilogueWarp) {
+    // EPI_PARTIAL into a double-buffered peer-exchange slot: the one of the
+    // coming exchange (epoch + 1)
+    int64_t* part = a.partial;
+    if (EPI == EPI_PARTIAL && a.xepoch) part += (size_t)((*a.xepoch + 1) & 1) * a.rows * 4;
     unsigned long long best = 0;
     for (uint32_t j = 0; j < ngroups; ++j) {
       const uint32_t sl = j % kTmaSlots, g = gfirst + j;
@@ -710,7 +714,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
       }
       if (EPI == EPI_PARTIAL) {
         const uint32_t row = g * kQ8TileRows + lane;
-        if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, a.partial + (size_t)row * 4);
+        if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, part + (size_t)row * 4);
       } else {
         gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
       }

@@ -87,6 +87,7 @@ struct ProductArgs {
   int32_t softcap;
   uint32_t row_base;         // global index of row 0 in first-maximum keys (vocabulary shards)
   int64_t* partial;          // EPI_PARTIAL: [tokens][rows][4] limbs
+  const uint32_t* xepoch;    // EPI_PARTIAL into a peer-exchange slot: partial + ((epoch + 1) & 1) rows 4
   // Decode GEMV split scratch (optional): 2 words a row and a slice count a
   // tile group for split_groups groups, all zero between launches.
   unsigned long long* split_acc;

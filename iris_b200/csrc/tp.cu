@@ -17,6 +17,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/iris_b200.h"
 #include "detnum.cuh"
@@ -78,9 +79,136 @@ __global__ void tp_finish_kernel(const int64_t* __restrict__ limbs, uint32_t tok
   out[i] = add_sat(acc128_round_q24(acc), resid[i]);
 }
 
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t ns_now() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// The peer-memory exchange of one row-parallel product (one token): this
+// rank's limbs are in its slot `parity` (written by the product); block 0
+// publishes them to every peer (release flag in the peer's memory), every
+// block waits - bounded - until every peer has published the same epoch,
+// then each thread sums its row's limbs over the ranks with loads from the
+// peers' memory (NVLink), rounds once and adds the residual. The last block
+// advances the epoch. Slots alternate by epoch parity: a rank rewrites a slot
+// only after every peer has published the next epoch, i.e. finished reading
+// this one.
+__global__ void tp_p2p_finish_kernel(TpExchange x, uint32_t rows, const int32_t* resid, int32_t* out) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ bool last_s;
+  const uint32_t epoch = *x.epoch + 1, parity = epoch & 1;
+  // The release store is cumulative over the product grid's writes of this
+  // rank's limbs, which the grid dependency made visible to this thread; a
+  // separate system fence before it cost ~3% of a decode step and adds nothing.
+  if (blockIdx.x == 0 && threadIdx.x < x.world && threadIdx.x != x.rank)
+    st_release_sys(x.peer_flags[threadIdx.x] + x.rank, epoch);
+  if (threadIdx.x < x.world && threadIdx.x != x.rank) {
+    const uint32_t* f = x.flags + threadIdx.x;
+    if (ld_acquire_sys(f) < epoch) {
+      const uint64_t t0 = ns_now();
+      for (uint32_t i = 1;; ++i) {  // the flag is in this GPU's memory: a tight poll stays in L2
+        if (ld_acquire_sys(f) >= epoch) break;
+        if ((i & 255) == 0 && ns_now() - t0 > 1000000000ull) {
+          if (x.fault) atomicOr(x.fault, 1u);
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row < rows) {
+    Acc128 acc{0, 0};
+    for (uint32_t j = 0; j < x.world; ++j) {
+      const int64_t* src = (j == x.rank ? x.part : x.peer_part[j]) + ((size_t)parity * rows + row) * 4;
+      const longlong2 a = __ldcg((const longlong2*)src), b = __ldcg((const longlong2*)(src + 2));
+      acc128_add(acc, (uint64_t)a.x, 0);
+      acc128_add(acc, (uint64_t)a.y << 32, (int64_t)((uint64_t)a.y >> 32));
+      acc128_add(acc, 0, b.x);
+      acc128_add(acc, 0, (int64_t)((uint64_t)b.y << 32));
+    }
+    out[row] = add_sat(acc128_round_q24(acc), resid[row]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) last_s = atomicAdd(x.done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (last_s && threadIdx.x == 0) {
+    *x.done = 0;
+    *x.epoch = epoch;
+  }
+}
+
 }  // namespace
 
 bool tp_available() { return nccl() != nullptr; }
+
+cudaError_t tp_exchange_setup(void* comm, uint32_t rank, uint32_t world, uint32_t rows, TpExchange* x,
+                              unsigned int* fault) {
+  *x = TpExchange{};
+  x->rank = rank;
+  x->world = world;
+  x->fault = fault;
+  if (world > kTpMaxWorld) return cudaErrorInvalidValue;
+  cudaError_t e = cudaMalloc((void**)&x->part, (size_t)2 * rows * 4 * sizeof(int64_t));
+  if (e == cudaSuccess) e = cudaMalloc((void**)&x->flags, kTpMaxWorld * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc((void**)&x->epoch, 2 * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(x->flags, 0, kTpMaxWorld * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(x->epoch, 0, 2 * sizeof(uint32_t));
+  x->done = x->epoch + 1;
+  // every rank's two IPC handles, gathered over NCCL
+  cudaIpcMemHandle_t mine[2];
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine[0], x->part);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine[1], x->flags);
+  uint8_t* dev = nullptr;
+  const size_t per = sizeof(mine);
+  if (e == cudaSuccess) e = cudaMalloc((void**)&dev, per * (world + 1));
+  if (e == cudaSuccess) e = cudaMemcpy(dev + per * world, mine, per, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = from_nccl(nccl()->all_gather(dev + per * world, dev, per, ncclInt8, (ncclComm_t)comm, 0));
+  std::vector<cudaIpcMemHandle_t> all(2 * world);
+  if (e == cudaSuccess) e = cudaMemcpy(all.data(), dev, per * world, cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  for (uint32_t j = 0; j < world && e == cudaSuccess; ++j) {
+    if (j == rank) {
+      x->peer_part[j] = x->part;
+      x->peer_flags[j] = x->flags;
+      continue;
+    }
+    void* p = nullptr;
+    e = cudaIpcOpenMemHandle(&p, all[2 * j], cudaIpcMemLazyEnablePeerAccess);
+    x->peer_part[j] = (int64_t*)p;
+    if (e == cudaSuccess) e = cudaIpcOpenMemHandle(&p, all[2 * j + 1], cudaIpcMemLazyEnablePeerAccess);
+    x->peer_flags[j] = (uint32_t*)p;
+  }
+  return e;
+}
+
+void tp_exchange_free(TpExchange* x) {
+  for (uint32_t j = 0; j < x->world; ++j) {
+    if (j == x->rank) continue;
+    if (x->peer_part[j]) cudaIpcCloseMemHandle(x->peer_part[j]);
+    if (x->peer_flags[j]) cudaIpcCloseMemHandle(x->peer_flags[j]);
+  }
+  cudaFree(x->part);
+  cudaFree(x->flags);
+  cudaFree(x->epoch);
+  *x = TpExchange{};
+}
+
+cudaError_t launch_tp_p2p_finish(const TpExchange& x, uint32_t rows, const int32_t* resid, int32_t* out,
+                                 cudaStream_t s) {
+  return launch_k(tp_p2p_finish_kernel, dim3((rows + 255) / 256), dim3(256), 0, s, x, rows, resid, out);
+}
 
 cudaError_t tp_unique_id(uint8_t* out) {
   const NcclApi* n = nccl();

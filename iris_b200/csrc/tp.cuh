@@ -6,6 +6,29 @@
 
 namespace iris {
 
+constexpr uint32_t kTpMaxWorld = 8;
+
+// Peer-memory exchange of one-token row-parallel products (tp.cu). Passed
+// by value to the finish kernel.
+struct TpExchange {
+  uint32_t rank, world;
+  int64_t* part;                    // this rank's two slots [2][rows][4] limbs
+  uint32_t* flags;                  // [world]: the last epoch each peer published
+  uint32_t* epoch;                  // exchanges finished; epoch + 1 is the coming one
+  uint32_t* done;                   // finish blocks done (last block advances the epoch)
+  int64_t* peer_part[kTpMaxWorld];  // every rank's slots (this rank's own at [rank])
+  uint32_t* peer_flags[kTpMaxWorld];
+  unsigned int* fault;
+};
+// Allocates the slots and flags, opens every peer's over CUDA IPC (handles
+// gathered over NCCL). Every rank calls it together.
+cudaError_t tp_exchange_setup(void* comm, uint32_t rank, uint32_t world, uint32_t rows, TpExchange* x,
+                              unsigned int* fault);
+void tp_exchange_free(TpExchange* x);
+// out[row] = add_sat(round_q24(sum over ranks of the slot limbs), resid[row]).
+cudaError_t launch_tp_p2p_finish(const TpExchange& x, uint32_t rows, const int32_t* resid, int32_t* out,
+                                 cudaStream_t s);
+
 bool tp_available();
 cudaError_t tp_unique_id(uint8_t* out);  // 128 bytes
 cudaError_t tp_comm_init(void** comm, uint32_t rank, uint32_t world, const uint8_t* id);

@@ -121,6 +121,10 @@ class DeviceModel:
     def handle(self):
         return self._h
 
+    def set_tp_exchange(self, mode: str) -> None:
+        """'peer' (NVLink loads of the peers' partial sums; default) or 'nccl'."""
+        check(lib().iris_model_set_tp_exchange(self._h, {"peer": 0, "nccl": 1}[mode]), "iris_model_set_tp_exchange")
+
     def load(self, weights: Dict[Key, np.ndarray]) -> None:
         table = tensor_table(self.cfg)
         for key, arr in weights.items():
@@ -200,6 +204,10 @@ class Session:
     def handle(self):
         return self._h
 
+    def set_tp_exchange(self, mode: str) -> None:
+        """'peer' (NVLink loads of the peers' partial sums; default) or 'nccl'."""
+        check(lib().iris_model_set_tp_exchange(self._h, {"peer": 0, "nccl": 1}[mode]), "iris_model_set_tp_exchange")
+
     def reset(self) -> None:
         check(lib().iris_session_reset(self._h), "iris_session_reset")
 
@@ -263,6 +271,14 @@ class Session:
         launches) or 'cluster' (the cluster launch where possible)."""
         check(lib().iris_session_set_attention(self._h, {"auto": 0, "split": 1, "cluster": 2}[mode]),
               "iris_session_set_attention")
+
+    @property
+    def attention_plan(self) -> dict:
+        """The decode attention in use (path, heads a block, blocks, positions a block)."""
+        plan = (C.c_uint32 * 4)()
+        check(lib().iris_session_attention_plan(self._h, plan), "iris_session_attention_plan")
+        return {"path": {3: "grid", 2: "cluster", 1: "split"}[plan[0]], "heads_per_block": plan[1],
+                "blocks": plan[2], "positions_per_block": plan[3]}
 
     def set_attention_shape(self, cluster: int, hpc: int, ring: int) -> None:
         """Explicit one-launch decode attention shape (tuning)."""

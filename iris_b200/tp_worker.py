@@ -1,7 +1,7 @@
 """One rank of a tensor-parallel decode, as a process (tests and tools).
 
   python -m iris_b200.tp_worker --rank R --world W --id HEX --config NAME \\
-      --seed S --prompt-seed P --prompt-len N --steps K --out FILE.npz [--untied]
+      --seed S --prompt-seed P --prompt-len N --steps K --out FILE.npz [--untied] [--exchange peer|nccl]
 
 Rank R uses CUDA device R, builds its shard of the seeded synthetic model,
 runs `Session.generate` twice (every pass's logits copied out, then the
@@ -32,6 +32,7 @@ def main() -> None:
     p.add_argument("--steps", type=int, default=8)
     p.add_argument("--out", required=True)
     p.add_argument("--untied", action="store_true", help="a separate head matrix (tensor parallelism shards it)")
+    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer")
     a = p.parse_args()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     import numpy as np
@@ -44,6 +45,7 @@ def main() -> None:
         cfg = type(cfg)(**{**cfg.__dict__, "tied": False})
     prompt = np.random.default_rng(a.prompt_seed).integers(0, cfg.vocab, size=a.prompt_len).tolist()
     dm = DeviceModel(cfg, seed=a.seed, tp=(a.rank, a.world, bytes.fromhex(a.id)))
+    dm.set_tp_exchange(a.exchange)
     sess = dm.session(a.prompt_len + a.steps + 8)
     toks, logits = sess.generate(prompt, a.steps, want_logits=True)
     toks2, _ = sess.generate(prompt, a.steps)

@@ -1,6 +1,8 @@
 """Tensor-parallel decode on two GPUs (iris_model_create_mistral_tp): the
-row-parallel o and down products exchange exact partial sums over NCCL, the
-head's vocabulary shards meet in a first-maximum reduction. Every token and
+row-parallel o and down products exchange exact partial sums (one-token
+passes through the peers' memory over NVLink, or over NCCL; many-token
+passes over NCCL), the head's vocabulary shards meet in a first-maximum
+reduction. Every token and
 every logit of a 2-way model must equal the CPU oracle's on the full model,
 through both decode loops (logits copied each pass; batched graph replays).
 Skipped with fewer than two GPUs."""
@@ -22,8 +24,9 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("config,seed,prompt_len,steps", [("parity-mistral", 41, 19, 10)])
-def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps):
+def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps, exchange):
     from iris_b200 import _lib, build
     from iris_b200.model import synth_host_weights
     from iris_b200.shapes import CONFIGS
@@ -36,7 +39,8 @@ def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, see
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs = [subprocess.Popen([sys.executable, "-m", "iris_b200.tp_worker", "--rank", str(r), "--world", "2",
                                "--id", nccl_id, "--config", config, "--seed", str(seed), "--prompt-seed", "3",
-                               "--prompt-len", str(prompt_len), "--steps", str(steps), "--out", str(out), "--untied"],
+                               "--prompt-len", str(prompt_len), "--steps", str(steps), "--out", str(out), "--untied",
+                               "--exchange", exchange],
                               cwd=ROOT, env=env) for r in range(2)]
     try:
         codes = [p.wait(timeout=600) for p in procs]
