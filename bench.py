@@ -48,6 +48,9 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="N > 1: how decode passes exchange partial sums")
+    p.add_argument("--decode-path", choices=["auto", "graph", "step"], default="auto",
+                   help="decode passes as the persistent step kernel (auto where the model allows) "
+                        "or as a CUDA graph of one kernel per operation")
     return p.parse_args()
 
 
@@ -99,10 +102,11 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def profiled_traffic():
+def profiled_traffic(name):
     """DRAM bytes (read + write) a launch of the roofline kernel moved in its
-    committed ncu capture (profiles/q8_gemv_gate_up_28672x4096.md), or None."""
-    path = ROOT / "profiles" / "q8_gemv_gate_up_28672x4096.md"
+    committed ncu capture (profiles/<name>, line traffic_bytes_per_launch),
+    or None."""
+    path = ROOT / "profiles" / name
     try:
         for line in path.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
@@ -259,6 +263,7 @@ def main():
     e2e_steps = args.steps
     cap = args.prompt + args.warmup + args.steps + e2e_steps + 8
     sess = model.session(cap)
+    sess.set_decode_path(args.decode_path)
     prompt = np.random.default_rng(seed).integers(0, cfg.vocab, size=args.prompt).tolist()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -304,10 +309,10 @@ def main():
         e2e_s = float(t.item())
     e2e_value = e2e_steps / e2e_s
 
-    # roofline of the dominant kernel: the decode GEMV over the fused gate|up
-    # matrix (28672 x 4096 Q8_0), one launch per layer (32 distinct 125 MB
-    # matrices, so nothing is served from L2), timed with events on the
-    # session's stream.
+    # The decode GEMV over the fused gate|up matrix (28672 x 4096 Q8_0) as its
+    # own launch, once per layer (32 distinct 125 MB matrices, so nothing is
+    # served from L2), timed with events on the session's stream: the roofline
+    # kernel of the graph path, reported beside the step kernel's.
     sess.product(0, 2)
     sess.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -326,6 +331,22 @@ def main():
     mean_ctx = ctx0 + (args.steps - 1) / 2.0 + 1
     step_bytes = algorithmic_bytes_per_step(cfg, mean_ctx)
     step_gbs = step_bytes / (ms_per_step / 1e3) / 1e9  # all ranks' bytes
+    gemv_roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": profiled_traffic("q8_gemv_gate_up_28672x4096.md"),
+                     "algorithmic_bytes": gemv_bytes,
+                     "kernel": "q8_gemv_tma_kernel<IN_NORM, EPI_SILU_MUL> (fused gate|up, 28672x4096)",
+                     "peak_kind": peak_kind}
+    path = sess.decode_path
+    if path == "step":
+        # the whole pass is one launch: its algorithmic bytes over the
+        # launch's average duration (events around the K timed launches)
+        roofline = {"bound": "hbm", "achieved": step_gbs, "peak": peak, "unit": "GB/s",
+                    "frac": step_gbs / peak, "traffic": profiled_traffic("decode_step_mistral7b.md"),
+                    "algorithmic_bytes": step_bytes,
+                    "kernel": "decode_step_kernel<16, 4> (persistent: the whole decode pass, one launch)",
+                    "peak_kind": peak_kind}
+    else:
+        roofline = gemv_roofline
 
     kernels = sess.kernels_per_pass
     line = {
@@ -339,11 +360,9 @@ def main():
                    "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
                    "tp_exchange": args.tp_exchange if world > 1 else None,
                    "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": profiled_traffic(),
-                     "algorithmic_bytes": gemv_bytes,
-                     "kernel": "q8_gemv_tma_kernel<IN_NORM, EPI_SILU_MUL> (fused gate|up, 28672x4096)",
-                     "peak_kind": peak_kind},
+        "roofline": roofline,
+        "gemv_roofline": gemv_roofline,
+        "decode_path": path,
         "step_roofline": {"achieved": step_gbs, "peak": peak * world, "unit": "GB/s",
                           "frac": step_gbs / (peak * world), "bytes_per_step": step_bytes},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,

@@ -203,21 +203,21 @@ int iris_session_decode(IrisSession* session, uint32_t token_in, int32_t* logits
  * max_tokens greedy selections, stopping after an EOS id or the budget (no
  * pass for the last token). out_tokens holds max_tokens entries; out_logits
  * (may be NULL) receives [passes][vocab], pass p being the scores that chose
- * out_tokens[p]. Decode passes replay one captured CUDA graph with the token
- * id kept on the device. */
+ * out_tokens[p]. Decode passes run on the device back to back (persistent
+ * step launches or graph replays) with the token id kept on the device. */
 int iris_generate(IrisSession* session, const uint32_t* prompt, uint32_t n_prompt,
                   uint32_t max_tokens, const uint32_t* eos, uint32_t n_eos, uint32_t* out_tokens,
                   uint32_t* out_count, int32_t* out_logits);
 /* Positions currently held. */
 uint32_t iris_session_length(const IrisSession* session);
-/* Device-resident decode loop: replays the captured decode pass `steps` times
- * on the session's stream without waiting (each pass feeds its first-maximum
+/* Device-resident decode loop: runs the decode pass `steps` times on the
+ * session's stream without waiting (each pass feeds its first-maximum
  * token to the next). iris_session_synchronize waits for them. */
 int iris_session_decode_steps(IrisSession* session, uint32_t steps);
 int iris_session_synchronize(IrisSession* session);
 /* The session's CUDA stream (cudaStream_t as void*), for timing with events. */
 void* iris_session_stream(IrisSession* session);
-/* Kernel launches in one captured decode pass. */
+/* Kernel launches in one decode pass (1 for the persistent step). */
 uint32_t iris_session_graph_kernels(IrisSession* session);
 /* Launches one decode product of layer `layer` on the session's stream
  * (which: 0 = fused q|k|v, 1 = o, 2 = gate|up, 3 = down, 4 = head) with the
@@ -227,12 +227,13 @@ int iris_session_product(IrisSession* session, uint32_t layer, int which);
  * stream: the last held position attends over the positions before it, with
  * the session's current query rows; the context is discarded. For timing. */
 int iris_session_attention(IrisSession* session, uint32_t layer);
-/* Selects the decode attention kernels of a session: IRIS_ATTN_AUTO (one
- * launch over the whole GPU where the shape and capacity allow it, else one
- * thread-block-cluster launch, else three launches), IRIS_ATTN_SPLIT (three
- * launches over position chunks) or IRIS_ATTN_CLUSTER (the cluster launch
- * where possible). All give the same values; the captured decode pass is
- * rebuilt. */
+/* Selects the decode attention kernels of the kernel-per-operation decode
+ * pass: IRIS_ATTN_AUTO (one launch over the whole GPU where the shape and
+ * capacity allow it, else one thread-block-cluster launch, else three
+ * launches), IRIS_ATTN_SPLIT (three launches over position chunks) or
+ * IRIS_ATTN_CLUSTER (the cluster launch where possible). All give the same
+ * values; the captured decode pass is rebuilt. SPLIT and CLUSTER also select
+ * that pass (IRIS_DECODE_GRAPH) over the persistent step. */
 int iris_session_set_attention(IrisSession* session, int mode);
 #define IRIS_ATTN_AUTO 0
 #define IRIS_ATTN_SPLIT 1
@@ -242,10 +243,40 @@ int iris_session_set_attention(IrisSession* session, int mode);
  * and shared-memory tile buffers a block (2..12). IRIS_EINVAL when the shape
  * does not fit the model, the capacity or the device. */
 int iris_session_set_attention_shape(IrisSession* session, uint32_t cluster, uint32_t hpc, uint32_t ring);
-/* The decode attention in use: plan[0] = 3 (whole-GPU launch), 2 (cluster
- * launch) or 1 (three launches); plan[1] query heads a block; plan[2] blocks
- * a head group (whole-GPU) or a cluster; plan[3] positions a block at most. */
+/* The decode attention in use: plan[0] = 4 (inside the persistent step), 3
+ * (whole-GPU launch), 2 (cluster launch) or 1 (three launches); plan[1] query
+ * heads a block; plan[2] blocks a head group (step, whole-GPU) or a cluster;
+ * plan[3] positions a block at most. */
 int iris_session_attention_plan(const IrisSession* session, uint32_t* plan);
+/* How decode passes run: IRIS_DECODE_AUTO (default: the persistent step where
+ * the model allows it, else the graph), IRIS_DECODE_GRAPH (a CUDA graph of
+ * one kernel per operation, ~5 a layer) or IRIS_DECODE_STEP (one cooperative
+ * launch a pass, one block a multiprocessor streaming every layer's weights
+ * through one shared-memory ring; mistral-dense without tensor parallelism;
+ * IRIS_EINVAL where the shape, capacity or device does not allow it). Both
+ * give the same values. */
+int iris_session_set_decode_path(IrisSession* session, int mode);
+#define IRIS_DECODE_AUTO 0
+#define IRIS_DECODE_GRAPH 1
+#define IRIS_DECODE_STEP 2
+/* The decode path in use: IRIS_DECODE_GRAPH or IRIS_DECODE_STEP. */
+int iris_session_decode_path(const IrisSession* session);
+/* The persistent step's launch plan: plan[0] = 0 when the session can use it,
+ * else why not (1 shape, 2 no kernel for the head shape, 3 device, 4 shared
+ * memory, 5 occupancy, 6 not a single-GPU mistral-dense model); then blocks,
+ * ring slots, bytes a slot, bytes of the planes region, dynamic shared
+ * memory, blocks a head group, positions a block at most (8 values). */
+int iris_session_step_plan(const IrisSession* session, uint32_t* plan);
+/* Profiling hook of the persistent step: with enable != 0 every pass records
+ * global-timer stamps (ns) per block and stage into a device buffer of
+ * blocks * stages * 8 values (blocks = plan[1], stages = 2 + 5 layers):
+ * 0 input ready, 7 share written; products: 1 prologue done, 2 warp 0's last
+ * tile taken, 6 the producer issued the last tile; attention: 1 first key
+ * slot landed, 2 scores done, 3 and 4 group exchanges passed, 5 value sums
+ * added, 6 the producer issued the last value row. iris_session_get_step_trace
+ * copies the last pass's out. */
+int iris_session_step_trace(IrisSession* session, int enable);
+int iris_session_get_step_trace(const IrisSession* session, uint64_t* out, uint64_t count);
 /* Reads count K/V rows of one layer starting at position first
  * (kv_heads*head_dim values each). For a gemma sliding layer these are the
  * positions the window still holds. */

@@ -19,6 +19,7 @@ IRIS_ESCRATCH = 10007
 NOALLOC_PLANES_BYTES = 16 << 20
 PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
 ATTN_AUTO, ATTN_SPLIT, ATTN_CLUSTER = 0, 1, 2
+DECODE_AUTO, DECODE_GRAPH, DECODE_STEP = 0, 1, 2
 
 # Tensor kinds (include/iris_b200.h)
 T = dict(EMBED=0, HEAD=1, FINAL_NORM=2, W_Q=3, W_K=4, W_V=5, W_O=6, W_GATE=7, W_UP=8, W_DOWN=9,
@@ -97,6 +98,11 @@ SIGNATURES = {
     "iris_session_attention": (C.c_int, [vp, C.c_uint32]),
     "iris_session_set_attention": (C.c_int, [vp, C.c_int]),
     "iris_session_attention_plan": (C.c_int, [vp, C.POINTER(C.c_uint32)]),
+    "iris_session_set_decode_path": (C.c_int, [vp, C.c_int]),
+    "iris_session_decode_path": (C.c_int, [vp]),
+    "iris_session_step_plan": (C.c_int, [vp, C.POINTER(C.c_uint32)]),
+    "iris_session_step_trace": (C.c_int, [vp, C.c_int]),
+    "iris_session_get_step_trace": (C.c_int, [vp, C.POINTER(C.c_uint64), C.c_uint64]),
     "iris_session_set_attention_shape": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32]),
     "iris_session_get_kv": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint32, i32p, i32p]),
     "iris_session_free": (None, [vp]),

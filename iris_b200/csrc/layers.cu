@@ -20,15 +20,6 @@
 
 namespace iris {
 
-__device__ __forceinline__ uint32_t window_start(uint32_t p, uint32_t window) {
-  // prefill_range.rs:866-874
-  if (window == 0) return 0;
-  return p + 1 > window ? p + 1 - window : 0;
-}
-
-__device__ __forceinline__ int32_t finish_score(int64_t sum, int mode, uint32_t scale) {
-  return mode == SCORE_MISTRAL ? scaled_score_finish(sum, scale) : requantize(sum);
-}
 
 __device__ __forceinline__ int64_t ldcg_i64(const int64_t* p) { return (int64_t)__ldcg((const long long*)p); }
 
@@ -340,14 +331,6 @@ struct TileCopier {
   }
 };
 
-// Warp-wide sums over the lanes that share lane % HPC; lane h < HPC ends with
-// the sum of head h's lanes.
-template <uint32_t HPC, typename T>
-__device__ __forceinline__ T head_lane_sum(T v) {
-#pragma unroll
-  for (uint32_t off = 16; off >= HPC; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  return v;
-}
 
 template <uint32_t PER, uint32_t HPC>
 __global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnArgs a) {
@@ -568,20 +551,6 @@ __global__ void __launch_bounds__(kCThreads, 1) attn_decode_cluster_kernel(AttnA
 
 constexpr uint32_t kGThreads = 256;
 
-__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int atom_add_acq_rel(unsigned int* p, unsigned int v) {
-  unsigned int old;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 
 // Arrival barrier of one head group: returns once *bar reaches target. The
 // block's earlier global atomics are published by the release arrival (after

@@ -135,4 +135,41 @@ cudaError_t launch_ple_prepare(const int32_t* projected, const Q8GpuMatrix* ple_
                                int32_t input_scale, uint32_t tokens, uint32_t layers, uint32_t P,
                                int32_t* out, cudaStream_t s);
 
+// ---- device helpers shared by the attention kernels (layers.cu, step.cu) ----
+
+// First position of the sliding window ending at p (prefill_range.rs:866-874).
+__device__ __forceinline__ uint32_t window_start(uint32_t p, uint32_t window) {
+  if (window == 0) return 0;
+  return p + 1 > window ? p + 1 - window : 0;
+}
+
+__device__ __forceinline__ int32_t finish_score(int64_t sum, int mode, uint32_t scale) {
+  return mode == SCORE_MISTRAL ? scaled_score_finish(sum, scale) : requantize(sum);
+}
+
+// Warp-wide sums over the lanes that share lane % HPC; lane h < HPC ends with
+// the sum of head h's lanes.
+template <uint32_t HPC, typename T>
+__device__ __forceinline__ T head_lane_sum(T v) {
+#pragma unroll
+  for (uint32_t off = 16; off >= HPC; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Device-scope acquire load, release reduction and acquire-release add of a
+// global 32-bit word (arrival counters between blocks of one launch).
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_add_release(unsigned int* p, unsigned int v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int atom_add_acq_rel(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 }  // namespace iris

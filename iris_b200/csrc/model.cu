@@ -23,6 +23,7 @@
 
 #include "../../include/iris_b200.h"
 #include "layers.cuh"
+#include "step.cuh"
 #include "tp.cuh"
 #include "synth.cuh"
 
@@ -157,6 +158,16 @@ struct IrisSession {
   unsigned long long* split_acc = nullptr;
   unsigned int* split_count = nullptr;
   uint32_t split_groups = 0;
+  // persistent decode step (step.cu): its plan, stage list and arrival counter
+  StepPlan step{};
+  StepStage* stages = nullptr;
+  uint32_t nstages = 0;
+  unsigned int* sync = nullptr;  // [nstages] arrival counters
+  unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
+  unsigned long long* sumsq = nullptr;  // [nstages][2] sums of squares of the residual stream
+  int decode_mode = IRIS_DECODE_AUTO;
+  int attn_mode = IRIS_ATTN_AUTO;
+  bool use_step = false;
   cudaStream_t stream = nullptr;
   cudaGraphExec_t graph = nullptr;
 };
@@ -171,10 +182,125 @@ void free_session(IrisSession* s) {
   void* ptrs[] = {s->kc, s->vc, s->x, s->tmp, s->q, s->qkv, s->xs, s->pg, s->ple_rows, s->ple_proj,
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
-                  s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full};
+                  s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
+                  s->stages, s->sync, s->trace, s->sumsq};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
+}
+
+// The stage list and launch plan of the persistent decode step
+// (mistral-dense without tensor parallelism); s->step.ok stays false when the
+// model or capacity needs the kernel-per-operation pass.
+cudaError_t setup_step(IrisSession* s) {
+  IrisModel* m = s->m;
+  s->step.why = 6;  // not a single-GPU mistral-dense model
+  if (m->family != kFamilyMistral || m->tp_world != 1 || !m->embed || !m->head) return cudaSuccess;
+  std::vector<StepStage> st;
+  std::vector<uint32_t> kcs;
+  auto product = [&](uint32_t kind, uint32_t layer, const Q8GpuMatrix* w, const int32_t* norm) {
+    StepStage x{};
+    x.q = w->q;
+    x.s = w->s;
+    x.norm_w = norm;
+    x.kind = kind;
+    x.layer = layer;
+    x.rows = w->rows;
+    x.cols = w->cols;
+    x.kc = w->kc;
+    x.nslices = w->nslices;
+    x.items = w->groups * w->nslices;
+    uint32_t lg = 0;  // as plan_gemv: S terms a lane stay below 2^62 for e <= 15 - ceil(log2 S)
+    while ((1u << lg) < w->nslices) ++lg;
+    x.e_fast = 15 - (int32_t)lg;
+    st.push_back(x);
+    kcs.push_back(w->kc);
+  };
+  auto plain = [&](uint32_t kind, uint32_t layer) {
+    StepStage x{};
+    x.kind = kind;
+    x.layer = layer;
+    st.push_back(x);
+  };
+  plain(STEP_EMBED, 0);
+  for (uint32_t l = 0; l < m->L; ++l) {
+    const LayerDev& L = m->layers[l];
+    if (!L.qkv || !L.o || !L.gu || !L.down) return cudaSuccess;
+    product(STEP_QKV, l, L.qkv, L.norm_attn);
+    plain(STEP_ATTN, l);
+    product(STEP_O, l, L.o, nullptr);
+    product(STEP_GU, l, L.gu, L.norm_ffn);
+    product(STEP_DOWN, l, L.down, nullptr);
+  }
+  product(STEP_HEAD, 0, m->head, m->final_norm);
+  StepPlan plan = plan_decode_step(m->H, m->F, m->heads, m->kvh, m->d, m->V, s->cap, kcs.data(), (uint32_t)kcs.size());
+  if (!plan.ok) {
+    s->step = plan;
+    return cudaSuccess;
+  }
+  cudaError_t e = dalloc(&s->stages, st.size());
+  if (e == cudaSuccess) e = cudaMemcpy(s->stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = dalloc(&s->sync, st.size());
+  if (e == cudaSuccess) e = cudaMemset(s->sync, 0, st.size() * sizeof(unsigned int));
+  if (e == cudaSuccess) e = dalloc(&s->sumsq, 2 * st.size());
+  if (e == cudaSuccess) e = cudaMemset(s->sumsq, 0, 2 * st.size() * sizeof(unsigned long long));
+  if (e != cudaSuccess) return e;
+  s->nstages = (uint32_t)st.size();
+  s->step = plan;
+  s->use_step = true;
+  return cudaSuccess;
+}
+
+// Arguments of one persistent decode step.
+StepArgs step_args(IrisSession* s) {
+  IrisModel* m = s->m;
+  StepArgs a{};
+  a.stages = s->stages;
+  a.nstages = s->nstages;
+  a.embed_q = m->embed->q;
+  a.embed_s = m->embed->s;
+  a.embed_kc = m->embed->kc;
+  a.embed_nslices = m->embed->nslices;
+  a.H = m->H;
+  a.heads = m->heads;
+  a.kv_heads = m->kvh;
+  a.d = m->d;
+  a.qd = m->qd;
+  a.kvd = m->kvd;
+  a.eps = m->eps;
+  a.scale_q32 = m->scale_q32;
+  a.freqs = m->freqs;
+  a.x = s->x;
+  a.q = s->q;
+  a.planes = s->planes;
+  a.planes2 = s->planes2;
+  a.kcache = s->kc;
+  a.vcache = s->vc;
+  a.cap = s->cap;
+  a.logits = s->logits;
+  a.best = s->best;
+  a.split_acc = s->split_acc;
+  a.split_count = s->split_count;
+  a.gbest = s->gbest;
+  a.gsum = s->gsum;
+  a.wsum = s->wsum;
+  a.acc = s->acc;
+  a.gbar = s->gbar;
+  a.chunks = s->step.chunks;
+  a.span_max = s->step.span_max;
+  a.d_token = s->d_token;
+  a.d_pos = s->d_pos;
+  a.d_step = s->d_step;
+  a.history = s->d_history;
+  a.history_cap = s->history_cap;
+  a.sync = s->sync;
+  a.fault = s->fault;
+  a.trace = s->trace;
+  a.sumsq = s->sumsq;
+  a.ring_slots = s->step.ring_slots;
+  a.slot_bytes = s->step.slot_bytes;
+  a.planes_bytes = s->step.planes_bytes;
+  return a;
 }
 
 int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
@@ -241,12 +367,18 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   if (e == cudaSuccess) e = cudaMemset(s->best, 0, R * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(s->d_pos, 0, 4);
   if (e == cudaSuccess) e = cudaMemset(s->d_step, 0, 4);
+  if (e == cudaSuccess) e = setup_step(s);
   if (e != cudaSuccess) {
     free_session(s);
     return (int)e;
   }
   *out = s;
   return 0;
+}
+
+// Whether decode passes run as the persistent step.
+void choose_decode_path(IrisSession* s) {
+  s->use_step = s->step.ok && s->decode_mode != IRIS_DECODE_GRAPH && s->attn_mode == IRIS_ATTN_AUTO;
 }
 
 // Product arguments with the session's GEMV split scratch.
@@ -566,6 +698,15 @@ int ensure_graph(IrisSession* s) {
 int decode_steps(IrisSession* s, uint32_t steps) {
   if (!s->has_logits) return IRIS_ESTATE;
   if ((uint64_t)s->len + steps > s->cap || (uint64_t)s->len + steps > s->m->max_positions) return IRIS_ERANGE;
+  if (s->use_step) {
+    const StepArgs a = step_args(s);
+    cudaError_t e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->sumsq, 0, 2 * s->nstages * sizeof(unsigned long long), s->stream);
+    for (uint32_t i = 0; i < steps && e == cudaSuccess; ++i) e = launch_decode_step(a, s->step, s->stream);
+    if (e != cudaSuccess) return (int)e;
+    s->len += steps;
+    return 0;
+  }
   int rc = ensure_graph(s);
   if (rc) return rc;
   for (uint32_t i = 0; i < steps; ++i) {
@@ -1070,6 +1211,7 @@ int iris_session_synchronize(IrisSession* s) {
 void* iris_session_stream(IrisSession* s) { return s ? (void*)s->stream : nullptr; }
 
 uint32_t iris_session_graph_kernels(IrisSession* s) {
+  if (s && s->use_step) return 1;
   if (!s || ensure_graph(s)) return 0;
   cudaGraph_t g = nullptr;
   // Count kernel nodes by re-capturing the pass into a throwaway graph
@@ -1115,11 +1257,63 @@ int iris_session_set_attention(IrisSession* s, int mode) {
   if (mode != IRIS_ATTN_SPLIT)
     attention_cluster_plan(m->heads, m->kvh, m->d, s->cap, &s->chpc, &s->cluster, &s->span, &s->ring);
   if (mode == IRIS_ATTN_AUTO) attention_grid_plan(m->heads, m->kvh, m->d, s->cap, &s->ghpc, &s->chunks, &s->gspan);
+  s->attn_mode = mode;
+  choose_decode_path(s);
   return rebuild_graph_later(s);
+}
+
+int iris_session_set_decode_path(IrisSession* s, int mode) {
+  if (!s || mode < IRIS_DECODE_AUTO || mode > IRIS_DECODE_STEP) return IRIS_EINVAL;
+  if (mode == IRIS_DECODE_STEP && !s->step.ok) return IRIS_EINVAL;
+  s->decode_mode = mode;
+  if (mode == IRIS_DECODE_STEP) s->attn_mode = IRIS_ATTN_AUTO;
+  choose_decode_path(s);
+  return 0;
+}
+
+int iris_session_decode_path(const IrisSession* s) {
+  if (!s) return IRIS_EINVAL;
+  return s->use_step ? IRIS_DECODE_STEP : IRIS_DECODE_GRAPH;
+}
+
+int iris_session_step_trace(IrisSession* s, int enable) {
+  if (!s || !s->step.ok) return IRIS_EINVAL;
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return (int)e;
+  cudaFree(s->trace);
+  s->trace = nullptr;
+  if (!enable) return 0;
+  const size_t n = (size_t)s->step.blocks * s->nstages * kStepTraceEvents;
+  e = dalloc(&s->trace, n);
+  if (e == cudaSuccess) e = cudaMemset(s->trace, 0, n * sizeof(unsigned long long));
+  return (int)e;
+}
+
+int iris_session_get_step_trace(const IrisSession* s, uint64_t* out, uint64_t count) {
+  if (!s || !s->trace || !out) return IRIS_EINVAL;
+  const size_t n = (size_t)s->step.blocks * s->nstages * kStepTraceEvents;
+  if (count < n) return IRIS_EINVAL;
+  return (int)cudaMemcpy(out, s->trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+}
+
+int iris_session_step_plan(const IrisSession* s, uint32_t* plan) {
+  if (!s || !plan) return IRIS_EINVAL;
+  const StepPlan& p = s->step;
+  const uint32_t v[8] = {p.ok ? 0u : (p.why ? p.why : 1u), p.blocks, p.ring_slots, p.slot_bytes, p.planes_bytes,
+                         p.smem, p.chunks, p.span_max};
+  for (int i = 0; i < 8; ++i) plan[i] = v[i];
+  return 0;
 }
 
 int iris_session_attention_plan(const IrisSession* s, uint32_t* plan) {
   if (!s || !plan) return IRIS_EINVAL;
+  if (s->use_step) {
+    plan[0] = 4;
+    plan[1] = s->step.hpc;
+    plan[2] = s->step.chunks;
+    plan[3] = s->step.span_max;
+    return 0;
+  }
   plan[0] = s->chunks ? 3 : s->cluster ? 2 : 1;
   plan[1] = s->chunks ? s->ghpc : s->cluster ? s->chpc : s->hpc;
   plan[2] = s->chunks ? s->chunks : s->cluster;
@@ -1137,6 +1331,8 @@ int iris_session_set_attention_shape(IrisSession* s, uint32_t cluster, uint32_t 
   s->ring = ring;
   s->span = span;
   s->chunks = 0;
+  s->attn_mode = IRIS_ATTN_CLUSTER;
+  choose_decode_path(s);
   return rebuild_graph_later(s);
 }
 

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/iris_b200.h"
+#include "gemv.cuh"
 #include "q8.cuh"
 #include "synth.cuh"
 
@@ -241,87 +242,6 @@ cudaError_t synth_values_dev(int32_t* dst, uint64_t seed, uint32_t tensor, int32
 // Byte planes
 // ---------------------------------------------------------------------------
 
-// Block-wide saturating sum of non-negative values (result valid in thread 0).
-__device__ uint64_t block_sum_sat(uint64_t v, uint64_t* red) {
-  v = warp_sum_sat_nonneg(v);
-  int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  uint64_t t = 0;
-  if (threadIdx.x < 32) {
-    t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0;
-    t = warp_sum_sat_nonneg(t);
-  }
-  return t;
-}
-
-// Builds the byte planes of one K-wide row into `planes` (shared or global),
-// RMS-normalising first when norm_w is given (ops.rs:98-114: two mul_sat per
-// value, by the inverse-RMS scale and then by the weight).
-__device__ bool row_to_planes(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
-                              int64_t eps, uint32_t K, uint8_t* planes, uint64_t* red,
-                              int32_t* s_scale) {
-  // Rows of up to kHeld values a thread are held in registers, the values and
-  // the norm weights loaded together: one pass over global memory.
-  constexpr uint32_t kHeld = 2;  // int4 pieces a thread
-  const uint32_t step = blockDim.x * 4;
-  const bool held = K <= kHeld * step;
-  int4 xv[kHeld], wv[kHeld];
-  if (held) {
-#pragma unroll
-    for (uint32_t j = 0; j < kHeld; ++j) {
-      const uint32_t i = threadIdx.x * 4 + j * step;
-      xv[j] = i < K ? *(const int4*)(x + i) : make_int4(0, 0, 0, 0);
-      wv[j] = i < K && norm_w ? *(const int4*)(norm_w + i) : make_int4(0, 0, 0, 0);
-    }
-  }
-  int32_t scale = 0;
-  if (norm_w) {
-    uint64_t ss = 0;
-    auto square_sum = [&](int4 v) {
-      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.x * v.x));
-      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.y * v.y));
-      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.z * v.z));
-      ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.w * v.w));
-    };
-    if (held) {
-#pragma unroll
-      for (uint32_t j = 0; j < kHeld; ++j) square_sum(xv[j]);
-    } else {
-      for (uint32_t i = threadIdx.x * 4; i < K; i += step) square_sum(*(const int4*)(x + i));
-    }
-    uint64_t total = block_sum_sat(ss, red);  // in every lane of warp 0
-    if (threadIdx.x < 32) {  // rms_scale_from_sumsq with the warp-parallel inverse square root
-      const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), eps));
-      if (threadIdx.x == 0) *s_scale = sc;
-    }
-    __syncthreads();
-    scale = *s_scale;
-  }
-  int wide = 0;
-  auto emit = [&](int4 v, int4 w, uint32_t i) {
-    if (norm_w) {
-      v.x = mul_sat(mul_sat(v.x, scale), w.x);
-      v.y = mul_sat(mul_sat(v.y, scale), w.y);
-      v.z = mul_sat(mul_sat(v.z, scale), w.z);
-      v.w = mul_sat(mul_sat(v.w, scale), w.w);
-    }
-    wide |= !fits_three_planes(v.x) | !fits_three_planes(v.y) | !fits_three_planes(v.z) | !fits_three_planes(v.w);
-    put_planes4(planes, K, i, v);
-  };
-  if (held) {
-#pragma unroll
-    for (uint32_t j = 0; j < kHeld; ++j) {
-      const uint32_t i = threadIdx.x * 4 + j * step;
-      if (i < K) emit(xv[j], wv[j], i);
-    }
-  } else {
-    for (uint32_t i = threadIdx.x * 4; i < K; i += step)
-      emit(*(const int4*)(x + i), norm_w ? *(const int4*)(norm_w + i) : make_int4(0, 0, 0, 0), i);
-  }
-  return __syncthreads_or(wide) != 0;
-}
-
 __global__ void planes_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ norm_w,
                               int64_t eps, uint32_t K, uint8_t* planes) {
   pdl_wait();
@@ -336,56 +256,6 @@ cudaError_t launch_planes(const int32_t* x, const int32_t* norm_w, int64_t eps, 
                           uint32_t cols, uint8_t* planes, cudaStream_t stream) {
   if (tokens == 0) return cudaSuccess;
   return launch_k(planes_kernel, dim3(tokens), dim3(256), 0, stream, x, norm_w, eps, cols, planes);
-}
-
-// ---------------------------------------------------------------------------
-// Epilogue helpers shared by both kernels
-// ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t token_position(const ProductArgs& a, uint32_t t) {
-  return (a.pos_ptr ? *a.pos_ptr : a.pos0) + t;
-}
-
-// A finished (even, odd) row pair of a paired epilogue for token t.
-template <int EPI>
-__device__ __forceinline__ void epi_pair(const ProductArgs& a, uint32_t t, uint32_t row, int32_t v0,
-                                         int32_t v1) {
-  if (EPI == EPI_QKV_ROPE) {
-    uint32_t pos = token_position(a, t);
-    if (row < a.qd) {
-      rotate_pair_q30(&v0, &v1, a.freqs[(row % a.head_dim) >> 1], pos);
-      int32_t* o = a.out + (size_t)t * a.out_stride + row;
-      o[0] = v0;
-      o[1] = v1;
-    } else if (row < a.qd + a.kvd) {
-      uint32_t c = row - a.qd;
-      rotate_pair_q30(&v0, &v1, a.freqs[(c % a.head_dim) >> 1], pos);
-      int32_t* o = a.kcache + (size_t)pos * a.kvd + c;
-      o[0] = v0;
-      o[1] = v1;
-    } else {
-      uint32_t c = row - a.qd - a.kvd;
-      int32_t* o = a.vcache + (size_t)pos * a.kvd + c;
-      o[0] = v0;
-      o[1] = v1;
-    }
-  } else {  // gated: v0 = gate_j, v1 = up_j
-    int32_t g = EPI == EPI_SILU_MUL ? silu(v0) : gelu_tanh(v0);
-    int32_t y = mul_sat(g, v1);
-    uint32_t F = a.rows >> 1;
-    put_planes(a.out_planes + (size_t)t * 4 * F, F, row >> 1, y);
-  }
-}
-
-template <int EPI>
-__device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uint32_t row, int32_t v) {
-  size_t o = (size_t)t * a.out_stride + row;
-  if (EPI == EPI_STORE) a.out[o] = v;
-  else if (EPI == EPI_RESID) a.out[o] = add_sat(v, a.resid[o]);
-  else if (EPI == EPI_LOGITS) {
-    if (a.softcap > 0) v = softcap_act(v, a.softcap);
-    if (a.out) a.out[o] = v;
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -419,28 +289,6 @@ __device__ __forceinline__ void epi_single(const ProductArgs& a, uint32_t t, uin
 
 __device__ unsigned int g_fault;
 
-constexpr int kTmaConsumerWarps = 16;
-constexpr int kTmaEpilogueWarp = kTmaConsumerWarps + 1;
-constexpr int kTmaThreads = (kTmaConsumerWarps + 2) * 32;
-constexpr int kTmaRowsPerWarp = 2;
-constexpr uint32_t kTmaMaxStages = 8;
-constexpr uint32_t kTmaSlots = 4;  // tile groups between the consumers and the epilogue warp
-constexpr uint32_t kTmaSmemBudget = 220 * 1024;
-
-struct GemvPlan {
-  uint32_t stages;
-  uint32_t stage_bytes;      // tile values (16 kc) + tile scales (kc), rounded to 128
-  uint32_t planes_bytes;     // 4 K, rounded to 128
-  uint32_t items;            // tiles of the matrix: groups * nslices
-  uint32_t groups_per_block; // whole-group ranges (split == 0)
-  uint32_t split;            // even item ranges through the split scratch
-  int32_t e_fast;            // largest scale exponent of the 64-bit accumulator (-1: none)
-  uint32_t smem;
-  uint32_t grid;
-};
-
-__host__ __device__ inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
-
 bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, bool split, GemvPlan* p) {
   if (K % 32 || rows == 0 || kc == 0) return false;
   p->planes_bytes = round_up(4 * K, 128);
@@ -469,121 +317,6 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, bool split, Gemv
   return true;
 }
 
-// One warp's share of a tile: two rows, one 32-value block b of the slice a
-// lane (a half slice is at most 32 blocks). The lane first copies its weights
-// and scale bits out of the stage into registers, so that the warp can release
-// the stage before the products run and the producer refills it at once.
-// Lanes 4-7 of every quarter-warp take the two 16-byte chunks in the other
-// order, so that each 8-lane phase of a 128-bit shared load touches 8
-// different 16-byte bank groups (the block sum does not depend on the order).
-struct RowBlocks {
-  uint4 wa[kTmaRowsPerWarp], wb[kTmaRowsPerWarp];
-  uint16_t sc[kTmaRowsPerWarp];
-};
-
-__device__ __forceinline__ void gemv_take_rows(const uint8_t* __restrict__ W, const uint16_t* __restrict__ Sc,
-                                               uint32_t kc, uint32_t b, uint32_t lane, RowBlocks& rb) {
-  const uint32_t blocks = kc / 32, swap = (lane >> 2) & 1;
-  const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
-#pragma unroll
-  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-    rb.wa[r] = *(const uint4*)(W + r * kc + c0 * 16);
-    rb.wb[r] = *(const uint4*)(W + r * kc + c1 * 16);
-    rb.sc[r] = Sc[r * blocks + b];
-  }
-}
-
-// The exact block sums of one lane's block for its two rows, times the
-// scales, into the row accumulators. Three planes (|a| < 2^23): one dp4a
-// chain a plane over the whole block (|s0|, |s1| < 2^20, |s2| < 2^19), then
-// p = (s0 + 256 s1) m + 2^16 (s2 m) with |p| < 2^46.1; a term p 2^e with
-// e <= e_fast goes to a 64-bit accumulator (the plan bounds the terms a lane
-// adds for a row so that their sum stays below 2^62), any other to the
-// 128-bit one. Four planes: the 128-bit path throughout.
-template <bool kThree>
-__device__ __forceinline__ void gemv_rows_product(const RowBlocks& rb, const uint4* __restrict__ P0,
-                                                  const uint4* __restrict__ P1, const uint4* __restrict__ P2,
-                                                  const uint4* __restrict__ P3, uint32_t cbase, uint32_t b,
-                                                  uint32_t lane, int32_t e_fast, Acc128* acc, int64_t* fast) {
-  const uint32_t swap = (lane >> 2) & 1;
-  const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
-  const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
-  const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1];
-  uint4 pa3, pb3;
-  if (!kThree) {
-    pa3 = P3[cbase + c0];
-    pb3 = P3[cbase + c1];
-  }
-#pragma unroll
-  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-    int32_t m, e;
-    q8_scale_parts(rb.sc[r], &m, &e);  // finite: checked at upload (padding rows: 0)
-    if (kThree) {
-      const uint4 wa = rb.wa[r], wb = rb.wb[r];
-      int s0 = dp4a_su(wa.x, pa0.x, 0), s1 = dp4a_su(wa.x, pa1.x, 0), s2 = dp4a_ss(wa.x, pa2.x, 0);
-      s0 = dp4a_su(wa.y, pa0.y, s0), s1 = dp4a_su(wa.y, pa1.y, s1), s2 = dp4a_ss(wa.y, pa2.y, s2);
-      s0 = dp4a_su(wa.z, pa0.z, s0), s1 = dp4a_su(wa.z, pa1.z, s1), s2 = dp4a_ss(wa.z, pa2.z, s2);
-      s0 = dp4a_su(wa.w, pa0.w, s0), s1 = dp4a_su(wa.w, pa1.w, s1), s2 = dp4a_ss(wa.w, pa2.w, s2);
-      s0 = dp4a_su(wb.x, pb0.x, s0), s1 = dp4a_su(wb.x, pb1.x, s1), s2 = dp4a_ss(wb.x, pb2.x, s2);
-      s0 = dp4a_su(wb.y, pb0.y, s0), s1 = dp4a_su(wb.y, pb1.y, s1), s2 = dp4a_ss(wb.y, pb2.y, s2);
-      s0 = dp4a_su(wb.z, pb0.z, s0), s1 = dp4a_su(wb.z, pb1.z, s1), s2 = dp4a_ss(wb.z, pb2.z, s2);
-      s0 = dp4a_su(wb.w, pb0.w, s0), s1 = dp4a_su(wb.w, pb1.w, s1), s2 = dp4a_ss(wb.w, pb2.w, s2);
-      const int64_t p = (int64_t)(s0 + s1 * 256) * m + ((int64_t)(s2 * m) << 16);
-      if (e <= e_fast) fast[r] += (int64_t)((uint64_t)p << e);
-      else acc128_add_shifted(acc[r], p, e);
-    } else {
-      const int64_t bs = q8_partial16(rb.wa[r], pa0, pa1, pa2, pa3) + q8_partial16(rb.wb[r], pb0, pb1, pb2, pb3);
-      acc128_add_shifted(acc[r], bs * m, e);
-    }
-  }
-}
-
-// Item range [*ib, *ie) of block b.
-__device__ __forceinline__ void gemv_range(const GemvPlan& p, uint32_t S, uint32_t groups, uint32_t b,
-                                           uint32_t* ib, uint32_t* ie) {
-  if (p.split) {
-    *ib = (uint32_t)((uint64_t)b * p.items / p.grid);
-    *ie = (uint32_t)((uint64_t)(b + 1) * p.items / p.grid);
-  } else {
-    const uint32_t g0 = b * p.groups_per_block, g1 = min(groups, g0 + p.groups_per_block);
-    *ib = g0 * S;
-    *ie = g0 < g1 ? g1 * S : g0 * S;
-  }
-}
-
-// Exact 128-bit addition into the split scratch (two 64-bit words a row).
-__device__ __forceinline__ void atomic_add_acc128(unsigned long long* dst, Acc128 v) {
-  const unsigned long long old = atomicAdd(dst, (unsigned long long)v.lo);
-  const unsigned long long carry = old + v.lo < old ? 1ull : 0ull;
-  atomicAdd(dst + 1, (unsigned long long)v.hi + carry);
-}
-
-// The epilogue of one finished tile group: lane l < 16 holds the rounded value
-// of row g * 16 + l.
-template <int EPI>
-__device__ __forceinline__ void gemv_group_epilogue(const ProductArgs& a, uint32_t g, int32_t v, uint32_t lane,
-                                                    unsigned long long* best) {
-  const uint32_t row0 = g * kQ8TileRows;
-  if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
-    // pairs (2j, 2j + 1): lane j < 8 takes pair j
-    const int32_t v0 = __shfl_sync(0xffffffffu, v, (2 * lane) & 31);
-    const int32_t v1 = __shfl_sync(0xffffffffu, v, (2 * lane + 1) & 31);
-    const uint32_t row = row0 + 2 * lane;
-    if (lane < kQ8TileRows / 2 && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
-  } else if (EPI == EPI_LOGITS) {
-    const uint32_t row = row0 + lane;
-    if (lane < kQ8TileRows && row < a.rows) {
-      const int32_t c = a.softcap > 0 ? softcap_act(v, a.softcap) : v;
-      if (a.out) a.out[row] = c;
-      const unsigned long long key = best_key(c, row + a.row_base);
-      *best = key > *best ? key : *best;
-    }
-  } else {
-    const uint32_t row = row0 + lane;
-    if (lane < kQ8TileRows && row < a.rows) epi_single<EPI>(a, 0, row, v);
-  }
-}
-
 template <int IN, int EPI>
 __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs a, GemvPlan p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -593,16 +326,15 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   __shared__ __align__(8) uint64_t slot_empty[kTmaSlots];
   __shared__ uint64_t red[32];
   __shared__ int32_t s_scale;
-  __shared__ Acc128 slot_sums[kTmaSlots][2][kQ8TileRows];  // [slot][half][row of the tile]
+  __shared__ Acc128 slot_sums[kTmaSlots][2][kQ8TileRows];
   const uint32_t K = a.cols, kc = a.kc, S = a.nslices;
   uint8_t* planes = smem;
-  uint8_t* stage0 = smem + p.planes_bytes;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool producer = warp == kTmaConsumerWarps;
   const uint32_t groups = (a.rows + kQ8TileRows - 1) / kQ8TileRows;
   uint32_t ib, ie;
   gemv_range(p, S, groups, blockIdx.x, &ib, &ie);
-  const uint32_t nitems = ie - ib;
+  const TileRing ring{smem + p.planes_bytes, p.stage_bytes, p.stages, full, empty};
+  const SumRing sums{slot_full, slot_empty, slot_sums};
 
   if (threadIdx.x == 0) {
     for (uint32_t st = 0; st < p.stages; ++st) {
@@ -617,21 +349,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   }
   __syncthreads();
 
-  const uint64_t policy = l2_evict_first_policy();
-  // Item k of the range is tile ib + k: the tiles of a range are consecutive.
-  auto issue = [&](uint32_t item, uint32_t st) {
-    const size_t tile = (size_t)ib + item;
-    uint8_t* dst = stage0 + st * p.stage_bytes;
-    mbar_arrive_expect_tx(&full[st], kQ8TileRows * kc + kc);
-    bulk_load(dst, a.q + tile * kQ8TileRows * kc, kQ8TileRows * kc, &full[st], policy);
-    bulk_load(dst + kQ8TileRows * kc, (const uint8_t*)a.s + tile * kc, kc, &full[st], policy);
-  };
-
-  // Weights never change: the first stages stream while the previous kernel
+  // Weights never change: the first tiles stream while the previous kernel
   // of the stream finishes; the activations are read only after pdl_wait().
-  const uint32_t first = nitems < p.stages ? nitems : p.stages;
-  if (producer && lane == 0)
-    for (uint32_t item = 0; item < first; ++item) issue(item, item);
+  RingCursor pc{0, 1, 0};
+  const uint64_t policy = l2_evict_first_policy();
+  const uint32_t first = min(ie, ib + p.stages);
+  if (warp == kTmaConsumerWarps && lane == 0) ring_issue<false>(ring, pc, a.q, a.s, kc, ib, first, policy, &g_fault);
   pdl_wait();
   pdl_trigger();
 
@@ -641,7 +364,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
     const uint4* src = (const uint4*)a.planes;
     int w = 0;
     for (uint32_t i = threadIdx.x; i < K / 16; i += blockDim.x) {
-      const uint4 v0 = src[i], v1 = src[K / 16 + i], v2 = src[2 * (K / 16) + i], v3 = src[3 * (K / 16) + i];
+      const uint4 v0 = __ldcg(src + i), v1 = __ldcg(src + K / 16 + i), v2 = __ldcg(src + 2 * (K / 16) + i),
+                  v3 = __ldcg(src + 3 * (K / 16) + i);
       ((uint4*)planes)[i] = v0;
       ((uint4*)planes)[K / 16 + i] = v1;
       ((uint4*)planes)[2 * (K / 16) + i] = v2;
@@ -654,142 +378,16 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
     wide = row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, planes, red, &s_scale);
   }
 
-  if (producer) {
-    if (lane == 0) {
-      uint32_t issued = first, st = 0, phase = 0;  // stage of item `first`, parity of its release
-      bool stalled = false;
-      for (uint32_t item = first; item < nitems; ++item) {
-        if (!mbar_wait_bounded(&empty[st], phase, &g_fault)) {
-          stalled = true;
-          break;
-        }
-        issue(item, st);
-        issued = item + 1;
-        if (++st == p.stages) {
-          st = 0;
-          phase ^= 1;
-        }
-      }
-      if (stalled)  // let the copies already issued land before the block exits
-        for (uint32_t item = issued > p.stages ? issued - p.stages : 0; item < issued; ++item)
-          mbar_wait_bounded(&full[item % p.stages], (item / p.stages) & 1, &g_fault);
-    }
-    return;
-  }
-
-  const uint32_t gfirst = ib / S, ngroups = nitems ? (ie - 1) / S - gfirst + 1 : 0;
-  if (warp == kTmaEpilogueWarp) {
-    // EPI_PARTIAL into a double-buffered peer-exchange slot: the one of the
-    // coming exchange (epoch + 1)
-    int64_t* part = a.partial;
-    if (EPI == EPI_PARTIAL && a.xepoch) part += (size_t)((*a.xepoch + 1) & 1) * a.rows * 4;
-    unsigned long long best = 0;
-    for (uint32_t j = 0; j < ngroups; ++j) {
-      const uint32_t sl = j % kTmaSlots, g = gfirst + j;
-      if (!mbar_wait_bounded(&slot_full[sl], (j / kTmaSlots) & 1, &g_fault)) return;
-      Acc128 v = Acc128{0, 0};
-      if (lane < kQ8TileRows) {
-        v = slot_sums[sl][0][lane];
-        if (kTmaConsumerWarps == 16) acc128_add(v, slot_sums[sl][1][lane].lo, slot_sums[sl][1][lane].hi);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&slot_empty[sl]);
-      const uint32_t lo = max(ib, g * S), hi = min(ie, (g + 1) * S);
-      if (hi - lo < S) {  // a share of a group split between blocks
-        unsigned long long* acc = a.split_acc + (size_t)g * kQ8TileRows * 2;
-        if (lane < kQ8TileRows) atomic_add_acc128(acc + 2 * lane, v);
-        __threadfence();
-        __syncwarp();
-        uint32_t done = 0;
-        if (lane == 0) done = atomicAdd(a.split_count + g, hi - lo) + (hi - lo) == S;
-        if (!__shfl_sync(0xffffffffu, done, 0)) continue;
-        __threadfence();
-        if (lane < kQ8TileRows) {
-          v.lo = (uint64_t)__ldcg(acc + 2 * lane);
-          v.hi = (int64_t)__ldcg(acc + 2 * lane + 1);
-          acc[2 * lane] = 0;
-          acc[2 * lane + 1] = 0;
-        }
-        if (lane == 0) a.split_count[g] = 0;
-      }
-      if (EPI == EPI_PARTIAL) {
-        const uint32_t row = g * kQ8TileRows + lane;
-        if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, part + (size_t)row * 4);
-      } else {
-        gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
-      }
-    }
-    if (EPI == EPI_LOGITS) {
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
-        best = o > best ? o : best;
-      }
-      if (lane == 0 && best) atomicMax(a.best, best);
-    }
-    return;
-  }
-
-  const uint4* P0 = (const uint4*)planes;
-  const uint4* P1 = P0 + K / 16;
-  const uint4* P2 = P1 + K / 16;
-  const uint4* P3 = P2 + K / 16;
-  // Warp w: rows 2 (w % 8) and 2 (w % 8) + 1 of each tile; with sixteen
-  // consumer warps, blocks of the slice's first half (w < 8) or second half
-  // (w >= 8), with eight the whole slice.
-  constexpr uint32_t kHalves = kTmaConsumerWarps / 8;
-  static_assert(kHalves == 2, "a lane takes one block a row: 2048-value slices need two halves");
-  const uint32_t pair = warp % 8, half = warp / 8;
-  const uint32_t lr0 = kTmaRowsPerWarp * pair, blocks = kc / 32, mid = kHalves == 2 ? (blocks + 1) / 2 : blocks;
-  const uint32_t b0 = half ? mid : 0, b1 = half ? blocks : mid;
-  Acc128 acc[kTmaRowsPerWarp];
-  int64_t fast[kTmaRowsPerWarp];
-#pragma unroll
-  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-    acc[r] = Acc128{0, 0};
-    fast[r] = 0;
-  }
-  uint32_t j = 0;        // tile groups finished
-  bool stalled = false;  // after a given-up wait: keep pace with the barriers, skip the waits
-  // stage, its fill parity and the slice of the current item, kept without divisions
-  uint32_t st = 0, phase = 0, sl = ib % S;
-  for (uint32_t item = 0; item < nitems; ++item) {
-    if (!stalled && !mbar_wait_bounded(&full[st], phase, &g_fault)) stalled = true;
-    const uint8_t* W = stage0 + st * p.stage_bytes + lr0 * kc;
-    const uint16_t* Sc = (const uint16_t*)(stage0 + st * p.stage_bytes + kQ8TileRows * kc) + lr0 * blocks;
-    const uint32_t cbase = sl * (kc / 16), b = b0 + lane;
-    RowBlocks rb;
-    if (b < b1) gemv_take_rows(W, Sc, kc, b, lane, rb);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);  // the stage is in registers: refill it
-    if (++st == p.stages) {
-      st = 0;
-      phase ^= 1;
-    }
-    if (b < b1) {
-      if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, p.e_fast, acc, fast);
-      else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, p.e_fast, acc, fast);
-    }
-    if (++sl == S) sl = 0;
-    if (sl == 0 || item + 1 == nitems) {
-#pragma unroll
-      for (int r = 0; r < kTmaRowsPerWarp; ++r) {
-        acc128_add(acc[r], (uint64_t)fast[r], fast[r] >> 63);
-        acc[r] = warp_sum_acc128(acc[r]);
-        fast[r] = 0;
-      }
-      const uint32_t slot = j % kTmaSlots;
-      if (j >= kTmaSlots && !stalled && !mbar_wait_bounded(&slot_empty[slot], (j / kTmaSlots - 1) & 1, &g_fault))
-        stalled = true;
-      if (lane == 0) {
-        slot_sums[slot][half][lr0] = acc[0];
-        slot_sums[slot][half][lr0 + 1] = acc[1];
-        mbar_arrive(&slot_full[slot]);
-      }
-      ++j;
-#pragma unroll
-      for (int r = 0; r < kTmaRowsPerWarp; ++r) acc[r] = Acc128{0, 0};
-    }
+  uint32_t j = 0;
+  if (warp == kTmaConsumerWarps) {
+    if (lane == 0 && !ring_issue<false>(ring, pc, a.q, a.s, kc, first, ie, policy, &g_fault))
+      ring_drain(ring, pc, &g_fault);  // let the copies already issued land before the block exits
+  } else if (warp == kTmaEpilogueWarp) {
+    ring_epilogue<EPI, false>(a, sums, j, ib, ie, S, &g_fault);
+  } else {
+    RingCursor cc{0, 0, 0};
+    bool stalled = false;
+    ring_consume<false>(ring, cc, sums, j, planes, wide, K, kc, S, p.e_fast, ib, ie, stalled, &g_fault);
   }
 }
 

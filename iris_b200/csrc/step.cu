@@ -1,0 +1,799 @@
+// The persistent decode step for mistral-dense models: one cooperative launch
+// of one block per multiprocessor runs the whole pass of one token.
+//
+// The kernel-per-operation pass (model.cu) pays, at every one of its ~160
+// kernel boundaries, the ramp and drain of a weight stream: the next product
+// can only prefetch what fits beside the previous kernel's blocks, and the
+// HBM pipe idles while the last tiles, the epilogue and the next prologue
+// run. Here each block keeps ONE tile ring (gemv.cuh) for the whole pass:
+// its producer lane walks the block's share of every matrix of every layer
+// in pass order and never waits for data, only for free slots, so while the
+// consumers wait for a stage's input (the arrival barrier below), attend, or
+// normalise, the ring keeps filling with the next product's weights - about
+// 20 MB across the GPU, several microseconds of HBM time.
+//
+// Stages (StepKind) run in pass order: embedding, then per layer q|k|v with
+// RoPE and the cache store, attention, o with the residual, gate|up with
+// SiLU gating, down with the residual, then the head and the greedy choice.
+// Every block arrives once per stage on the stage's global counter after its
+// share of the stage is written (release); a stage's consumers start after
+// all blocks arrived at the stage before (acquire). Products split their
+// tiles over the blocks in whole tile groups, so each block rounds its groups
+// once and applies the fused epilogue itself, exactly as the one-product
+// kernel does. The attention of a head group is split over `chunks` blocks
+// that meet through global exchange words (first maximum, exp sums, value
+// sums) with bounded group barriers, as in the whole-GPU attention kernel
+// (layers.cu). The residual epilogues also leave the exact sum of squares of
+// the stream they wrote, so a normalised input needs no block-wide reduction.
+// The last block to arrive at the head stage selects the next token,
+// advances the position and clears the counters for the next launch.
+//
+// All blocks must be resident at once: the launch is cooperative. Every wait
+// is bounded (about one second); after any recorded fault every later wait
+// gives up at once, so a stalled pass drains in milliseconds and the host
+// reports IRIS_ESTALL.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "gemv.cuh"
+#include "step.cuh"
+
+namespace iris {
+
+namespace {
+
+constexpr uint32_t kStepConsumers = kTmaConsumerWarps * 32;  // threads of the consumer warps
+constexpr int kStepProducerWarp = kTmaConsumerWarps;
+constexpr int kStepEpilogueWarp = kTmaEpilogueWarp;
+
+__device__ __forceinline__ bool step_is_product(uint32_t kind) { return kind != STEP_EMBED && kind != STEP_ATTN; }
+
+// Tiles [*ib, *ie) of a product stage for block b of nb: whole tile groups,
+// spread evenly (the counts differ by at most one group). Splitting groups
+// between blocks would balance exactly but end every stage with an exchange
+// of partial sums through L2 (dependent atomics, a fence, a re-read), which
+// costs more than one group's stream.
+__device__ __forceinline__ void step_range(const StepStage& st, uint32_t b, uint32_t nb, uint32_t* ib,
+                                           uint32_t* ie) {
+  const uint32_t groups = st.items / st.nslices;
+  *ib = (uint32_t)((uint64_t)b * groups / nb) * st.nslices;
+  *ie = (uint32_t)((uint64_t)(b + 1) * groups / nb) * st.nslices;
+}
+
+// Optional timeline stamp (one thread of the block).
+__device__ __forceinline__ void step_stamp(const StepArgs& A, uint32_t k, uint32_t ev) {
+  if (A.trace) A.trace[((size_t)blockIdx.x * A.nstages + k) * kStepTraceEvents + ev] = global_ns();
+}
+
+// Bounded poll of a global arrival counter (one thread).
+__device__ __forceinline__ void step_poll(const unsigned int* ctr, unsigned int target, unsigned int* fault) {
+  if (ld_acquire_u32(ctr) >= target) return;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_u32(ctr) >= target) return;
+    if ((i & 63) == 0) {
+      if (*(volatile unsigned int*)fault) return;
+      if (global_ns() - t0 > 1000000000ull) {
+        atomicOr(fault, 1u);
+        return;
+      }
+    }
+  }
+}
+
+// Consumer warps: every block has arrived at stage k - 1. Every stage has
+// work for at least one block, and a block with work at a stage has waited
+// for the stage before, so this also orders every earlier stage.
+__device__ __forceinline__ void step_wait(const StepArgs& A, uint32_t k) {
+  if (threadIdx.x == 0) {
+    step_poll(A.sync + k - 1, gridDim.x, A.fault);
+    step_stamp(A, k, 0);
+  }
+  part_sync<kStepConsumers>();
+}
+
+// Consumer warps: this block's share of stage k is written.
+__device__ __forceinline__ void step_consumers_arrive(const StepArgs& A, uint32_t k) {
+  part_sync<kStepConsumers>();
+  if (threadIdx.x == 0) {
+    step_stamp(A, k, 7);
+    __threadfence();
+    red_add_release(A.sync + k, 1u);
+  }
+}
+
+// x = dequantize_row(embed[token]) (q8.rs:76-91); blocks take 512 values
+// each and add the squares of theirs into the stage's sum of squares.
+__device__ __forceinline__ void step_embed(const StepArgs& A) {
+  const uint32_t tok = *A.d_token;
+  Acc128 sq{0, 0};
+  for (uint32_t i = blockIdx.x * kStepConsumers + threadIdx.x; i < A.H; i += gridDim.x * kStepConsumers) {
+    int32_t m, e;
+    q8_scale_parts(A.embed_s[q8_scale_offset(A.embed_kc, A.embed_nslices, tok, i >> 5)], &m, &e);
+    const int32_t v = q8_dequant(A.embed_q[q8_value_offset(A.embed_kc, A.embed_nslices, tok, i)], m, e);
+    A.x[i] = v;
+    acc128_add(sq, (uint64_t)((int64_t)v * v), 0);
+  }
+  sq = warp_sum_acc128(sq);
+  if ((threadIdx.x & 31) == 0 && (sq.lo | (uint64_t)sq.hi)) atomic_add_acc128(A.sumsq, sq);
+}
+
+// The byte planes of rms_norm(x) (ops.rs:98-114) for a product whose input is
+// the residual stream written by stage k - 1, which also left the 128-bit
+// sum of the squares of x: the norm's sum of squares saturates at i64::MAX
+// term by term (add_sat_nonneg), which for non-negative terms is the exact
+// sum clamped to i64::MAX. wv holds this thread's
+// norm weights (loaded before the stage's wait); x is read through L2.
+template <uint32_t kHeld>
+__device__ __forceinline__ bool step_norm_planes(const StepArgs& A, uint32_t k, uint32_t K, const int4 (&wv)[kHeld],
+                                                 const int32_t* norm_w, uint8_t* planes, int32_t* s_scale) {
+  constexpr uint32_t step = kStepConsumers * 4;
+  const bool held = K <= kHeld * step;
+  int4 xv[kHeld];
+  if (held) {
+#pragma unroll
+    for (uint32_t j = 0; j < kHeld; ++j) {
+      const uint32_t i = threadIdx.x * 4 + j * step;
+      xv[j] = i < K ? __ldcg((const int4*)(A.x + i)) : make_int4(0, 0, 0, 0);
+    }
+  }
+  if (threadIdx.x < 32) {
+    const uint64_t lo = __ldcg(A.sumsq + 2 * (k - 1)), hi = __ldcg(A.sumsq + 2 * (k - 1) + 1);
+    const uint64_t total = (hi || lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : lo;
+    const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), A.eps));
+    if (threadIdx.x == 0) *s_scale = sc;
+  }
+  part_sync<kStepConsumers>();
+  if (threadIdx.x == 0) step_stamp(A, k, 3);
+  const int32_t scale = *s_scale;
+  int wide = 0;
+  auto emit = [&](int4 v, int4 w, uint32_t i) {
+    v.x = mul_sat(mul_sat(v.x, scale), w.x);
+    v.y = mul_sat(mul_sat(v.y, scale), w.y);
+    v.z = mul_sat(mul_sat(v.z, scale), w.z);
+    v.w = mul_sat(mul_sat(v.w, scale), w.w);
+    wide |= !fits_three_planes(v.x) | !fits_three_planes(v.y) | !fits_three_planes(v.z) | !fits_three_planes(v.w);
+    put_planes4(planes, K, i, v);
+  };
+  if (held) {
+#pragma unroll
+    for (uint32_t j = 0; j < kHeld; ++j) {
+      const uint32_t i = threadIdx.x * 4 + j * step;
+      if (i < K) emit(xv[j], wv[j], i);
+    }
+  } else {
+    for (uint32_t i = threadIdx.x * 4; i < K; i += step)
+      emit(__ldcg((const int4*)(A.x + i)), __ldg((const int4*)(norm_w + i)), i);
+  }
+  if (threadIdx.x == 0) step_stamp(A, k, 4);
+  return part_or<kStepConsumers>(wide);
+}
+
+// Activation planes written by an earlier stage -> shared memory; true when
+// some value needs the fourth plane.
+__device__ __forceinline__ bool step_copy_planes(const uint8_t* src8, uint32_t K, uint8_t* planes) {
+  const uint4* src = (const uint4*)src8;
+  int w = 0;
+  for (uint32_t i = threadIdx.x; i < K / 16; i += kStepConsumers) {
+    const uint4 v0 = __ldcg(src + i), v1 = __ldcg(src + K / 16 + i), v2 = __ldcg(src + 2 * (K / 16) + i),
+                v3 = __ldcg(src + 3 * (K / 16) + i);
+    ((uint4*)planes)[i] = v0;
+    ((uint4*)planes)[K / 16 + i] = v1;
+    ((uint4*)planes)[2 * (K / 16) + i] = v2;
+    ((uint4*)planes)[3 * (K / 16) + i] = v3;
+    w |= !planes_sign_extended(v2.x, v3.x) | !planes_sign_extended(v2.y, v3.y) |
+         !planes_sign_extended(v2.z, v3.z) | !planes_sign_extended(v2.w, v3.w);
+  }
+  return part_or<kStepConsumers>(w);
+}
+
+// The epilogue arguments of product stage k.
+__device__ __forceinline__ ProductArgs step_product_args(const StepArgs& A, const StepStage& st, uint32_t k,
+                                                         uint32_t p) {
+  ProductArgs a{};
+  a.rows = st.rows;
+  a.cols = st.cols;
+  a.tokens = 1;
+  a.kc = st.kc;
+  a.nslices = st.nslices;
+  a.out_stride = st.rows;
+  a.split_acc = A.split_acc;
+  a.split_count = A.split_count;
+  a.split_groups = 0;
+  if (st.kind == STEP_QKV) {
+    a.out = A.q;
+    a.out_stride = A.qd;
+    a.freqs = A.freqs;
+    a.head_dim = A.d;
+    a.qd = A.qd;
+    a.kvd = A.kvd;
+    a.kcache = A.kcache + (size_t)st.layer * A.cap * A.kvd;
+    a.vcache = A.vcache + (size_t)st.layer * A.cap * A.kvd;
+    a.pos0 = p;
+  } else if (st.kind == STEP_O || st.kind == STEP_DOWN) {
+    a.out = A.x;
+    a.resid = A.x;
+    a.sumsq = A.sumsq + 2 * k;  // for the normalised input of stage k + 1
+  } else if (st.kind == STEP_GU) {
+    a.out_planes = A.planes2;
+  } else {  // STEP_HEAD
+    a.out = A.logits;
+    a.best = A.best;
+  }
+  return a;
+}
+
+// Greedy bookkeeping of the pass (generation.rs:25-58), by the last block.
+__device__ __forceinline__ void step_finish(const StepArgs& A, uint32_t p) {
+  const uint32_t tok = best_key_token(__ldcg(A.best));
+  *A.d_token = tok;
+  *A.best = 0;
+  const uint32_t step = *A.d_step;
+  if (A.history && step < A.history_cap) A.history[step] = tok;
+  *A.d_step = step + 1;
+  *A.d_pos = p + 1;
+  for (uint32_t k = 0; k < A.nstages; ++k) {
+    A.sync[k] = 0;
+    A.sumsq[2 * k] = 0;
+    A.sumsq[2 * k + 1] = 0;
+  }
+}
+
+// ---- attention stage --------------------------------------------------------
+
+template <uint32_t HPC>
+struct StepAttnShared {
+  unsigned long long best[HPC], sum[HPC], gbest[HPC], gtot[HPC], ginv[HPC];
+  int32_t wsum[HPC], resid[HPC];
+  bool last;
+};
+
+// Bounded arrival barrier of the `chunks` blocks of one head group.
+__device__ __forceinline__ void step_group_barrier(unsigned int* bar, unsigned int target, unsigned int* fault) {
+  part_sync<kStepConsumers>();
+  if (threadIdx.x == 0) {
+    red_add_release(bar, 1u);
+    step_poll(bar, target, fault);
+  }
+  part_sync<kStepConsumers>();
+}
+
+// This block's share of the attention of a decode pass: the head group and
+// the chunk [r0, r1) of positions [0, p] (empty when r0 = p + 1); rows
+// [r0, rc), rc = max(r0, min(r1, p)) (written by earlier passes) travel
+// through the tile ring, row p (written by this pass's q|k|v stage) is read
+// from the cache by the consumers.
+struct AttnChunk {
+  bool active;
+  uint32_t h0, g, r0, r1, rc;
+  unsigned int* bar;
+};
+template <uint32_t HPC>
+__device__ __forceinline__ AttnChunk attn_chunk(const StepArgs& A, uint32_t p) {
+  AttnChunk c{};
+  const uint32_t groups = A.heads / HPC, chunks = A.chunks;
+  c.active = blockIdx.x < groups * chunks;
+  if (!c.active) return c;
+  const uint32_t grp = blockIdx.x / chunks, rank = blockIdx.x % chunks;
+  c.h0 = grp * HPC;
+  c.g = c.h0 / (A.heads / A.kv_heads);
+  const uint32_t n = p + 1, span = (n + chunks - 1) / chunks;
+  c.r0 = min(n, rank * span);
+  c.r1 = min(n, c.r0 + span);
+  c.rc = max(c.r0, min(c.r1, p));  // an empty chunk (r0 = p + 1) copies nothing
+  c.bar = A.gbar + grp;
+  return c;
+}
+
+// Producer warp: the chunk's cached key rows, then its value rows, into ring
+// slots (slot_bytes / (4 D) rows a slot, one bulk copy a row, the warp's 32
+// lanes issuing a slot's copies together). Lane 0 waits for the slot and arms
+// its barrier; every lane keeps the same cursor.
+template <uint32_t PER, uint32_t HPC>
+__device__ __forceinline__ bool step_issue_kv(const StepArgs& A, const TileRing& ring, RingCursor& pc, uint32_t layer,
+                                              uint32_t p, uint64_t policy) {
+  constexpr uint32_t D = PER * 8;
+  const AttnChunk c = attn_chunk<HPC>(A, p);
+  if (!c.active) return true;
+  const uint32_t lane = threadIdx.x & 31, per_slot = ring.slot_bytes / (D * 4);
+  const size_t base = (size_t)layer * A.cap * A.kvd + (size_t)c.g * D;
+  for (int kv = 0; kv < 2; ++kv) {
+    const int32_t* src = (kv ? A.vcache : A.kcache) + base;
+    for (uint32_t a = c.r0; a < c.rc; a += per_slot) {
+      const uint32_t n = min(per_slot, c.rc - a);
+      uint32_t ok = 1;
+      if (lane == 0) {
+        ok = pc.count < ring.slots || ring_wait<true>(&ring.empty[pc.slot], pc.parity, A.fault);
+        if (ok) mbar_arrive_expect_tx(&ring.full[pc.slot], n * D * 4);
+      }
+      if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
+      uint8_t* dst = ring.base + pc.slot * ring.slot_bytes;
+      for (uint32_t i = lane; i < n; i += 32)
+        bulk_load(dst + i * D * 4, src + (size_t)(a + i) * A.kvd, D * 4, &ring.full[pc.slot], policy);
+      ring_advance(ring, pc);
+    }
+  }
+  return true;
+}
+
+// attention_softmax (ops.rs:233-261) for the HPC query heads of one group
+// over this block's chunk of positions; the same three exchanges as
+// attn_decode_grid_kernel (first maximum, exp sums, weighted value sums, each
+// through global words of the head group), with the chunk's key and value
+// rows taken from ring slots in shared memory (the producer copied them
+// ahead, while the q|k|v stage ran) and the scores, exp terms and weights in
+// shared `scratch`.
+template <uint32_t PER, uint32_t HPC>
+__device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, uint32_t layer, uint32_t p,
+                                               uint8_t* scratch, StepAttnShared<HPC>& sh, const TileRing& ring,
+                                               RingCursor& cc, bool& stalled) {
+  constexpr uint32_t D = PER * 8, kWarps = kStepConsumers / 32, DL = D / 32;
+  static_assert(DL >= 1 && HPC * DL <= 16, "value sums a lane");
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const AttnChunk c = attn_chunk<HPC>(A, p);
+  if (!c.active) return;
+  const uint32_t h0 = c.h0, g = c.g, r0 = c.r0, cnt = c.r1 - c.r0, nsm = c.rc - c.r0;
+  const bool has_p = cnt > nsm;  // row p is this chunk's last row
+  const uint32_t per_slot = ring.slot_bytes / (D * 4);
+  const size_t lay = (size_t)layer * A.cap * A.kvd;
+  int32_t* sw = (int32_t*)scratch;                                           // [span][HPC] scores, then weights
+  uint64_t* tm = (uint64_t*)(scratch + round_up(A.span_max * HPC * 4, 16));  // [span][HPC] exp terms
+  uint64_t* tree = tm + A.span_max * HPC;  // [kWarps / 2][HPC DL][32] partial value sums
+  unsigned int* bar = c.bar;
+
+  if (tid < HPC) {
+    sh.best[tid] = 0;
+    sh.sum[tid] = 0;
+    sh.wsum[tid] = 0;
+  }
+  // Scores: LPP lanes a position (NV interleaved int4 chunks each, so that a
+  // position's lanes read its key row contiguously), PW positions a warp.
+  constexpr uint32_t LPP = D / 4 < 16 ? D / 4 : 16, NV = D / LPP / 4, PW = 32 / LPP;
+  const uint32_t pl = lane % LPP, pslot = lane / LPP;
+  int4 q[HPC][NV];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < NV; ++i) q[h][i] = __ldcg((const int4*)(A.q + (size_t)(h0 + h) * D + 4 * (pl + LPP * i)));
+  part_sync<kStepConsumers>();
+
+  // ---- 1. scores and each head's first maximum
+  unsigned long long best[HPC];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
+  // The scores of local row t (all lanes of the warp take part in the
+  // sums): each lane's HPC partial dot products are summed over the
+  // position's LPP lanes with a halving exchange, after which lane pl holds
+  // head pl / (LPP / HPC)'s total and one lane a head finishes its score.
+  constexpr uint32_t LPH = LPP / HPC;  // lanes that end with the same head
+  static_assert(HPC <= LPP, "a head's sum per lane group");
+  auto score = [&](const int4* kv, bool live, uint32_t t) {
+    uint64_t v[HPC];
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      int64_t c0 = 0, c1 = 0;
+#pragma unroll
+      for (uint32_t i = 0; i < NV; ++i) {
+        mac_wide(c0, q[h][i].x, kv[i].x);
+        mac_wide(c1, q[h][i].y, kv[i].y);
+        mac_wide(c0, q[h][i].z, kv[i].z);
+        mac_wide(c1, q[h][i].w, kv[i].w);
+      }
+      v[h] = (uint64_t)c0 + (uint64_t)c1;
+    }
+#pragma unroll
+    for (uint32_t n = HPC, off = LPP / 2; n > 1; n >>= 1, off >>= 1) {
+      const bool upper = (pl & off) != 0;
+#pragma unroll
+      for (uint32_t i = 0; i < n / 2; ++i) {
+        const uint64_t send = upper ? v[i] : v[i + n / 2];
+        const uint64_t keep = upper ? v[i + n / 2] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    uint64_t sum = v[0];
+#pragma unroll
+    for (uint32_t off = LPH / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (pl % LPH == 0 && live) {
+      const uint32_t h = pl / LPH;
+      const int32_t sc = finish_score((int64_t)sum, SCORE_MISTRAL, A.scale_q32);
+      sw[t * HPC + h] = sc;
+      const unsigned long long key = best_key(sc, r0 + t);
+#pragma unroll
+      for (uint32_t hh = 0; hh < HPC; ++hh)
+        if (hh == h) best[hh] = key > best[hh] ? key : best[hh];
+    }
+  };
+  for (uint32_t sb = 0; sb < nsm; sb += per_slot) {
+    const uint32_t nrows = min(per_slot, nsm - sb);
+    if (!stalled && !ring_wait<true>(&ring.full[cc.slot], cc.parity, A.fault)) stalled = true;
+    if (sb == 0 && tid == 0) step_stamp(A, k, 1);
+    const int32_t* ks = (const int32_t*)(ring.base + cc.slot * ring.slot_bytes);
+    for (uint32_t base = 0; base < nrows; base += kWarps * PW) {
+      const uint32_t t = base + warp * PW + pslot;
+      const bool live = t < nrows;
+      int4 kv[NV];
+#pragma unroll
+      for (uint32_t i = 0; i < NV; ++i)
+        kv[i] = live ? *(const int4*)(ks + t * D + 4 * (pl + LPP * i)) : make_int4(0, 0, 0, 0);
+      score(kv, live, sb + t);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[cc.slot]);  // the slot's key rows are used
+    ring_advance(ring, cc);
+  }
+  if (has_p && warp == 0) {  // row p, written by this pass: from the cache, through L2
+    const bool live = pslot == 0;
+    int4 kv[NV];
+#pragma unroll
+    for (uint32_t i = 0; i < NV; ++i)
+      kv[i] = live ? __ldcg((const int4*)(A.kcache + lay + (size_t)p * A.kvd + g * D + 4 * (pl + LPP * i)))
+                   : make_int4(0, 0, 0, 0);
+    score(kv, live, nsm);
+  }
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+    if (best[h]) atomicMax(&sh.best[h], best[h]);
+  part_sync<kStepConsumers>();
+  if (tid < HPC && sh.best[tid]) atomicMax(A.gbest + h0 + tid, sh.best[tid]);
+  if (tid == 0) step_stamp(A, k, 2);
+  step_group_barrier(bar, A.chunks, A.fault);
+  if (tid == 0) step_stamp(A, k, 3);
+  if (tid < HPC) sh.gbest[tid] = __ldcg(A.gbest + h0 + tid);
+  part_sync<kStepConsumers>();
+
+  // ---- 2. exp terms against the group's first maximum, their sums.
+  // Element e = position * HPC + head: thread tid always meets head tid % HPC.
+  const uint32_t my_h = tid % HPC;
+  {
+    const int32_t mx = best_key_value(sh.gbest[my_h]);
+    uint64_t e = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kStepConsumers) {
+      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
+      tm[el] = term;
+      e += term;
+    }
+    e = head_lane_sum<HPC>(e);
+    if (lane < HPC && e) atomicAdd(&sh.sum[lane], (unsigned long long)e);
+  }
+  part_sync<kStepConsumers>();
+  if (tid < HPC && sh.sum[tid]) atomicAdd(A.gsum + h0 + tid, sh.sum[tid]);
+  step_group_barrier(bar, 2 * A.chunks, A.fault);
+  if (tid == 0) step_stamp(A, k, 4);
+  if (tid < HPC) {
+    const unsigned long long tot = __ldcg(A.gsum + h0 + tid);
+    sh.gtot[tid] = tot;
+    sh.ginv[tid] = tot ? UINT64_MAX / tot : 0;  // tot >= 2^32 after a complete exchange
+  }
+  part_sync<kStepConsumers>();
+
+  // ---- 3. weights and their sums, then the value sums: warp w takes rows w,
+  // w + 16, ... of each slot, lane l dimensions [l DL, (l + 1) DL) of each
+  {
+    const uint64_t tot = sh.gtot[my_h], inv = sh.ginv[my_h];
+    int32_t wsum = 0;
+    for (uint32_t el = tid; el < cnt * HPC; el += kStepConsumers) {
+      const int32_t w = tot ? softmax_weight_inv((int64_t)tm[el], tot, inv) : 0;
+      sw[el] = w;
+      wsum += w;
+    }
+    wsum = head_lane_sum<HPC>(wsum);
+    if (lane < HPC && wsum) atomicAdd(&sh.wsum[lane], wsum);
+  }
+  part_sync<kStepConsumers>();
+  if (tid < HPC && sh.wsum[tid]) atomicAdd(A.wsum + h0 + tid, sh.wsum[tid]);
+  uint64_t acc[HPC][DL];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < DL; ++i) acc[h][i] = 0;
+  auto add_row = [&](const int32_t* vrow, uint32_t t, bool global) {
+    int32_t v[DL];
+    if constexpr (DL % 4 == 0) {
+#pragma unroll
+      for (uint32_t i = 0; i < DL / 4; ++i) {
+        const int4 x = global ? __ldcg((const int4*)(vrow + lane * DL) + i) : *((const int4*)(vrow + lane * DL) + i);
+        v[4 * i] = x.x, v[4 * i + 1] = x.y, v[4 * i + 2] = x.z, v[4 * i + 3] = x.w;
+      }
+    } else if constexpr (DL == 2) {
+      const int2 x = global ? __ldcg((const int2*)(vrow + lane * DL)) : *(const int2*)(vrow + lane * DL);
+      v[0] = x.x, v[1 % DL] = x.y;
+    } else {
+      v[0] = global ? __ldcg(vrow + lane) : vrow[lane];
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      const int32_t w = sw[t * HPC + h];
+#pragma unroll
+      for (uint32_t i = 0; i < DL; ++i) acc[h][i] += (uint64_t)((int64_t)w * (int64_t)v[i]);
+    }
+  };
+  for (uint32_t sb = 0; sb < nsm; sb += per_slot) {
+    const uint32_t nrows = min(per_slot, nsm - sb);
+    if (!stalled && !ring_wait<true>(&ring.full[cc.slot], cc.parity, A.fault)) stalled = true;
+    const int32_t* vs = (const int32_t*)(ring.base + cc.slot * ring.slot_bytes);
+    for (uint32_t t = warp; t < nrows; t += kWarps) add_row(vs + t * D, sb + t, false);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&ring.empty[cc.slot]);  // the slot's value rows are used
+    ring_advance(ring, cc);
+  }
+  if (has_p && warp == kWarps - 1) add_row(A.vcache + lay + (size_t)p * A.kvd + g * D, nsm, true);
+  // the sixteen warps' sums, pairwise through shared memory (four rounds),
+  // then warp 0 adds the block's sums into the group's words
+  constexpr uint32_t NA = HPC * DL;
+  for (uint32_t half = kWarps / 2; half >= 1; half >>= 1) {
+    if (warp >= half && warp < 2 * half) {
+#pragma unroll
+      for (uint32_t v = 0; v < NA; ++v) tree[((warp - half) * NA + v) * 32 + lane] = acc[v / DL][v % DL];
+    }
+    part_sync<kStepConsumers>();
+    if (warp < half) {
+#pragma unroll
+      for (uint32_t v = 0; v < NA; ++v) acc[v / DL][v % DL] += tree[(warp * NA + v) * 32 + lane];
+    }
+    part_sync<kStepConsumers>();
+  }
+  if (warp == 0) {
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+      for (uint32_t i = 0; i < DL; ++i)
+        if (acc[h][i])
+          atomicAdd((unsigned long long*)(A.acc + (size_t)(h0 + h) * D + lane * DL + i), (unsigned long long)acc[h][i]);
+  }
+  if (tid == 0) step_stamp(A, k, 5);
+
+  // ---- 4. the group's last block finishes every output of the group and
+  // clears the exchange words for the next layer
+  part_sync<kStepConsumers>();
+  if (tid == 0) {
+    __threadfence();
+    sh.last = atom_add_acq_rel(bar, 1u) == 3 * A.chunks - 1;
+  }
+  part_sync<kStepConsumers>();
+  if (!sh.last) return;
+  if (tid < HPC) sh.resid[tid] = sub_sat(kOneAct, (int32_t)__ldcg((const int*)(A.wsum + h0 + tid)));  // ops.rs:274-276
+  part_sync<kStepConsumers>();
+  for (uint32_t o = tid; o < HPC * D; o += kStepConsumers) {
+    const uint32_t h = o / D, i = o % D, hh = h0 + h;
+    unsigned long long* accp = (unsigned long long*)(A.acc + (size_t)hh * D + i);
+    uint64_t s = (uint64_t)__ldcg(accp);
+    *accp = 0;
+    const uint32_t tmax = best_key_token(sh.gbest[h]);
+    s += (uint64_t)((int64_t)sh.resid[h] * __ldcg(A.vcache + lay + (size_t)tmax * A.kvd + g * D + i));
+    put_planes(A.planes, A.qd, hh * D + i, requantize((int64_t)s));
+  }
+  if (tid < HPC) {
+    A.gbest[h0 + tid] = 0;
+    A.gsum[h0 + tid] = 0;
+    A.wsum[h0 + tid] = 0;
+  }
+  if (tid == 0) bar[0] = 0;
+}
+
+// ---- the kernel --------------------------------------------------------------
+
+template <uint32_t PER, uint32_t HPC>
+__global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepArgs A) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kTmaMaxStages];
+  __shared__ __align__(8) uint64_t empty[kTmaMaxStages];
+  __shared__ __align__(8) uint64_t slot_full[kTmaSlots];
+  __shared__ __align__(8) uint64_t slot_empty[kTmaSlots];
+  __shared__ int32_t s_scale;
+  __shared__ Acc128 slot_sums[kTmaSlots][2][kQ8TileRows];
+  __shared__ StepAttnShared<HPC> ash;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nb = gridDim.x;
+  uint8_t* planes = smem;  // activation planes of a product, or the attention scratch
+  const TileRing ring{smem + A.planes_bytes, A.slot_bytes, A.ring_slots, full, empty};
+  const SumRing sums{slot_full, slot_empty, slot_sums};
+  const StepStage* __restrict__ stages = A.stages;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t st = 0; st < A.ring_slots; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kTmaConsumerWarps);
+    }
+    for (uint32_t sl = 0; sl < kTmaSlots; ++sl) {
+      mbar_init(&slot_full[sl], kTmaConsumerWarps);
+      mbar_init(&slot_empty[sl], 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  const uint32_t p = *A.d_pos;  // this token's position (advanced by the previous launch)
+
+  if (warp == kStepProducerWarp) {
+    // lane 0 issues the weight tiles; the whole warp issues attention rows
+    RingCursor pc{0, 1, 0};
+    const uint64_t policy = l2_evict_first_policy();
+    bool ok = true;
+    for (uint32_t k = 0; k < A.nstages && ok; ++k) {
+      const StepStage st = stages[k];
+      if (st.kind == STEP_ATTN) {
+        ok = step_issue_kv<PER, HPC>(A, ring, pc, st.layer, p, policy);
+        if (lane == 0) step_stamp(A, k, 6);
+      }
+      if (!step_is_product(st.kind)) continue;
+      uint32_t ib, ie;
+      step_range(st, blockIdx.x, nb, &ib, &ie);
+      uint32_t good = 1;
+      if (lane == 0) {
+        good = ring_issue<true>(ring, pc, st.q, st.s, st.kc, ib, ie, policy, A.fault);
+        step_stamp(A, k, 6);
+      }
+      ok = __shfl_sync(0xffffffffu, good, 0) != 0;
+      // the other lanes keep the cursor in step with lane 0's
+      if (lane != 0)
+        for (uint32_t t = ib; t < ie; ++t) ring_advance(ring, pc);
+    }
+    if (lane == 0) ring_drain(ring, pc, A.fault);  // no copy may land after the block exits
+    return;
+  }
+
+  if (warp == kStepEpilogueWarp) {
+    uint32_t j = 0;
+    for (uint32_t k = 0; k < A.nstages; ++k) {
+      const StepStage st = stages[k];
+      if (!step_is_product(st.kind)) continue;
+      uint32_t ib, ie;
+      step_range(st, blockIdx.x, nb, &ib, &ie);
+      const ProductArgs a = step_product_args(A, st, k, p);
+      if (st.kind == STEP_QKV) ring_epilogue<EPI_QKV_ROPE, true>(a, sums, j, ib, ie, st.nslices, A.fault);
+      else if (st.kind == STEP_GU) ring_epilogue<EPI_SILU_MUL, true>(a, sums, j, ib, ie, st.nslices, A.fault);
+      else if (st.kind == STEP_HEAD) ring_epilogue<EPI_LOGITS, true>(a, sums, j, ib, ie, st.nslices, A.fault);
+      else ring_epilogue<EPI_RESID, true>(a, sums, j, ib, ie, st.nslices, A.fault);
+      __syncwarp();
+      if (lane == 0) {
+        step_stamp(A, k, 7);
+        __threadfence();
+        if (k + 1 < A.nstages) red_add_release(A.sync + k, 1u);
+        else if (atom_add_acq_rel(A.sync + k, 1u) == nb - 1) step_finish(A, p);  // the head stage, last of all
+      }
+    }
+    return;
+  }
+
+  // consumer warps
+  RingCursor cc{0, 0, 0};
+  uint32_t j = 0;
+  bool stalled = false;
+  for (uint32_t k = 0; k < A.nstages; ++k) {
+    const StepStage st = stages[k];
+    if (st.kind == STEP_EMBED) {
+      step_embed(A);
+      step_consumers_arrive(A, k);
+      continue;
+    }
+    if (st.kind == STEP_ATTN) {
+      step_wait(A, k);
+      step_attention<PER, HPC>(A, k, st.layer, p, planes, ash, ring, cc, stalled);
+      step_consumers_arrive(A, k);
+      continue;
+    }
+    uint32_t ib, ie;
+    step_range(st, blockIdx.x, nb, &ib, &ie);
+    if (ib == ie) continue;
+    constexpr uint32_t kHeld = 2;  // int4 pieces of x a thread holds (K up to 4096 values)
+    int4 wv[kHeld];
+    if (st.norm_w) {  // the norm weights never change: load them before the wait
+#pragma unroll
+      for (uint32_t jj = 0; jj < kHeld; ++jj) {
+        const uint32_t i = threadIdx.x * 4 + jj * kStepConsumers * 4;
+        wv[jj] = i < st.cols ? __ldg((const int4*)(st.norm_w + i)) : make_int4(0, 0, 0, 0);
+      }
+    }
+    step_wait(A, k);
+    const bool wide = st.norm_w ? step_norm_planes<kHeld>(A, k, st.cols, wv, st.norm_w, planes, &s_scale)
+                                : step_copy_planes(st.kind == STEP_O ? A.planes : A.planes2, st.cols, planes);
+    if (threadIdx.x == 0) step_stamp(A, k, 1);
+    ring_consume<true>(ring, cc, sums, j, planes, wide, st.cols, st.kc, st.nslices, st.e_fast, ib, ie, stalled,
+                       A.fault);
+    if (threadIdx.x == 0) step_stamp(A, k, 2);
+  }
+}
+
+#define IRIS_STEP_SHAPES(X) X(4, 1) X(4, 2) X(4, 4) X(8, 2) X(8, 4) X(16, 1) X(16, 2) X(16, 4)
+
+template <uint32_t PER, uint32_t HPC>
+const void* step_kernel_ptr() {
+  return (const void*)decode_step_kernel<PER, HPC>;
+}
+
+const void* step_kernel_for(uint32_t per, uint32_t hpc) {
+#define IRIS_STEP_PICK(PER, HPC) \
+  if (per == PER && hpc == HPC) return step_kernel_ptr<PER, HPC>();
+  IRIS_STEP_SHAPES(IRIS_STEP_PICK)
+#undef IRIS_STEP_PICK
+  return nullptr;
+}
+
+}  // namespace
+
+StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t V,
+                          uint32_t cap, const uint32_t* kcs, uint32_t nkcs) {
+  StepPlan p{};
+  p.why = 1;
+  if (heads == 0 || kv_heads == 0 || heads % kv_heads || d % 8 || cap == 0) return p;
+  const uint32_t G = heads / kv_heads;
+  uint32_t hpc = 4;
+  while (hpc > 1 && (G % hpc || hpc * d > 512)) hpc >>= 1;
+  p.why = 2;
+  const void* fn = step_kernel_for(d / 8, hpc);
+  if (!fn) return p;
+  p.why = 3;
+  int dev = 0, sms = 0, coop = 0, optin = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || !coop ||
+      sms <= 0) {
+    cudaGetLastError();
+    return p;
+  }
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) {
+    cudaGetLastError();
+    return p;
+  }
+  p.why = 1;
+  const uint32_t groups = heads / hpc, chunks = (uint32_t)sms / groups;
+  if (chunks == 0) return p;
+  p.why = 4;
+  const uint32_t span_max = (cap + chunks - 1) / chunks;
+  uint32_t slot = 0;
+  for (uint32_t i = 0; i < nkcs; ++i) slot = std::max(slot, round_up(kQ8TileRows * kcs[i] + kcs[i], 128));
+  const uint32_t widest = std::max(std::max(H, heads * d), F);
+  // attention scratch: scores / weights, exp terms, the cross-warp value-sum tree
+  const uint32_t attn = round_up(span_max * hpc * 4, 16) + span_max * hpc * 8 + 8 * 32 * hpc * (d / 32) * 8;
+  const uint32_t planes = round_up(std::max(4 * widest, attn), 128);
+  if ((size_t)optin <= fa.sharedSizeBytes) return p;
+  const uint32_t dyn = (uint32_t)optin - (uint32_t)fa.sharedSizeBytes;
+  if (planes + 2 * slot > dyn) return p;
+  const uint32_t slots = std::min<uint32_t>(kTmaMaxStages, (dyn - planes) / slot);
+  const uint32_t smem = planes + slots * slot;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+    cudaGetLastError();
+    return p;
+  }
+  p.why = 5;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTmaThreads, smem) != cudaSuccess || per_sm < 1) {
+    cudaGetLastError();
+    return p;
+  }
+  p.blocks = (uint32_t)sms;
+  p.ring_slots = slots;
+  p.slot_bytes = slot;
+  p.planes_bytes = planes;
+  p.smem = smem;
+  p.chunks = chunks;
+  p.span_max = span_max;
+  p.hpc = hpc;
+  (void)V;
+  p.why = 0;
+  p.ok = true;
+  return p;
+}
+
+cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_t s) {
+  const void* fn = step_kernel_for(a.d / 8, p.hpc);
+  if (!fn || !p.ok) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.blocks);
+  cfg.blockDim = dim3(kTmaThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {(void*)&a};
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t prepare_step_kernels() { return cudaSuccess; }
+
+}  // namespace iris

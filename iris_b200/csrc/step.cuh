@@ -1,0 +1,96 @@
+// The persistent decode step: one cooperative launch runs a whole
+// mistral-dense decode pass (embedding, every layer, head, greedy selection).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "layers.cuh"
+
+namespace iris {
+
+enum StepKind : uint32_t {
+  STEP_EMBED = 0,  // x = dequantize_row(embed[token])
+  STEP_QKV = 1,    // q|k|v = W rms_norm(x); RoPE; k, v to the cache
+  STEP_ATTN = 2,   // ctx = attention(q, K/V cache) as byte planes
+  STEP_O = 3,      // x = x + W_o ctx
+  STEP_GU = 4,     // g = silu(W_gate m) * (W_up m), m = rms_norm(x)
+  STEP_DOWN = 5,   // x = x + W_down g
+  STEP_HEAD = 6    // logits = W_head rms_norm(x); first maximum -> next token
+};
+
+// One stage of the pass (a device array built once per session).
+struct StepStage {
+  const int8_t* q;         // product stages: the matrix in the tiled layout
+  const uint16_t* s;
+  const int32_t* norm_w;   // RMSNorm weights of a normalised input, else NULL
+  uint32_t kind, layer;
+  uint32_t rows, cols, kc, nslices, items;
+  int32_t e_fast;
+};
+
+// Timeline stamps a block records per stage (StepArgs::trace): 0 input ready,
+// 7 share written; products: 1 prologue done, 2 warp 0's last tile taken,
+// 6 the producer issued the stage's last tile (normalised inputs: 3 scale
+// known, 4 thread 0's planes written); attention: 1 first key slot
+// landed, 2 scores done, 3 and 4 first and second group exchange passed,
+// 5 value sums added, 6 the producer issued the chunk's last value row.
+constexpr uint32_t kStepTraceEvents = 8;
+
+struct StepArgs {
+  const StepStage* stages;
+  uint32_t nstages;
+  // model
+  const int8_t* embed_q;
+  const uint16_t* embed_s;
+  uint32_t embed_kc, embed_nslices;
+  uint32_t H, heads, kv_heads, d, qd, kvd;
+  int64_t eps;
+  uint32_t scale_q32;
+  const int64_t* freqs;
+  // session buffers
+  int32_t* x;            // [H] residual stream
+  int32_t* q;            // [qd] rotated queries
+  uint8_t* planes;       // [4][qd] attention output planes
+  uint8_t* planes2;      // [4][F] gated FFN planes
+  int32_t* kcache;       // [layers][cap][kvd]
+  int32_t* vcache;
+  uint32_t cap;
+  int32_t* logits;       // [V]
+  unsigned long long* best;
+  unsigned long long* split_acc;
+  unsigned int* split_count;
+  // attention exchange words of a head group (zero between stages)
+  unsigned long long* gbest;
+  unsigned long long* gsum;
+  int32_t* wsum;
+  int64_t* acc;
+  unsigned int* gbar;
+  uint32_t chunks;       // blocks a head group
+  uint32_t span_max;     // positions a block at most
+  // bookkeeping of the greedy loop
+  uint32_t* d_token;
+  uint32_t* d_pos;
+  uint32_t* d_step;
+  uint32_t* history;
+  uint32_t history_cap;
+  unsigned int* sync;    // [nstages] arrivals a stage of the running pass (zero between launches)
+  unsigned long long* sumsq;  // [nstages][2] 128-bit sums of squares of the x a stage wrote (zero between launches)
+  unsigned int* fault;
+  unsigned long long* trace;  // optional timeline of the last pass: [block][stage][kStepTraceEvents] ns
+  // shared-memory layout
+  uint32_t ring_slots, slot_bytes, planes_bytes;
+};
+
+// The launch plan of a model and cache capacity, or ok = false when the
+// shape needs the kernel-per-operation pass.
+struct StepPlan {
+  bool ok;
+  uint32_t why;  // when not ok: 1 shape, 2 no kernel for the head shape, 3 device, 4 shared memory, 5 occupancy
+  uint32_t blocks, ring_slots, slot_bytes, planes_bytes, smem, chunks, span_max, hpc;
+};
+StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t V,
+                          uint32_t cap, const uint32_t* kcs, uint32_t nkcs);
+cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_t s);
+cudaError_t prepare_step_kernels();
+
+}  // namespace iris

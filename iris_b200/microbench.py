@@ -13,7 +13,12 @@
       reference kernel;
   python -m iris_b200.microbench product [--product 2 --layers 2]
       one of the decode pass's own products (0 q|k|v, 1 o, 2 gate|up,
-      3 down, 4 head) of a mistral-7b-shaped session, layer after layer.
+      3 down, 4 head) of a mistral-7b-shaped session, layer after layer;
+  python -m iris_b200.microbench step [--context 2048 --layers 32]
+      the persistent decode step's timeline: per stage kind, how long the
+      stage took end to end and the median block's intervals between its
+      stamps (wake-up after the stage before, prologue, streaming, tail;
+      attention: key slots, scores, the two group exchanges, value sums).
 
 Each prints one JSON line (average device time a launch, bytes or ops a
 launch, the implied rate). Inputs are seeded synthetic values; the launches
@@ -253,9 +258,63 @@ def sweep(args):
     return {"sweep": len(lines)}
 
 
+def step(args):
+    """Timeline of one persistent decode pass (global-timer stamps per block
+    and stage), summarised per stage kind (µs)."""
+    from iris_b200.model import DeviceModel
+    from iris_b200.shapes import mistral_7b
+    cfg = mistral_7b()
+    cfg = type(cfg)(**{**cfg.__dict__, "layers": args.layers})
+    model = DeviceModel(cfg, seed=args.seed)
+    sess = model.session(args.context + 8 + args.iters)
+    sess.set_decode_path("step")
+    sess.prefill(np.random.default_rng(args.seed).integers(0, cfg.vocab, size=args.context).tolist())
+    sess.step_trace(True)
+    sess.decode_steps(args.iters)
+    sess.synchronize()
+    tr = sess.get_step_trace().astype(np.int64)  # [blocks][stages][8]
+    sess.step_trace(False)
+    if args.raw:
+        np.save(args.raw, tr)
+    kinds = ["embed"] + ["qkv", "attn", "o", "gate_up", "down"] * cfg.layers + ["head"]
+    stages = tr.shape[1]
+    end = np.array([tr[:, k, 7].max() for k in range(stages)])
+    t0 = tr[:, 0, 7][tr[:, 0, 7] > 0].min()
+    # intervals between stamps (events of step.cuh's timeline), medians over
+    # the blocks that worked at the stage, then means over the layers
+    spans = {"product": [("wake", None, 0), ("prologue", 0, 1), ("consume", 1, 2), ("tail", 2, 7),
+                         ("producer_done", None, 6)],
+             "norm": [("wake", None, 0), ("norm_scale", 0, 3), ("norm_emit", 3, 4), ("norm_sync", 4, 1),
+                      ("consume", 1, 2), ("tail", 2, 7), ("producer_done", None, 6)],
+             "attn": [("wake", None, 0), ("first_key_slot", 0, 1), ("scores", 1, 2), ("exchange1", 2, 3),
+                      ("exchange2", 3, 4), ("values", 4, 5), ("finish", 5, 7), ("producer_done", None, 6)]}
+    acc = {}
+    for k in range(1, stages):
+        kind = kinds[k]
+        st = tr[:, k, :]
+        lst = spans["attn" if kind == "attn" else "norm" if kind in ("qkv", "gate_up", "head") else "product"]
+        need = [e for _, a, b in lst for e in (a, b) if e is not None and e != 6]
+        act = np.all(st[:, sorted(set(need))] > 0, axis=1)
+        d = acc.setdefault(kind, {"stage": [], **{n: [] for n, _, _ in lst}})
+        d["stage"].append((end[k] - end[k - 1]) / 1e3)
+        if not act.any():
+            continue
+        for name, a, b in lst:
+            va = end[k - 1] if a is None else st[act, a]
+            vb = st[act, b]
+            if b == 6 and not (vb > 0).any():
+                continue
+            d[name].append(float(np.median(vb - va)) / 1e3)
+    out = {kind: {n: round(float(np.mean(v)), 2) for n, v in d.items() if v} for kind, d in acc.items()}
+    sess.close()
+    model.close()
+    return {"kernel": "decode_step_kernel", "context": args.context, "layers": cfg.layers,
+            "pass_us": (end[-1] - t0) / 1e3, "per_kind_us": out}
+
+
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep"])
+    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep", "step"])
     p.add_argument("--product", type=int, default=2, dest="product_which")
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
@@ -267,10 +326,11 @@ def main():
     p.add_argument("--shape", default="", help="cluster,hpc,ring of the one-launch attention")
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--seed", type=int, default=7)
+    p.add_argument("--raw", default="", help="step: also save the raw stamps (.npy)")
     args = p.parse_args()
     from iris_b200 import build
     build.build()
-    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep}[args.which](args)), flush=True)
+    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep, "step": step}[args.which](args)), flush=True)
 
 
 if __name__ == "__main__":

@@ -277,8 +277,40 @@ class Session:
         """The decode attention in use (path, heads a block, blocks, positions a block)."""
         plan = (C.c_uint32 * 4)()
         check(lib().iris_session_attention_plan(self._h, plan), "iris_session_attention_plan")
-        return {"path": {3: "grid", 2: "cluster", 1: "split"}[plan[0]], "heads_per_block": plan[1],
+        return {"path": {4: "step", 3: "grid", 2: "cluster", 1: "split"}[plan[0]], "heads_per_block": plan[1],
                 "blocks": plan[2], "positions_per_block": plan[3]}
+
+    def set_decode_path(self, mode: str) -> None:
+        """'auto' (the persistent step where the model allows it), 'graph'
+        (a CUDA graph of one kernel per operation) or 'step' (one cooperative
+        launch a pass; refused where the model does not allow it)."""
+        check(lib().iris_session_set_decode_path(self._h, {"auto": 0, "graph": 1, "step": 2}[mode]),
+              "iris_session_set_decode_path")
+
+    @property
+    def decode_path(self) -> str:
+        return {1: "graph", 2: "step"}[lib().iris_session_decode_path(self._h)]
+
+    def step_trace(self, enable: bool) -> None:
+        """Per-stage timeline of every persistent-step pass (profiling)."""
+        check(lib().iris_session_step_trace(self._h, int(enable)), "iris_session_step_trace")
+
+    def get_step_trace(self):
+        """The last pass's stamps as [blocks][stages][8] uint64 ns."""
+        plan = self.step_plan
+        stages = 2 + 5 * self.model.cfg.layers
+        out = np.zeros((plan["blocks"], stages, 8), np.uint64)
+        check(lib().iris_session_get_step_trace(self._h, out.ctypes.data_as(C.POINTER(C.c_uint64)), out.size),
+              "iris_session_get_step_trace")
+        return out
+
+    @property
+    def step_plan(self) -> dict:
+        """The persistent step's plan (why 0 when usable)."""
+        v = (C.c_uint32 * 8)()
+        check(lib().iris_session_step_plan(self._h, v), "iris_session_step_plan")
+        keys = ("why", "blocks", "ring_slots", "slot_bytes", "planes_bytes", "smem", "chunks", "span_max")
+        return dict(zip(keys, list(v)))
 
     def set_attention_shape(self, cluster: int, hpc: int, ring: int) -> None:
         """Explicit one-launch decode attention shape (tuning)."""

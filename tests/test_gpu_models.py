@@ -25,13 +25,14 @@ def seeded_prompt(seed, n, vocab):
     return np.random.default_rng(seed).integers(0, vocab, size=n).tolist()
 
 
-def run_both(cfg, seed, prompt, steps, per_block=False, eos=(), attn="auto"):
+def run_both(cfg, seed, prompt, steps, per_block=False, eos=(), attn="auto", path="auto"):
     from iris_b200.model import DeviceModel, synth_host_weights
     from oracle.models import OracleModel
     w = synth_host_weights(cfg, seed, per_block)
     dm = DeviceModel(cfg, weights=w)
     sess = dm.session(len(prompt) + steps + 8)
     sess.set_attention(attn)
+    sess.set_decode_path(path)
     got = sess.generate(prompt, steps, eos, want_logits=True)
     want = OracleModel(cfg, w).generate(prompt, steps, eos)
     return dm, sess, w, got, want
@@ -65,12 +66,70 @@ def test_tiny_gemma_config_1():
 
 
 def test_parity_mistral_prefill_and_decode():
+    """Both decode paths: the persistent step (the default for
+    mistral-dense) and the graph of one kernel per operation."""
     from iris_b200.shapes import parity_mistral
     cfg = parity_mistral()
     for seed, per_block in [(3, False), (4, True)]:
         prompt = seeded_prompt(seed, 19, cfg.vocab)
-        dm, sess, w, got, want = run_both(cfg, seed, prompt, 12, per_block)
-        assert_same(got, want)
+        for path in ("auto", "graph"):
+            dm, sess, w, got, want = run_both(cfg, seed, prompt, 12, per_block, path=path)
+            assert sess.decode_path == ("step" if path == "auto" else "graph"), sess.step_plan
+            assert_same(got, want)
+
+
+def test_saturating_residual_norms():
+    """Embedding rows near the Q16.16 limit (every block scale 16000): the
+    residual stream's sum of squares saturates at i64::MAX in every norm
+    (add_sat_nonneg, ops.rs:98-114). Both decode paths against the oracle:
+    the persistent step takes that sum from the residual epilogues, the graph
+    path from a block-wide reduction."""
+    from iris_b200.model import DeviceModel, synth_host_weights
+    from iris_b200.shapes import parity_mistral
+    from oracle.models import OracleModel
+    cfg = parity_mistral()
+    w = synth_host_weights(cfg, 41)
+    emb = w[("EMBED", -1)].reshape(-1, 34).copy()
+    emb[:, 0:2] = np.frombuffer(np.float16(16000.0).tobytes(), np.uint8)
+    w[("EMBED", -1)] = emb.reshape(-1)
+    prompt = seeded_prompt(41, 9, cfg.vocab)
+    want = OracleModel(cfg, w).generate(prompt, 6)
+    for path in ("auto", "graph"):
+        dm = DeviceModel(cfg, weights=w)
+        sess = dm.session(32)
+        sess.set_decode_path(path)
+        assert sess.decode_path == ("step" if path == "auto" else "graph")
+        assert_same(sess.generate(prompt, 6, want_logits=True), want)
+        sess.close()
+        dm.close()
+
+
+def test_step_matches_graph_on_mistral_7b_shapes():
+    """The persistent step against the kernel-per-operation pass (itself
+    pinned to the oracle) on the Mistral-7B layer shapes (2 of its 32 layers):
+    4096 hidden, 14336 FFN, 32 heads over 8 kv heads of 128, 32000 vocab;
+    a 700-token prompt so that every attention block holds several rows.
+    Every logit of every pass, every token and the K/V rows agree."""
+    import dataclasses
+    from iris_b200.model import DeviceModel
+    from iris_b200.shapes import mistral_7b
+    cfg = dataclasses.replace(mistral_7b(), name="mistral-7b-2l", layers=2)
+    dm = DeviceModel(cfg, seed=0x7B)
+    prompt = seeded_prompt(0x7B, 700, cfg.vocab)
+    out = {}
+    for path in ("step", "graph"):
+        sess = dm.session(len(prompt) + 16)
+        sess.set_decode_path(path)
+        assert sess.decode_path == path
+        toks, logits = sess.generate(prompt, 10, want_logits=True)
+        batched, _ = sess.generate(prompt, 10)  # device-resident loop with history
+        assert batched == toks
+        out[path] = (toks, logits, sess.kv(1, len(prompt) - 2, 10))
+        sess.close()
+    assert out["step"][0] == out["graph"][0]
+    assert np.array_equal(out["step"][1], out["graph"][1])
+    for a, b in zip(out["step"][2], out["graph"][2]):
+        assert np.array_equal(a, b)
 
 
 def test_parity_gemma_window_donors_softcap():
