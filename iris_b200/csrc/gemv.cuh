@@ -436,6 +436,7 @@ __device__ __forceinline__ void ring_drain(const TileRing& r, const RingCursor& 
 // and 2 (w % 8) + 1 of each tile, blocks of the slice's first (w < 8) or
 // second half. j counts the sum slots used; after a given-up wait `stalled`
 // keeps the warp in step with the others without waiting.
+
 template <bool kWatch>
 __device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, const SumRing& sr, uint32_t& j,
                                              const uint8_t* planes, bool wide, uint32_t K, uint32_t kc,
@@ -505,9 +506,17 @@ __device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, c
 // exact 128-bit atomics; the block whose share completes the group's slice
 // count rounds it once (q8.rs:69-71) and applies the epilogue. Returns false
 // after a given-up wait.
+//
 template <int EPI, bool kWatch>
 __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRing& sr, uint32_t& j, uint32_t ib,
                                               uint32_t ie, uint32_t S, unsigned int* fault) {
+  // Paired epilogues (RoPE, SiLU / GELU gating) cost hundreds of dependent
+  // integer operations a pair and take one lane a pair, eight a group: the
+  // warp takes up to four finished groups at once (lane 8 q + p: pair p of
+  // the q-th), every slot released as soon as it is read.
+  constexpr bool kPaired = EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL;
+  constexpr uint32_t kBatch = kPaired ? 4 : 1;
+  static_assert(kBatch <= kTmaSlots, "a batch fits the sum slots");
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t gfirst = ib / S, ngroups = ie > ib ? (ie - 1) / S - gfirst + 1 : 0;
   // EPI_PARTIAL into a double-buffered peer-exchange slot: the one of the
@@ -517,43 +526,66 @@ __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRin
   unsigned long long best = 0;
   Acc128 squares{0, 0};  // EPI_RESID with a.sumsq: this lane's written values, squared
   bool ok = true;
-  for (uint32_t k = 0; k < ngroups; ++k, ++j) {
-    const uint32_t sl = j % kTmaSlots, g = gfirst + k;
-    if (!ring_wait<kWatch>(&sr.full[sl], (j / kTmaSlots) & 1, fault)) {
-      ok = false;
-      if (!kWatch) return false;
-    }
-    Acc128 v = Acc128{0, 0};
-    if (lane < kQ8TileRows) {
-      v = sr.sums[sl][0][lane];
-      acc128_add(v, sr.sums[sl][1][lane].lo, sr.sums[sl][1][lane].hi);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sr.empty[sl]);
-    const uint32_t lo = max(ib, g * S), hi = min(ie, (g + 1) * S);
-    if (hi - lo < S) {  // a share of a group split between blocks
-      unsigned long long* acc = a.split_acc + (size_t)g * kQ8TileRows * 2;
-      if (lane < kQ8TileRows) atomic_add_acc128(acc + 2 * lane, v);
-      __threadfence();
-      __syncwarp();
-      uint32_t done = 0;
-      if (lane == 0) done = atomicAdd(a.split_count + g, hi - lo) + (hi - lo) == S;
-      if (!__shfl_sync(0xffffffffu, done, 0)) continue;
-      __threadfence();
-      if (lane < kQ8TileRows) {
-        v.lo = (uint64_t)__ldcg(acc + 2 * lane);
-        v.hi = (int64_t)__ldcg(acc + 2 * lane + 1);
-        acc[2 * lane] = 0;
-        acc[2 * lane + 1] = 0;
+  for (uint32_t k0 = 0; k0 < ngroups; k0 += kBatch) {
+    const uint32_t nbat = min(kBatch, ngroups - k0);
+    int32_t r[kBatch];    // lane l < 16: the rounded value of row l of the batch's q-th group
+    uint32_t fin = 0;     // bit q: this block completes the q-th group
+#pragma unroll
+    for (uint32_t q = 0; q < kBatch; ++q) {
+      r[q] = 0;
+      if (q >= nbat) continue;
+      const uint32_t sl = j % kTmaSlots, g = gfirst + k0 + q;
+      if (!ring_wait<kWatch>(&sr.full[sl], (j / kTmaSlots) & 1, fault)) {
+        ok = false;
+        if (!kWatch) return false;
       }
-      if (lane == 0) a.split_count[g] = 0;
+      Acc128 v = Acc128{0, 0};
+      if (lane < kQ8TileRows) {
+        v = sr.sums[sl][0][lane];
+        acc128_add(v, sr.sums[sl][1][lane].lo, sr.sums[sl][1][lane].hi);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sr.empty[sl]);
+      ++j;
+      const uint32_t lo = max(ib, g * S), hi = min(ie, (g + 1) * S);
+      if (hi - lo < S) {  // a share of a group split between blocks
+        unsigned long long* acc = a.split_acc + (size_t)g * kQ8TileRows * 2;
+        if (lane < kQ8TileRows) atomic_add_acc128(acc + 2 * lane, v);
+        __threadfence();
+        __syncwarp();
+        uint32_t done = 0;
+        if (lane == 0) done = atomicAdd(a.split_count + g, hi - lo) + (hi - lo) == S;
+        if (!__shfl_sync(0xffffffffu, done, 0)) continue;
+        __threadfence();
+        if (lane < kQ8TileRows) {
+          v.lo = (uint64_t)__ldcg(acc + 2 * lane);
+          v.hi = (int64_t)__ldcg(acc + 2 * lane + 1);
+          acc[2 * lane] = 0;
+          acc[2 * lane + 1] = 0;
+        }
+        if (lane == 0) a.split_count[g] = 0;
+      }
+      fin |= 1u << q;
+      if (EPI == EPI_PARTIAL) {
+        const uint32_t row = g * kQ8TileRows + lane;
+        if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, part + (size_t)row * 4);
+      } else if (kPaired) {
+        r[q] = acc128_round_q24(v);
+      } else {
+        const int32_t y = gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
+        if (EPI == EPI_RESID && a.sumsq) acc128_add(squares, (uint64_t)((int64_t)y * y), 0);
+      }
     }
-    if (EPI == EPI_PARTIAL) {
-      const uint32_t row = g * kQ8TileRows + lane;
-      if (lane < kQ8TileRows && row < a.rows) limbs_from_acc128(v.lo, v.hi, part + (size_t)row * 4);
-    } else {
-      const int32_t y = gemv_group_epilogue<EPI>(a, g, acc128_round_q24(v), lane, &best);
-      if (EPI == EPI_RESID && a.sumsq) acc128_add(squares, (uint64_t)((int64_t)y * y), 0);
+    if (kPaired) {
+      const uint32_t q = lane >> 3, pr = lane & 7;
+      int32_t v0 = 0, v1 = 0;
+#pragma unroll
+      for (uint32_t qq = 0; qq < kBatch; ++qq) {
+        const int32_t t0 = __shfl_sync(0xffffffffu, r[qq], 2 * pr), t1 = __shfl_sync(0xffffffffu, r[qq], 2 * pr + 1);
+        if (qq == q) v0 = t0, v1 = t1;
+      }
+      const uint32_t row = (gfirst + k0 + q) * kQ8TileRows + 2 * pr;
+      if (q < nbat && ((fin >> q) & 1) && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
     }
   }
   if (EPI == EPI_RESID && a.sumsq) {

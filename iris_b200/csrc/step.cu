@@ -259,6 +259,30 @@ __device__ __forceinline__ void step_group_barrier(unsigned int* bar, unsigned i
   part_sync<kStepConsumers>();
 }
 
+// Sums M values a lane over the W-lane groups of a warp (W a power of two,
+// M <= W): lane l of a group ends with the group's total of value
+// l / (W / M). Halving exchange (offsets W/2, W/4, ...) while a lane holds
+// more than one value, then plain sums over the remaining offsets. Wrapping
+// 64-bit additions, like the atomics they feed.
+template <uint32_t M, uint32_t W>
+__device__ __forceinline__ uint64_t reduce_scatter_lanes(uint64_t (&v)[M], uint32_t pos) {
+  static_assert(M >= 1 && M <= W && W <= 32 && (M & (M - 1)) == 0 && (W & (W - 1)) == 0, "powers of two");
+#pragma unroll
+  for (uint32_t n = M, off = W / 2; n > 1; n >>= 1, off >>= 1) {
+    const bool upper = (pos & off) != 0;
+#pragma unroll
+    for (uint32_t i = 0; i < n / 2; ++i) {
+      const uint64_t send = upper ? v[i] : v[i + n / 2];
+      const uint64_t keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  uint64_t r = v[0];
+#pragma unroll
+  for (uint32_t off = W / M / 2; off >= 1; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+  return r;
+}
+
 // This block's share of the attention of a decode pass: the head group and
 // the chunk [r0, r1) of positions [0, p] (empty when r0 = p + 1); rows
 // [r0, rc), rc = max(r0, min(r1, p)) (written by earlier passes) travel
@@ -286,8 +310,16 @@ __device__ __forceinline__ AttnChunk attn_chunk(const StepArgs& A, uint32_t p) {
   return c;
 }
 
+// Key and value rows sit in a ring slot 4 D + 16 bytes apart: lane l of a warp
+// reading row t0 + l at a fixed column then starts 4 (t0 + l) banks further
+// on, so eight lanes' 16-byte pieces cover all 32 banks (no conflicts).
+template <uint32_t D>
+__host__ __device__ constexpr uint32_t kv_pitch() {
+  return D * 4 + 16;
+}
+
 // Producer warp: the chunk's cached key rows, then its value rows, into ring
-// slots (slot_bytes / (4 D) rows a slot, one bulk copy a row, the warp's 32
+// slots (slot_bytes / pitch rows a slot, one bulk copy a row, the warp's 32
 // lanes issuing a slot's copies together). Lane 0 waits for the slot and arms
 // its barrier; every lane keeps the same cursor.
 template <uint32_t PER, uint32_t HPC>
@@ -296,7 +328,7 @@ __device__ __forceinline__ bool step_issue_kv(const StepArgs& A, const TileRing&
   constexpr uint32_t D = PER * 8;
   const AttnChunk c = attn_chunk<HPC>(A, p);
   if (!c.active) return true;
-  const uint32_t lane = threadIdx.x & 31, per_slot = ring.slot_bytes / (D * 4);
+  const uint32_t lane = threadIdx.x & 31, per_slot = ring.slot_bytes / kv_pitch<D>();
   const size_t base = (size_t)layer * A.cap * A.kvd + (size_t)c.g * D;
   for (int kv = 0; kv < 2; ++kv) {
     const int32_t* src = (kv ? A.vcache : A.kcache) + base;
@@ -310,7 +342,7 @@ __device__ __forceinline__ bool step_issue_kv(const StepArgs& A, const TileRing&
       if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
       uint8_t* dst = ring.base + pc.slot * ring.slot_bytes;
       for (uint32_t i = lane; i < n; i += 32)
-        bulk_load(dst + i * D * 4, src + (size_t)(a + i) * A.kvd, D * 4, &ring.full[pc.slot], policy);
+        bulk_load(dst + i * kv_pitch<D>(), src + (size_t)(a + i) * A.kvd, D * 4, &ring.full[pc.slot], policy);
       ring_advance(ring, pc);
     }
   }
@@ -328,18 +360,17 @@ template <uint32_t PER, uint32_t HPC>
 __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, uint32_t layer, uint32_t p,
                                                uint8_t* scratch, StepAttnShared<HPC>& sh, const TileRing& ring,
                                                RingCursor& cc, bool& stalled) {
-  constexpr uint32_t D = PER * 8, kWarps = kStepConsumers / 32, DL = D / 32;
-  static_assert(DL >= 1 && HPC * DL <= 16, "value sums a lane");
+  constexpr uint32_t D = PER * 8, kWarps = kStepConsumers / 32;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const AttnChunk c = attn_chunk<HPC>(A, p);
   if (!c.active) return;
   const uint32_t h0 = c.h0, g = c.g, r0 = c.r0, cnt = c.r1 - c.r0, nsm = c.rc - c.r0;
   const bool has_p = cnt > nsm;  // row p is this chunk's last row
-  const uint32_t per_slot = ring.slot_bytes / (D * 4);
+  constexpr uint32_t PITCH = kv_pitch<D>() / 4;  // int32 values from one row to the next
+  const uint32_t per_slot = ring.slot_bytes / kv_pitch<D>();
   const size_t lay = (size_t)layer * A.cap * A.kvd;
   int32_t* sw = (int32_t*)scratch;                                           // [span][HPC] scores, then weights
   uint64_t* tm = (uint64_t*)(scratch + round_up(A.span_max * HPC * 4, 16));  // [span][HPC] exp terms
-  uint64_t* tree = tm + A.span_max * HPC;  // [kWarps / 2][HPC DL][32] partial value sums
   unsigned int* bar = c.bar;
 
   if (tid < HPC) {
@@ -416,7 +447,7 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
       int4 kv[NV];
 #pragma unroll
       for (uint32_t i = 0; i < NV; ++i)
-        kv[i] = live ? *(const int4*)(ks + t * D + 4 * (pl + LPP * i)) : make_int4(0, 0, 0, 0);
+        kv[i] = live ? *(const int4*)(ks + t * PITCH + 4 * (pl + LPP * i)) : make_int4(0, 0, 0, 0);
       score(kv, live, sb + t);
     }
     __syncwarp();
@@ -468,8 +499,7 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
   }
   part_sync<kStepConsumers>();
 
-  // ---- 3. weights and their sums, then the value sums: warp w takes rows w,
-  // w + 16, ... of each slot, lane l dimensions [l DL, (l + 1) DL) of each
+  // ---- 3. weights and their sums, then the value sums
   {
     const uint64_t tot = sh.gtot[my_h], inv = sh.ginv[my_h];
     int32_t wsum = 0;
@@ -483,64 +513,53 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
   }
   part_sync<kStepConsumers>();
   if (tid < HPC && sh.wsum[tid]) atomicAdd(A.wsum + h0 + tid, sh.wsum[tid]);
-  uint64_t acc[HPC][DL];
+  // Value sums: warp w takes dimensions [w DW, (w + 1) DW) of every row. Its
+  // HPC DW sums are split into VG groups of at most 16 (lane l takes group
+  // l / (32 / VG)) and the rows over the 32 / VG lanes of a group; the lanes'
+  // sums then meet in a halving exchange within the group and the lanes
+  // holding a total add it into the head group's words.
+  constexpr uint32_t DW = D / kWarps, NV_ALL = HPC * DW, VG = NV_ALL > 16 ? NV_ALL / 16 : 1;
+  constexpr uint32_t MV = NV_ALL / VG, W = 32 / VG;  // sums a lane, lanes a group
+  static_assert(DW >= 1 && MV <= W && NV_ALL % VG == 0, "value sums a lane");
+  const uint32_t vg = lane / W, pos = lane % W;
+  uint64_t acc[MV];
 #pragma unroll
-  for (uint32_t h = 0; h < HPC; ++h)
+  for (uint32_t i = 0; i < MV; ++i) acc[i] = 0;
+  auto add_row = [&](const int32_t* vrow, uint32_t t, bool global) {  // vrow: the row's DW values
+    int32_t v[DW];
+    if constexpr (DW % 4 == 0) {
 #pragma unroll
-    for (uint32_t i = 0; i < DL; ++i) acc[h][i] = 0;
-  auto add_row = [&](const int32_t* vrow, uint32_t t, bool global) {
-    int32_t v[DL];
-    if constexpr (DL % 4 == 0) {
-#pragma unroll
-      for (uint32_t i = 0; i < DL / 4; ++i) {
-        const int4 x = global ? __ldcg((const int4*)(vrow + lane * DL) + i) : *((const int4*)(vrow + lane * DL) + i);
+      for (uint32_t i = 0; i < DW / 4; ++i) {
+        const int4 x = global ? __ldcg((const int4*)vrow + i) : *((const int4*)vrow + i);
         v[4 * i] = x.x, v[4 * i + 1] = x.y, v[4 * i + 2] = x.z, v[4 * i + 3] = x.w;
       }
-    } else if constexpr (DL == 2) {
-      const int2 x = global ? __ldcg((const int2*)(vrow + lane * DL)) : *(const int2*)(vrow + lane * DL);
-      v[0] = x.x, v[1 % DL] = x.y;
+    } else if constexpr (DW == 2) {
+      const int2 x = global ? __ldcg((const int2*)vrow) : *(const int2*)vrow;
+      v[0] = x.x, v[1 % DW] = x.y;
     } else {
-      v[0] = global ? __ldcg(vrow + lane) : vrow[lane];
+      v[0] = global ? __ldcg(vrow) : *vrow;
     }
 #pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h) {
-      const int32_t w = sw[t * HPC + h];
-#pragma unroll
-      for (uint32_t i = 0; i < DL; ++i) acc[h][i] += (uint64_t)((int64_t)w * (int64_t)v[i]);
+    for (uint32_t j = 0; j < MV; ++j) {
+      const uint32_t val = vg * MV + j, h = val / DW, i = val % DW;
+      acc[j] += (uint64_t)((int64_t)sw[t * HPC + h] * (int64_t)v[i]);
     }
   };
   for (uint32_t sb = 0; sb < nsm; sb += per_slot) {
     const uint32_t nrows = min(per_slot, nsm - sb);
     if (!stalled && !ring_wait<true>(&ring.full[cc.slot], cc.parity, A.fault)) stalled = true;
     const int32_t* vs = (const int32_t*)(ring.base + cc.slot * ring.slot_bytes);
-    for (uint32_t t = warp; t < nrows; t += kWarps) add_row(vs + t * D, sb + t, false);
+    for (uint32_t t = pos; t < nrows; t += W) add_row(vs + t * PITCH + warp * DW, sb + t, false);
     __syncwarp();
     if (lane == 0) mbar_arrive(&ring.empty[cc.slot]);  // the slot's value rows are used
     ring_advance(ring, cc);
   }
-  if (has_p && warp == kWarps - 1) add_row(A.vcache + lay + (size_t)p * A.kvd + g * D, nsm, true);
-  // the sixteen warps' sums, pairwise through shared memory (four rounds),
-  // then warp 0 adds the block's sums into the group's words
-  constexpr uint32_t NA = HPC * DL;
-  for (uint32_t half = kWarps / 2; half >= 1; half >>= 1) {
-    if (warp >= half && warp < 2 * half) {
-#pragma unroll
-      for (uint32_t v = 0; v < NA; ++v) tree[((warp - half) * NA + v) * 32 + lane] = acc[v / DL][v % DL];
-    }
-    part_sync<kStepConsumers>();
-    if (warp < half) {
-#pragma unroll
-      for (uint32_t v = 0; v < NA; ++v) acc[v / DL][v % DL] += tree[(warp * NA + v) * 32 + lane];
-    }
-    part_sync<kStepConsumers>();
-  }
-  if (warp == 0) {
-#pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h)
-#pragma unroll
-      for (uint32_t i = 0; i < DL; ++i)
-        if (acc[h][i])
-          atomicAdd((unsigned long long*)(A.acc + (size_t)(h0 + h) * D + lane * DL + i), (unsigned long long)acc[h][i]);
+  if (has_p && pos == 0) add_row(A.vcache + lay + (size_t)p * A.kvd + g * D + warp * DW, nsm, true);
+  const uint64_t tot = reduce_scatter_lanes<MV, W>(acc, pos);
+  constexpr uint32_t kLanesPer = W / MV;
+  if (pos % kLanesPer == 0 && tot) {
+    const uint32_t val = vg * MV + pos / kLanesPer, h = val / DW, i = val % DW;
+    atomicAdd((unsigned long long*)(A.acc + (size_t)(h0 + h) * D + warp * DW + i), (unsigned long long)tot);
   }
   if (tid == 0) step_stamp(A, k, 5);
 
@@ -685,8 +704,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
       }
     }
     step_wait(A, k);
+    const uint8_t* src = st.kind == STEP_O ? A.planes : A.planes2;
     const bool wide = st.norm_w ? step_norm_planes<kHeld>(A, k, st.cols, wv, st.norm_w, planes, &s_scale)
-                                : step_copy_planes(st.kind == STEP_O ? A.planes : A.planes2, st.cols, planes);
+                                : step_copy_planes(src, st.cols, planes);
     if (threadIdx.x == 0) step_stamp(A, k, 1);
     ring_consume<true>(ring, cc, sums, j, planes, wide, st.cols, st.kc, st.nslices, st.e_fast, ib, ie, stalled,
                        A.fault);
@@ -744,9 +764,11 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
   const uint32_t span_max = (cap + chunks - 1) / chunks;
   uint32_t slot = 0;
   for (uint32_t i = 0; i < nkcs; ++i) slot = std::max(slot, round_up(kQ8TileRows * kcs[i] + kcs[i], 128));
+  // The planes region holds the widest input's byte planes and the attention
+  // scratch (scores, then weights, and exp terms); the rest of the shared
+  // memory is ring slots.
   const uint32_t widest = std::max(std::max(H, heads * d), F);
-  // attention scratch: scores / weights, exp terms, the cross-warp value-sum tree
-  const uint32_t attn = round_up(span_max * hpc * 4, 16) + span_max * hpc * 8 + 8 * 32 * hpc * (d / 32) * 8;
+  const uint32_t attn = round_up(span_max * hpc * 4, 16) + span_max * hpc * 8;
   const uint32_t planes = round_up(std::max(4 * widest, attn), 128);
   if ((size_t)optin <= fa.sharedSizeBytes) return p;
   const uint32_t dyn = (uint32_t)optin - (uint32_t)fa.sharedSizeBytes;

@@ -88,6 +88,7 @@ struct StepPlan {
   uint32_t why;  // when not ok: 1 shape, 2 no kernel for the head shape, 3 device, 4 shared memory, 5 occupancy
   uint32_t blocks, ring_slots, slot_bytes, planes_bytes, smem, chunks, span_max, hpc;
 };
+// kcs: the slice width of every matrix of the pass.
 StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t V,
                           uint32_t cap, const uint32_t* kcs, uint32_t nkcs);
 cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_t s);

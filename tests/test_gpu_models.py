@@ -104,6 +104,20 @@ def test_saturating_residual_norms():
         dm.close()
 
 
+def test_wide_ffn_model():
+    """A parity-bundle-shaped model with an 8192-wide FFN (four 2048-column
+    slices a down row, 32 KB of input planes) against the oracle, on both
+    decode paths."""
+    import dataclasses
+    from iris_b200.shapes import parity_mistral
+    cfg = dataclasses.replace(parity_mistral(), name="parity-mistral-ffn8192", ffn=8192)
+    prompt = seeded_prompt(43, 17, cfg.vocab)
+    for path in ("auto", "graph"):
+        dm, sess, w, got, want = run_both(cfg, 43, prompt, 8, path=path)
+        assert sess.decode_path == ("step" if path == "auto" else "graph")
+        assert_same(got, want)
+
+
 def test_step_matches_graph_on_mistral_7b_shapes():
     """The persistent step against the kernel-per-operation pass (itself
     pinned to the oracle) on the Mistral-7B layer shapes (2 of its 32 layers):
