@@ -56,8 +56,14 @@ IRIS_HD int64_t shift_round_even(int64_t x, int s) {
 
 // ops.rs:448-451 requantize: Q32.32 -> Q16.16, ties to even, saturated.
 IRIS_HD int32_t requantize(int64_t x) { return clamp_i32(shift_round_even(x, 16)); }
-// ops.rs:41-45 mul_sat
-IRIS_HD int32_t mul_sat(int32_t a, int32_t b) { return requantize((int64_t)a * (int64_t)b); }
+// ops.rs:41-45 mul_sat. |a b| <= 2^62, so x + 2^15 cannot overflow and the
+// ties-to-even rounding is one addition: with f = floor(x / 2^16) and
+// r = x - 2^16 f, (x + 2^15 - 1 + (f & 1)) >> 16 = f + [r + 2^15 - 1 + (f & 1)
+// >= 2^16], i.e. f + 1 exactly when r > 2^15, or r = 2^15 and f is odd.
+IRIS_HD int32_t mul_sat(int32_t a, int32_t b) {
+  const int64_t x = (int64_t)a * (int64_t)b;
+  return clamp_i32((x + 0x7FFF + ((x >> 16) & 1)) >> 16);
+}
 // ops.rs:36-38 add_sat, ops.rs:431-433 sub_sat (i32 saturating)
 IRIS_HD int32_t add_sat(int32_t a, int32_t b) { return clamp_i32((int64_t)a + (int64_t)b); }
 IRIS_HD int32_t sub_sat(int32_t a, int32_t b) { return clamp_i32((int64_t)a - (int64_t)b); }

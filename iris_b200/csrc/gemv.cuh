@@ -588,9 +588,9 @@ __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRin
       if (q < nbat && ((fin >> q) & 1) && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
     }
   }
-  if (EPI == EPI_RESID && a.sumsq) {
+  if (EPI == EPI_RESID && a.sumsq) {  // the block's share, clamped: the norm's sum saturates there anyway
     squares = warp_sum_acc128(squares);
-    if (lane == 0 && (squares.lo | (uint64_t)squares.hi)) atomic_add_acc128(a.sumsq, squares);
+    if (lane == 0) *a.sumsq = (squares.hi || squares.lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : squares.lo;
   }
   if (EPI == EPI_LOGITS) {
 #pragma unroll

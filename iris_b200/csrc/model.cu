@@ -164,7 +164,7 @@ struct IrisSession {
   uint32_t nstages = 0;
   unsigned int* sync = nullptr;  // [nstages] arrival counters
   unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
-  unsigned long long* sumsq = nullptr;  // [nstages][2] sums of squares of the residual stream
+  unsigned long long* sumsq = nullptr;  // [nstages][blocks] sums of squares of the residual stream
   int decode_mode = IRIS_DECODE_AUTO;
   int attn_mode = IRIS_ATTN_AUTO;
   bool use_step = false;
@@ -242,8 +242,8 @@ cudaError_t setup_step(IrisSession* s) {
   if (e == cudaSuccess) e = cudaMemcpy(s->stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = dalloc(&s->sync, st.size());
   if (e == cudaSuccess) e = cudaMemset(s->sync, 0, st.size() * sizeof(unsigned int));
-  if (e == cudaSuccess) e = dalloc(&s->sumsq, 2 * st.size());
-  if (e == cudaSuccess) e = cudaMemset(s->sumsq, 0, 2 * st.size() * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = dalloc(&s->sumsq, st.size() * plan.blocks);
+  if (e == cudaSuccess) e = cudaMemset(s->sumsq, 0, st.size() * plan.blocks * sizeof(unsigned long long));
   if (e != cudaSuccess) return e;
   s->nstages = (uint32_t)st.size();
   s->step = plan;
@@ -701,7 +701,6 @@ int decode_steps(IrisSession* s, uint32_t steps) {
   if (s->use_step) {
     const StepArgs a = step_args(s);
     cudaError_t e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(s->sumsq, 0, 2 * s->nstages * sizeof(unsigned long long), s->stream);
     for (uint32_t i = 0; i < steps && e == cudaSuccess; ++i) e = launch_decode_step(a, s->step, s->stream);
     if (e != cudaSuccess) return (int)e;
     s->len += steps;

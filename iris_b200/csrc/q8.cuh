@@ -87,8 +87,8 @@ struct ProductArgs {
   int32_t softcap;
   uint32_t row_base;         // global index of row 0 in first-maximum keys (vocabulary shards)
   int64_t* partial;          // EPI_PARTIAL: [tokens][rows][4] limbs
-  unsigned long long* sumsq; // decode EPI_RESID (optional): the 128-bit sum of the squares of the
-                             // written values, added atomically (two words, lo then hi)
+  unsigned long long* sumsq; // decode EPI_RESID (optional): receives the sum of the squares of the
+                             // values this block wrote, clamped to i64::MAX
   const uint32_t* xepoch;    // EPI_PARTIAL into a peer-exchange slot: partial + ((epoch + 1) & 1) rows 4
   // Decode GEMV split scratch (optional): 2 words a row and a slice count a
   // tile group for split_groups groups, all zero between launches.

@@ -103,9 +103,15 @@ __device__ __forceinline__ void step_consumers_arrive(const StepArgs& A, uint32_
   }
 }
 
+// The sum of squares slots of stage k: one a block, each clamped to
+// i64::MAX (the norm's saturating sum of non-negative terms clamps there too).
+__device__ __forceinline__ unsigned long long* step_sumsq_slot(const StepArgs& A, uint32_t k) {
+  return A.sumsq + (size_t)k * gridDim.x + blockIdx.x;
+}
+
 // x = dequantize_row(embed[token]) (q8.rs:76-91); blocks take 512 values
-// each and add the squares of theirs into the stage's sum of squares.
-__device__ __forceinline__ void step_embed(const StepArgs& A) {
+// each and leave the sum of the squares of theirs in their slot.
+__device__ __forceinline__ void step_embed(const StepArgs& A, Acc128* warp_sq) {
   const uint32_t tok = *A.d_token;
   Acc128 sq{0, 0};
   for (uint32_t i = blockIdx.x * kStepConsumers + threadIdx.x; i < A.H; i += gridDim.x * kStepConsumers) {
@@ -116,7 +122,13 @@ __device__ __forceinline__ void step_embed(const StepArgs& A) {
     acc128_add(sq, (uint64_t)((int64_t)v * v), 0);
   }
   sq = warp_sum_acc128(sq);
-  if ((threadIdx.x & 31) == 0 && (sq.lo | (uint64_t)sq.hi)) atomic_add_acc128(A.sumsq, sq);
+  if ((threadIdx.x & 31) == 0) warp_sq[threadIdx.x >> 5] = sq;
+  part_sync<kStepConsumers>();
+  if (threadIdx.x < 32) {
+    Acc128 t = threadIdx.x < kStepConsumers / 32 ? warp_sq[threadIdx.x] : Acc128{0, 0};
+    t = warp_sum_acc128(t);
+    if (threadIdx.x == 0) *step_sumsq_slot(A, 0) = (t.hi || t.lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : t.lo;
+  }
 }
 
 // The byte planes of rms_norm(x) (ops.rs:98-114) for a product whose input is
@@ -138,9 +150,12 @@ __device__ __forceinline__ bool step_norm_planes(const StepArgs& A, uint32_t k, 
       xv[j] = i < K ? __ldcg((const int4*)(A.x + i)) : make_int4(0, 0, 0, 0);
     }
   }
-  if (threadIdx.x < 32) {
-    const uint64_t lo = __ldcg(A.sumsq + 2 * (k - 1)), hi = __ldcg(A.sumsq + 2 * (k - 1) + 1);
-    const uint64_t total = (hi || lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : lo;
+  if (threadIdx.x < 32) {  // the blocks' shares of stage k - 1, summed exactly, then clamped
+    const unsigned long long* slots = A.sumsq + (size_t)(k - 1) * gridDim.x;
+    Acc128 t{0, 0};
+    for (uint32_t b = threadIdx.x; b < gridDim.x; b += 32) acc128_add(t, __ldcg(slots + b), 0);
+    t = warp_sum_acc128(t);
+    const uint64_t total = (t.hi || t.lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : t.lo;
     const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), A.eps));
     if (threadIdx.x == 0) *s_scale = sc;
   }
@@ -214,7 +229,7 @@ __device__ __forceinline__ ProductArgs step_product_args(const StepArgs& A, cons
   } else if (st.kind == STEP_O || st.kind == STEP_DOWN) {
     a.out = A.x;
     a.resid = A.x;
-    a.sumsq = A.sumsq + 2 * k;  // for the normalised input of stage k + 1
+    a.sumsq = step_sumsq_slot(A, k);  // for the normalised input of stage k + 1
   } else if (st.kind == STEP_GU) {
     a.out_planes = A.planes2;
   } else {  // STEP_HEAD
@@ -233,11 +248,7 @@ __device__ __forceinline__ void step_finish(const StepArgs& A, uint32_t p) {
   if (A.history && step < A.history_cap) A.history[step] = tok;
   *A.d_step = step + 1;
   *A.d_pos = p + 1;
-  for (uint32_t k = 0; k < A.nstages; ++k) {
-    A.sync[k] = 0;
-    A.sumsq[2 * k] = 0;
-    A.sumsq[2 * k + 1] = 0;
-  }
+  for (uint32_t k = 0; k < A.nstages; ++k) A.sync[k] = 0;
 }
 
 // ---- attention stage --------------------------------------------------------
@@ -247,6 +258,7 @@ struct StepAttnShared {
   unsigned long long best[HPC], sum[HPC], gbest[HPC], gtot[HPC], ginv[HPC];
   int32_t wsum[HPC], resid[HPC];
   bool last;
+  Acc128 warp_sq[kStepConsumers / 32];  // the embedding stage's per-warp sums of squares
 };
 
 // Bounded arrival barrier of the `chunks` blocks of one head group.
@@ -681,7 +693,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
   for (uint32_t k = 0; k < A.nstages; ++k) {
     const StepStage st = stages[k];
     if (st.kind == STEP_EMBED) {
-      step_embed(A);
+      step_embed(A, ash.warp_sq);
       step_consumers_arrive(A, k);
       continue;
     }

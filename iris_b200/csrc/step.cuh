@@ -74,7 +74,7 @@ struct StepArgs {
   uint32_t* history;
   uint32_t history_cap;
   unsigned int* sync;    // [nstages] arrivals a stage of the running pass (zero between launches)
-  unsigned long long* sumsq;  // [nstages][2] 128-bit sums of squares of the x a stage wrote (zero between launches)
+  unsigned long long* sumsq;  // [nstages][blocks] each block's sum of squares of the x it wrote, clamped to i64::MAX
   unsigned int* fault;
   unsigned long long* trace;  // optional timeline of the last pass: [block][stage][kStepTraceEvents] ns
   // shared-memory layout

@@ -51,6 +51,23 @@ def test_requantize_mul_sat_div_act(S, L):
                 assert S.shim_div_act(a, b) == L.oracle_div_act(a, b), (a, b)
 
 
+def test_mul_sat_rounding_ties_and_extremes(S, L):
+    """mul_sat's one-addition rounding against the oracle where it matters:
+    products exactly halfway (r = 2^15) with odd and even quotients of both
+    signs, one unit either side of halfway, and the saturating extremes."""
+    cases = []
+    for f in range(-6, 7):
+        for r in (0x7FFF, 0x8000, 0x8001, 0, 1, 0xFFFF):
+            x = f * 65536 + r
+            cases += [(x, 1), (-x, 1), (x, -1)]
+    for a in (2**31 - 1, -(2**31), 2**30, -(2**30), 46341, -46341, 65535, 65536, 32768, 98304):
+        for b in (2**31 - 1, -(2**31), 1, -1, 2, 3, 65536, 32768, 65537):
+            cases.append((a, b))
+    for a, b in cases:
+        if -(2**31) <= a < 2**31 and -(2**31) <= b < 2**31:
+            assert S.shim_mul_sat(a, b) == L.oracle_mul_sat(a, b), (a, b)
+
+
 def test_inv_sqrt_and_rms_scale(S, L):
     rng = np.random.default_rng(2)
     xs = [1, 2, 3, 4, 42950, 4295, 2**32, 2**32 + 1, 2**62, 2**63 - 1, 7, 1 << 20]
