@@ -165,6 +165,7 @@ struct IrisSession {
   unsigned int* sync = nullptr;  // [nstages] arrival counters
   unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
   unsigned long long* sumsq = nullptr;  // [nstages][blocks] sums of squares of the residual stream
+  uint32_t xchanges = 0;                // tensor parallelism: exchanges a pass
   int decode_mode = IRIS_DECODE_AUTO;
   int attn_mode = IRIS_ATTN_AUTO;
   bool use_step = false;
@@ -194,8 +195,9 @@ void free_session(IrisSession* s) {
 // model or capacity needs the kernel-per-operation pass.
 cudaError_t setup_step(IrisSession* s) {
   IrisModel* m = s->m;
-  s->step.why = 6;  // not a single-GPU mistral-dense model
-  if (m->family != kFamilyMistral || m->tp_world != 1 || !m->embed || !m->head) return cudaSuccess;
+  s->step.why = 6;  // not a mistral-dense model (with the peer-memory exchange when tensor-parallel)
+  if (m->family != kFamilyMistral || !m->embed || !m->head) return cudaSuccess;
+  if (m->tp_world > 1 && (!m->xch.part || m->tp_world > kTpMaxWorld)) return cudaSuccess;
   std::vector<StepStage> st;
   std::vector<uint32_t> kcs;
   auto product = [&](uint32_t kind, uint32_t layer, const Q8GpuMatrix* w, const int32_t* norm) {
@@ -222,6 +224,18 @@ cudaError_t setup_step(IrisSession* s) {
     x.layer = layer;
     st.push_back(x);
   };
+  // with tensor parallelism o and down leave partial sums that an exchange
+  // stage sums over the ranks (exchange j feeds on the product tagged j)
+  const bool tp = m->tp_world > 1;
+  uint32_t xj = 0;
+  auto exchange = [&](uint32_t layer) {
+    st.back().xj = ++xj;
+    StepStage x{};
+    x.kind = STEP_XCHG;
+    x.layer = layer;
+    x.xj = xj;
+    st.push_back(x);
+  };
   plain(STEP_EMBED, 0);
   for (uint32_t l = 0; l < m->L; ++l) {
     const LayerDev& L = m->layers[l];
@@ -229,8 +243,10 @@ cudaError_t setup_step(IrisSession* s) {
     product(STEP_QKV, l, L.qkv, L.norm_attn);
     plain(STEP_ATTN, l);
     product(STEP_O, l, L.o, nullptr);
+    if (tp) exchange(l);
     product(STEP_GU, l, L.gu, L.norm_ffn);
     product(STEP_DOWN, l, L.down, nullptr);
+    if (tp) exchange(l);
   }
   product(STEP_HEAD, 0, m->head, m->final_norm);
   StepPlan plan = plan_decode_step(m->H, m->F, m->heads, m->kvh, m->d, m->V, s->cap, kcs.data(), (uint32_t)kcs.size());
@@ -246,6 +262,7 @@ cudaError_t setup_step(IrisSession* s) {
   if (e == cudaSuccess) e = cudaMemset(s->sumsq, 0, st.size() * plan.blocks * sizeof(unsigned long long));
   if (e != cudaSuccess) return e;
   s->nstages = (uint32_t)st.size();
+  s->xchanges = xj;
   s->step = plan;
   s->use_step = true;
   return cudaSuccess;
@@ -297,6 +314,20 @@ StepArgs step_args(IrisSession* s) {
   a.fault = s->fault;
   a.trace = s->trace;
   a.sumsq = s->sumsq;
+  if (m->tp_world > 1) {
+    a.tp_rank = m->tp_rank;
+    a.tp_world = m->tp_world;
+    a.xchanges = s->xchanges;
+    a.xpart = m->xch.part;
+    a.xflags = m->xch.flags;
+    a.xepoch = m->xch.epoch;
+    for (uint32_t j = 0; j < m->tp_world; ++j) {
+      a.xpeer_part[j] = m->xch.peer_part[j];
+      a.xpeer_flags[j] = m->xch.peer_flags[j];
+    }
+  } else {
+    a.tp_world = 1;
+  }
   a.ring_slots = s->step.ring_slots;
   a.slot_bytes = s->step.slot_bytes;
   a.planes_bytes = s->step.planes_bytes;
@@ -376,9 +407,12 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
   return 0;
 }
 
-// Whether decode passes run as the persistent step.
+// Whether decode passes run as the persistent step (tensor-parallel models:
+// only with the peer-memory exchange).
 void choose_decode_path(IrisSession* s) {
-  s->use_step = s->step.ok && s->decode_mode != IRIS_DECODE_GRAPH && s->attn_mode == IRIS_ATTN_AUTO;
+  const bool nccl_exchange = s->m->tp_world > 1 && s->m->xch_nccl;
+  s->use_step = s->step.ok && !nccl_exchange && s->decode_mode != IRIS_DECODE_GRAPH &&
+                s->attn_mode == IRIS_ATTN_AUTO;
 }
 
 // Product arguments with the session's GEMV split scratch.
@@ -698,6 +732,7 @@ int ensure_graph(IrisSession* s) {
 int decode_steps(IrisSession* s, uint32_t steps) {
   if (!s->has_logits) return IRIS_ESTATE;
   if ((uint64_t)s->len + steps > s->cap || (uint64_t)s->len + steps > s->m->max_positions) return IRIS_ERANGE;
+  choose_decode_path(s);
   if (s->use_step) {
     const StepArgs a = step_args(s);
     cudaError_t e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);

@@ -47,7 +47,9 @@ constexpr uint32_t kStepConsumers = kTmaConsumerWarps * 32;  // threads of the c
 constexpr int kStepProducerWarp = kTmaConsumerWarps;
 constexpr int kStepEpilogueWarp = kTmaEpilogueWarp;
 
-__device__ __forceinline__ bool step_is_product(uint32_t kind) { return kind != STEP_EMBED && kind != STEP_ATTN; }
+__device__ __forceinline__ bool step_is_product(uint32_t kind) {
+  return kind != STEP_EMBED && kind != STEP_ATTN && kind != STEP_XCHG;
+}
 
 // Tiles [*ib, *ie) of a product stage for block b of nb: whole tile groups,
 // spread evenly (the counts differ by at most one group). Splitting groups
@@ -203,9 +205,10 @@ __device__ __forceinline__ bool step_copy_planes(const uint8_t* src8, uint32_t K
   return part_or<kStepConsumers>(w);
 }
 
-// The epilogue arguments of product stage k.
+// The epilogue arguments of product stage k (xbase: the exchanges finished
+// before this pass).
 __device__ __forceinline__ ProductArgs step_product_args(const StepArgs& A, const StepStage& st, uint32_t k,
-                                                         uint32_t p) {
+                                                         uint32_t p, uint32_t xbase) {
   ProductArgs a{};
   a.rows = st.rows;
   a.cols = st.cols;
@@ -226,22 +229,108 @@ __device__ __forceinline__ ProductArgs step_product_args(const StepArgs& A, cons
     a.kcache = A.kcache + (size_t)st.layer * A.cap * A.kvd;
     a.vcache = A.vcache + (size_t)st.layer * A.cap * A.kvd;
     a.pos0 = p;
+  } else if ((st.kind == STEP_O || st.kind == STEP_DOWN) && A.tp_world > 1) {
+    // this rank's input columns: unrounded partial sums for exchange xj
+    a.partial = A.xpart + (size_t)((xbase + st.xj) & 1) * A.H * 4;
   } else if (st.kind == STEP_O || st.kind == STEP_DOWN) {
     a.out = A.x;
     a.resid = A.x;
     a.sumsq = step_sumsq_slot(A, k);  // for the normalised input of stage k + 1
   } else if (st.kind == STEP_GU) {
     a.out_planes = A.planes2;
-  } else {  // STEP_HEAD
+  } else {  // STEP_HEAD: this rank's vocabulary rows
     a.out = A.logits;
     a.best = A.best;
+    a.row_base = A.tp_rank * st.rows;
   }
   return a;
 }
 
+// Tensor parallelism: exchange xj of the pass. Every block of this rank has
+// written its partial limbs (the stage before); block 0 publishes the epoch
+// into every peer's flags (release, system scope: the blocks' writes are
+// ordered before it through the stage counter), every block waits - bounded -
+// for every peer's flag of the same epoch, then sums its rows' limbs over the
+// ranks (peers' slots read over NVLink), rounds once (q8.rs:69-71), adds the
+// residual and leaves the sum of squares of its rows in its slot. Slots
+// alternate by epoch parity: a rank rewrites one only after every peer has
+// published the next epoch, i.e. finished reading it.
+__device__ __forceinline__ void step_exchange(const StepArgs& A, uint32_t k, uint32_t epoch, Acc128* warp_sq) {
+  const uint32_t tid = threadIdx.x;
+  if (blockIdx.x == 0 && tid < A.tp_world && tid != A.tp_rank) st_release_sys(A.xpeer_flags[tid] + A.tp_rank, epoch);
+  if (tid < A.tp_world && tid != A.tp_rank && ld_acquire_sys(A.xflags + tid) < epoch) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+      if (ld_acquire_sys(A.xflags + tid) >= epoch) break;
+      if ((i & 63) == 0) {
+        if (*(volatile unsigned int*)A.fault) break;
+        if (global_ns() - t0 > 1000000000ull) {
+          atomicOr(A.fault, 1u);
+          break;
+        }
+      }
+    }
+  }
+  part_sync<kStepConsumers>();
+  const uint32_t r0 = (uint32_t)((uint64_t)blockIdx.x * A.H / gridDim.x);
+  const uint32_t r1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * A.H / gridDim.x);
+  const size_t slot = (size_t)(epoch & 1) * A.H * 4;
+  Acc128 sq{0, 0};
+  for (uint32_t row = r0 + tid; row < r1; row += kStepConsumers) {
+    Acc128 acc{0, 0};
+    for (uint32_t j = 0; j < A.tp_world; ++j) {
+      const int64_t* src = A.xpeer_part[j] + slot + (size_t)row * 4;
+      const longlong2 a = __ldcg((const longlong2*)src), b = __ldcg((const longlong2*)(src + 2));
+      acc128_add(acc, (uint64_t)a.x, 0);
+      acc128_add(acc, (uint64_t)a.y << 32, (int64_t)((uint64_t)a.y >> 32));
+      acc128_add(acc, 0, b.x);
+      acc128_add(acc, 0, (int64_t)((uint64_t)b.y << 32));
+    }
+    const int32_t y = add_sat(acc128_round_q24(acc), __ldcg(A.x + row));
+    A.x[row] = y;
+    acc128_add(sq, (uint64_t)((int64_t)y * y), 0);
+  }
+  sq = warp_sum_acc128(sq);
+  if ((tid & 31) == 0) warp_sq[tid >> 5] = sq;
+  part_sync<kStepConsumers>();
+  if (tid < 32) {
+    Acc128 t = tid < kStepConsumers / 32 ? warp_sq[tid] : Acc128{0, 0};
+    t = warp_sum_acc128(t);
+    if (tid == 0) *step_sumsq_slot(A, k) = (t.hi || t.lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : t.lo;
+  }
+}
+
 // Greedy bookkeeping of the pass (generation.rs:25-58), by the last block.
-__device__ __forceinline__ void step_finish(const StepArgs& A, uint32_t p) {
-  const uint32_t tok = best_key_token(__ldcg(A.best));
+// With tensor parallelism each rank holds the first maximum of its
+// vocabulary shard: it publishes it into every peer's key slot (value, then
+// the epoch with release semantics), waits - bounded - for every peer's, and
+// all ranks take the same global first maximum.
+__device__ __forceinline__ void step_finish(const StepArgs& A, uint32_t p, uint32_t xbase) {
+  unsigned long long key = __ldcg(A.best);
+  if (A.tp_world > 1) {
+    const uint32_t epoch = xbase + A.xchanges;
+    for (uint32_t j = 0; j < A.tp_world; ++j) {
+      if (j == A.tp_rank) continue;
+      unsigned long long* slot = tp_key_slots(A.xpeer_part[j], A.H) + 2 * A.tp_rank;
+      st_relaxed_sys(slot, key);
+      st_release_sys(slot + 1, (unsigned long long)epoch);
+    }
+    unsigned long long* mine = tp_key_slots(A.xpart, A.H);
+    for (uint32_t j = 0; j < A.tp_world; ++j) {
+      if (j == A.tp_rank) continue;
+      const uint64_t t0 = global_ns();
+      for (uint32_t i = 1; ld_acquire_sys(mine + 2 * j + 1) < epoch; ++i) {
+        if ((i & 63) == 0 && ((*(volatile unsigned int*)A.fault) || global_ns() - t0 > 1000000000ull)) {
+          atomicOr(A.fault, 1u);
+          break;
+        }
+      }
+      const unsigned long long other = __ldcg(mine + 2 * j);
+      key = other > key ? other : key;
+    }
+    *A.xepoch = epoch;
+  }
+  const uint32_t tok = best_key_token(key);
   *A.d_token = tok;
   *A.best = 0;
   const uint32_t step = *A.d_step;
@@ -634,6 +723,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
   }
   __syncthreads();
   const uint32_t p = *A.d_pos;  // this token's position (advanced by the previous launch)
+  const uint32_t xbase = A.tp_world > 1 ? *A.xepoch : 0;  // exchanges before this pass
 
   if (warp == kStepProducerWarp) {
     // lane 0 issues the weight tiles; the whole warp issues attention rows
@@ -670,17 +760,18 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
       if (!step_is_product(st.kind)) continue;
       uint32_t ib, ie;
       step_range(st, blockIdx.x, nb, &ib, &ie);
-      const ProductArgs a = step_product_args(A, st, k, p);
+      const ProductArgs a = step_product_args(A, st, k, p, xbase);
       if (st.kind == STEP_QKV) ring_epilogue<EPI_QKV_ROPE, true>(a, sums, j, ib, ie, st.nslices, A.fault);
       else if (st.kind == STEP_GU) ring_epilogue<EPI_SILU_MUL, true>(a, sums, j, ib, ie, st.nslices, A.fault);
       else if (st.kind == STEP_HEAD) ring_epilogue<EPI_LOGITS, true>(a, sums, j, ib, ie, st.nslices, A.fault);
+      else if (A.tp_world > 1) ring_epilogue<EPI_PARTIAL, true>(a, sums, j, ib, ie, st.nslices, A.fault);
       else ring_epilogue<EPI_RESID, true>(a, sums, j, ib, ie, st.nslices, A.fault);
       __syncwarp();
       if (lane == 0) {
         step_stamp(A, k, 7);
         __threadfence();
         if (k + 1 < A.nstages) red_add_release(A.sync + k, 1u);
-        else if (atom_add_acq_rel(A.sync + k, 1u) == nb - 1) step_finish(A, p);  // the head stage, last of all
+        else if (atom_add_acq_rel(A.sync + k, 1u) == nb - 1) step_finish(A, p, xbase);  // the head stage, last of all
       }
     }
     return;
@@ -700,6 +791,12 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
     if (st.kind == STEP_ATTN) {
       step_wait(A, k);
       step_attention<PER, HPC>(A, k, st.layer, p, planes, ash, ring, cc, stalled);
+      step_consumers_arrive(A, k);
+      continue;
+    }
+    if (st.kind == STEP_XCHG) {
+      step_wait(A, k);
+      step_exchange(A, k, xbase + st.xj, ash.warp_sq);
       step_consumers_arrive(A, k);
       continue;
     }

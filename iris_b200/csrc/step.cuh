@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "layers.cuh"
+#include "tp.cuh"
 
 namespace iris {
 
@@ -15,7 +16,8 @@ enum StepKind : uint32_t {
   STEP_O = 3,      // x = x + W_o ctx
   STEP_GU = 4,     // g = silu(W_gate m) * (W_up m), m = rms_norm(x)
   STEP_DOWN = 5,   // x = x + W_down g
-  STEP_HEAD = 6    // logits = W_head rms_norm(x); first maximum -> next token
+  STEP_HEAD = 6,   // logits = W_head rms_norm(x); first maximum -> next token
+  STEP_XCHG = 7    // tensor parallelism: x = x + round(sum over ranks of the o / down partial sums)
 };
 
 // One stage of the pass (a device array built once per session).
@@ -26,6 +28,7 @@ struct StepStage {
   uint32_t kind, layer;
   uint32_t rows, cols, kc, nslices, items;
   int32_t e_fast;
+  uint32_t xj;  // tensor parallelism: the pass's exchange (1-based) an o / down product feeds or an exchange is
 };
 
 // Timeline stamps a block records per stage (StepArgs::trace): 0 input ready,
@@ -79,6 +82,16 @@ struct StepArgs {
   unsigned long long* trace;  // optional timeline of the last pass: [block][stage][kStepTraceEvents] ns
   // shared-memory layout
   uint32_t ring_slots, slot_bytes, planes_bytes;
+  // tensor parallelism (tp_world > 1): the peer-memory exchange of tp.cuh.
+  // Exchange j of a pass has epoch *xepoch + j (the count advances by the
+  // pass's exchanges when the pass finishes); its limbs sit in slot
+  // epoch & 1 of every rank's xpart; flags and key slots as in tp.cu.
+  uint32_t tp_rank, tp_world, xchanges;
+  int64_t* xpart;
+  int64_t* xpeer_part[kTpMaxWorld];
+  uint32_t* xflags;
+  uint32_t* xpeer_flags[kTpMaxWorld];
+  uint32_t* xepoch;
 };
 
 // The launch plan of a model and cache capacity, or ok = false when the

@@ -79,14 +79,6 @@ __global__ void tp_finish_kernel(const int64_t* __restrict__ limbs, uint32_t tok
   out[i] = add_sat(acc128_round_q24(acc), resid[i]);
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ uint64_t ns_now() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -157,9 +149,12 @@ cudaError_t tp_exchange_setup(void* comm, uint32_t rank, uint32_t world, uint32_
   *x = TpExchange{};
   x->rank = rank;
   x->world = world;
+  x->rows = rows;
   x->fault = fault;
   if (world > kTpMaxWorld) return cudaErrorInvalidValue;
-  cudaError_t e = cudaMalloc((void**)&x->part, (size_t)2 * rows * 4 * sizeof(int64_t));
+  const size_t part_words = (size_t)2 * rows * 4 + 2 * kTpMaxWorld;  // limb slots, then key slots
+  cudaError_t e = cudaMalloc((void**)&x->part, part_words * sizeof(int64_t));
+  if (e == cudaSuccess) e = cudaMemset(x->part, 0, part_words * sizeof(int64_t));
   if (e == cudaSuccess) e = cudaMalloc((void**)&x->flags, kTpMaxWorld * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc((void**)&x->epoch, 2 * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemset(x->flags, 0, kTpMaxWorld * sizeof(uint32_t));

@@ -11,8 +11,8 @@ constexpr uint32_t kTpMaxWorld = 8;
 // Peer-memory exchange of one-token row-parallel products (tp.cu). Passed
 // by value to the finish kernel.
 struct TpExchange {
-  uint32_t rank, world;
-  int64_t* part;                    // this rank's two slots [2][rows][4] limbs
+  uint32_t rank, world, rows;
+  int64_t* part;                    // this rank's two slots [2][rows][4] limbs, then the key slots
   uint32_t* flags;                  // [world]: the last epoch each peer published
   uint32_t* epoch;                  // exchanges finished; epoch + 1 is the coming one
   uint32_t* done;                   // finish blocks done (last block advances the epoch)
@@ -20,6 +20,11 @@ struct TpExchange {
   uint32_t* peer_flags[kTpMaxWorld];
   unsigned int* fault;
 };
+// The first-maximum key slots of a rank (after its limb slots): [world][2] =
+// (key, epoch) written by each peer, epoch last with release semantics.
+__host__ __device__ inline unsigned long long* tp_key_slots(int64_t* part, uint32_t rows) {
+  return (unsigned long long*)(part + (size_t)2 * rows * 4);
+}
 // Allocates the slots and flags, opens every peer's over CUDA IPC (handles
 // gathered over NCCL). Every rank calls it together.
 cudaError_t tp_exchange_setup(void* comm, uint32_t rank, uint32_t world, uint32_t rows, TpExchange* x,

@@ -33,6 +33,7 @@ def main() -> None:
     p.add_argument("--out", required=True)
     p.add_argument("--untied", action="store_true", help="a separate head matrix (tensor parallelism shards it)")
     p.add_argument("--exchange", choices=["peer", "nccl"], default="peer")
+    p.add_argument("--path", choices=["auto", "graph", "step"], default="auto", help="decode path")
     a = p.parse_args()
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     import numpy as np
@@ -47,12 +48,15 @@ def main() -> None:
     dm = DeviceModel(cfg, seed=a.seed, tp=(a.rank, a.world, bytes.fromhex(a.id)))
     dm.set_tp_exchange(a.exchange)
     sess = dm.session(a.prompt_len + a.steps + 8)
+    sess.set_decode_path(a.path)
+    path = sess.decode_path
     toks, logits = sess.generate(prompt, a.steps, want_logits=True)
     toks2, _ = sess.generate(prompt, a.steps)
     sess.close()
     dm.close()
     if a.rank == 0:
-        np.savez(a.out, tokens=np.array(toks), logits=logits, tokens_graph=np.array(toks2), prompt=np.array(prompt))
+        np.savez(a.out, tokens=np.array(toks), logits=logits, tokens_graph=np.array(toks2), prompt=np.array(prompt),
+                 path=np.array(path))
 
 
 if __name__ == "__main__":

@@ -24,9 +24,13 @@ def gpu_count():
 
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("exchange,path", [("peer", "step"), ("peer", "graph"), ("nccl", "graph")])
 @pytest.mark.parametrize("config,seed,prompt_len,steps", [("parity-mistral", 41, 19, 10)])
-def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps, exchange):
+def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps, exchange, path):
+    """exchange "peer" with path "step": the persistent step on each rank,
+    the o / down partial sums exchanged inside it over peer memory and the
+    head's first maximum through peer key slots; "graph": one kernel per
+    operation (peer-memory finish kernel, or NCCL sums)."""
     from iris_b200 import _lib, build
     from iris_b200.model import synth_host_weights
     from iris_b200.shapes import CONFIGS
@@ -40,7 +44,7 @@ def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, see
     procs = [subprocess.Popen([sys.executable, "-m", "iris_b200.tp_worker", "--rank", str(r), "--world", "2",
                                "--id", nccl_id, "--config", config, "--seed", str(seed), "--prompt-seed", "3",
                                "--prompt-len", str(prompt_len), "--steps", str(steps), "--out", str(out), "--untied",
-                               "--exchange", exchange],
+                               "--exchange", exchange, "--path", path],
                               cwd=ROOT, env=env) for r in range(2)]
     try:
         codes = [p.wait(timeout=600) for p in procs]
@@ -50,6 +54,7 @@ def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, see
                 p.kill()
     assert codes == [0, 0], codes
     got = np.load(out)
+    assert str(got["path"]) == path
     cfg = CONFIGS[config]
     cfg = type(cfg)(**{**cfg.__dict__, "tied": False})  # the head is sharded by vocabulary
     want_tokens, want_logits = OracleModel(cfg, synth_host_weights(cfg, seed)).generate(got["prompt"].tolist(), steps)
