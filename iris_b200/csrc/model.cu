@@ -165,6 +165,7 @@ struct IrisSession {
   unsigned int* sync = nullptr;  // [nstages] arrival counters
   unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
   unsigned long long* sumsq = nullptr;  // [nstages][blocks] sums of squares of the residual stream
+  unsigned long long *kslots = nullptr, *sslots = nullptr;  // attention exchange slots [heads][blocks]
   uint32_t xchanges = 0;                // tensor parallelism: exchanges a pass
   int decode_mode = IRIS_DECODE_AUTO;
   int attn_mode = IRIS_ATTN_AUTO;
@@ -184,7 +185,7 @@ void free_session(IrisSession* s) {
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
-                  s->stages, s->sync, s->trace, s->sumsq};
+                  s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -258,6 +259,11 @@ cudaError_t setup_step(IrisSession* s) {
   if (e == cudaSuccess) e = cudaMemcpy(s->stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = dalloc(&s->sync, st.size());
   if (e == cudaSuccess) e = cudaMemset(s->sync, 0, st.size() * sizeof(unsigned int));
+  const size_t nslots = (size_t)m->heads * plan.blocks;
+  if (e == cudaSuccess) e = dalloc(&s->kslots, nslots);
+  if (e == cudaSuccess) e = dalloc(&s->sslots, nslots);
+  if (e == cudaSuccess) e = cudaMemset(s->kslots, 0, nslots * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(s->sslots, 0, nslots * sizeof(unsigned long long));
   if (e == cudaSuccess) e = dalloc(&s->sumsq, st.size() * plan.blocks);
   if (e == cudaSuccess) e = cudaMemset(s->sumsq, 0, st.size() * plan.blocks * sizeof(unsigned long long));
   if (e != cudaSuccess) return e;
@@ -298,8 +304,8 @@ StepArgs step_args(IrisSession* s) {
   a.best = s->best;
   a.split_acc = s->split_acc;
   a.split_count = s->split_count;
-  a.gbest = s->gbest;
-  a.gsum = s->gsum;
+  a.kslots = s->kslots;
+  a.sslots = s->sslots;
   a.wsum = s->wsum;
   a.acc = s->acc;
   a.gbar = s->gbar;

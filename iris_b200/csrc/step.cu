@@ -348,17 +348,53 @@ struct StepAttnShared {
   int32_t wsum[HPC], resid[HPC];
   bool last;
   Acc128 warp_sq[kStepConsumers / 32];  // the embedding stage's per-warp sums of squares
+  unsigned long long wbest[kStepConsumers / 32][HPC];  // each warp's first-maximum keys
 };
 
-// Bounded arrival barrier of the `chunks` blocks of one head group.
-__device__ __forceinline__ void step_group_barrier(unsigned int* bar, unsigned int target, unsigned int* fault) {
-  part_sync<kStepConsumers>();
-  if (threadIdx.x == 0) {
-    red_add_release(bar, 1u);
-    step_poll(bar, target, fault);
-  }
-  part_sync<kStepConsumers>();
+__device__ __forceinline__ void st_relaxed_gpu(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One exchange of a head group: every block of the group has published HPC
+// words (non-zero once written) into its own slots [chunk][HPC]; warp 0
+// waits - bounded - until all chunks x HPC are written and combines them per
+// head (the maximum, or the sum of the words minus one each), out[h].
+// Slots lane, lane + 32, ... all belong to head lane % HPC (32 % HPC == 0).
+template <uint32_t HPC, bool kMax>
+__device__ __forceinline__ void group_gather(const unsigned long long* slots, uint32_t chunks,
+                                             unsigned long long* out, unsigned int* fault) {
+  const uint32_t lane = threadIdx.x & 31, n = chunks * HPC;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    bool ready = true;
+    for (uint32_t i = lane; i < n; i += 32) ready &= ld_relaxed_gpu(slots + i) != 0;
+    if (__all_sync(0xffffffffu, ready)) break;
+    if ((it & 15) == 0) {
+      const bool give_up = *(volatile unsigned int*)fault || global_ns() - t0 > 1000000000ull;
+      if (__any_sync(0xffffffffu, give_up)) {
+        if (lane == 0) atomicOr(fault, 1u);
+        break;
+      }
+    }
+  }
+  unsigned long long v = 0;
+  for (uint32_t i = lane; i < n; i += 32) {
+    const unsigned long long w = ld_relaxed_gpu(slots + i);
+    v = kMax ? (w > v ? w : v) : v + (w ? w - 1 : 0);
+  }
+#pragma unroll
+  for (uint32_t off = 16; off >= HPC; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = kMax ? (o > v ? o : v) : v + o;
+  }
+  if (lane < HPC) out[lane] = v;
+}
+
 
 // Sums M values a lane over the W-lane groups of a warp (W a power of two,
 // M <= W): lane l of a group ends with the group's total of value
@@ -391,7 +427,7 @@ __device__ __forceinline__ uint64_t reduce_scatter_lanes(uint64_t (&v)[M], uint3
 // from the cache by the consumers.
 struct AttnChunk {
   bool active;
-  uint32_t h0, g, r0, r1, rc;
+  uint32_t grp, rank, h0, g, r0, r1, rc;
   unsigned int* bar;
 };
 template <uint32_t HPC>
@@ -401,6 +437,8 @@ __device__ __forceinline__ AttnChunk attn_chunk(const StepArgs& A, uint32_t p) {
   c.active = blockIdx.x < groups * chunks;
   if (!c.active) return c;
   const uint32_t grp = blockIdx.x / chunks, rank = blockIdx.x % chunks;
+  c.grp = grp;
+  c.rank = rank;
   c.h0 = grp * HPC;
   c.g = c.h0 / (A.heads / A.kv_heads);
   const uint32_t n = p + 1, span = (n + chunks - 1) / chunks;
@@ -475,7 +513,6 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
   unsigned int* bar = c.bar;
 
   if (tid < HPC) {
-    sh.best[tid] = 0;
     sh.sum[tid] = 0;
     sh.wsum[tid] = 0;
   }
@@ -490,10 +527,9 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     for (uint32_t i = 0; i < NV; ++i) q[h][i] = __ldcg((const int4*)(A.q + (size_t)(h0 + h) * D + 4 * (pl + LPP * i)));
   part_sync<kStepConsumers>();
 
-  // ---- 1. scores and each head's first maximum
-  unsigned long long best[HPC];
-#pragma unroll
-  for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
+  // ---- 1. scores and each head's first maximum (lane pl keeps the key of
+  // head pl / LPH, the head its exchange ends with)
+  unsigned long long best = 0;
   // The scores of local row t (all lanes of the warp take part in the
   // sums): each lane's HPC partial dot products are summed over the
   // position's LPP lanes with a halving exchange, after which lane pl holds
@@ -528,15 +564,19 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
 #pragma unroll
     for (uint32_t off = LPH / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     if (pl % LPH == 0 && live) {
-      const uint32_t h = pl / LPH;
       const int32_t sc = finish_score((int64_t)sum, SCORE_MISTRAL, A.scale_q32);
-      sw[t * HPC + h] = sc;
+      sw[t * HPC + pl / LPH] = sc;
       const unsigned long long key = best_key(sc, r0 + t);
-#pragma unroll
-      for (uint32_t hh = 0; hh < HPC; ++hh)
-        if (hh == h) best[hh] = key > best[hh] ? key : best[hh];
+      best = key > best ? key : best;
     }
   };
+  int4 kvp[NV];  // row p (written by this pass): its load starts before the slots are scored
+  if (has_p && warp == 0) {
+#pragma unroll
+    for (uint32_t i = 0; i < NV; ++i)
+      kvp[i] = pslot == 0 ? __ldcg((const int4*)(A.kcache + lay + (size_t)p * A.kvd + g * D + 4 * (pl + LPP * i)))
+                          : make_int4(0, 0, 0, 0);
+  }
   for (uint32_t sb = 0; sb < nsm; sb += per_slot) {
     const uint32_t nrows = min(per_slot, nsm - sb);
     if (!stalled && !ring_wait<true>(&ring.full[cc.slot], cc.parity, A.fault)) stalled = true;
@@ -555,25 +595,30 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     if (lane == 0) mbar_arrive(&ring.empty[cc.slot]);  // the slot's key rows are used
     ring_advance(ring, cc);
   }
-  if (has_p && warp == 0) {  // row p, written by this pass: from the cache, through L2
-    const bool live = pslot == 0;
-    int4 kv[NV];
+  if (has_p && warp == 0) score(kvp, pslot == 0, nsm);
+  // the warp's keys a head: its PW position slots (lanes pl + LPP j) meet
+  // by shuffles, then the sixteen warps through shared memory
 #pragma unroll
-    for (uint32_t i = 0; i < NV; ++i)
-      kv[i] = live ? __ldcg((const int4*)(A.kcache + lay + (size_t)p * A.kvd + g * D + 4 * (pl + LPP * i)))
-                   : make_int4(0, 0, 0, 0);
-    score(kv, live, nsm);
+  for (uint32_t off = LPP; off < 32; off <<= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+    best = o > best ? o : best;
   }
-#pragma unroll
-  for (uint32_t h = 0; h < HPC; ++h)
-    if (best[h]) atomicMax(&sh.best[h], best[h]);
+  if (lane < LPP && lane % LPH == 0) sh.wbest[warp][lane / LPH] = best;
   part_sync<kStepConsumers>();
-  if (tid < HPC && sh.best[tid]) atomicMax(A.gbest + h0 + tid, sh.best[tid]);
+  if (tid < HPC) {
+    unsigned long long b = 0;
+    for (uint32_t w = 0; w < kWarps; ++w) b = sh.wbest[w][tid] > b ? sh.wbest[w][tid] : b;
+    sh.best[tid] = b;
+  }
+  part_sync<kStepConsumers>();
+  // exchange 1: the group's first maximum (an empty chunk publishes 1, below
+  // every key)
+  unsigned long long* kslots = A.kslots + (size_t)c.grp * A.chunks * HPC;
+  if (tid < HPC) st_relaxed_gpu(kslots + c.rank * HPC + tid, sh.best[tid] ? sh.best[tid] : 1ull);
   if (tid == 0) step_stamp(A, k, 2);
-  step_group_barrier(bar, A.chunks, A.fault);
-  if (tid == 0) step_stamp(A, k, 3);
-  if (tid < HPC) sh.gbest[tid] = __ldcg(A.gbest + h0 + tid);
+  if (warp == 0) group_gather<HPC, true>(kslots, A.chunks, sh.gbest, A.fault);
   part_sync<kStepConsumers>();
+  if (tid == 0) step_stamp(A, k, 3);
 
   // ---- 2. exp terms against the group's first maximum, their sums.
   // Element e = position * HPC + head: thread tid always meets head tid % HPC.
@@ -590,12 +635,14 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     if (lane < HPC && e) atomicAdd(&sh.sum[lane], (unsigned long long)e);
   }
   part_sync<kStepConsumers>();
-  if (tid < HPC && sh.sum[tid]) atomicAdd(A.gsum + h0 + tid, sh.sum[tid]);
-  step_group_barrier(bar, 2 * A.chunks, A.fault);
+  // exchange 2: the sums of exp terms (each published plus one: non-zero)
+  unsigned long long* sslots = A.sslots + (size_t)c.grp * A.chunks * HPC;
+  if (tid < HPC) st_relaxed_gpu(sslots + c.rank * HPC + tid, sh.sum[tid] + 1);
+  if (warp == 0) group_gather<HPC, false>(sslots, A.chunks, sh.gtot, A.fault);
+  part_sync<kStepConsumers>();
   if (tid == 0) step_stamp(A, k, 4);
   if (tid < HPC) {
-    const unsigned long long tot = __ldcg(A.gsum + h0 + tid);
-    sh.gtot[tid] = tot;
+    const unsigned long long tot = sh.gtot[tid];
     sh.ginv[tid] = tot ? UINT64_MAX / tot : 0;  // tot >= 2^32 after a complete exchange
   }
   part_sync<kStepConsumers>();
@@ -669,7 +716,7 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
   part_sync<kStepConsumers>();
   if (tid == 0) {
     __threadfence();
-    sh.last = atom_add_acq_rel(bar, 1u) == 3 * A.chunks - 1;
+    sh.last = atom_add_acq_rel(bar, 1u) == A.chunks - 1;
   }
   part_sync<kStepConsumers>();
   if (!sh.last) return;
@@ -684,10 +731,10 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     s += (uint64_t)((int64_t)sh.resid[h] * __ldcg(A.vcache + lay + (size_t)tmax * A.kvd + g * D + i));
     put_planes(A.planes, A.qd, hh * D + i, requantize((int64_t)s));
   }
-  if (tid < HPC) {
-    A.gbest[h0 + tid] = 0;
-    A.gsum[h0 + tid] = 0;
-    A.wsum[h0 + tid] = 0;
+  if (tid < HPC) A.wsum[h0 + tid] = 0;
+  for (uint32_t i = tid; i < A.chunks * HPC; i += kStepConsumers) {  // every block has read them
+    kslots[i] = 0;
+    sslots[i] = 0;
   }
   if (tid == 0) bar[0] = 0;
 }

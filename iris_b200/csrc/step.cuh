@@ -62,9 +62,10 @@ struct StepArgs {
   unsigned long long* best;
   unsigned long long* split_acc;
   unsigned int* split_count;
-  // attention exchange words of a head group (zero between stages)
-  unsigned long long* gbest;
-  unsigned long long* gsum;
+  // attention exchanges of a head group (zero between stages): the blocks'
+  // first-maximum keys and exp-term sums, one slot [group][chunk][head] each
+  unsigned long long* kslots;
+  unsigned long long* sslots;
   int32_t* wsum;
   int64_t* acc;
   unsigned int* gbar;
