@@ -13,6 +13,7 @@
 //      1.0 - sum(weights) times the first maximum's value row (the same as
 //      adding it to that weight first, since no weight saturates) and
 //      requantizes.
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -1060,10 +1061,232 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) 
   }
 }
 
+// Many queries, one block a (query, head group): the group's HPC query heads
+// share each key and value row of the cache (one read for all of them).
+// attention_softmax (ops.rs:233-261) as in the decode kernels: scores with
+// LPP lanes a key row (the group's query pieces in registers) and each
+// head's first maximum, exp terms and their sums, weights by one exact
+// reciprocal a head, then the weighted value sums: warp w takes rows w,
+// w + 8, ..., lane l dimensions [4 l, 4 l + 4) (DL = D / 32 values), and the
+// eight warps' sums meet in shared memory. The residual 1.0 - sum(weights)
+// times the first maximum's value row is added before the one rounding
+// (the same as adding it to that weight, since no weight saturates).
+constexpr uint32_t kPrefillThreads = 256;
+
+template <uint32_t PER, uint32_t HPC>
+__global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr uint32_t D = PER * 8, kWarps = kPrefillThreads / 32, DL = D / 32;
+  constexpr uint32_t LPP = D / 4 < 16 ? D / 4 : 16, NV = D / LPP / 4, PW = 32 / LPP, LPH = LPP / HPC;
+  static_assert(HPC <= LPP && DL >= 1 && HPC * DL <= 16, "shapes");
+  extern __shared__ __align__(16) unsigned char sm[];
+  __shared__ unsigned long long wkey[kWarps][HPC], wsum[kWarps][HPC], gkey[HPC], ginv[HPC], gtot[HPC];
+  __shared__ int32_t wws[kWarps][HPC], resid[HPC];
+  const uint32_t tok = blockIdx.x, h0 = blockIdx.y * HPC, g = h0 / (a.heads / a.kv_heads);
+  const uint32_t p = a.pos0 + tok, ws = window_start(p, a.window), n = p - ws + 1;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, pl = lane % LPP, pslot = lane / LPP;
+  const uint32_t qd = a.heads * D;
+  int32_t* sw = (int32_t*)sm;                                           // [n][HPC] scores, then weights
+  uint64_t* tm = (uint64_t*)(sm + (((size_t)n * HPC * 4 + 15) & ~(size_t)15));  // [n][HPC] exp terms
+  const int32_t* kbase = a.kcache + (size_t)ws * a.kvd + g * D;
+  const int32_t* vbase = a.vcache + (size_t)ws * a.kvd + g * D;
+
+  int4 q[HPC][NV];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < NV; ++i)
+      q[h][i] = *(const int4*)(a.q + (size_t)tok * qd + (size_t)(h0 + h) * D + 4 * (pl + LPP * i));
+
+  // ---- 1. scores (lane pl keeps the key of head pl / LPH)
+  unsigned long long best = 0;
+  for (uint32_t base = 0; base < n; base += 2 * kWarps * PW) {
+    int4 kv[2][NV];
+#pragma unroll
+    for (uint32_t u = 0; u < 2; ++u) {
+      const uint32_t t = base + u * kWarps * PW + warp * PW + pslot;
+      const int32_t* krow = kbase + (size_t)(t < n ? t : n - 1) * a.kvd;
+#pragma unroll
+      for (uint32_t i = 0; i < NV; ++i) kv[u][i] = __ldg((const int4*)(krow + 4 * (pl + LPP * i)));
+    }
+#pragma unroll
+    for (uint32_t u = 0; u < 2; ++u) {
+      const uint32_t t = base + u * kWarps * PW + warp * PW + pslot;
+      uint64_t v[HPC];
+#pragma unroll
+      for (uint32_t h = 0; h < HPC; ++h) {
+        int64_t c0 = 0, c1 = 0;
+#pragma unroll
+        for (uint32_t i = 0; i < NV; ++i) {
+          mac_wide(c0, q[h][i].x, kv[u][i].x);
+          mac_wide(c1, q[h][i].y, kv[u][i].y);
+          mac_wide(c0, q[h][i].z, kv[u][i].z);
+          mac_wide(c1, q[h][i].w, kv[u][i].w);
+        }
+        v[h] = (uint64_t)c0 + (uint64_t)c1;
+      }
+#pragma unroll
+      for (uint32_t m = HPC, off = LPP / 2; m > 1; m >>= 1, off >>= 1) {
+        const bool upper = (pl & off) != 0;
+#pragma unroll
+        for (uint32_t i = 0; i < m / 2; ++i) {
+          const uint64_t send = upper ? v[i] : v[i + m / 2];
+          const uint64_t keep = upper ? v[i + m / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      uint64_t sum = v[0];
+#pragma unroll
+      for (uint32_t off = LPH / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      if (pl % LPH == 0 && t < n) {
+        const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
+        sw[t * HPC + pl / LPH] = sc;
+        const unsigned long long key = best_key(sc, t);
+        best = key > best ? key : best;
+      }
+    }
+  }
+#pragma unroll
+  for (uint32_t off = LPP; off < 32; off <<= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+    best = o > best ? o : best;
+  }
+  if (lane < LPP && lane % LPH == 0) wkey[warp][lane / LPH] = best;
+  __syncthreads();
+  if (tid < HPC) {
+    unsigned long long b = 0;
+    for (uint32_t w = 0; w < kWarps; ++w) b = wkey[w][tid] > b ? wkey[w][tid] : b;
+    gkey[tid] = b;
+  }
+  __syncthreads();
+
+  // ---- 2. exp terms against each head's first maximum, their sums.
+  // Element e = position * HPC + head: thread tid always meets head tid % HPC.
+  const uint32_t my_h = tid % HPC;
+  {
+    const int32_t mx = best_key_value(gkey[my_h]);
+    uint64_t e = 0;
+    for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
+      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
+      tm[el] = term;
+      e += term;
+    }
+    e = head_lane_sum<HPC>(e);
+    if (lane < HPC) wsum[warp][lane] = e;
+  }
+  __syncthreads();
+  if (tid < HPC) {
+    unsigned long long t = 0;
+    for (uint32_t w = 0; w < kWarps; ++w) t += wsum[w][tid];
+    gtot[tid] = t;
+    ginv[tid] = t ? UINT64_MAX / t : 0;
+  }
+  __syncthreads();
+
+  // ---- 3. weights and their sums
+  {
+    const uint64_t tot = gtot[my_h], inv = ginv[my_h];
+    int32_t wsl = 0;
+    for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
+      const int32_t w = tot ? softmax_weight_inv((int64_t)tm[el], tot, inv) : 0;
+      sw[el] = w;
+      wsl += w;
+    }
+    wsl = head_lane_sum<HPC>(wsl);
+    if (lane < HPC) wws[warp][lane] = wsl;
+  }
+  __syncthreads();
+  if (tid < HPC) {
+    int32_t t = 0;
+    for (uint32_t w = 0; w < kWarps; ++w) t += wws[w][tid];
+    resid[tid] = sub_sat(kOneAct, t);  // ops.rs:274-276
+  }
+
+  // ---- 4. value sums
+  uint64_t acc[HPC][DL];
+#pragma unroll
+  for (uint32_t h = 0; h < HPC; ++h)
+#pragma unroll
+    for (uint32_t i = 0; i < DL; ++i) acc[h][i] = 0;
+#pragma unroll 2
+  for (uint32_t t = warp; t < n; t += kWarps) {
+    const int32_t* vrow = vbase + (size_t)t * a.kvd + lane * DL;
+    int32_t v[DL];
+    if constexpr (DL % 4 == 0) {
+#pragma unroll
+      for (uint32_t i = 0; i < DL / 4; ++i) {
+        const int4 x = __ldg((const int4*)vrow + i);
+        v[4 * i] = x.x, v[4 * i + 1] = x.y, v[4 * i + 2] = x.z, v[4 * i + 3] = x.w;
+      }
+    } else if constexpr (DL == 2) {
+      const int2 x = __ldg((const int2*)vrow);
+      v[0] = x.x, v[1 % DL] = x.y;
+    } else {
+      v[0] = __ldg(vrow);
+    }
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      const int32_t w = sw[t * HPC + h];
+#pragma unroll
+      for (uint32_t i = 0; i < DL; ++i) acc[h][i] += (uint64_t)((int64_t)w * (int64_t)v[i]);
+    }
+  }
+  __syncthreads();  // every weight is read: tm's space takes the warps' sums
+  uint64_t* tree = tm;  // [kWarps / 2][HPC DL][32]
+  constexpr uint32_t NA = HPC * DL;
+  for (uint32_t half = kWarps / 2; half >= 1; half >>= 1) {
+    if (warp >= half && warp < 2 * half) {
+#pragma unroll
+      for (uint32_t v = 0; v < NA; ++v) tree[((warp - half) * NA + v) * 32 + lane] = acc[v / DL][v % DL];
+    }
+    __syncthreads();
+    if (warp < half) {
+#pragma unroll
+      for (uint32_t v = 0; v < NA; ++v) acc[v / DL][v % DL] += tree[(warp * NA + v) * 32 + lane];
+    }
+    __syncthreads();
+  }
+  if (warp == 0) {
+#pragma unroll
+    for (uint32_t h = 0; h < HPC; ++h) {
+      const uint32_t tmax = best_key_token(gkey[h]);
+#pragma unroll
+      for (uint32_t i = 0; i < DL; ++i) {
+        const uint32_t dim = lane * DL + i;
+        const uint64_t s = acc[h][i] + (uint64_t)((int64_t)resid[h] * __ldg(vbase + (size_t)tmax * a.kvd + dim));
+        const int32_t y = requantize((int64_t)s);
+        put_planes(a.ctx_planes + (size_t)tok * 4 * qd, qd, (h0 + h) * D + dim, y);
+        if (a.ctx) a.ctx[(size_t)tok * qd + (h0 + h) * D + dim] = y;
+      }
+    }
+  }
+}
+
+size_t prefill_group_smem(uint32_t hpc, uint32_t d, uint32_t max_visible) {
+  const size_t tree = (size_t)kPrefillThreads / 64 * hpc * (d / 32) * 32 * 8;  // [warps / 2][HPC DL][32] u64
+  const size_t terms = std::max((size_t)max_visible * hpc * 8, tree);
+  return (((size_t)max_visible * hpc * 4 + 15) & ~(size_t)15) + terms;
+}
+
+#define IRIS_PREFILL_SHAPES(X) X(4, 1) X(4, 2) X(4, 4) X(8, 1) X(8, 2) X(8, 4) X(16, 1) X(16, 2) X(16, 4) X(32, 1) X(32, 2)
+
 cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_t max_visible,
                                      cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   if (a.d % 4) return cudaErrorInvalidValue;
+  // the group kernel: the group's query heads share each cached row
+  const uint32_t G = a.heads / a.kv_heads, per = a.d / 8;
+  uint32_t hpc = 4;
+  while (hpc > 1 && (G % hpc || hpc * a.d > 512)) hpc >>= 1;
+  const size_t gsmem = prefill_group_smem(hpc, a.d, max_visible);
+  if (a.d % 32 == 0 && gsmem <= 200 * 1024) {
+    const dim3 grid(tokens, a.heads / hpc);
+#define IRIS_PREFILL_LAUNCH(PER, HPC) \
+    if (per == PER && hpc == HPC) return launch_k(attn_prefill_group_kernel<PER, HPC>, grid, dim3(kPrefillThreads), gsmem, s, a);
+    IRIS_PREFILL_SHAPES(IRIS_PREFILL_LAUNCH)
+#undef IRIS_PREFILL_LAUNCH
+  }
   size_t smem = ((a.d * 4 + 15) & ~15u) + (size_t)max_visible * 12;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   dim3 grid(tokens, a.heads);
@@ -1072,6 +1295,12 @@ cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_
 
 cudaError_t prepare_layer_kernels() {
   cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+#define IRIS_PREFILL_PREPARE(PER, HPC)                                                                          \
+  if (e == cudaSuccess)                                                                                        \
+    e = cudaFuncSetAttribute(attn_prefill_group_kernel<PER, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                             200 * 1024);
+  IRIS_PREFILL_SHAPES(IRIS_PREFILL_PREPARE)
+#undef IRIS_PREFILL_PREPARE
   if (e == cudaSuccess) e = prepare_attention_cluster_kernels();
   return e;
 }
