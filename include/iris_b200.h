@@ -75,12 +75,18 @@ int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
 int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                            uint32_t tokens, int32_t* d_out, void* stream);
 /* Generic-kernel timing hooks for the Q8 sweep: same product, forced through
- * the decode GEMV (tokens must be 1) or the tiled GEMM. */
+ * the decode GEMV (tokens must be 1), the mma.sync GEMM or the tcgen05
+ * tensor-core GEMM. The automatic path takes the tensor-core GEMM for 32 or
+ * more tokens when the matrix qualifies (every row's block-scale exponents
+ * within 5 of each other, cols <= 22016), building its pre-scaled copy
+ * (3 bytes a weight) on the first such call; IRIS_PATH_TC on a matrix that
+ * does not qualify fails with cudaErrorInvalidValue. */
 int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                                 uint32_t tokens, int32_t* d_out, void* stream, int path);
 #define IRIS_PATH_AUTO 0
 #define IRIS_PATH_GEMV 1
 #define IRIS_PATH_GEMM 2
+#define IRIS_PATH_TC 3
 /* No counterpart in the reference. The same product as
  * iris_q8_product_device, allocating nothing: the GEMM path's byte planes
  * live in a fixed 16 MiB device array, so tokens > 1 needs
@@ -184,6 +190,18 @@ int iris_model_get_values(const IrisModel* model, int tensor, int32_t layer, int
                           uint64_t count);
 /* Device bytes held by the model's weights. */
 uint64_t iris_model_weight_bytes(const IrisModel* model);
+/* Many-token products (prefill, layer ranges) of a model: IRIS_GEMM_AUTO
+ * (default) runs them on the tcgen05 tensor-core GEMM for ranges of 32 or
+ * more tokens, over a pre-scaled copy of each qualifying matrix built on its
+ * first such product (3 bytes a weight, freed with the model; a matrix whose
+ * rows' block-scale exponents spread by more than 5 keeps the mma.sync GEMM);
+ * IRIS_GEMM_MMA runs them all on the mma.sync GEMM. */
+int iris_model_set_gemm(IrisModel* model, int mode);
+#define IRIS_GEMM_AUTO 0
+#define IRIS_GEMM_MMA 1
+/* Number of the model's matrices holding a tensor-core copy; *bytes (if not
+ * NULL) receives the device bytes those copies take. */
+int iris_model_tc_matrices(const IrisModel* model, uint64_t* bytes);
 void iris_model_free(IrisModel* model);
 
 /* A decoding session: the K/V cache for up to max_positions positions. */

@@ -17,7 +17,8 @@ LIB_PATH = PKG / "libiris_b200.so"
 IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 10001, 10002, 10003, 10004, 10005, 10006
 IRIS_ESCRATCH = 10007
 NOALLOC_PLANES_BYTES = 16 << 20
-PATH_AUTO, PATH_GEMV, PATH_GEMM = 0, 1, 2
+PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_TC = 0, 1, 2, 3
+GEMM_AUTO, GEMM_MMA = 0, 1
 ATTN_AUTO, ATTN_SPLIT, ATTN_CLUSTER = 0, 1, 2
 DECODE_AUTO, DECODE_GRAPH, DECODE_STEP = 0, 1, 2
 
@@ -83,6 +84,8 @@ SIGNATURES = {
     "iris_model_get_q8": (C.c_int, [vp, C.c_int, C.c_int32, u8p, C.c_uint64]),
     "iris_model_get_values": (C.c_int, [vp, C.c_int, C.c_int32, i32p, C.c_uint64]),
     "iris_model_weight_bytes": (C.c_uint64, [vp]),
+    "iris_model_set_gemm": (C.c_int, [vp, C.c_int]),
+    "iris_model_tc_matrices": (C.c_int, [vp, C.POINTER(C.c_uint64)]),
     "iris_model_free": (None, [vp]),
     "iris_session_create": (C.c_int, [vp, C.c_uint32, C.POINTER(vp)]),
     "iris_session_reset": (C.c_int, [vp]),

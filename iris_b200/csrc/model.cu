@@ -24,6 +24,7 @@
 #include "../../include/iris_b200.h"
 #include "layers.cuh"
 #include "step.cuh"
+#include "tc.cuh"
 #include "tp.cuh"
 #include "synth.cuh"
 
@@ -125,6 +126,7 @@ struct IrisModel {
   void* comm = nullptr;
   TpExchange xch{};       // peer-memory exchange of one-token row-parallel products
   bool xch_nccl = false;  // exchange one-token products over NCCL instead
+  int gemm_mode = IRIS_GEMM_AUTO;  // many-token products: tensor-core GEMM where it applies, or mma.sync only
 };
 
 struct IrisSession {
@@ -423,7 +425,15 @@ void choose_decode_path(IrisSession* s) {
 
 // Product arguments with the session's GEMV split scratch.
 ProductArgs session_product_args(IrisSession* s, const Q8GpuMatrix* w, uint32_t tokens) {
+  // many-token products: the tensor-core copy of the weights, built on first use
+  const bool tc = s->m->gemm_mode == IRIS_GEMM_AUTO && tokens >= kTcMinTokens;
+  if (tc && w->tc_state == 0) tc_prepare(const_cast<Q8GpuMatrix*>(w), s->stream);
   ProductArgs a = product_args(w, tokens);
+  if (!tc) {
+    a.tc = nullptr;
+    a.tc_shift = nullptr;
+    a.tc_rows = 0;
+  }
   a.split_acc = s->split_acc;
   a.split_count = s->split_count;
   a.split_groups = s->split_groups;
@@ -1119,6 +1129,33 @@ int iris_model_synthesize(IrisModel* m, uint64_t seed, int per_block) {
 }
 
 uint64_t iris_model_weight_bytes(const IrisModel* m) { return m ? m->weight_bytes : 0; }
+
+int iris_model_set_gemm(IrisModel* m, int mode) {
+  if (!m || (mode != IRIS_GEMM_AUTO && mode != IRIS_GEMM_MMA)) return IRIS_EINVAL;
+  m->gemm_mode = mode;
+  return 0;
+}
+
+int iris_model_tc_matrices(const IrisModel* m, uint64_t* bytes) {
+  if (!m) return -1;
+  int n = 0;
+  uint64_t b = 0;
+  auto count = [&](const Q8GpuMatrix* w) {
+    if (w && w->tc_state == 1) {
+      ++n;
+      b += (uint64_t)3 * w->tc_rows * w->cols + w->tc_rows;
+    }
+  };
+  for (const LayerDev& L : m->layers) {
+    count(L.qkv);
+    count(L.o);
+    count(L.gu);
+    count(L.down);
+  }
+  count(m->head);
+  if (bytes) *bytes = b;
+  return n;
+}
 
 int iris_session_create(IrisModel* m, uint32_t max_positions, IrisSession** out) {
   if (!m || !out) return IRIS_EINVAL;

@@ -28,6 +28,7 @@
 
 #include "../../include/iris_b200.h"
 #include "gemv.cuh"
+#include "tc.cuh"
 #include "q8.cuh"
 #include "synth.cuh"
 
@@ -158,6 +159,8 @@ void free_q8(Q8GpuMatrix* m) {
     cudaFree(m->q);
     cudaFree(m->s);
   }
+  cudaFree(m->tc);
+  cudaFree(m->tc_shift);
   std::free(m);
 }
 
@@ -170,12 +173,28 @@ ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
   a.kc = w->kc;
   a.nslices = w->nslices;
   a.tokens = tokens;
+  if (w->tc_state == 1) {
+    a.tc = w->tc;
+    a.tc_shift = w->tc_shift;
+    a.tc_rows = w->tc_rows;
+  }
   return a;
+}
+
+// Drops the tensor-core copy of a matrix whose weights change.
+void tc_invalidate(Q8GpuMatrix* m) {
+  cudaFree(m->tc);
+  cudaFree(m->tc_shift);
+  m->tc = nullptr;
+  m->tc_shift = nullptr;
+  m->tc_rows = 0;
+  m->tc_state = 0;
 }
 
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
                              uint32_t cols, uint32_t row_stride, uint32_t row_offset,
                              int* bad_scale) {
+  tc_invalidate(dst);
   size_t bytes = (size_t)rows * (cols / 32) * 34;
   uint8_t* staging = nullptr;
   int* bad = nullptr;
@@ -223,6 +242,7 @@ cudaError_t synth_q8_block(Q8GpuMatrix* dst, uint64_t seed, uint32_t tensor, int
                            uint32_t cols, uint32_t row0, uint32_t col0, uint32_t full_cols, uint32_t row_stride,
                            uint32_t row_offset, int per_block, cudaStream_t stream) {
   if (cols % 32 || col0 % 32) return cudaErrorInvalidValue;
+  tc_invalidate(dst);
   uint64_t nblk = (uint64_t)rows * (cols / 32);
   if (nblk == 0) return cudaSuccess;
   return launch_k(synth_q8_kernel, dim3((unsigned)((nblk + 255) / 256)), dim3(256), 0, stream, dst->q, dst->s,
@@ -813,6 +833,7 @@ cudaError_t prepare_product_kernels() {
   cudaError_t e = prepare_gemv_in<IN_PLANES>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_NORM>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_RAW>();
+  if (e == cudaSuccess) e = prepare_tc_kernels();
   return e;
 }
 
@@ -850,7 +871,7 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
   if (a.out_stride == 0) a.out_stride = a.rows;
   if (a.tokens == 0 || a.rows == 0) return cudaSuccess;
   if (a.cols == 0 || a.cols % 32 || a.kc == 0) return cudaErrorInvalidValue;
-  bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
+  bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC) || path == IRIS_PATH_GEMV;
   if (gemv) {
     if (a.tokens != 1) return cudaErrorInvalidValue;
     switch (in) {
@@ -861,6 +882,8 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
     return cudaErrorInvalidValue;
   }
   if (in != IN_PLANES) return cudaErrorInvalidValue;  // callers build planes first
+  if (path == IRIS_PATH_TC || (path == IRIS_PATH_AUTO && a.tokens >= kTcMinTokens && tc_usable(a)))
+    return launch_gemm_tc(a, epi, stream);
   switch (epi) {
     case EPI_STORE: return launch_gemm<EPI_STORE>(a, stream);
     case EPI_RESID: return launch_gemm<EPI_RESID>(a, stream);
@@ -897,6 +920,16 @@ cudaError_t reserve(T** buf, size_t* cap, size_t bytes) {
   cudaError_t e = cudaMalloc((void**)buf, bytes);
   if (e == cudaSuccess) *cap = bytes;
   return e;
+}
+
+// Builds the matrix's tensor-core copy the first time a product that may use
+// it runs (many tokens on the automatic path, or the tensor-core path asked
+// for). The copy is a cache of the weights: the matrix stays logically const.
+cudaError_t prepare_tc_for(const Q8GpuMatrix* m, uint32_t tokens, int path, cudaStream_t s) {
+  if (m->tc_state != 0) return cudaSuccess;
+  if (path == IRIS_PATH_TC || (path == IRIS_PATH_AUTO && tokens >= kTcMinTokens))
+    return tc_prepare(const_cast<Q8GpuMatrix*>(m), s);
+  return cudaSuccess;
 }
 
 // The fp16 bits whose exact Q.24 value is v (inverse of q8.rs:27-43).
@@ -1007,20 +1040,25 @@ int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
 int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
                                 int32_t* d_out, void* stream, int path) {
   if (!m || tokens == 0) return tokens == 0 ? 0 : IRIS_EINVAL;
+  if (path < IRIS_PATH_AUTO || path > IRIS_PATH_TC) return IRIS_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;
-  ProductArgs a = product_args(m, tokens);
-  a.out = d_out;
-  bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM) || path == IRIS_PATH_GEMV;
+  bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC) || path == IRIS_PATH_GEMV;
   if (gemv) {
+    ProductArgs a = product_args(m, tokens);
+    a.out = d_out;
     a.x = d_act;
     return (int)launch_product(a, IN_RAW, EPI_STORE, s, IRIS_PATH_GEMV);
   }
-  // The tiled GEMM reads byte planes: build them into the shared scratch.
+  cudaError_t e = prepare_tc_for(m, tokens, path, s);
+  if (e != cudaSuccess) return (int)e;
+  ProductArgs a = product_args(m, tokens);
+  a.out = d_out;
+  // The tiled GEMMs read byte planes: build them into the shared scratch.
   std::lock_guard<std::mutex> lock(g_product_mutex);
-  cudaError_t e = reserve(&g_planes, &g_planes_bytes, (size_t)tokens * m->cols * 4);
+  e = reserve(&g_planes, &g_planes_bytes, (size_t)tokens * m->cols * 4);
   if (e == cudaSuccess) e = launch_planes(d_act, nullptr, 0, tokens, m->cols, g_planes, s);
   a.planes = g_planes;
-  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, IRIS_PATH_GEMM);
+  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, path);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // scratch is reused by the next call
   return (int)e;
 }
@@ -1076,8 +1114,8 @@ int iris_q8_product_device_noalloc(const Q8GpuMatrix* m, const int32_t* d_act, u
     return (int)launch_product(a, IN_RAW, EPI_STORE, s, IRIS_PATH_GEMV);
   }
   e = launch_planes(d_act, nullptr, 0, tokens, m->cols, planes, s);
-  a.planes = planes;
-  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, IRIS_PATH_GEMM);
+  a.planes = planes;  // the tensor-core GEMM when its copy is already built
+  if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, s, IRIS_PATH_AUTO);
   return (int)e;
 }
 
@@ -1090,6 +1128,7 @@ int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tok
   if (e == cudaSuccess) e = reserve(&g_out, &g_out_bytes, out_bytes);
   if (e == cudaSuccess && tokens > 1) e = reserve(&g_planes, &g_planes_bytes, act_bytes);
   if (e == cudaSuccess) e = cudaMemcpy(g_act, activations, act_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && tokens > 1) e = prepare_tc_for(m, tokens, IRIS_PATH_AUTO, 0);
   if (e != cudaSuccess) return (int)e;
   ProductArgs a = product_args(m, tokens);
   a.out = g_out;
@@ -1099,7 +1138,7 @@ int q8gpu_product(const Q8GpuMatrix* m, const int32_t* activations, uint32_t tok
   } else {
     e = launch_planes(g_act, nullptr, 0, tokens, m->cols, g_planes, 0);
     a.planes = g_planes;
-    if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, 0, IRIS_PATH_GEMM);
+    if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_STORE, 0, IRIS_PATH_AUTO);
   }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e == cudaSuccess) e = cudaMemcpy(out, g_out, out_bytes, cudaMemcpyDeviceToHost);

@@ -28,6 +28,14 @@ struct Q8GpuMatrix {
   uint32_t rows, cols;
   uint32_t kc, nslices, groups;
   bool owns;
+  // Tensor-core copy for many-token products (built on first use): byte
+  // planes p of W'[r][k] = q m 2^(e - shift[r]) at tc + (p * tc_rows + r) * cols
+  // (planes 0 and 1 unsigned, plane 2 signed), tc_rows = rows rounded up to
+  // 128. tc_state: 0 not built, 1 ready, 2 not usable.
+  uint8_t* tc;
+  uint8_t* tc_shift;
+  uint32_t tc_rows;
+  int tc_state;
 };
 
 namespace iris {
@@ -95,6 +103,10 @@ struct ProductArgs {
   unsigned long long* split_acc;
   unsigned int* split_count;
   uint32_t split_groups;
+  // The matrix's tensor-core copy (Q8GpuMatrix::tc), or NULL
+  const uint8_t* tc;
+  const uint8_t* tc_shift;
+  uint32_t tc_rows;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);

@@ -1,0 +1,424 @@
+// Many-token Q8_0 products on the tcgen05 tensor cores (kind::i8).
+//
+// The exact product (q8.rs:56-72) is sum over 32-value blocks b of
+// m_b 2^e_b * sum_{k in b} q_k a_k, rounded once (>> 24, ties to even). With
+// e0 the smallest exponent of a row, every weight becomes the integer
+// W'_k = q_k m_b 2^(e_b - e0), and the row's product is 2^e0 sum_k W'_k a_k:
+// one contraction over the whole K, with no per-block read-out. When a row's
+// exponents spread by at most kTcMaxSpread, |W'| < 2^23 and W' is three bytes
+// (w0, w1 unsigned, w2 signed); the Q16.16 activations are the four byte
+// planes a0..a2 (unsigned), a3 (signed) the other products use. So
+//   sum_k W'_k a_k = sum_{i,j} 2^(8 (i + j)) sum_k a_i[k] w_j[k],
+// twelve int8 contractions, one tcgen05 MMA each per 32 columns. The pairs
+// with equal i + j accumulate into one int32 TMEM accumulator (six
+// "diagonals"): each diagonal's true sum lies in [L_s, L_s + 2^32) for a
+// lower bound L_s known from K and the operand signs (K <= kTcMaxCols), so
+// its wrapped int32 value gives it back exactly. The epilogue adds the six
+// diagonals in 128 bits, shifts by e0, rounds once and applies the same
+// epilogues as the other products (RoPE and cache stores, gating, residual,
+// logits, partial limbs).
+//
+// A block: 128 weight rows (MMA M, TMEM lane = row) x 64 tokens (MMA N).
+// Warp 0 lane 0 issues the TMA loads (three weight planes of 128 rows x 128
+// columns, four activation planes of 64 tokens x 128 columns, 128-byte
+// swizzle) into a two-stage ring; warp 1 lane 0 issues the MMAs and commits
+// each stage back to the producer; sixteen epilogue warps wait for the last
+// commit, read the accumulators (tcgen05.ld) and finish the outputs. Every
+// wait is bounded (about one second) and records a give-up in the fault word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "detnum.cuh"
+#include "gemv.cuh"
+#include "tc.cuh"
+
+namespace iris {
+
+namespace {
+
+constexpr uint32_t kTcAPlane = kTcRows * kTcKChunk;             // bytes of one weight plane a stage
+constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one activation plane a stage
+constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
+constexpr uint32_t kTcStages = 2;
+constexpr uint32_t kTcEpiWarps = 16;
+constexpr uint32_t kTcThreads = 32 * (2 + kTcEpiWarps);
+constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to align the ring to 1024 bytes
+constexpr uint32_t kTcTmemCols = 512;                          // 6 diagonals x 64 tokens used
+constexpr uint32_t kTcDiagonals = 6;
+
+// Lower bounds of one column's contribution to each diagonal (i + j = s):
+// u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127.
+__host__ __device__ constexpr int64_t tc_diag_min(uint32_t s) {
+  return s == 2 ? -32640 : (s == 3 || s == 4) ? -65280 : s == 5 ? -16256 : 0;
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte rows in
+// the 128-byte swizzle (eight-row groups 1024 bytes apart), sm_100 version.
+__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: int32 accumulator, A (weights) and B (activations)
+// K-major, u8 or s8 each, M = 128, N = 64.
+__host__ __device__ constexpr uint32_t tc_idesc(bool a_signed, bool b_signed) {
+  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((kTcTok >> 3) << 17) |
+         ((kTcRows >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Arrives on `bar` once every MMA this thread issued so far has completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Eight consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 3-D tiled TMA load (no multicast) completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// The output of one (token, row) from its 128-bit total.
+template <int EPI>
+__device__ __forceinline__ void tc_finish(const ProductArgs& a, uint32_t tok, uint32_t row, const Acc128& tot,
+                                          uint32_t lane) {
+  int32_t v = acc128_round_q24(tot);
+  if (EPI == EPI_PARTIAL) {
+    if (tok < a.tokens && row < a.rows) limbs_from_acc128(tot.lo, tot.hi, a.partial + ((size_t)tok * a.rows + row) * 4);
+  } else if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+    const int32_t partner = __shfl_xor_sync(0xffffffffu, v, 1);  // row ^ 1, same token
+    if ((lane & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
+  } else if (EPI == EPI_LOGITS) {
+    if (tok < a.tokens && row < a.rows) {
+      if (a.softcap > 0) v = softcap_act(v, a.softcap);
+      if (a.out) a.out[(size_t)tok * a.out_stride + row] = v;
+      atomicMax(a.best + tok, best_key(v, row + a.row_base));
+    }
+  } else if (tok < a.tokens && row < a.rows) {
+    epi_single<EPI>(a, tok, row, v);
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    q8_gemm_tc_kernel(ProductArgs a, const __grid_constant__ CUtensorMap wmap,
+                      const __grid_constant__ CUtensorMap pmap, unsigned int* fault) {
+  extern __shared__ uint8_t tc_raw[];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ uint32_t tmem_slot;
+  uint8_t* ring = (uint8_t*)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t m0 = blockIdx.x * kTcTok, n0 = blockIdx.y * kTcRows;
+  const uint32_t nk = (a.cols + kTcKChunk - 1) / kTcKChunk;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kTcStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                 "r"(kTcTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  pdl_wait();  // the activation planes come from the kernel before
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      uint32_t issued[kTcStages] = {};
+      for (uint32_t kt = 0; kt < nk; ++kt) {
+        const uint32_t s = kt % kTcStages, use = kt / kTcStages;
+        if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) break;
+        uint8_t* st = ring + s * kTcStage;
+        mbar_arrive_expect_tx(&full[s], kTcStage);
+#pragma unroll
+        for (uint32_t j = 0; j < 3; ++j) tma_load_3d(st + j * kTcAPlane, &wmap, kt * kTcKChunk, n0, j, &full[s]);
+#pragma unroll
+        for (uint32_t i = 0; i < 4; ++i)
+          tma_load_3d(st + 3 * kTcAPlane + i * kTcBPlane, &pmap, kt * kTcKChunk, i, m0, &full[s]);
+        ++issued[s];
+      }
+      // every issued copy has landed before the block may exit
+      for (uint32_t s = 0; s < kTcStages; ++s)
+        if (issued[s]) mbar_wait_bounded(&full[s], (issued[s] - 1) & 1, fault);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      uint32_t touched = 0;
+      for (uint32_t kt = 0; kt < nk; ++kt) {
+        const uint32_t s = kt % kTcStages, use = kt / kTcStages;
+        if (!mbar_wait_bounded(&full[s], use & 1, fault)) break;
+        tc_fence_after();
+        const uint32_t base = smem_addr(ring + s * kTcStage);
+#pragma unroll
+        for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk) {
+#pragma unroll
+          for (uint32_t j = 0; j < 3; ++j) {
+            const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
+#pragma unroll
+            for (uint32_t i = 0; i < 4; ++i) {
+              const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
+              const uint32_t d = i + j;
+              tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
+              touched |= 1u << d;
+            }
+          }
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(&done);
+    }
+  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31
+    const bool ok = mbar_wait_bounded(&done, 0, fault);
+    tc_fence_after();
+    if (ok) {
+      const uint32_t quad = warp & 3, cg = (warp - 2) >> 2;
+      const uint32_t row = n0 + 32 * quad + lane;
+      const int32_t shift = row < a.tc_rows ? a.tc_shift[row] : 0;
+      int64_t lo_bound[kTcDiagonals];
+#pragma unroll
+      for (uint32_t d = 0; d < kTcDiagonals; ++d) lo_bound[d] = tc_diag_min(d) * (int64_t)a.cols;
+#pragma unroll 1
+      for (uint32_t h = 0; h < kTcTok / 4 / 8; ++h) {
+        const uint32_t c0 = cg * (kTcTok / 4) + h * 8;
+        uint32_t r[kTcDiagonals][8];
+#pragma unroll
+        for (uint32_t d = 0; d < kTcDiagonals; ++d) tmem_ld8(tmem + ((32 * quad) << 16) + d * kTcTok + c0, r[d]);
+        tmem_ld_wait();
+#pragma unroll
+        for (uint32_t t = 0; t < 8; ++t) {
+          int64_t T[kTcDiagonals];
+#pragma unroll
+          for (uint32_t d = 0; d < kTcDiagonals; ++d)
+            T[d] = lo_bound[d] + (int64_t)(uint32_t)(r[d][t] - (uint32_t)lo_bound[d]);
+          // |T| < 2^33: the first four fit one int64 at weights 2^0..2^24,
+          // the last two another at 2^32, 2^40
+          const int64_t lo = T[0] + T[1] * 256 + T[2] * 65536 + T[3] * 16777216;
+          const int64_t hi = T[4] + T[5] * 256;
+          Acc128 tot{0, 0};
+          acc128_add_shifted(tot, lo, shift);
+          acc128_add_shifted(tot, hi, shift + 32);
+          tc_finish<EPI>(a, m0 + c0 + t, row, tot, lane);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+  }
+}
+
+// One weight row a block: the row's smallest scale exponent (over blocks
+// with a non-zero scale), then the three byte planes of the pre-scaled
+// weights. *bad is set when a row's exponents spread wider than the planes
+// hold.
+__global__ void tc_planes_kernel(const int8_t* __restrict__ q, const uint16_t* __restrict__ s, uint32_t rows,
+                                 uint32_t cols, uint32_t kc, uint32_t nslices, uint32_t tc_rows,
+                                 uint8_t* __restrict__ planes, uint8_t* __restrict__ shift,
+                                 unsigned int* bad) {
+  __shared__ int smin, smax;
+  const uint32_t row = blockIdx.x, nb = cols / 32;
+  if (threadIdx.x == 0) {
+    smin = 64;
+    smax = -1;
+  }
+  __syncthreads();
+  if (row < rows) {
+    int lmin = 64, lmax = -1;
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) {
+      int32_t m, e;
+      q8_scale_parts_finite(s[q8_scale_offset(kc, nslices, row, b)], &m, &e);
+      if (m != 0) {
+        lmin = min(lmin, e);
+        lmax = max(lmax, e);
+      }
+    }
+    atomicMin(&smin, lmin);
+    atomicMax(&smax, lmax);
+  }
+  __syncthreads();
+  const int e0 = smax < 0 ? 0 : smin;
+  if (threadIdx.x == 0) {
+    shift[row] = (uint8_t)e0;
+    if (smax >= 0 && smax - smin > kTcMaxSpread) atomicOr(bad, 1u);
+  }
+  uint8_t* p0 = planes + (size_t)row * cols;
+  uint8_t* p1 = planes + ((size_t)tc_rows + row) * cols;
+  uint8_t* p2 = planes + ((size_t)2 * tc_rows + row) * cols;
+  for (uint32_t k = threadIdx.x * 4; k < cols; k += blockDim.x * 4) {
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+    if (row < rows) {
+      int32_t m, e;
+      q8_scale_parts_finite(s[q8_scale_offset(kc, nslices, row, k / 32)], &m, &e);
+      const char4 qv = *(const char4*)(q + q8_value_offset(kc, nslices, row, k));
+      const int32_t f = m != 0 ? m * (1 << min(e - e0, 8)) : 0;  // spread checked above
+      const int32_t w[4] = {qv.x * f, qv.y * f, qv.z * f, qv.w * f};
+#pragma unroll
+      for (uint32_t u = 0; u < 4; ++u) {
+        b0 |= ((uint32_t)w[u] & 0xFFu) << (8 * u);
+        b1 |= (((uint32_t)w[u] >> 8) & 0xFFu) << (8 * u);
+        b2 |= (((uint32_t)(w[u] >> 16)) & 0xFFu) << (8 * u);
+      }
+    }
+    *(uint32_t*)(p0 + k) = b0;
+    *(uint32_t*)(p1 + k) = b1;
+    *(uint32_t*)(p2 + k) = b2;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 3-D u8 tensor map (x innermost) with a 128-byte swizzled box.
+bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
+              uint64_t stride_z, uint32_t box_y, uint32_t box_z) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {x, y, z};
+  cuuint64_t strides[2] = {stride_y, stride_z};
+  cuuint32_t box[3] = {kTcKChunk, box_y, box_z};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI>
+cudaError_t launch_tc_one(const ProductArgs& a, cudaStream_t stream) {
+  CUtensorMap wmap, pmap;
+  if (!make_map(&wmap, a.tc, a.cols, a.tc_rows, 3, a.cols, (uint64_t)a.tc_rows * a.cols, kTcRows, 1) ||
+      !make_map(&pmap, a.planes, a.cols, 4, a.tokens, a.cols, (uint64_t)4 * a.cols, 1, kTcTok))
+    return cudaErrorInvalidValue;
+  unsigned int* fault = device_fault_word();
+  if (!fault) return cudaErrorInvalidValue;
+  const dim3 grid((a.tokens + kTcTok - 1) / kTcTok, a.tc_rows / kTcRows);
+  return launch_k(q8_gemm_tc_kernel<EPI>, grid, dim3(kTcThreads), kTcSmem, stream, a, wmap, pmap, fault);
+}
+
+template <int EPI>
+cudaError_t prepare_tc_one() {
+  return cudaFuncSetAttribute(q8_gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem);
+}
+
+}  // namespace
+
+cudaError_t prepare_tc_kernels() {
+  cudaError_t e = prepare_tc_one<EPI_STORE>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_RESID>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_QKV_ROPE>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_SILU_MUL>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_GELU_MUL>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_LOGITS>();
+  if (e == cudaSuccess) e = prepare_tc_one<EPI_PARTIAL>();
+  return e;
+}
+
+bool tc_usable(const ProductArgs& a) {
+  return a.tc && a.tc_shift && a.tc_rows % kTcRows == 0 && a.tc_rows >= a.rows && a.cols % 32 == 0 &&
+         a.cols <= kTcMaxCols && a.tokens > 0 && a.planes && ((uintptr_t)a.planes & 15) == 0 &&
+         ((uintptr_t)a.tc & 15) == 0 && a.tc_rows / kTcRows <= 65535 && tensor_map_encoder() != nullptr;
+}
+
+cudaError_t launch_gemm_tc(const ProductArgs& a, EpiMode epi, cudaStream_t stream) {
+  if (!tc_usable(a)) return cudaErrorInvalidValue;
+  switch (epi) {
+    case EPI_STORE: return launch_tc_one<EPI_STORE>(a, stream);
+    case EPI_RESID: return launch_tc_one<EPI_RESID>(a, stream);
+    case EPI_QKV_ROPE: return launch_tc_one<EPI_QKV_ROPE>(a, stream);
+    case EPI_SILU_MUL: return launch_tc_one<EPI_SILU_MUL>(a, stream);
+    case EPI_GELU_MUL: return launch_tc_one<EPI_GELU_MUL>(a, stream);
+    case EPI_LOGITS: return launch_tc_one<EPI_LOGITS>(a, stream);
+    case EPI_PARTIAL: return launch_tc_one<EPI_PARTIAL>(a, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream) {
+  if (m->tc_state != 0) return cudaSuccess;
+  m->tc_state = 2;
+  if (m->cols == 0 || m->cols % 32 || m->cols > kTcMaxCols || m->rows == 0) return cudaSuccess;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    m->tc_state = 0;  // not inside a capture; a later call builds it
+    return cudaSuccess;
+  }
+  const uint32_t tc_rows = (m->rows + kTcRows - 1) / kTcRows * kTcRows;
+  uint8_t *planes = nullptr, *shift = nullptr;
+  unsigned int* bad = nullptr;
+  if (cudaMalloc((void**)&planes, (size_t)3 * tc_rows * m->cols) != cudaSuccess ||
+      cudaMalloc((void**)&shift, tc_rows) != cudaSuccess || cudaMalloc((void**)&bad, 4) != cudaSuccess) {
+    cudaGetLastError();  // no room: the mma.sync GEMM serves this matrix
+    cudaFree(planes);
+    cudaFree(shift);
+    cudaFree(bad);
+    return cudaSuccess;
+  }
+  unsigned int h_bad = 1;
+  cudaError_t e = cudaMemsetAsync(bad, 0, 4, stream);
+  if (e == cudaSuccess) {
+    tc_planes_kernel<<<tc_rows, 256, 0, stream>>>(m->q, m->s, m->rows, m->cols, m->kc, m->nslices, tc_rows, planes,
+                                                  shift, bad);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&h_bad, bad, 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  cudaFree(bad);
+  if (e != cudaSuccess || h_bad) {
+    cudaFree(planes);
+    cudaFree(shift);
+    return e;
+  }
+  m->tc = planes;
+  m->tc_shift = shift;
+  m->tc_rows = tc_rows;
+  m->tc_state = 1;
+  return cudaSuccess;
+}
+
+}  // namespace iris

@@ -158,6 +158,17 @@ class DeviceModel:
     def weight_bytes(self) -> int:
         return int(lib().iris_model_weight_bytes(self._h))
 
+    def set_gemm(self, mode: str) -> None:
+        """Many-token products: 'auto' (tcgen05 tensor-core GEMM where a matrix
+        qualifies, default) or 'mma' (the mma.sync GEMM only)."""
+        check(lib().iris_model_set_gemm(self._h, {"auto": 0, "mma": 1}[mode]), "iris_model_set_gemm")
+
+    def tc_matrices(self):
+        """(number of matrices with a tensor-core copy, device bytes of those copies)."""
+        b = C.c_uint64(0)
+        n = lib().iris_model_tc_matrices(self._h, C.byref(b))
+        return int(n), int(b.value)
+
     def session(self, max_positions: int) -> "Session":
         return Session(self, max_positions)
 

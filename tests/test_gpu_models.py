@@ -197,12 +197,39 @@ def test_long_context_attention():
 
 
 def test_long_prompt_crosses_device_ranges():
-    """A 300-token prompt is processed as two device ranges (256 + 44)."""
+    """A 300-token prompt is processed as two device ranges (256 + 44), both
+    through the tensor-core GEMM (ranges of 32 or more tokens)."""
     from iris_b200.shapes import parity_mistral
     cfg = parity_mistral()
     prompt = seeded_prompt(9, 300, cfg.vocab)
-    _, _, _, got, want = run_both(cfg, 9, prompt, 3)
+    dm, _, _, got, want = run_both(cfg, 9, prompt, 3)
     assert_same(got, want)
+    n, nbytes = dm.tc_matrices()
+    assert n == 4 * cfg.layers and nbytes > 0  # every layer product took the tensor-core copy
+
+
+@pytest.mark.parametrize("per_block", [False, True])
+def test_prefill_tensor_core_and_mma_gemms_agree(per_block):
+    """The same prefill (ranges of 256 and 44 tokens) through the tcgen05 GEMM
+    and through the mma.sync GEMM: every logit and every K/V row equal."""
+    from iris_b200.model import DeviceModel, synth_host_weights
+    from iris_b200.shapes import parity_mistral
+    cfg = parity_mistral()
+    w = synth_host_weights(cfg, 41, per_block)
+    prompt = seeded_prompt(41, 300, cfg.vocab)
+    out = {}
+    for mode in ("auto", "mma"):
+        dm = DeviceModel(cfg, weights=w)
+        dm.set_gemm(mode)
+        sess = dm.session(len(prompt) + 8)
+        tok, logits = sess.prefill(prompt, want_logits=True)
+        kvs = [sess.kv(l, 0, len(prompt)) for l in range(cfg.layers)]
+        out[mode] = (tok, logits, *[x for kv in kvs for x in kv])
+        assert (dm.tc_matrices()[0] > 0) == (mode == "auto")
+    a, b = out["auto"], out["mma"]
+    assert a[0] == b[0]
+    for x, y in zip(a[1:], b[1:]):
+        assert np.array_equal(np.asarray(x), np.asarray(y))
 
 
 def test_eos_stops_the_loop_and_batches_agree():

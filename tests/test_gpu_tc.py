@@ -1,0 +1,143 @@
+"""GPU parity of the tcgen05 tensor-core GEMM (many-token Q8_0 products over
+the pre-scaled byte planes) against the CPU oracle, bit for bit.
+
+The product is the reference's dot_row per value (q8.rs:56-72); the cases
+push what the tensor-core form depends on: rows whose block-scale exponents
+spread by the most the three weight planes hold (5), weights of -128 and
+127, activations at i32::MIN / MAX (all four byte planes extreme), K up to
+the widest the int32 diagonal accumulators recover (22016), ragged row and
+token counts, and a matrix one exponent too wide, which the tensor-core path
+refuses and the automatic path serves with the mma.sync GEMM.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+I32_MIN, I32_MAX = -(2**31), 2**31 - 1
+
+
+@pytest.fixture(scope="module")
+def L():
+    from iris_b200 import build, _lib
+    build.build()
+    lib = _lib.lib()
+    assert lib.q8gpu_init() == 0, "no usable CUDA device"
+    return lib
+
+
+@pytest.fixture(scope="module")
+def O():
+    from oracle import oracle
+    oracle.build()
+    return oracle
+
+
+def spread_matrix(rng, rows, cols, base_ex, spread, q_extreme=False):
+    """Q8_0 blocks whose fp16 scale exponents lie in [base_ex, base_ex + spread]
+    for every row (random signs and mantissas); q uniform over all 256 byte
+    values, or only -128 / 127 when q_extreme."""
+    nb = rows * cols // 32
+    ex = base_ex + rng.integers(0, spread + 1, size=nb)
+    ex[:: max(1, cols // 32)] = base_ex + spread  # every row reaches both ends
+    ex[1:: max(1, cols // 32)] = base_ex
+    man = rng.integers(0, 1024, size=nb)
+    sign = rng.integers(0, 2, size=nb)
+    bits = (sign << 15) | (ex << 10) | man
+    out = np.empty((nb, 34), np.uint8)
+    out[:, 0] = bits & 0xFF
+    out[:, 1] = (bits >> 8) & 0xFF
+    if q_extreme:
+        out[:, 2:] = np.where(rng.integers(0, 2, size=(nb, 32)) == 1, 0x7F, 0x80)
+    else:
+        out[:, 2:] = rng.integers(0, 256, size=(nb, 32), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+def full_range_acts(rng, tokens, cols):
+    r = rng.integers(I32_MIN, I32_MAX, size=(tokens, cols), dtype=np.int64, endpoint=True)
+    sel = rng.integers(0, 17, size=(tokens, cols))
+    r = np.where(sel == 0, I32_MAX, np.where(sel == 1, I32_MIN, np.where(sel == 2, 0, r)))
+    return r.astype(np.int32)
+
+
+def run(L, blocks, rows, cols, acts, path):
+    import torch
+    from iris_b200 import _lib
+    h = C.c_void_p()
+    _lib.check(L.iris_q8_upload_blocks(_lib.ptr(blocks, C.c_uint8), rows, cols, C.byref(h)), "upload")
+    try:
+        a = torch.from_numpy(np.ascontiguousarray(acts, np.int32)).cuda()
+        out = torch.full((acts.shape[0], rows), 7, dtype=torch.int32, device="cuda")
+        rc = L.iris_q8_product_device_path(h, a.data_ptr(), acts.shape[0], out.data_ptr(), None, path)
+        torch.cuda.synchronize()
+        return rc, out.cpu().numpy()
+    finally:
+        L.q8gpu_free(h)
+
+
+@pytest.mark.parametrize("rows,cols,tokens,base_ex,spread", [
+    (128, 128, 64, 10, 5),
+    (200, 4096, 100, 1, 5),     # ragged rows and tokens; subnormal-adjacent exponents
+    (130, 1536, 33, 25, 3),
+    (64, 14336, 72, 12, 5),
+    (40, 22016, 40, 20, 5),     # the widest K
+])
+def test_tc_matches_oracle(L, O, rows, cols, tokens, base_ex, spread):
+    from iris_b200 import _lib
+    rng = np.random.default_rng(rows * 131 + cols + tokens)
+    blocks = spread_matrix(rng, rows, cols, base_ex, spread)
+    acts = full_range_acts(rng, tokens, cols)
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0, _lib.lib().iris_error(rc)
+    assert np.array_equal(got, want), np.argwhere(got != want)[:5]
+
+
+def test_tc_diagonal_sums_past_int32(L, O):
+    """Activations i32::MAX / MIN (byte planes 255, 255, 255, 127 / 0, 0, 0,
+    -128) against weights of 127 and -128 at the largest pre-scaled size:
+    the diagonal sums leave the int32 range and come back exactly."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(5)
+    rows, cols, tokens = 128, 14336, 64
+    blocks = spread_matrix(rng, rows, cols, 15, 5, q_extreme=True)
+    b = blocks.reshape(-1, 34)
+    b[:, 0] = 0xFF  # mantissa 2047
+    b[:, 1] = (b[:, 1] & 0xFC) | 0x03
+    acts = np.where(rng.integers(0, 4, size=(tokens, cols)) == 0, I32_MIN, I32_MAX).astype(np.int32)
+    acts[0, :] = I32_MAX
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0
+    assert np.array_equal(got, want)
+
+
+def test_tc_refuses_a_wider_spread_and_auto_falls_back(L, O):
+    from iris_b200 import _lib
+    rng = np.random.default_rng(11)
+    rows, cols, tokens = 96, 512, 48
+    blocks = spread_matrix(rng, rows, cols, 8, 6)
+    acts = full_range_acts(rng, tokens, cols)
+    want = O.linear(acts, blocks, rows)
+    rc, _ = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 1  # cudaErrorInvalidValue: the matrix does not qualify
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_AUTO)
+    assert rc == 0 and np.array_equal(got, want)
+
+
+def test_tc_equals_mma_gemm_at_2048_tokens(L):
+    """M = 2048 (the sweep's largest): the tensor-core GEMM against the
+    mma.sync GEMM on every output."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(2048)
+    rows, cols, tokens = 2048, 2048, 2048
+    blocks = spread_matrix(rng, rows, cols, 12, 4)
+    acts = full_range_acts(rng, tokens, cols)
+    rc, tc = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0
+    rc, mma = run(L, blocks, rows, cols, acts, _lib.PATH_GEMM)
+    assert rc == 0
+    assert np.array_equal(tc, mma)
