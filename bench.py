@@ -265,6 +265,7 @@ def main():
     sess = model.session(cap)
     sess.set_decode_path(args.decode_path)
     prompt = np.random.default_rng(seed).integers(0, cfg.vocab, size=args.prompt).tolist()
+    model.prepare_gemm()  # the prefill GEMM's pre-scaled weight copies, built once per model
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     tok, _ = sess.prefill(prompt)

@@ -199,6 +199,10 @@ uint64_t iris_model_weight_bytes(const IrisModel* model);
 int iris_model_set_gemm(IrisModel* model, int mode);
 #define IRIS_GEMM_AUTO 0
 #define IRIS_GEMM_MMA 1
+/* Builds the tensor-core copies of every layer matrix now (otherwise the
+ * first many-token product of each builds its own), so that a timed or
+ * latency-bound prefill does not pay for them. Synchronous. */
+int iris_model_prepare_gemm(IrisModel* model);
 /* Number of the model's matrices holding a tensor-core copy; *bytes (if not
  * NULL) receives the device bytes those copies take. */
 int iris_model_tc_matrices(const IrisModel* model, uint64_t* bytes);

@@ -1136,6 +1136,16 @@ int iris_model_set_gemm(IrisModel* m, int mode) {
   return 0;
 }
 
+int iris_model_prepare_gemm(IrisModel* m) {
+  if (!m) return IRIS_EINVAL;
+  if (m->gemm_mode != IRIS_GEMM_AUTO) return 0;
+  cudaError_t e = cudaSuccess;
+  for (LayerDev& L : m->layers)
+    for (Q8GpuMatrix* w : {L.qkv, L.o, L.gu, L.down})
+      if (w && e == cudaSuccess) e = tc_prepare(w, 0);
+  return (int)e;
+}
+
 int iris_model_tc_matrices(const IrisModel* m, uint64_t* bytes) {
   if (!m) return -1;
   int n = 0;

@@ -21,7 +21,9 @@
 // A block: 128 weight rows (MMA M, TMEM lane = row) x 64 tokens (MMA N).
 // Warp 0 lane 0 issues the TMA loads (three weight planes of 128 rows x 128
 // columns, four activation planes of 64 tokens x 128 columns, 128-byte
-// swizzle) into a two-stage ring; warp 1 lane 0 issues the MMAs and commits
+// swizzle) into a two-stage ring, and L2 prefetches of the weight tiles
+// kTcPrefetch stages ahead (the activations stay in L2: every block of a
+// launch reads them); warp 1 lane 0 issues the MMAs and commits
 // each stage back to the producer; sixteen epilogue warps wait for the last
 // commit, read the accumulators (tcgen05.ld) and finish the outputs. Every
 // wait is bounded (about one second) and records a give-up in the fault word.
@@ -44,11 +46,21 @@ constexpr uint32_t kTcAPlane = kTcRows * kTcKChunk;             // bytes of one 
 constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one activation plane a stage
 constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
 constexpr uint32_t kTcStages = 2;
+constexpr uint32_t kTcPrefetch = 6;
 constexpr uint32_t kTcEpiWarps = 16;
 constexpr uint32_t kTcThreads = 32 * (2 + kTcEpiWarps);
 constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to align the ring to 1024 bytes
-constexpr uint32_t kTcTmemCols = 512;                          // 6 diagonals x 64 tokens used
+constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDiagonals = 6;
+constexpr uint32_t kTcAccCols = kTcDiagonals * kTcTok;         // accumulators: columns [0, 384)
+// With kTcATmem the weight operand is copied into TMEM (tcgen05.cp), 32
+// columns of the three planes at a time (8 TMEM columns each), through
+// kTcAGroups groups after the accumulators, and the MMAs read it there. Off:
+// measured slower on B200 (the copies and the MMAs serialise), kept as the
+// documented alternative.
+constexpr bool kTcATmem = false;
+constexpr uint32_t kTcAGroups = 5;
+static_assert(kTcAccCols + kTcAGroups * 24 <= kTcTmemCols, "TMEM columns");
 
 // Lower bounds of one column's contribution to each diagonal (i + j = s):
 // u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127.
@@ -58,8 +70,11 @@ __host__ __device__ constexpr int64_t tc_diag_min(uint32_t s) {
 
 // Shared-memory matrix descriptor of a K-major tile with 128-byte rows in
 // the 128-byte swizzle (eight-row groups 1024 bytes apart), sm_100 version.
+// A start 32 k bytes into the rows addresses their columns 32 k ..: the
+// swizzle is a function of the address bits, as the TMA wrote them.
+static_assert(kTcKChunk == 128, "descriptor and tensor maps assume 128-byte rows");
 __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(8 * kTcKChunk >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor: int32 accumulator, A (weights) and B (activations)
@@ -76,6 +91,19 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uin
       "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
       : "memory");
 }
+// The same with A (128 rows x 32 bytes) in TMEM at column address `a`.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bd, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(bd), "r"(idesc), "r"(acc)
+      : "memory");
+}
+// Copies a 128-row x 32-byte shared-memory tile (descriptor sd) into TMEM
+// lanes 0-127, 8 columns from column address `t`.
+__device__ __forceinline__ void tc_cp(uint32_t t, uint64_t sd) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(t), "l"(sd) : "memory");
+}
 // Arrives on `bar` once every MMA this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
@@ -91,6 +119,12 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// L2 prefetch of a 3-D tile (no shared-memory destination).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
 
 // 3-D tiled TMA load (no multicast) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
@@ -128,7 +162,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     q8_gemm_tc_kernel(ProductArgs a, const __grid_constant__ CUtensorMap wmap,
                       const __grid_constant__ CUtensorMap pmap, unsigned int* fault) {
   extern __shared__ uint8_t tc_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done;
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done, agroup[kTcAGroups];
   __shared__ uint32_t tmem_slot;
   uint8_t* ring = (uint8_t*)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -141,6 +175,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&done, 1);
+    for (uint32_t g = 0; g < kTcAGroups; ++g) mbar_init(&agroup[g], 1);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -159,8 +194,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // producer
       uint32_t issued[kTcStages] = {};
+      for (uint32_t kt = 0; kt < nk && kt < kTcPrefetch; ++kt)
+        for (uint32_t j = 0; j < 3; ++j) tma_prefetch_3d(&wmap, kt * kTcKChunk, n0, j);
       for (uint32_t kt = 0; kt < nk; ++kt) {
         const uint32_t s = kt % kTcStages, use = kt / kTcStages;
+        if (kt + kTcPrefetch < nk)
+          for (uint32_t j = 0; j < 3; ++j) tma_prefetch_3d(&wmap, (kt + kTcPrefetch) * kTcKChunk, n0, j);
         if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) break;
         uint8_t* st = ring + s * kTcStage;
         mbar_arrive_expect_tx(&full[s], kTcStage);
@@ -177,14 +216,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
-      uint32_t touched = 0;
-      for (uint32_t kt = 0; kt < nk; ++kt) {
+      uint32_t touched = 0, g = 0;
+      bool ok = true;
+      for (uint32_t kt = 0; kt < nk && ok; ++kt) {
         const uint32_t s = kt % kTcStages, use = kt / kTcStages;
         if (!mbar_wait_bounded(&full[s], use & 1, fault)) break;
         tc_fence_after();
         const uint32_t base = smem_addr(ring + s * kTcStage);
 #pragma unroll
-        for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk) {
+        for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk, ++g) {
+          uint32_t acol = 0;
+          if (kTcATmem) {  // the group's TMEM columns are free once the MMAs that read them completed
+            const uint32_t grp = g % kTcAGroups, round = g / kTcAGroups;
+            if (round > 0 && !mbar_wait_bounded(&agroup[grp], (round - 1) & 1, fault)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            acol = tmem + kTcAccCols + grp * 24;
+#pragma unroll
+            for (uint32_t j = 0; j < 3; ++j) tc_cp(acol + 8 * j, tc_desc(base + j * kTcAPlane + kk * 32));
+          }
 #pragma unroll
           for (uint32_t j = 0; j < 3; ++j) {
             const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
@@ -192,11 +244,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (uint32_t i = 0; i < 4; ++i) {
               const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
               const uint32_t d = i + j;
-              tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
+              if (kTcATmem) tc_mma_ts(tmem + d * kTcTok, acol + 8 * j, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
+              else tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
               touched |= 1u << d;
             }
           }
+          if (kTcATmem) tc_commit(&agroup[g % kTcAGroups]);
         }
+        if (!ok) break;
         tc_commit(&empty[s]);
       }
       tc_commit(&done);

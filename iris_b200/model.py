@@ -163,6 +163,10 @@ class DeviceModel:
         qualifies, default) or 'mma' (the mma.sync GEMM only)."""
         check(lib().iris_model_set_gemm(self._h, {"auto": 0, "mma": 1}[mode]), "iris_model_set_gemm")
 
+    def prepare_gemm(self) -> None:
+        """Builds the tensor-core copies of the layer matrices now (not on first use)."""
+        check(lib().iris_model_prepare_gemm(self._h), "iris_model_prepare_gemm")
+
     def tc_matrices(self):
         """(number of matrices with a tensor-core copy, device bytes of those copies)."""
         b = C.c_uint64(0)
