@@ -21,9 +21,7 @@
 // A block: 128 weight rows (MMA M, TMEM lane = row) x 64 tokens (MMA N).
 // Warp 0 lane 0 issues the TMA loads (three weight planes of 128 rows x 128
 // columns, four activation planes of 64 tokens x 128 columns, 128-byte
-// swizzle) into a two-stage ring, and L2 prefetches of the weight tiles
-// kTcPrefetch stages ahead (the activations stay in L2: every block of a
-// launch reads them); warp 1 lane 0 issues the MMAs and commits
+// swizzle) into a two-stage ring; warp 1 lane 0 issues the MMAs and commits
 // each stage back to the producer; sixteen epilogue warps wait for the last
 // commit, read the accumulators (tcgen05.ld) and finish the outputs. Every
 // wait is bounded (about one second) and records a give-up in the fault word.
@@ -46,7 +44,6 @@ constexpr uint32_t kTcAPlane = kTcRows * kTcKChunk;             // bytes of one 
 constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one activation plane a stage
 constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
 constexpr uint32_t kTcStages = 2;
-constexpr uint32_t kTcPrefetch = 6;
 constexpr uint32_t kTcEpiWarps = 16;
 constexpr uint32_t kTcThreads = 32 * (2 + kTcEpiWarps);
 constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to align the ring to 1024 bytes
@@ -120,12 +117,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// L2 prefetch of a 3-D tile (no shared-memory destination).
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t x, int32_t y, int32_t z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
 // 3-D tiled TMA load (no multicast) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
                                             uint64_t* bar) {
@@ -194,12 +185,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // producer
       uint32_t issued[kTcStages] = {};
-      for (uint32_t kt = 0; kt < nk && kt < kTcPrefetch; ++kt)
-        for (uint32_t j = 0; j < 3; ++j) tma_prefetch_3d(&wmap, kt * kTcKChunk, n0, j);
       for (uint32_t kt = 0; kt < nk; ++kt) {
         const uint32_t s = kt % kTcStages, use = kt / kTcStages;
-        if (kt + kTcPrefetch < nk)
-          for (uint32_t j = 0; j < 3; ++j) tma_prefetch_3d(&wmap, (kt + kTcPrefetch) * kTcKChunk, n0, j);
         if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) break;
         uint8_t* st = ring + s * kTcStage;
         mbar_arrive_expect_tx(&full[s], kTcStage);
