@@ -22,9 +22,10 @@
 // Warp 0 lane 0 issues the TMA loads (three weight planes of 128 rows x 128
 // columns, four activation planes of 64 tokens x 128 columns, 128-byte
 // swizzle) into a two-stage ring; warp 1 lane 0 issues the MMAs and commits
-// each stage back to the producer; sixteen epilogue warps wait for the last
-// commit, read the accumulators (tcgen05.ld) and finish the outputs. Every
-// wait is bounded (about one second) and records a give-up in the fault word.
+// each stage back to the producer; sixteen epilogue warps wait for a tile's
+// last commit, read its accumulators (tcgen05.ld), release them and finish
+// the outputs while the next tile accumulates. Every wait is bounded (about
+// one second) and records a give-up in the fault word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -50,14 +51,7 @@ constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to alig
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDiagonals = 6;
 constexpr uint32_t kTcAccCols = kTcDiagonals * kTcTok;         // accumulators: columns [0, 384)
-// With kTcATmem the weight operand is copied into TMEM (tcgen05.cp), 32
-// columns of the three planes at a time (8 TMEM columns each), through
-// kTcAGroups groups after the accumulators, and the MMAs read it there. Off:
-// measured slower on B200 (the copies and the MMAs serialise), kept as the
-// documented alternative.
-constexpr bool kTcATmem = false;
-constexpr uint32_t kTcAGroups = 5;
-static_assert(kTcAccCols + kTcAGroups * 24 <= kTcTmemCols, "TMEM columns");
+static_assert(kTcAccCols <= kTcTmemCols, "TMEM columns");
 
 // Lower bounds of one column's contribution to each diagonal (i + j = s):
 // u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127.
@@ -88,19 +82,6 @@ __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uin
       "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
       : "memory");
 }
-// The same with A (128 rows x 32 bytes) in TMEM at column address `a`.
-__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bd, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
-      "r"(a), "l"(bd), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// Copies a 128-row x 32-byte shared-memory tile (descriptor sd) into TMEM
-// lanes 0-127, 8 columns from column address `t`.
-__device__ __forceinline__ void tc_cp(uint32_t t, uint64_t sd) {
-  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(t), "l"(sd) : "memory");
-}
 // Arrives on `bar` once every MMA this thread issued so far has completed.
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
@@ -127,14 +108,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
       : "memory");
 }
 
-// The output of one (token, row) from its 128-bit total.
+// The output of one (token, row) from its rounded value (every epilogue but
+// EPI_PARTIAL, which writes its limbs while the accumulators are read).
 template <int EPI>
-__device__ __forceinline__ void tc_finish(const ProductArgs& a, uint32_t tok, uint32_t row, const Acc128& tot,
+__device__ __forceinline__ void tc_finish(const ProductArgs& a, uint32_t tok, uint32_t row, int32_t v,
                                           uint32_t lane) {
-  int32_t v = acc128_round_q24(tot);
-  if (EPI == EPI_PARTIAL) {
-    if (tok < a.tokens && row < a.rows) limbs_from_acc128(tot.lo, tot.hi, a.partial + ((size_t)tok * a.rows + row) * 4);
-  } else if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+  if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
     const int32_t partner = __shfl_xor_sync(0xffffffffu, v, 1);  // row ^ 1, same token
     if ((lane & 1) == 0 && tok < a.tokens && row + 1 < a.rows) epi_pair<EPI>(a, tok, row, v, partner);
   } else if (EPI == EPI_LOGITS) {
@@ -148,17 +127,23 @@ __device__ __forceinline__ void tc_finish(const ProductArgs& a, uint32_t tok, ui
   }
 }
 
+// Persistent: block b takes tiles b, b + gridDim.x, ... (token tiles vary
+// fastest, so the blocks sharing a weight tile run at the same time). The
+// ring runs on across tiles; the MMA warp starts a tile's accumulation once
+// the epilogue warps have read the previous tile's accumulators out of TMEM
+// (tfree), so that the epilogue arithmetic (RoPE, the gating's sigmoid,
+// residual adds, stores) overlaps the next tile's MMAs.
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q8_gemm_tc_kernel(ProductArgs a, const __grid_constant__ CUtensorMap wmap,
                       const __grid_constant__ CUtensorMap pmap, unsigned int* fault) {
   extern __shared__ uint8_t tc_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done, agroup[kTcAGroups];
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done, tfree;
   __shared__ uint32_t tmem_slot;
   uint8_t* ring = (uint8_t*)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m0 = blockIdx.x * kTcTok, n0 = blockIdx.y * kTcRows;
   const uint32_t nk = (a.cols + kTcKChunk - 1) / kTcKChunk;
+  const uint32_t ntt = (a.tokens + kTcTok - 1) / kTcTok, ntiles = ntt * (a.tc_rows / kTcRows);
 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < kTcStages; ++s) {
@@ -166,7 +151,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(&done, 1);
-    for (uint32_t g = 0; g < kTcAGroups; ++g) mbar_init(&agroup[g], 1);
+    mbar_init(&tfree, kTcEpiWarps);
     mbar_fence_init();
   }
   if (warp == 0) {
@@ -185,17 +170,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     if (lane == 0) {  // producer
       uint32_t issued[kTcStages] = {};
-      for (uint32_t kt = 0; kt < nk; ++kt) {
-        const uint32_t s = kt % kTcStages, use = kt / kTcStages;
-        if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) break;
-        uint8_t* st = ring + s * kTcStage;
-        mbar_arrive_expect_tx(&full[s], kTcStage);
+      uint32_t G = 0;  // stages issued so far (all tiles)
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const uint32_t m0 = (t % ntt) * kTcTok, n0 = (t / ntt) * kTcRows;
+        for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
+          const uint32_t s = G % kTcStages, use = G / kTcStages;
+          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + s * kTcStage;
+          mbar_arrive_expect_tx(&full[s], kTcStage);
 #pragma unroll
-        for (uint32_t j = 0; j < 3; ++j) tma_load_3d(st + j * kTcAPlane, &wmap, kt * kTcKChunk, n0, j, &full[s]);
+          for (uint32_t j = 0; j < 3; ++j) tma_load_3d(st + j * kTcAPlane, &wmap, kt * kTcKChunk, n0, j, &full[s]);
 #pragma unroll
-        for (uint32_t i = 0; i < 4; ++i)
-          tma_load_3d(st + 3 * kTcAPlane + i * kTcBPlane, &pmap, kt * kTcKChunk, i, m0, &full[s]);
-        ++issued[s];
+          for (uint32_t i = 0; i < 4; ++i)
+            tma_load_3d(st + 3 * kTcAPlane + i * kTcBPlane, &pmap, kt * kTcKChunk, i, m0, &full[s]);
+          ++issued[s];
+        }
       }
       // every issued copy has landed before the block may exit
       for (uint32_t s = 0; s < kTcStages; ++s)
@@ -203,57 +196,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer
-      uint32_t touched = 0, g = 0;
+      uint32_t G = 0, it = 0;
       bool ok = true;
-      for (uint32_t kt = 0; kt < nk && ok; ++kt) {
-        const uint32_t s = kt % kTcStages, use = kt / kTcStages;
-        if (!mbar_wait_bounded(&full[s], use & 1, fault)) break;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+        if (it > 0 && !mbar_wait_bounded(&tfree, (it - 1) & 1, fault)) break;
         tc_fence_after();
-        const uint32_t base = smem_addr(ring + s * kTcStage);
-#pragma unroll
-        for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk, ++g) {
-          uint32_t acol = 0;
-          if (kTcATmem) {  // the group's TMEM columns are free once the MMAs that read them completed
-            const uint32_t grp = g % kTcAGroups, round = g / kTcAGroups;
-            if (round > 0 && !mbar_wait_bounded(&agroup[grp], (round - 1) & 1, fault)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            acol = tmem + kTcAccCols + grp * 24;
-#pragma unroll
-            for (uint32_t j = 0; j < 3; ++j) tc_cp(acol + 8 * j, tc_desc(base + j * kTcAPlane + kk * 32));
+        uint32_t touched = 0;
+        for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
+          const uint32_t s = G % kTcStages, use = G / kTcStages;
+          if (!mbar_wait_bounded(&full[s], use & 1, fault)) {
+            ok = false;
+            break;
           }
+          tc_fence_after();
+          const uint32_t base = smem_addr(ring + s * kTcStage);
 #pragma unroll
-          for (uint32_t j = 0; j < 3; ++j) {
-            const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
+          for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk) {
 #pragma unroll
-            for (uint32_t i = 0; i < 4; ++i) {
-              const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
-              const uint32_t d = i + j;
-              if (kTcATmem) tc_mma_ts(tmem + d * kTcTok, acol + 8 * j, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
-              else tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
-              touched |= 1u << d;
+            for (uint32_t j = 0; j < 3; ++j) {
+              const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
+#pragma unroll
+              for (uint32_t i = 0; i < 4; ++i) {
+                const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
+                const uint32_t d = i + j;
+                tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
+                touched |= 1u << d;
+              }
             }
           }
-          if (kTcATmem) tc_commit(&agroup[g % kTcAGroups]);
+          tc_commit(&empty[s]);
         }
-        if (!ok) break;
-        tc_commit(&empty[s]);
+        tc_commit(&done);  // also after a give-up: the epilogue's wait then ends
       }
-      tc_commit(&done);
     }
-  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31
-    const bool ok = mbar_wait_bounded(&done, 0, fault);
-    tc_fence_after();
-    if (ok) {
-      const uint32_t quad = warp & 3, cg = (warp - 2) >> 2;
+  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, 16 of the 64 token columns
+    const uint32_t quad = warp & 3, cg = (warp - 2) >> 2;
+    int64_t lo_bound[kTcDiagonals];
+#pragma unroll
+    for (uint32_t d = 0; d < kTcDiagonals; ++d) lo_bound[d] = tc_diag_min(d) * (int64_t)a.cols;
+    uint32_t it = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      const uint32_t m0 = (t % ntt) * kTcTok, n0 = (t / ntt) * kTcRows;
+      if (!mbar_wait_bounded(&done, it & 1, fault)) break;
+      tc_fence_after();
       const uint32_t row = n0 + 32 * quad + lane;
       const int32_t shift = row < a.tc_rows ? a.tc_shift[row] : 0;
-      int64_t lo_bound[kTcDiagonals];
+      int32_t v[kTcTok / 4];
 #pragma unroll
-      for (uint32_t d = 0; d < kTcDiagonals; ++d) lo_bound[d] = tc_diag_min(d) * (int64_t)a.cols;
-#pragma unroll 1
       for (uint32_t h = 0; h < kTcTok / 4 / 8; ++h) {
         const uint32_t c0 = cg * (kTcTok / 4) + h * 8;
         uint32_t r[kTcDiagonals][8];
@@ -261,11 +250,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (uint32_t d = 0; d < kTcDiagonals; ++d) tmem_ld8(tmem + ((32 * quad) << 16) + d * kTcTok + c0, r[d]);
         tmem_ld_wait();
 #pragma unroll
-        for (uint32_t t = 0; t < 8; ++t) {
+        for (uint32_t c = 0; c < 8; ++c) {
           int64_t T[kTcDiagonals];
 #pragma unroll
           for (uint32_t d = 0; d < kTcDiagonals; ++d)
-            T[d] = lo_bound[d] + (int64_t)(uint32_t)(r[d][t] - (uint32_t)lo_bound[d]);
+            T[d] = lo_bound[d] + (int64_t)(uint32_t)(r[d][c] - (uint32_t)lo_bound[d]);
           // |T| < 2^33: the first four fit one int64 at weights 2^0..2^24,
           // the last two another at 2^32, 2^40
           const int64_t lo = T[0] + T[1] * 256 + T[2] * 65536 + T[3] * 16777216;
@@ -273,8 +262,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           Acc128 tot{0, 0};
           acc128_add_shifted(tot, lo, shift);
           acc128_add_shifted(tot, hi, shift + 32);
-          tc_finish<EPI>(a, m0 + c0 + t, row, tot, lane);
+          if (EPI == EPI_PARTIAL) {
+            const uint32_t tok = m0 + c0 + c;
+            if (tok < a.tokens && row < a.rows)
+              limbs_from_acc128(tot.lo, tot.hi, a.partial + ((size_t)tok * a.rows + row) * 4);
+          } else {
+            v[h * 8 + c] = acc128_round_q24(tot);
+          }
         }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree);  // the accumulators may be overwritten
+      if (EPI != EPI_PARTIAL) {
+#pragma unroll
+        for (uint32_t c = 0; c < kTcTok / 4; ++c) tc_finish<EPI>(a, m0 + cg * (kTcTok / 4) + c, row, v[c], lane);
       }
     }
   }
@@ -379,7 +381,9 @@ cudaError_t launch_tc_one(const ProductArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   unsigned int* fault = device_fault_word();
   if (!fault) return cudaErrorInvalidValue;
-  const dim3 grid((a.tokens + kTcTok - 1) / kTcTok, a.tc_rows / kTcRows);
+  // one block a multiprocessor (the shared memory allows no second), persistent over the tiles
+  const uint32_t tiles = (a.tokens + kTcTok - 1) / kTcTok * (a.tc_rows / kTcRows);
+  const dim3 grid(std::min<uint32_t>(tiles, (uint32_t)device_sms()));
   return launch_k(q8_gemm_tc_kernel<EPI>, grid, dim3(kTcThreads), kTcSmem, stream, a, wmap, pmap, fault);
 }
 

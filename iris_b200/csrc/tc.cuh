@@ -30,5 +30,7 @@ cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream);
 bool tc_usable(const ProductArgs& a);
 cudaError_t launch_gemm_tc(const ProductArgs& a, EpiMode epi, cudaStream_t stream);
 cudaError_t prepare_tc_kernels();
+// Multiprocessors of the current device (q8.cu).
+int device_sms();
 
 }  // namespace iris
