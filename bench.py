@@ -48,10 +48,19 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="N > 1: how decode passes exchange partial sums")
+    p.add_argument("--chain-tokens", type=int, default=4096,
+                   help="tokens of the chain-shaped prefill measured after the decode (0: skip)")
     p.add_argument("--decode-path", choices=["auto", "graph", "step"], default="auto",
                    help="decode passes as the persistent step kernel (auto where the model allows) "
                         "or as a CUDA graph of one kernel per operation")
     return p.parse_args()
+
+
+def bf16_peak():
+    try:
+        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0  # the profiling recipe's fallback burst figure
 
 
 def peaks():
@@ -349,6 +358,49 @@ def main():
     else:
         roofline = gemv_roofline
 
+    # The teacher-forced chain's pass (BASELINE config 5 on one GPU, or one
+    # claim tensor-parallel over N): 4096 seeded tokens through the
+    # device-resident prefill in ranges of 256 rows, every layer's products
+    # on the tcgen05 GEMM. Whole-call time (ids in, first-maximum token out).
+    chain = None
+    if args.chain_tokens > 0:
+        csess = model.session(args.chain_tokens + 8)
+        cprompt = np.random.default_rng(seed + 5).integers(0, cfg.vocab, size=args.chain_tokens).tolist()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        csess.prefill(cprompt)
+        cs = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([cs], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            cs = float(t.item())
+        csess.close()
+        chain = {"tokens": args.chain_tokens, "tok_s": args.chain_tokens / cs, "ms": cs * 1e3,
+                 "range_rows": 256, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
+                 "note": "the chain stages' arithmetic through iris_session_prefill; checkpoint records "
+                         "are not hashed (their Raster encoding is absent)"}
+    # The prefill GEMM on its own (gate|up shape, 256 tokens, the tensor-core
+    # copy of a seeded matrix), timed with events over a captured graph of
+    # launches: algorithmic int8 ops 2*M*N*K against the dense int8 peak,
+    # which is taken as twice the measured bf16 cuBLAS figure (the nominal
+    # int8:bf16 ratio of B200; no int8 GEMM is measured here). The twelve
+    # byte-plane MMAs a product issues are reported beside it.
+    gemm_roofline = None
+    if rank == 0 and world == 1:
+        from iris_b200 import microbench
+        g = microbench.gemm(argparse.Namespace(seed=seed, rows=2 * cfg.ffn, cols=cfg.hidden, tokens=256,
+                                               iters=10, gemm="tc"))
+        bf16 = bf16_peak()
+        if bf16:
+            int8_peak = 2 * bf16
+            gemm_roofline = {"bound": "tensor", "achieved": g["TOPS"], "peak": int8_peak, "unit": "TOPS",
+                             "frac": g["TOPS"] / int8_peak, "plane_mma_frac": 12 * g["TOPS"] / int8_peak,
+                             "us_per_launch": g["us_per_launch"], "shape": [256, 2 * cfg.ffn, cfg.hidden],
+                             "kernel": "q8_gemm_tc_kernel<EPI_STORE> (+ planes_kernel)",
+                             "peak_kind": "2 x measured bf16 (MEASURED_PEAKS.json)",
+                             "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_256tok.md")}
+
     kernels = sess.kernels_per_pass
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -372,6 +424,8 @@ def main():
         "kernels_per_step": kernels,
         "attention": sess.attention_plan,
         "prefill_tok_s": args.prompt / prefill_s,
+        "chain_prefill": chain,
+        "prefill_gemm_roofline": gemm_roofline,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

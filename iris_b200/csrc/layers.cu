@@ -1064,13 +1064,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) 
 // Many queries, one block a (query, head group): the group's HPC query heads
 // share each key and value row of the cache (one read for all of them).
 // attention_softmax (ops.rs:233-261) as in the decode kernels: scores with
-// LPP lanes a key row (the group's query pieces in registers) and each
-// head's first maximum, exp terms and their sums, weights by one exact
-// reciprocal a head, then the weighted value sums: warp w takes rows w,
-// w + 8, ..., lane l dimensions [4 l, 4 l + 4) (DL = D / 32 values), and the
-// eight warps' sums meet in shared memory. The residual 1.0 - sum(weights)
-// times the first maximum's value row is added before the one rounding
-// (the same as adding it to that weight, since no weight saturates).
+// one key row a thread (the group's query heads in shared memory, read as
+// broadcasts) and each head's first maximum, exp terms and their sums,
+// weights by one exact reciprocal a head, then the weighted value sums:
+// warp w takes rows w, w + 8, ..., lane l dimensions [DL l, DL l + DL)
+// (DL = D / 32 values), and the eight warps' sums meet in shared memory. The
+// residual 1.0 - sum(weights) times the first maximum's value row is added
+// before the one rounding (the same as adding it to that weight, since no
+// weight saturates). Exp terms are held in 32 bits: every term is below 2^32
+// but those of the positions whose score is the maximum, which are exactly
+// 2^32 (ops.rs:508-556 at delta 0) and are recognised by their score.
 constexpr uint32_t kPrefillThreads = 256;
 
 template <uint32_t PER, uint32_t HPC>
@@ -1078,81 +1081,61 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
   pdl_wait();
   pdl_trigger();
   constexpr uint32_t D = PER * 8, kWarps = kPrefillThreads / 32, DL = D / 32;
-  constexpr uint32_t LPP = D / 4 < 16 ? D / 4 : 16, NV = D / LPP / 4, PW = 32 / LPP, LPH = LPP / HPC;
-  static_assert(HPC <= LPP && DL >= 1 && HPC * DL <= 16, "shapes");
+  static_assert(DL >= 1 && HPC * DL <= 16, "shapes");
   extern __shared__ __align__(16) unsigned char sm[];
   __shared__ unsigned long long wkey[kWarps][HPC], wsum[kWarps][HPC], gkey[HPC], ginv[HPC], gtot[HPC];
   __shared__ int32_t wws[kWarps][HPC], resid[HPC];
+  __shared__ __align__(16) int32_t qs[HPC * D];
   const uint32_t tok = blockIdx.x, h0 = blockIdx.y * HPC, g = h0 / (a.heads / a.kv_heads);
   const uint32_t p = a.pos0 + tok, ws = window_start(p, a.window), n = p - ws + 1;
-  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, pl = lane % LPP, pslot = lane / LPP;
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t qd = a.heads * D;
-  int32_t* sw = (int32_t*)sm;                                           // [n][HPC] scores, then weights
-  uint64_t* tm = (uint64_t*)(sm + (((size_t)n * HPC * 4 + 15) & ~(size_t)15));  // [n][HPC] exp terms
+  int32_t* sw = (int32_t*)sm;                                            // [n][HPC] scores, then weights
+  uint32_t* tm = (uint32_t*)(sm + (((size_t)n * HPC * 4 + 15) & ~(size_t)15));  // [n][HPC] exp terms
   const int32_t* kbase = a.kcache + (size_t)ws * a.kvd + g * D;
   const int32_t* vbase = a.vcache + (size_t)ws * a.kvd + g * D;
+  for (uint32_t i = tid; i < HPC * D / 4; i += kPrefillThreads)
+    ((int4*)qs)[i] = *(const int4*)(a.q + (size_t)tok * qd + (size_t)h0 * D + 4 * i);
+  __syncthreads();
 
-  int4 q[HPC][NV];
+  // ---- 1. scores: thread tid takes rows tid, tid + 256, ...
+  unsigned long long best[HPC];
 #pragma unroll
-  for (uint32_t h = 0; h < HPC; ++h)
+  for (uint32_t h = 0; h < HPC; ++h) best[h] = 0;
+  for (uint32_t t = tid; t < n; t += kPrefillThreads) {
+    const int4* krow = (const int4*)(kbase + (size_t)t * a.kvd);
+    int64_t c0[HPC], c1[HPC];
 #pragma unroll
-    for (uint32_t i = 0; i < NV; ++i)
-      q[h][i] = *(const int4*)(a.q + (size_t)tok * qd + (size_t)(h0 + h) * D + 4 * (pl + LPP * i));
-
-  // ---- 1. scores (lane pl keeps the key of head pl / LPH)
-  unsigned long long best = 0;
-  for (uint32_t base = 0; base < n; base += 2 * kWarps * PW) {
-    int4 kv[2][NV];
-#pragma unroll
-    for (uint32_t u = 0; u < 2; ++u) {
-      const uint32_t t = base + u * kWarps * PW + warp * PW + pslot;
-      const int32_t* krow = kbase + (size_t)(t < n ? t : n - 1) * a.kvd;
-#pragma unroll
-      for (uint32_t i = 0; i < NV; ++i) kv[u][i] = __ldg((const int4*)(krow + 4 * (pl + LPP * i)));
-    }
-#pragma unroll
-    for (uint32_t u = 0; u < 2; ++u) {
-      const uint32_t t = base + u * kWarps * PW + warp * PW + pslot;
-      uint64_t v[HPC];
+    for (uint32_t h = 0; h < HPC; ++h) c0[h] = c1[h] = 0;
+#pragma unroll 4
+    for (uint32_t i = 0; i < D / 4; ++i) {
+      const int4 k = __ldg(krow + i);
 #pragma unroll
       for (uint32_t h = 0; h < HPC; ++h) {
-        int64_t c0 = 0, c1 = 0;
-#pragma unroll
-        for (uint32_t i = 0; i < NV; ++i) {
-          mac_wide(c0, q[h][i].x, kv[u][i].x);
-          mac_wide(c1, q[h][i].y, kv[u][i].y);
-          mac_wide(c0, q[h][i].z, kv[u][i].z);
-          mac_wide(c1, q[h][i].w, kv[u][i].w);
-        }
-        v[h] = (uint64_t)c0 + (uint64_t)c1;
+        const int4 q = ((const int4*)qs)[h * (D / 4) + i];
+        mac_wide(c0[h], q.x, k.x);
+        mac_wide(c1[h], q.y, k.y);
+        mac_wide(c0[h], q.z, k.z);
+        mac_wide(c1[h], q.w, k.w);
       }
+    }
 #pragma unroll
-      for (uint32_t m = HPC, off = LPP / 2; m > 1; m >>= 1, off >>= 1) {
-        const bool upper = (pl & off) != 0;
-#pragma unroll
-        for (uint32_t i = 0; i < m / 2; ++i) {
-          const uint64_t send = upper ? v[i] : v[i + m / 2];
-          const uint64_t keep = upper ? v[i + m / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-        }
-      }
-      uint64_t sum = v[0];
-#pragma unroll
-      for (uint32_t off = LPH / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-      if (pl % LPH == 0 && t < n) {
-        const int32_t sc = finish_score((int64_t)sum, a.mode, a.scale_q32);
-        sw[t * HPC + pl / LPH] = sc;
-        const unsigned long long key = best_key(sc, t);
-        best = key > best ? key : best;
-      }
+    for (uint32_t h = 0; h < HPC; ++h) {
+      const int32_t sc = finish_score((int64_t)((uint64_t)c0[h] + (uint64_t)c1[h]), a.mode, a.scale_q32);
+      sw[t * HPC + h] = sc;
+      const unsigned long long key = best_key(sc, t);
+      best[h] = key > best[h] ? key : best[h];
     }
   }
 #pragma unroll
-  for (uint32_t off = LPP; off < 32; off <<= 1) {
-    const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
-    best = o > best ? o : best;
+  for (uint32_t h = 0; h < HPC; ++h) {
+#pragma unroll
+    for (uint32_t off = 16; off >= 1; off >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, best[h], off);
+      best[h] = o > best[h] ? o : best[h];
+    }
+    if (lane == 0) wkey[warp][h] = best[h];
   }
-  if (lane < LPP && lane % LPH == 0) wkey[warp][lane / LPH] = best;
   __syncthreads();
   if (tid < HPC) {
     unsigned long long b = 0;
@@ -1164,12 +1147,12 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
   // ---- 2. exp terms against each head's first maximum, their sums.
   // Element e = position * HPC + head: thread tid always meets head tid % HPC.
   const uint32_t my_h = tid % HPC;
+  const int32_t my_max = best_key_value(gkey[my_h]);
   {
-    const int32_t mx = best_key_value(gkey[my_h]);
     uint64_t e = 0;
     for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
-      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
-      tm[el] = term;
+      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], my_max);
+      tm[el] = (uint32_t)term;  // 2^32 (score == maximum) wraps to 0 and is restored below
       e += term;
     }
     e = head_lane_sum<HPC>(e);
@@ -1189,7 +1172,8 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
     const uint64_t tot = gtot[my_h], inv = ginv[my_h];
     int32_t wsl = 0;
     for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
-      const int32_t w = tot ? softmax_weight_inv((int64_t)tm[el], tot, inv) : 0;
+      const int64_t term = sw[el] == my_max ? (int64_t)kOneAcc : (int64_t)tm[el];
+      const int32_t w = tot ? softmax_weight_inv(term, tot, inv) : 0;
       sw[el] = w;
       wsl += w;
     }
@@ -1233,7 +1217,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
     }
   }
   __syncthreads();  // every weight is read: tm's space takes the warps' sums
-  uint64_t* tree = tm;  // [kWarps / 2][HPC DL][32]
+  uint64_t* tree = (uint64_t*)tm;  // [kWarps / 2][HPC DL][32] (tm is 16-byte aligned)
   constexpr uint32_t NA = HPC * DL;
   for (uint32_t half = kWarps / 2; half >= 1; half >>= 1) {
     if (warp >= half && warp < 2 * half) {
@@ -1265,7 +1249,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
 
 size_t prefill_group_smem(uint32_t hpc, uint32_t d, uint32_t max_visible) {
   const size_t tree = (size_t)kPrefillThreads / 64 * hpc * (d / 32) * 32 * 8;  // [warps / 2][HPC DL][32] u64
-  const size_t terms = std::max((size_t)max_visible * hpc * 8, tree);
+  const size_t terms = std::max((size_t)max_visible * hpc * 4, tree);
   return (((size_t)max_visible * hpc * 4 + 15) & ~(size_t)15) + terms;
 }
 

@@ -128,6 +128,30 @@ def attention(args):
             "kv_bytes": nbytes, "GB_s": nbytes / us / 1e3}
 
 
+def prefill(args):
+    """A prefill of --context seeded tokens through an --layers-layer model of
+    the Mistral-7B layer shapes (vocabulary 512): whole-call time, and the
+    kernels of its ranges for ncu (attention and tensor-core GEMMs)."""
+    import time
+    from iris_b200.model import DeviceModel
+    from iris_b200.shapes import mistral_7b
+    cfg = mistral_7b()
+    cfg = type(cfg)(**{**cfg.__dict__, "layers": args.layers, "vocab": 512})
+    model = DeviceModel(cfg, seed=args.seed)
+    model.prepare_gemm()
+    prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab, size=args.context).tolist()
+    times = []
+    for _ in range(max(1, args.iters)):
+        sess = model.session(args.context + 8)
+        t0 = time.perf_counter()
+        sess.prefill(prompt)
+        times.append(time.perf_counter() - t0)
+        sess.close()
+    model.close()
+    best = min(times)
+    return {"layers": args.layers, "context": args.context, "ms": best * 1e3, "tok_s": args.context / best}
+
+
 def gemm(args):
     import torch
     from iris_b200 import _lib
@@ -318,7 +342,7 @@ def step(args):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep", "step"])
+    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep", "step", "prefill"])
     p.add_argument("--product", type=int, default=2, dest="product_which")
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
@@ -335,7 +359,7 @@ def main():
     args = p.parse_args()
     from iris_b200 import build
     build.build()
-    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep, "step": step}[args.which](args)), flush=True)
+    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep, "step": step, "prefill": prefill}[args.which](args)), flush=True)
 
 
 if __name__ == "__main__":
