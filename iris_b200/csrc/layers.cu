@@ -1071,13 +1071,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(AttnArgs a) 
 // (DL = D / 32 values), and the eight warps' sums meet in shared memory. The
 // residual 1.0 - sum(weights) times the first maximum's value row is added
 // before the one rounding (the same as adding it to that weight, since no
-// weight saturates). Exp terms are held in 32 bits: every term is below 2^32
-// but those of the positions whose score is the maximum, which are exactly
-// 2^32 (ops.rs:508-556 at delta 0) and are recognised by their score.
+// weight saturates). Shared memory holds only the scores (then the weights):
+// the exp terms are computed twice, for their sums and for the weights, so
+// that the footprint (16 B a position) leaves room for four blocks a
+// multiprocessor up to 3,000-odd positions.
 constexpr uint32_t kPrefillThreads = 256;
 
 template <uint32_t PER, uint32_t HPC>
-__global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kPrefillThreads, 4) attn_prefill_group_kernel(AttnArgs a) {
   pdl_wait();
   pdl_trigger();
   constexpr uint32_t D = PER * 8, kWarps = kPrefillThreads / 32, DL = D / 32;
@@ -1090,8 +1091,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
   const uint32_t p = a.pos0 + tok, ws = window_start(p, a.window), n = p - ws + 1;
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t qd = a.heads * D;
-  int32_t* sw = (int32_t*)sm;                                            // [n][HPC] scores, then weights
-  uint32_t* tm = (uint32_t*)(sm + (((size_t)n * HPC * 4 + 15) & ~(size_t)15));  // [n][HPC] exp terms
+  int32_t* sw = (int32_t*)sm;  // [n][HPC] scores, then weights; then the warps' value sums
   const int32_t* kbase = a.kcache + (size_t)ws * a.kvd + g * D;
   const int32_t* vbase = a.vcache + (size_t)ws * a.kvd + g * D;
   for (uint32_t i = tid; i < HPC * D / 4; i += kPrefillThreads)
@@ -1150,11 +1150,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
   const int32_t my_max = best_key_value(gkey[my_h]);
   {
     uint64_t e = 0;
-    for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
-      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], my_max);
-      tm[el] = (uint32_t)term;  // 2^32 (score == maximum) wraps to 0 and is restored below
-      e += term;
-    }
+    for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) e += (uint64_t)softmax_exp_term_act(sw[el], my_max);
     e = head_lane_sum<HPC>(e);
     if (lane < HPC) wsum[warp][lane] = e;
   }
@@ -1172,8 +1168,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
     const uint64_t tot = gtot[my_h], inv = ginv[my_h];
     int32_t wsl = 0;
     for (uint32_t el = tid; el < n * HPC; el += kPrefillThreads) {
-      const int64_t term = sw[el] == my_max ? (int64_t)kOneAcc : (int64_t)tm[el];
-      const int32_t w = tot ? softmax_weight_inv(term, tot, inv) : 0;
+      const int32_t w = tot ? softmax_weight_inv(softmax_exp_term_act(sw[el], my_max), tot, inv) : 0;
       sw[el] = w;
       wsl += w;
     }
@@ -1216,8 +1211,8 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
       for (uint32_t i = 0; i < DL; ++i) acc[h][i] += (uint64_t)((int64_t)w * (int64_t)v[i]);
     }
   }
-  __syncthreads();  // every weight is read: tm's space takes the warps' sums
-  uint64_t* tree = (uint64_t*)tm;  // [kWarps / 2][HPC DL][32] (tm is 16-byte aligned)
+  __syncthreads();  // every weight is read: their space takes the warps' sums
+  uint64_t* tree = (uint64_t*)sm;  // [kWarps / 2][HPC DL][32], over the weights (all read)
   constexpr uint32_t NA = HPC * DL;
   for (uint32_t half = kWarps / 2; half >= 1; half >>= 1) {
     if (warp >= half && warp < 2 * half) {
@@ -1249,8 +1244,7 @@ __global__ void __launch_bounds__(kPrefillThreads) attn_prefill_group_kernel(Att
 
 size_t prefill_group_smem(uint32_t hpc, uint32_t d, uint32_t max_visible) {
   const size_t tree = (size_t)kPrefillThreads / 64 * hpc * (d / 32) * 32 * 8;  // [warps / 2][HPC DL][32] u64
-  const size_t terms = std::max((size_t)max_visible * hpc * 4, tree);
-  return (((size_t)max_visible * hpc * 4 + 15) & ~(size_t)15) + terms;
+  return std::max((size_t)max_visible * hpc * 4, tree);
 }
 
 #define IRIS_PREFILL_SHAPES(X) X(4, 1) X(4, 2) X(4, 4) X(8, 1) X(8, 2) X(8, 4) X(16, 1) X(16, 2) X(16, 4) X(32, 1) X(32, 2)
