@@ -319,6 +319,18 @@ void iris_graph_free(void* graph_exec);
  *    (mistral/layer.rs:107-270 via stage.rs:172-226; gemma
  *    prefill_range.rs:307-333). Host buffers in and out.
  * ------------------------------------------------------------------------- */
+/* The chain's head check (kernels/src/kernels/sequence_check.rs:232-300,
+ * run_sequence_check_direct): for each of the n predicting rows (H values
+ * each; check_positions at sequence_check.rs:89-125 lists them: the
+ * previous range's last row, then this range's rows), rms_norm with the
+ * model's final norm, the exact dot_row against every vocabulary row of the
+ * head, softcap, and the first maximum (Argmax, sequence_check.rs:55-70):
+ * token_ids[i] and (if values is not NULL) values[i] = its score. Ranges of
+ * 32 or more rows run on the tensor-core GEMM (logits epilogue). The
+ * selection bookkeeping around it (decode_edge, faults, the transcript) is
+ * the caller's. Tensor-parallel models: every rank calls it. */
+int iris_sequence_check_select(IrisModel* model, const int32_t* rows, uint32_t n, uint32_t* token_ids,
+                               int32_t* values);
 /* mistral-dense: prior_k/prior_v hold the layer's keys for positions
  * 0..start (start rows). Writes m output rows and the range's own K/V. */
 int iris_mistral_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows_in, uint32_t m,

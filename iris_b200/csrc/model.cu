@@ -1489,6 +1489,48 @@ void iris_graph_free(void* graph_exec) {
   if (graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
 }
 
+int iris_sequence_check_select(IrisModel* m, const int32_t* rows, uint32_t n, uint32_t* token_ids,
+                               int32_t* values) {
+  if (!m || !rows || !token_ids) return IRIS_EINVAL;
+  if (n == 0) return 0;
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  if (!m->scratch) {
+    rc = create_session(m, 512, &m->scratch);
+    if (rc) return rc;
+  }
+  IrisSession* s = m->scratch;
+  cudaStream_t st = s->stream;
+  std::vector<unsigned long long> keys(kMaxRows);
+  cudaError_t e = cudaSuccess;
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    const uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->x, rows + (size_t)r0 * m->H, (size_t)cnt * m->H * 4, cudaMemcpyHostToDevice, st);
+    // rms_norm with the final norm (sequence_check.rs:118-125), as byte planes
+    if (e == cudaSuccess) e = launch_planes(s->x, m->final_norm, m->eps, cnt, m->H, s->planes, st);
+    if (e == cudaSuccess) e = launch_fill_u64(s->best, cnt, st);
+    if (e == cudaSuccess) {
+      // every vocabulary row's dot_row, softcap, first maximum (sequence_check.rs:274-288)
+      ProductArgs h = session_product_args(s, m->head, cnt);
+      h.planes = s->planes;
+      h.out = nullptr;
+      h.best = s->best;
+      h.softcap = m->softcap;
+      h.row_base = m->tp_rank * m->V;  // vocabulary shard
+      e = launch_product(h, IN_PLANES, EPI_LOGITS, st);
+    }
+    if (e == cudaSuccess && m->tp_world > 1) e = tp_max_keys(m->comm, s->best, cnt, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(keys.data(), s->best, (size_t)cnt * 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    for (uint32_t i = 0; i < cnt && e == cudaSuccess; ++i) {
+      token_ids[r0 + i] = best_key_token(keys[i]);
+      if (values) values[r0 + i] = best_key_value(keys[i]);
+    }
+  }
+  if (e != cudaSuccess) return (int)e;
+  return check_fault();
+}
+
 int iris_mistral_layer_range(IrisModel* m, uint32_t layer, const int32_t* rows_in, uint32_t n, uint32_t start,
                              const int32_t* prior_k, const int32_t* prior_v, int32_t* rows_out, int32_t* own_k,
                              int32_t* own_v) {

@@ -167,6 +167,17 @@ class DeviceModel:
         """Builds the tensor-core copies of the layer matrices now (not on first use)."""
         check(lib().iris_model_prepare_gemm(self._h), "iris_model_prepare_gemm")
 
+    def sequence_check_select(self, rows: np.ndarray):
+        """The chain's head check over predicting rows [n][hidden]: the
+        first-maximum token id and its score for each row."""
+        r = np.ascontiguousarray(rows, np.int32)
+        n = r.shape[0]
+        tok = np.empty(n, np.uint32)
+        val = np.empty(n, np.int32)
+        check(lib().iris_sequence_check_select(self._h, ptr(r, C.c_int32), n, ptr(tok, C.c_uint32),
+                                               ptr(val, C.c_int32)), "iris_sequence_check_select")
+        return tok, val
+
     def tc_matrices(self):
         """(number of matrices with a tensor-core copy, device bytes of those copies)."""
         b = C.c_uint64(0)

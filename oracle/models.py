@@ -90,6 +90,22 @@ class OracleModel:
         n = count.value
         return out[:n].tolist(), (logits[:n] if logits is not None else None)
 
+    def head_select(self, rows, threads=None):
+        """sequence_check.rs:274-288 per row: rms_norm(final), dot_row over the
+        head, softcap, first maximum -> (token ids, scores)."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        tok = np.empty(rows.shape[0], np.uint32)
+        val = np.empty(rows.shape[0], np.int32)
+        logits = np.empty(self.cfg.vocab, np.int32)
+        for i in range(rows.shape[0]):
+            rc = O.lib().oracle_head_logits(C.byref(self.model.head), O.ptr(rows[i], C.c_int32),
+                                            O.ptr(logits, C.c_int32), threads or O.threads_default())
+            if rc:
+                raise RuntimeError(f"oracle_head_logits failed: {rc}")
+            tok[i] = int(np.argmax(logits))  # the first maximum
+            val[i] = logits[tok[i]]
+        return tok, val
+
     def mistral_layer_range(self, l, rows, start, prior_k, prior_v, threads=None):
         c = self.cfg
         kvd = c.kv_heads * c.head_dim

@@ -300,3 +300,28 @@ def test_refusals():
     with pytest.raises(_lib.IrisError) as e:
         sess.prefill([cfg.vocab])
     assert e.value.code == _lib.IRIS_EINVAL
+
+
+@pytest.mark.parametrize("family", ["mistral", "gemma"])
+def test_sequence_check_select_matches_oracle(family):
+    """The chain's head check (sequence_check.rs:232-300): rms_norm(final),
+    dot_row over the head, softcap (the gemma model's is on), first maximum,
+    for every predicting row; 300 rows cross the device's 256-row ranges (both
+    on the tensor-core GEMM) and 5 rows take the mma.sync GEMM. A zero row
+    ties every score and selects token 0."""
+    from iris_b200.model import DeviceModel, synth_host_weights
+    from iris_b200.shapes import parity_gemma, parity_mistral
+    from oracle.models import OracleModel
+    cfg = parity_mistral() if family == "mistral" else parity_gemma()
+    w = synth_host_weights(cfg, 51)
+    dm = DeviceModel(cfg, weights=w)
+    om = OracleModel(cfg, w)
+    rng = np.random.default_rng(51)
+    rows = rng.integers(-(1 << 21), 1 << 21, size=(300, cfg.hidden)).astype(np.int32)
+    rows[7] = 0
+    rows[8, :3] = [2**31 - 1, -(2**31), 2**31 - 1]
+    for sel in (rows, rows[:5]):
+        tok, val = dm.sequence_check_select(sel)
+        want_tok, want_val = om.head_select(sel)
+        assert np.array_equal(tok, want_tok) and np.array_equal(val, want_val)
+    assert dm.sequence_check_select(rows[7:8])[0][0] == 0
