@@ -1,0 +1,490 @@
+// Prefill attention on the tcgen05 tensor cores (kind::i8), exact.
+//
+// attention_softmax (ops.rs:233-276) over a range of queries with the
+// scores (mistral.rs:130-145) and the weighted value sums
+// (tensor.rs:530-536) as byte-plane contractions:
+//   1. scores: S[h][q][t] = finish_score(sum_d q[d] k[t][d]). q and k are
+//      Q16.16 (four byte planes each, planes 0-2 unsigned, 3 signed), so the
+//      dot product is sum_{i,j} 2^(8 (i + j)) sum_d k_i[d] q_j[d]: sixteen
+//      int8 MMAs (M = 128 keys, N = 64 queries, K = 32 of the 128 dims) into
+//      seven int32 diagonals, each exact (|sum| < 2^26 over 128 dims); the
+//      epilogue adds them modulo 2^64, as the reference's wrapping sum.
+//   2. softmax on CUDA cores, one block a (query, head): first maximum, exp
+//      terms and their sum, weights by one exact reciprocal, the residual
+//      1.0 - sum(weights) on the first maximum's weight; the weights
+//      (0..65536) are written as three byte planes, zero past the query's
+//      position (the causal mask).
+//   3. values: ctx[q][h][d] = requantize(sum_t w[q][t] v[t][d]): twelve MMAs
+//      (M = 128 dims from the transposed value planes, N = 64 queries, K = the
+//      positions) into six diagonals; a diagonal's true sum lies in
+//      [L_s, L_s + 2^32) (L_s from the positions and the operand signs), so
+//      its wrapped int32 value gives it back exactly up to 22,016 positions.
+// The two contractions run the same persistent pipeline as q8_gemm_tc_kernel
+// (TMA producer lane, MMA lane, 16 epilogue warps that release the
+// accumulators before their arithmetic). Operands are packed per layer range
+// into K-major byte planes: queries [h][plane][q][d], keys [g][plane][t][d],
+// values transposed [g][plane][d][t], weights [h][plane][q][t].
+#include <algorithm>
+
+#include "common.cuh"
+#include "detnum.cuh"
+#include "layers.cuh"
+#include "q8.cuh"
+#include "tc.cuh"
+#include "tcgen05.cuh"
+
+namespace iris {
+
+namespace {
+
+constexpr uint32_t kAtD = 128;  // head dim these kernels take
+constexpr uint32_t kAtEpiWarps = 16;
+constexpr uint32_t kAtThreads = 32 * (2 + kAtEpiWarps);
+constexpr uint32_t kAtAPlane = kTcTileM * kTcTileK, kAtBPlane = kTcTileN * kTcTileK;
+constexpr uint32_t kAtStages = 2;
+constexpr uint32_t kAtMaxPositions = 22016;
+
+// Lower bound of one position's contribution to a value-sum diagonal s
+// (value planes i: 0-2 unsigned, 3 signed; weight planes j: 0-1 unsigned,
+// 2 holds 0 or 1).
+__host__ __device__ constexpr int64_t pv_diag_min(uint32_t s) { return s == 3 || s == 4 ? -32640 : s == 5 ? -128 : 0; }
+
+struct ScoreTiles {  // tile = (head, query tile, key tile); one K stage (the 128 dims)
+  uint32_t heads, group, qtiles, ktiles;
+  __device__ uint32_t count() const { return heads * qtiles * ktiles; }
+  __device__ uint32_t nk(uint32_t) const { return 1; }
+  __device__ void a_coord(uint32_t t, uint32_t, uint32_t i, int32_t* c) const {  // keys [g][plane][t][d]
+    const uint32_t h = t / (qtiles * ktiles), kt = t % ktiles;
+    c[0] = 0, c[1] = (int32_t)(kt * kTcTileM), c[2] = (int32_t)((h / group) * 4 + i);
+  }
+  __device__ void b_coord(uint32_t t, uint32_t, uint32_t j, int32_t* c) const {  // queries [h][plane][q][d]
+    const uint32_t h = t / (qtiles * ktiles), qt = (t / ktiles) % qtiles;
+    c[0] = 0, c[1] = (int32_t)(qt * kTcTileN), c[2] = (int32_t)(h * 4 + j);
+  }
+};
+
+struct ValueTiles {  // tile = (head, query tile); K stages over the positions
+  uint32_t heads, group, qtiles, kstages;
+  __device__ uint32_t count() const { return heads * qtiles; }
+  __device__ uint32_t nk(uint32_t) const { return kstages; }
+  __device__ void a_coord(uint32_t t, uint32_t kt, uint32_t i, int32_t* c) const {  // values [g][plane][d][t]
+    const uint32_t h = t / qtiles;
+    c[0] = (int32_t)(kt * kTcTileK), c[1] = 0, c[2] = (int32_t)((h / group) * 4 + i);
+  }
+  __device__ void b_coord(uint32_t t, uint32_t kt, uint32_t j, int32_t* c) const {  // weights [h][plane][q][t]
+    const uint32_t h = t / qtiles, qt = t % qtiles;
+    c[0] = (int32_t)(kt * kTcTileK), c[1] = (int32_t)(qt * kTcTileN), c[2] = (int32_t)(h * 3 + j);
+  }
+};
+
+// The persistent tensor-core pipeline over a problem's tiles: NA planes of A
+// (M = 128 rows) against NB planes of B (N = 64 columns), pair (i, j) into
+// diagonal i + j. Epi::value turns the diagonals' raw int32 values of one
+// (TMEM lane row, column) into the output, Epi::store writes it (after the
+// accumulators are released).
+template <uint32_t NA, uint32_t NB, class Tiles, class Epi>
+__device__ __forceinline__ void at_pipeline(const Tiles& tiles, const Epi& epi, const CUtensorMap* amap,
+                                            const CUtensorMap* bmap, unsigned int* fault, uint8_t* ring) {
+  constexpr uint32_t ND = NA + NB - 1, kStage = NA * kAtAPlane + NB * kAtBPlane;
+  static_assert(ND * kTcTileN <= 512, "TMEM columns");
+  __shared__ __align__(8) uint64_t full[kAtStages], empty[kAtStages], done, tfree;
+  __shared__ uint32_t tmem_slot;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t ntiles = tiles.count();
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < kAtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done, 1);
+    mbar_init(&tfree, kAtEpiWarps);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_slot)),
+                 "r"(512u)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {  // producer
+      uint32_t issued[kAtStages] = {};
+      uint32_t G = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const uint32_t nk = tiles.nk(t);
+        for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
+          const uint32_t s = G % kAtStages, use = G / kAtStages;
+          if (use > 0 && !mbar_wait_bounded(&empty[s], (use - 1) & 1, fault)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = ring + s * kStage;
+          mbar_arrive_expect_tx(&full[s], kStage);
+          int32_t c[3];
+#pragma unroll
+          for (uint32_t i = 0; i < NA; ++i) {
+            tiles.a_coord(t, kt, i, c);
+            tma_load_3d(st + i * kAtAPlane, amap, c[0], c[1], c[2], &full[s]);
+          }
+#pragma unroll
+          for (uint32_t j = 0; j < NB; ++j) {
+            tiles.b_coord(t, kt, j, c);
+            tma_load_3d(st + NA * kAtAPlane + j * kAtBPlane, bmap, c[0], c[1], c[2], &full[s]);
+          }
+          ++issued[s];
+        }
+      }
+      for (uint32_t s = 0; s < kAtStages; ++s)
+        if (issued[s]) mbar_wait_bounded(&full[s], (issued[s] - 1) & 1, fault);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      uint32_t G = 0, it = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++it) {
+        if (it > 0 && !mbar_wait_bounded(&tfree, (it - 1) & 1, fault)) break;
+        tc_fence_after();
+        uint32_t touched = 0;
+        const uint32_t nk = tiles.nk(t);
+        for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
+          const uint32_t s = G % kAtStages, use = G / kAtStages;
+          if (!mbar_wait_bounded(&full[s], use & 1, fault)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_addr(ring + s * kStage);
+#pragma unroll
+          for (uint32_t kk = 0; kk < kTcTileK / 32; ++kk) {
+#pragma unroll
+            for (uint32_t i = 0; i < NA; ++i) {
+              const uint64_t ad = tc_desc(base + i * kAtAPlane + kk * 32);
+#pragma unroll
+              for (uint32_t j = 0; j < NB; ++j) {
+                const uint64_t bd = tc_desc(base + NA * kAtAPlane + j * kAtBPlane + kk * 32);
+                const uint32_t d = i + j;
+                tc_mma(tmem + d * kTcTileN, ad, bd, tc_idesc(i == 3, Tiles::kBSigned && j == 3), (touched >> d) & 1u);
+                touched |= 1u << d;
+              }
+            }
+          }
+          tc_commit(&empty[s]);
+        }
+        tc_commit(&done);
+      }
+    }
+  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, 16 of the 64 columns
+    const uint32_t quad = warp & 3, cg = (warp - 2) >> 2;
+    uint32_t it = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, ++it) {
+      if (!mbar_wait_bounded(&done, it & 1, fault)) break;
+      tc_fence_after();
+      const uint32_t row = 32 * quad + lane;
+      int32_t y[16];
+#pragma unroll
+      for (uint32_t h = 0; h < 2; ++h) {
+        uint32_t r[ND][8];
+#pragma unroll
+        for (uint32_t d = 0; d < ND; ++d) tmem_ld8(tmem + ((32 * quad) << 16) + d * kTcTileN + cg * 16 + h * 8, r[d]);
+        tmem_ld_wait();
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) {
+          uint32_t v[ND];
+#pragma unroll
+          for (uint32_t d = 0; d < ND; ++d) v[d] = r[d][c];
+          y[h * 8 + c] = epi.value(v);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree);  // the accumulators may be overwritten
+#pragma unroll
+      for (uint32_t c = 0; c < 16; ++c) epi.store(t, row, cg * 16 + c, y[c]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u) : "memory");
+  }
+}
+
+struct ScoreEpi {
+  int32_t* s;  // [heads][qcap][pcap]
+  uint32_t qtiles, ktiles, qcap, pcap, tokens;
+  int mode;
+  uint32_t scale;
+  __device__ int32_t value(const uint32_t* v) const {  // each diagonal exact in int32; the sum wraps as the reference's
+    uint64_t sum = 0;
+#pragma unroll
+    for (uint32_t d = 0; d < 7; ++d) sum += (uint64_t)(int64_t)(int32_t)v[d] << (8 * d);
+    return finish_score((int64_t)sum, mode, scale);
+  }
+  __device__ void store(uint32_t t, uint32_t row, uint32_t col, int32_t y) const {
+    const uint32_t h = t / (qtiles * ktiles), qt = (t / ktiles) % qtiles, kt = t % ktiles;
+    const uint32_t q = qt * kTcTileN + col, key = kt * kTcTileM + row;
+    if (q < tokens) s[((size_t)h * qcap + q) * pcap + key] = y;
+  }
+};
+
+struct ValueEpi {
+  uint8_t* ctx_planes;  // [tokens][4][heads*d]
+  int32_t* ctx;
+  uint32_t qtiles, tokens, qd, pcap;
+  __device__ int32_t value(const uint32_t* v) const {
+    uint64_t acc = 0;
+#pragma unroll
+    for (uint32_t d = 0; d < 6; ++d) {
+      const int64_t lb = pv_diag_min(d) * (int64_t)pcap;
+      const int64_t T = lb + (int64_t)(uint32_t)(v[d] - (uint32_t)lb);
+      acc += (uint64_t)T << (8 * d);
+    }
+    return requantize((int64_t)acc);
+  }
+  __device__ void store(uint32_t t, uint32_t row, uint32_t col, int32_t y) const {
+    const uint32_t h = t / qtiles, qt = t % qtiles, q = qt * kTcTileN + col;
+    if (q < tokens) {
+      put_planes(ctx_planes + (size_t)q * 4 * qd, qd, h * kAtD + row, y);
+      if (ctx) ctx[(size_t)q * qd + h * kAtD + row] = y;
+    }
+  }
+};
+
+struct ScoreTilesS : ScoreTiles {
+  static constexpr bool kBSigned = true;
+};
+struct ValueTilesS : ValueTiles {
+  static constexpr bool kBSigned = false;  // weight planes are unsigned
+};
+
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc_scores_kernel(ScoreTilesS tiles, ScoreEpi epi, const __grid_constant__ CUtensorMap kmap,
+                          const __grid_constant__ CUtensorMap qmap, unsigned int* fault) {
+  extern __shared__ uint8_t at_raw[];
+  uint8_t* ring = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
+  at_pipeline<4, 4>(tiles, epi, &kmap, &qmap, fault, ring);
+}
+
+__global__ void __launch_bounds__(kAtThreads, 1)
+    attn_tc_values_kernel(ValueTilesS tiles, ValueEpi epi, const __grid_constant__ CUtensorMap vmap,
+                          const __grid_constant__ CUtensorMap wmap, unsigned int* fault) {
+  extern __shared__ uint8_t at_raw[];
+  uint8_t* ring = (uint8_t*)(((uintptr_t)at_raw + 1023) & ~(uintptr_t)1023);
+  at_pipeline<4, 3>(tiles, epi, &vmap, &wmap, fault, ring);
+}
+
+// Byte planes of int32 rows: src row r, group g's 128 values at
+// src + r * stride + g * 128 -> dst[g][plane][r][d] (rows_cap rows a plane).
+__global__ void at_pack_rows_kernel(const int32_t* __restrict__ src, uint32_t rows, uint32_t stride, uint32_t groups,
+                                    uint32_t rows_cap, uint8_t* __restrict__ dst) {
+  const uint32_t idx = blockIdx.x * blockDim.x + threadIdx.x;  // (row, group, 4-dim chunk)
+  const uint32_t chunk = idx % (kAtD / 4), g = (idx / (kAtD / 4)) % groups, r = idx / (kAtD / 4) / groups;
+  if (r >= rows) return;
+  const int4 x = *(const int4*)(src + (size_t)r * stride + g * kAtD + 4 * chunk);
+  const uint32_t u[4] = {(uint32_t)x.x, (uint32_t)x.y, (uint32_t)x.z, (uint32_t)x.w};
+#pragma unroll
+  for (uint32_t p = 0; p < 4; ++p) {
+    const uint32_t b = ((u[0] >> (8 * p)) & 0xFF) | (((u[1] >> (8 * p)) & 0xFF) << 8) |
+                       (((u[2] >> (8 * p)) & 0xFF) << 16) | (((u[3] >> (8 * p)) & 0xFF) << 24);
+    *(uint32_t*)(dst + (((size_t)g * 4 + p) * rows_cap + r) * kAtD + 4 * chunk) = b;
+  }
+}
+
+// Transposed value planes: dst[g][plane][d][t] for t < rows (a 32 x 32 tile a
+// block through shared memory).
+__global__ void at_pack_values_t_kernel(const int32_t* __restrict__ src, uint32_t rows, uint32_t stride,
+                                        uint32_t pcap, uint8_t* __restrict__ dst) {
+  __shared__ int32_t tile[32][33];
+  const uint32_t t0 = blockIdx.x * 32, d0 = blockIdx.y * 32, g = blockIdx.z;
+  const uint32_t tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 256 threads: 8 rows a pass
+  for (uint32_t r = ty; r < 32; r += 8) {
+    const uint32_t t = t0 + r;
+    tile[r][tx] = t < rows ? src[(size_t)t * stride + g * kAtD + d0 + tx] : 0;
+  }
+  __syncthreads();
+  for (uint32_t r = ty; r < 32; r += 8) {  // r: dimension, tx: position
+    const uint32_t u = (uint32_t)tile[tx][r], t = t0 + tx;
+    if (t < pcap) {
+#pragma unroll
+      for (uint32_t p = 0; p < 4; ++p) dst[(((size_t)g * 4 + p) * kAtD + d0 + r) * pcap + t] = (uint8_t)(u >> (8 * p));
+    }
+  }
+}
+
+// One block a (query, head): the integer softmax of the query's scores
+// (positions 0..p) into three weight planes over the pcap positions.
+constexpr uint32_t kSoftThreads = 256;
+__global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t* __restrict__ s, uint8_t* wp,
+                                                                  uint32_t qcap, uint32_t pcap, uint32_t pos0,
+                                                                  uint32_t heads) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ unsigned long long red_key[kSoftThreads / 32], red_sum[kSoftThreads / 32];
+  __shared__ int32_t red_w[kSoftThreads / 32];
+  __shared__ unsigned long long g_key, g_tot;
+  const uint32_t q = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t n = pos0 + q + 1;
+  const int32_t* row = s + ((size_t)h * qcap + q) * pcap;
+  unsigned long long best = 0;
+  for (uint32_t t = tid; t < n; t += kSoftThreads) {
+    const unsigned long long k = best_key(row[t], t);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (uint32_t off = 16; off >= 1; off >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+    best = o > best ? o : best;
+  }
+  if (lane == 0) red_key[warp] = best;
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long b = 0;
+    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) b = red_key[w] > b ? red_key[w] : b;
+    g_key = b;
+  }
+  __syncthreads();
+  const int32_t mx = best_key_value(g_key);
+  const uint32_t tmax = best_key_token(g_key);
+  uint64_t e = 0;
+  for (uint32_t t = tid; t < n; t += kSoftThreads) e += (uint64_t)softmax_exp_term_act(row[t], mx);
+#pragma unroll
+  for (uint32_t off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
+  if (lane == 0) red_sum[warp] = e;
+  __syncthreads();
+  if (tid == 0) {
+    unsigned long long tsum = 0;
+    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) tsum += red_sum[w];
+    g_tot = tsum;
+  }
+  __syncthreads();
+  const uint64_t tot = g_tot, inv = tot ? UINT64_MAX / tot : 0;
+  uint8_t* w0 = wp + ((size_t)h * 3 * qcap + q) * pcap;
+  uint8_t* w1 = w0 + (size_t)qcap * pcap;
+  uint8_t* w2 = w1 + (size_t)qcap * pcap;
+  int32_t wsl = 0;
+  for (uint32_t t = tid; t < pcap; t += kSoftThreads) {
+    int32_t w = 0;
+    if (t < n) {
+      w = tot ? softmax_weight_inv(softmax_exp_term_act(row[t], mx), tot, inv) : 0;
+      wsl += w;
+    }
+    w0[t] = (uint8_t)w;
+    w1[t] = (uint8_t)(w >> 8);
+    w2[t] = (uint8_t)(w >> 16);
+  }
+#pragma unroll
+  for (uint32_t off = 16; off >= 1; off >>= 1) wsl += __shfl_xor_sync(0xffffffffu, wsl, off);
+  if (lane == 0) red_w[warp] = wsl;
+  __syncthreads();
+  if (tid == 0) {
+    int32_t ws = 0;
+    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) ws += red_w[w];
+    // the residual on the first maximum's weight (ops.rs:274-276); no weight saturates
+    const int32_t wm = tot ? softmax_weight_inv(softmax_exp_term_act(row[tmax], mx), tot, inv) : 0;
+    const int32_t w = wm + sub_sat(kOneAct, ws);
+    w0[tmax] = (uint8_t)w;
+    w1[tmax] = (uint8_t)(w >> 8);
+    w2[tmax] = (uint8_t)(w >> 16);
+  }
+  (void)heads;
+}
+
+constexpr uint32_t score_smem() { return kAtStages * (4 * kAtAPlane + 4 * kAtBPlane) + 1024; }
+constexpr uint32_t value_smem() { return kAtStages * (4 * kAtAPlane + 3 * kAtBPlane) + 1024; }
+
+}  // namespace
+
+size_t attn_tc_scratch_bytes(uint32_t heads, uint32_t kv_heads, uint32_t pcap, uint32_t qcap) {
+  return (size_t)heads * qcap * pcap * 4           // scores
+         + (size_t)heads * 3 * qcap * pcap          // weight planes
+         + 2 * (size_t)kv_heads * 4 * pcap * kAtD   // key planes, transposed value planes
+         + (size_t)heads * 4 * qcap * kAtD;         // query planes
+}
+
+void attn_tc_scratch_carve(uint8_t* base, uint32_t heads, uint32_t kv_heads, uint32_t pcap, uint32_t qcap,
+                           AttnTcScratch* sc) {
+  sc->pcap = pcap;
+  sc->qcap = qcap;
+  sc->s = (int32_t*)base;
+  base += (size_t)heads * qcap * pcap * 4;
+  sc->wp = base;
+  base += (size_t)heads * 3 * qcap * pcap;
+  sc->kp = base;
+  base += (size_t)kv_heads * 4 * pcap * kAtD;
+  sc->vt = base;
+  base += (size_t)kv_heads * 4 * pcap * kAtD;
+  sc->qp = base;
+}
+
+bool attn_tc_usable(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc) {
+  if (!sc.s || a.d != kAtD || tokens == 0 || tokens > sc.qcap || a.heads % a.kv_heads) return false;
+  const uint32_t last = a.pos0 + tokens;  // positions 0..last-1 are seen
+  if (a.window != 0 && last > a.window) return false;  // a sliding window cuts the prefix
+  const uint32_t pcap = (last + kTcTileM - 1) / kTcTileM * kTcTileM;
+  return pcap <= sc.pcap && pcap <= kAtMaxPositions && tensor_map_encoder() != nullptr;
+}
+
+cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc,
+                                        cudaStream_t stream) {
+  if (!attn_tc_usable(a, tokens, sc)) return cudaErrorInvalidValue;
+  unsigned int* fault = device_fault_word();
+  if (!fault) return cudaErrorInvalidValue;
+  const uint32_t last = a.pos0 + tokens;
+  const uint32_t pcap = (last + kTcTileM - 1) / kTcTileM * kTcTileM;  // positions in this launch's planes
+  const uint32_t qcap = (tokens + kTcTileN - 1) / kTcTileN * kTcTileN;
+  const uint32_t group = a.heads / a.kv_heads, qd = a.heads * kAtD;
+  // operand planes (the scratch is laid out for sc.pcap / sc.qcap; this
+  // launch uses the leading pcap / qcap of each)
+  cudaError_t e;
+  {
+    const uint32_t n = tokens * a.heads * (kAtD / 4);
+    at_pack_rows_kernel<<<(n + 255) / 256, 256, 0, stream>>>(a.q, tokens, qd, a.heads, qcap, sc.qp);
+    const uint32_t m = last * a.kv_heads * (kAtD / 4);
+    at_pack_rows_kernel<<<(m + 255) / 256, 256, 0, stream>>>(a.kcache, last, a.kvd, a.kv_heads, pcap, sc.kp);
+    at_pack_values_t_kernel<<<dim3(pcap / 32, kAtD / 32, a.kv_heads), 256, 0, stream>>>(a.vcache, last, a.kvd, pcap,
+                                                                                        sc.vt);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  CUtensorMap kmap, qmap, vmap, wmap;
+  if (!make_map(&kmap, sc.kp, kAtD, pcap, (uint64_t)a.kv_heads * 4, kAtD, (uint64_t)pcap * kAtD, kTcTileM, 1) ||
+      !make_map(&qmap, sc.qp, kAtD, qcap, (uint64_t)a.heads * 4, kAtD, (uint64_t)qcap * kAtD, kTcTileN, 1) ||
+      !make_map(&vmap, sc.vt, pcap, kAtD, (uint64_t)a.kv_heads * 4, pcap, (uint64_t)kAtD * pcap, kTcTileM, 1) ||
+      !make_map(&wmap, sc.wp, pcap, qcap, (uint64_t)a.heads * 3, pcap, (uint64_t)qcap * pcap, kTcTileN, 1))
+    return cudaErrorInvalidValue;
+  const uint32_t qtiles = qcap / kTcTileN, ktiles = pcap / kTcTileM, sms = (uint32_t)device_sms();
+  ScoreTilesS st;
+  st.heads = a.heads, st.group = group, st.qtiles = qtiles, st.ktiles = ktiles;
+  ScoreEpi se{sc.s, qtiles, ktiles, qcap, pcap, tokens, a.mode, a.scale_q32};
+  const uint32_t sc_tiles = a.heads * qtiles * ktiles;
+  e = launch_k(attn_tc_scores_kernel, dim3(std::min(sc_tiles, sms)), dim3(kAtThreads), score_smem(), stream, st, se,
+               kmap, qmap, fault);
+  if (e != cudaSuccess) return e;
+  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), 0, stream, (const int32_t*)sc.s, sc.wp,
+               qcap, pcap, a.pos0, a.heads);
+  if (e != cudaSuccess) return e;
+  ValueTilesS vt;
+  vt.heads = a.heads, vt.group = group, vt.qtiles = qtiles, vt.kstages = pcap / kTcTileK;
+  ValueEpi ve{a.ctx_planes, a.ctx, qtiles, tokens, qd, pcap};
+  const uint32_t v_tiles = a.heads * qtiles;
+  return launch_k(attn_tc_values_kernel, dim3(std::min(v_tiles, sms)), dim3(kAtThreads), value_smem(), stream, vt,
+                  ve, vmap, wmap, fault);
+}
+
+cudaError_t prepare_attn_tc_kernels() {
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)score_smem());
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_tc_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)value_smem());
+  return e;
+}
+
+}  // namespace iris

@@ -73,6 +73,25 @@ bool attention_cluster_shape_ok(uint32_t heads, uint32_t kv_heads, uint32_t d, u
 cudaError_t launch_attention_decode(const AttnArgs& a, cudaStream_t s);
 // Many queries at positions pos0.. (prefill, chain ranges): one block a
 // (query, head). max_visible bounds the shared memory.
+// Scratch of the tensor-core prefill attention (attn_tc.cu), carved from one
+// allocation sized for pcap positions (a multiple of 128) and qcap queries (a
+// multiple of 64): scores [heads][qcap][pcap] int32, weight planes
+// [heads][3][qcap][pcap], key planes [kv_heads][4][pcap][128], transposed
+// value planes [kv_heads][4][128][pcap], query planes [heads][4][qcap][128].
+struct AttnTcScratch {
+  int32_t* s = nullptr;
+  uint8_t *wp = nullptr, *kp = nullptr, *vt = nullptr, *qp = nullptr;
+  uint32_t pcap = 0, qcap = 0;
+};
+size_t attn_tc_scratch_bytes(uint32_t heads, uint32_t kv_heads, uint32_t pcap, uint32_t qcap);
+void attn_tc_scratch_carve(uint8_t* base, uint32_t heads, uint32_t kv_heads, uint32_t pcap, uint32_t qcap,
+                           AttnTcScratch* sc);
+// Whether the tensor-core path takes this range: head_dim 128, no sliding
+// window cutting the prefix, at most 22,016 positions and the scratch's.
+bool attn_tc_usable(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc);
+cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc,
+                                        cudaStream_t stream);
+cudaError_t prepare_attn_tc_kernels();
 cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_t max_visible,
                                      cudaStream_t s);
 

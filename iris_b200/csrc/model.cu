@@ -132,6 +132,11 @@ struct IrisModel {
 struct IrisSession {
   IrisModel* m = nullptr;
   uint32_t cap = 0, len = 0;
+  // tensor-core prefill attention scratch, allocated on the first range that
+  // takes it (attn_tc_state: 0 not tried, 1 ready, 2 unavailable)
+  uint8_t* attn_tc_buf = nullptr;
+  AttnTcScratch attn_tc;
+  int attn_tc_state = 0;
   bool has_logits = false;  // a pass has run since the last reset
   int32_t *kc = nullptr, *vc = nullptr;
   int32_t *x = nullptr, *tmp = nullptr, *q = nullptr, *qkv = nullptr, *xs = nullptr, *pg = nullptr,
@@ -187,7 +192,7 @@ void free_session(IrisSession* s) {
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
-                  s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots};
+                  s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
   for (void* p : ptrs) cudaFree(p);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -509,6 +514,30 @@ cudaError_t row_parallel_resid(IrisSession* s, ProductArgs a, uint32_t tokens) {
   return e;
 }
 
+// Many-query attention of a mistral range: the tensor-core kernels where the
+// shape allows (head_dim 128, no window cutting the prefix) and the model's
+// many-token products are on the tensor cores, else the CUDA-core kernel.
+cudaError_t launch_prefill_attention(IrisSession* s, const AttnArgs& at, uint32_t tokens, cudaStream_t st) {
+  IrisModel* m = s->m;
+  if (m->gemm_mode == IRIS_GEMM_AUTO && tokens >= kTcMinTokens && s->attn_tc_state != 2) {
+    if (s->attn_tc_state == 0) {
+      s->attn_tc_state = 2;
+      const uint32_t pcap = (std::min<uint32_t>(s->cap, 22016) + 127) / 128 * 128;
+      const uint32_t qcap = (kMaxRows + 63) / 64 * 64;
+      const size_t bytes = attn_tc_scratch_bytes(m->heads, m->kvh, pcap, qcap);
+      if (m->d == 128 && cudaMalloc((void**)&s->attn_tc_buf, bytes) == cudaSuccess) {
+        attn_tc_scratch_carve(s->attn_tc_buf, m->heads, m->kvh, pcap, qcap, &s->attn_tc);
+        s->attn_tc_state = 1;
+      } else {
+        cudaGetLastError();  // no room: the CUDA-core kernel serves this session
+      }
+    }
+    if (s->attn_tc_state == 1 && attn_tc_usable(at, tokens, s->attn_tc))
+      return launch_attention_prefill_tc(at, tokens, s->attn_tc, st);
+  }
+  return launch_attention_prefill(at, tokens, at.pos0 + tokens, st);
+}
+
 cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint32_t* pos_ptr,
                           uint32_t pos0) {
   IrisModel* m = s->m;
@@ -541,7 +570,7 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   if (e != cudaSuccess) return e;
   // attention over positions 0..=p, context as planes
   AttnArgs at = attn_args(s, l, pos_ptr, pos0);
-  e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, pos0 + tokens, st);
+  e = one ? launch_attention_decode(at, st) : launch_prefill_attention(s, at, tokens, st);
   if (e != cudaSuccess) return e;
   // x = x + W_o ctx
   ProductArgs o = session_product_args(s, L.o, tokens);
@@ -887,6 +916,7 @@ int alloc_layers(IrisModel* m) {
   }
   if (e == cudaSuccess) e = prepare_product_kernels();
   if (e == cudaSuccess) e = prepare_layer_kernels();
+  if (e == cudaSuccess) e = prepare_attn_tc_kernels();
   return (int)e;
 }
 

@@ -36,11 +36,13 @@
 #include "detnum.cuh"
 #include "gemv.cuh"
 #include "tc.cuh"
+#include "tcgen05.cuh"
 
 namespace iris {
 
 namespace {
 
+static_assert(kTcRows == kTcTileM && kTcTok == kTcTileN && kTcKChunk == kTcTileK, "tile shape of tcgen05.cuh");
 constexpr uint32_t kTcAPlane = kTcRows * kTcKChunk;             // bytes of one weight plane a stage
 constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one activation plane a stage
 constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
@@ -57,55 +59,6 @@ static_assert(kTcAccCols <= kTcTmemCols, "TMEM columns");
 // u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127.
 __host__ __device__ constexpr int64_t tc_diag_min(uint32_t s) {
   return s == 2 ? -32640 : (s == 3 || s == 4) ? -65280 : s == 5 ? -16256 : 0;
-}
-
-// Shared-memory matrix descriptor of a K-major tile with 128-byte rows in
-// the 128-byte swizzle (eight-row groups 1024 bytes apart), sm_100 version.
-// A start 32 k bytes into the rows addresses their columns 32 k ..: the
-// swizzle is a function of the address bits, as the TMA wrote them.
-static_assert(kTcKChunk == 128, "descriptor and tensor maps assume 128-byte rows");
-__device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
-  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(8 * kTcKChunk >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-// Instruction descriptor: int32 accumulator, A (weights) and B (activations)
-// K-major, u8 or s8 each, M = 128, N = 64.
-__host__ __device__ constexpr uint32_t tc_idesc(bool a_signed, bool b_signed) {
-  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((kTcTok >> 3) << 17) |
-         ((kTcRows >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
-      "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-      : "memory");
-}
-// Arrives on `bar` once every MMA this thread issued so far has completed.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Eight consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// 3-D tiled TMA load (no multicast) completing on `bar`.
-__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y, int32_t z,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
-      : "memory");
 }
 
 // The output of one (token, row) from its rounded value (every epilogue but
@@ -344,33 +297,6 @@ __global__ void tc_planes_kernel(const int8_t* __restrict__ q, const uint16_t* _
     *(uint32_t*)(p1 + k) = b1;
     *(uint32_t*)(p2 + k) = b2;
   }
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
-  });
-  return fn;
-}
-
-// 3-D u8 tensor map (x innermost) with a 128-byte swizzled box.
-bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
-              uint64_t stride_z, uint32_t box_y, uint32_t box_z) {
-  PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
-  if (!enc) return false;
-  cuuint64_t dims[3] = {x, y, z};
-  cuuint64_t strides[2] = {stride_y, stride_z};
-  cuuint32_t box[3] = {kTcKChunk, box_y, box_z};
-  cuuint32_t es[3] = {1, 1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int EPI>

@@ -15,6 +15,13 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
+# torch first: its own CUDA and NCCL libraries are then the process's copies,
+# whatever a test loads before its first use of torch.
+try:
+    import torch  # noqa: F401
+except Exception:  # the CPU-only tests do not need it
+    pass
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200) and the built CUDA library")
