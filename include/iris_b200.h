@@ -78,7 +78,7 @@ int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activatio
  * the decode GEMV (tokens must be 1), the mma.sync GEMM or the tcgen05
  * tensor-core GEMM. The automatic path takes the tensor-core GEMM for 32 or
  * more tokens when the matrix qualifies (every row's block-scale exponents
- * within 5 of each other, cols <= 22016), building its pre-scaled copy
+ * within 5 of each other, cols <= 18848), building its pre-scaled copy
  * (3 bytes a weight) on the first such call; IRIS_PATH_TC on a matrix that
  * does not qualify fails with cudaErrorInvalidValue. */
 int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_activations,

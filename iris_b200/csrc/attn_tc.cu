@@ -321,13 +321,16 @@ __global__ void at_pack_values_t_kernel(const int32_t* __restrict__ src, uint32_
 }
 
 // One block a (query, head): the integer softmax of the query's scores
-// (positions 0..p) into three weight planes over the pcap positions.
+// (positions 0..p) into three weight planes over the pcap positions; the exp
+// terms wait in shared memory (8 B a position) between their sum and the
+// weights.
 constexpr uint32_t kSoftThreads = 256;
 __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t* __restrict__ s, uint8_t* wp,
                                                                   uint32_t qcap, uint32_t pcap, uint32_t pos0,
                                                                   uint32_t heads) {
   pdl_wait();
   pdl_trigger();
+  extern __shared__ __align__(16) unsigned char soft_terms[];
   __shared__ unsigned long long red_key[kSoftThreads / 32], red_sum[kSoftThreads / 32];
   __shared__ int32_t red_w[kSoftThreads / 32];
   __shared__ unsigned long long g_key, g_tot;
@@ -354,8 +357,13 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   __syncthreads();
   const int32_t mx = best_key_value(g_key);
   const uint32_t tmax = best_key_token(g_key);
+  uint64_t* terms = (uint64_t*)soft_terms;  // [n]: each exp term computed once
   uint64_t e = 0;
-  for (uint32_t t = tid; t < n; t += kSoftThreads) e += (uint64_t)softmax_exp_term_act(row[t], mx);
+  for (uint32_t t = tid; t < n; t += kSoftThreads) {
+    const uint64_t term = (uint64_t)softmax_exp_term_act(row[t], mx);
+    terms[t] = term;
+    e += term;
+  }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
   if (lane == 0) red_sum[warp] = e;
@@ -374,7 +382,7 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   for (uint32_t t = tid; t < pcap; t += kSoftThreads) {
     int32_t w = 0;
     if (t < n) {
-      w = tot ? softmax_weight_inv(softmax_exp_term_act(row[t], mx), tot, inv) : 0;
+      w = tot ? softmax_weight_inv((int64_t)terms[t], tot, inv) : 0;
       wsl += w;
     }
     w0[t] = (uint8_t)w;
@@ -389,7 +397,7 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
     int32_t ws = 0;
     for (uint32_t w = 0; w < kSoftThreads / 32; ++w) ws += red_w[w];
     // the residual on the first maximum's weight (ops.rs:274-276); no weight saturates
-    const int32_t wm = tot ? softmax_weight_inv(softmax_exp_term_act(row[tmax], mx), tot, inv) : 0;
+    const int32_t wm = tot ? softmax_weight_inv((int64_t)terms[tmax], tot, inv) : 0;
     const int32_t w = wm + sub_sat(kOneAct, ws);
     w0[tmax] = (uint8_t)w;
     w1[tmax] = (uint8_t)(w >> 8);
@@ -468,8 +476,8 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
   e = launch_k(attn_tc_scores_kernel, dim3(std::min(sc_tiles, sms)), dim3(kAtThreads), score_smem(), stream, st, se,
                kmap, qmap, fault);
   if (e != cudaSuccess) return e;
-  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), 0, stream, (const int32_t*)sc.s, sc.wp,
-               qcap, pcap, a.pos0, a.heads);
+  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), (size_t)last * 8, stream,
+               (const int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, a.heads);
   if (e != cudaSuccess) return e;
   ValueTilesS vt;
   vt.heads = a.heads, vt.group = group, vt.qtiles = qtiles, vt.kstages = pcap / kTcTileK;
@@ -482,6 +490,8 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
 cudaError_t prepare_attn_tc_kernels() {
   cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)score_smem());
+  if (e == cudaSuccess)  // the exp terms of up to kAtMaxPositions positions
+    e = cudaFuncSetAttribute(at_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kAtMaxPositions * 8));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_tc_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)value_smem());
   return e;

@@ -48,18 +48,34 @@ constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one 
 constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
 constexpr uint32_t kTcStages = 2;
 constexpr uint32_t kTcEpiWarps = 16;
-constexpr uint32_t kTcThreads = 32 * (2 + kTcEpiWarps);
 constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to align the ring to 1024 bytes
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDiagonals = 6;
 constexpr uint32_t kTcAccCols = kTcDiagonals * kTcTok;         // accumulators: columns [0, 384)
 static_assert(kTcAccCols <= kTcTmemCols, "TMEM columns");
 
-// Lower bounds of one column's contribution to each diagonal (i + j = s):
-// u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127.
+// Narrow stages: where every activation of a stage's 64 tokens x 128 columns
+// fits 24 bits (plane 3 is the sign extension of plane 2, checked in shared
+// memory by a checker warp), a = a0 + 2^8 a1 + 2^16 a2 with a2 signed, and
+// the stage issues nine MMAs instead of twelve. A tile's first stage always
+// takes the four-plane form, so that every diagonal is initialised. Measured
+// slower on B200 (465 against 377 us for the gate|up shape at 256 tokens:
+// the nine-MMA stages do not run faster on the shared-memory-bound pipe and
+// the check adds reads), so off; the bounds below cover both forms.
+constexpr bool kTcNarrow = false;
+// warps: 0 TMA producer, 1 MMA issuer, 2-17 epilogue, 18 the narrow check
+constexpr uint32_t kTcCheckWarp = 2 + kTcEpiWarps;
+constexpr uint32_t kTcThreads = 32 * (kTcCheckWarp + (kTcNarrow ? 1 : 0));
+
+// Lower bounds of one column's contribution to each diagonal (i + j = s),
+// over both forms (plane 2 unsigned with plane 3, or plane 2 signed alone):
+// u8 x u8 >= 0, u8 x s8 >= 255 * -128, s8 x s8 >= -128 * 127. The largest
+// span of a diagonal, 227,715 a column (s = 2, 3), keeps K * span < 2^32 for
+// K <= kTcMaxCols.
 __host__ __device__ constexpr int64_t tc_diag_min(uint32_t s) {
-  return s == 2 ? -32640 : (s == 3 || s == 4) ? -65280 : s == 5 ? -16256 : 0;
+  return s == 2 || s == 4 ? -65280 : s == 3 ? -97920 : s == 5 ? -16256 : 0;
 }
+static_assert((uint64_t)kTcMaxCols * 227715 < (1ull << 32), "diagonal span");
 
 // The output of one (token, row) from its rounded value (every epilogue but
 // EPI_PARTIAL, which writes its limbs while the accumulators are read).
@@ -80,6 +96,28 @@ __device__ __forceinline__ void tc_finish(const ProductArgs& a, uint32_t tok, ui
   }
 }
 
+// The MMAs of one stage: the three weight planes against the four activation
+// planes, or (kNarrow) three with plane 2 signed; pair (i, j) into diagonal
+// i + j, overwriting a diagonal not yet touched in the tile.
+template <bool kNarrow>
+__device__ __forceinline__ void tc_issue_stage(uint32_t tmem, uint32_t base, uint32_t& touched) {
+  constexpr uint32_t NI = kNarrow ? 3 : 4;
+#pragma unroll
+  for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk) {
+#pragma unroll
+    for (uint32_t j = 0; j < 3; ++j) {
+      const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
+#pragma unroll
+      for (uint32_t i = 0; i < NI; ++i) {
+        const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
+        const uint32_t d = i + j;
+        tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3 || (kNarrow && i == 2)), (touched >> d) & 1u);
+        touched |= 1u << d;
+      }
+    }
+  }
+}
+
 // Persistent: block b takes tiles b, b + gridDim.x, ... (token tiles vary
 // fastest, so the blocks sharing a weight tile run at the same time). The
 // ring runs on across tiles; the MMA warp starts a tile's accumulation once
@@ -91,7 +129,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     q8_gemm_tc_kernel(ProductArgs a, const __grid_constant__ CUtensorMap wmap,
                       const __grid_constant__ CUtensorMap pmap, unsigned int* fault) {
   extern __shared__ uint8_t tc_raw[];
-  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], done, tfree;
+  __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], checked[kTcStages], done, tfree;
+  __shared__ uint32_t narrow_flag[kTcStages];
   __shared__ uint32_t tmem_slot;
   uint8_t* ring = (uint8_t*)(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,6 +142,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    for (uint32_t s = 0; s < kTcStages; ++s) mbar_init(&checked[s], 1);
     mbar_init(&done, 1);
     mbar_init(&tfree, kTcEpiWarps);
     mbar_fence_init();
@@ -157,29 +197,49 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t touched = 0;
         for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
           const uint32_t s = G % kTcStages, use = G / kTcStages;
-          if (!mbar_wait_bounded(&full[s], use & 1, fault)) {
+          if ((kTcNarrow && !mbar_wait_bounded(&checked[s], use & 1, fault)) ||
+              !mbar_wait_bounded(&full[s], use & 1, fault)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t base = smem_addr(ring + s * kTcStage);
-#pragma unroll
-          for (uint32_t kk = 0; kk < kTcKChunk / 32; ++kk) {
-#pragma unroll
-            for (uint32_t j = 0; j < 3; ++j) {
-              const uint64_t ad = tc_desc(base + j * kTcAPlane + kk * 32);
-#pragma unroll
-              for (uint32_t i = 0; i < 4; ++i) {
-                const uint64_t bd = tc_desc(base + 3 * kTcAPlane + i * kTcBPlane + kk * 32);
-                const uint32_t d = i + j;
-                tc_mma(tmem + d * kTcTok, ad, bd, tc_idesc(j == 2, i == 3), (touched >> d) & 1u);
-                touched |= 1u << d;
-              }
-            }
-          }
+          if (kTcNarrow && narrow_flag[s]) tc_issue_stage<true>(tmem, base, touched);
+          else tc_issue_stage<false>(tmem, base, touched);
           tc_commit(&empty[s]);
         }
         tc_commit(&done);  // also after a give-up: the epilogue's wait then ends
+      }
+    }
+  } else if (warp == kTcCheckWarp) {
+    // narrow check: follows the ring stage by stage; a stage past a tile's
+    // first is narrow when plane 3 is the sign extension of plane 2 throughout
+    uint32_t G = 0;
+    bool ok = true;
+    for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (uint32_t kt = 0; kt < nk; ++kt, ++G) {
+        const uint32_t s = G % kTcStages, use = G / kTcStages;
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[s], use & 1, fault))) {
+          ok = false;
+          break;
+        }
+        bool n = kt > 0;
+        if (n) {
+          const uint4* p2 = (const uint4*)(ring + s * kTcStage + 3 * kTcAPlane + 2 * kTcBPlane);
+          const uint4* p3 = p2 + kTcBPlane / 16;
+#pragma unroll 4
+          for (uint32_t k = lane; k < kTcBPlane / 16; k += 32) {
+            const uint4 x = p2[k], y = p3[k];
+            n = n && planes_sign_extended(x.x, y.x) && planes_sign_extended(x.y, y.y) &&
+                planes_sign_extended(x.z, y.z) && planes_sign_extended(x.w, y.w);
+          }
+          n = __all_sync(0xffffffffu, n);
+        }
+        if (lane == 0) {
+          narrow_flag[s] = n;
+          mbar_arrive(&checked[s]);
+        }
+        __syncwarp();
       }
     }
   } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, 16 of the 64 token columns
@@ -227,7 +287,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tfree);  // the accumulators may be overwritten
-      if (EPI != EPI_PARTIAL) {
+      if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
+        // rows 2i, 2i + 1 (lanes 2i, 2i + 1) form a pair: the even lane
+        // finishes the pair for the first 8 tokens, the odd lane for the last 8
+        const bool odd = lane & 1;
+        const uint32_t rowe = row & ~1u;
+#pragma unroll
+        for (uint32_t c = 0; c < kTcTok / 8; ++c) {
+          const int32_t got = __shfl_xor_sync(0xffffffffu, odd ? v[c] : v[kTcTok / 8 + c], 1);
+          const uint32_t tok = m0 + cg * (kTcTok / 4) + (odd ? kTcTok / 8 + c : c);
+          const int32_t v0 = odd ? got : v[c], v1 = odd ? v[kTcTok / 8 + c] : got;
+          if (tok < a.tokens && rowe + 1 < a.rows) epi_pair<EPI>(a, tok, rowe, v0, v1);
+        }
+      } else if (EPI != EPI_PARTIAL) {
 #pragma unroll
         for (uint32_t c = 0; c < kTcTok / 4; ++c) tc_finish<EPI>(a, m0 + cg * (kTcTok / 4) + c, row, v[c], lane);
       }

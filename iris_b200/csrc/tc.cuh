@@ -13,7 +13,7 @@ namespace iris {
 constexpr uint32_t kTcRows = 128, kTcTok = 64, kTcKChunk = 128;
 // Widest K: the largest diagonal sum (three byte-plane products a column)
 // spans less than 2^32, so its int32 accumulator is exact modulo 2^32.
-constexpr uint32_t kTcMaxCols = 22016;
+constexpr uint32_t kTcMaxCols = 18848;
 // Fewest tokens worth a tensor-core launch (below: the mma.sync GEMM).
 constexpr uint32_t kTcMinTokens = 32;
 // Widest spread of a row's block-scale exponents that the three weight

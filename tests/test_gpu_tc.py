@@ -5,9 +5,10 @@ The product is the reference's dot_row per value (q8.rs:56-72); the cases
 push what the tensor-core form depends on: rows whose block-scale exponents
 spread by the most the three weight planes hold (5), weights of -128 and
 127, activations at i32::MIN / MAX (all four byte planes extreme), K up to
-the widest the int32 diagonal accumulators recover (22016), ragged row and
-token counts, and a matrix one exponent too wide, which the tensor-core path
-refuses and the automatic path serves with the mma.sync GEMM.
+the widest the int32 diagonal accumulators recover (18848), activations that
+fit 24 bits (the narrow three-plane stages, alone and mixed with wide ones),
+ragged row and token counts, and a matrix one exponent too wide, which the
+tensor-core path refuses and the automatic path serves with the mma.sync GEMM.
 """
 import ctypes as C
 
@@ -83,7 +84,7 @@ def run(L, blocks, rows, cols, acts, path):
     (200, 4096, 100, 1, 5),     # ragged rows and tokens; subnormal-adjacent exponents
     (130, 1536, 33, 25, 3),
     (64, 14336, 72, 12, 5),
-    (40, 22016, 40, 20, 5),     # the widest K
+    (40, 18848, 40, 20, 5),     # the widest K (a partial last K stage)
 ])
 def test_tc_matches_oracle(L, O, rows, cols, tokens, base_ex, spread):
     from iris_b200 import _lib
@@ -113,6 +114,30 @@ def test_tc_diagonal_sums_past_int32(L, O):
     rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
     assert rc == 0
     assert np.array_equal(got, want)
+
+
+def test_tc_narrow_stages(L, O):
+    """Activations within 24 bits take three planes (plane 2 signed) after a
+    tile's first stage; extremes of that range (2^23 - 1, -2^23) against the
+    largest pre-scaled weights, and one wide value in one stage of one token
+    tile mixing the two forms."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(23)
+    rows, cols, tokens = 256, 14336, 128
+    blocks = spread_matrix(rng, rows, cols, 15, 5, q_extreme=True)
+    b = blocks.reshape(-1, 34)
+    b[:, 0] = 0xFF
+    b[:, 1] = (b[:, 1] & 0xFC) | 0x03
+    acts = np.where(rng.integers(0, 2, size=(tokens, cols)) == 0, (1 << 23) - 1, -(1 << 23)).astype(np.int32)
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0 and np.array_equal(got, want)
+    acts = rng.integers(-(1 << 23), 1 << 23, size=(tokens, cols)).astype(np.int32)
+    acts[70, 5000] = 2**31 - 1
+    acts[3, 9000] = -(2**31)
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0 and np.array_equal(got, want)
 
 
 def test_tc_refuses_a_wider_spread_and_auto_falls_back(L, O):
