@@ -25,12 +25,15 @@ def gpu_count():
 
 @pytest.mark.skipif(gpu_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("exchange,path", [("peer", "step"), ("peer", "graph"), ("nccl", "graph")])
-@pytest.mark.parametrize("config,seed,prompt_len,steps", [("parity-mistral", 41, 19, 10)])
+@pytest.mark.parametrize("config,seed,prompt_len,steps", [("parity-mistral", 41, 19, 10),
+                                                         ("parity-mistral", 43, 100, 4)])
 def test_two_way_tensor_parallel_decode_matches_the_oracle(tmp_path, config, seed, prompt_len, steps, exchange, path):
     """exchange "peer" with path "step": the persistent step on each rank,
     the o / down partial sums exchanged inside it over peer memory and the
     head's first maximum through peer key slots; "graph": one kernel per
-    operation (peer-memory finish kernel, or NCCL sums)."""
+    operation (peer-memory finish kernel, or NCCL sums). The 100-token prompt
+    runs its products on the tensor-core GEMM, the row-parallel ones ending in
+    partial limbs summed over NCCL."""
     from iris_b200 import _lib, build
     from iris_b200.model import synth_host_weights
     from iris_b200.shapes import CONFIGS
