@@ -360,7 +360,7 @@ def main():
 
     # The teacher-forced chain's pass (BASELINE config 5 on one GPU, or one
     # claim tensor-parallel over N): 4096 seeded tokens through the
-    # device-resident prefill in ranges of 256 rows, every layer's products
+    # device-resident prefill in ranges of 512 rows, every layer's products
     # on the tcgen05 GEMM. Whole-call time (ids in, first-maximum token out).
     chain = None
     if args.chain_tokens > 0:
@@ -377,10 +377,10 @@ def main():
             cs = float(t.item())
         csess.close()
         chain = {"tokens": args.chain_tokens, "tok_s": args.chain_tokens / cs, "ms": cs * 1e3,
-                 "range_rows": 256, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
+                 "range_rows": 512, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
                  "note": "the chain stages' arithmetic through iris_session_prefill; checkpoint records "
                          "are not hashed (their Raster encoding is absent)"}
-    # The prefill GEMM on its own (gate|up shape, 256 tokens, the tensor-core
+    # The prefill GEMM on its own (gate|up shape, 512 tokens: one range, the tensor-core
     # copy of a seeded matrix), timed with events over a captured graph of
     # launches: algorithmic int8 ops 2*M*N*K against the dense int8 peak,
     # which is taken as twice the measured bf16 cuBLAS figure (the nominal
@@ -389,17 +389,17 @@ def main():
     gemm_roofline = None
     if rank == 0 and world == 1:
         from iris_b200 import microbench
-        g = microbench.gemm(argparse.Namespace(seed=seed, rows=2 * cfg.ffn, cols=cfg.hidden, tokens=256,
+        g = microbench.gemm(argparse.Namespace(seed=seed, rows=2 * cfg.ffn, cols=cfg.hidden, tokens=512,
                                                iters=10, gemm="tc"))
         bf16 = bf16_peak()
         if bf16:
             int8_peak = 2 * bf16
             gemm_roofline = {"bound": "tensor", "achieved": g["TOPS"], "peak": int8_peak, "unit": "TOPS",
                              "frac": g["TOPS"] / int8_peak, "plane_mma_frac": 12 * g["TOPS"] / int8_peak,
-                             "us_per_launch": g["us_per_launch"], "shape": [256, 2 * cfg.ffn, cfg.hidden],
+                             "us_per_launch": g["us_per_launch"], "shape": [512, 2 * cfg.ffn, cfg.hidden],
                              "kernel": "q8_gemm_tc_kernel<EPI_STORE> (+ planes_kernel)",
                              "peak_kind": "2 x measured bf16 (MEASURED_PEAKS.json)",
-                             "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_256tok.md")}
+                             "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_512tok.md")}
 
     kernels = sess.kernels_per_pass
     line = {

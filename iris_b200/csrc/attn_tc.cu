@@ -337,10 +337,17 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   const uint32_t q = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t n = pos0 + q + 1;
   const int32_t* row = s + ((size_t)h * qcap + q) * pcap;
+  // four consecutive positions a thread (rows and planes are 16-byte aligned:
+  // pcap is a multiple of 128)
   unsigned long long best = 0;
-  for (uint32_t t = tid; t < n; t += kSoftThreads) {
-    const unsigned long long k = best_key(row[t], t);
-    best = k > best ? k : best;
+  for (uint32_t t = 4 * tid; t < n; t += 4 * kSoftThreads) {
+    const int4 v = *(const int4*)(row + t);
+    const int32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      const unsigned long long k = t + u < n ? best_key(x[u], t + u) : 0;
+      best = k > best ? k : best;
+    }
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) {
@@ -357,12 +364,17 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   __syncthreads();
   const int32_t mx = best_key_value(g_key);
   const uint32_t tmax = best_key_token(g_key);
-  uint64_t* terms = (uint64_t*)soft_terms;  // [n]: each exp term computed once
+  uint64_t* terms = (uint64_t*)soft_terms;  // [n rounded up to 4]: each exp term computed once
   uint64_t e = 0;
-  for (uint32_t t = tid; t < n; t += kSoftThreads) {
-    const uint64_t term = (uint64_t)softmax_exp_term_act(row[t], mx);
-    terms[t] = term;
-    e += term;
+  for (uint32_t t = 4 * tid; t < n; t += 4 * kSoftThreads) {
+    const int4 v = *(const int4*)(row + t);
+    const int32_t x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      const uint64_t term = t + u < n ? (uint64_t)softmax_exp_term_act(x[u], mx) : 0;
+      terms[t + u] = term;
+      e += term;
+    }
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
@@ -379,15 +391,22 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   uint8_t* w1 = w0 + (size_t)qcap * pcap;
   uint8_t* w2 = w1 + (size_t)qcap * pcap;
   int32_t wsl = 0;
-  for (uint32_t t = tid; t < pcap; t += kSoftThreads) {
-    int32_t w = 0;
-    if (t < n) {
-      w = tot ? softmax_weight_inv((int64_t)terms[t], tot, inv) : 0;
-      wsl += w;
+  for (uint32_t t = 4 * tid; t < pcap; t += 4 * kSoftThreads) {
+    uint32_t b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (uint32_t u = 0; u < 4; ++u) {
+      int32_t w = 0;
+      if (t + u < n) {
+        w = tot ? softmax_weight_inv((int64_t)terms[t + u], tot, inv) : 0;
+        wsl += w;
+      }
+      b0 |= ((uint32_t)w & 0xFFu) << (8 * u);
+      b1 |= (((uint32_t)w >> 8) & 0xFFu) << (8 * u);
+      b2 |= (((uint32_t)w >> 16) & 0xFFu) << (8 * u);
     }
-    w0[t] = (uint8_t)w;
-    w1[t] = (uint8_t)(w >> 8);
-    w2[t] = (uint8_t)(w >> 16);
+    *(uint32_t*)(w0 + t) = b0;
+    *(uint32_t*)(w1 + t) = b1;
+    *(uint32_t*)(w2 + t) = b2;
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) wsl += __shfl_xor_sync(0xffffffffu, wsl, off);
@@ -476,7 +495,7 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
   e = launch_k(attn_tc_scores_kernel, dim3(std::min(sc_tiles, sms)), dim3(kAtThreads), score_smem(), stream, st, se,
                kmap, qmap, fault);
   if (e != cudaSuccess) return e;
-  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), (size_t)last * 8, stream,
+  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), (size_t)(last + 3) / 4 * 32, stream,
                (const int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, a.heads);
   if (e != cudaSuccess) return e;
   ValueTilesS vt;
@@ -491,7 +510,8 @@ cudaError_t prepare_attn_tc_kernels() {
   cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)score_smem());
   if (e == cudaSuccess)  // the exp terms of up to kAtMaxPositions positions
-    e = cudaFuncSetAttribute(at_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(kAtMaxPositions * 8));
+    e = cudaFuncSetAttribute(at_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)((kAtMaxPositions + 3) / 4 * 32));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_tc_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)value_smem());
   return e;

@@ -32,7 +32,7 @@ using namespace iris;
 
 namespace {
 
-constexpr uint32_t kMaxRows = 256;  // rows a prefill range holds on the device
+constexpr uint32_t kMaxRows = 512;  // rows a prefill range holds on the device (the chain's range_size)
 constexpr int kFamilyMistral = 0, kFamilyGemma = 1;
 
 struct LayerDev {

@@ -197,11 +197,11 @@ def test_long_context_attention():
 
 
 def test_long_prompt_crosses_device_ranges():
-    """A 300-token prompt is processed as two device ranges (256 + 44), both
+    """A 600-token prompt is processed as two device ranges (512 + 88), both
     through the tensor-core GEMM (ranges of 32 or more tokens)."""
     from iris_b200.shapes import parity_mistral
     cfg = parity_mistral()
-    prompt = seeded_prompt(9, 300, cfg.vocab)
+    prompt = seeded_prompt(9, 600, cfg.vocab)
     dm, _, _, got, want = run_both(cfg, 9, prompt, 3)
     assert_same(got, want)
     n, nbytes = dm.tc_matrices()
@@ -210,13 +210,13 @@ def test_long_prompt_crosses_device_ranges():
 
 @pytest.mark.parametrize("per_block", [False, True])
 def test_prefill_tensor_core_and_mma_gemms_agree(per_block):
-    """The same prefill (ranges of 256 and 44 tokens) through the tcgen05 GEMM
+    """The same prefill (ranges of 512 and 88 tokens) through the tcgen05 GEMM
     and through the mma.sync GEMM: every logit and every K/V row equal."""
     from iris_b200.model import DeviceModel, synth_host_weights
     from iris_b200.shapes import parity_mistral
     cfg = parity_mistral()
     w = synth_host_weights(cfg, 41, per_block)
-    prompt = seeded_prompt(41, 300, cfg.vocab)
+    prompt = seeded_prompt(41, 600, cfg.vocab)
     out = {}
     for mode in ("auto", "mma"):
         dm = DeviceModel(cfg, weights=w)
@@ -306,7 +306,7 @@ def test_refusals():
 def test_sequence_check_select_matches_oracle(family):
     """The chain's head check (sequence_check.rs:232-300): rms_norm(final),
     dot_row over the head, softcap (the gemma model's is on), first maximum,
-    for every predicting row; 300 rows cross the device's 256-row ranges (both
+    for every predicting row; 600 rows cross the device's 512-row ranges (both
     on the tensor-core GEMM) and 5 rows take the mma.sync GEMM. A zero row
     ties every score and selects token 0."""
     from iris_b200.model import DeviceModel, synth_host_weights
@@ -317,7 +317,7 @@ def test_sequence_check_select_matches_oracle(family):
     dm = DeviceModel(cfg, weights=w)
     om = OracleModel(cfg, w)
     rng = np.random.default_rng(51)
-    rows = rng.integers(-(1 << 21), 1 << 21, size=(300, cfg.hidden)).astype(np.int32)
+    rows = rng.integers(-(1 << 21), 1 << 21, size=(600, cfg.hidden)).astype(np.int32)
     rows[7] = 0
     rows[8, :3] = [2**31 - 1, -(2**31), 2**31 - 1]
     for sel in (rows, rows[:5]):
