@@ -94,6 +94,8 @@ class MistralConfig:
     eps: float = 1e-5
     tied: bool = False
     family: str = "mistral"
+    # YaRN (factor, low, high) from an imported config.json; None: plain RoPE
+    yarn: Optional[tuple] = None
 
     @property
     def norm_eps(self) -> int:
@@ -102,7 +104,8 @@ class MistralConfig:
     @property
     def freqs(self) -> List[int]:
         # plain RoPE: YaRN factor 1 reduces to base^(-j / pairs)
-        return yarn_inverse_frequencies(self.rope_base, self.head_dim // 2, 1, 0, 1)
+        factor, low, high = self.yarn or (1, 0, 1)
+        return yarn_inverse_frequencies(self.rope_base, self.head_dim // 2, factor, low, high)
 
     @property
     def scale_q32(self) -> int:

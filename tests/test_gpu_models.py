@@ -325,3 +325,44 @@ def test_sequence_check_select_matches_oracle(family):
         want_tok, want_val = om.head_select(sel)
         assert np.array_equal(tok, want_tok) and np.array_equal(val, want_val)
     assert dm.sequence_check_select(rows[7:8])[0][0] == 0
+
+
+def test_detwgt_bundle_matches_the_oracle(tmp_path):
+    """A model bundle in the reference's .detwgt format (written here from
+    seeded weights under their file names, with a YaRN config.json shaped as
+    the reference's parity bundle) loaded through iris_b200.detwgt: every
+    logit and token of a prefill and 8 decode steps equals the oracle's on
+    the same weights and rotary table."""
+    import json
+    from iris_b200 import detwgt
+    from iris_b200.model import DeviceModel, synth_host_weights, tensor_table
+    from iris_b200.shapes import parity_mistral
+    from oracle.models import OracleModel
+    from test_detwgt import write_detwgt
+    config = {"model_type": "mistral3", "text_config": {
+        "hidden_act": "silu", "hidden_size": 128, "intermediate_size": 2048, "num_hidden_layers": 4,
+        "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 32, "vocab_size": 512,
+        "max_position_embeddings": 262144, "sliding_window": None, "rms_norm_eps": 1e-05,
+        "tie_word_embeddings": True,
+        "rope_parameters": {"beta_fast": 32.0, "beta_slow": 1.0, "factor": 16.0, "llama_4_scaling_beta": 0.1,
+                            "mscale": 1.0, "mscale_all_dim": 1.0, "original_max_position_embeddings": 16384,
+                            "rope_theta": 1000000.0, "rope_type": "yarn"}}}
+    cfg = detwgt.mistral_config(config)
+    w = synth_host_weights(parity_mistral(), 61)
+    names = detwgt.mistral_tensor_names(cfg)
+    tensors = []
+    for key, arr in w.items():
+        kind, rows, cols, _ = tensor_table(cfg)[key]
+        dims = [cols] if kind == "values" and rows == 1 else [rows, cols]
+        tensors.append((names[key][0], dims, 8 if kind == "q8" else 32, arr))
+    write_detwgt(tmp_path / "model.detwgt", tensors)
+    (tmp_path / "config.json").write_text(json.dumps(config))
+    cfg2, w2, f = detwgt.load_mistral_bundle(tmp_path)
+    assert cfg2.yarn == (16, 5, 10) and cfg2.freqs != parity_mistral().freqs
+    dm = DeviceModel(cfg2, weights=w2)
+    prompt = seeded_prompt(61, 40, cfg2.vocab)
+    got = dm.session(64).generate(prompt, 8, want_logits=True)
+    want = OracleModel(cfg2, {k: np.array(v) for k, v in w2.items()}).generate(prompt, 8)
+    assert_same(got, want)
+    del w2
+    f.close()
