@@ -319,6 +319,11 @@ void iris_graph_free(void* graph_exec);
  *    (mistral/layer.rs:107-270 via stage.rs:172-226; gemma
  *    prefill_range.rs:307-333). Host buffers in and out.
  * ------------------------------------------------------------------------- */
+/* The embedding rows of token ids (direct/src/view_kernels.rs:37-57 ->
+ * model.rs:316-330 dequantize_row; gemma-dense times embedding_scale):
+ * rows[i*H ..] for ids[i], host buffers. The chain's first stage takes these
+ * rows as its input. Single-GPU models. */
+int iris_model_embed(IrisModel* model, const uint32_t* ids, uint32_t n, int32_t* rows);
 /* The chain's head check (kernels/src/kernels/sequence_check.rs:232-300,
  * run_sequence_check_direct): for each of the n predicting rows (H values
  * each; check_positions at sequence_check.rs:89-125 lists them: the

@@ -87,6 +87,7 @@ SIGNATURES = {
     "iris_model_set_gemm": (C.c_int, [vp, C.c_int]),
     "iris_model_prepare_gemm": (C.c_int, [vp]),
     "iris_sequence_check_select": (C.c_int, [vp, i32p, C.c_uint32, C.POINTER(C.c_uint32), i32p]),
+    "iris_model_embed": (C.c_int, [vp, C.POINTER(C.c_uint32), C.c_uint32, i32p]),
     "iris_model_tc_matrices": (C.c_int, [vp, C.POINTER(C.c_uint64)]),
     "iris_model_free": (None, [vp]),
     "iris_session_create": (C.c_int, [vp, C.c_uint32, C.POINTER(vp)]),

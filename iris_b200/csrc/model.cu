@@ -1519,6 +1519,31 @@ void iris_graph_free(void* graph_exec) {
   if (graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
 }
 
+int iris_model_embed(IrisModel* m, const uint32_t* ids, uint32_t n, int32_t* rows) {
+  if (!m || !ids || !rows || m->tp_world > 1) return IRIS_EINVAL;
+  if (n == 0) return 0;
+  for (uint32_t i = 0; i < n; ++i)
+    if (ids[i] >= m->Vfull) return IRIS_EINVAL;
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  if (!m->scratch) {
+    rc = create_session(m, 512, &m->scratch);
+    if (rc) return rc;
+  }
+  IrisSession* s = m->scratch;
+  const bool gemma = m->family == kFamilyGemma;
+  cudaError_t e = cudaSuccess;
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    const uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->d_ids, ids + r0, (size_t)cnt * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = launch_embed(m->embed, s->d_ids, cnt, gemma, m->embedding_scale, s->x, s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rows + (size_t)r0 * m->H, s->x, (size_t)cnt * m->H * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  }
+  return (int)e;
+}
+
 int iris_sequence_check_select(IrisModel* m, const int32_t* rows, uint32_t n, uint32_t* token_ids,
                                int32_t* values) {
   if (!m || !rows || !token_ids) return IRIS_EINVAL;

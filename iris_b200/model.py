@@ -167,6 +167,13 @@ class DeviceModel:
         """Builds the tensor-core copies of the layer matrices now (not on first use)."""
         check(lib().iris_model_prepare_gemm(self._h), "iris_model_prepare_gemm")
 
+    def embed(self, ids: Sequence[int]) -> np.ndarray:
+        """The embedding rows [n][hidden] of token ids (the chain's first input)."""
+        a = np.ascontiguousarray(ids, np.uint32)
+        out = np.empty((a.size, self.cfg.hidden), np.int32)
+        check(lib().iris_model_embed(self._h, ptr(a, C.c_uint32), a.size, ptr(out, C.c_int32)), "iris_model_embed")
+        return out
+
     def sequence_check_select(self, rows: np.ndarray):
         """The chain's head check over predicting rows [n][hidden]: the
         first-maximum token id and its score for each row."""

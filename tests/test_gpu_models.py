@@ -366,3 +366,41 @@ def test_detwgt_bundle_matches_the_oracle(tmp_path):
     assert_same(got, want)
     del w2
     f.close()
+
+
+def test_chain_records_match_the_oracle():
+    """A claim's teacher-forced pass stage by stage (600 tokens in ranges of
+    512: 2 ranges x 4 layers, K/V carried) through iris_mistral_layer_range,
+    starting from iris_model_embed's rows: every stage's canonical record
+    digest (iris_b200/records.py) equals the digest of the oracle's rows and
+    K/V for the same stage."""
+    import ctypes as C
+    from iris_b200 import records
+    from iris_b200.model import DeviceModel, synth_host_weights
+    from iris_b200.shapes import parity_mistral
+    from oracle import oracle as O
+    from oracle.models import OracleModel
+    cfg = parity_mistral()
+    w = synth_host_weights(cfg, 71)
+    dm = DeviceModel(cfg, weights=w)
+    om = OracleModel(cfg, w)
+    ids = seeded_prompt(71, 600, cfg.vocab)
+    emb = np.asarray(w[("EMBED", -1)]).reshape(cfg.vocab, -1)
+    want_rows = np.empty((len(ids), cfg.hidden), np.int32)
+    for i, t in enumerate(ids):
+        assert O.lib().oracle_dequantize_row(O.ptr(np.ascontiguousarray(emb[t]), C.c_uint8), emb.shape[1],
+                                              O.ptr(want_rows[i], C.c_int32), cfg.hidden) == 0
+    assert np.array_equal(dm.embed(ids), want_rows)
+    got = records.chain_records(dm, ids, range_size=512)
+    kvd = cfg.kv_heads * cfg.head_dim
+    ck = [np.zeros((0, kvd), np.int32) for _ in range(cfg.layers)]
+    cv = [np.zeros((0, kvd), np.int32) for _ in range(cfg.layers)]
+    want = []
+    for start in range(0, len(ids), 512):
+        rows = want_rows[start:start + 512]
+        for l in range(cfg.layers):
+            rows, ok, ov = om.mistral_layer_range(l, rows, start, ck[l], cv[l])
+            want.append((f"layer_mistral/{l}", start, records.stage_digest(f"layer_mistral/{l}", start, rows, ok, ov)))
+            ck[l] = np.concatenate([ck[l], ok])
+            cv[l] = np.concatenate([cv[l], ov])
+    assert got == want and len(got) == 2 * cfg.layers
