@@ -320,6 +320,27 @@ __global__ void at_pack_values_t_kernel(const int32_t* __restrict__ src, uint32_
   }
 }
 
+// The exp term of every distance below the maximum: softmax_exp_term_act
+// (ops.rs:508-556) depends only on d = sub_sat(score, max), an integer in
+// (-2^20, 0] where it is non-zero (d <= -16.0 in Q16.16 gives 0). The table
+// holds the term of d = -i at i, filled once per device by the same device
+// function; d = 0 gives 2^32, which the 32-bit entry wraps to 0 and
+// exp_term_lookup restores. 4 MB, read through L2.
+constexpr uint32_t kExpTableSize = 1u << 20;
+__device__ uint32_t g_exp_terms[kExpTableSize];
+
+__global__ void exp_table_kernel() {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < kExpTableSize) g_exp_terms[i] = (uint32_t)softmax_exp_term_act(-(int32_t)i, 0);
+}
+
+__device__ __forceinline__ uint64_t exp_term_lookup(int32_t score, int32_t mx) {
+  const int32_t d = sub_sat(score, mx);  // <= 0: mx is the maximum
+  if (d >= 0) return (uint64_t)1 << 32;
+  const uint32_t i = (uint32_t)(-(int64_t)d) < kExpTableSize ? (uint32_t)(-(int64_t)d) : 0;
+  return i ? (uint64_t)__ldg(g_exp_terms + i) : 0;
+}
+
 // One block a (query, head): the integer softmax of the query's scores
 // (positions 0..p) into three weight planes over the pcap positions; the exp
 // terms wait in shared memory (8 B a position) between their sum and the
@@ -371,7 +392,7 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
     const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (uint32_t u = 0; u < 4; ++u) {
-      const uint64_t term = t + u < n ? (uint64_t)softmax_exp_term_act(x[u], mx) : 0;
+      const uint64_t term = t + u < n ? exp_term_lookup(x[u], mx) : 0;
       terms[t + u] = term;
       e += term;
     }
@@ -507,6 +528,19 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
 }
 
 cudaError_t prepare_attn_tc_kernels() {
+  {
+    static bool filled[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !filled[dev]) {
+      exp_table_kernel<<<kExpTableSize / 256, 256>>>();
+      e = cudaGetLastError();
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();  // before any stream reads it
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) filled[dev] = true;
+    }
+  }
   cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)score_smem());
   if (e == cudaSuccess)  // the exp terms of up to kAtMaxPositions positions
