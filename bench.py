@@ -358,14 +358,21 @@ def main():
     else:
         roofline = gemv_roofline
 
-    # The teacher-forced chain's pass (BASELINE config 5 on one GPU, or one
-    # claim tensor-parallel over N): 4096 seeded tokens through the
-    # device-resident prefill in ranges of 512 rows, every layer's products
-    # on the tcgen05 GEMM. Whole-call time (ids in, first-maximum token out).
+    # The teacher-forced chain's pass: claims are
+    # independent, so with N GPUs each rank runs its own claim on its own
+    # whole-model copy (replicas; the decode model above is tensor-parallel):
+    # 4096 seeded tokens a claim through the device-resident prefill in ranges
+    # of 512 rows, every layer's products on the tcgen05 GEMM and attention on
+    # the tensor cores. Whole-call time (ids in, first-maximum token out), the
+    # maximum over ranks; tok_s counts every rank's tokens.
     chain = None
     if args.chain_tokens > 0:
-        csess = model.session(args.chain_tokens + 8)
-        cprompt = np.random.default_rng(seed + 5).integers(0, cfg.vocab, size=args.chain_tokens).tolist()
+        cmodel = model
+        if world > 1:
+            cmodel = DeviceModel(cfg, seed=seed)
+            cmodel.prepare_gemm()
+        csess = cmodel.session(args.chain_tokens + 8)
+        cprompt = np.random.default_rng(seed + 5 + rank).integers(0, cfg.vocab, size=args.chain_tokens).tolist()
         if dist:
             dist.barrier()
         t0 = time.perf_counter()
@@ -376,10 +383,13 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             cs = float(t.item())
         csess.close()
-        chain = {"tokens": args.chain_tokens, "tok_s": args.chain_tokens / cs, "ms": cs * 1e3,
+        if cmodel is not model:
+            cmodel.close()
+        chain = {"tokens_per_claim": args.chain_tokens, "claims": world, "tok_s": world * args.chain_tokens / cs,
+                 "ms": cs * 1e3, "parallelism": "replicas (one claim a GPU)" if world > 1 else "single",
                  "range_rows": 512, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
-                 "note": "the chain stages' arithmetic through iris_session_prefill; checkpoint records "
-                         "are not hashed (their Raster encoding is absent)"}
+                 "note": "the chain stages' arithmetic through iris_session_prefill; the canonical stage "
+                         "records (iris_b200/records.py) are not computed in the timed region"}
     # The prefill GEMM on its own (gate|up shape, 512 tokens: one range, the tensor-core
     # copy of a seeded matrix), timed with events over a captured graph of
     # launches: algorithmic int8 ops 2*M*N*K against the dense int8 peak,

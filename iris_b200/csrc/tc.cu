@@ -47,7 +47,9 @@ constexpr uint32_t kTcAPlane = kTcRows * kTcKChunk;             // bytes of one 
 constexpr uint32_t kTcBPlane = kTcTok * kTcKChunk;              // bytes of one activation plane a stage
 constexpr uint32_t kTcStage = 3 * kTcAPlane + 4 * kTcBPlane;    // 81,920
 constexpr uint32_t kTcStages = 2;
-constexpr uint32_t kTcEpiWarps = 16;
+constexpr uint32_t kTcEpiWarps = 16;  // four a TMEM lane quadrant (8 measured slower: 15.0 against 14.5 ms a 2-layer 2048-token prefill)
+constexpr uint32_t kTcEpiCols = kTcTok * 4 / kTcEpiWarps;  // token columns an epilogue warp finishes
+static_assert(kTcEpiWarps % 4 == 0 && kTcEpiCols % 16 == 0, "epilogue split");
 constexpr uint32_t kTcSmem = kTcStages * kTcStage + 1024;      // + room to align the ring to 1024 bytes
 constexpr uint32_t kTcTmemCols = 512;
 constexpr uint32_t kTcDiagonals = 6;
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
       }
     }
-  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, 16 of the 64 token columns
+  } else {  // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, kTcEpiCols token columns
     const uint32_t quad = warp & 3, cg = (warp - 2) >> 2;
     int64_t lo_bound[kTcDiagonals];
 #pragma unroll
@@ -254,10 +256,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const uint32_t row = n0 + 32 * quad + lane;
       const int32_t shift = row < a.tc_rows ? a.tc_shift[row] : 0;
-      int32_t v[kTcTok / 4];
+      int32_t v[kTcEpiCols];
 #pragma unroll
-      for (uint32_t h = 0; h < kTcTok / 4 / 8; ++h) {
-        const uint32_t c0 = cg * (kTcTok / 4) + h * 8;
+      for (uint32_t h = 0; h < kTcEpiCols / 8; ++h) {
+        const uint32_t c0 = cg * kTcEpiCols + h * 8;
         uint32_t r[kTcDiagonals][8];
 #pragma unroll
         for (uint32_t d = 0; d < kTcDiagonals; ++d) tmem_ld8(tmem + ((32 * quad) << 16) + d * kTcTok + c0, r[d]);
@@ -289,19 +291,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive(&tfree);  // the accumulators may be overwritten
       if (EPI == EPI_QKV_ROPE || EPI == EPI_SILU_MUL || EPI == EPI_GELU_MUL) {
         // rows 2i, 2i + 1 (lanes 2i, 2i + 1) form a pair: the even lane
-        // finishes the pair for the first 8 tokens, the odd lane for the last 8
+        // finishes the pair for the first half of the tokens, the odd lane for the second
         const bool odd = lane & 1;
         const uint32_t rowe = row & ~1u;
 #pragma unroll
-        for (uint32_t c = 0; c < kTcTok / 8; ++c) {
-          const int32_t got = __shfl_xor_sync(0xffffffffu, odd ? v[c] : v[kTcTok / 8 + c], 1);
-          const uint32_t tok = m0 + cg * (kTcTok / 4) + (odd ? kTcTok / 8 + c : c);
-          const int32_t v0 = odd ? got : v[c], v1 = odd ? v[kTcTok / 8 + c] : got;
+        for (uint32_t c = 0; c < kTcEpiCols / 2; ++c) {
+          const int32_t got = __shfl_xor_sync(0xffffffffu, odd ? v[c] : v[kTcEpiCols / 2 + c], 1);
+          const uint32_t tok = m0 + cg * kTcEpiCols + (odd ? kTcEpiCols / 2 + c : c);
+          const int32_t v0 = odd ? got : v[c], v1 = odd ? v[kTcEpiCols / 2 + c] : got;
           if (tok < a.tokens && rowe + 1 < a.rows) epi_pair<EPI>(a, tok, rowe, v0, v1);
         }
       } else if (EPI != EPI_PARTIAL) {
 #pragma unroll
-        for (uint32_t c = 0; c < kTcTok / 4; ++c) tc_finish<EPI>(a, m0 + cg * (kTcTok / 4) + c, row, v[c], lane);
+        for (uint32_t c = 0; c < kTcEpiCols; ++c) tc_finish<EPI>(a, m0 + cg * kTcEpiCols + c, row, v[c], lane);
       }
     }
   }
