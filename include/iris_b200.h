@@ -95,7 +95,10 @@ int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_acti
  * address up (make it before any stream capture begins). Nothing must start
  * at zero. Asynchronous and not synchronized: calls in flight at the same time
  * on one device (other streams or host threads) share the array and race;
- * calls on one stream are ordered. */
+ * calls on one stream are ordered. It never builds a matrix's tensor-core
+ * copy (that allocates): 32 or more tokens take the tcgen05 GEMM when an
+ * earlier call of another entry point built the copy, else the mma.sync
+ * GEMM; both give the same values. */
 int iris_q8_product_device_noalloc(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                                    uint32_t tokens, int32_t* d_out, void* stream);
 
