@@ -40,8 +40,8 @@ UNIT = "tok/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=256)
-    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--warmup", type=int, default=4)
     p.add_argument("--impl", default="iris", choices=["iris", "reference"])
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--seed", type=int, default=0x1215B200)
@@ -139,97 +139,89 @@ def algorithmic_bytes_per_step(cfg, context_positions):
     return layer_w * L + head + q8(1, H) + kv_read + kv_write
 
 
-def cpu_baseline(cfg, seed, prompt_len, budget_s=12.0, sample_layers=2):
-    """The oracle (C++ restatement of the reference's Rust CPU path) on the
-    host cores: decode passes of `sample_layers` layers at context
-    `prompt_len`, plus the head; tok/s extrapolated to all layers."""
-    import ctypes as C
-    from iris_b200 import _lib
-    from iris_b200.model import synth_host_weights
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def decode_config(prompt, warmup, world, tp_exchange):
+    """The `config` object of the decode line, the same for both arms."""
+    return {"workload": f"mistral-7b-arch greedy decode after a {prompt}-token prompt (BASELINE config 4)",
+            "model": "mistral-7b-arch", "prompt": prompt, "context_at_start": prompt + warmup,
+            "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
+            "tp_exchange": tp_exchange if world > 1 else None,
+            "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"}
+
+
+def cpu_decode(seed, prompt_len, warmup, steps):
+    """Whole decode passes of the Mistral-7B-architecture model on the host
+    cores through the oracle (the C++ restatement of the reference's Rust CPU
+    path, row-sharded over all host threads as tensor.rs:175-185): the same
+    seeded weights as the device model, generated by the oracle's own copy of
+    the generator (the product library is not loaded). The K/V of the
+    `prompt_len` context positions are seeded random rows in place of a CPU
+    prompt pass (a pass's arithmetic does not depend on their values); each
+    pass then runs the token at the next position through all 32 layers and
+    the head and selects the first maximum, which feeds the next pass.
+    Returns (seconds a pass over `steps` timed passes, threads)."""
     from oracle import oracle as O
-    from oracle.models import OracleModel
+    from oracle.models import CpuDecoder, OracleModel, mistral_7b_shape, synth_mistral_weights
     O.build()
-    keys = [("EMBED", -1), ("FINAL_NORM", -1), ("HEAD", -1)]
-    for l in range(sample_layers):
-        keys += [(n, l) for n in ("W_Q", "W_K", "W_V", "W_O", "W_GATE", "W_UP", "W_DOWN", "NORM_ATTN", "NORM_FFN")]
-    w = synth_host_weights(cfg, seed, only=keys)
-    sub = type(cfg)(**{**cfg.__dict__, "layers": sample_layers})
-    om = OracleModel(sub, w)
     threads = O.threads_default()
-    rng = np.random.default_rng(seed)
-    kvd = cfg.kv_heads * cfg.head_dim
-    pk = rng.integers(-(1 << 17), 1 << 17, size=(prompt_len, kvd)).astype(np.int32)
-    pv = rng.integers(-(1 << 17), 1 << 17, size=(prompt_len, kvd)).astype(np.int32)
-    x = rng.integers(-(2 << 16), 2 << 16, size=(1, cfg.hidden)).astype(np.int32)
-    layer_times, t_start = [], time.perf_counter()
-    while time.perf_counter() - t_start < budget_s or len(layer_times) < sample_layers:
-        l = len(layer_times) % sample_layers
-        t0 = time.perf_counter()
-        x2, _, _ = om.mistral_layer_range(l, x, prompt_len, pk, pv, threads)
-        layer_times.append(time.perf_counter() - t0)
-    logits = np.empty(cfg.vocab, np.int32)
+    cfg = mistral_7b_shape()
+    om = OracleModel(cfg, synth_mistral_weights(cfg, seed, threads=threads))
+    dec = CpuDecoder(om, prompt_len + warmup + steps + 1, threads)
+    dec.fill(prompt_len, seed)
+    tok = int(np.random.default_rng(seed).integers(0, cfg.vocab))
+    for _ in range(warmup):
+        tok = dec.step(tok)
     t0 = time.perf_counter()
-    rc = O.lib().oracle_head_logits(C.byref(om.model.head), O.ptr(np.ascontiguousarray(x2[0]), C.c_int32),
-                                    O.ptr(logits, C.c_int32), threads)
-    head_t = time.perf_counter() - t0
-    assert rc == 0
-    per_token = statistics.mean(layer_times) * cfg.layers + head_t
-    return {"value": 1.0 / per_token, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{len(layer_times)} single-layer decode passes (M=1) at context {prompt_len} over "
-                      f"{sample_layers} layers + 1 head pass, extrapolated to {cfg.layers} layers; "
-                      f"C++ oracle (Rust reference not buildable here), {threads} threads"}
+    for _ in range(steps):
+        tok = dec.step(tok)
+    return (time.perf_counter() - t0) / max(steps, 1), threads
+
+
+def cpu_baseline(seed, prompt_len, steps=4):
+    """The GPU arm's reported CPU baseline: a bounded sample (one untimed and
+    `steps` timed whole decode passes, ~10 s of CPU work on 16 cores)."""
+    per_pass, threads = cpu_decode(seed, prompt_len, 1, steps)
+    return {"value": 1.0 / per_pass, "unit": UNIT, "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+            "sample": f"{steps} whole 32-layer decode passes (+ head, first maximum) at context {prompt_len + 2}.."
+                      f"{prompt_len + steps + 1}, seeded random K/V in place of the CPU prompt pass; C++ oracle "
+                      f"(the Rust reference is not buildable here), {threads} threads"}
 
 
 def run_reference(args):
-    """--impl reference: the CPU reference path (the oracle port) timed on the
-    host cores; each step is one single-layer decode pass at context 2048
-    (rotating over 2 layers), the head timed once; tok/s extrapolated."""
+    """--impl reference: the reference's CPU path (the oracle port: the Rust
+    workspace cannot be built here) timed on the host cores, on this arm's
+    metric and config: W untimed and K timed whole decode passes of the
+    Mistral-7B-architecture model (32 layers + head + first maximum) after a
+    `prompt`-token context, all host threads. Rank 0 alone runs and prints;
+    the other ranks of a torchrun launch exit without work. Imports only the
+    oracle (no product library)."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    import ctypes as C
-    from iris_b200.model import synth_host_weights
-    from iris_b200.shapes import mistral_7b
-    from oracle import oracle as O
-    from oracle.models import OracleModel
-    cfg = mistral_7b()
-    O.build()
-    sample_layers = 2
-    keys = [("EMBED", -1), ("FINAL_NORM", -1), ("HEAD", -1)]
-    for l in range(sample_layers):
-        keys += [(n, l) for n in ("W_Q", "W_K", "W_V", "W_O", "W_GATE", "W_UP", "W_DOWN", "NORM_ATTN", "NORM_FFN")]
-    w = synth_host_weights(cfg, args.seed, only=keys)
-    sub = type(cfg)(**{**cfg.__dict__, "layers": sample_layers})
-    om = OracleModel(sub, w)
-    threads = O.threads_default()
-    rng = np.random.default_rng(args.seed)
-    kvd = cfg.kv_heads * cfg.head_dim
-    pk = rng.integers(-(1 << 17), 1 << 17, size=(args.prompt, kvd)).astype(np.int32)
-    pv = rng.integers(-(1 << 17), 1 << 17, size=(args.prompt, kvd)).astype(np.int32)
-    x = rng.integers(-(2 << 16), 2 << 16, size=(1, cfg.hidden)).astype(np.int32)
-    logits = np.empty(cfg.vocab, np.int32)
-    t0 = time.perf_counter()
-    O.lib().oracle_head_logits(C.byref(om.model.head), O.ptr(np.ascontiguousarray(x[0]), C.c_int32),
-                               O.ptr(logits, C.c_int32), threads)
-    head_t = time.perf_counter() - t0
-    for i in range(args.warmup):
-        om.mistral_layer_range(i % sample_layers, x, args.prompt, pk, pv, threads)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        om.mistral_layer_range(i % sample_layers, x, args.prompt, pk, pv, threads)
-    layer_t = (time.perf_counter() - t0) / max(args.steps, 1)
-    per_token = layer_t * cfg.layers + head_t
-    value = 1.0 / per_token
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_t * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int64",
-            "data": "synthetic (seeded Q8_0 weights and tokens)",
-            "config": {"workload": "mistral-7b-arch decode, 2048-token context, CPU reference path",
-                       "model": "mistral-7b-arch", "context": args.prompt, "parallelism": "replicas"},
+    per_pass, threads = cpu_decode(args.seed, args.prompt, args.warmup, args.steps)
+    value = 1.0 / per_pass
+    sample = (f"each step: one whole 32-layer decode pass (+ head, first maximum) at context "
+              f"{args.prompt + args.warmup + 1}..{args.prompt + args.warmup + args.steps}, seeded random K/V "
+              f"in place of the CPU prompt pass; C++ oracle (the Rust reference cannot be built: no cargo, "
+              f"absent ../raster), {threads} threads")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_pass * 1e3,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+            "dtype": "int64", "data": "synthetic (seeded Q8_0 weights, seeded prompt tokens)",
+            "config": decode_config(args.prompt, args.warmup, world, args.tp_exchange),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"each step: one single-layer decode pass (M=1) at context {args.prompt}; "
-                                       f"tok/s = 1/(32 x mean layer step + head pass); C++ oracle "
-                                       f"(the Rust reference cannot be built: no cargo, absent ../raster)"},
+                             "cpu_model": cpu_model(), "nproc": os.cpu_count(), "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -418,11 +410,7 @@ def main():
         "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "int64",
         "data": "synthetic (seeded Q8_0 weights, seeded prompt tokens)",
-        "config": {"workload": "mistral-7b-arch greedy decode after a 2048-token prompt (BASELINE config 4)",
-                   "model": "mistral-7b-arch", "prompt": args.prompt, "context_at_start": ctx0,
-                   "global_batch": 1, "parallelism": f"tp{world}" if world > 1 else "single",
-                   "tp_exchange": args.tp_exchange if world > 1 else None,
-                   "l2": "not flushed: every step streams ~7.6 GB of weights (> 126 MB L2)"},
+        "config": decode_config(args.prompt, args.warmup, world, args.tp_exchange),
         "roofline": roofline,
         "gemv_roofline": gemv_roofline,
         "decode_path": path,
@@ -439,7 +427,7 @@ def main():
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(cfg, seed, args.prompt)
+        line["cpu_baseline"] = cpu_baseline(seed, args.prompt)
     sess.close()
     model.close()
     if dist:

@@ -71,7 +71,10 @@ int q8gpu_product(const Q8GpuMatrix* matrix, const int32_t* activations, uint32_
 int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
                           Q8GpuMatrix** out_matrix);
 /* The same product as q8gpu_product with device pointers on a CUDA stream
- * (cudaStream_t passed as void*, NULL = default stream). Asynchronous. */
+ * (cudaStream_t passed as void*, NULL = default stream). One token is
+ * asynchronous; more tokens build their byte planes in a scratch buffer the
+ * next call reuses, so the call waits for the stream before it returns (and
+ * the first many-token call on a matrix builds its tensor-core copy). */
 int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                            uint32_t tokens, int32_t* d_out, void* stream);
 /* Generic-kernel timing hooks for the Q8 sweep: same product, forced through
@@ -92,7 +95,9 @@ int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_acti
  * live in a fixed 16 MiB device array, so tokens > 1 needs
  * tokens * cols * 4 <= 16 MiB (else IRIS_ESCRATCH, nothing launched); one
  * token needs no scratch. The first call on each device looks the array's
- * address up (make it before any stream capture begins). Nothing must start
+ * address up (make it before any stream capture begins) and keeps it for the
+ * life of the process: a cudaDeviceReset, which also frees every uploaded
+ * matrix, ends the use of this entry point on that device. Nothing must start
  * at zero. Asynchronous and not synchronized: calls in flight at the same time
  * on one device (other streams or host threads) share the array and race;
  * calls on one stream are ordered. It never builds a matrix's tensor-core
@@ -209,6 +214,10 @@ int iris_model_prepare_gemm(IrisModel* model);
 /* Number of the model's matrices holding a tensor-core copy; *bytes (if not
  * NULL) receives the device bytes those copies take. */
 int iris_model_tc_matrices(const IrisModel* model, uint64_t* bytes);
+/* No counterpart in the reference (inspection). counts[0] = many-query
+ * (prefill and chain-range) attention launches of this model that ran on the
+ * tensor cores, counts[1] = those that ran on the CUDA-core kernel. */
+int iris_model_attention_ranges(const IrisModel* model, uint64_t* counts);
 void iris_model_free(IrisModel* model);
 
 /* A decoding session: the K/V cache for up to max_positions positions. */
@@ -358,6 +367,24 @@ int iris_synth_q8_block(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t 
                         uint8_t* blocks);
 int iris_synth_values(uint64_t seed, uint32_t tensor, int32_t layer, uint64_t count, uint32_t fan_in,
                       int32_t* values);
+
+/* No counterpart in the reference (inspection of the softmax_exp_term
+ * table, det-num ops.rs:508-556). out[i] = the exp term the many-query
+ * softmax uses for a score first+i below the maximum (2^32 at distance 0, 0
+ * from 2^20 = 16.0 on), read through the same device lookup. Fills the
+ * current device's table if needed; synchronous; first + count <= 2^31. */
+int iris_softmax_exp_terms(uint32_t first, uint32_t count, uint64_t* out);
+
+/* No counterpart in the reference (the reference has no device waits; its
+ * host side latches a failed device call and falls back, gpu.rs:126-134).
+ * Runs the library's two bounded device waits alone in one small kernel on
+ * the current device: kind 0 an mbarrier phase (the TMA and tensor-core
+ * pipelines), kind 1 a global arrival counter (the persistent step's
+ * stages). With release != 0 another thread completes the wait and the call
+ * returns 0; with release == 0 nothing does, the wait gives up after about a
+ * second and the call returns IRIS_ESTALL, the device staying usable.
+ * Synchronous; clears the library's fault word before and after. */
+int iris_wait_probe(int kind, int release);
 
 /* Message for any status this library returns. */
 const char* iris_error(int code);

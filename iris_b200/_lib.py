@@ -89,6 +89,9 @@ SIGNATURES = {
     "iris_sequence_check_select": (C.c_int, [vp, i32p, C.c_uint32, C.POINTER(C.c_uint32), i32p]),
     "iris_model_embed": (C.c_int, [vp, C.POINTER(C.c_uint32), C.c_uint32, i32p]),
     "iris_model_tc_matrices": (C.c_int, [vp, C.POINTER(C.c_uint64)]),
+    "iris_model_attention_ranges": (C.c_int, [vp, C.POINTER(C.c_uint64)]),
+    "iris_softmax_exp_terms": (C.c_int, [C.c_uint32, C.c_uint32, C.POINTER(C.c_uint64)]),
+    "iris_wait_probe": (C.c_int, [C.c_int, C.c_int]),
     "iris_model_free": (None, [vp]),
     "iris_session_create": (C.c_int, [vp, C.c_uint32, C.POINTER(vp)]),
     "iris_session_reset": (C.c_int, [vp]),

@@ -25,7 +25,9 @@
 // into K-major byte planes: queries [h][plane][q][d], keys [g][plane][t][d],
 // values transposed [g][plane][d][t], weights [h][plane][q][t].
 #include <algorithm>
+#include <mutex>
 
+#include "../../include/iris_b200.h"
 #include "common.cuh"
 #include "detnum.cuh"
 #include "layers.cuh"
@@ -329,9 +331,14 @@ __global__ void at_pack_values_t_kernel(const int32_t* __restrict__ src, uint32_
 constexpr uint32_t kExpTableSize = 1u << 20;
 __device__ uint32_t g_exp_terms[kExpTableSize];
 
+// Entry 0 is never read as a term (distance 0 returns 2^32 before the
+// lookup), so it holds a marker: a table without it (a fresh module, or one
+// reloaded after cudaDeviceReset) is filled again.
+constexpr uint32_t kExpTableMarker = 0x45585054u;
+
 __global__ void exp_table_kernel() {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < kExpTableSize) g_exp_terms[i] = (uint32_t)softmax_exp_term_act(-(int32_t)i, 0);
+  if (i < kExpTableSize) g_exp_terms[i] = i ? (uint32_t)softmax_exp_term_act(-(int32_t)i, 0) : kExpTableMarker;
 }
 
 __device__ __forceinline__ uint64_t exp_term_lookup(int32_t score, int32_t mx) {
@@ -527,20 +534,29 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
                   ve, vmap, wmap, fault);
 }
 
+// Fills the current device's exp-term table unless it holds the marker. The
+// marker is read from the device (not a host flag), so a module reloaded
+// after cudaDeviceReset is filled again; the mutex keeps two threads creating
+// models from filling it at once.
+cudaError_t ensure_exp_table() {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  uint32_t marker = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&marker, g_exp_terms, sizeof(marker));
+  if (e != cudaSuccess || marker == kExpTableMarker) return e;
+  exp_table_kernel<<<kExpTableSize / 256, 256>>>();
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // before any stream reads it
+  return e;
+}
+
+__global__ void exp_terms_probe_kernel(uint64_t* out, uint32_t first, uint32_t count) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < count) out[i] = exp_term_lookup(-(int32_t)(first + i), 0);
+}
+
 cudaError_t prepare_attn_tc_kernels() {
-  {
-    static bool filled[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !filled[dev]) {
-      exp_table_kernel<<<kExpTableSize / 256, 256>>>();
-      e = cudaGetLastError();
-      if (e == cudaSuccess) e = cudaDeviceSynchronize();  // before any stream reads it
-      if (e != cudaSuccess) return e;
-      if (dev >= 0 && dev < 64) filled[dev] = true;
-    }
-  }
+  if (cudaError_t e = ensure_exp_table(); e != cudaSuccess) return e;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)score_smem());
   if (e == cudaSuccess)  // the exp terms of up to kAtMaxPositions positions
@@ -552,3 +568,19 @@ cudaError_t prepare_attn_tc_kernels() {
 }
 
 }  // namespace iris
+
+extern "C" int iris_softmax_exp_terms(uint32_t first, uint32_t count, uint64_t* out) {
+  using namespace iris;
+  if (!out || (uint64_t)first + count > 0x80000000ull) return IRIS_EINVAL;
+  if (!count) return 0;
+  cudaError_t e = ensure_exp_table();
+  uint64_t* d = nullptr;
+  if (e == cudaSuccess) e = cudaMalloc((void**)&d, (size_t)count * 8);
+  if (e == cudaSuccess) {
+    exp_terms_probe_kernel<<<(count + 255) / 256, 256>>>(d, first, count);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(out, d, (size_t)count * 8, cudaMemcpyDeviceToHost);
+  if (d) cudaFree(d);
+  return (int)e;
+}

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -127,6 +128,8 @@ struct IrisModel {
   TpExchange xch{};       // peer-memory exchange of one-token row-parallel products
   bool xch_nccl = false;  // exchange one-token products over NCCL instead
   int gemm_mode = IRIS_GEMM_AUTO;  // many-token products: tensor-core GEMM where it applies, or mma.sync only
+  // many-query (prefill) attention launches so far: [0] tensor-core, [1] CUDA-core
+  std::atomic<uint64_t> attn_ranges[2] = {};
 };
 
 struct IrisSession {
@@ -432,7 +435,7 @@ void choose_decode_path(IrisSession* s) {
 ProductArgs session_product_args(IrisSession* s, const Q8GpuMatrix* w, uint32_t tokens) {
   // many-token products: the tensor-core copy of the weights, built on first use
   const bool tc = s->m->gemm_mode == IRIS_GEMM_AUTO && tokens >= kTcMinTokens;
-  if (tc && w->tc_state == 0) tc_prepare(const_cast<Q8GpuMatrix*>(w), s->stream);
+  if (tc && tc_state_get(w) == 0) tc_prepare(const_cast<Q8GpuMatrix*>(w), s->stream);
   ProductArgs a = product_args(w, tokens);
   if (!tc) {
     a.tc = nullptr;
@@ -532,9 +535,12 @@ cudaError_t launch_prefill_attention(IrisSession* s, const AttnArgs& at, uint32_
         cudaGetLastError();  // no room: the CUDA-core kernel serves this session
       }
     }
-    if (s->attn_tc_state == 1 && attn_tc_usable(at, tokens, s->attn_tc))
+    if (s->attn_tc_state == 1 && attn_tc_usable(at, tokens, s->attn_tc)) {
+      m->attn_ranges[0].fetch_add(1, std::memory_order_relaxed);
       return launch_attention_prefill_tc(at, tokens, s->attn_tc, st);
+    }
   }
+  m->attn_ranges[1].fetch_add(1, std::memory_order_relaxed);
   return launch_attention_prefill(at, tokens, at.pos0 + tokens, st);
 }
 
@@ -638,6 +644,7 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   if (e != cudaSuccess) return e;
   AttnArgs at = attn_args(s, l, pos_ptr, pos0);
   uint32_t max_vis = L.window ? std::min(L.window, pos0 + tokens) : pos0 + tokens;
+  if (!one) m->attn_ranges[1].fetch_add(1, std::memory_order_relaxed);
   e = one ? launch_attention_decode(at, st) : launch_attention_prefill(at, tokens, max_vis, st);
   if (e != cudaSuccess) return e;
   ProductArgs o = session_product_args(s, L.o, tokens);
@@ -1181,7 +1188,7 @@ int iris_model_tc_matrices(const IrisModel* m, uint64_t* bytes) {
   int n = 0;
   uint64_t b = 0;
   auto count = [&](const Q8GpuMatrix* w) {
-    if (w && w->tc_state == 1) {
+    if (w && tc_state_get(w) == 1) {
       ++n;
       b += (uint64_t)3 * w->tc_rows * w->cols + w->tc_rows;
     }
@@ -1195,6 +1202,13 @@ int iris_model_tc_matrices(const IrisModel* m, uint64_t* bytes) {
   count(m->head);
   if (bytes) *bytes = b;
   return n;
+}
+
+int iris_model_attention_ranges(const IrisModel* m, uint64_t* counts) {
+  if (!m || !counts) return IRIS_EINVAL;
+  counts[0] = m->attn_ranges[0].load(std::memory_order_relaxed);
+  counts[1] = m->attn_ranges[1].load(std::memory_order_relaxed);
+  return 0;
 }
 
 int iris_session_create(IrisModel* m, uint32_t max_positions, IrisSession** out) {

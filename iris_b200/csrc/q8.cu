@@ -173,7 +173,7 @@ ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
   a.kc = w->kc;
   a.nslices = w->nslices;
   a.tokens = tokens;
-  if (w->tc_state == 1) {
+  if (tc_state_get(w) == 1) {
     a.tc = w->tc;
     a.tc_shift = w->tc_shift;
     a.tc_rows = w->tc_rows;
@@ -188,7 +188,7 @@ void tc_invalidate(Q8GpuMatrix* m) {
   m->tc = nullptr;
   m->tc_shift = nullptr;
   m->tc_rows = 0;
-  m->tc_state = 0;
+  tc_state_set(m, 0);
 }
 
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
@@ -926,7 +926,7 @@ cudaError_t reserve(T** buf, size_t* cap, size_t bytes) {
 // it runs (many tokens on the automatic path, or the tensor-core path asked
 // for). The copy is a cache of the weights: the matrix stays logically const.
 cudaError_t prepare_tc_for(const Q8GpuMatrix* m, uint32_t tokens, int path, cudaStream_t s) {
-  if (m->tc_state != 0) return cudaSuccess;
+  if (tc_state_get(m) != 0) return cudaSuccess;
   if (path == IRIS_PATH_TC || (path == IRIS_PATH_AUTO && tokens >= kTcMinTokens))
     return tc_prepare(const_cast<Q8GpuMatrix*>(m), s);
   return cudaSuccess;

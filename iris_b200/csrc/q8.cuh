@@ -35,10 +35,22 @@ struct Q8GpuMatrix {
   uint8_t* tc;
   uint8_t* tc_shift;
   uint32_t tc_rows;
-  int tc_state;
+  int tc_state;  // read and written only through tc_state_get / _set / _claim
 };
 
 namespace iris {
+
+// A matrix may be used from several host threads at once (one product builds
+// the tensor-core copy while another reads the state): the state word is
+// published with release after tc / tc_shift / tc_rows are written, and read
+// with acquire before they are used. Building starts by claiming 0 -> 2, so
+// two threads never build one copy twice.
+inline int tc_state_get(const Q8GpuMatrix* m) { return __atomic_load_n(&m->tc_state, __ATOMIC_ACQUIRE); }
+inline void tc_state_set(Q8GpuMatrix* m, int v) { __atomic_store_n(&m->tc_state, v, __ATOMIC_RELEASE); }
+inline bool tc_state_claim(Q8GpuMatrix* m) {
+  int expected = 0;
+  return __atomic_compare_exchange_n(&m->tc_state, &expected, 2, false, __ATOMIC_ACQ_REL, __ATOMIC_ACQUIRE);
+}
 
 // Slice width for a matrix of `cols` columns (cols a multiple of 32).
 __host__ __device__ inline uint32_t q8_slice_cols(uint32_t cols) {

@@ -36,6 +36,7 @@
 
 #include <algorithm>
 
+#include "../../include/iris_b200.h"
 #include "gemv.cuh"
 #include "step.cuh"
 
@@ -974,4 +975,55 @@ cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_
 
 cudaError_t prepare_step_kernels() { return cudaSuccess; }
 
+namespace {
+
+// The two bounded waits the kernels use, alone in one block: thread 0 waits
+// for an mbarrier phase (kind 0, as the TMA rings and the tensor-core
+// pipelines do) or polls a global arrival counter (kind 1, as the persistent
+// step's stage barriers do); thread 32 arrives or adds first unless `release`
+// is 0, in which case nothing ever does and the wait runs out after about a
+// second, records the give-up in the fault word and the kernel returns.
+// Nothing asynchronous is in flight, so the block ends cleanly either way.
+__global__ void wait_probe_kernel(int kind, int release, unsigned int* ctr, unsigned int* fault) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 32 && release) {
+    if (kind == 0) mbar_arrive(&bar);
+    else red_add_release(ctr, 1u);
+  }
+  if (threadIdx.x == 0) {
+    if (kind == 0) mbar_wait_bounded(&bar, 0, fault);
+    else step_poll(ctr, 1u, fault);
+  }
+  __syncthreads();
+}
+
+}  // namespace
+
 }  // namespace iris
+
+extern "C" int iris_wait_probe(int kind, int release) {
+  using namespace iris;
+  if (kind != 0 && kind != 1) return IRIS_EINVAL;
+  uint32_t stale = 0;
+  cudaError_t e = take_device_fault(&stale);  // start from a clear fault word
+  unsigned int* fault = device_fault_word();
+  if (e == cudaSuccess && !fault) e = cudaErrorInvalidDevice;
+  unsigned int* ctr = nullptr;
+  if (e == cudaSuccess) e = cudaMalloc((void**)&ctr, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemset(ctr, 0, sizeof(unsigned int));
+  if (e == cudaSuccess) {
+    wait_probe_kernel<<<1, 64>>>(kind, release, ctr, fault);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (ctr) cudaFree(ctr);
+  uint32_t gave_up = 0;
+  if (e == cudaSuccess) e = take_device_fault(&gave_up);
+  if (e != cudaSuccess) return (int)e;
+  return gave_up ? IRIS_ESTALL : 0;
+}

@@ -426,12 +426,11 @@ cudaError_t launch_gemm_tc(const ProductArgs& a, EpiMode epi, cudaStream_t strea
 }
 
 cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream) {
-  if (m->tc_state != 0) return cudaSuccess;
-  m->tc_state = 2;
+  if (!tc_state_claim(m)) return cudaSuccess;  // built, unusable, or another thread is building it
   if (m->cols == 0 || m->cols % 32 || m->cols > kTcMaxCols || m->rows == 0) return cudaSuccess;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
-    m->tc_state = 0;  // not inside a capture; a later call builds it
+    tc_state_set(m, 0);  // not inside a capture; a later call builds it
     return cudaSuccess;
   }
   const uint32_t tc_rows = (m->rows + kTcRows - 1) / kTcRows * kTcRows;
@@ -463,7 +462,7 @@ cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream) {
   m->tc = planes;
   m->tc_shift = shift;
   m->tc_rows = tc_rows;
-  m->tc_state = 1;
+  tc_state_set(m, 1);
   return cudaSuccess;
 }
 

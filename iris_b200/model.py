@@ -191,6 +191,12 @@ class DeviceModel:
         n = lib().iris_model_tc_matrices(self._h, C.byref(b))
         return int(n), int(b.value)
 
+    def attention_ranges(self):
+        """(many-query attention launches on the tensor cores, on CUDA cores) so far."""
+        v = (C.c_uint64 * 2)()
+        check(lib().iris_model_attention_ranges(self._h, v), "iris_model_attention_ranges")
+        return int(v[0]), int(v[1])
+
     def session(self, max_positions: int) -> "Session":
         return Session(self, max_positions)
 

@@ -298,7 +298,7 @@ int64_t softmax_exp_term(int64_t delta) {
 
 int64_t attention_softmax_exp_term(int32_t logit, int32_t max_logit) {
   int32_t d = sub_sat(logit, max_logit);
-  return softmax_exp_term((int64_t)d << REQ_SHIFT);  // act_to_acc ops.rs:500-502
+  return softmax_exp_term((int64_t)d * ((int64_t)1 << REQ_SHIFT));  // act_to_acc ops.rs:500-502
 }
 
 void attention_softmax(const int32_t* logits, size_t n, int32_t* weights) {

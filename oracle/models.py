@@ -1,15 +1,111 @@
 """TEST INFRASTRUCTURE ONLY: builds the oracle's model structs from host
-tensors (the same bytes the device model is loaded with).
+tensors (the same bytes the device model is loaded with), the seeded
+synthetic weights of the benchmark configurations, and the CPU decode pass
+the CPU legs time.
 
-Used by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg.
+Used by tests/, __graft_entry__.smoke() and bench.py's CPU legs (its
+reference arm and CPU baseline); nothing here loads the product library.
 """
 from __future__ import annotations
 
 import ctypes as C
+from types import SimpleNamespace
 
 import numpy as np
 
 from . import oracle as O
+
+# Tensor ids of the seeded generator: the numbering of the product's tensor
+# kinds, so that both sides hash the same (tensor, layer, index).
+SYNTH_IDS = {"EMBED": 0, "HEAD": 1, "FINAL_NORM": 2, "W_Q": 3, "W_K": 4, "W_V": 5, "W_O": 6, "W_GATE": 7,
+             "W_UP": 8, "W_DOWN": 9, "NORM_ATTN": 10, "NORM_FFN": 11}
+
+
+def synth_q8(seed, name, layer, rows, cols, per_block=False, threads=None):
+    out = np.empty(rows * (cols // 32) * 34, np.uint8)
+    if O.lib().oracle_synth_q8(seed, SYNTH_IDS[name], layer, rows, cols, int(per_block), O.ptr(out, C.c_uint8),
+                               threads or O.threads_default()):
+        raise ValueError("oracle_synth_q8: bad shape")
+    return out
+
+
+def synth_values(seed, name, layer, count, fan_in=0, threads=None):
+    out = np.empty(count, np.int32)
+    if O.lib().oracle_synth_values(seed, SYNTH_IDS[name], layer, count, fan_in, O.ptr(out, C.c_int32),
+                                   threads or O.threads_default()):
+        raise ValueError("oracle_synth_values: bad arguments")
+    return out
+
+
+def mistral_7b_shape(layers=32):
+    """BASELINE config 4's mistral-dense shape (L32, H4096, F14336, 32q/8kv,
+    d128, V32000, untied head, RoPE base 1e6 as the factor-1 YaRN table,
+    eps 1e-5), its derived values computed by the oracle's own restatements
+    of mistral.rs:148-160 / 185-214 and convert.rs."""
+    d = 128
+    freqs = np.zeros(d // 2, np.int64)
+    if O.lib().oracle_yarn_inverse_frequencies(1_000_000, d // 2, 1, 0, 1, O.ptr(freqs, C.c_int64)):
+        raise ValueError("yarn_inverse_frequencies refused the plain table")
+    return SimpleNamespace(name="mistral-7b-arch", family="mistral", layers=layers, hidden=4096, ffn=14336,
+                           heads=32, kv_heads=8, head_dim=d, vocab=32000, tied=False, max_positions=32768,
+                           norm_eps=int(O.lib().oracle_f32_to_acc(1e-5)),
+                           scale_q32=int(O.lib().oracle_attention_scale_q32(d)), freqs=freqs.tolist())
+
+
+def synth_mistral_weights(cfg, seed, per_block=False, threads=None):
+    """Every tensor of a mistral-dense model from the seeded generator."""
+    H, F, V = cfg.hidden, cfg.ffn, cfg.vocab
+    qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    w = {("EMBED", -1): synth_q8(seed, "EMBED", -1, V, H, per_block, threads),
+         ("FINAL_NORM", -1): synth_values(seed, "FINAL_NORM", -1, H, 0, threads)}
+    if not cfg.tied:
+        w[("HEAD", -1)] = synth_q8(seed, "HEAD", -1, V, H, per_block, threads)
+    for l in range(cfg.layers):
+        for name, rows, cols in (("W_Q", qd, H), ("W_K", kvd, H), ("W_V", kvd, H), ("W_O", H, qd),
+                                 ("W_GATE", F, H), ("W_UP", F, H), ("W_DOWN", H, F)):
+            w[(name, l)] = synth_q8(seed, name, l, rows, cols, per_block, threads)
+        w[("NORM_ATTN", l)] = synth_values(seed, "NORM_ATTN", l, H, 0, threads)
+        w[("NORM_FFN", l)] = synth_values(seed, "NORM_FFN", l, H, 0, threads)
+    return w
+
+
+class CpuDecoder:
+    """The direct decode step on the CPU (executor.rs:172-184): the token's
+    embedding row, every layer at the next position with the K/V of the
+    positions before it, the head and the first maximum. The K/V cache is
+    held here ([layer][position][kv]); `fill` seeds positions 0..n-1 with
+    random rows in place of a prompt pass."""
+
+    def __init__(self, om, capacity, threads=None):
+        c = om.cfg
+        self.om, self.threads = om, threads or O.threads_default()
+        kvd = c.kv_heads * c.head_dim
+        self.k = np.zeros((c.layers, capacity, kvd), np.int32)
+        self.v = np.zeros((c.layers, capacity, kvd), np.int32)
+        self.pos = 0
+        self.logits = np.empty(c.vocab, np.int32)
+        self.emb = np.asarray(om.w[("EMBED", -1)]).reshape(c.vocab, -1)
+
+    def fill(self, n, seed):
+        rng = np.random.default_rng(seed)
+        self.k[:, :n] = rng.integers(-(1 << 17), 1 << 17, size=self.k[:, :n].shape, dtype=np.int32)
+        self.v[:, :n] = rng.integers(-(1 << 17), 1 << 17, size=self.v[:, :n].shape, dtype=np.int32)
+        self.pos = n
+
+    def step(self, token):
+        c, p = self.om.cfg, self.pos
+        x = np.empty((1, c.hidden), np.int32)
+        row = np.ascontiguousarray(self.emb[token])
+        if O.lib().oracle_dequantize_row(O.ptr(row, C.c_uint8), row.size, O.ptr(x[0], C.c_int32), c.hidden):
+            raise RuntimeError("dequantize_row failed")
+        for l in range(c.layers):
+            x, ok, ov = self.om.mistral_layer_range(l, x, p, self.k[l, :p], self.v[l, :p], self.threads)
+            self.k[l, p], self.v[l, p] = ok[0], ov[0]
+        if O.lib().oracle_head_logits(C.byref(self.om.model.head), O.ptr(x[0], C.c_int32),
+                                      O.ptr(self.logits, C.c_int32), self.threads):
+            raise RuntimeError("oracle_head_logits failed")
+        self.pos = p + 1
+        return int(np.argmax(self.logits))  # the first maximum
 
 
 class OracleModel:

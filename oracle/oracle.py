@@ -18,9 +18,22 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "liboracle.so"
 # The reference's GPU product kernel, built unchanged from its own source
 # where the reference checkout is present (oracle/Makefile, _ref/ target).
-REF_Q8_SOURCE = Path(os.environ.get("IRIS_REFERENCE", "/root/reference")) / \
-    "crates/inference/kernels/cuda/q8_product.cu"
+REF_Q8_RELPATH = "crates/inference/kernels/cuda/q8_product.cu"
 REF_Q8_LIB = HERE / "_ref" / "libq8ref.so"
+
+
+def reference_root() -> Path | None:
+    """The reference checkout: $IRIS_REFERENCE, else the `reference_path`
+    that BASELINE.json at the repository root records; None when neither
+    names an existing directory (the GPU box has no checkout)."""
+    cand = os.environ.get("IRIS_REFERENCE")
+    if not cand:
+        try:
+            import json
+            cand = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return Path(cand) if cand and Path(cand).is_dir() else None
 
 i32p = C.POINTER(C.c_int32)
 i64p = C.POINTER(C.c_int64)
@@ -82,12 +95,13 @@ def build(force: bool = False, reference: bool = False) -> Path:
     `reference`, also the reference's own GPU product kernel into _ref/ when
     the reference checkout is present (nvcc). Tests and the GPU box only use
     the prebuilt _ref/ file."""
-    sources = [HERE / n for n in ("det_num.cc", "layers.cc", "det_num.h", "oracle_abi.h")]
+    sources = [HERE / n for n in ("det_num.cc", "layers.cc", "synth.cc", "det_num.h", "oracle_abi.h", "Makefile")]
     if force or not LIB_PATH.exists() or any(
             s.stat().st_mtime > LIB_PATH.stat().st_mtime for s in sources):
         subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
-    if reference and REF_Q8_SOURCE.exists() and (force or not REF_Q8_LIB.exists()):
-        subprocess.run(["make", "-s", "-C", str(HERE), "_ref/libq8ref.so"], check=True)
+    root = reference_root() if reference else None
+    if root is not None and (root / REF_Q8_RELPATH).exists() and (force or not REF_Q8_LIB.exists()):
+        subprocess.run(["make", "-s", "-C", str(HERE), f"REFERENCE={root}", "_ref/libq8ref.so"], check=True)
     return LIB_PATH
 
 
@@ -176,6 +190,10 @@ def _declare(L):
                                          i32p]),
         "oracle_generate": (C.c_int, [C.POINTER(Model), u32p, C.c_size_t, C.c_uint32, u32p,
                                       C.c_size_t, u32p, u32p, i32p, C.c_int]),
+        "oracle_synth_q8": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.c_int,
+                                      u8p, C.c_int]),
+        "oracle_synth_values": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint64, C.c_uint32, i32p,
+                                          C.c_int]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -165,6 +165,15 @@ int oracle_generate(const OracleModel* model, const uint32_t* prompt, size_t n_p
                     uint32_t max_tokens, const uint32_t* eos, size_t n_eos, uint32_t* out_tokens,
                     uint32_t* out_count, int32_t* out_logits, int threads);
 
+// Seeded synthetic weights of the benchmark configurations (synth.cc): Q8_0
+// blocks of a rows x cols tensor, or count dense / norm values (fan_in 0:
+// norm weights). `tensor` is the tensor's id in the generator's numbering,
+// `layer` -1 for model-level tensors. Returns 0, or -1 on a bad shape.
+int oracle_synth_q8(uint64_t seed, uint32_t tensor, int32_t layer, uint32_t rows, uint32_t cols,
+                    int per_block_scales, uint8_t* blocks, int threads);
+int oracle_synth_values(uint64_t seed, uint32_t tensor, int32_t layer, uint64_t count, uint32_t fan_in,
+                        int32_t* values, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -17,7 +17,13 @@ import struct
 import numpy as np
 import pytest
 
-BUNDLE = "/root/reference/model-bundles/parity-mistral"
+def _bundle():
+    from oracle.oracle import reference_root
+    root = reference_root()
+    return str(root / "model-bundles" / "parity-mistral") if root else ""
+
+
+BUNDLE = _bundle()
 
 
 def write_detwgt(path, tensors):
@@ -93,7 +99,7 @@ def test_config_import_refusals():
     assert detwgt.mistral_config(scaled).max_positions == 16384  # mistral.rs:255-266
 
 
-@pytest.mark.skipif(not os.path.isdir(BUNDLE), reason="the reference's parity bundle is not present")
+@pytest.mark.skipif(not BUNDLE or not os.path.isdir(BUNDLE), reason="the reference's parity bundle is not present")
 def test_reference_parity_bundle():
     from iris_b200 import detwgt
     sums = json.load(open(os.path.join(BUNDLE, "checksums.json")))
