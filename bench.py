@@ -63,6 +63,30 @@ def bf16_peak():
         return 1590.0  # the profiling recipe's fallback burst figure
 
 
+def int8_peak_tops(torch):
+    """Dense int8 tensor peak measured here: cuBLASLt's int8 GEMM through
+    torch._int_mm at 8192^3 (2 N^3 ops), best of 10 launches timed with
+    events; twice the measured bf16 figure if that call is unavailable."""
+    try:
+        a = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        b = torch.randint(-128, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = float("inf")
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return 2 * 8192 ** 3 / (best / 1e3) / 1e12, "measured int8 (cuBLASLt via torch._int_mm, 8192^3, this run)"
+    except Exception:
+        return 2 * bf16_peak(), "2 x measured bf16 (MEASURED_PEAKS.json)"
+
+
 def peaks():
     try:
         d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -382,26 +406,29 @@ def main():
                  "range_rows": 512, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
                  "note": "the chain stages' arithmetic through iris_session_prefill; the canonical stage "
                          "records (iris_b200/records.py) are not computed in the timed region"}
-    # The prefill GEMM on its own (gate|up shape, 512 tokens: one range, the tensor-core
-    # copy of a seeded matrix), timed with events over a captured graph of
-    # launches: algorithmic int8 ops 2*M*N*K against the dense int8 peak,
-    # which is taken as twice the measured bf16 cuBLAS figure (the nominal
-    # int8:bf16 ratio of B200; no int8 GEMM is measured here). The twelve
-    # byte-plane MMAs a product issues are reported beside it.
-    gemm_roofline = None
+    # The prefill GEMM on its own (gate|up shape, 512 tokens: one range), timed
+    # with events over a captured graph of launches: algorithmic int8 ops
+    # 2*M*N*K against the dense int8 peak measured in this run (cuBLASLt int8
+    # GEMM through torch._int_mm, 8192^3). Two forms of the tensor-core copy:
+    # one plane (the benchmark's weights have one scale a row: four byte-plane
+    # MMAs a product) and three planes (what per-block scales need: twelve).
+    gemm_roofline = gemm_roofline3 = None
     if rank == 0 and world == 1:
         from iris_b200 import microbench
-        g = microbench.gemm(argparse.Namespace(seed=seed, rows=2 * cfg.ffn, cols=cfg.hidden, tokens=512,
-                                               iters=10, gemm="tc"))
-        bf16 = bf16_peak()
-        if bf16:
-            int8_peak = 2 * bf16
-            gemm_roofline = {"bound": "tensor", "achieved": g["TOPS"], "peak": int8_peak, "unit": "TOPS",
-                             "frac": g["TOPS"] / int8_peak, "plane_mma_frac": 12 * g["TOPS"] / int8_peak,
-                             "us_per_launch": g["us_per_launch"], "shape": [512, 2 * cfg.ffn, cfg.hidden],
-                             "kernel": "q8_gemm_tc_kernel<EPI_STORE> (+ planes_kernel)",
-                             "peak_kind": "2 x measured bf16 (MEASURED_PEAKS.json)",
-                             "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_512tok.md")}
+        int8_peak, int8_kind = int8_peak_tops(torch)
+        for form, planes_mmas in (("tc", 4), ("tc3", 12)):
+            g = microbench.gemm(argparse.Namespace(seed=seed, rows=2 * cfg.ffn, cols=cfg.hidden, tokens=512,
+                                                   iters=10, gemm=form))
+            r = {"bound": "tensor", "achieved": g["TOPS"], "peak": int8_peak, "unit": "TOPS",
+                 "frac": g["TOPS"] / int8_peak, "plane_mma_frac": planes_mmas * g["TOPS"] / int8_peak,
+                 "us_per_launch": g["us_per_launch"], "shape": [512, 2 * cfg.ffn, cfg.hidden],
+                 "kernel": "planes_kernel + " + g["kernel"].split("planes_kernel + ")[-1], "peak_kind": int8_kind,
+                 "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_512tok.md" if form == "tc"
+                                             else "q8_gemm_tc3_gateup_28672x4096_512tok.md")}
+            if form == "tc":
+                gemm_roofline = r
+            else:
+                gemm_roofline3 = r
 
     kernels = sess.kernels_per_pass
     line = {
@@ -424,6 +451,7 @@ def main():
         "prefill_tok_s": args.prompt / prefill_s,
         "chain_prefill": chain,
         "prefill_gemm_roofline": gemm_roofline,
+        "prefill_gemm_roofline_per_block_scales": gemm_roofline3,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -80,16 +80,21 @@ int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activatio
 /* Generic-kernel timing hooks for the Q8 sweep: same product, forced through
  * the decode GEMV (tokens must be 1), the mma.sync GEMM or the tcgen05
  * tensor-core GEMM. The automatic path takes the tensor-core GEMM for 32 or
- * more tokens when the matrix qualifies (every row's block-scale exponents
- * within 5 of each other, cols <= 18848), building its pre-scaled copy
- * (3 bytes a weight) on the first such call; IRIS_PATH_TC on a matrix that
- * does not qualify fails with cudaErrorInvalidValue. */
+ * more tokens when the matrix qualifies (cols <= 18848, and either every row
+ * has one scale, or every row's block-scale exponents lie within 5 of each
+ * other), building its copy on the first such call: 1 byte a weight where
+ * every row has one scale (four MMAs a 32-column step), else 3 bytes a
+ * weight (twelve). IRIS_PATH_TC3 builds and uses the 3-byte form in any case
+ * (measurement; it fails if another form was built first). IRIS_PATH_TC or
+ * IRIS_PATH_TC3 on a matrix that does not qualify fails with
+ * cudaErrorInvalidValue. */
 int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                                 uint32_t tokens, int32_t* d_out, void* stream, int path);
 #define IRIS_PATH_AUTO 0
 #define IRIS_PATH_GEMV 1
 #define IRIS_PATH_GEMM 2
 #define IRIS_PATH_TC 3
+#define IRIS_PATH_TC3 4
 /* No counterpart in the reference. The same product as
  * iris_q8_product_device, allocating nothing: the GEMM path's byte planes
  * live in a fixed 16 MiB device array, so tokens > 1 needs
@@ -200,9 +205,10 @@ int iris_model_get_values(const IrisModel* model, int tensor, int32_t layer, int
 uint64_t iris_model_weight_bytes(const IrisModel* model);
 /* Many-token products (prefill, layer ranges) of a model: IRIS_GEMM_AUTO
  * (default) runs them on the tcgen05 tensor-core GEMM for ranges of 32 or
- * more tokens, over a pre-scaled copy of each qualifying matrix built on its
- * first such product (3 bytes a weight, freed with the model; a matrix whose
- * rows' block-scale exponents spread by more than 5 keeps the mma.sync GEMM);
+ * more tokens, over a copy of each qualifying matrix built on its first such
+ * product (freed with the model: 1 byte a weight where every row has one
+ * scale, else 3 bytes a weight of pre-scaled weights; a matrix whose rows'
+ * block-scale exponents spread by more than 5 keeps the mma.sync GEMM);
  * IRIS_GEMM_MMA runs them all on the mma.sync GEMM. */
 int iris_model_set_gemm(IrisModel* model, int mode);
 #define IRIS_GEMM_AUTO 0

@@ -206,11 +206,29 @@ IRIS_HD void acc128_add(Acc128& a, uint64_t lo, int64_t hi) {
   a.lo = s;
 #endif
 }
-// a += p * 2^e for a signed 64-bit p and 0 <= e <= 29.
+// a += p * 2^e for a signed 64-bit p and 0 <= e <= 63.
 IRIS_HD void acc128_add_shifted(Acc128& a, int64_t p, int32_t e) {
   uint64_t lo = (uint64_t)p << e;
   int64_t hi = e == 0 ? (p >> 63) : (p >> (64 - e));
   acc128_add(a, lo, hi);
+}
+// The limbs of an unrounded 128-bit row sum (tensor parallelism's partial
+// sums): bits 0-31, 32-63, 64-95 (unsigned) and 96-127 (signed), each in an
+// int64, so that the sums of up to 2^31 shards' limbs are exact in int64.
+IRIS_HD void limbs_from_acc128(uint64_t lo, int64_t hi, int64_t* l) {
+  l[0] = (int64_t)(lo & 0xffffffffull);
+  l[1] = (int64_t)(lo >> 32);
+  l[2] = (int64_t)((uint64_t)hi & 0xffffffffull);
+  l[3] = hi >> 32;
+}
+// a += the 128-bit total the (summed) limbs l0 + 2^32 l1 + 2^64 l2 + 2^96 l3
+// stand for, modulo 2^128: l0, l1, l2 are sums of unsigned 32-bit limbs
+// (non-negative, below 2^63), l3 of signed ones.
+IRIS_HD void acc128_add_limbs(Acc128& a, int64_t l0, int64_t l1, int64_t l2, int64_t l3) {
+  acc128_add(a, (uint64_t)l0, 0);
+  acc128_add(a, (uint64_t)l1 << 32, (int64_t)((uint64_t)l1 >> 32));
+  acc128_add(a, 0, l2);
+  acc128_add(a, 0, (int64_t)((uint64_t)l3 << 32));
 }
 // round_to_i32(total, 24) (q8.rs:94-104): total / 2^24, ties to even, saturated.
 IRIS_HD int32_t acc128_round_q24(Acc128 a) {

@@ -440,7 +440,9 @@ ProductArgs session_product_args(IrisSession* s, const Q8GpuMatrix* w, uint32_t 
   if (!tc) {
     a.tc = nullptr;
     a.tc_shift = nullptr;
+    a.tc_mant = nullptr;
     a.tc_rows = 0;
+    a.tc_planes = 0;
   }
   a.split_acc = s->split_acc;
   a.split_count = s->split_count;
@@ -1190,7 +1192,7 @@ int iris_model_tc_matrices(const IrisModel* m, uint64_t* bytes) {
   auto count = [&](const Q8GpuMatrix* w) {
     if (w && tc_state_get(w) == 1) {
       ++n;
-      b += (uint64_t)3 * w->tc_rows * w->cols + w->tc_rows;
+      b += (uint64_t)w->tc_planes * w->tc_rows * w->cols + 3ull * w->tc_rows;
     }
   };
   for (const LayerDev& L : m->layers) {

@@ -161,6 +161,7 @@ void free_q8(Q8GpuMatrix* m) {
   }
   cudaFree(m->tc);
   cudaFree(m->tc_shift);
+  cudaFree(m->tc_mant);
   std::free(m);
 }
 
@@ -176,7 +177,9 @@ ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
   if (tc_state_get(w) == 1) {
     a.tc = w->tc;
     a.tc_shift = w->tc_shift;
+    a.tc_mant = w->tc_mant;
     a.tc_rows = w->tc_rows;
+    a.tc_planes = w->tc_planes;
   }
   return a;
 }
@@ -185,9 +188,12 @@ ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens) {
 void tc_invalidate(Q8GpuMatrix* m) {
   cudaFree(m->tc);
   cudaFree(m->tc_shift);
+  cudaFree(m->tc_mant);
   m->tc = nullptr;
   m->tc_shift = nullptr;
+  m->tc_mant = nullptr;
   m->tc_rows = 0;
+  m->tc_planes = 0;
   tc_state_set(m, 0);
 }
 
@@ -871,7 +877,8 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
   if (a.out_stride == 0) a.out_stride = a.rows;
   if (a.tokens == 0 || a.rows == 0) return cudaSuccess;
   if (a.cols == 0 || a.cols % 32 || a.kc == 0) return cudaErrorInvalidValue;
-  bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC) || path == IRIS_PATH_GEMV;
+  const bool tc_path = path == IRIS_PATH_TC || path == IRIS_PATH_TC3;
+  bool gemv = (a.tokens == 1 && path != IRIS_PATH_GEMM && !tc_path) || path == IRIS_PATH_GEMV;
   if (gemv) {
     if (a.tokens != 1) return cudaErrorInvalidValue;
     switch (in) {
@@ -882,7 +889,8 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
     return cudaErrorInvalidValue;
   }
   if (in != IN_PLANES) return cudaErrorInvalidValue;  // callers build planes first
-  if (path == IRIS_PATH_TC || (path == IRIS_PATH_AUTO && a.tokens >= kTcMinTokens && tc_usable(a)))
+  if (path == IRIS_PATH_TC3 && a.tc_planes != 3) return cudaErrorInvalidValue;
+  if (tc_path || (path == IRIS_PATH_AUTO && a.tokens >= kTcMinTokens && tc_usable(a)))
     return launch_gemm_tc(a, epi, stream);
   switch (epi) {
     case EPI_STORE: return launch_gemm<EPI_STORE>(a, stream);
@@ -927,6 +935,7 @@ cudaError_t reserve(T** buf, size_t* cap, size_t bytes) {
 // for). The copy is a cache of the weights: the matrix stays logically const.
 cudaError_t prepare_tc_for(const Q8GpuMatrix* m, uint32_t tokens, int path, cudaStream_t s) {
   if (tc_state_get(m) != 0) return cudaSuccess;
+  if (path == IRIS_PATH_TC3) return tc_prepare(const_cast<Q8GpuMatrix*>(m), s, 3);
   if (path == IRIS_PATH_TC || (path == IRIS_PATH_AUTO && tokens >= kTcMinTokens))
     return tc_prepare(const_cast<Q8GpuMatrix*>(m), s);
   return cudaSuccess;
@@ -1040,9 +1049,10 @@ int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
 int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
                                 int32_t* d_out, void* stream, int path) {
   if (!m || tokens == 0) return tokens == 0 ? 0 : IRIS_EINVAL;
-  if (path < IRIS_PATH_AUTO || path > IRIS_PATH_TC) return IRIS_EINVAL;
+  if (path < IRIS_PATH_AUTO || path > IRIS_PATH_TC3) return IRIS_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;
-  bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC) || path == IRIS_PATH_GEMV;
+  bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC && path != IRIS_PATH_TC3) ||
+              path == IRIS_PATH_GEMV;
   if (gemv) {
     ProductArgs a = product_args(m, tokens);
     a.out = d_out;

@@ -28,13 +28,20 @@ struct Q8GpuMatrix {
   uint32_t rows, cols;
   uint32_t kc, nslices, groups;
   bool owns;
-  // Tensor-core copy for many-token products (built on first use): byte
-  // planes p of W'[r][k] = q m 2^(e - shift[r]) at tc + (p * tc_rows + r) * cols
-  // (planes 0 and 1 unsigned, plane 2 signed), tc_rows = rows rounded up to
-  // 128. tc_state: 0 not built, 1 ready, 2 not usable.
+  // Tensor-core copy for many-token products (built on first use), in one of
+  // two forms (tc_planes), tc_rows = rows rounded up to 128:
+  //  - 1: every row has one scale (each block with a non-zero scale has the
+  //    same scale bits): the signed byte plane W'[r][k] = q (0 in blocks
+  //    whose scale is zero) at tc + r * cols, the row's scale as the signed
+  //    mantissa tc_mant[r] and exponent tc_shift[r] (q8_scale_parts);
+  //  - 3: byte planes p of W'[r][k] = q m 2^(e - shift[r]) at
+  //    tc + (p * tc_rows + r) * cols (planes 0 and 1 unsigned, plane 2
+  //    signed), tc_mant unused.
+  // tc_state: 0 not built, 1 ready, 2 not usable.
   uint8_t* tc;
   uint8_t* tc_shift;
-  uint32_t tc_rows;
+  int16_t* tc_mant;
+  uint32_t tc_rows, tc_planes;
   int tc_state;  // read and written only through tc_state_get / _set / _claim
 };
 
@@ -118,7 +125,8 @@ struct ProductArgs {
   // The matrix's tensor-core copy (Q8GpuMatrix::tc), or NULL
   const uint8_t* tc;
   const uint8_t* tc_shift;
-  uint32_t tc_rows;
+  const int16_t* tc_mant;
+  uint32_t tc_rows, tc_planes;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);
@@ -130,15 +138,6 @@ cudaError_t launch_product(const ProductArgs& a, InMode in, EpiMode epi, cudaStr
 // int32 rows -> byte planes (optionally RMS-normalised), one block a token.
 cudaError_t launch_planes(const int32_t* x, const int32_t* norm_w, int64_t eps, uint32_t tokens,
                           uint32_t cols, uint8_t* planes, cudaStream_t stream);
-// The limbs of an unrounded 128-bit row sum (EPI_PARTIAL): bits 0-31, 32-63,
-// 64-95 (unsigned) and 96-127 (signed), each in an int64, so that the sums of
-// up to 2^31 shards' limbs are exact in int64.
-__host__ __device__ inline void limbs_from_acc128(uint64_t lo, int64_t hi, int64_t* l) {
-  l[0] = (int64_t)(lo & 0xffffffffull);
-  l[1] = (int64_t)(lo >> 32);
-  l[2] = (int64_t)((uint64_t)hi & 0xffffffffull);
-  l[3] = hi >> 32;
-}
 
 // Decodes a first-maximum key (value, lowest index) into its token id.
 __host__ __device__ inline uint32_t best_key_token(unsigned long long key) {

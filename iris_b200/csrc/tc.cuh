@@ -9,7 +9,8 @@
 namespace iris {
 
 // Tile of one block: 128 weight rows (the MMA's M, one TMEM lane a row) by
-// 64 tokens (its N), K staged 128 bytes at a time.
+// 128 tokens (one-plane copies) or kTcTok = 64 tokens (three-plane copies),
+// K staged 128 bytes at a time.
 constexpr uint32_t kTcRows = 128, kTcTok = 64, kTcKChunk = 128;
 // Widest K: the largest diagonal sum (three byte-plane products a column)
 // spans less than 2^32, so its int32 accumulator is exact modulo 2^32.
@@ -20,12 +21,15 @@ constexpr uint32_t kTcMinTokens = 32;
 // planes hold (|q m 2^spread| < 2^23).
 constexpr int32_t kTcMaxSpread = 5;
 
-// Builds the tensor-core copy of a matrix once (three byte planes of the
-// pre-scaled weights and a shift a row). Sets m->tc_state to 1 when the
-// copy is usable, 2 when the matrix does not qualify (a row's scale
-// exponents spread wider than kTcMaxSpread, K above kTcMaxCols) or the
-// device has no room for it; only a launch failure is an error.
-cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream);
+// Builds the tensor-core copy of a matrix once: one signed byte plane and a
+// (mantissa, exponent) a row where every row has one scale, else three byte
+// planes of the pre-scaled weights and a shift a row (planes = 3 asks for
+// the three-plane form in any case, for measurement). Sets m->tc_state to 1
+// when the copy is usable, 2 when the matrix does not qualify (three planes
+// needed and a row's scale exponents spread wider than kTcMaxSpread, K above
+// kTcMaxCols) or the device has no room for it; only a launch failure is an
+// error. Synchronises `stream`.
+cudaError_t tc_prepare(Q8GpuMatrix* m, cudaStream_t stream, int planes = 0);
 // Whether the tensor-core GEMM takes this product.
 bool tc_usable(const ProductArgs& a);
 cudaError_t launch_gemm_tc(const ProductArgs& a, EpiMode epi, cudaStream_t stream);

@@ -27,10 +27,14 @@ __device__ __forceinline__ uint64_t tc_desc(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor: int32 accumulator, A and B K-major, u8 or s8
-// each, M = 128, N = 64.
-__host__ __device__ constexpr uint32_t tc_idesc(bool a_signed, bool b_signed) {
-  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((kTcTileN >> 3) << 17) |
+// each, M = 128, N = n (a multiple of 16, at most 256).
+__host__ __device__ constexpr uint32_t tc_idesc_n(bool a_signed, bool b_signed, uint32_t n) {
+  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) | ((n >> 3) << 17) |
          ((kTcTileM >> 4) << 24);
+}
+// The same with N = 64.
+__host__ __device__ constexpr uint32_t tc_idesc(bool a_signed, bool b_signed) {
+  return tc_idesc_n(a_signed, b_signed, kTcTileN);
 }
 
 __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {

@@ -70,12 +70,8 @@ __global__ void tp_finish_kernel(const int64_t* __restrict__ limbs, uint32_t tok
   const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (uint64_t)tokens * rows) return;
   const int64_t* l = limbs + i * 4;
-  // total = l0 + 2^32 l1 + 2^64 l2 + 2^96 l3; l0, l1, l2 are sums of unsigned
-  // 32-bit limbs (non-negative, below 2^63), l3 of signed ones
-  Acc128 acc{(uint64_t)l[0], 0};
-  acc128_add(acc, (uint64_t)l[1] << 32, (int64_t)((uint64_t)l[1] >> 32));
-  acc128_add(acc, 0, l[2]);
-  acc128_add(acc, 0, (int64_t)((uint64_t)l[3] << 32));
+  Acc128 acc{0, 0};
+  acc128_add_limbs(acc, l[0], l[1], l[2], l[3]);
   out[i] = add_sat(acc128_round_q24(acc), resid[i]);
 }
 
@@ -124,10 +120,7 @@ __global__ void tp_p2p_finish_kernel(TpExchange x, uint32_t rows, const int32_t*
     for (uint32_t j = 0; j < x.world; ++j) {
       const int64_t* src = (j == x.rank ? x.part : x.peer_part[j]) + ((size_t)parity * rows + row) * 4;
       const longlong2 a = __ldcg((const longlong2*)src), b = __ldcg((const longlong2*)(src + 2));
-      acc128_add(acc, (uint64_t)a.x, 0);
-      acc128_add(acc, (uint64_t)a.y << 32, (int64_t)((uint64_t)a.y >> 32));
-      acc128_add(acc, 0, b.x);
-      acc128_add(acc, 0, (int64_t)((uint64_t)b.y << 32));
+      acc128_add_limbs(acc, a.x, a.y, b.x, b.y);
     }
     out[row] = add_sat(acc128_round_q24(acc), resid[row]);
   }

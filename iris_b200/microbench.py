@@ -164,9 +164,10 @@ def gemm(args):
     out = torch.empty((args.tokens, args.rows), dtype=torch.int32, device="cuda")
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
-    if args.gemm == "tc":  # builds the tensor-core copy; the no-alloc calls below then take it
-        _lib.check(L.iris_q8_product_device_path(h, x.data_ptr(), args.tokens, out.data_ptr(), None,
-                                                 _lib.PATH_TC), "tensor-core gemm")
+    if args.gemm in ("tc", "tc3"):  # builds the tensor-core copy; the no-alloc calls below then take it
+        path = _lib.PATH_TC if args.gemm == "tc" else _lib.PATH_TC3
+        _lib.check(L.iris_q8_product_device_path(h, x.data_ptr(), args.tokens, out.data_ptr(), None, path),
+                   "tensor-core gemm")
     # the no-alloc entry point: the tiled GEMM path without a synchronisation
     run = lambda: _lib.check(L.iris_q8_product_device_noalloc(h, x.data_ptr(), args.tokens, out.data_ptr(),
                                                               stream.cuda_stream), "gemm")
@@ -175,7 +176,9 @@ def gemm(args):
     us = device_us(torch, stream, lambda i: run(), args.iters)
     ops = 2 * args.rows * args.cols * args.tokens
     L.q8gpu_free(h)
-    kernel = "q8_gemm_tc_kernel<EPI_STORE>" if args.gemm == "tc" else "q8_gemm_mma_kernel<EPI_STORE>"
+    kernel = {"tc": "q8_gemm_tc_kernel<EPI_STORE, 1> (one-plane copy: one scale a row)",
+              "tc3": "q8_gemm_tc_kernel<EPI_STORE, 3> (three-plane copy: per-block scales)",
+              "mma": "q8_gemm_mma_kernel<EPI_STORE>"}[args.gemm]
     return {"kernel": "planes_kernel + " + kernel, "rows": args.rows, "cols": args.cols,
             "tokens": args.tokens, "us_per_launch": us, "TOPS": ops / us / 1e6}
 
@@ -347,7 +350,7 @@ def main():
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
     p.add_argument("--tokens", type=int, default=256)
-    p.add_argument("--gemm", choices=["tc", "mma"], default="tc", help="gemm: the tcgen05 or the mma.sync GEMM")
+    p.add_argument("--gemm", choices=["tc", "tc3", "mma"], default="tc", help="gemm: the tcgen05 or the mma.sync GEMM")
     p.add_argument("--copies", type=int, default=1)
     p.add_argument("--context", type=int, default=2560)
     p.add_argument("--layers", type=int, default=1)

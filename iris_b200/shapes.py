@@ -222,6 +222,14 @@ def parity_mistral() -> MistralConfig:
                          vocab=512, rope_base=1_000_000, max_positions=16384, tied=True)
 
 
+def tp_mistral() -> MistralConfig:
+    """A small mistral-dense shape for the tensor-parallel tests: its kv heads
+    (8), FFN blocks (1024 / 32) and vocabulary (1024) divide 2, 4 and 8 ranks;
+    the 7B model's group of 4 query heads a kv head."""
+    return MistralConfig("tp-mistral", layers=2, hidden=256, ffn=1024, heads=32, kv_heads=8, head_dim=32,
+                         vocab=1024, rope_base=1_000_000, max_positions=16384, tied=True)
+
+
 def parity_gemma() -> GemmaConfig:
     """A small gemma-dense shape with what the reference's parity bundle
     exercises: a sliding window of 16, two K/V-sharing layers, a full layer
@@ -233,4 +241,5 @@ def parity_gemma() -> GemmaConfig:
                        partial_rotary=0.25, softcap=1.0, layer_scalars=[0, 3 << 15, 0, 1 << 16])
 
 
-CONFIGS = {c.name: c for c in (tiny_gemma(), gemma_2b(), mistral_7b(), parity_mistral(), parity_gemma())}
+CONFIGS = {c.name: c for c in (tiny_gemma(), gemma_2b(), mistral_7b(), parity_mistral(), parity_gemma(),
+                               tp_mistral())}

@@ -55,7 +55,19 @@ def detnum_shim(tmp_path_factory):
         "shim_q8_dequant": (C.c_int32, [C.c_int8, C.c_uint16]),
         "shim_rotate_half": (None, [i32p, i32p, C.c_int64, C.c_uint32]),
     }
+    declare_shim_limbs(L)
     for name, (res, args) in sig.items():
         getattr(L, name).restype = res
         getattr(L, name).argtypes = args
+    L.path = str(out)
     return L
+
+
+def declare_shim_limbs(L):
+    """Signatures of the shim's tensor-parallel limb functions (also used by
+    child processes that load the shim by path)."""
+    i32p, i64p = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
+    L.shim_partial_limbs.restype = None
+    L.shim_partial_limbs.argtypes = [i32p, C.POINTER(C.c_uint8), C.c_uint32, C.c_uint32, i64p]
+    L.shim_round_limb_sums.restype = C.c_int32
+    L.shim_round_limb_sums.argtypes = [i64p]

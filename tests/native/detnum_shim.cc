@@ -61,4 +61,26 @@ int32_t shim_q8_dequant(int8_t q, uint16_t bits) {
   return q8_dequant(q, m, e);
 }
 void shim_rotate_half(int32_t* l, int32_t* r, int64_t f, uint32_t pos) { rotate_half_pair(l, r, f, pos); }
+// Tensor parallelism's partial sum of one row over the blocks [b0, b1) of a
+// raw Q8_0 row: the unrounded 128-bit total as the four limbs of
+// limbs_from_acc128 (the rank's EPI_PARTIAL output).
+void shim_partial_limbs(const int32_t* act, const uint8_t* row, uint32_t b0, uint32_t b1, int64_t* limbs) {
+  Acc128 acc{0, 0};
+  for (uint32_t b = b0; b < b1; ++b) {
+    const uint8_t* blk = row + b * 34;
+    int32_t m, e;
+    q8_scale_parts_finite((uint16_t)(blk[0] | (blk[1] << 8)), &m, &e);
+    int64_t bs = 0;
+    for (int j = 0; j < 32; ++j) bs += (int64_t)(int8_t)blk[2 + j] * act[b * 32 + j];
+    acc128_add_shifted(acc, (bs & 0xFFFFFFFFll) * m, e);
+    acc128_add_shifted(acc, (bs >> 32) * m, e + 32);
+  }
+  limbs_from_acc128(acc.lo, acc.hi, limbs);
+}
+// The rounded output from the limbs summed over the ranks (tp_finish).
+int32_t shim_round_limb_sums(const int64_t* l) {
+  Acc128 acc{0, 0};
+  acc128_add_limbs(acc, l[0], l[1], l[2], l[3]);
+  return acc128_round_q24(acc);
+}
 }

@@ -1,14 +1,20 @@
 """GPU parity of the tcgen05 tensor-core GEMM (many-token Q8_0 products over
-the pre-scaled byte planes) against the CPU oracle, bit for bit.
+the tensor-core copy of the weights) against the CPU oracle, bit for bit.
 
-The product is the reference's dot_row per value (q8.rs:56-72); the cases
-push what the tensor-core form depends on: rows whose block-scale exponents
-spread by the most the three weight planes hold (5), weights of -128 and
-127, activations at i32::MIN / MAX (all four byte planes extreme), K up to
-the widest the int32 diagonal accumulators recover (18848), activations that
-fit 24 bits (the narrow three-plane stages, alone and mixed with wide ones),
-ragged row and token counts, and a matrix one exponent too wide, which the
-tensor-core path refuses and the automatic path serves with the mma.sync GEMM.
+The product is the reference's dot_row per value (q8.rs:56-72). Both forms of
+the copy are covered:
+- three planes (block scales that differ within a row): rows whose
+  block-scale exponents spread by the most the three weight planes hold (5),
+  weights of -128 and 127, activations at i32::MIN / MAX (all four byte
+  planes extreme), K up to the widest the int32 diagonal accumulators recover
+  (18848), activations within 24 bits, ragged row and token counts, and a
+  matrix one exponent too wide, which the tensor-core path refuses and the
+  automatic path serves with the mma.sync GEMM;
+- one plane (one scale a row, 128-token tiles): random signs, exponents from
+  subnormal to the largest finite, blocks whose scale is +0 or -0 mixed into
+  a row, rows with no non-zero scale, extreme weights and activations (totals
+  that saturate), ragged shapes, K = 18848, 2048 tokens against the mma.sync
+  GEMM, and the three-plane form of the same matrices.
 """
 import ctypes as C
 
@@ -116,11 +122,11 @@ def test_tc_diagonal_sums_past_int32(L, O):
     assert np.array_equal(got, want)
 
 
-def test_tc_narrow_stages(L, O):
-    """Activations within 24 bits take three planes (plane 2 signed) after a
-    tile's first stage; extremes of that range (2^23 - 1, -2^23) against the
-    largest pre-scaled weights, and one wide value in one stage of one token
-    tile mixing the two forms."""
+def test_tc_activations_within_24_bits(L, O):
+    """Activations at the extremes of 24 bits (2^23 - 1, -2^23; byte plane 3
+    the sign extension of plane 2) against the largest pre-scaled weights,
+    then a 24-bit matrix with one full-range value in one stage of one token
+    tile."""
     from iris_b200 import _lib
     rng = np.random.default_rng(23)
     rows, cols, tokens = 256, 14336, 128
@@ -166,3 +172,93 @@ def test_tc_equals_mma_gemm_at_2048_tokens(L):
     rc, mma = run(L, blocks, rows, cols, acts, _lib.PATH_GEMM)
     assert rc == 0
     assert np.array_equal(tc, mma)
+
+
+def uniform_matrix(rng, rows, cols, q_extreme=False, exponents=(1, 30)):
+    """Q8_0 blocks with one scale a row (random sign, exponent and mantissa),
+    except blocks whose scale is +0 or -0 (about one in eight; their q stay
+    random) and every seventh row with no non-zero scale at all."""
+    nb_row = cols // 32
+    ex = rng.integers(exponents[0], exponents[1] + 1, size=rows)
+    ex[0], ex[-1] = exponents[1], 0  # the largest exponent; a subnormal row
+    bits = (rng.integers(0, 2, size=rows) << 15) | (ex << 10) | rng.integers(0, 1024, size=rows)
+    bits[0] = 0x7BFF  # 65504, the largest finite scale
+    per_block = np.repeat(bits, nb_row).reshape(rows, nb_row)
+    zero = rng.integers(0, 8, size=(rows, nb_row)) == 0
+    per_block = np.where(zero, np.where(rng.integers(0, 2, size=(rows, nb_row)) == 0, 0x0000, 0x8000), per_block)
+    per_block[::7] = 0x8000
+    per_block = per_block.reshape(-1)
+    nb = rows * nb_row
+    out = np.empty((nb, 34), np.uint8)
+    out[:, 0] = per_block & 0xFF
+    out[:, 1] = (per_block >> 8) & 0xFF
+    if q_extreme:
+        out[:, 2:] = np.where(rng.integers(0, 2, size=(nb, 32)) == 1, 0x7F, 0x80)
+    else:
+        out[:, 2:] = rng.integers(0, 256, size=(nb, 32), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("rows,cols,tokens", [
+    (128, 128, 128),
+    (200, 4096, 100),   # ragged rows and tokens
+    (130, 1536, 33),
+    (64, 14336, 300),   # three 128-token tiles, the last partial
+    (40, 18848, 129),   # the widest K
+])
+def test_one_plane_matches_oracle(L, O, rows, cols, tokens):
+    from iris_b200 import _lib
+    rng = np.random.default_rng(rows * 7 + cols + tokens)
+    blocks = uniform_matrix(rng, rows, cols)
+    acts = full_range_acts(rng, tokens, cols)
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0, _lib.lib().iris_error(rc)
+    assert np.array_equal(got, want), np.argwhere(got != want)[:5]
+
+
+def test_one_plane_extremes(L, O):
+    """q of -128 / 127 under the largest scales against i32::MIN / MAX
+    activations: every accumulator at its bound, totals far past the int32
+    output (saturated by the rounding)."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(17)
+    rows, cols, tokens = 256, 16384, 128
+    blocks = uniform_matrix(rng, rows, cols, q_extreme=True, exponents=(28, 30))
+    acts = np.where(rng.integers(0, 4, size=(tokens, cols)) == 0, I32_MIN, I32_MAX).astype(np.int32)
+    acts[0, :] = I32_MAX
+    acts[1, :] = I32_MIN
+    want = O.linear(acts, blocks, rows)
+    rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_TC)
+    assert rc == 0 and np.array_equal(got, want)
+
+
+def test_one_plane_is_built_and_equals_three_planes_and_mma(L, O):
+    """A one-scale-a-row matrix takes the one-plane form (asking the same
+    handle for the three-plane form afterwards is refused); a fresh upload
+    forced to three planes, and the mma.sync GEMM, give the same 2048 x 2048
+    x 2048 product."""
+    import torch
+    from iris_b200 import _lib
+    rng = np.random.default_rng(2049)
+    rows, cols, tokens = 2048, 2048, 2048
+    blocks = uniform_matrix(rng, rows, cols, exponents=(10, 16))
+    acts = full_range_acts(rng, tokens, cols)
+    h = C.c_void_p()
+    _lib.check(L.iris_q8_upload_blocks(_lib.ptr(blocks, C.c_uint8), rows, cols, C.byref(h)), "upload")
+    try:
+        a = torch.from_numpy(acts).cuda()
+        out = torch.zeros((tokens, rows), dtype=torch.int32, device="cuda")
+        assert L.iris_q8_product_device_path(h, a.data_ptr(), tokens, out.data_ptr(), None, _lib.PATH_TC) == 0
+        assert L.iris_q8_product_device_path(h, a.data_ptr(), tokens, out.data_ptr(), None, _lib.PATH_TC3) == 1
+        torch.cuda.synchronize()
+        one = out.cpu().numpy()
+    finally:
+        L.q8gpu_free(h)
+    rc, three = run(L, blocks, rows, cols, acts, _lib.PATH_TC3)
+    assert rc == 0
+    rc, mma = run(L, blocks, rows, cols, acts, _lib.PATH_GEMM)
+    assert rc == 0
+    assert np.array_equal(one, mma) and np.array_equal(three, mma)
+    sample = rng.choice(tokens, size=24, replace=False)
+    assert np.array_equal(one[sample], O.linear(acts[sample], blocks, rows))
