@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--seed", type=int, default=0x1215B200)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-other-configs", action="store_true",
+                   help="skip BASELINE configs 1 and 3 (tiny Gemma, Gemma-2B decode) after the main line")
     p.add_argument("--tp-exchange", choices=["peer", "nccl"], default="peer",
                    help="N > 1: how decode passes exchange partial sums")
     p.add_argument("--chain-tokens", type=int, default=4096,
@@ -149,6 +151,13 @@ def profiled_traffic(name):
     return None
 
 
+def layer_weights(cfg):
+    """Weights of one mistral-dense layer (q, k, v, o, gate, up, down)."""
+    H, F = cfg.hidden, cfg.ffn
+    qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    return H * (qd + 2 * kvd) + qd * H + 3 * H * F
+
+
 def algorithmic_bytes_per_step(cfg, context_positions):
     """Bytes a decode pass must move: every Q8_0 weight once (34 bytes per 32
     weights), the norm vectors, the embedding row, the K/V rows it reads and
@@ -161,6 +170,77 @@ def algorithmic_bytes_per_step(cfg, context_positions):
     kv_read = 2 * kvd * 4 * context_positions * L
     kv_write = 2 * kvd * 4 * L
     return layer_w * L + head + q8(1, H) + kv_read + kv_write
+
+
+def gemma_decode_bytes(cfg, context):
+    """Algorithmic bytes of one gemma-dense decode pass: every Q8_0 weight
+    once (layers and the tied head), the per-layer dense PLE matrices and the
+    model projection (int32), the token's PLE embedding row, the norm
+    vectors, the K/V rows each layer's window reads and the row it writes."""
+    H, F, V, L, P = cfg.hidden, cfg.ffn, cfg.vocab, cfg.layers, cfg.ple_width
+    qd, kvd, d = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim, cfg.head_dim
+    q8 = lambda r, c: r * c * 34 // 32
+    layer = q8(qd + 2 * kvd, H) + q8(H, qd) + q8(2 * F, H) + q8(H, F) + 2 * P * H * 4 + (5 * H + 2 * d) * 4
+    kv = sum(2 * kvd * 4 * (min(context, cfg.window(l)) if cfg.window(l) else context) for l in range(L))
+    return L * layer + q8(V, H) + L * P * H * 4 + q8(1, L * P) + P * 4 + H * 4 + kv + 2 * kvd * 4 * L
+
+
+def other_configs(torch, seed, peak):
+    """BASELINE configs 1 and 3 on this GPU (device-resident decode loop,
+    CUDA events on the session stream around the timed passes):
+    - config 1, tiny Gemma: 32-token prompt, 64 greedy steps; the same
+      workload through the oracle's decode loop on the host cores beside it;
+    - config 3, Gemma-2B architecture (18 layers, 256k tied head, PLE 256):
+      512-token prompt, 256 greedy steps, with the HBM fraction of the passes'
+      algorithmic bytes (no CPU figure: the oracle's 512-token prompt pass
+      alone takes minutes)."""
+    from iris_b200.model import DeviceModel, synth_host_weights
+    from iris_b200.shapes import gemma_2b, tiny_gemma
+    from oracle.models import OracleModel
+    out = {}
+    for name, cfg, n_prompt, steps in (("config1_tiny_gemma", tiny_gemma(), 32, 64),
+                                       ("config3_gemma_2b", gemma_2b(), 512, 256)):
+        tiny = name.startswith("config1")
+        w = synth_host_weights(cfg, seed) if tiny else None
+        dm = DeviceModel(cfg, weights=w) if tiny else DeviceModel(cfg, seed=seed)
+        dm.prepare_gemm()
+        prompt = np.random.default_rng(seed + 3).integers(0, cfg.vocab, size=n_prompt).tolist()
+        sess = dm.session(n_prompt + steps + 8)
+        stream = torch.cuda.ExternalStream(sess.stream_ptr)
+        times = []
+        for _ in range(2):  # the first run warms the captured pass up
+            sess.reset()
+            sess.prefill(prompt)
+            sess.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            sess.decode_steps(steps)
+            e1.record(stream)
+            sess.synchronize()
+            times.append(e0.elapsed_time(e1) / 1e3)
+        t = times[-1]
+        t0 = time.perf_counter()
+        toks, _ = sess.generate(prompt, steps)
+        e2e = time.perf_counter() - t0
+        r = {"workload": f"{cfg.name}: {n_prompt}-token prompt, {steps} greedy steps",
+             "decode_tok_s": steps / t, "ms_per_step": t * 1e3 / steps,
+             "e2e_generate_s": e2e, "api_e2e": "iris_generate (prompt in, tokens out, prefill included)",
+             "decode_path": sess.decode_path, "kernels_per_step": sess.kernels_per_pass}
+        mean_ctx = n_prompt + (steps + 1) / 2
+        nbytes = gemma_decode_bytes(cfg, mean_ctx)
+        r["roofline"] = {"bound": "hbm", "achieved": nbytes / (t / steps) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": nbytes / (t / steps) / 1e9 / peak, "bytes_per_step": nbytes}
+        if tiny:
+            t0 = time.perf_counter()
+            want, _ = OracleModel(cfg, w).generate(prompt, steps, want_logits=False)
+            cpu = time.perf_counter() - t0
+            r["cpu_baseline"] = {"value": steps / cpu, "unit": "tok/s", "kind": "port", "cores": os.cpu_count(),
+                                 "sample": "the oracle's decode loop (prompt pass included) on all host threads"}
+            r["tokens_equal_oracle"] = toks == want
+        sess.close()
+        dm.close()
+        out[name] = r
+    return out
 
 
 def cpu_model() -> str:
@@ -387,25 +467,45 @@ def main():
         if world > 1:
             cmodel = DeviceModel(cfg, seed=seed)
             cmodel.prepare_gemm()
+        from iris_b200 import records
         csess = cmodel.session(args.chain_tokens + 8)
         cprompt = np.random.default_rng(seed + 5 + rank).integers(0, cfg.vocab, size=args.chain_tokens).tolist()
+        records.chain_claim(csess, cprompt[:512], range_size=512)  # warm: buffers, pinned memory, kernels
+        csess.reset()
         if dist:
             dist.barrier()
         t0 = time.perf_counter()
-        csess.prefill(cprompt)
+        recs, selected, _ = records.chain_claim(csess, cprompt, range_size=512)
         cs = time.perf_counter() - t0
+        # the stages' arithmetic alone: the same claim through iris_session_prefill
+        csess.reset()
+        t0 = time.perf_counter()
+        csess.prefill(cprompt)
+        arith = time.perf_counter() - t0
         if dist:
-            t = torch.tensor([cs], device="cuda")
+            t = torch.tensor([cs, arith], device="cuda")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            cs = float(t.item())
+            cs, arith = (float(x) for x in t.tolist())
         csess.close()
         if cmodel is not model:
             cmodel.close()
-        chain = {"tokens_per_claim": args.chain_tokens, "claims": world, "tok_s": world * args.chain_tokens / cs,
-                 "ms": cs * 1e3, "parallelism": "replicas (one claim a GPU)" if world > 1 else "single",
-                 "range_rows": 512, "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)",
-                 "note": "the chain stages' arithmetic through iris_session_prefill; the canonical stage "
-                         "records (iris_b200/records.py) are not computed in the timed region"}
+        import hashlib
+        T, L = args.chain_tokens, cfg.layers
+        ops = 2 * T * layer_weights(cfg) * L + 4 * cfg.heads * cfg.head_dim * T * (T + 1) // 2 * L  # + QK and PV
+        int8_peak_c = int8_peak_tops(torch)[0] if rank == 0 else None
+        chain = {"tokens_per_claim": T, "claims": world, "tok_s": world * T / cs, "ms": cs * 1e3,
+                 "tok_s_per_gpu": T / cs, "stages": len(recs), "range_rows": 512,
+                 "records_digest": hashlib.sha256("".join(d for _, _, d in recs).encode()).hexdigest(),
+                 "selected_first": [int(x) for x in selected[:4]],
+                 "parallelism": "replicas (one claim a GPU)" if world > 1 else "single",
+                 "api": "iris_session_range_begin/_layer/_end per range and layer (records.chain_claim)",
+                 "in_timed_region": "every stage (32 layers x 8 ranges) on the device, its rows and own K/V "
+                                    "copied out and its canonical record hashed (SHA-256) on host threads, "
+                                    "the head check's first maximum for every row",
+                 "arith_only_ms": arith * 1e3, "arith_only_tok_s": T / arith,
+                 "algorithmic_int8_ops": ops,
+                 "int8_frac": (ops / cs / 1e12 / int8_peak_c) if int8_peak_c else None,
+                 "gemm": "q8_gemm_tc_kernel (tcgen05 kind::i8)"}
     # The prefill GEMM on its own (gate|up shape, 512 tokens: one range), timed
     # with events over a captured graph of launches: algorithmic int8 ops
     # 2*M*N*K against the dense int8 peak measured in this run (cuBLASLt int8
@@ -454,6 +554,8 @@ def main():
         "prefill_gemm_roofline_per_block_scales": gemm_roofline3,
         "clocks": clk,
     }
+    if rank == 0 and world == 1 and not args.no_other_configs:
+        line["other_configs"] = other_configs(torch, seed, peak)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(seed, args.prompt)
     sess.close()

@@ -359,6 +359,60 @@ int iris_sequence_check_select(IrisModel* model, const int32_t* rows, uint32_t n
 int iris_mistral_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows_in, uint32_t m,
                              uint32_t start, const int32_t* prior_k, const int32_t* prior_v,
                              int32_t* rows_out, int32_t* own_k, int32_t* own_v);
+/* gemma-dense: the per-layer inputs of token ids (direct/src/view_kernels.rs:
+ * 59-99, prefill_prepare_aux: embedding row, model projection, norm, scales
+ * and the PLE embedding): out[i*layers*ple + l*ple ..] is layer l's PLE row
+ * of ids[i]. Single-GPU models. */
+int iris_model_ple_rows(IrisModel* model, const uint32_t* ids, uint32_t n, int32_t* out);
+/* gemma-dense: one layer over one range of m rows starting at position start
+ * (kernels/src/prefill_range.rs:82-172, run_prefill_range_direct_with_weight_
+ * cache; the layer prefill_range.rs:307-957). ple_rows: the range's PLE rows
+ * of this layer ([m][ple], from iris_model_ple_rows). A layer with its own
+ * K/V takes the keys carried from the ranges before (n_prior rows at
+ * consecutive positions prior_pos[0].., kv_heads*head_dim values each) and
+ * must be given every position its window still holds before the range,
+ * [max(0, start + 1 - window), start) (window 0: [0, start)), ending at
+ * start - 1; a layer that shares a donor's K/V (kv_donor_layer >= 0) takes
+ * the donor layer's keys for this range instead (n_donor rows at consecutive
+ * positions covering [max(0, start + 1 - window), start + m)). Keys that do
+ * not cover those positions are refused with IRIS_EWINDOW before anything
+ * runs: the reference's cache-coverage fault (prefill-range/src/lib.rs:
+ * 1237-1288), which it reports as empty rows with the carried K/V handed
+ * on. Writes m output rows and the range's own K/V (sharing layers compute
+ * theirs too). The keys this range hands to the next one are the carried
+ * keys from position max(0, start + 1 - window) on, then its own
+ * (prefill_range.rs:849-860, output_kv); the caller assembles them. */
+int iris_gemma_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows_in, uint32_t m,
+                           uint32_t start, const int32_t* ple_rows, uint32_t n_prior, const uint32_t* prior_pos,
+                           const int32_t* prior_k, const int32_t* prior_v, uint32_t n_donor,
+                           const uint32_t* donor_pos, const int32_t* donor_k, const int32_t* donor_v,
+                           int32_t* rows_out, int32_t* own_k, int32_t* own_v);
+
+/* The claim's teacher-forced pass range by range on a session (device-
+ * resident: the session's cache carries every layer's K/V from range to
+ * range; kernels/src/mistral/stage.rs:172-226, prefill_range.rs:82-172 per
+ * stage, chain_runner.rs:503-597 for the order). A range of n <= 512 rows at
+ * positions [length, length + n): iris_session_range_begin embeds the ids
+ * (gemma: also every layer's PLE rows); iris_session_range_layer runs layer
+ * `layer` (0, 1, ... in order) and queues asynchronous copies of the
+ * stage's output rows ([n][hidden]) and own K/V ([n][kv_heads*head_dim]
+ * each) into the host buffers given (NULL skips one; pinned memory from
+ * iris_host_alloc keeps the copies asynchronous), and returns a ticket that
+ * iris_session_ticket_wait waits for (the buffers may be read, or reused,
+ * after that; a session tracks the last 64 tickets); iris_session_range_end,
+ * after the last layer, runs the head check over the range's final rows
+ * (rms_norm(final), the head, softcap, first maximum per row,
+ * sequence_check.rs:232-300) into token_ids / values (NULL skips it), waits
+ * for the range and advances the session's length by n. Single-GPU models;
+ * IRIS_ESTATE when called out of order. */
+int iris_session_range_begin(IrisSession* session, const uint32_t* ids, uint32_t n);
+int iris_session_range_layer(IrisSession* session, uint32_t layer, int32_t* rows_out, int32_t* own_k,
+                             int32_t* own_v, uint32_t* ticket);
+int iris_session_ticket_wait(IrisSession* session, uint32_t ticket);
+int iris_session_range_end(IrisSession* session, uint32_t* token_ids, int32_t* values);
+/* Page-locked host memory for the copies above (cudaHostAlloc). */
+int iris_host_alloc(uint64_t bytes, void** out);
+void iris_host_free(void* ptr);
 
 /* ---------------------------------------------------------------------------
  * 5. Seeded synthetic weights (the benchmark configs' inputs). Host copies of

@@ -121,6 +121,16 @@ SIGNATURES = {
     "iris_graph_free": (None, [vp]),
     "iris_mistral_layer_range": (C.c_int, [vp, C.c_uint32, i32p, C.c_uint32, C.c_uint32, i32p, i32p,
                                            i32p, i32p, i32p]),
+    "iris_model_ple_rows": (C.c_int, [vp, C.POINTER(C.c_uint32), C.c_uint32, i32p]),
+    "iris_gemma_layer_range": (C.c_int, [vp, C.c_uint32, i32p, C.c_uint32, C.c_uint32, i32p,
+                                         C.c_uint32, C.POINTER(C.c_uint32), i32p, i32p,
+                                         C.c_uint32, C.POINTER(C.c_uint32), i32p, i32p, i32p, i32p, i32p]),
+    "iris_session_range_begin": (C.c_int, [vp, C.POINTER(C.c_uint32), C.c_uint32]),
+    "iris_session_range_layer": (C.c_int, [vp, C.c_uint32, vp, vp, vp, C.POINTER(C.c_uint32)]),
+    "iris_session_ticket_wait": (C.c_int, [vp, C.c_uint32]),
+    "iris_session_range_end": (C.c_int, [vp, C.POINTER(C.c_uint32), i32p]),
+    "iris_host_alloc": (C.c_int, [C.c_uint64, C.POINTER(vp)]),
+    "iris_host_free": (None, [vp]),
     "iris_synth_q8": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint32, C.c_uint32, C.c_int, u8p]),
     "iris_synth_values": (C.c_int, [C.c_uint64, C.c_uint32, C.c_int32, C.c_uint64, C.c_uint32, i32p]),
     "iris_error": (C.c_char_p, [C.c_int]),

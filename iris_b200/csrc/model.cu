@@ -105,6 +105,8 @@ cudaError_t dalloc(T** p, size_t count) {
 
 }  // namespace
 
+constexpr uint32_t kChainTickets = 64;  // copies of chain stages a session tracks at once
+
 struct IrisModel {
   int family = 0;
   uint32_t L = 0, H = 0, F = 0, heads = 0, kvh = 0, d = 0, V = 0, P = 0, max_positions = 0;
@@ -182,6 +184,11 @@ struct IrisSession {
   bool use_step = false;
   cudaStream_t stream = nullptr;
   cudaGraphExec_t graph = nullptr;
+  // device-resident chain ranges (iris_session_range_*): rows of the range in
+  // progress (0: none), the next layer to run, and the events behind tickets
+  uint32_t range_n = 0, range_layer = 0;
+  cudaEvent_t tickets[kChainTickets] = {};
+  std::atomic<uint32_t> next_ticket{0};  // read by threads waiting for tickets
 };
 
 namespace {
@@ -197,6 +204,8 @@ void free_session(IrisSession* s) {
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
                   s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
   for (void* p : ptrs) cudaFree(p);
+  for (cudaEvent_t ev : s->tickets)
+    if (ev) cudaEventDestroy(ev);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
 }
@@ -605,9 +614,12 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   return row_parallel_resid(s, dn, tokens);
 }
 
-// One gemma-dense layer (prefill_range.rs:307-333, 497-741, 879-957).
+// One gemma-dense layer (prefill_range.rs:307-333, 497-741, 879-957). A
+// layer that shares its donor's K/V attends over the donor's cache; with
+// keep_own_kv its own (unused) keys and values are still stored in its own
+// cache rows (the chain stage hands them on, prefill_range.rs:542-575).
 cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint32_t* pos_ptr,
-                        uint32_t pos0) {
+                        uint32_t pos0, bool keep_own_kv = false) {
   IrisModel* m = s->m;
   const LayerDev& L = m->layers[l];
   cudaStream_t st = s->stream;
@@ -629,7 +641,7 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   QkvFinishArgs f{};
   f.qkv = s->qkv;
   f.q_out = s->q;
-  bool own = L.kv_donor < 0;  // a sharing layer attends over its donor's cache
+  bool own = L.kv_donor < 0 || keep_own_kv;  // a sharing layer attends over its donor's cache
   f.kcache = own ? s->kc + kv_offset(s, l) : nullptr;
   f.vcache = own ? s->vc + kv_offset(s, l) : nullptr;
   f.q_norm = L.q_norm;
@@ -1224,6 +1236,7 @@ int iris_session_reset(IrisSession* s) {
   if (!s) return IRIS_EINVAL;
   s->len = 0;
   s->has_logits = false;
+  s->range_n = 0;
   cudaError_t e = cudaMemsetAsync(s->d_pos, 0, 4, s->stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(s->d_step, 0, 4, s->stream);
   if (e == cudaSuccess) e = launch_fill_u64(s->best, kMaxRows, s->stream);
@@ -1234,6 +1247,113 @@ int iris_session_reset(IrisSession* s) {
 int iris_session_prefill(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits, uint32_t* token) {
   if (!s || !ids) return IRIS_EINVAL;
   return prefill_ids(s, ids, n, logits, token);
+}
+
+// ---- the chain's ranges, device-resident ---------------------------------
+
+int iris_session_range_begin(IrisSession* s, const uint32_t* ids, uint32_t n) {
+  if (!s || !ids || n == 0 || n > kMaxRows || s->range_n || s->m->tp_world > 1) return IRIS_EINVAL;
+  IrisModel* m = s->m;
+  if ((uint64_t)s->len + n > s->cap || (uint64_t)s->len + n > m->max_positions) return IRIS_ERANGE;
+  for (uint32_t i = 0; i < n; ++i)
+    if (ids[i] >= m->Vfull) return IRIS_EINVAL;
+  cudaError_t e = cudaMemcpyAsync(s->d_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream);
+  const bool gemma = m->family == kFamilyGemma;
+  if (e == cudaSuccess) e = launch_embed(m->embed, s->d_ids, n, gemma, m->embedding_scale, s->x, s->stream);
+  if (gemma && e == cudaSuccess) {  // view_kernels.rs:59-99, every layer's PLE row of the range
+    e = launch_dense(m->ple_model_proj, m->L * m->P, m->H, s->x, m->H, n, s->ple_proj, m->L * m->P, nullptr, 0,
+                     s->stream);
+    if (e == cudaSuccess)
+      e = launch_ple_prepare(s->ple_proj, m->ple_embed, s->d_ids, m->ple_norm, m->eps, m->ple_projection_scalar,
+                             m->ple_embedding_scale, m->ple_input_scale, n, m->L, m->P, s->ple_rows, s->stream);
+  }
+  if (e != cudaSuccess) return (int)e;
+  s->range_n = n;
+  s->range_layer = 0;
+  return 0;
+}
+
+int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, int32_t* own_k, int32_t* own_v,
+                             uint32_t* ticket) {
+  if (!s || !s->range_n || layer != s->range_layer) return s ? IRIS_ESTATE : IRIS_EINVAL;
+  IrisModel* m = s->m;
+  const uint32_t n = s->range_n, start = s->len;
+  cudaError_t e = m->family == kFamilyGemma ? gemma_layer(s, layer, n, nullptr, start, true)
+                                            : mistral_layer(s, layer, n, nullptr, start);
+  const size_t kvd = m->kvd;
+  if (e == cudaSuccess && rows_out)
+    e = cudaMemcpyAsync(rows_out, s->x, (size_t)n * m->H * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && own_k)
+    e = cudaMemcpyAsync(own_k, s->kc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
+                        cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && own_v)
+    e = cudaMemcpyAsync(own_v, s->vc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
+                        cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && ticket) {
+    const uint32_t t = s->next_ticket.load();
+    cudaEvent_t& ev = s->tickets[t % kChainTickets];
+    if (!ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(ev, s->stream);
+    if (e == cudaSuccess) s->next_ticket.store(t + 1);  // published after the event is recorded
+    *ticket = t;
+  }
+  if (e != cudaSuccess) return (int)e;
+  s->range_layer = layer + 1;
+  return 0;
+}
+
+int iris_session_ticket_wait(IrisSession* s, uint32_t ticket) {
+  if (!s) return IRIS_EINVAL;
+  const uint32_t issued = s->next_ticket.load();
+  if (ticket >= issued || issued - ticket > kChainTickets) return IRIS_EINVAL;
+  cudaEvent_t ev = s->tickets[ticket % kChainTickets];
+  return ev ? (int)cudaEventSynchronize(ev) : IRIS_EINVAL;
+}
+
+int iris_session_range_end(IrisSession* s, uint32_t* token_ids, int32_t* values) {
+  if (!s) return IRIS_EINVAL;
+  IrisModel* m = s->m;
+  if (!s->range_n || s->range_layer != m->L) return IRIS_ESTATE;
+  const uint32_t n = s->range_n;
+  cudaStream_t st = s->stream;
+  cudaError_t e = cudaSuccess;
+  std::vector<unsigned long long> keys(n);
+  if (token_ids) {  // rms_norm(final), the head, softcap, first maximum per row (sequence_check.rs:232-300)
+    e = launch_planes(s->x, m->final_norm, m->eps, n, m->H, s->planes, st);
+    if (e == cudaSuccess) e = launch_fill_u64(s->best, n, st);
+    if (e == cudaSuccess) {
+      ProductArgs h = session_product_args(s, m->head, n);
+      h.planes = s->planes;
+      h.out = nullptr;
+      h.best = s->best;
+      h.softcap = m->softcap;
+      e = launch_product(h, IN_PLANES, EPI_LOGITS, st);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(keys.data(), s->best, (size_t)n * 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = launch_fill_u64(s->best, n, st);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return (int)e;
+  int rc = check_fault();
+  if (rc) return rc;
+  for (uint32_t i = 0; token_ids && i < n; ++i) {
+    token_ids[i] = best_key_token(keys[i]);
+    if (values) values[i] = best_key_value(keys[i]);
+  }
+  s->len += n;
+  s->range_n = 0;
+  s->has_logits = false;  // a decode pass needs a prefill's state
+  return 0;
+}
+
+int iris_host_alloc(uint64_t bytes, void** out) {
+  if (!out) return IRIS_EINVAL;
+  *out = nullptr;
+  return (int)cudaHostAlloc(out, bytes ? bytes : 1, cudaHostAllocDefault);
+}
+
+void iris_host_free(void* p) {
+  if (p) cudaFreeHost(p);
 }
 
 int iris_session_decode(IrisSession* s, uint32_t token_in, int32_t* logits, uint32_t* token_out) {
@@ -1556,6 +1676,116 @@ int iris_model_embed(IrisModel* m, const uint32_t* ids, uint32_t n, int32_t* row
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(rows + (size_t)r0 * m->H, s->x, (size_t)cnt * m->H * 4, cudaMemcpyDeviceToHost, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  }
+  return (int)e;
+}
+
+int iris_model_ple_rows(IrisModel* m, const uint32_t* ids, uint32_t n, int32_t* out) {
+  if (!m || !ids || !out || m->family != kFamilyGemma || m->tp_world > 1) return IRIS_EINVAL;
+  if (n == 0) return 0;
+  for (uint32_t i = 0; i < n; ++i)
+    if (ids[i] >= m->Vfull) return IRIS_EINVAL;
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  if (!m->scratch) {
+    rc = create_session(m, 512, &m->scratch);
+    if (rc) return rc;
+  }
+  IrisSession* s = m->scratch;
+  const size_t LP = (size_t)m->L * m->P;
+  cudaError_t e = cudaSuccess;
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    const uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->d_ids, ids + r0, (size_t)cnt * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = launch_embed(m->embed, s->d_ids, cnt, true, m->embedding_scale, s->x, s->stream);
+    if (e == cudaSuccess)
+      e = launch_dense(m->ple_model_proj, m->L * m->P, m->H, s->x, m->H, cnt, s->ple_proj, m->L * m->P, nullptr, 0,
+                       s->stream);
+    if (e == cudaSuccess)
+      e = launch_ple_prepare(s->ple_proj, m->ple_embed, s->d_ids, m->ple_norm, m->eps, m->ple_projection_scalar,
+                             m->ple_embedding_scale, m->ple_input_scale, cnt, m->L, m->P, s->ple_rows, s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out + (size_t)r0 * LP, s->ple_rows, (size_t)cnt * LP * 4, cudaMemcpyDeviceToHost, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  }
+  return (int)e;
+}
+
+namespace {
+// Keys given as (count, positions): consecutive positions (each one more than
+// the one before) that cover [lo, hi). Empty coverage (lo == hi) needs no keys.
+bool keys_cover(uint32_t count, const uint32_t* pos, uint32_t lo, uint32_t hi) {
+  if (lo >= hi) return true;
+  if (count == 0 || !pos) return false;
+  for (uint32_t i = 1; i < count; ++i)
+    if (pos[i] != pos[i - 1] + 1) return false;
+  return pos[0] <= lo && (uint64_t)pos[0] + count >= hi;
+}
+}  // namespace
+
+int iris_gemma_layer_range(IrisModel* m, uint32_t layer, const int32_t* rows_in, uint32_t n, uint32_t start,
+                           const int32_t* ple_rows, uint32_t n_prior, const uint32_t* prior_pos,
+                           const int32_t* prior_k, const int32_t* prior_v, uint32_t n_donor,
+                           const uint32_t* donor_pos, const int32_t* donor_k, const int32_t* donor_v,
+                           int32_t* rows_out, int32_t* own_k, int32_t* own_v) {
+  if (!m || m->family != kFamilyGemma || layer >= m->L || m->tp_world > 1) return IRIS_EINVAL;
+  if (n == 0) return 0;  // prefill_range.rs:141-155: a range with no rows produces nothing
+  if (!rows_in || !rows_out || !ple_rows) return IRIS_EINVAL;
+  if ((uint64_t)start + n > 0xFFFFFFFFull) return IRIS_ERANGE;
+  const LayerDev& L = m->layers[layer];
+  // the positions the first query sees before itself, and those the last sees
+  const uint32_t w = L.window;
+  const uint32_t first_vis = w == 0 ? 0 : (start + 1 > w ? start + 1 - w : 0);
+  const bool shares = L.kv_donor >= 0;
+  if (!shares) {
+    if (n_prior && (!prior_k || !prior_v)) return IRIS_EINVAL;
+    if (!keys_cover(n_prior, prior_pos, first_vis, start)) return IRIS_EWINDOW;
+    if (n_prior && prior_pos[n_prior - 1] + 1 != start) return IRIS_EWINDOW;  // nothing at or past the range
+  } else {
+    if (n_donor && (!donor_k || !donor_v)) return IRIS_EINVAL;
+    if (!keys_cover(n_donor, donor_pos, first_vis, start + n)) return IRIS_EWINDOW;
+  }
+  int rc = check_model_ready(m);
+  if (rc) return rc;
+  const uint32_t cap_needed = std::max(start + n, shares && n_donor ? donor_pos[0] + n_donor : 0u);
+  if (!m->scratch || m->scratch->cap < cap_needed) {
+    free_session(m->scratch);
+    m->scratch = nullptr;
+    rc = create_session(m, std::max<uint32_t>(cap_needed, 512), &m->scratch);
+    if (rc) return rc;
+  }
+  IrisSession* s = m->scratch;
+  const size_t kvd = m->kvd, H = m->H, P = m->P, LP = (size_t)m->L * m->P;
+  cudaError_t e = cudaSuccess;
+  // the keys the layer attends over, at their positions in the cache
+  const uint32_t src_layer = shares ? (uint32_t)L.kv_donor : layer;
+  const uint32_t nk = shares ? n_donor : n_prior;
+  if (nk) {
+    const uint32_t p0 = shares ? donor_pos[0] : prior_pos[0];
+    int32_t* kc = s->kc + kv_offset(s, src_layer) + (size_t)p0 * kvd;
+    int32_t* vc = s->vc + kv_offset(s, src_layer) + (size_t)p0 * kvd;
+    e = cudaMemcpyAsync(kc, shares ? donor_k : prior_k, (size_t)nk * kvd * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(vc, shares ? donor_v : prior_v, (size_t)nk * kvd * 4, cudaMemcpyHostToDevice, s->stream);
+  }
+  for (uint32_t r0 = 0; r0 < n && e == cudaSuccess; r0 += kMaxRows) {
+    const uint32_t cnt = std::min(kMaxRows, n - r0);
+    e = cudaMemcpyAsync(s->x, rows_in + (size_t)r0 * H, (size_t)cnt * H * 4, cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(s->ple_rows + (size_t)layer * P, LP * 4, ple_rows + (size_t)r0 * P, P * 4, P * 4, cnt,
+                            cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = gemma_layer(s, layer, cnt, nullptr, start + r0, true);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(rows_out + (size_t)r0 * H, s->x, (size_t)cnt * H * 4, cudaMemcpyDeviceToHost, s->stream);
+  }
+  int32_t* kc = s->kc + kv_offset(s, layer) + (size_t)start * kvd;
+  int32_t* vc = s->vc + kv_offset(s, layer) + (size_t)start * kvd;
+  if (e == cudaSuccess && own_k) e = cudaMemcpyAsync(own_k, kc, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess && own_v) e = cudaMemcpyAsync(own_v, vc, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e == cudaSuccess) {
+    rc = check_fault();
+    if (rc) return rc;
   }
   return (int)e;
 }

@@ -209,6 +209,9 @@ def product(args):
             "us_per_launch": us, "bytes_per_launch": nbytes, "GB_s": nbytes / us / 1e3}
 
 
+kTcWarmTokens = 64  # a many-token product: builds a matrix's tensor-core copy
+
+
 def sweep(args):
     """Q8 sweep: one JSON line a (M, N, K). `device_us`: this library's
     product on device buffers (GEMV for M = 1, tiled GEMM otherwise);
@@ -228,12 +231,19 @@ def sweep(args):
     for n, k in [(2048, 2048), (16384, 2048), (4096, 4096), (14336, 4096)]:
         nb = n * k // 32
         bits = (rng.integers(0, 64, size=nb) + 0x2400).astype(np.int64)  # finite positive scales
+        if args.scales == "row":  # one scale an output row, in every block of the row
+            bits = np.repeat(bits[:: k // 32], k // 32)
         ex, man = (bits >> 10) & 0x1F, bits & 0x3FF
         scales = ((1024 + man) << np.maximum(ex - 1, 0)).astype(np.int64)
         weights = rng.integers(-127, 128, size=n * k).astype(np.int8)
         h = C.c_void_p()
         _lib.check(L.q8gpu_upload(weights.ctypes.data_as(C.POINTER(C.c_int8)), _lib.ptr(scales, C.c_int64), n, k,
                                   C.byref(h)), "upload")
+        # the tensor-core copy is built once per matrix, outside the timed calls
+        warm = torch.zeros((kTcWarmTokens, k), dtype=torch.int32, device="cuda")
+        wout = torch.empty((kTcWarmTokens, n), dtype=torch.int32, device="cuda")
+        _lib.check(L.iris_q8_product_device(h, warm.data_ptr(), kTcWarmTokens, wout.data_ptr(), None), "warm")
+        del warm, wout
         hr = C.c_void_p()
         if ref is not None:
             assert ref.q8gpu_upload(weights.ctypes.data_as(C.POINTER(C.c_int8)),
@@ -274,7 +284,7 @@ def sweep(args):
                 return (time.perf_counter() - t0) / reps * 1e6
             mine_host = host_time(L, h)
             mine_vals = host_out.copy()
-            line = {"m": m, "n": n, "k": k, "device_us": dev, "host_us": mine_host,
+            line = {"m": m, "n": n, "k": k, "scales": args.scales, "device_us": dev, "host_us": mine_host,
                     "bytes": n * k * 34 // 32 + 4 * m * k + 4 * m * n, "ops": 2 * m * n * k}
             line["GB_s"] = line["bytes"] / dev / 1e3
             line["TOPS"] = line["ops"] / dev / 1e6
@@ -350,6 +360,8 @@ def main():
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
     p.add_argument("--tokens", type=int, default=256)
+    p.add_argument("--scales", choices=["block", "row"], default="block",
+                   help="sweep: random scales per block (as GGUF) or one scale a row (BASELINE's weights)")
     p.add_argument("--gemm", choices=["tc", "tc3", "mma"], default="tc", help="gemm: the tcgen05 or the mma.sync GEMM")
     p.add_argument("--copies", type=int, default=1)
     p.add_argument("--context", type=int, default=2560)

@@ -18,6 +18,7 @@ from ._lib import T, check, lib, ptr
 from .shapes import GemmaConfig, MistralConfig
 
 Key = Tuple[str, int]  # (tensor name, layer or -1)
+KeyRows = Tuple[np.ndarray, np.ndarray, np.ndarray]  # (positions, k rows, v rows)
 
 
 def tensor_table(cfg) -> Dict[Key, tuple]:
@@ -56,17 +57,35 @@ def tensor_table(cfg) -> Dict[Key, tuple]:
 def synth_host_weights(cfg, seed: int, per_block: bool = False,
                        only: Optional[Iterable[Key]] = None) -> Dict[Key, np.ndarray]:
     """The seeded synthetic tensors, generated on the host by the same code the
-    device runs in `DeviceModel.synthesize` (iris_b200/csrc/synth.cuh)."""
+    device runs in `DeviceModel.synthesize` (iris_b200/csrc/synth.cuh); Q8_0
+    tensors in row chunks on a thread pool (the C calls run without the GIL)."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
     out = {}
     table = tensor_table(cfg)
     keys = list(only) if only is not None else list(table)
+    jobs = []
     for key in keys:
         kind, rows, cols, fan = table[key]
         name, layer = key
         if kind == "q8":
-            out[key] = _lib.synth_q8(seed, T[name], layer, rows, cols, per_block)
+            buf = np.empty(rows * (cols // 32) * 34, np.uint8)
+            out[key] = buf
+            step = max(1, (1 << 22) // cols)  # ~4 MB of weights a job
+            for r0 in range(0, rows, step):
+                n = min(step, rows - r0)
+                view = buf[r0 * (cols // 32) * 34:(r0 + n) * (cols // 32) * 34]
+                jobs.append((T[name], layer, n, cols, r0, view))
         else:
             out[key] = _lib.synth_values(seed, T[name], layer, rows * cols, fan)
+
+    def run(job):
+        tensor, layer, n, cols, r0, view = job
+        check(lib().iris_synth_q8_block(seed, tensor, layer, n, cols, r0, 0, cols, int(per_block),
+                                        ptr(view, C.c_uint8)), "iris_synth_q8_block")
+
+    with ThreadPoolExecutor(max_workers=min(32, os.cpu_count() or 1)) as pool:
+        list(pool.map(run, jobs))
     return out
 
 
@@ -217,6 +236,42 @@ class DeviceModel:
                                              ptr(pv, C.c_int32) if start else None,
                                              ptr(out, C.c_int32), ptr(ok, C.c_int32), ptr(ov, C.c_int32)),
               "iris_mistral_layer_range")
+        return out, ok, ov
+
+    def ple_rows(self, ids: Sequence[int]) -> np.ndarray:
+        """gemma-dense: the PLE rows [n][layers][ple] of token ids (view_kernels.rs:59-99)."""
+        a = np.ascontiguousarray(ids, np.uint32)
+        out = np.empty((a.size, self.cfg.layers, self.cfg.ple_width), np.int32)
+        check(lib().iris_model_ple_rows(self._h, ptr(a, C.c_uint32), a.size, ptr(out, C.c_int32)),
+              "iris_model_ple_rows")
+        return out
+
+    def gemma_layer_range(self, layer: int, rows: np.ndarray, start: int, ple_rows: np.ndarray,
+                          prior: Optional[KeyRows] = None, donor: Optional[KeyRows] = None):
+        """One gemma-dense layer over a range (prefill_range.rs:82-172):
+        returns (rows_out, own_k, own_v). `prior`: the layer's carried keys
+        (positions, k, v); `donor`: the donor layer's keys for a layer that
+        shares them."""
+        rows = np.ascontiguousarray(rows, np.int32)
+        m = rows.shape[0]
+        kvd = self.cfg.kv_heads * self.cfg.head_dim
+        ple = np.ascontiguousarray(ple_rows, np.int32)
+        out = np.empty_like(rows)
+        ok = np.empty((m, kvd), np.int32)
+        ov = np.empty((m, kvd), np.int32)
+        args, keep = [], []  # keep: the arrays behind the pointers, alive until the call returns
+        for keys in (prior, donor):
+            if keys is None or len(keys[0]) == 0:
+                args += [0, None, None, None]
+            else:
+                pos = np.ascontiguousarray(keys[0], np.uint32)
+                k = np.ascontiguousarray(keys[1], np.int32)
+                v = np.ascontiguousarray(keys[2], np.int32)
+                keep += [pos, k, v]
+                args += [pos.size, ptr(pos, C.c_uint32), ptr(k, C.c_int32), ptr(v, C.c_int32)]
+        check(lib().iris_gemma_layer_range(self._h, layer, ptr(rows, C.c_int32), m, start, ptr(ple, C.c_int32),
+                                           *args, ptr(out, C.c_int32), ptr(ok, C.c_int32), ptr(ov, C.c_int32)),
+              "iris_gemma_layer_range")
         return out, ok, ov
 
     def close(self) -> None:

@@ -17,8 +17,12 @@ Record layout (all integers little-endian):
     rows x kv_width int32 (K), then the same for V
 
 `chain_records` runs a claim's teacher-forced pass stage by stage on the
-device (`iris_mistral_layer_range` per range and layer, K/V carried across
-ranges, mistral/stage.rs:172-226) and returns each stage's record digest.
+device and returns each stage's record digest: mistral-dense through
+`iris_mistral_layer_range` per range and layer, K/V carried across ranges
+(mistral/stage.rs:172-226); gemma-dense through `iris_gemma_layer_range`,
+with the range's PLE rows, the carried K/V pruned to each layer's window as
+the reference hands it on (prefill_range.rs:82-172, 849-860) and a sharing
+layer attending over its donor's keys of the same range.
 """
 from __future__ import annotations
 
@@ -51,13 +55,51 @@ def stage_record(stage: str, start: int, rows: np.ndarray, k: Optional[np.ndarra
 
 
 def stage_digest(stage: str, start: int, rows: np.ndarray, k=None, v=None) -> str:
-    return hashlib.sha256(stage_record(stage, start, rows, k, v)).hexdigest()
+    """SHA-256 of the stage's record, fed piece by piece (no copy of the
+    arrays; hashlib runs without the GIL on large pieces)."""
+    rows = np.ascontiguousarray(rows, "<i4")
+    if rows.ndim != 2:
+        raise ValueError("rows must be [n][width]")
+    name = stage.encode()
+    h = hashlib.sha256(MAGIC + struct.pack("<I", len(name)) + name +
+                       struct.pack("<III", start, rows.shape[0], rows.shape[1]))
+    h.update(memoryview(rows).cast("B"))
+    if k is None:
+        h.update(struct.pack("<I", 0))
+    else:
+        k = np.ascontiguousarray(k, "<i4")
+        v = np.ascontiguousarray(v, "<i4")
+        if k.shape != v.shape or k.shape[0] != rows.shape[0]:
+            raise ValueError("K and V must hold one row per output row")
+        h.update(struct.pack("<I", k.shape[1]))
+        h.update(memoryview(k).cast("B"))
+        h.update(memoryview(v).cast("B"))
+    return h.hexdigest()
+
+
+def window_start(position: int, window: int) -> int:
+    """prefill_range.rs:866-874: the first position a query at `position` sees."""
+    return 0 if window == 0 else max(0, position + 1 - window)
+
+
+def output_kv(carried, own_k, own_v, start: int, window: int):
+    """prefill_range.rs:849-860: the keys a range hands on, (positions, k, v):
+    the carried keys the window still holds for the range's first position,
+    then the range's own."""
+    pos, k, v = carried
+    keep = pos >= window_start(start, window)
+    n = own_k.shape[0]
+    return (np.concatenate([pos[keep], np.arange(start, start + n, dtype=np.uint32)]),
+            np.concatenate([k[keep], own_k]), np.concatenate([v[keep], own_v]))
 
 
 def chain_records(model, ids: Sequence[int], range_size: int = 512) -> List[Tuple[str, int, str]]:
     """(stage, start_position, SHA-256 of its record) for every (range, layer)
-    stage of a mistral-dense claim whose prompt-and-output token ids are
-    `ids`, ranges of `range_size` rows."""
+    stage of a claim whose prompt-and-output token ids are `ids`, ranges of
+    `range_size` rows. `model` offers embed / layer_range (mistral-dense) or
+    embed / ple_rows / gemma_layer_range (gemma-dense)."""
+    if model.cfg.family == "gemma":
+        return _gemma_chain_records(model, ids, range_size)
     cfg = model.cfg
     kvd = cfg.kv_heads * cfg.head_dim
     carried_k = [np.zeros((0, kvd), np.int32) for _ in range(cfg.layers)]
@@ -72,3 +114,110 @@ def chain_records(model, ids: Sequence[int], range_size: int = 512) -> List[Tupl
             carried_k[layer] = np.concatenate([carried_k[layer], own_k])
             carried_v[layer] = np.concatenate([carried_v[layer], own_v])
     return out
+
+
+def _gemma_chain_records(model, ids, range_size):
+    cfg = model.cfg
+    kvd = cfg.kv_heads * cfg.head_dim
+    empty = (np.zeros(0, np.uint32), np.zeros((0, kvd), np.int32), np.zeros((0, kvd), np.int32))
+    carried = [empty] * cfg.layers
+    out = []
+    for start in range(0, len(ids), range_size):
+        part = ids[start:start + range_size]
+        rows = model.embed(part)
+        ple = model.ple_rows(part)
+        handed = []
+        for layer in range(cfg.layers):
+            donor = cfg.kv_donor(layer)
+            rows, own_k, own_v = model.gemma_layer_range(layer, rows, start, ple[:, layer],
+                                                         prior=carried[layer],
+                                                         donor=handed[donor] if donor >= 0 else None)
+            name = f"prefill_range/{layer}"
+            out.append((name, start, stage_digest(name, start, rows, own_k, own_v)))
+            handed.append(output_kv(carried[layer], own_k, own_v, start, cfg.window(layer)))
+        carried = handed
+    return out
+
+
+class _Pinned:
+    """A page-locked host array from iris_host_alloc."""
+
+    def __init__(self, shape):
+        import ctypes as C
+        from . import _lib
+        n = int(np.prod(shape))
+        self._p = C.c_void_p()
+        _lib.check(_lib.lib().iris_host_alloc(n * 4, C.byref(self._p)), "iris_host_alloc")
+        self.a = np.ctypeslib.as_array(C.cast(self._p, C.POINTER(C.c_int32)), shape=(n,)).reshape(shape)
+
+    @property
+    def ptr(self):
+        return self._p
+
+    def free(self):
+        from . import _lib
+        if self._p:
+            _lib.lib().iris_host_free(self._p)
+            self._p = None
+
+
+def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int = 8, workers: int = 8):
+    """A claim's teacher-forced pass range by range on a session, every stage's
+    record hashed while the device runs the next stages: each stage's rows
+    and own K/V are copied into one of `slots` page-locked buffer sets and a
+    worker thread waits for the copy (iris_session_ticket_wait), hashes the
+    record (the same digest as stage_digest) and frees the set. After each
+    range the head check selects a token for every row. Returns (records
+    [(stage, start, digest)], selected token ids, their scores)."""
+    import ctypes as C
+    from concurrent.futures import ThreadPoolExecutor
+    from . import _lib
+    L = _lib.lib()
+    model = session.model
+    cfg = model.cfg
+    if not 0 < range_size <= 512:
+        raise ValueError("ranges hold 1 to 512 rows")
+    kvd = cfg.kv_heads * cfg.head_dim
+    stage_name = "prefill_range" if cfg.family == "gemma" else "layer_mistral"
+    sets = [(_Pinned((range_size, cfg.hidden)), _Pinned((range_size, kvd)), _Pinned((range_size, kvd)))
+            for _ in range(slots)]
+    busy = [None] * slots
+    ids = np.ascontiguousarray(ids, np.uint32)
+    selected = np.empty(len(ids), np.uint32)
+    scores = np.empty(len(ids), np.int32)
+    jobs = []
+
+    def digest(slot, ticket, name, start, n):
+        _lib.check(L.iris_session_ticket_wait(session.handle, ticket), "iris_session_ticket_wait")
+        r, k, v = sets[slot]
+        return name, start, stage_digest(name, start, r.a[:n], k.a[:n], v.a[:n])
+
+    try:
+        with ThreadPoolExecutor(max_workers=workers) as pool:
+            j, base = 0, session.length
+            for start in range(base, base + len(ids), range_size):
+                off = start - base
+                part = ids[off:off + range_size]
+                n = len(part)
+                _lib.check(L.iris_session_range_begin(session.handle, _lib.ptr(part, C.c_uint32), n),
+                           "iris_session_range_begin")
+                for layer in range(cfg.layers):
+                    slot = j % slots
+                    if busy[slot] is not None:
+                        busy[slot].result()  # the set's previous record is hashed
+                    ticket = C.c_uint32()
+                    r, k, v = sets[slot]
+                    _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
+                                                          C.byref(ticket)), "iris_session_range_layer")
+                    busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
+                    jobs.append(busy[slot])
+                    j += 1
+                _lib.check(L.iris_session_range_end(session.handle, _lib.ptr(selected[off:off + n], C.c_uint32),
+                                                    _lib.ptr(scores[off:off + n], C.c_int32)),
+                           "iris_session_range_end")
+            records = [f.result() for f in jobs]
+    finally:
+        for trio in sets:
+            for b in trio:
+                b.free()
+    return records, selected, scores

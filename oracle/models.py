@@ -219,3 +219,86 @@ class OracleModel:
         if rc:
             raise RuntimeError(f"oracle_mistral_layer failed: {rc}")
         return out, ok, ov
+
+
+def _keys(keys):
+    """OracleKeys over (positions, k, v) arrays (kept alive by the caller)."""
+    if keys is None or len(keys[0]) == 0:
+        return O.Keys(0, None, None, None)
+    pos, k, v = keys
+    return O.Keys(len(pos), O.ptr(pos, C.c_uint32), O.ptr(k, C.c_int32), O.ptr(v, C.c_int32))
+
+
+def gemma_ple_rows(om, ids):
+    """PLE rows [n][layers][ple] of token ids (view_kernels.rs:59-99) from the
+    embedding rows times embedding_scale (model.rs:316-330)."""
+    c = om.cfg
+    emb = np.asarray(om.w[("EMBED", -1)]).reshape(c.vocab, -1)
+    out = np.empty((len(ids), c.layers, c.ple_width), np.int32)
+    row = np.empty(c.hidden, np.int32)
+    for i, t in enumerate(ids):
+        e = np.ascontiguousarray(emb[t])
+        if O.lib().oracle_dequantize_row(O.ptr(e, C.c_uint8), e.size, O.ptr(row, C.c_int32), c.hidden):
+            raise RuntimeError("dequantize_row failed")
+        seed = np.array([O.lib().oracle_mul_sat(int(x), c.embedding_scale) for x in row], np.int32)
+        for l in range(c.layers):
+            if O.lib().oracle_ple_prepare(C.byref(om.model.ple), c.layers, l, O.ptr(seed, C.c_int32), int(t),
+                                          O.ptr(out[i, l], C.c_int32)):
+                raise RuntimeError("oracle_ple_prepare failed")
+    return out
+
+
+def gemma_layer_range(om, l, rows, start, ple, prior=None, donor_a=None, donor_b=None, threads=None):
+    """One gemma-dense layer over a range (prefill_range.rs:307-333):
+    (rows_out, own_k, own_v). prior / donor_*: (positions uint32, k, v)."""
+    c = om.cfg
+    kvd = c.kv_heads * c.head_dim
+    rows = np.ascontiguousarray(rows, np.int32)
+    ple = np.ascontiguousarray(ple, np.int32)
+    m = rows.shape[0]
+    out = np.empty_like(rows)
+    ok = np.empty((m, kvd), np.int32)
+    ov = np.empty((m, kvd), np.int32)
+    keep = [tuple(np.ascontiguousarray(a, t) for a, t in zip(ks, (np.uint32, np.int32, np.int32)))
+            if ks is not None and len(ks[0]) else None for ks in (prior, donor_a, donor_b)]
+    rc = O.lib().oracle_gemma_layer(C.byref(om.model.gemma[l]), O.ptr(rows, C.c_int32), m, start,
+                                    _keys(keep[0]), _keys(keep[1]), _keys(keep[2]), O.ptr(ple, C.c_int32),
+                                    O.ptr(out, C.c_int32), O.ptr(ok, C.c_int32), O.ptr(ov, C.c_int32),
+                                    threads or O.threads_default())
+    if rc:
+        raise RuntimeError(f"oracle_gemma_layer failed: {rc}")
+    return out, ok, ov
+
+
+class OracleStages:
+    """The chain-stage calls of a device model (embed, layer_range,
+    ple_rows, gemma_layer_range) computed by the oracle, so that one driver
+    (iris_b200.records.chain_records) runs a claim stage by stage on either."""
+
+    def __init__(self, om, threads=None):
+        self.om, self.cfg, self.threads = om, om.cfg, threads
+
+    def embed(self, ids):
+        c = self.cfg
+        emb = np.asarray(self.om.w[("EMBED", -1)]).reshape(c.vocab, -1)
+        out = np.empty((len(ids), c.hidden), np.int32)
+        for i, t in enumerate(ids):
+            e = np.ascontiguousarray(emb[t])
+            if O.lib().oracle_dequantize_row(O.ptr(e, C.c_uint8), e.size, O.ptr(out[i], C.c_int32), c.hidden):
+                raise RuntimeError("dequantize_row failed")
+            if c.family == "gemma":  # model.rs:316-330
+                out[i] = [O.lib().oracle_mul_sat(int(x), c.embedding_scale) for x in out[i]]
+        return out
+
+    def layer_range(self, layer, rows, start, prior_k, prior_v):
+        return self.om.mistral_layer_range(layer, rows, start, prior_k, prior_v, self.threads)
+
+    def ple_rows(self, ids):
+        return gemma_ple_rows(self.om, ids)
+
+    def gemma_layer_range(self, layer, rows, start, ple, prior=None, donor=None):
+        da, db = self.cfg.donor_candidates()
+        d = self.cfg.kv_donor(layer)
+        return gemma_layer_range(self.om, layer, rows, start, ple, prior=prior,
+                                 donor_a=donor if d >= 0 and d == da else None,
+                                 donor_b=donor if d >= 0 and d == db else None, threads=self.threads)
