@@ -397,7 +397,8 @@ int iris_gemma_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows
  * `layer` (0, 1, ... in order) and queues asynchronous copies of the
  * stage's output rows ([n][hidden]) and own K/V ([n][kv_heads*head_dim]
  * each) into the host buffers given (NULL skips one; pinned memory from
- * iris_host_alloc keeps the copies asynchronous), and returns a ticket that
+ * iris_host_alloc keeps the copies asynchronous; they run on a copy stream
+ * of the session's, beside the next layers), and returns a ticket that
  * iris_session_ticket_wait waits for (the buffers may be read, or reused,
  * after that; a session tracks the last 64 tickets); iris_session_range_end,
  * after the last layer, runs the head check over the range's final rows

@@ -189,6 +189,13 @@ struct IrisSession {
   uint32_t range_n = 0, range_layer = 0;
   cudaEvent_t tickets[kChainTickets] = {};
   std::atomic<uint32_t> next_ticket{0};  // read by threads waiting for tickets
+  // the stages' copies run on their own stream: the rows go through one of
+  // two device staging buffers (the next layer overwrites x), K/V straight
+  // from the cache; staged: the compute stream's "rows staged" event,
+  // stage_read[b]: the copy stream finished reading buffer b
+  cudaStream_t copy_stream = nullptr;
+  int32_t* stage_rows[2] = {};
+  cudaEvent_t staged = nullptr, stage_read[2] = {};
 };
 
 namespace {
@@ -203,9 +210,14 @@ void free_session(IrisSession* s) {
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
                   s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
+  if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
   for (void* p : ptrs) cudaFree(p);
+  for (int32_t* p : s->stage_rows) cudaFree(p);
   for (cudaEvent_t ev : s->tickets)
     if (ev) cudaEventDestroy(ev);
+  for (cudaEvent_t ev : {s->staged, s->stage_read[0], s->stage_read[1]})
+    if (ev) cudaEventDestroy(ev);
+  if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
 }
@@ -1234,6 +1246,10 @@ int iris_session_create(IrisModel* m, uint32_t max_positions, IrisSession** out)
 
 int iris_session_reset(IrisSession* s) {
   if (!s) return IRIS_EINVAL;
+  if (s->copy_stream) {  // chain copies still reading the cache
+    cudaError_t e = cudaStreamSynchronize(s->copy_stream);
+    if (e != cudaSuccess) return (int)e;
+  }
   s->len = 0;
   s->has_logits = false;
   s->range_n = 0;
@@ -1257,7 +1273,19 @@ int iris_session_range_begin(IrisSession* s, const uint32_t* ids, uint32_t n) {
   if ((uint64_t)s->len + n > s->cap || (uint64_t)s->len + n > m->max_positions) return IRIS_ERANGE;
   for (uint32_t i = 0; i < n; ++i)
     if (ids[i] >= m->Vfull) return IRIS_EINVAL;
-  cudaError_t e = cudaMemcpyAsync(s->d_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream);
+  cudaError_t e = cudaSuccess;
+  if (!s->copy_stream) {  // the stages' copy stream, staging buffers and events, on first use
+    e = cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking);
+    for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+      e = dalloc(&s->stage_rows[b], (size_t)kMaxRows * m->H);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->stage_read[b], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&s->staged, cudaEventDisableTiming);
+    // both staging buffers start unread
+    for (int b = 0; b < 2 && e == cudaSuccess; ++b) e = cudaEventRecord(s->stage_read[b], s->copy_stream);
+    if (e != cudaSuccess) return (int)e;
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(s->d_ids, ids, (size_t)n * 4, cudaMemcpyHostToDevice, s->stream);
   const bool gemma = m->family == kFamilyGemma;
   if (e == cudaSuccess) e = launch_embed(m->embed, s->d_ids, n, gemma, m->embedding_scale, s->x, s->stream);
   if (gemma && e == cudaSuccess) {  // view_kernels.rs:59-99, every layer's PLE row of the range
@@ -1281,21 +1309,29 @@ int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, 
   cudaError_t e = m->family == kFamilyGemma ? gemma_layer(s, layer, n, nullptr, start, true)
                                             : mistral_layer(s, layer, n, nullptr, start);
   const size_t kvd = m->kvd;
+  // the stage's rows into staging buffer b once the copy stream has read it,
+  // then every copy to the host on the copy stream while the next layer runs
+  const uint32_t t = s->next_ticket.load(), b = t & 1;
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s->stream, s->stage_read[b], 0);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(s->stage_rows[b], s->x, (size_t)n * m->H * 4, cudaMemcpyDeviceToDevice, s->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(s->staged, s->stream);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(s->copy_stream, s->staged, 0);
   if (e == cudaSuccess && rows_out)
-    e = cudaMemcpyAsync(rows_out, s->x, (size_t)n * m->H * 4, cudaMemcpyDeviceToHost, s->stream);
+    e = cudaMemcpyAsync(rows_out, s->stage_rows[b], (size_t)n * m->H * 4, cudaMemcpyDeviceToHost, s->copy_stream);
   if (e == cudaSuccess && own_k)
     e = cudaMemcpyAsync(own_k, s->kc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
-                        cudaMemcpyDeviceToHost, s->stream);
+                        cudaMemcpyDeviceToHost, s->copy_stream);
   if (e == cudaSuccess && own_v)
     e = cudaMemcpyAsync(own_v, s->vc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
-                        cudaMemcpyDeviceToHost, s->stream);
-  if (e == cudaSuccess && ticket) {
-    const uint32_t t = s->next_ticket.load();
+                        cudaMemcpyDeviceToHost, s->copy_stream);
+  if (e == cudaSuccess) e = cudaEventRecord(s->stage_read[b], s->copy_stream);
+  if (e == cudaSuccess) {
     cudaEvent_t& ev = s->tickets[t % kChainTickets];
     if (!ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
-    if (e == cudaSuccess) e = cudaEventRecord(ev, s->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(ev, s->copy_stream);
     if (e == cudaSuccess) s->next_ticket.store(t + 1);  // published after the event is recorded
-    *ticket = t;
+    if (ticket) *ticket = t;
   }
   if (e != cudaSuccess) return (int)e;
   s->range_layer = layer + 1;

@@ -161,7 +161,8 @@ class _Pinned:
             self._p = None
 
 
-def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int = 8, workers: int = 8):
+def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int = 12,
+                workers: Optional[int] = None):
     """A claim's teacher-forced pass range by range on a session, every stage's
     record hashed while the device runs the next stages: each stage's rows
     and own K/V are copied into one of `slots` page-locked buffer sets and a
@@ -170,9 +171,11 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
     range the head check selects a token for every row. Returns (records
     [(stage, start, digest)], selected token ids, their scores)."""
     import ctypes as C
+    import os
     from concurrent.futures import ThreadPoolExecutor
     from . import _lib
     L = _lib.lib()
+    workers = workers or max(1, os.cpu_count() or 1)
     model = session.model
     cfg = model.cfg
     if not 0 < range_size <= 512:
