@@ -40,7 +40,7 @@ UNIT = "tok/s"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--steps", type=int, default=256)
     p.add_argument("--warmup", type=int, default=4)
     p.add_argument("--impl", default="iris", choices=["iris", "reference"])
     p.add_argument("--prompt", type=int, default=2048)
@@ -107,10 +107,17 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-i", str(index), "-lms", "100"], stdout=self.f,
+                                       "-i", str(index), "-lms", "50"], stdout=self.f,
                                       stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+        # nvidia-smi takes a moment to start: the timed region begins once it
+        # has written its first sample (at most ~10 s)
+        t0 = time.monotonic()
+        while self.p and self.p.poll() is None and time.monotonic() - t0 < 10:
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if not self.p:
@@ -382,10 +389,10 @@ def main():
     stream = torch.cuda.ExternalStream(sess.stream_ptr)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx0 = sess.length
+    clocks = Clocks(local)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local)
     ev0.record(stream)
     sess.decode_steps(args.steps)
     ev1.record(stream)
@@ -523,7 +530,7 @@ def main():
                  "frac": g["TOPS"] / int8_peak, "plane_mma_frac": planes_mmas * g["TOPS"] / int8_peak,
                  "us_per_launch": g["us_per_launch"], "shape": [512, 2 * cfg.ffn, cfg.hidden],
                  "kernel": "planes_kernel + " + g["kernel"].split("planes_kernel + ")[-1], "peak_kind": int8_kind,
-                 "traffic": profiled_traffic("q8_gemm_tc_gateup_28672x4096_512tok.md" if form == "tc"
+                 "traffic": profiled_traffic("q8_gemm_tc1_gateup_28672x4096_512tok.md" if form == "tc"
                                              else "q8_gemm_tc3_gateup_28672x4096_512tok.md")}
             if form == "tc":
                 gemm_roofline = r

@@ -142,6 +142,7 @@ typedef struct {
   const uint32_t* rope_freq_base_dim;
   const int32_t* kv_donor_layer;      /* -1 = own K/V */
   const int32_t* layer_scalar;        /* 0 = none */
+  uint32_t tied_head;                 /* head = embedding table (tie_word_embeddings) */
 } IrisGemmaShape;
 
 /* Tensor kinds for iris_model_set_q8 / iris_model_set_values. */

@@ -57,7 +57,8 @@ class GemmaShape(C.Structure):
                 ("ple_projection_scalar", C.c_int32), ("ple_input_scale", C.c_int32),
                 ("final_logit_softcap", C.c_int32),
                 ("sliding_window", u32p), ("rope_base", i64p), ("rotary_dim", u32p),
-                ("rope_freq_base_dim", u32p), ("kv_donor_layer", i32p), ("layer_scalar", i32p)]
+                ("rope_freq_base_dim", u32p), ("kv_donor_layer", i32p), ("layer_scalar", i32p),
+                ("tied_head", C.c_uint32)]
 
 
 # name -> (restype, argtypes); every symbol include/iris_b200.h declares.

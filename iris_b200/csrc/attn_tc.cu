@@ -9,7 +9,7 @@
 //      int8 MMAs (M = 128 keys, N = 64 queries, K = 32 of the 128 dims) into
 //      seven int32 diagonals, each exact (|sum| < 2^26 over 128 dims); the
 //      epilogue adds them modulo 2^64, as the reference's wrapping sum.
-//   2. softmax on CUDA cores, one block a (query, head): first maximum, exp
+//   2. softmax on CUDA cores, one warp a (query, head): first maximum, exp
 //      terms and their sum, weights by one exact reciprocal, the residual
 //      1.0 - sum(weights) on the first maximum's weight; the weights
 //      (0..65536) are written as three byte planes, zero past the query's
@@ -348,27 +348,28 @@ __device__ __forceinline__ uint64_t exp_term_lookup(int32_t score, int32_t mx) {
   return i ? (uint64_t)__ldg(g_exp_terms + i) : 0;
 }
 
-// One block a (query, head): the integer softmax of the query's scores
-// (positions 0..p) into three weight planes over the pcap positions; the exp
-// terms wait in shared memory (8 B a position) between their sum and the
-// weights.
-constexpr uint32_t kSoftThreads = 256;
-__global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t* __restrict__ s, uint8_t* wp,
-                                                                  uint32_t qcap, uint32_t pcap, uint32_t pos0,
-                                                                  uint32_t heads) {
+// A warp a (query, head), eight a block: the integer softmax of the query's
+// scores (positions 0..p) into three weight planes over the pcap positions,
+// in three passes over the row with warp shuffles only (no block barrier, no
+// shared memory): the first maximum, the exp terms' sum, then each term again
+// (from the table) into its weight (attention_softmax_into, ops.rs:233-261);
+// the residual 1.0 - sum of weights goes onto the first maximum (:274-276).
+// Four consecutive positions a lane (rows and planes are 16-byte aligned).
+constexpr uint32_t kSoftRowsPerBlock = 8;
+__global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel(const int32_t* __restrict__ s,
+                                                                                 uint8_t* wp, uint32_t qcap,
+                                                                                 uint32_t pcap, uint32_t pos0,
+                                                                                 uint32_t tokens, uint32_t heads) {
   pdl_wait();
   pdl_trigger();
-  extern __shared__ __align__(16) unsigned char soft_terms[];
-  __shared__ unsigned long long red_key[kSoftThreads / 32], red_sum[kSoftThreads / 32];
-  __shared__ int32_t red_w[kSoftThreads / 32];
-  __shared__ unsigned long long g_key, g_tot;
-  const uint32_t q = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t r = blockIdx.x * kSoftRowsPerBlock + (threadIdx.x >> 5);  // row = h * tokens + q
+  if (r >= tokens * heads) return;
+  const uint32_t h = r / tokens, q = r % tokens;
   const uint32_t n = pos0 + q + 1;
   const int32_t* row = s + ((size_t)h * qcap + q) * pcap;
-  // four consecutive positions a thread (rows and planes are 16-byte aligned:
-  // pcap is a multiple of 128)
   unsigned long long best = 0;
-  for (uint32_t t = 4 * tid; t < n; t += 4 * kSoftThreads) {
+  for (uint32_t t = 4 * lane; t < n; t += 128) {
     const int4 v = *(const int4*)(row + t);
     const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -382,55 +383,38 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
     const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
     best = o > best ? o : best;
   }
-  if (lane == 0) red_key[warp] = best;
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long b = 0;
-    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) b = red_key[w] > b ? red_key[w] : b;
-    g_key = b;
-  }
-  __syncthreads();
-  const int32_t mx = best_key_value(g_key);
-  const uint32_t tmax = best_key_token(g_key);
-  uint64_t* terms = (uint64_t*)soft_terms;  // [n rounded up to 4]: each exp term computed once
+  const int32_t mx = best_key_value(best);
+  const uint32_t tmax = best_key_token(best);
   uint64_t e = 0;
-  for (uint32_t t = 4 * tid; t < n; t += 4 * kSoftThreads) {
+  for (uint32_t t = 4 * lane; t < n; t += 128) {
     const int4 v = *(const int4*)(row + t);
     const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (uint32_t u = 0; u < 4; ++u) {
-      const uint64_t term = t + u < n ? exp_term_lookup(x[u], mx) : 0;
-      terms[t + u] = term;
-      e += term;
-    }
+    for (uint32_t u = 0; u < 4; ++u) e += t + u < n ? exp_term_lookup(x[u], mx) : 0;
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
-  if (lane == 0) red_sum[warp] = e;
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long tsum = 0;
-    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) tsum += red_sum[w];
-    g_tot = tsum;
-  }
-  __syncthreads();
-  const uint64_t tot = g_tot, inv = tot ? UINT64_MAX / tot : 0;
+  const uint64_t tot = e, inv = tot ? UINT64_MAX / tot : 0;
   uint8_t* w0 = wp + ((size_t)h * 3 * qcap + q) * pcap;
   uint8_t* w1 = w0 + (size_t)qcap * pcap;
   uint8_t* w2 = w1 + (size_t)qcap * pcap;
   int32_t wsl = 0;
-  for (uint32_t t = 4 * tid; t < pcap; t += 4 * kSoftThreads) {
+  for (uint32_t t = 4 * lane; t < pcap; t += 128) {
     uint32_t b0 = 0, b1 = 0, b2 = 0;
+    if (t < n) {
+      const int4 v = *(const int4*)(row + t);
+      const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (uint32_t u = 0; u < 4; ++u) {
-      int32_t w = 0;
-      if (t + u < n) {
-        w = tot ? softmax_weight_inv((int64_t)terms[t + u], tot, inv) : 0;
-        wsl += w;
+      for (uint32_t u = 0; u < 4; ++u) {
+        int32_t w = 0;
+        if (t + u < n) {
+          w = tot ? softmax_weight_inv((int64_t)exp_term_lookup(x[u], mx), tot, inv) : 0;
+          wsl += w;
+        }
+        b0 |= ((uint32_t)w & 0xFFu) << (8 * u);
+        b1 |= (((uint32_t)w >> 8) & 0xFFu) << (8 * u);
+        b2 |= (((uint32_t)w >> 16) & 0xFFu) << (8 * u);
       }
-      b0 |= ((uint32_t)w & 0xFFu) << (8 * u);
-      b1 |= (((uint32_t)w >> 8) & 0xFFu) << (8 * u);
-      b2 |= (((uint32_t)w >> 16) & 0xFFu) << (8 * u);
     }
     *(uint32_t*)(w0 + t) = b0;
     *(uint32_t*)(w1 + t) = b1;
@@ -438,20 +422,16 @@ __global__ void __launch_bounds__(kSoftThreads) at_softmax_kernel(const int32_t*
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) wsl += __shfl_xor_sync(0xffffffffu, wsl, off);
-  if (lane == 0) red_w[warp] = wsl;
-  __syncthreads();
-  if (tid == 0) {
-    int32_t ws = 0;
-    for (uint32_t w = 0; w < kSoftThreads / 32; ++w) ws += red_w[w];
-    // the residual on the first maximum's weight (ops.rs:274-276); no weight saturates
-    const int32_t wm = tot ? softmax_weight_inv((int64_t)terms[tmax], tot, inv) : 0;
-    const int32_t w = wm + sub_sat(kOneAct, ws);
+  __syncwarp();  // every lane's plane stores come before the first maximum's correction
+  if (lane == 0) {
+    const int32_t wm = tot ? softmax_weight_inv((int64_t)exp_term_lookup(mx, mx), tot, inv) : 0;
+    const int32_t w = wm + sub_sat(kOneAct, wsl);  // no weight saturates
     w0[tmax] = (uint8_t)w;
     w1[tmax] = (uint8_t)(w >> 8);
     w2[tmax] = (uint8_t)(w >> 16);
   }
-  (void)heads;
 }
+
 
 constexpr uint32_t score_smem() { return kAtStages * (4 * kAtAPlane + 4 * kAtBPlane) + 1024; }
 constexpr uint32_t value_smem() { return kAtStages * (4 * kAtAPlane + 3 * kAtBPlane) + 1024; }
@@ -523,8 +503,9 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
   e = launch_k(attn_tc_scores_kernel, dim3(std::min(sc_tiles, sms)), dim3(kAtThreads), score_smem(), stream, st, se,
                kmap, qmap, fault);
   if (e != cudaSuccess) return e;
-  e = launch_k(at_softmax_kernel, dim3(tokens, a.heads), dim3(kSoftThreads), (size_t)(last + 3) / 4 * 32, stream,
-               (const int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, a.heads);
+  e = launch_k(at_softmax_warp_kernel, dim3((tokens * a.heads + kSoftRowsPerBlock - 1) / kSoftRowsPerBlock),
+               dim3(32 * kSoftRowsPerBlock), 0, stream, (const int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, tokens,
+               a.heads);
   if (e != cudaSuccess) return e;
   ValueTilesS vt;
   vt.heads = a.heads, vt.group = group, vt.qtiles = qtiles, vt.kstages = pcap / kTcTileK;
@@ -559,9 +540,6 @@ cudaError_t prepare_attn_tc_kernels() {
   if (cudaError_t e = ensure_exp_table(); e != cudaSuccess) return e;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)score_smem());
-  if (e == cudaSuccess)  // the exp terms of up to kAtMaxPositions positions
-    e = cudaFuncSetAttribute(at_softmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)((kAtMaxPositions + 3) / 4 * 32));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_tc_values_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)value_smem());
   return e;

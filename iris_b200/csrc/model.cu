@@ -1080,7 +1080,7 @@ int iris_model_create_gemma(const IrisGemmaShape* sh, IrisModel** out) {
   m->qd = m->heads * m->d;
   m->kvd = m->kvh * m->d;
   m->eps = sh->norm_eps;
-  m->tied = true;  // direct/src/model.rs:577-597 (the Gemma configs tie the head)
+  m->tied = sh->tied_head != 0;  // direct/src/model.rs:577-597 (tie_word_embeddings)
   m->embedding_scale = sh->embedding_scale;
   m->ple_embedding_scale = sh->ple_embedding_scale;
   m->ple_projection_scalar = sh->ple_projection_scalar;

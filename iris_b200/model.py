@@ -26,7 +26,7 @@ def tensor_table(cfg) -> Dict[Key, tuple]:
     H, F, V, L = cfg.hidden, cfg.ffn, cfg.vocab, cfg.layers
     qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
     t: Dict[Key, tuple] = {("EMBED", -1): ("q8", V, H, 0), ("FINAL_NORM", -1): ("values", 1, H, 0)}
-    if cfg.family == "mistral" and not cfg.tied:
+    if not cfg.tied:
         t[("HEAD", -1)] = ("q8", V, H, 0)
     for l in range(L):
         t[("W_Q", l)] = ("q8", qd, H, 0)
@@ -129,7 +129,7 @@ class DeviceModel:
                                     cfg.ple_projection_scalar, cfg.ple_input_scale, cfg.softcap_bits,
                                     ptr(self._win, C.c_uint32), ptr(self._base, C.c_int64),
                                     ptr(self._rot, C.c_uint32), ptr(self._fbd, C.c_uint32),
-                                    ptr(self._donor, C.c_int32), ptr(self._scal, C.c_int32))
+                                    ptr(self._donor, C.c_int32), ptr(self._scal, C.c_int32), int(cfg.tied))
             check(L.iris_model_create_gemma(C.byref(shape), C.byref(self._h)), "iris_model_create_gemma")
         if weights is not None:
             self.load(weights)

@@ -133,6 +133,7 @@ class GemmaConfig:
     softcap: float = 0.0
     eps: float = 1e-6
     layer_scalars: Optional[List[int]] = None
+    tied: bool = True
     family: str = "gemma"
 
     def types(self) -> List[str]:

@@ -136,7 +136,7 @@ class OracleModel:
                 layers[l] = self.gemma_layer(l)
             m.gemma = layers
             m.head = O.Head(cfg.hidden, cfg.vocab, cfg.norm_eps, cfg.softcap_bits, self.i32("FINAL_NORM", -1),
-                            self.u8("EMBED", -1))
+                            self.u8(*(("EMBED", -1) if cfg.tied else ("HEAD", -1))))
             m.ple = O.Ple(cfg.hidden, cfg.ple_width, cfg.ple_embedding_scale, cfg.ple_projection_scalar,
                           cfg.ple_input_scale, cfg.norm_eps, self.i32("PLE_NORM", -1), self.u8("PLE_EMBED", -1),
                           self.i32("PLE_MODEL_PROJECTION", -1))

@@ -113,3 +113,82 @@ def test_reference_parity_bundle():
     assert weights[("W_GATE", 0)].size == 2048 * 128 // 32 * 34
     assert weights[("FINAL_NORM", -1)].dtype == np.int32
     f.close()
+
+
+# ---- gemma-dense ----------------------------------------------------------
+
+def _gemma_bundle():
+    from oracle.oracle import reference_root
+    root = reference_root()
+    return str(root / "model-bundles" / "parity-gemma") if root else ""
+
+
+GEMMA_BUNDLE = _gemma_bundle()
+
+
+def gemma_text_config(**over):
+    """A gemma-dense config.json text section of the parity shape: two
+    sliding and two full layers, the last two sharing K/V, a 16-key window,
+    PLE 32, partial rotary on the full layers, softcap, an untied head."""
+    text = {"hidden_size": 128, "intermediate_size": 512, "num_hidden_layers": 4, "num_attention_heads": 4,
+            "num_key_value_heads": 2, "head_dim": 32, "hidden_size_per_layer_input": 32, "vocab_size": 512,
+            "sliding_window": 16, "num_kv_shared_layers": 2, "rms_norm_eps": 1e-06, "tie_word_embeddings": False,
+            "final_logit_softcapping": 1.0,
+            "layer_types": ["sliding_attention", "full_attention", "sliding_attention", "full_attention"],
+            "rope_parameters": {"sliding_attention": {"rope_theta": 10000},
+                                "full_attention": {"rope_theta": 1000000, "partial_rotary_factor": 0.5}}}
+    text.update(over)
+    return text
+
+
+def test_gemma_config_import():
+    """gemma.rs:126-190: the shape, rotary split, K/V donors and head tying
+    derived from a config.json, and the refusals."""
+    from iris_b200 import detwgt
+    cfg = detwgt.gemma_config({"text_config": gemma_text_config()}, 512, [65536, 1 << 15, 0, 65536])
+    assert (cfg.layers, cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ple_width) == (4, 128, 4, 2, 32, 32)
+    assert cfg.tied is False and cfg.softcap == 1.0 and cfg.layer_scalars == [65536, 1 << 15, 0, 65536]
+    assert [cfg.kv_donor(l) for l in range(4)] == [-1, -1, 0, 1]
+    assert cfg.rope(0) == (10_000 << 32, 32, 32) and cfg.rope(1) == (1_000_000 << 32, 16, 32)
+    assert cfg.window(0) == 16 and cfg.window(1) == 0
+    # a layer without a declared type is full attention; bases fall back to the defaults
+    bare = gemma_text_config(layer_types=["sliding_attention"], rope_parameters=None, num_kv_shared_layers=0)
+    cfg = detwgt.gemma_config(bare, 512, [0] * 4)
+    assert cfg.types() == ["sliding_attention"] + ["full_attention"] * 3
+    assert (cfg.rope_base_sliding, cfg.rope_base_full, cfg.partial_rotary) == (10_000, 1_000_000, 1.0)
+    assert detwgt.gemma_config(gemma_text_config(tie_word_embeddings=True), 512, [0] * 4).tied
+    for bad in ({"global_head_dim": 64},
+                {"rope_parameters": {"sliding_attention": {"rope_theta": 10000.5}}},
+                {"num_hidden_layers": 6, "num_kv_shared_layers": 3,
+                 "layer_types": ["sliding_attention", "full_attention", "local", "sliding_attention",
+                                 "full_attention", "local"]}):
+        with pytest.raises(ValueError):
+            detwgt.gemma_config(gemma_text_config(**bad), 512, [0] * 6)
+
+
+@pytest.mark.skipif(not GEMMA_BUNDLE or not os.path.isdir(GEMMA_BUNDLE),
+                    reason="the reference's gemma parity bundle is not present")
+def test_reference_parity_gemma_bundle():
+    """The reference's gemma parity bundle: its file checksum, every tensor
+    the import reads placed, the derived shape, and the oracle generating
+    from it on the bundle's own prompts (cases.json: short, near the window,
+    over the window)."""
+    from iris_b200 import detwgt
+    from oracle.models import OracleModel
+    sums = json.load(open(os.path.join(GEMMA_BUNDLE, "checksums.json")))
+    data = open(os.path.join(GEMMA_BUNDLE, "model.detwgt"), "rb").read()
+    assert hashlib.sha256(data).hexdigest() == sums["model.detwgt"]
+    cfg, weights, f = detwgt.load_gemma_bundle(GEMMA_BUNDLE)
+    try:
+        assert (cfg.layers, cfg.hidden, cfg.ffn, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.vocab, cfg.ple_width) \
+            == (4, 128, 2048, 4, 2, 32, 512, 32)
+        assert cfg.tied is False and ("HEAD", -1) in weights and cfg.sliding_window == 16
+        assert [cfg.kv_donor(l) for l in range(4)] == [-1, -1, 0, 1] and cfg.rope(1)[1] == 16
+        assert len(f.tensors) == 74 and len(weights) == 2 + 3 + 1 + 4 * 16
+        om = OracleModel(cfg, {k: np.array(v) for k, v in weights.items()})
+        for case in json.load(open(os.path.join(GEMMA_BUNDLE, "cases.json"))):
+            toks, _ = om.generate(case["input_token_ids"], case["tokens"])
+            assert len(toks) == case["tokens"] and all(0 <= t < cfg.vocab for t in toks)
+    finally:
+        del weights
+        f.close()

@@ -1,6 +1,6 @@
 """GPU parity of the gemma-dense path against the CPU oracle, bit for bit.
 
-- BASELINE config 3's shapes (Gemma-2B architecture: 2048 hidden, 8 query
+- the benchmark's config 3 shapes (Gemma-2B architecture: 2048 hidden, 8 query
   heads over one kv head of 256, GeGLU 16384, a 256,000-row tied head with
   softcap 30, PLE width 256, a 768-position sliding window), two of its 18
   layers: a short prompt and greedy steps (every logit of the 256k head), and
@@ -13,7 +13,9 @@
   20 and 7 rows, and for the Gemma-2B slice across its window;
 - PLE rows of token ids (iris_model_ple_rows, view_kernels.rs:59-99);
 - the stage's refusal of carried keys that do not cover the window
-  (IRIS_EWINDOW, the reference's cache-coverage fault).
+  (IRIS_EWINDOW, the reference's cache-coverage fault);
+- a gemma bundle in the .detwgt format with an untied head and layer
+  scalars, read by iris_b200.detwgt, generating as the oracle does.
 """
 import dataclasses
 
@@ -125,3 +127,48 @@ def test_gemma_stage_refuses_keys_that_do_not_cover_the_window():
         dm.gemma_layer_range(2, rows, start, ple, prior=good, donor=good)
     assert e.value.code == _lib.IRIS_EWINDOW
     dm.close()
+
+
+@pytest.mark.parametrize("n_prompt,steps", [(5, 1), (15, 8), (34, 8)])
+def test_gemma_detwgt_bundle_matches_the_oracle(tmp_path, n_prompt, steps):
+    """A gemma-dense bundle in the reference's .detwgt format (written here
+    from seeded weights under the import's tensor names, with per-layer
+    `layer_scalar` tensors, one layer without one, and an untied lm_head;
+    config.json shaped as the reference's gemma parity bundle) loaded
+    through iris_b200.detwgt: every logit and token of a prompt short of,
+    near and over the 16-key window and its greedy steps equals the
+    oracle's on the same weights."""
+    import json
+    from iris_b200 import detwgt
+    from iris_b200.model import DeviceModel, synth_host_weights, tensor_table
+    from oracle.models import OracleModel
+    from test_detwgt import gemma_text_config, write_detwgt
+    config = {"model_type": "gemma3n", "text_config": gemma_text_config()}
+    scalars = [1 << 16, 3 << 15, 0, 1 << 16]
+    cfg = detwgt.gemma_config(config, 512, scalars)
+    w = synth_host_weights(cfg, 0x6E)
+    assert ("HEAD", -1) in w
+    names = detwgt.gemma_tensor_names(cfg.layers)
+    table = tensor_table(cfg)
+    tensors = []
+    for key, arr in w.items():
+        kind, rows, cols, _ = table[key]
+        dims = [cols] if kind == "values" and rows == 1 else [rows, cols]
+        tensors.append((names[key][0], dims, 8 if kind == "q8" else 32, arr))
+    for l, s in enumerate(scalars):
+        if s:
+            tensors.append((f"model.language_model.layers.{l}.layer_scalar", [1], 32, np.array([s])))
+    write_detwgt(tmp_path / "model.detwgt", tensors)
+    (tmp_path / "config.json").write_text(json.dumps(config))
+    cfg2, w2, f = detwgt.load_bundle(tmp_path)
+    assert cfg2.family == "gemma" and not cfg2.tied and cfg2.layer_scalars == scalars
+    dm = DeviceModel(cfg2, weights=w2)
+    prompt = seeded_prompt(n_prompt, n_prompt, cfg2.vocab)
+    sess = dm.session(64)
+    got = sess.generate(prompt, steps, want_logits=True)
+    want = OracleModel(cfg2, {k: np.array(v) for k, v in w2.items()}).generate(prompt, steps)
+    assert_same(got, want)
+    sess.close()
+    dm.close()
+    del w2
+    f.close()
