@@ -351,12 +351,19 @@ __device__ __forceinline__ uint64_t exp_term_lookup(int32_t score, int32_t mx) {
 // A warp a (query, head), eight a block: the integer softmax of the query's
 // scores (positions 0..p) into three weight planes over the pcap positions,
 // in three passes over the row with warp shuffles only (no block barrier, no
-// shared memory): the first maximum, the exp terms' sum, then each term again
-// (from the table) into its weight (attention_softmax_into, ops.rs:233-261);
-// the residual 1.0 - sum of weights goes onto the first maximum (:274-276).
-// Four consecutive positions a lane (rows and planes are 16-byte aligned).
+// shared memory): the first maximum; the exp terms (one table lookup each),
+// their sum, each term written over its score; then each stored term into
+// its weight (attention_softmax_into, ops.rs:233-261); the residual 1.0 - sum
+// of weights goes onto the first maximum (:274-276). Terms are below 2^32
+// except at distance 0, where the term is exactly 2^32: stored as
+// 0xFFFFFFFF, a value no other distance gives (distance 1 gives 2^32 - 65536).
+// Four consecutive positions a lane, two 16-byte loads in flight (rows and
+// planes are 16-byte aligned; pcap is a multiple of 128).
 constexpr uint32_t kSoftRowsPerBlock = 8;
-__global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel(const int32_t* __restrict__ s,
+constexpr uint32_t kTermOne = 0xFFFFFFFFu;
+__device__ __forceinline__ uint64_t stored_term(uint32_t v) { return v == kTermOne ? (uint64_t)1 << 32 : v; }
+
+__global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel(int32_t* __restrict__ s,
                                                                                  uint8_t* wp, uint32_t qcap,
                                                                                  uint32_t pcap, uint32_t pos0,
                                                                                  uint32_t tokens, uint32_t heads) {
@@ -367,16 +374,21 @@ __global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel
   if (r >= tokens * heads) return;
   const uint32_t h = r / tokens, q = r % tokens;
   const uint32_t n = pos0 + q + 1;
-  const int32_t* row = s + ((size_t)h * qcap + q) * pcap;
+  int32_t* row = s + ((size_t)h * qcap + q) * pcap;
   unsigned long long best = 0;
-  for (uint32_t t = 4 * lane; t < n; t += 128) {
-    const int4 v = *(const int4*)(row + t);
+  auto max4 = [&](int4 v, uint32_t t) {
     const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (uint32_t u = 0; u < 4; ++u) {
       const unsigned long long k = t + u < n ? best_key(x[u], t + u) : 0;
       best = k > best ? k : best;
     }
+  };
+  for (uint32_t t = 4 * lane; t < n; t += 256) {
+    const int4 v0 = *(const int4*)(row + t);
+    const int4 v1 = t + 128 < n ? *(const int4*)(row + t + 128) : make_int4(0, 0, 0, 0);
+    max4(v0, t);
+    if (t + 128 < n) max4(v1, t + 128);
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) {
@@ -386,11 +398,22 @@ __global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel
   const int32_t mx = best_key_value(best);
   const uint32_t tmax = best_key_token(best);
   uint64_t e = 0;
-  for (uint32_t t = 4 * lane; t < n; t += 128) {
-    const int4 v = *(const int4*)(row + t);
+  auto terms4 = [&](int4 v, uint32_t t) {
     const int32_t x[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
 #pragma unroll
-    for (uint32_t u = 0; u < 4; ++u) e += t + u < n ? exp_term_lookup(x[u], mx) : 0;
+    for (uint32_t u = 0; u < 4; ++u) {
+      const uint64_t term = t + u < n ? exp_term_lookup(x[u], mx) : 0;
+      e += term;
+      o[u] = term >> 32 ? kTermOne : (uint32_t)term;
+    }
+    *(uint4*)(row + t) = make_uint4(o[0], o[1], o[2], o[3]);
+  };
+  for (uint32_t t = 4 * lane; t < n; t += 256) {
+    const int4 v0 = *(const int4*)(row + t);
+    const int4 v1 = t + 128 < n ? *(const int4*)(row + t + 128) : make_int4(0, 0, 0, 0);
+    terms4(v0, t);
+    if (t + 128 < n) terms4(v1, t + 128);
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) e += __shfl_xor_sync(0xffffffffu, e, off);
@@ -399,32 +422,35 @@ __global__ void __launch_bounds__(32 * kSoftRowsPerBlock) at_softmax_warp_kernel
   uint8_t* w1 = w0 + (size_t)qcap * pcap;
   uint8_t* w2 = w1 + (size_t)qcap * pcap;
   int32_t wsl = 0;
-  for (uint32_t t = 4 * lane; t < pcap; t += 128) {
+  auto weights4 = [&](uint4 v, uint32_t t) {
+    const uint32_t x[4] = {v.x, v.y, v.z, v.w};
     uint32_t b0 = 0, b1 = 0, b2 = 0;
-    if (t < n) {
-      const int4 v = *(const int4*)(row + t);
-      const int32_t x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (uint32_t u = 0; u < 4; ++u) {
-        int32_t w = 0;
-        if (t + u < n) {
-          w = tot ? softmax_weight_inv((int64_t)exp_term_lookup(x[u], mx), tot, inv) : 0;
-          wsl += w;
-        }
-        b0 |= ((uint32_t)w & 0xFFu) << (8 * u);
-        b1 |= (((uint32_t)w >> 8) & 0xFFu) << (8 * u);
-        b2 |= (((uint32_t)w >> 16) & 0xFFu) << (8 * u);
+    for (uint32_t u = 0; u < 4; ++u) {
+      int32_t w = 0;
+      if (t + u < n) {
+        w = tot ? softmax_weight_inv((int64_t)stored_term(x[u]), tot, inv) : 0;
+        wsl += w;
       }
+      b0 |= ((uint32_t)w & 0xFFu) << (8 * u);
+      b1 |= (((uint32_t)w >> 8) & 0xFFu) << (8 * u);
+      b2 |= (((uint32_t)w >> 16) & 0xFFu) << (8 * u);
     }
     *(uint32_t*)(w0 + t) = b0;
     *(uint32_t*)(w1 + t) = b1;
     *(uint32_t*)(w2 + t) = b2;
+  };
+  for (uint32_t t = 4 * lane; t < pcap; t += 256) {
+    const uint4 v0 = t < n ? *(const uint4*)(row + t) : make_uint4(0, 0, 0, 0);
+    const uint4 v1 = t + 128 < n ? *(const uint4*)(row + t + 128) : make_uint4(0, 0, 0, 0);
+    weights4(v0, t);
+    if (t + 128 < pcap) weights4(v1, t + 128);
   }
 #pragma unroll
   for (uint32_t off = 16; off >= 1; off >>= 1) wsl += __shfl_xor_sync(0xffffffffu, wsl, off);
   __syncwarp();  // every lane's plane stores come before the first maximum's correction
   if (lane == 0) {
-    const int32_t wm = tot ? softmax_weight_inv((int64_t)exp_term_lookup(mx, mx), tot, inv) : 0;
+    const int32_t wm = tot ? softmax_weight_inv((int64_t)1 << 32, tot, inv) : 0;  // the first maximum's term
     const int32_t w = wm + sub_sat(kOneAct, wsl);  // no weight saturates
     w0[tmax] = (uint8_t)w;
     w1[tmax] = (uint8_t)(w >> 8);
@@ -504,7 +530,7 @@ cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, cons
                kmap, qmap, fault);
   if (e != cudaSuccess) return e;
   e = launch_k(at_softmax_warp_kernel, dim3((tokens * a.heads + kSoftRowsPerBlock - 1) / kSoftRowsPerBlock),
-               dim3(32 * kSoftRowsPerBlock), 0, stream, (const int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, tokens,
+               dim3(32 * kSoftRowsPerBlock), 0, stream, (int32_t*)sc.s, sc.wp, qcap, pcap, a.pos0, tokens,
                a.heads);
   if (e != cudaSuccess) return e;
   ValueTilesS vt;

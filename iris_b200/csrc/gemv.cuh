@@ -298,6 +298,71 @@ __device__ __forceinline__ void gemv_rows_product(const RowBlocks& rb, const uin
   }
 }
 
+// Rows with one scale (every block of the row has the same scale bits): the
+// lane's plane sums of its block for its two rows, added into int32 plane
+// accumulators that run over the lane's blocks of a whole tile group; the
+// scale is applied once a group (gemv_flush_uniform). Over a group a lane
+// adds S blocks of 32 products below 128 * 255 in magnitude: below 2^31 for
+// S < 2056.
+template <bool kThree>
+__device__ __forceinline__ void gemv_rows_sums(const RowBlocks& rb, const uint4* __restrict__ P0,
+                                               const uint4* __restrict__ P1, const uint4* __restrict__ P2,
+                                               const uint4* __restrict__ P3, uint32_t cbase, uint32_t b,
+                                               uint32_t lane, int32_t (&ps)[kTmaRowsPerWarp][4]) {
+  const uint32_t swap = (lane >> 2) & 1;
+  const uint32_t c0 = 2 * b + swap, c1 = 2 * b + (swap ^ 1);
+  const uint4 pa0 = P0[cbase + c0], pa1 = P1[cbase + c0], pa2 = P2[cbase + c0];
+  const uint4 pb0 = P0[cbase + c1], pb1 = P1[cbase + c1], pb2 = P2[cbase + c1];
+  uint4 pa3, pb3;
+  if (!kThree) {
+    pa3 = P3[cbase + c0];
+    pb3 = P3[cbase + c1];
+  }
+#pragma unroll
+  for (int r = 0; r < kTmaRowsPerWarp; ++r) {
+    const uint4 wa = rb.wa[r], wb = rb.wb[r];
+    int s0 = ps[r][0], s1 = ps[r][1], s2 = ps[r][2];
+    if (kThree) {
+      s0 = dp4a_su(wa.x, pa0.x, s0), s1 = dp4a_su(wa.x, pa1.x, s1), s2 = dp4a_ss(wa.x, pa2.x, s2);
+      s0 = dp4a_su(wa.y, pa0.y, s0), s1 = dp4a_su(wa.y, pa1.y, s1), s2 = dp4a_ss(wa.y, pa2.y, s2);
+      s0 = dp4a_su(wa.z, pa0.z, s0), s1 = dp4a_su(wa.z, pa1.z, s1), s2 = dp4a_ss(wa.z, pa2.z, s2);
+      s0 = dp4a_su(wa.w, pa0.w, s0), s1 = dp4a_su(wa.w, pa1.w, s1), s2 = dp4a_ss(wa.w, pa2.w, s2);
+      s0 = dp4a_su(wb.x, pb0.x, s0), s1 = dp4a_su(wb.x, pb1.x, s1), s2 = dp4a_ss(wb.x, pb2.x, s2);
+      s0 = dp4a_su(wb.y, pb0.y, s0), s1 = dp4a_su(wb.y, pb1.y, s1), s2 = dp4a_ss(wb.y, pb2.y, s2);
+      s0 = dp4a_su(wb.z, pb0.z, s0), s1 = dp4a_su(wb.z, pb1.z, s1), s2 = dp4a_ss(wb.z, pb2.z, s2);
+      s0 = dp4a_su(wb.w, pb0.w, s0), s1 = dp4a_su(wb.w, pb1.w, s1), s2 = dp4a_ss(wb.w, pb2.w, s2);
+    } else {
+      int s3 = ps[r][3];
+      s0 = dp4a_su(wa.x, pa0.x, s0), s1 = dp4a_su(wa.x, pa1.x, s1), s2 = dp4a_su(wa.x, pa2.x, s2), s3 = dp4a_ss(wa.x, pa3.x, s3);
+      s0 = dp4a_su(wa.y, pa0.y, s0), s1 = dp4a_su(wa.y, pa1.y, s1), s2 = dp4a_su(wa.y, pa2.y, s2), s3 = dp4a_ss(wa.y, pa3.y, s3);
+      s0 = dp4a_su(wa.z, pa0.z, s0), s1 = dp4a_su(wa.z, pa1.z, s1), s2 = dp4a_su(wa.z, pa2.z, s2), s3 = dp4a_ss(wa.z, pa3.z, s3);
+      s0 = dp4a_su(wa.w, pa0.w, s0), s1 = dp4a_su(wa.w, pa1.w, s1), s2 = dp4a_su(wa.w, pa2.w, s2), s3 = dp4a_ss(wa.w, pa3.w, s3);
+      s0 = dp4a_su(wb.x, pb0.x, s0), s1 = dp4a_su(wb.x, pb1.x, s1), s2 = dp4a_su(wb.x, pb2.x, s2), s3 = dp4a_ss(wb.x, pb3.x, s3);
+      s0 = dp4a_su(wb.y, pb0.y, s0), s1 = dp4a_su(wb.y, pb1.y, s1), s2 = dp4a_su(wb.y, pb2.y, s2), s3 = dp4a_ss(wb.y, pb3.y, s3);
+      s0 = dp4a_su(wb.z, pb0.z, s0), s1 = dp4a_su(wb.z, pb1.z, s1), s2 = dp4a_su(wb.z, pb2.z, s2), s3 = dp4a_ss(wb.z, pb3.z, s3);
+      s0 = dp4a_su(wb.w, pb0.w, s0), s1 = dp4a_su(wb.w, pb1.w, s1), s2 = dp4a_su(wb.w, pb2.w, s2), s3 = dp4a_ss(wb.w, pb3.w, s3);
+      ps[r][3] = s3;
+    }
+    ps[r][0] = s0, ps[r][1] = s1, ps[r][2] = s2;
+  }
+}
+
+// The end of a tile group for rows with one scale: the warp's exact row sum
+// x = sum over its lanes of s0 + 2^8 s1 + 2^16 s2 + 2^24 s3 (the products of
+// the row's weights in this half with the whole activations: below
+// K 2^37 in magnitude), then x m 2^e (m, e: the row's scale, q8.rs:27-43)
+// as a 128-bit value; |x m| < 2^63 for K <= 32768.
+__device__ __forceinline__ Acc128 gemv_flush_uniform(const int32_t (&ps)[4], uint16_t scale_bits) {
+  int64_t x = (int64_t)ps[0] + (int64_t)ps[1] * 256 + (int64_t)ps[2] * 65536 + (int64_t)ps[3] * 16777216;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  int32_t m = 0, e = 0;
+  q8_scale_parts_finite(scale_bits, &m, &e);
+  Acc128 v{0, 0};
+  acc128_add_shifted(v, x * m, e);
+  return v;
+}
+
 // Item range [*ib, *ie) of block b.
 __device__ __forceinline__ void gemv_range(const GemvPlan& p, uint32_t S, uint32_t groups, uint32_t b,
                                            uint32_t* ib, uint32_t* ie) {
@@ -437,11 +502,11 @@ __device__ __forceinline__ void ring_drain(const TileRing& r, const RingCursor& 
 // second half. j counts the sum slots used; after a given-up wait `stalled`
 // keeps the warp in step with the others without waiting.
 
-template <bool kWatch>
-__device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, const SumRing& sr, uint32_t& j,
-                                             const uint8_t* planes, bool wide, uint32_t K, uint32_t kc,
-                                             uint32_t S, int32_t e_fast, uint32_t ib, uint32_t ie, bool& stalled,
-                                             unsigned int* fault) {
+template <bool kWatch, bool kUniform>
+__device__ __forceinline__ void ring_consume_impl(const TileRing& r, RingCursor& c, const SumRing& sr, uint32_t& j,
+                                                  const uint8_t* planes, bool wide, uint32_t K, uint32_t kc,
+                                                  uint32_t S, int32_t e_fast, uint32_t ib, uint32_t ie,
+                                                  bool& stalled, unsigned int* fault) {
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint4* P0 = (const uint4*)planes;
   const uint4* P1 = P0 + K / 16;
@@ -454,11 +519,13 @@ __device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, c
   const uint32_t b0 = half ? mid : 0, b1 = half ? blocks : mid;
   Acc128 acc[kTmaRowsPerWarp];
   int64_t fast[kTmaRowsPerWarp], fast_hi[kTmaRowsPerWarp];
+  int32_t ps[kTmaRowsPerWarp][4];  // one scale a row: plane sums of the group so far
 #pragma unroll
   for (int i = 0; i < kTmaRowsPerWarp; ++i) {
     acc[i] = Acc128{0, 0};
     fast[i] = 0;
     fast_hi[i] = 0;
+    ps[i][0] = ps[i][1] = ps[i][2] = ps[i][3] = 0;
   }
   uint32_t sl = ib % S;  // slice of the current tile, kept without divisions
   for (uint32_t t = ib; t < ie; ++t) {
@@ -469,22 +536,36 @@ __device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, c
     const uint32_t cbase = sl * (kc / 16), b = b0 + lane;
     RowBlocks rb;
     if (b < b1) gemv_take_rows(W, Sc, kc, b, lane, rb);
+    else
+#pragma unroll
+      for (int i = 0; i < kTmaRowsPerWarp; ++i) rb.sc[i] = 0;  // a lane without a block adds nothing
     __syncwarp();
     if (lane == 0) mbar_arrive(&r.empty[c.slot]);  // the tile is in registers: refill the slot
     ring_advance(r, c);
     if (b < b1) {
-      if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, e_fast, acc, fast, fast_hi);
-      else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, e_fast, acc, fast, fast_hi);
+      if (kUniform) {
+        if (wide) gemv_rows_sums<false>(rb, P0, P1, P2, P3, cbase, b, lane, ps);
+        else gemv_rows_sums<true>(rb, P0, P1, P2, P3, cbase, b, lane, ps);
+      } else {
+        if (wide) gemv_rows_product<false>(rb, P0, P1, P2, P3, cbase, b, lane, e_fast, acc, fast, fast_hi);
+        else gemv_rows_product<true>(rb, P0, P1, P2, P3, cbase, b, lane, e_fast, acc, fast, fast_hi);
+      }
     }
     if (++sl == S) sl = 0;
     if (sl == 0 || t + 1 == ie) {  // the end of a tile group in this range
 #pragma unroll
       for (int i = 0; i < kTmaRowsPerWarp; ++i) {
-        acc128_add(acc[i], (uint64_t)fast[i], fast[i] >> 63);
-        acc128_add(acc[i], (uint64_t)fast_hi[i] << 16, fast_hi[i] >> 48);  // 2^16 fast_hi
-        acc[i] = warp_sum_acc128(acc[i]);
-        fast[i] = 0;
-        fast_hi[i] = 0;
+        if (kUniform) {
+          // lane 0 has a block whenever any lane does; then its scale is the row's
+          acc[i] = gemv_flush_uniform(ps[i], __shfl_sync(0xffffffffu, rb.sc[i], 0));
+          ps[i][0] = ps[i][1] = ps[i][2] = ps[i][3] = 0;
+        } else {
+          acc128_add(acc[i], (uint64_t)fast[i], fast[i] >> 63);
+          acc128_add(acc[i], (uint64_t)fast_hi[i] << 16, fast_hi[i] >> 48);  // 2^16 fast_hi
+          acc[i] = warp_sum_acc128(acc[i]);
+          fast[i] = 0;
+          fast_hi[i] = 0;
+        }
       }
       const uint32_t slot = j % kTmaSlots;
       if (j >= kTmaSlots && !stalled && !ring_wait<kWatch>(&sr.empty[slot], (j / kTmaSlots - 1) & 1, fault))
@@ -499,6 +580,19 @@ __device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, c
       for (int i = 0; i < kTmaRowsPerWarp; ++i) acc[i] = Acc128{0, 0};
     }
   }
+}
+
+// The consumer loop for a matrix whose rows each have one scale (uniform:
+// scaled once a tile group) or per-block scales.
+template <bool kWatch>
+__device__ __forceinline__ void ring_consume(const TileRing& r, RingCursor& c, const SumRing& sr, uint32_t& j,
+                                             const uint8_t* planes, bool wide, bool uniform, uint32_t K,
+                                             uint32_t kc, uint32_t S, int32_t e_fast, uint32_t ib, uint32_t ie,
+                                             bool& stalled, unsigned int* fault) {
+  if (uniform)
+    ring_consume_impl<kWatch, true>(r, c, sr, j, planes, wide, K, kc, S, e_fast, ib, ie, stalled, fault);
+  else
+    ring_consume_impl<kWatch, false>(r, c, sr, j, planes, wide, K, kc, S, e_fast, ib, ie, stalled, fault);
 }
 
 // Epilogue warp: the tile groups overlapping tiles [ib, ie) (S tiles a

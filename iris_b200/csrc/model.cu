@@ -174,6 +174,11 @@ struct IrisSession {
   StepPlan step{};
   StepStage* stages = nullptr;
   uint32_t nstages = 0;
+  // host copy of the stage list, the matrix of each product stage and the
+  // weights version its one-scale-a-row flag was taken at
+  std::vector<StepStage> step_host;
+  std::vector<const Q8GpuMatrix*> step_mats;
+  std::vector<uint32_t> step_versions;
   unsigned int* sync = nullptr;  // [nstages] arrival counters
   unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
   unsigned long long* sumsq = nullptr;  // [nstages][blocks] sums of squares of the residual stream
@@ -232,7 +237,10 @@ cudaError_t setup_step(IrisSession* s) {
   if (m->tp_world > 1 && (!m->xch.part || m->tp_world > kTpMaxWorld)) return cudaSuccess;
   std::vector<StepStage> st;
   std::vector<uint32_t> kcs;
+  std::vector<const Q8GpuMatrix*> mats;
   auto product = [&](uint32_t kind, uint32_t layer, const Q8GpuMatrix* w, const int32_t* norm) {
+    mats.resize(st.size());
+    mats.push_back(w);
     StepStage x{};
     x.q = w->q;
     x.s = w->s;
@@ -286,6 +294,10 @@ cudaError_t setup_step(IrisSession* s) {
     s->step = plan;
     return cudaSuccess;
   }
+  mats.resize(st.size());
+  s->step_host = st;
+  s->step_mats = mats;
+  s->step_versions.assign(st.size(), UINT32_MAX);  // flags taken before the first pass
   cudaError_t e = dalloc(&s->stages, st.size());
   if (e == cudaSuccess) e = cudaMemcpy(s->stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = dalloc(&s->sync, st.size());
@@ -806,6 +818,32 @@ int ensure_graph(IrisSession* s) {
   return (int)e;
 }
 
+// The persistent step's one-scale-a-row flags of every product stage whose
+// matrix changed since they were taken (weights written after the session
+// was made), copied to the device stage list before the next pass.
+cudaError_t refresh_step_flags(IrisSession* s) {
+  bool stale = false;
+  for (size_t i = 0; i < s->step_mats.size(); ++i)
+    stale |= s->step_mats[i] && q8_version(s->step_mats[i]) != s->step_versions[i];
+  if (!stale) return cudaSuccess;
+  cudaError_t e = cudaDeviceSynchronize();  // weight writes may have run on any stream
+  for (size_t i = 0; i < s->step_mats.size() && e == cudaSuccess; ++i) {
+    const Q8GpuMatrix* w = s->step_mats[i];
+    if (!w) continue;
+    const uint32_t v = q8_version(w);
+    if (v == s->step_versions[i]) continue;
+    bool uniform = false;
+    e = q8_rows_uniform(w, s->stream, &uniform);
+    s->step_host[i].uniform = uniform ? 1u : 0u;
+    s->step_versions[i] = v;
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(s->stages, s->step_host.data(), s->step_host.size() * sizeof(StepStage),
+                        cudaMemcpyHostToDevice, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);  // the host copy may change again
+  return e;
+}
+
 // Replays the decode graph `steps` times (positions len, len+1, ...).
 int decode_steps(IrisSession* s, uint32_t steps) {
   if (!s->has_logits) return IRIS_ESTATE;
@@ -813,8 +851,11 @@ int decode_steps(IrisSession* s, uint32_t steps) {
   choose_decode_path(s);
   if (s->use_step) {
     const StepArgs a = step_args(s);
-    cudaError_t e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);
-    for (uint32_t i = 0; i < steps && e == cudaSuccess; ++i) e = launch_decode_step(a, s->step, s->stream);
+    cudaError_t e = refresh_step_flags(s);
+    bool uniform = true;
+    for (size_t i = 0; i < s->step_mats.size(); ++i) uniform &= !s->step_mats[i] || s->step_host[i].uniform;
+    if (e == cudaSuccess) e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);
+    for (uint32_t i = 0; i < steps && e == cudaSuccess; ++i) e = launch_decode_step(a, s->step, uniform, s->stream);
     if (e != cudaSuccess) return (int)e;
     s->len += steps;
     return 0;

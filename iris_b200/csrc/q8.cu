@@ -195,6 +195,39 @@ void tc_invalidate(Q8GpuMatrix* m) {
   m->tc_rows = 0;
   m->tc_planes = 0;
   tc_state_set(m, 0);
+  __atomic_add_fetch(&m->version, 1u, __ATOMIC_RELEASE);
+}
+
+namespace {
+// One row a thread: flags[0] |= 1 when a row's blocks have different scale bits.
+__global__ void rows_uniform_kernel(const uint16_t* __restrict__ s, uint32_t rows, uint32_t cols, uint32_t kc,
+                                    uint32_t nslices, unsigned int* flags) {
+  const uint32_t row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const uint16_t first = s[q8_scale_offset(kc, nslices, row, 0)];
+  bool differ = false;
+  for (uint32_t b = 1; b < cols / 32 && !differ; ++b) differ = s[q8_scale_offset(kc, nslices, row, b)] != first;
+  if (differ) atomicOr(flags, 1u);
+}
+}  // namespace
+
+cudaError_t q8_rows_uniform(const Q8GpuMatrix* m, cudaStream_t stream, bool* uniform) {
+  *uniform = false;
+  if (m->cols > 32768 || m->cols == 0 || m->rows == 0) return cudaSuccess;
+  unsigned int* flags = nullptr;
+  cudaError_t e = cudaMallocAsync((void**)&flags, sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(flags, 0, sizeof(unsigned int), stream);
+  if (e == cudaSuccess)
+    e = launch_k(rows_uniform_kernel, dim3((m->rows + 255) / 256), dim3(256), 0, stream, m->s, m->rows, m->cols,
+                 m->kc, m->nslices, flags);
+  unsigned int h = 1;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&h, flags, sizeof(h), cudaMemcpyDeviceToHost, stream);
+  cudaError_t f = cudaFreeAsync(flags, stream);
+  if (e == cudaSuccess) e = f;
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess) *uniform = h == 0;
+  return e;
 }
 
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
@@ -413,7 +446,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   } else {
     RingCursor cc{0, 0, 0};
     bool stalled = false;
-    ring_consume<false>(ring, cc, sums, j, planes, wide, K, kc, S, p.e_fast, ib, ie, stalled, &g_fault);
+    ring_consume<false>(ring, cc, sums, j, planes, wide, false, K, kc, S, p.e_fast, ib, ie, stalled, &g_fault);
   }
 }
 

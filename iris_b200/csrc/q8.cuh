@@ -43,6 +43,7 @@ struct Q8GpuMatrix {
   int16_t* tc_mant;
   uint32_t tc_rows, tc_planes;
   int tc_state;  // read and written only through tc_state_get / _set / _claim
+  uint32_t version;  // bumped whenever the weights change (tc_invalidate); read through q8_version
 };
 
 namespace iris {
@@ -54,6 +55,7 @@ namespace iris {
 // two threads never build one copy twice.
 inline int tc_state_get(const Q8GpuMatrix* m) { return __atomic_load_n(&m->tc_state, __ATOMIC_ACQUIRE); }
 inline void tc_state_set(Q8GpuMatrix* m, int v) { __atomic_store_n(&m->tc_state, v, __ATOMIC_RELEASE); }
+inline uint32_t q8_version(const Q8GpuMatrix* m) { return __atomic_load_n(&m->version, __ATOMIC_ACQUIRE); }
 inline bool tc_state_claim(Q8GpuMatrix* m) {
   int expected = 0;
   return __atomic_compare_exchange_n(&m->tc_state, &expected, 2, false, __ATOMIC_ACQ_REL, __ATOMIC_ACQUIRE);
@@ -177,5 +179,9 @@ cudaError_t synth_values_dev(int32_t* dst, uint64_t seed, uint32_t tensor, int32
                              uint64_t count, uint32_t fan_in, cudaStream_t stream);
 Q8GpuMatrix* alloc_q8(uint32_t rows, uint32_t cols, cudaError_t* err);
 void free_q8(Q8GpuMatrix* m);
+// Whether every row of the matrix has one scale (all its blocks' scale bits
+// equal) and cols <= 32768, so that a decode product may scale each row once
+// (gemv_flush_uniform); runs a scan on `stream` and waits for it.
+cudaError_t q8_rows_uniform(const Q8GpuMatrix* m, cudaStream_t stream, bool* uniform);
 
 }  // namespace iris

@@ -742,7 +742,11 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
 
 // ---- the kernel --------------------------------------------------------------
 
-template <uint32_t PER, uint32_t HPC>
+// kUniform: every product stage's matrix has one scale a row (StepStage::
+// uniform), so the consumers run only the once-a-group scaling loop; the
+// general instantiation runs only the per-block one (one loop a kernel keeps
+// the register allocation of each to its own loop).
+template <uint32_t PER, uint32_t HPC, bool kUniform>
 __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kTmaMaxStages];
@@ -865,8 +869,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
     const bool wide = st.norm_w ? step_norm_planes<kHeld>(A, k, st.cols, wv, st.norm_w, planes, &s_scale)
                                 : step_copy_planes(src, st.cols, planes);
     if (threadIdx.x == 0) step_stamp(A, k, 1);
-    ring_consume<true>(ring, cc, sums, j, planes, wide, st.cols, st.kc, st.nslices, st.e_fast, ib, ie, stalled,
-                       A.fault);
+    ring_consume_impl<true, kUniform>(ring, cc, sums, j, planes, wide, st.cols, st.kc, st.nslices, st.e_fast, ib,
+                                      ie, stalled, A.fault);
     if (threadIdx.x == 0) step_stamp(A, k, 2);
   }
 }
@@ -874,13 +878,13 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
 #define IRIS_STEP_SHAPES(X) X(4, 1) X(4, 2) X(4, 4) X(8, 2) X(8, 4) X(16, 1) X(16, 2) X(16, 4)
 
 template <uint32_t PER, uint32_t HPC>
-const void* step_kernel_ptr() {
-  return (const void*)decode_step_kernel<PER, HPC>;
+const void* step_kernel_ptr(bool uniform) {
+  return uniform ? (const void*)decode_step_kernel<PER, HPC, true> : (const void*)decode_step_kernel<PER, HPC, false>;
 }
 
-const void* step_kernel_for(uint32_t per, uint32_t hpc) {
+const void* step_kernel_for(uint32_t per, uint32_t hpc, bool uniform) {
 #define IRIS_STEP_PICK(PER, HPC) \
-  if (per == PER && hpc == HPC) return step_kernel_ptr<PER, HPC>();
+  if (per == PER && hpc == HPC) return step_kernel_ptr<PER, HPC>(uniform);
   IRIS_STEP_SHAPES(IRIS_STEP_PICK)
 #undef IRIS_STEP_PICK
   return nullptr;
@@ -897,8 +901,8 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
   uint32_t hpc = 4;
   while (hpc > 1 && (G % hpc || hpc * d > 512)) hpc >>= 1;
   p.why = 2;
-  const void* fn = step_kernel_for(d / 8, hpc);
-  if (!fn) return p;
+  const void* fns[2] = {step_kernel_for(d / 8, hpc, false), step_kernel_for(d / 8, hpc, true)};
+  if (!fns[0] || !fns[1]) return p;
   p.why = 3;
   int dev = 0, sms = 0, coop = 0, optin = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -909,10 +913,14 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
     cudaGetLastError();
     return p;
   }
-  cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) {
-    cudaGetLastError();
-    return p;
+  size_t static_smem = 0;  // the larger of the two instantiations'
+  for (const void* fn : fns) {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, fn) != cudaSuccess) {
+      cudaGetLastError();
+      return p;
+    }
+    static_smem = std::max(static_smem, fa.sharedSizeBytes);
   }
   p.why = 1;
   const uint32_t groups = heads / hpc, chunks = (uint32_t)sms / groups;
@@ -927,20 +935,24 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
   const uint32_t widest = std::max(std::max(H, heads * d), F);
   const uint32_t attn = round_up(span_max * hpc * 4, 16) + span_max * hpc * 8;
   const uint32_t planes = round_up(std::max(4 * widest, attn), 128);
-  if ((size_t)optin <= fa.sharedSizeBytes) return p;
-  const uint32_t dyn = (uint32_t)optin - (uint32_t)fa.sharedSizeBytes;
+  if ((size_t)optin <= static_smem) return p;
+  const uint32_t dyn = (uint32_t)optin - (uint32_t)static_smem;
   if (planes + 2 * slot > dyn) return p;
   const uint32_t slots = std::min<uint32_t>(kTmaMaxStages, (dyn - planes) / slot);
   const uint32_t smem = planes + slots * slot;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-    cudaGetLastError();
-    return p;
+  for (const void* fn : fns) {
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+      cudaGetLastError();
+      return p;
+    }
   }
   p.why = 5;
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTmaThreads, smem) != cudaSuccess || per_sm < 1) {
-    cudaGetLastError();
-    return p;
+  for (const void* fn : fns) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTmaThreads, smem) != cudaSuccess || per_sm < 1) {
+      cudaGetLastError();
+      return p;
+    }
   }
   p.blocks = (uint32_t)sms;
   p.ring_slots = slots;
@@ -956,8 +968,8 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
   return p;
 }
 
-cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_t s) {
-  const void* fn = step_kernel_for(a.d / 8, p.hpc);
+cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, bool uniform, cudaStream_t s) {
+  const void* fn = step_kernel_for(a.d / 8, p.hpc, uniform);
   if (!fn || !p.ok) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.blocks);

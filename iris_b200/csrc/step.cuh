@@ -29,6 +29,7 @@ struct StepStage {
   uint32_t rows, cols, kc, nslices, items;
   int32_t e_fast;
   uint32_t xj;  // tensor parallelism: the pass's exchange (1-based) an o / down product feeds or an exchange is
+  uint32_t uniform;  // 1: every row of the matrix has one scale (products scaled once a tile group)
 };
 
 // Timeline stamps a block records per stage (StepArgs::trace): 0 input ready,
@@ -105,7 +106,8 @@ struct StepPlan {
 // kcs: the slice width of every matrix of the pass.
 StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_heads, uint32_t d, uint32_t V,
                           uint32_t cap, const uint32_t* kcs, uint32_t nkcs);
-cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, cudaStream_t s);
+// uniform: every product stage's matrix has one scale a row (StepStage::uniform).
+cudaError_t launch_decode_step(const StepArgs& a, const StepPlan& p, bool uniform, cudaStream_t s);
 cudaError_t prepare_step_kernels();
 
 }  // namespace iris
