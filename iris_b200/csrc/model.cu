@@ -480,6 +480,7 @@ ProductArgs session_product_args(IrisSession* s, const Q8GpuMatrix* w, uint32_t 
   a.split_acc = s->split_acc;
   a.split_count = s->split_count;
   a.split_groups = s->split_groups;
+  if (tokens == 1) a.uniform = q8_uniform_cached(const_cast<Q8GpuMatrix*>(w), s->stream) ? 1u : 0u;
   return a;
 }
 
@@ -801,6 +802,13 @@ int prefill_ids(IrisSession* s, const uint32_t* ids, uint32_t n, int32_t* logits
 
 int ensure_graph(IrisSession* s) {
   if (s->graph) return 0;
+  {  // the one-scale-a-row flags of the pass's products, taken before the capture
+    IrisModel* m = s->m;
+    for (uint32_t l = 0; l < m->L; ++l)
+      for (Q8GpuMatrix* w : {m->layers[l].qkv, m->layers[l].o, m->layers[l].gu, m->layers[l].down})
+        if (w) q8_uniform_cached(w, s->stream);
+    if (m->head) q8_uniform_cached(m->head, s->stream);
+  }
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return (int)e;
@@ -832,9 +840,7 @@ cudaError_t refresh_step_flags(IrisSession* s) {
     if (!w) continue;
     const uint32_t v = q8_version(w);
     if (v == s->step_versions[i]) continue;
-    bool uniform = false;
-    e = q8_rows_uniform(w, s->stream, &uniform);
-    s->step_host[i].uniform = uniform ? 1u : 0u;
+    s->step_host[i].uniform = q8_uniform_cached(const_cast<Q8GpuMatrix*>(w), s->stream) ? 1u : 0u;
     s->step_versions[i] = v;
   }
   if (e == cudaSuccess)
@@ -1369,7 +1375,9 @@ int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, 
   if (e == cudaSuccess) e = cudaEventRecord(s->stage_read[b], s->copy_stream);
   if (e == cudaSuccess) {
     cudaEvent_t& ev = s->tickets[t % kChainTickets];
-    if (!ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    // a thread waiting on a ticket sleeps (blocking sync) instead of spinning
+    // on a host core the record hashing needs
+    if (!ev) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming | cudaEventBlockingSync);
     if (e == cudaSuccess) e = cudaEventRecord(ev, s->copy_stream);
     if (e == cudaSuccess) s->next_ticket.store(t + 1);  // published after the event is recorded
     if (ticket) *ticket = t;

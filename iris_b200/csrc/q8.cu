@@ -230,6 +230,25 @@ cudaError_t q8_rows_uniform(const Q8GpuMatrix* m, cudaStream_t stream, bool* uni
   return e;
 }
 
+bool q8_uniform_cached(Q8GpuMatrix* m, cudaStream_t stream) {
+  const uint64_t v = q8_version(m);
+  const uint64_t c = __atomic_load_n(&m->uniform_cache, __ATOMIC_ACQUIRE);
+  if (c && (c >> 1) == v + 1) return (c & 1) != 0;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return false;
+  }
+  bool u = false;
+  // the weights may have been written on any stream
+  if (cudaDeviceSynchronize() != cudaSuccess || q8_rows_uniform(m, stream, &u) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  __atomic_store_n(&m->uniform_cache, ((v + 1) << 1) | (u ? 1u : 0u), __ATOMIC_RELEASE);
+  return u;
+}
+
 cudaError_t upload_q8_blocks(Q8GpuMatrix* dst, const uint8_t* host_blocks, uint32_t rows,
                              uint32_t cols, uint32_t row_stride, uint32_t row_offset,
                              int* bad_scale) {
@@ -376,7 +395,9 @@ bool plan_gemv(uint32_t rows, uint32_t K, uint32_t kc, int sms, bool split, Gemv
   return true;
 }
 
-template <int IN, int EPI>
+// kUniform: every row of the matrix has one scale (ProductArgs::uniform):
+// the consumers add plane sums over a tile group and scale each row once.
+template <int IN, int EPI, bool kUniform>
 __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs a, GemvPlan p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kTmaMaxStages];
@@ -446,7 +467,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
   } else {
     RingCursor cc{0, 0, 0};
     bool stalled = false;
-    ring_consume<false>(ring, cc, sums, j, planes, wide, false, K, kc, S, p.e_fast, ib, ie, stalled, &g_fault);
+    ring_consume_impl<false, kUniform>(ring, cc, sums, j, planes, wide, K, kc, S, p.e_fast, ib, ie, stalled,
+                                       &g_fault);
   }
 }
 
@@ -830,13 +852,19 @@ cudaError_t launch_gemv(const ProductArgs& a, cudaStream_t stream) {
   const uint32_t groups = (a.rows + kQ8TileRows - 1) / kQ8TileRows;
   const bool split = a.split_acc && a.split_count && groups <= a.split_groups;
   if (!plan_gemv(a.rows, a.cols, a.kc, device_sms(), split, &p)) return cudaErrorInvalidValue;
-  return launch_k(q8_gemv_tma_kernel<IN, EPI>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, a, p);
+  if (a.uniform)
+    return launch_k(q8_gemv_tma_kernel<IN, EPI, true>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, a, p);
+  return launch_k(q8_gemv_tma_kernel<IN, EPI, false>, dim3(p.grid), dim3(kTmaThreads), p.smem, stream, a, p);
 }
 
 template <int IN, int EPI>
 cudaError_t prepare_gemv_one() {
-  return cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)kTmaSmemBudget);
+  cudaError_t e = cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI, false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTmaSmemBudget);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(q8_gemv_tma_kernel<IN, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kTmaSmemBudget);
+  return e;
 }
 
 template <int IN>

@@ -44,6 +44,7 @@ struct Q8GpuMatrix {
   uint32_t tc_rows, tc_planes;
   int tc_state;  // read and written only through tc_state_get / _set / _claim
   uint32_t version;  // bumped whenever the weights change (tc_invalidate); read through q8_version
+  uint64_t uniform_cache;  // q8_uniform_cached: ((version + 1) << 1) | one scale a row, 0 when not taken
 };
 
 namespace iris {
@@ -129,6 +130,9 @@ struct ProductArgs {
   const uint8_t* tc_shift;
   const int16_t* tc_mant;
   uint32_t tc_rows, tc_planes;
+  // One-token products: every row of the matrix has one scale
+  // (q8_uniform_cached), so the GEMV scales each row once a tile group
+  uint32_t uniform;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);
@@ -183,5 +187,9 @@ void free_q8(Q8GpuMatrix* m);
 // equal) and cols <= 32768, so that a decode product may scale each row once
 // (gemv_flush_uniform); runs a scan on `stream` and waits for it.
 cudaError_t q8_rows_uniform(const Q8GpuMatrix* m, cudaStream_t stream, bool* uniform);
+// q8_rows_uniform cached by weights version (a scan after a device-wide
+// synchronisation when the cache is stale); false, without a scan, while
+// `stream` is capturing a graph.
+bool q8_uniform_cached(Q8GpuMatrix* m, cudaStream_t stream);
 
 }  // namespace iris

@@ -175,7 +175,9 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
     from concurrent.futures import ThreadPoolExecutor
     from . import _lib
     L = _lib.lib()
-    workers = workers or max(1, os.cpu_count() or 1)
+    if not workers:  # the host cores this process may use, shared with the node's other ranks
+        cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        workers = max(1, cores // max(1, int(os.environ.get("LOCAL_WORLD_SIZE", "1"))))
     model = session.model
     cfg = model.cfg
     if not 0 < range_size <= 512:
