@@ -505,10 +505,11 @@ def main():
                  "records_digest": hashlib.sha256("".join(d for _, _, d in recs).encode()).hexdigest(),
                  "selected_first": [int(x) for x in selected[:4]],
                  "parallelism": "replicas (one claim a GPU)" if world > 1 else "single",
-                 "api": "iris_session_range_begin/_layer/_end per range and layer (records.chain_claim)",
+                 "api": "iris_session_range_begin/_layer_leaves/_end per range and layer (records.chain_claim)",
                  "in_timed_region": "every stage (32 layers x 8 ranges) on the device, its rows and own K/V "
-                                    "copied out and its canonical record hashed (SHA-256) on host threads, "
-                                    "the head check's first maximum for every row",
+                                    "hashed on the device into the canonical record's SHA-256 leaf digests "
+                                    "(4096-byte leaves), the leaves copied out and the record digest taken on "
+                                    "host threads, the head check's first maximum for every row",
                  "arith_only_ms": arith * 1e3, "arith_only_tok_s": T / arith,
                  "algorithmic_int8_ops": ops,
                  "int8_frac": (ops / cs / 1e12 / int8_peak_c) if int8_peak_c else None,

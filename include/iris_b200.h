@@ -410,6 +410,16 @@ int iris_gemma_layer_range(IrisModel* model, uint32_t layer, const int32_t* rows
 int iris_session_range_begin(IrisSession* session, const uint32_t* ids, uint32_t n);
 int iris_session_range_layer(IrisSession* session, uint32_t layer, int32_t* rows_out, int32_t* own_k,
                              int32_t* own_v, uint32_t* ticket);
+/* As iris_session_range_layer, but the stage's rows, own K and own V are
+ * hashed on the device instead of copied out: leaves_out receives the
+ * SHA-256 (FIPS 180-4) of every consecutive leaf_bytes piece of the rows'
+ * bytes, then of the K rows', then of the V rows' (the last piece of each
+ * shorter), 32 bytes a digest: ceil(n*hidden*4 / leaf_bytes) +
+ * 2 ceil(n*kv_heads*head_dim*4 / leaf_bytes) digests. leaf_bytes: a
+ * multiple of 64 up to 1 MiB. The leaf digests of a stage record whose
+ * digest is taken on the host (the two-level canonical record). */
+int iris_session_range_layer_leaves(IrisSession* session, uint32_t layer, uint32_t leaf_bytes, uint8_t* leaves_out,
+                                    uint32_t* ticket);
 int iris_session_ticket_wait(IrisSession* session, uint32_t ticket);
 int iris_session_range_end(IrisSession* session, uint32_t* token_ids, int32_t* values);
 /* Page-locked host memory for the copies above (cudaHostAlloc). */

@@ -17,7 +17,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libiris_b200.so"
 SOURCES = ["q8.cu", "layers.cu", "model.cu", "tp.cu", "step.cu", "tc.cu", "attn_tc.cu"]
-HEADERS = ["common.cuh", "detnum.cuh", "q8.cuh", "gemv.cuh", "layers.cuh", "synth.cuh", "tp.cuh", "step.cuh", "tc.cuh", "tcgen05.cuh"]
+HEADERS = ["common.cuh", "detnum.cuh", "sha256.cuh", "q8.cuh", "gemv.cuh", "layers.cuh", "synth.cuh", "tp.cuh", "step.cuh", "tc.cuh", "tcgen05.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr"]

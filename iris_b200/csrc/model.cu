@@ -24,6 +24,7 @@
 
 #include "../../include/iris_b200.h"
 #include "layers.cuh"
+#include "sha256.cuh"
 #include "step.cuh"
 #include "tc.cuh"
 #include "tp.cuh"
@@ -200,6 +201,8 @@ struct IrisSession {
   // stage_read[b]: the copy stream finished reading buffer b
   cudaStream_t copy_stream = nullptr;
   int32_t* stage_rows[2] = {};
+  uint8_t* stage_leaves[2] = {};  // iris_session_range_layer_leaves: the stage's leaf digests
+  uint32_t leaves_cap = 0;        // leaf digests each holds
   cudaEvent_t staged = nullptr, stage_read[2] = {};
 };
 
@@ -216,6 +219,7 @@ void free_session(IrisSession* s) {
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
                   s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
   if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
+  for (int b = 0; b < 2; ++b) cudaFree(s->stage_leaves[b]);
   for (void* p : ptrs) cudaFree(p);
   for (int32_t* p : s->stage_rows) cudaFree(p);
   for (cudaEvent_t ev : s->tickets)
@@ -1348,30 +1352,87 @@ int iris_session_range_begin(IrisSession* s, const uint32_t* ids, uint32_t n) {
   return 0;
 }
 
-int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, int32_t* own_k, int32_t* own_v,
-                             uint32_t* ticket) {
+namespace {
+
+// One leaf a thread: the SHA-256 of bytes [j leaf, min((j + 1) leaf, bytes))
+// of segment s (the stage's rows, then its K rows, then its V rows), leaf
+// digest i = first[s] + j at out + 32 i.
+struct LeafSegments {
+  const uint32_t* p[3];
+  uint32_t bytes[3];
+  uint32_t first[4];  // first leaf of each segment; first[3]: all leaves
+};
+
+__global__ void __launch_bounds__(128) record_leaves_kernel(LeafSegments g, uint32_t leaf, uint8_t* out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= g.first[3]) return;
+  const uint32_t sg = i < g.first[1] ? 0 : i < g.first[2] ? 1 : 2;
+  const uint32_t off = (i - g.first[sg]) * leaf;
+  sha256_words(g.p[sg] + off / 4, min(leaf, g.bytes[sg] - off), out + (size_t)32 * i);
+}
+
+uint32_t leaves_of(uint64_t bytes, uint32_t leaf) { return (uint32_t)((bytes + leaf - 1) / leaf); }
+
+// A chain stage: run `layer` over the range, then on the copy stream either
+// copy its rows and own K/V to the host (leaf == 0) or hash them on the
+// device into leaf digests and copy those (leaf > 0); a ticket's event marks
+// the copies done.
+int range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, int32_t* own_k, int32_t* own_v, uint32_t leaf,
+                uint8_t* leaves_out, uint32_t* ticket) {
   if (!s || !s->range_n || layer != s->range_layer) return s ? IRIS_ESTATE : IRIS_EINVAL;
   IrisModel* m = s->m;
   const uint32_t n = s->range_n, start = s->len;
-  cudaError_t e = m->family == kFamilyGemma ? gemma_layer(s, layer, n, nullptr, start, true)
-                                            : mistral_layer(s, layer, n, nullptr, start);
   const size_t kvd = m->kvd;
+  cudaError_t e = cudaSuccess;
+  if (leaf) {  // leaf digest buffers for a whole range at this leaf size
+    const uint32_t need = leaves_of((uint64_t)kMaxRows * m->H * 4, leaf) + 2 * leaves_of((uint64_t)kMaxRows * kvd * 4, leaf);
+    if (need > s->leaves_cap) {
+      e = cudaStreamSynchronize(s->copy_stream);
+      for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+        cudaFree(s->stage_leaves[b]);
+        s->stage_leaves[b] = nullptr;
+        e = dalloc(&s->stage_leaves[b], (size_t)need * 32);
+      }
+      if (e != cudaSuccess) return (int)e;
+      s->leaves_cap = need;
+    }
+  }
+  e = m->family == kFamilyGemma ? gemma_layer(s, layer, n, nullptr, start, true)
+                                : mistral_layer(s, layer, n, nullptr, start);
   // the stage's rows into staging buffer b once the copy stream has read it,
-  // then every copy to the host on the copy stream while the next layer runs
+  // then every copy (or the hashing) on the copy stream while the next layer runs
   const uint32_t t = s->next_ticket.load(), b = t & 1;
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s->stream, s->stage_read[b], 0);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(s->stage_rows[b], s->x, (size_t)n * m->H * 4, cudaMemcpyDeviceToDevice, s->stream);
   if (e == cudaSuccess) e = cudaEventRecord(s->staged, s->stream);
   if (e == cudaSuccess) e = cudaStreamWaitEvent(s->copy_stream, s->staged, 0);
-  if (e == cudaSuccess && rows_out)
-    e = cudaMemcpyAsync(rows_out, s->stage_rows[b], (size_t)n * m->H * 4, cudaMemcpyDeviceToHost, s->copy_stream);
-  if (e == cudaSuccess && own_k)
-    e = cudaMemcpyAsync(own_k, s->kc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
-                        cudaMemcpyDeviceToHost, s->copy_stream);
-  if (e == cudaSuccess && own_v)
-    e = cudaMemcpyAsync(own_v, s->vc + kv_offset(s, layer) + (size_t)start * kvd, (size_t)n * kvd * 4,
-                        cudaMemcpyDeviceToHost, s->copy_stream);
+  const int32_t* kown = s->kc + kv_offset(s, layer) + (size_t)start * kvd;
+  const int32_t* vown = s->vc + kv_offset(s, layer) + (size_t)start * kvd;
+  if (leaf) {
+    LeafSegments g{};
+    g.p[0] = (const uint32_t*)s->stage_rows[b];
+    g.p[1] = (const uint32_t*)kown;
+    g.p[2] = (const uint32_t*)vown;
+    g.bytes[0] = n * m->H * 4;
+    g.bytes[1] = g.bytes[2] = (uint32_t)(n * kvd * 4);
+    g.first[0] = 0;
+    for (int sg = 0; sg < 3; ++sg) g.first[sg + 1] = g.first[sg] + leaves_of(g.bytes[sg], leaf);
+    if (e == cudaSuccess)
+      e = launch_k(record_leaves_kernel, dim3((g.first[3] + 127) / 128), dim3(128), 0, s->copy_stream, g, leaf,
+                   s->stage_leaves[b]);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(leaves_out, s->stage_leaves[b], (size_t)g.first[3] * 32, cudaMemcpyDeviceToHost,
+                          s->copy_stream);
+  } else {
+    if (e == cudaSuccess && rows_out)
+      e = cudaMemcpyAsync(rows_out, s->stage_rows[b], (size_t)n * m->H * 4, cudaMemcpyDeviceToHost,
+                          s->copy_stream);
+    if (e == cudaSuccess && own_k)
+      e = cudaMemcpyAsync(own_k, kown, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->copy_stream);
+    if (e == cudaSuccess && own_v)
+      e = cudaMemcpyAsync(own_v, vown, (size_t)n * kvd * 4, cudaMemcpyDeviceToHost, s->copy_stream);
+  }
   if (e == cudaSuccess) e = cudaEventRecord(s->stage_read[b], s->copy_stream);
   if (e == cudaSuccess) {
     cudaEvent_t& ev = s->tickets[t % kChainTickets];
@@ -1385,6 +1446,19 @@ int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, 
   if (e != cudaSuccess) return (int)e;
   s->range_layer = layer + 1;
   return 0;
+}
+
+}  // namespace
+
+int iris_session_range_layer(IrisSession* s, uint32_t layer, int32_t* rows_out, int32_t* own_k, int32_t* own_v,
+                             uint32_t* ticket) {
+  return range_layer(s, layer, rows_out, own_k, own_v, 0, nullptr, ticket);
+}
+
+int iris_session_range_layer_leaves(IrisSession* s, uint32_t layer, uint32_t leaf_bytes, uint8_t* leaves_out,
+                                    uint32_t* ticket) {
+  if (!leaves_out || leaf_bytes < 64 || leaf_bytes % 64 || leaf_bytes > (1u << 20)) return IRIS_EINVAL;
+  return range_layer(s, layer, nullptr, nullptr, nullptr, leaf_bytes, leaves_out, ticket);
 }
 
 int iris_session_ticket_wait(IrisSession* s, uint32_t ticket) {

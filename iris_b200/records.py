@@ -5,16 +5,20 @@ The reference commits each stage's outputs through Raster encodings
 crates/inference/staged/src/artifact_io.rs:46-58); the Raster crate is not
 available to this build, so those commitments cannot be reproduced. This
 module defines a documented substitute that pins the same content: a stage's
-output rows and its own K/V rows, byte for byte, under SHA-256.
+output rows and its own K/V rows, byte for byte, under SHA-256, as a
+two-level hash so that the device can hash the rows where they live.
 
-Record layout (all integers little-endian):
+Record layout (all integers little-endian; the digest is the SHA-256 of the
+record):
 
-    b"IRISREC1"
+    b"IRISREC2"
     u32 len(stage), stage name (UTF-8)      e.g. "layer_mistral/3"
-    u32 start_position, u32 rows, u32 width
-    rows x width int32                      the stage's output activations
-    u32 kv_width (0 when there are none)
-    rows x kv_width int32 (K), then the same for V
+    u32 start_position, u32 rows, u32 width, u32 kv_width (0 when none)
+    u32 leaf                                 bytes a leaf (4096)
+    leaf digests of the rows x width int32 (the stage's output activations),
+    then of the K rows, then of the V rows (rows x kv_width int32 each):
+    SHA-256 of each consecutive `leaf`-byte piece of the array, the last
+    piece shorter.
 
 `chain_records` runs a claim's teacher-forced pass stage by stage on the
 device and returns each stage's record digest: mistral-dense through
@@ -32,49 +36,56 @@ from typing import List, Optional, Sequence, Tuple
 
 import numpy as np
 
-MAGIC = b"IRISREC1"
+MAGIC = b"IRISREC2"
+LEAF = 4096
+
+
+def _checked(rows, k, v):
+    rows = np.ascontiguousarray(rows, "<i4")
+    if rows.ndim != 2:
+        raise ValueError("rows must be [n][width]")
+    if k is not None:
+        k = np.ascontiguousarray(k, "<i4")
+        v = np.ascontiguousarray(v, "<i4")
+        if k.shape != v.shape or k.ndim != 2 or k.shape[0] != rows.shape[0]:
+            raise ValueError("K and V must hold one row per output row")
+    return rows, k, v
+
+
+def leaf_digests(a: np.ndarray, leaf: int = LEAF) -> bytes:
+    """SHA-256 of each consecutive `leaf`-byte piece of the array's bytes."""
+    b = memoryview(np.ascontiguousarray(a)).cast("B")
+    return b"".join(hashlib.sha256(b[i:i + leaf]).digest() for i in range(0, len(b), leaf))
+
+
+def record_header(stage: str, start: int, n: int, width: int, kv_width: int, leaf: int = LEAF) -> bytes:
+    name = stage.encode()
+    return MAGIC + struct.pack("<I", len(name)) + name + struct.pack("<IIIII", start, n, width, kv_width, leaf)
 
 
 def stage_record(stage: str, start: int, rows: np.ndarray, k: Optional[np.ndarray] = None,
-                 v: Optional[np.ndarray] = None) -> bytes:
-    rows = np.ascontiguousarray(rows, "<i4")
-    if rows.ndim != 2:
-        raise ValueError("rows must be [n][width]")
-    name = stage.encode()
-    out = [MAGIC, struct.pack("<I", len(name)), name, struct.pack("<III", start, rows.shape[0], rows.shape[1]),
-           rows.tobytes()]
-    if k is None:
-        out.append(struct.pack("<I", 0))
-    else:
-        k = np.ascontiguousarray(k, "<i4")
-        v = np.ascontiguousarray(v, "<i4")
-        if k.shape != v.shape or k.shape[0] != rows.shape[0]:
-            raise ValueError("K and V must hold one row per output row")
-        out += [struct.pack("<I", k.shape[1]), k.tobytes(), v.tobytes()]
+                 v: Optional[np.ndarray] = None, leaf: int = LEAF) -> bytes:
+    rows, k, v = _checked(rows, k, v)
+    out = [record_header(stage, start, rows.shape[0], rows.shape[1], 0 if k is None else k.shape[1], leaf),
+           leaf_digests(rows, leaf)]
+    if k is not None:
+        out += [leaf_digests(k, leaf), leaf_digests(v, leaf)]
     return b"".join(out)
 
 
-def stage_digest(stage: str, start: int, rows: np.ndarray, k=None, v=None) -> str:
-    """SHA-256 of the stage's record, fed piece by piece (no copy of the
-    arrays; hashlib runs without the GIL on large pieces)."""
-    rows = np.ascontiguousarray(rows, "<i4")
-    if rows.ndim != 2:
-        raise ValueError("rows must be [n][width]")
-    name = stage.encode()
-    h = hashlib.sha256(MAGIC + struct.pack("<I", len(name)) + name +
-                       struct.pack("<III", start, rows.shape[0], rows.shape[1]))
-    h.update(memoryview(rows).cast("B"))
-    if k is None:
-        h.update(struct.pack("<I", 0))
-    else:
-        k = np.ascontiguousarray(k, "<i4")
-        v = np.ascontiguousarray(v, "<i4")
-        if k.shape != v.shape or k.shape[0] != rows.shape[0]:
-            raise ValueError("K and V must hold one row per output row")
-        h.update(struct.pack("<I", k.shape[1]))
-        h.update(memoryview(k).cast("B"))
-        h.update(memoryview(v).cast("B"))
-    return h.hexdigest()
+def stage_digest(stage: str, start: int, rows: np.ndarray, k=None, v=None, leaf: int = LEAF) -> str:
+    """SHA-256 of the stage's record."""
+    return hashlib.sha256(stage_record(stage, start, rows, k, v, leaf)).hexdigest()
+
+
+def digest_from_leaves(stage: str, start: int, n: int, width: int, kv_width: int, leaves: bytes,
+                       leaf: int = LEAF) -> str:
+    """The record digest from leaf digests computed elsewhere (the device's)."""
+    return hashlib.sha256(record_header(stage, start, n, width, kv_width, leaf) + leaves).hexdigest()
+
+
+def leaf_count(nbytes: int, leaf: int = LEAF) -> int:
+    return (nbytes + leaf - 1) // leaf
 
 
 def window_start(position: int, window: int) -> int:
@@ -142,13 +153,15 @@ def _gemma_chain_records(model, ids, range_size):
 class _Pinned:
     """A page-locked host array from iris_host_alloc."""
 
-    def __init__(self, shape):
+    def __init__(self, shape, dtype=np.int32):
         import ctypes as C
         from . import _lib
         n = int(np.prod(shape))
+        dtype = np.dtype(dtype)
         self._p = C.c_void_p()
-        _lib.check(_lib.lib().iris_host_alloc(n * 4, C.byref(self._p)), "iris_host_alloc")
-        self.a = np.ctypeslib.as_array(C.cast(self._p, C.POINTER(C.c_int32)), shape=(n,)).reshape(shape)
+        _lib.check(_lib.lib().iris_host_alloc(n * dtype.itemsize, C.byref(self._p)), "iris_host_alloc")
+        ctype = {np.dtype(np.int32): C.c_int32, np.dtype(np.uint8): C.c_uint8}[dtype]
+        self.a = np.ctypeslib.as_array(C.cast(self._p, C.POINTER(ctype)), shape=(n,)).reshape(shape)
 
     @property
     def ptr(self):
@@ -162,14 +175,17 @@ class _Pinned:
 
 
 def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int = 12,
-                workers: Optional[int] = None):
+                workers: Optional[int] = None, device_hash: bool = True):
     """A claim's teacher-forced pass range by range on a session, every stage's
-    record hashed while the device runs the next stages: each stage's rows
-    and own K/V are copied into one of `slots` page-locked buffer sets and a
-    worker thread waits for the copy (iris_session_ticket_wait), hashes the
-    record (the same digest as stage_digest) and frees the set. After each
-    range the head check selects a token for every row. Returns (records
-    [(stage, start, digest)], selected token ids, their scores)."""
+    record digest taken while the device runs the next stages. With
+    `device_hash` the device hashes each stage's rows and own K/V into the
+    record's leaf digests (iris_session_range_layer_leaves) and a worker
+    thread waits for them (iris_session_ticket_wait) and takes the record's
+    digest from the leaves; otherwise the rows and K/V are copied out and
+    hashed on the host. Either way the digest is stage_digest's. `slots`
+    page-locked buffer sets are in flight at most. After each range the head
+    check selects a token for every row. Returns (records [(stage, start,
+    digest)], selected token ids, their scores)."""
     import ctypes as C
     import os
     from concurrent.futures import ThreadPoolExecutor
@@ -184,8 +200,12 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
         raise ValueError("ranges hold 1 to 512 rows")
     kvd = cfg.kv_heads * cfg.head_dim
     stage_name = "prefill_range" if cfg.family == "gemma" else "layer_mistral"
-    sets = [(_Pinned((range_size, cfg.hidden)), _Pinned((range_size, kvd)), _Pinned((range_size, kvd)))
-            for _ in range(slots)]
+    if device_hash:
+        nleaves = leaf_count(range_size * cfg.hidden * 4) + 2 * leaf_count(range_size * kvd * 4)
+        sets = [(_Pinned((nleaves * 32,), np.uint8),) for _ in range(slots)]
+    else:
+        sets = [(_Pinned((range_size, cfg.hidden)), _Pinned((range_size, kvd)), _Pinned((range_size, kvd)))
+                for _ in range(slots)]
     busy = [None] * slots
     ids = np.ascontiguousarray(ids, np.uint32)
     selected = np.empty(len(ids), np.uint32)
@@ -194,6 +214,9 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
 
     def digest(slot, ticket, name, start, n):
         _lib.check(L.iris_session_ticket_wait(session.handle, ticket), "iris_session_ticket_wait")
+        if device_hash:
+            count = leaf_count(n * cfg.hidden * 4) + 2 * leaf_count(n * kvd * 4)
+            return name, start, digest_from_leaves(name, start, n, cfg.hidden, kvd, sets[slot][0].a[:count * 32].tobytes())
         r, k, v = sets[slot]
         return name, start, stage_digest(name, start, r.a[:n], k.a[:n], v.a[:n])
 
@@ -211,9 +234,14 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
                     if busy[slot] is not None:
                         busy[slot].result()  # the set's previous record is hashed
                     ticket = C.c_uint32()
-                    r, k, v = sets[slot]
-                    _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
-                                                          C.byref(ticket)), "iris_session_range_layer")
+                    if device_hash:
+                        _lib.check(L.iris_session_range_layer_leaves(session.handle, layer, LEAF, sets[slot][0].ptr,
+                                                                     C.byref(ticket)),
+                                   "iris_session_range_layer_leaves")
+                    else:
+                        r, k, v = sets[slot]
+                        _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
+                                                              C.byref(ticket)), "iris_session_range_layer")
                     busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
                     jobs.append(busy[slot])
                     j += 1

@@ -36,6 +36,7 @@ def detnum_shim(tmp_path_factory):
     L = C.CDLL(str(out))
     i32p, i64p = C.POINTER(C.c_int32), C.POINTER(C.c_int64)
     sig = {
+        "shim_sha256_leaves": (None, [C.POINTER(C.c_uint32), C.c_uint32, C.c_uint32, C.POINTER(C.c_uint8)]),
         "shim_requantize": (C.c_int32, [C.c_int64]),
         "shim_mul_sat": (C.c_int32, [C.c_int32, C.c_int32]),
         "shim_div_act": (C.c_int32, [C.c_int32, C.c_int32]),

@@ -2,10 +2,17 @@
 // (iris_b200/csrc/detnum.cuh, compiled here as host C++) with a C ABI so the
 // CPU tests can compare it against the oracle without a GPU.
 #include "../../iris_b200/csrc/detnum.cuh"
+#include "../../iris_b200/csrc/sha256.cuh"
 
 using namespace iris;
 
 extern "C" {
+// SHA-256 of each consecutive `chunk`-byte piece of data (the last one
+// shorter), 32 bytes a piece, as the device's record leaves are computed.
+void shim_sha256_leaves(const uint32_t* data, uint32_t bytes, uint32_t chunk, uint8_t* out) {
+  for (uint32_t off = 0, i = 0; off < bytes; off += chunk, ++i)
+    sha256_words(data + off / 4, bytes - off < chunk ? bytes - off : chunk, out + 32 * i);
+}
 int32_t shim_requantize(int64_t x) { return requantize(x); }
 int32_t shim_mul_sat(int32_t a, int32_t b) { return mul_sat(a, b); }
 int32_t shim_div_act(int32_t a, int32_t b) { return div_act(a, b); }

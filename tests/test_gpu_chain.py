@@ -1,7 +1,9 @@
 """The claim's teacher-forced pass on a session, range by range and
 device-resident (iris_session_range_begin / _layer / _end, driven by
-iris_b200.records.chain_claim with the stage records hashed on host threads
-while the device runs on): every stage's record digest equals the oracle's
+iris_b200.records.chain_claim, the stage records hashed while the device
+runs on: their leaves on the device (iris_session_range_layer_leaves,
+SHA-256 of every 4096-byte piece of the rows and K/V where they live) or
+everything on host threads from copies): every stage's record digest equals the oracle's
 stage by stage (chain_records over oracle/models.OracleStages), and the head
 check's selection of every row equals the oracle's first maximum over its
 final rows (sequence_check.rs:232-300). Both families; mistral ranges of 512
@@ -43,9 +45,10 @@ class FinalRows:
         return out
 
 
+@pytest.mark.parametrize("device_hash", [True, False])
 @pytest.mark.parametrize("family,n,range_size", [("mistral", 600, 512), ("mistral", 250, 100),
                                                  ("gemma", 45, 20)])
-def test_device_chain_matches_the_oracle(family, n, range_size):
+def test_device_chain_matches_the_oracle(family, n, range_size, device_hash):
     from iris_b200 import records
     from iris_b200.model import DeviceModel, synth_host_weights
     from iris_b200.shapes import parity_gemma, parity_mistral
@@ -56,7 +59,8 @@ def test_device_chain_matches_the_oracle(family, n, range_size):
     om = OracleModel(cfg, w)
     ids = np.random.default_rng(n).integers(0, cfg.vocab, size=n).tolist()
     sess = dm.session(n + 8)
-    got, selected, scores = records.chain_claim(sess, ids, range_size=range_size, slots=3, workers=2)
+    got, selected, scores = records.chain_claim(sess, ids, range_size=range_size, slots=3, workers=2,
+                                                device_hash=device_hash)
     assert sess.length == n
     oracle = FinalRows(OracleStages(om))
     want = records.chain_records(oracle, ids, range_size=range_size)
@@ -68,7 +72,7 @@ def test_device_chain_matches_the_oracle(family, n, range_size):
     from iris_b200 import _lib
     sess.reset()
     with pytest.raises(_lib.IrisError) as e:
-        records.chain_claim(sess, ids + ids, range_size=range_size, slots=2, workers=1)
+        records.chain_claim(sess, ids + ids, range_size=range_size, slots=2, workers=1, device_hash=device_hash)
     assert e.value.code == _lib.IRIS_ERANGE
     sess.close()
     dm.close()
