@@ -477,7 +477,9 @@ def main():
         from iris_b200 import records
         csess = cmodel.session(args.chain_tokens + 8)
         cprompt = np.random.default_rng(seed + 5 + rank).integers(0, cfg.vocab, size=args.chain_tokens).tolist()
-        records.chain_claim(csess, cprompt[:512], range_size=512)  # warm: buffers, pinned memory, kernels
+        # warm: buffers, pinned memory, kernels, and the attention scratch every
+        # range position of the claim needs (sized on first use)
+        records.chain_claim(csess, cprompt, range_size=512)
         csess.reset()
         if dist:
             dist.barrier()
