@@ -56,7 +56,7 @@ __device__ __forceinline__ bool step_is_product(uint32_t kind) {
 // spread evenly (the counts differ by at most one group). Splitting groups
 // between blocks would balance exactly but end every stage with an exchange
 // of partial sums through L2 (dependent atomics, a fence, a re-read), which
-// costs more than one group's stream.
+// costs more than one group's stream (measured: 2,580 -> 2,828 us a pass).
 __device__ __forceinline__ void step_range(const StepStage& st, uint32_t b, uint32_t nb, uint32_t* ib,
                                            uint32_t* ie) {
   const uint32_t groups = st.items / st.nslices;
@@ -450,6 +450,13 @@ __device__ __forceinline__ AttnChunk attn_chunk(const StepArgs& A, uint32_t p) {
   return c;
 }
 
+// The attention scratch of a block (the planes region during the attention
+// stage): scores / weights [span][HPC] int32, exp terms [span][HPC] u64, then
+// the group's query rows and row p's keys (HPC + 1 rows, kv_pitch apart).
+__host__ __device__ inline uint32_t step_attn_q_offset(uint32_t span_max, uint32_t hpc) {
+  return round_up(round_up(span_max * hpc * 4, 16) + span_max * hpc * 8, 16);
+}
+
 // Key and value rows sit in a ring slot 4 D + 16 bytes apart: lane l of a warp
 // reading row t0 + l at a fixed column then starts 4 (t0 + l) banks further
 // on, so eight lanes' 16-byte pieces cover all 32 banks (no conflicts).
@@ -517,94 +524,66 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     sh.sum[tid] = 0;
     sh.wsum[tid] = 0;
   }
-  // Scores: LPP lanes a position (NV interleaved int4 chunks each, so that a
-  // position's lanes read its key row contiguously), PW positions a warp.
-  constexpr uint32_t LPP = D / 4 < 16 ? D / 4 : 16, NV = D / LPP / 4, PW = 32 / LPP;
-  const uint32_t pl = lane % LPP, pslot = lane / LPP;
-  int4 q[HPC][NV];
-#pragma unroll
-  for (uint32_t h = 0; h < HPC; ++h)
-#pragma unroll
-    for (uint32_t i = 0; i < NV; ++i) q[h][i] = __ldcg((const int4*)(A.q + (size_t)(h0 + h) * D + 4 * (pl + LPP * i)));
+  // Scores: one lane a (position, head), HPC lanes a position, PPW positions
+  // a warp; each lane runs its dot product over all D dimensions, reading
+  // the key row (the position's HPC lanes read the same words: a broadcast)
+  // and its head's query from shared memory. Query rows and row p's keys are
+  // staged behind the exp terms, kv_pitch apart so that the HPC heads'
+  // words fall in different banks.
+  constexpr uint32_t PPW = 32 / HPC;
+  static_assert(32 % HPC == 0, "whole positions a warp");
+  const uint32_t my_h = lane % HPC, my_p = lane / HPC;
+  int32_t* qs = (int32_t*)(scratch + step_attn_q_offset(A.span_max, HPC));  // [HPC][PITCH]
+  int32_t* prow = qs + HPC * PITCH;                                          // row p's keys
+  for (uint32_t o = tid * 4; o < HPC * D; o += kStepConsumers * 4)
+    *(int4*)(qs + (o / D) * PITCH + o % D) = __ldcg((const int4*)(A.q + (size_t)h0 * D + o));
+  if (has_p)
+    for (uint32_t o = tid * 4; o < D; o += kStepConsumers * 4)
+      *(int4*)(prow + o) = __ldcg((const int4*)(A.kcache + lay + (size_t)p * A.kvd + g * D + o));
   part_sync<kStepConsumers>();
 
-  // ---- 1. scores and each head's first maximum (lane pl keeps the key of
-  // head pl / LPH, the head its exchange ends with)
+  // ---- 1. scores and each head's first maximum (every lane keeps the key of
+  // its head my_h)
   unsigned long long best = 0;
-  // The scores of local row t (all lanes of the warp take part in the
-  // sums): each lane's HPC partial dot products are summed over the
-  // position's LPP lanes with a halving exchange, after which lane pl holds
-  // head pl / (LPP / HPC)'s total and one lane a head finishes its score.
-  constexpr uint32_t LPH = LPP / HPC;  // lanes that end with the same head
-  static_assert(HPC <= LPP, "a head's sum per lane group");
-  auto score = [&](const int4* kv, bool live, uint32_t t) {
-    uint64_t v[HPC];
-#pragma unroll
-    for (uint32_t h = 0; h < HPC; ++h) {
-      int64_t c0 = 0, c1 = 0;
-#pragma unroll
-      for (uint32_t i = 0; i < NV; ++i) {
-        mac_wide(c0, q[h][i].x, kv[i].x);
-        mac_wide(c1, q[h][i].y, kv[i].y);
-        mac_wide(c0, q[h][i].z, kv[i].z);
-        mac_wide(c1, q[h][i].w, kv[i].w);
-      }
-      v[h] = (uint64_t)c0 + (uint64_t)c1;
+  const int4* q4 = (const int4*)(qs + my_h * PITCH);
+  auto score_row = [&](const int32_t* krow, uint32_t t) {  // t: the row's index in the chunk
+    const int4* k4 = (const int4*)krow;
+    int64_t c0 = 0, c1 = 0;
+#pragma unroll 8
+    for (uint32_t i = 0; i < D / 4; ++i) {
+      const int4 kv = k4[i], qv = q4[i];
+      mac_wide(c0, qv.x, kv.x);
+      mac_wide(c1, qv.y, kv.y);
+      mac_wide(c0, qv.z, kv.z);
+      mac_wide(c1, qv.w, kv.w);
     }
-#pragma unroll
-    for (uint32_t n = HPC, off = LPP / 2; n > 1; n >>= 1, off >>= 1) {
-      const bool upper = (pl & off) != 0;
-#pragma unroll
-      for (uint32_t i = 0; i < n / 2; ++i) {
-        const uint64_t send = upper ? v[i] : v[i + n / 2];
-        const uint64_t keep = upper ? v[i + n / 2] : v[i];
-        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-      }
-    }
-    uint64_t sum = v[0];
-#pragma unroll
-    for (uint32_t off = LPH / 2; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if (pl % LPH == 0 && live) {
-      const int32_t sc = finish_score((int64_t)sum, SCORE_MISTRAL, A.scale_q32);
-      sw[t * HPC + pl / LPH] = sc;
-      const unsigned long long key = best_key(sc, r0 + t);
-      best = key > best ? key : best;
-    }
+    const int32_t sc = finish_score((int64_t)((uint64_t)c0 + (uint64_t)c1), SCORE_MISTRAL, A.scale_q32);
+    sw[t * HPC + my_h] = sc;
+    const unsigned long long key = best_key(sc, r0 + t);
+    best = key > best ? key : best;
   };
-  int4 kvp[NV];  // row p (written by this pass): its load starts before the slots are scored
-  if (has_p && warp == 0) {
-#pragma unroll
-    for (uint32_t i = 0; i < NV; ++i)
-      kvp[i] = pslot == 0 ? __ldcg((const int4*)(A.kcache + lay + (size_t)p * A.kvd + g * D + 4 * (pl + LPP * i)))
-                          : make_int4(0, 0, 0, 0);
-  }
   for (uint32_t sb = 0; sb < nsm; sb += per_slot) {
     const uint32_t nrows = min(per_slot, nsm - sb);
     if (!stalled && !ring_wait<true>(&ring.full[cc.slot], cc.parity, A.fault)) stalled = true;
     if (sb == 0 && tid == 0) step_stamp(A, k, 1);
     const int32_t* ks = (const int32_t*)(ring.base + cc.slot * ring.slot_bytes);
-    for (uint32_t base = 0; base < nrows; base += kWarps * PW) {
-      const uint32_t t = base + warp * PW + pslot;
-      const bool live = t < nrows;
-      int4 kv[NV];
-#pragma unroll
-      for (uint32_t i = 0; i < NV; ++i)
-        kv[i] = live ? *(const int4*)(ks + t * PITCH + 4 * (pl + LPP * i)) : make_int4(0, 0, 0, 0);
-      score(kv, live, sb + t);
+    for (uint32_t base = 0; base < nrows; base += kWarps * PPW) {
+      const uint32_t t = base + warp * PPW + my_p;
+      if (t < nrows) score_row(ks + t * PITCH, sb + t);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&ring.empty[cc.slot]);  // the slot's key rows are used
     ring_advance(ring, cc);
   }
-  if (has_p && warp == 0) score(kvp, pslot == 0, nsm);
-  // the warp's keys a head: its PW position slots (lanes pl + LPP j) meet
-  // by shuffles, then the sixteen warps through shared memory
+  if (has_p && warp == 0 && my_p == 0) score_row(prow, nsm);
+  // the warp's keys a head (lanes my_h, my_h + HPC, ...), then the sixteen
+  // warps through shared memory
 #pragma unroll
-  for (uint32_t off = LPP; off < 32; off <<= 1) {
+  for (uint32_t off = HPC; off < 32; off <<= 1) {
     const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
     best = o > best ? o : best;
   }
-  if (lane < LPP && lane % LPH == 0) sh.wbest[warp][lane / LPH] = best;
+  if (lane < HPC) sh.wbest[warp][lane] = best;
   part_sync<kStepConsumers>();
   if (tid < HPC) {
     unsigned long long b = 0;
@@ -622,8 +601,8 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
   if (tid == 0) step_stamp(A, k, 3);
 
   // ---- 2. exp terms against the group's first maximum, their sums.
-  // Element e = position * HPC + head: thread tid always meets head tid % HPC.
-  const uint32_t my_h = tid % HPC;
+  // Element e = position * HPC + head: thread tid always meets head tid % HPC
+  // (= my_h: 32 % HPC == 0).
   {
     const int32_t mx = best_key_value(sh.gbest[my_h]);
     uint64_t e = 0;
@@ -933,7 +912,7 @@ StepPlan plan_decode_step(uint32_t H, uint32_t F, uint32_t heads, uint32_t kv_he
   // scratch (scores, then weights, and exp terms); the rest of the shared
   // memory is ring slots.
   const uint32_t widest = std::max(std::max(H, heads * d), F);
-  const uint32_t attn = round_up(span_max * hpc * 4, 16) + span_max * hpc * 8;
+  const uint32_t attn = step_attn_q_offset(span_max, hpc) + (hpc + 1) * (d * 4 + 16);
   const uint32_t planes = round_up(std::max(4 * widest, attn), 128);
   if ((size_t)optin <= static_smem) return p;
   const uint32_t dyn = (uint32_t)optin - (uint32_t)static_smem;
