@@ -328,7 +328,7 @@ __global__ void at_pack_values_t_kernel(const int32_t* __restrict__ src, uint32_
 // holds the term of d = -i at i, filled once per device by the same device
 // function; d = 0 gives 2^32, which the 32-bit entry wraps to 0 and
 // exp_term_lookup restores. 4 MB, read through L2.
-constexpr uint32_t kExpTableSize = 1u << 20;
+constexpr uint32_t kExpTableSize = kExpTerms;
 __device__ uint32_t g_exp_terms[kExpTableSize];
 
 // Entry 0 is never read as a term (distance 0 returns 2^32 before the
@@ -560,6 +560,14 @@ cudaError_t ensure_exp_table() {
 __global__ void exp_terms_probe_kernel(uint64_t* out, uint32_t first, uint32_t count) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < count) out[i] = exp_term_lookup(-(int32_t)(first + i), 0);
+}
+
+cudaError_t exp_term_table(const uint32_t** table) {
+  cudaError_t e = ensure_exp_table();
+  void* p = nullptr;
+  if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_exp_terms);
+  *table = (const uint32_t*)p;
+  return e;
 }
 
 cudaError_t prepare_attn_tc_kernels() {

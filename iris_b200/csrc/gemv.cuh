@@ -383,6 +383,11 @@ __device__ __forceinline__ void atomic_add_acc128(unsigned long long* dst, Acc12
   atomicAdd(dst + 1, (unsigned long long)v.hi + carry);
 }
 
+// Release add of 1 on a global counter (the writes ordered before it first).
+__device__ __forceinline__ void gemv_red_add_release(unsigned int* p) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p) : "memory");
+}
+
 // The epilogue of one finished tile group: lane l < 16 holds the rounded value
 // of row g * 16 + l. Single-row epilogues return the value the lane wrote
 // (0 for none).
@@ -680,6 +685,21 @@ __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRin
       }
       const uint32_t row = (gfirst + k0 + q) * kQ8TileRows + 2 * pr;
       if (q < nbat && ((fin >> q) & 1) && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
+      if (EPI == EPI_QKV_ROPE && a.gready) {
+        // each finished group's rows, stored by this batch's lanes (ordered
+        // before the adds by __syncwarp), to the attention groups reading them
+        __syncwarp();
+        if (lane < nbat && ((fin >> lane) & 1)) {
+          const uint32_t r0 = (gfirst + k0 + lane) * kQ8TileRows, G = a.qd / a.kvd;  // query heads a kv head
+          const uint32_t hpc = a.gready_hpc, per_kv = G / hpc;  // attention groups a kv head
+          if (r0 < a.qd) {
+            gemv_red_add_release(a.gready + r0 / a.head_dim / hpc);
+          } else {
+            const uint32_t kh = ((r0 - a.qd) % a.kvd) / a.head_dim;  // the K or V rows' kv head
+            for (uint32_t j = 0; j < per_kv; ++j) gemv_red_add_release(a.gready + kh * per_kv + j);
+          }
+        }
+      }
     }
   }
   if (EPI == EPI_RESID && a.sumsq) {  // the block's share, clamped: the norm's sum saturates there anyway

@@ -92,6 +92,11 @@ bool attn_tc_usable(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc)
 cudaError_t launch_attention_prefill_tc(const AttnArgs& a, uint32_t tokens, const AttnTcScratch& sc,
                                         cudaStream_t stream);
 cudaError_t prepare_attn_tc_kernels();
+// The device's table of softmax exp terms (filled on first use): entry i
+// (1 <= i < kExpTerms) is softmax_exp_term at distance -i (Q16.16) below the
+// maximum; distances of kExpTerms or more give 0, distance 0 gives 2^32.
+constexpr uint32_t kExpTerms = 1u << 20;
+cudaError_t exp_term_table(const uint32_t** table);
 cudaError_t launch_attention_prefill(const AttnArgs& a, uint32_t tokens, uint32_t max_visible,
                                      cudaStream_t s);
 

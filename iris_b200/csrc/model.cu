@@ -173,6 +173,7 @@ struct IrisSession {
   uint32_t split_groups = 0;
   // persistent decode step (step.cu): its plan, stage list and arrival counter
   StepPlan step{};
+  const uint32_t* exp_terms = nullptr;  // the device's exp-term table (the step's attention)
   StepStage* stages = nullptr;
   uint32_t nstages = 0;
   // host copy of the stage list, the matrix of each product stage and the
@@ -181,6 +182,7 @@ struct IrisSession {
   std::vector<const Q8GpuMatrix*> step_mats;
   std::vector<uint32_t> step_versions;
   unsigned int* sync = nullptr;  // [nstages] arrival counters
+  unsigned int* gready = nullptr;  // [layers][heads / hpc] the attention groups' q|k|v tile groups stored
   unsigned long long* trace = nullptr;  // optional per-stage timeline of the last pass
   unsigned long long* sumsq = nullptr;  // [nstages][blocks] sums of squares of the residual stream
   unsigned long long *kslots = nullptr, *sslots = nullptr;  // attention exchange slots [heads][blocks]
@@ -217,7 +219,7 @@ void free_session(IrisSession* s) {
                   s->logits, s->planes, s->planes2, s->best, s->d_ids, s->d_pos, s->d_token, s->d_step,
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
-                  s->stages, s->sync, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
+                  s->stages, s->sync, s->gready, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf};
   if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
   for (int b = 0; b < 2; ++b) cudaFree(s->stage_leaves[b]);
   for (void* p : ptrs) cudaFree(p);
@@ -293,6 +295,7 @@ cudaError_t setup_step(IrisSession* s) {
     if (tp) exchange(l);
   }
   product(STEP_HEAD, 0, m->head, m->final_norm);
+  if (cudaError_t e = exp_term_table(&s->exp_terms); e != cudaSuccess) return e;
   StepPlan plan = plan_decode_step(m->H, m->F, m->heads, m->kvh, m->d, m->V, s->cap, kcs.data(), (uint32_t)kcs.size());
   if (!plan.ok) {
     s->step = plan;
@@ -306,6 +309,9 @@ cudaError_t setup_step(IrisSession* s) {
   if (e == cudaSuccess) e = cudaMemcpy(s->stages, st.data(), st.size() * sizeof(StepStage), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = dalloc(&s->sync, st.size());
   if (e == cudaSuccess) e = cudaMemset(s->sync, 0, st.size() * sizeof(unsigned int));
+  const size_t ngready = (size_t)m->L * (m->heads / plan.hpc);
+  if (e == cudaSuccess) e = dalloc(&s->gready, ngready);
+  if (e == cudaSuccess) e = cudaMemset(s->gready, 0, ngready * sizeof(unsigned int));
   const size_t nslots = (size_t)m->heads * plan.blocks;
   if (e == cudaSuccess) e = dalloc(&s->kslots, nslots);
   if (e == cudaSuccess) e = dalloc(&s->sslots, nslots);
@@ -332,6 +338,7 @@ StepArgs step_args(IrisSession* s) {
   a.embed_kc = m->embed->kc;
   a.embed_nslices = m->embed->nslices;
   a.H = m->H;
+  a.layers = m->L;
   a.heads = m->heads;
   a.kv_heads = m->kvh;
   a.d = m->d;
@@ -358,6 +365,9 @@ StepArgs step_args(IrisSession* s) {
   a.gbar = s->gbar;
   a.chunks = s->step.chunks;
   a.span_max = s->step.span_max;
+  a.gready = s->gready;
+  a.hpc = s->step.hpc;
+  a.exp_terms = s->exp_terms;
   a.d_token = s->d_token;
   a.d_pos = s->d_pos;
   a.d_step = s->d_step;
@@ -865,6 +875,9 @@ int decode_steps(IrisSession* s, uint32_t steps) {
     bool uniform = true;
     for (size_t i = 0; i < s->step_mats.size(); ++i) uniform &= !s->step_mats[i] || s->step_host[i].uniform;
     if (e == cudaSuccess) e = cudaMemsetAsync(s->sync, 0, s->nstages * sizeof(unsigned int), s->stream);
+    if (e == cudaSuccess)
+      e = cudaMemsetAsync(s->gready, 0, (size_t)s->m->L * (s->m->heads / s->step.hpc) * sizeof(unsigned int),
+                          s->stream);
     for (uint32_t i = 0; i < steps && e == cudaSuccess; ++i) e = launch_decode_step(a, s->step, uniform, s->stream);
     if (e != cudaSuccess) return (int)e;
     s->len += steps;

@@ -133,6 +133,11 @@ struct ProductArgs {
   // One-token products: every row of the matrix has one scale
   // (q8_uniform_cached), so the GEMV scales each row once a tile group
   uint32_t uniform;
+  // Decode EPI_QKV_ROPE in the persistent step (optional): a release add on
+  // gready[attention group] for each finished tile group of rows, for every
+  // group of gready_hpc query heads that reads those rows
+  unsigned int* gready;
+  uint32_t gready_hpc;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);

@@ -230,6 +230,8 @@ __device__ __forceinline__ ProductArgs step_product_args(const StepArgs& A, cons
     a.kcache = A.kcache + (size_t)st.layer * A.cap * A.kvd;
     a.vcache = A.vcache + (size_t)st.layer * A.cap * A.kvd;
     a.pos0 = p;
+    a.gready = A.gready + (size_t)st.layer * (A.heads / A.hpc);
+    a.gready_hpc = A.hpc;
   } else if ((st.kind == STEP_O || st.kind == STEP_DOWN) && A.tp_world > 1) {
     // this rank's input columns: unrounded partial sums for exchange xj
     a.partial = A.xpart + (size_t)((xbase + st.xj) & 1) * A.H * 4;
@@ -339,6 +341,7 @@ __device__ __forceinline__ void step_finish(const StepArgs& A, uint32_t p, uint3
   *A.d_step = step + 1;
   *A.d_pos = p + 1;
   for (uint32_t k = 0; k < A.nstages; ++k) A.sync[k] = 0;
+  for (uint32_t i = 0; i < A.layers * (A.heads / A.hpc); ++i) A.gready[i] = 0;
 }
 
 // ---- attention stage --------------------------------------------------------
@@ -421,6 +424,16 @@ __device__ __forceinline__ uint64_t reduce_scatter_lanes(uint64_t (&v)[M], uint3
   return r;
 }
 
+// Consumer warps of an attention stage: only the rows this block's head
+// group reads must be written: the group's q rows (HPC heads) and its kv
+// head's K and V rows at position p, (HPC + 2) D / 16 tile groups of the
+// q|k|v product, each counted on gready once its rows are stored (a release
+// add after the stores; the poll acquires). Earlier stages are ordered
+// before through the blocks that wrote those rows (each waited for the
+// stage before its own).
+template <uint32_t HPC>
+__device__ __forceinline__ void step_attn_wait(const StepArgs& A, uint32_t k, uint32_t layer, uint32_t p);
+
 // This block's share of the attention of a decode pass: the head group and
 // the chunk [r0, r1) of positions [0, p] (empty when r0 = p + 1); rows
 // [r0, rc), rc = max(r0, min(r1, p)) (written by earlier passes) travel
@@ -455,6 +468,17 @@ __device__ __forceinline__ AttnChunk attn_chunk(const StepArgs& A, uint32_t p) {
 // the group's query rows and row p's keys (HPC + 1 rows, kv_pitch apart).
 __host__ __device__ inline uint32_t step_attn_q_offset(uint32_t span_max, uint32_t hpc) {
   return round_up(round_up(span_max * hpc * 4, 16) + span_max * hpc * 8, 16);
+}
+
+template <uint32_t HPC>
+__device__ __forceinline__ void step_attn_wait(const StepArgs& A, uint32_t k, uint32_t layer, uint32_t p) {
+  const AttnChunk c = attn_chunk<HPC>(A, p);
+  if (threadIdx.x == 0) {
+    if (c.active)
+      step_poll(A.gready + (size_t)layer * (A.heads / HPC) + c.grp, (HPC + 2) * A.d / kQ8TileRows, A.fault);
+    step_stamp(A, k, 0);
+  }
+  part_sync<kStepConsumers>();
 }
 
 // Key and value rows sit in a ring slot 4 D + 16 bytes apart: lane l of a warp
@@ -607,7 +631,10 @@ __device__ __forceinline__ void step_attention(const StepArgs& A, uint32_t k, ui
     const int32_t mx = best_key_value(sh.gbest[my_h]);
     uint64_t e = 0;
     for (uint32_t el = tid; el < cnt * HPC; el += kStepConsumers) {
-      const uint64_t term = (uint64_t)softmax_exp_term_act(sw[el], mx);
+      // softmax_exp_term_act(sw[el], mx) from the table (filled by that function)
+      const int32_t dist = sub_sat(sw[el], mx);  // <= 0: mx is the maximum
+      const uint32_t back = (uint32_t)(-(int64_t)dist);
+      const uint64_t term = dist >= 0 ? (uint64_t)1 << 32 : back < kExpTerms ? (uint64_t)__ldg(A.exp_terms + back) : 0;
       tm[el] = term;
       e += term;
     }
@@ -820,7 +847,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) decode_step_kernel(const StepA
       continue;
     }
     if (st.kind == STEP_ATTN) {
-      step_wait(A, k);
+      step_attn_wait<HPC>(A, k, st.layer, p);
       step_attention<PER, HPC>(A, k, st.layer, p, planes, ash, ring, cc, stalled);
       step_consumers_arrive(A, k);
       continue;

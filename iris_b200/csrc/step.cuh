@@ -59,6 +59,7 @@ struct StepArgs {
   int32_t* kcache;       // [layers][cap][kvd]
   int32_t* vcache;
   uint32_t cap;
+  uint32_t layers;       // model layers
   int32_t* logits;       // [V]
   unsigned long long* best;
   unsigned long long* split_acc;
@@ -70,6 +71,9 @@ struct StepArgs {
   int32_t* wsum;
   int64_t* acc;
   unsigned int* gbar;
+  const uint32_t* exp_terms;  // exp_term_table
+  unsigned int* gready;  // [layers][heads / hpc] q|k|v tile groups stored for each attention group (zero between launches)
+  uint32_t hpc;          // query heads an attention group
   uint32_t chunks;       // blocks a head group
   uint32_t span_max;     // positions a block at most
   // bookkeeping of the greedy loop
