@@ -9,6 +9,7 @@
 // library precomputes tables and how the CPU tests check these functions
 // against the oracle without a GPU.
 #pragma once
+#include <math.h>
 #include <stdint.h>
 
 #if defined(__CUDACC__)
@@ -163,6 +164,34 @@ IRIS_HD int32_t inv_sqrt_acc(int64_t xs) {
     else high = mid - 1;
   }
   return inv_sqrt_pick(low, x);
+}
+// inv_sqrt_acc from a double-precision estimate of 2^32 / sqrt(x), moved to
+// the exact largest c with c^2 x <= 2^64 by exact tests (the estimate is
+// within one of it: x < 2^63 and the double's 53-bit rounding), then the
+// same tie-break; the binary search of inv_sqrt_acc if the steps ever fail.
+IRIS_HD int32_t inv_sqrt_acc_fast(int64_t xs) {
+  if (xs <= 0) return INT32_MAX;
+  const uint64_t x = (uint64_t)xs;
+  if (inv_sqrt_le_target((uint32_t)INT32_MAX, x)) return INT32_MAX;
+  const double est = 4294967296.0 / sqrt((double)x);
+  uint32_t c = est >= 2147483646.0 ? 2147483646u : (uint32_t)est;
+  for (int i = 0; i < 4 && !inv_sqrt_le_target(c, x); ++i) --c;
+  for (int i = 0; i < 4 && inv_sqrt_le_target(c + 1, x); ++i) ++c;
+  if (!inv_sqrt_le_target(c, x) || inv_sqrt_le_target(c + 1, x)) return inv_sqrt_acc(xs);
+  return inv_sqrt_pick(c, x);
+}
+// n / d rounded half to even for d >= 1, with the power-of-two divisors
+// (the models' widths) as a shift.
+IRIS_HD uint64_t div_round_even_width(uint64_t n, uint32_t d) {
+  if (d >= 2 && (d & (d - 1)) == 0) {
+    int s = 0;
+    while ((1u << s) != d) ++s;
+    uint64_t q = n >> s;
+    const uint64_t r = n & (d - 1), half = d >> 1;
+    if (r > half || (r == half && (q & 1))) ++q;
+    return q;
+  }
+  return div_round_even_u64(n, d);
 }
 // rms_norm_scale (ops.rs:409-428) from the saturated sum of squares.
 IRIS_HD int32_t rms_scale_from_sumsq(uint64_t sumsq_sat, uint32_t n, int64_t eps) {

@@ -101,7 +101,7 @@ __device__ __forceinline__ bool row_to_planes(const int32_t* x, const int32_t* _
     }
     uint64_t total = block_sum_sat<NT>(ss, red);  // in every lane of warp 0
     if (threadIdx.x < 32) {  // rms_scale_from_sumsq with the warp-parallel inverse square root
-      const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), eps));
+      const int32_t sc = inv_sqrt_acc_fast(acc_add_sat((int64_t)div_round_even_width(total, K), eps));
       if (threadIdx.x == 0) *s_scale = sc;
     }
     part_sync<NT>();

@@ -159,7 +159,7 @@ __device__ __forceinline__ bool step_norm_planes(const StepArgs& A, uint32_t k, 
     for (uint32_t b = threadIdx.x; b < gridDim.x; b += 32) acc128_add(t, __ldcg(slots + b), 0);
     t = warp_sum_acc128(t);
     const uint64_t total = (t.hi || t.lo > (uint64_t)INT64_MAX) ? (uint64_t)INT64_MAX : t.lo;
-    const int32_t sc = inv_sqrt_acc_warp(acc_add_sat((int64_t)div_round_even_u64(total, K), A.eps));
+    const int32_t sc = inv_sqrt_acc_fast(acc_add_sat((int64_t)div_round_even_width(total, K), A.eps));
     if (threadIdx.x == 0) *s_scale = sc;
   }
   part_sync<kStepConsumers>();

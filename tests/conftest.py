@@ -41,6 +41,9 @@ def detnum_shim(tmp_path_factory):
         "shim_mul_sat": (C.c_int32, [C.c_int32, C.c_int32]),
         "shim_div_act": (C.c_int32, [C.c_int32, C.c_int32]),
         "shim_inv_sqrt_acc": (C.c_int32, [C.c_int64]),
+        "shim_inv_sqrt_acc_fast": (C.c_int32, [C.c_int64]),
+        "shim_div_round_even_width": (C.c_uint64, [C.c_uint64, C.c_uint32]),
+        "shim_div_round_even_u64": (C.c_uint64, [C.c_uint64, C.c_uint64]),
         "shim_rms_scale": (C.c_int32, [i32p, C.c_uint32, C.c_int64]),
         "shim_silu": (C.c_int32, [C.c_int32]),
         "shim_sin_cos_q30": (None, [C.c_int64, i64p, i64p]),

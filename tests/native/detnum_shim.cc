@@ -17,6 +17,9 @@ int32_t shim_requantize(int64_t x) { return requantize(x); }
 int32_t shim_mul_sat(int32_t a, int32_t b) { return mul_sat(a, b); }
 int32_t shim_div_act(int32_t a, int32_t b) { return div_act(a, b); }
 int32_t shim_inv_sqrt_acc(int64_t x) { return inv_sqrt_acc(x); }
+int32_t shim_inv_sqrt_acc_fast(int64_t x) { return inv_sqrt_acc_fast(x); }
+uint64_t shim_div_round_even_width(uint64_t n, uint32_t d) { return div_round_even_width(n, d); }
+uint64_t shim_div_round_even_u64(uint64_t n, uint64_t d) { return div_round_even_u64(n, d); }
 int32_t shim_rms_scale(const int32_t* v, uint32_t n, int64_t eps) {
   uint64_t s = 0;
   for (uint32_t i = 0; i < n; ++i) s = add_sat_nonneg(s, (uint64_t)((int64_t)v[i] * v[i]));

@@ -87,6 +87,27 @@ def test_inv_sqrt_and_rms_scale(S, L):
         O.ptr(big, C.c_int32), 4096, 0)
 
 
+def test_fast_inv_sqrt_and_width_division(S, L):
+    """The norm prologues' inverse square root from a double estimate with
+    exact steps, and the division by a power-of-two width as a shift, equal
+    the oracle's binary search and the general rounded division."""
+    rng = np.random.default_rng(21)
+    xs = [0, 1, 2, 3, 4, 5, 42950, 4295, 2**32 - 1, 2**32, 2**32 + 1, 2**62, 2**63 - 1, 7, 1 << 20,
+          (2**31 - 1) ** 2, (2**31 - 1) ** 2 - 1, 3 * 2**30, 2**34 - 1]
+    xs += rng.integers(1, 2**63 - 1, size=20000, dtype=np.int64).tolist()
+    xs += (2 ** rng.uniform(0, 63, size=20000)).astype(np.int64).clip(1, 2**63 - 1).tolist()
+    sq = rng.integers(1, 2**31, size=5000, dtype=np.int64)  # around exact squares of the targets
+    xs += [int(v) for c in sq for v in ((2**64 // (int(c) * int(c))), (2**64 // (int(c) * int(c))) + 1)
+           if 0 < v < 2**63]
+    for x in xs:
+        assert S.shim_inv_sqrt_acc_fast(x) == L.oracle_inv_sqrt_acc(x), x
+    for d in [1, 2, 3, 64, 96, 128, 2048, 4096, 14336, 16384, 1 << 20]:
+        ns = [0, 1, d // 2, d // 2 + 1, d - 1, d, d + d // 2, 3 * d + d // 2, 2**64 - 1, 2**63]
+        ns += rng.integers(0, 2**63, size=300, dtype=np.int64).tolist()
+        for n in ns:
+            assert S.shim_div_round_even_width(n, d) == S.shim_div_round_even_u64(n, d), (n, d)
+
+
 def test_mistral_functions(S, L):
     rng = np.random.default_rng(3)
     for x in EDGE32 + rand32(rng, 5000) + rand32(rng, 5000, 22):
