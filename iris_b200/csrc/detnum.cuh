@@ -273,6 +273,27 @@ IRIS_HD int32_t acc128_round_q24(Acc128 a) {
   if (fhi < -1 || (fhi == -1 && flo < 0xFFFFFFFF80000000ull)) return INT32_MIN;
   return (int32_t)(int64_t)flo;
 }
+// acc128_round_q24 of the exact product x m 2^e (|m| < 2^11, 0 <= e <= 29):
+// the one-plane GEMM's row value. In 64 bits when |x m| < 2^62 (a rounding
+// shift right by 24 - e, or a shift left by e - 24 that saturates), else
+// through the 128-bit sum of the two halves of x.
+IRIS_HD int32_t round_q24_scaled(int64_t x, int32_t m, int32_t e) {
+  const int64_t p = (int64_t)((uint64_t)x * (uint64_t)(int64_t)m);  // the low half
+  const int64_t ph = mulhi_s64(x, (int64_t)m);
+  if (ph == (p >> 63) && p > -((int64_t)1 << 62) && p < ((int64_t)1 << 62)) {
+    if (e < 24) return clamp_i32(shift_round_even(p, 24 - e));
+    if (e == 24) return clamp_i32(p);
+    const int s = e - 24;
+    if (p > ((int64_t)INT32_MAX >> s)) return INT32_MAX;
+    if (p < ((int64_t)INT32_MIN >> s)) return INT32_MIN;
+    return (int32_t)(p << s);
+  }
+  Acc128 t{0, 0};
+  acc128_add_shifted(t, (int64_t)(x & 0xFFFFFFFFll) * m, e);
+  acc128_add_shifted(t, (x >> 32) * m, e + 32);
+  return acc128_round_q24(t);
+}
+
 // One dequantized weight (dequantize_row, q8.rs:76-91): q * scale / 2^8, ties
 // to even, saturated (|q * scale| < 2^47, so it is exact in 64 bits).
 IRIS_HD int32_t q8_dequant(int8_t q, int32_t m, int32_t e) {

@@ -270,6 +270,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (uint32_t c = 0; c < 8; ++c) {
+          if constexpr (P == 1 && EPI != EPI_PARTIAL) {  // the rounded value in 64 bits where it fits
+            const int64_t x = (int64_t)(int32_t)r[0][c] + (int64_t)(int32_t)r[1][c] * 256 +
+                              (int64_t)(int32_t)r[2][c] * 65536 + (int64_t)(int32_t)r[3][c] * 16777216;
+            v[h * 8 + c] = round_q24_scaled(x, mant, shift);
+            continue;
+          }
           const Acc128 tot = tc_total<P>(r, c, lo_bound, shift, mant);
           if (EPI == EPI_PARTIAL) {
             const uint32_t tok = m0 + c0 + c;

@@ -42,6 +42,8 @@ def detnum_shim(tmp_path_factory):
         "shim_div_act": (C.c_int32, [C.c_int32, C.c_int32]),
         "shim_inv_sqrt_acc": (C.c_int32, [C.c_int64]),
         "shim_inv_sqrt_acc_fast": (C.c_int32, [C.c_int64]),
+        "shim_round_q24_scaled": (C.c_int32, [C.c_int64, C.c_int32, C.c_int32]),
+        "shim_round_q24_scaled_ref": (C.c_int32, [C.c_int64, C.c_int32, C.c_int32]),
         "shim_div_round_even_width": (C.c_uint64, [C.c_uint64, C.c_uint32]),
         "shim_div_round_even_u64": (C.c_uint64, [C.c_uint64, C.c_uint64]),
         "shim_rms_scale": (C.c_int32, [i32p, C.c_uint32, C.c_int64]),

@@ -18,6 +18,14 @@ int32_t shim_mul_sat(int32_t a, int32_t b) { return mul_sat(a, b); }
 int32_t shim_div_act(int32_t a, int32_t b) { return div_act(a, b); }
 int32_t shim_inv_sqrt_acc(int64_t x) { return inv_sqrt_acc(x); }
 int32_t shim_inv_sqrt_acc_fast(int64_t x) { return inv_sqrt_acc_fast(x); }
+int32_t shim_round_q24_scaled(int64_t x, int32_t m, int32_t e) { return round_q24_scaled(x, m, e); }
+// the 128-bit formulation the GEMM's one-plane epilogue used (two halves of x)
+int32_t shim_round_q24_scaled_ref(int64_t x, int32_t m, int32_t e) {
+  Acc128 t{0, 0};
+  acc128_add_shifted(t, (int64_t)(x & 0xFFFFFFFFll) * m, e);
+  acc128_add_shifted(t, (x >> 32) * m, e + 32);
+  return acc128_round_q24(t);
+}
 uint64_t shim_div_round_even_width(uint64_t n, uint32_t d) { return div_round_even_width(n, d); }
 uint64_t shim_div_round_even_u64(uint64_t n, uint64_t d) { return div_round_even_u64(n, d); }
 int32_t shim_rms_scale(const int32_t* v, uint32_t n, int64_t eps) {

@@ -108,6 +108,20 @@ def test_fast_inv_sqrt_and_width_division(S, L):
             assert S.shim_div_round_even_width(n, d) == S.shim_div_round_even_u64(n, d), (n, d)
 
 
+def test_one_plane_row_rounding(S):
+    """The one-plane GEMM's rounding of x m 2^e in 64 bits equals the
+    128-bit formulation: every exponent, both signs, ties, saturation and the
+    products past 2^62 that take the 128-bit path."""
+    rng = np.random.default_rng(33)
+    xs = rng.integers(-(2**56), 2**56, size=4000, dtype=np.int64).tolist()
+    xs += (rng.choice([-1, 1], size=4000) * (2 ** rng.uniform(0, 56, size=4000))).astype(np.int64).tolist()
+    xs += [0, 1, -1, 2**23, -(2**23), 2**24 + 2**23, 3 * 2**23, -(3 * 2**23), 2**55, -(2**55), 2**56 - 1]
+    for x in xs:
+        for m in (1, -1, 1024, 2047, -2047, int(rng.integers(-2047, 2048))):
+            for e in (0, 1, 12, 23, 24, 25, 29, int(rng.integers(0, 30))):
+                assert S.shim_round_q24_scaled(x, m, e) == S.shim_round_q24_scaled_ref(x, m, e), (x, m, e)
+
+
 def test_mistral_functions(S, L):
     rng = np.random.default_rng(3)
     for x in EDGE32 + rand32(rng, 5000) + rand32(rng, 5000, 22):
