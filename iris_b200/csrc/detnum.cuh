@@ -193,11 +193,6 @@ IRIS_HD uint64_t div_round_even_width(uint64_t n, uint32_t d) {
   }
   return div_round_even_u64(n, d);
 }
-// rms_norm_scale (ops.rs:409-428) from the saturated sum of squares.
-IRIS_HD int32_t rms_scale_from_sumsq(uint64_t sumsq_sat, uint32_t n, int64_t eps) {
-  int64_t mean = (int64_t)div_round_even_u64(sumsq_sat, n);
-  return inv_sqrt_acc(acc_add_sat(mean, eps));
-}
 
 // ---- Q8_0 (q8.rs) ---------------------------------------------------------
 
@@ -273,6 +268,12 @@ IRIS_HD int32_t acc128_round_q24(Acc128 a) {
   if (fhi < -1 || (fhi == -1 && flo < 0xFFFFFFFF80000000ull)) return INT32_MIN;
   return (int32_t)(int64_t)flo;
 }
+// rms_norm_scale (ops.rs:409-428) from the saturated sum of squares.
+IRIS_HD int32_t rms_scale_from_sumsq(uint64_t sumsq_sat, uint32_t n, int64_t eps) {
+  int64_t mean = (int64_t)div_round_even_width(sumsq_sat, n);
+  return inv_sqrt_acc_fast(acc_add_sat(mean, eps));
+}
+
 // acc128_round_q24 of the exact product x m 2^e (|m| < 2^11, 0 <= e <= 29):
 // the one-plane GEMM's row value. In 64 bits when |x m| < 2^62 (a rounding
 // shift right by 24 - e, or a shift left by e - 24 that saturates), else
