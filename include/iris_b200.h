@@ -420,6 +420,11 @@ int iris_session_range_layer(IrisSession* session, uint32_t layer, int32_t* rows
  * digest is taken on the host (the two-level canonical record). */
 int iris_session_range_layer_leaves(IrisSession* session, uint32_t layer, uint32_t leaf_bytes, uint8_t* leaves_out,
                                     uint32_t* ticket);
+/* The next `count` layers of the range (count <= 64) in one call, as
+ * iris_session_range_layer_leaves each: leaves_out[i] and tickets[i] are
+ * layer i's (fewer host calls a range). */
+int iris_session_range_layers_leaves(IrisSession* session, uint32_t count, uint32_t leaf_bytes,
+                                     uint8_t* const* leaves_out, uint32_t* tickets);
 int iris_session_ticket_wait(IrisSession* session, uint32_t ticket);
 int iris_session_range_end(IrisSession* session, uint32_t* token_ids, int32_t* values);
 /* Page-locked host memory for the copies above (cudaHostAlloc). */

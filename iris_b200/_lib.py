@@ -129,6 +129,8 @@ SIGNATURES = {
     "iris_session_range_begin": (C.c_int, [vp, C.POINTER(C.c_uint32), C.c_uint32]),
     "iris_session_range_layer": (C.c_int, [vp, C.c_uint32, vp, vp, vp, C.POINTER(C.c_uint32)]),
     "iris_session_range_layer_leaves": (C.c_int, [vp, C.c_uint32, C.c_uint32, vp, C.POINTER(C.c_uint32)]),
+    "iris_session_range_layers_leaves": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.POINTER(vp),
+                                                   C.POINTER(C.c_uint32)]),
     "iris_session_ticket_wait": (C.c_int, [vp, C.c_uint32]),
     "iris_session_range_end": (C.c_int, [vp, C.POINTER(C.c_uint32), i32p]),
     "iris_host_alloc": (C.c_int, [C.c_uint64, C.POINTER(vp)]),

@@ -1474,6 +1474,16 @@ int iris_session_range_layer_leaves(IrisSession* s, uint32_t layer, uint32_t lea
   return range_layer(s, layer, nullptr, nullptr, nullptr, leaf_bytes, leaves_out, ticket);
 }
 
+int iris_session_range_layers_leaves(IrisSession* s, uint32_t count, uint32_t leaf_bytes, uint8_t* const* leaves_out,
+                                     uint32_t* tickets) {
+  if (!s || !leaves_out || !tickets || count > kChainTickets) return IRIS_EINVAL;
+  for (uint32_t i = 0; i < count; ++i) {
+    const int rc = iris_session_range_layer_leaves(s, s->range_layer, leaf_bytes, leaves_out[i], tickets + i);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
 int iris_session_ticket_wait(IrisSession* s, uint32_t ticket) {
   if (!s) return IRIS_EINVAL;
   const uint32_t issued = s->next_ticket.load();

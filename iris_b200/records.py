@@ -200,7 +200,9 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
         raise ValueError("ranges hold 1 to 512 rows")
     kvd = cfg.kv_heads * cfg.head_dim
     stage_name = "prefill_range" if cfg.family == "gemma" else "layer_mistral"
-    if device_hash:
+    if device_hash:  # a range's layers are issued in batches of up to 32 (a session keeps 64 tickets)
+        batch = min(cfg.layers, 32)
+        slots = max(slots, 2 * batch)
         nleaves = leaf_count(range_size * cfg.hidden * 4) + 2 * leaf_count(range_size * kvd * 4)
         sets = [(_Pinned((nleaves * 32,), np.uint8),) for _ in range(slots)]
     else:
@@ -229,22 +231,33 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
                 n = len(part)
                 _lib.check(L.iris_session_range_begin(session.handle, _lib.ptr(part, C.c_uint32), n),
                            "iris_session_range_begin")
-                for layer in range(cfg.layers):
-                    slot = j % slots
-                    if busy[slot] is not None:
-                        busy[slot].result()  # the set's previous record is hashed
-                    ticket = C.c_uint32()
-                    if device_hash:
-                        _lib.check(L.iris_session_range_layer_leaves(session.handle, layer, LEAF, sets[slot][0].ptr,
-                                                                     C.byref(ticket)),
-                                   "iris_session_range_layer_leaves")
-                    else:
+                if device_hash:
+                    for first in range(0, cfg.layers, batch):
+                        cnt = min(batch, cfg.layers - first)
+                        use = [(j + i) % slots for i in range(cnt)]
+                        for slot in use:
+                            if busy[slot] is not None:
+                                busy[slot].result()  # the set's previous record is hashed
+                        ptrs = (C.c_void_p * cnt)(*[sets[slot][0].ptr for slot in use])
+                        tickets = (C.c_uint32 * cnt)()
+                        _lib.check(L.iris_session_range_layers_leaves(session.handle, cnt, LEAF, ptrs, tickets),
+                                   "iris_session_range_layers_leaves")
+                        for i, slot in enumerate(use):
+                            busy[slot] = pool.submit(digest, slot, tickets[i], f"{stage_name}/{first + i}", start, n)
+                            jobs.append(busy[slot])
+                        j += cnt
+                else:
+                    for layer in range(cfg.layers):
+                        slot = j % slots
+                        if busy[slot] is not None:
+                            busy[slot].result()  # the set's previous record is hashed
+                        ticket = C.c_uint32()
                         r, k, v = sets[slot]
                         _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
                                                               C.byref(ticket)), "iris_session_range_layer")
-                    busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
-                    jobs.append(busy[slot])
-                    j += 1
+                        busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
+                        jobs.append(busy[slot])
+                        j += 1
                 _lib.check(L.iris_session_range_end(session.handle, _lib.ptr(selected[off:off + n], C.c_uint32),
                                                     _lib.ptr(scores[off:off + n], C.c_int32)),
                            "iris_session_range_end")
