@@ -419,6 +419,11 @@ class Session:
         return k, v
 
     def close(self) -> None:
+        for sets in getattr(self, "_pinned_sets", {}).values():  # records.chain_claim's buffers
+            for group in sets:
+                for b in group:
+                    b.free()
+        self._pinned_sets = {}
         if self._h:
             lib().iris_session_free(self._h)
             self._h = C.c_void_p()

@@ -208,11 +208,19 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
     if device_hash:  # a range's layers are issued in batches of up to 32 (a session keeps 64 tickets)
         batch = min(cfg.layers, 32)
         slots = max(slots, 2 * batch)
-        nleaves = leaf_count(range_size * cfg.hidden * 4) + 2 * leaf_count(range_size * kvd * 4)
-        sets = [(_Pinned((nleaves * 32,), np.uint8),) for _ in range(slots)]
-    else:
-        sets = [(_Pinned((range_size, cfg.hidden)), _Pinned((range_size, kvd)), _Pinned((range_size, kvd)))
-                for _ in range(slots)]
+    # page-locked buffer sets, kept on the session for its next claims (pinning
+    # host pages can take long; Session.close frees them)
+    cache = session.__dict__.setdefault("_pinned_sets", {})
+    key = (device_hash, range_size, slots)
+    sets = cache.get(key)
+    if sets is None:
+        if device_hash:
+            nleaves = leaf_count(range_size * cfg.hidden * 4) + 2 * leaf_count(range_size * kvd * 4)
+            sets = [(_Pinned((nleaves * 32,), np.uint8),) for _ in range(slots)]
+        else:
+            sets = [(_Pinned((range_size, cfg.hidden)), _Pinned((range_size, kvd)), _Pinned((range_size, kvd)))
+                    for _ in range(slots)]
+        cache[key] = sets
     busy = [None] * slots
     ids = np.ascontiguousarray(ids, np.uint32)
     selected = np.empty(len(ids), np.uint32)
@@ -227,48 +235,43 @@ def chain_claim(session, ids: Sequence[int], range_size: int = 512, slots: int =
         r, k, v = sets[slot]
         return name, start, stage_digest(name, start, r.a[:n], k.a[:n], v.a[:n])
 
-    try:
-        with ThreadPoolExecutor(max_workers=workers) as pool:
-            j, base = 0, session.length
-            for start in range(base, base + len(ids), range_size):
-                off = start - base
-                part = ids[off:off + range_size]
-                n = len(part)
-                _lib.check(L.iris_session_range_begin(session.handle, _lib.ptr(part, C.c_uint32), n),
-                           "iris_session_range_begin")
-                if device_hash:
-                    for first in range(0, cfg.layers, batch):
-                        cnt = min(batch, cfg.layers - first)
-                        use = [(j + i) % slots for i in range(cnt)]
-                        for slot in use:
-                            if busy[slot] is not None:
-                                busy[slot].result()  # the set's previous record is hashed
-                        ptrs = (C.c_void_p * cnt)(*[sets[slot][0].ptr for slot in use])
-                        tickets = (C.c_uint32 * cnt)()
-                        _lib.check(L.iris_session_range_layers_leaves(session.handle, cnt, LEAF, ptrs, tickets),
-                                   "iris_session_range_layers_leaves")
-                        for i, slot in enumerate(use):
-                            busy[slot] = pool.submit(digest, slot, tickets[i], f"{stage_name}/{first + i}", start, n)
-                            jobs.append(busy[slot])
-                        j += cnt
-                else:
-                    for layer in range(cfg.layers):
-                        slot = j % slots
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        j, base = 0, session.length
+        for start in range(base, base + len(ids), range_size):
+            off = start - base
+            part = ids[off:off + range_size]
+            n = len(part)
+            _lib.check(L.iris_session_range_begin(session.handle, _lib.ptr(part, C.c_uint32), n),
+                       "iris_session_range_begin")
+            if device_hash:
+                for first in range(0, cfg.layers, batch):
+                    cnt = min(batch, cfg.layers - first)
+                    use = [(j + i) % slots for i in range(cnt)]
+                    for slot in use:
                         if busy[slot] is not None:
                             busy[slot].result()  # the set's previous record is hashed
-                        ticket = C.c_uint32()
-                        r, k, v = sets[slot]
-                        _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
-                                                              C.byref(ticket)), "iris_session_range_layer")
-                        busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
+                    ptrs = (C.c_void_p * cnt)(*[sets[slot][0].ptr for slot in use])
+                    tickets = (C.c_uint32 * cnt)()
+                    _lib.check(L.iris_session_range_layers_leaves(session.handle, cnt, LEAF, ptrs, tickets),
+                               "iris_session_range_layers_leaves")
+                    for i, slot in enumerate(use):
+                        busy[slot] = pool.submit(digest, slot, tickets[i], f"{stage_name}/{first + i}", start, n)
                         jobs.append(busy[slot])
-                        j += 1
-                _lib.check(L.iris_session_range_end(session.handle, _lib.ptr(selected[off:off + n], C.c_uint32),
-                                                    _lib.ptr(scores[off:off + n], C.c_int32)),
-                           "iris_session_range_end")
-            records = [f.result() for f in jobs]
-    finally:
-        for trio in sets:
-            for b in trio:
-                b.free()
+                    j += cnt
+            else:
+                for layer in range(cfg.layers):
+                    slot = j % slots
+                    if busy[slot] is not None:
+                        busy[slot].result()  # the set's previous record is hashed
+                    ticket = C.c_uint32()
+                    r, k, v = sets[slot]
+                    _lib.check(L.iris_session_range_layer(session.handle, layer, r.ptr, k.ptr, v.ptr,
+                                                          C.byref(ticket)), "iris_session_range_layer")
+                    busy[slot] = pool.submit(digest, slot, ticket.value, f"{stage_name}/{layer}", start, n)
+                    jobs.append(busy[slot])
+                    j += 1
+            _lib.check(L.iris_session_range_end(session.handle, _lib.ptr(selected[off:off + n], C.c_uint32),
+                                                _lib.ptr(scores[off:off + n], C.c_int32)),
+                       "iris_session_range_end")
+        records = [f.result() for f in jobs]
     return records, selected, scores
