@@ -87,7 +87,11 @@ int iris_q8_product_device(const Q8GpuMatrix* matrix, const int32_t* d_activatio
  * weight (twelve). IRIS_PATH_TC3 builds and uses the 3-byte form in any case
  * (measurement; it fails if another form was built first). IRIS_PATH_TC or
  * IRIS_PATH_TC3 on a matrix that does not qualify fails with
- * cudaErrorInvalidValue. */
+ * cudaErrorInvalidValue. IRIS_PATH_GEMV1 forces the decode GEMV's
+ * one-scale-a-row form (int32 plane sums over a tile group, each row scaled
+ * once: the form a session's one-token products take for such matrices);
+ * tokens must be 1, every row must have one scale and cols <= 32768, else it
+ * fails with cudaErrorInvalidValue. */
 int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_activations,
                                 uint32_t tokens, int32_t* d_out, void* stream, int path);
 #define IRIS_PATH_AUTO 0
@@ -95,6 +99,7 @@ int iris_q8_product_device_path(const Q8GpuMatrix* matrix, const int32_t* d_acti
 #define IRIS_PATH_GEMM 2
 #define IRIS_PATH_TC 3
 #define IRIS_PATH_TC3 4
+#define IRIS_PATH_GEMV1 5
 /* No counterpart in the reference. The same product as
  * iris_q8_product_device, allocating nothing: the GEMM path's byte planes
  * live in a fixed 16 MiB device array, so tokens > 1 needs

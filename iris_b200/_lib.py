@@ -17,7 +17,7 @@ LIB_PATH = PKG / "libiris_b200.so"
 IRIS_EINVAL, IRIS_ESCALE, IRIS_ERANGE, IRIS_ESTATE, IRIS_EWINDOW, IRIS_ESTALL = 10001, 10002, 10003, 10004, 10005, 10006
 IRIS_ESCRATCH = 10007
 NOALLOC_PLANES_BYTES = 16 << 20
-PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_TC, PATH_TC3 = 0, 1, 2, 3, 4
+PATH_AUTO, PATH_GEMV, PATH_GEMM, PATH_TC, PATH_TC3, PATH_GEMV1 = 0, 1, 2, 3, 4, 5
 GEMM_AUTO, GEMM_MMA = 0, 1
 ATTN_AUTO, ATTN_SPLIT, ATTN_CLUSTER = 0, 1, 2
 DECODE_AUTO, DECODE_GRAPH, DECODE_STEP = 0, 1, 2

@@ -1110,14 +1110,18 @@ int iris_q8_upload_blocks(const uint8_t* blocks, uint32_t rows, uint32_t cols,
 int iris_q8_product_device_path(const Q8GpuMatrix* m, const int32_t* d_act, uint32_t tokens,
                                 int32_t* d_out, void* stream, int path) {
   if (!m || tokens == 0) return tokens == 0 ? 0 : IRIS_EINVAL;
-  if (path < IRIS_PATH_AUTO || path > IRIS_PATH_TC3) return IRIS_EINVAL;
+  if (path < IRIS_PATH_AUTO || path > IRIS_PATH_GEMV1) return IRIS_EINVAL;
   cudaStream_t s = (cudaStream_t)stream;
   bool gemv = (tokens == 1 && path != IRIS_PATH_GEMM && path != IRIS_PATH_TC && path != IRIS_PATH_TC3) ||
-              path == IRIS_PATH_GEMV;
+              path == IRIS_PATH_GEMV || path == IRIS_PATH_GEMV1;
   if (gemv) {
     ProductArgs a = product_args(m, tokens);
     a.out = d_out;
     a.x = d_act;
+    if (path == IRIS_PATH_GEMV1) {
+      if (tokens != 1 || !q8_uniform_cached(const_cast<Q8GpuMatrix*>(m), s)) return (int)cudaErrorInvalidValue;
+      a.uniform = 1;
+    }
     return (int)launch_product(a, IN_RAW, EPI_STORE, s, IRIS_PATH_GEMV);
   }
   cudaError_t e = prepare_tc_for(m, tokens, path, s);

@@ -15,6 +15,11 @@ the copy are covered:
   a row, rows with no non-zero scale, extreme weights and activations (totals
   that saturate), ragged shapes, K = 18848, 2048 tokens against the mma.sync
   GEMM, and the three-plane form of the same matrices.
+
+The decode GEMV's one-scale-a-row form (one token; int32 plane sums over a
+tile group, each row scaled once) is checked against the oracle and the
+general GEMV over slice widths of 96 to 2048 columns and K up to 32768, with
+extreme weights, scales and activations, and its refusals.
 """
 import ctypes as C
 
@@ -262,3 +267,81 @@ def test_one_plane_is_built_and_equals_three_planes_and_mma(L, O):
     assert np.array_equal(one, mma) and np.array_equal(three, mma)
     sample = rng.choice(tokens, size=24, replace=False)
     assert np.array_equal(one[sample], O.linear(acts[sample], blocks, rows))
+
+
+# ---- the decode GEMV's one-scale-a-row form (mma.sync on the byte planes) ----
+
+def strict_row_matrix(rng, rows, cols, q_extreme=False, exponents=(0, 30)):
+    """Q8_0 blocks where every block of a row has the same scale bits (the
+    decode GEMV's one-scale-a-row condition): random signs, exponents and
+    mantissas, row 0 at the largest finite scale (65504), row 1 subnormal,
+    rows 2 and 3 at +0 and -0."""
+    nb_row = cols // 32
+    ex = rng.integers(exponents[0], exponents[1] + 1, size=rows)
+    bits = (rng.integers(0, 2, size=rows) << 15) | (ex << 10) | rng.integers(0, 1024, size=rows)
+    bits[0] = 0x7BFF
+    if rows > 3:
+        bits[1], bits[2], bits[3] = 0x03FF, 0x0000, 0x8000
+    per_block = np.repeat(bits, nb_row)
+    nb = rows * nb_row
+    out = np.empty((nb, 34), np.uint8)
+    out[:, 0] = per_block & 0xFF
+    out[:, 1] = (per_block >> 8) & 0xFF
+    if q_extreme:
+        out[:, 2:] = np.where(rng.integers(0, 2, size=(nb, 32)) == 1, 0x7F, 0x80)
+    else:
+        out[:, 2:] = rng.integers(0, 256, size=(nb, 32), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("rows,cols", [
+    (256, 4096),    # two 2048-column slices a tile group
+    (100, 14336),   # seven slices, ragged rows
+    (64, 3072),     # 1024-column slices
+    (48, 384),      # one 384-column slice
+    (40, 96),       # one 96-column slice: three blocks a row
+    (32, 32768),    # the widest K
+    (16, 2048),
+])
+def test_gemv_one_scale_a_row_matches_oracle(L, O, rows, cols):
+    """The one-token product in the one-scale-a-row form against the oracle
+    and against the general GEMV: full-range activations (all four byte
+    planes, i32::MIN / MAX mixed in) and activations within 24 bits."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(rows * 3 + cols)
+    blocks = strict_row_matrix(rng, rows, cols)
+    for acts in (full_range_acts(rng, 1, cols), rng.integers(-(2**23), 2**23, size=(1, cols)).astype(np.int32)):
+        want = O.linear(acts, blocks, rows)
+        rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_GEMV1)
+        assert rc == 0, _lib.lib().iris_error(rc)
+        assert np.array_equal(got, want), np.argwhere(got != want)[:5]
+        rc, general = run(L, blocks, rows, cols, acts, _lib.PATH_GEMV)
+        assert rc == 0 and np.array_equal(general, want)
+
+
+def test_gemv_one_scale_a_row_extremes(L, O):
+    """q of -128 / 127 under the largest scales against i32::MIN / MAX
+    activations at K = 32768: row sums near 2^53 before the scale, totals far
+    past the int32 output (saturated by the rounding)."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(5)
+    rows, cols = 48, 32768
+    blocks = strict_row_matrix(rng, rows, cols, q_extreme=True, exponents=(28, 30))
+    for acts in (np.full((1, cols), I32_MIN, np.int32), np.full((1, cols), I32_MAX, np.int32),
+                 np.where(rng.integers(0, 2, size=(1, cols)) == 0, I32_MIN, I32_MAX).astype(np.int32)):
+        want = O.linear(acts, blocks, rows)
+        rc, got = run(L, blocks, rows, cols, acts, _lib.PATH_GEMV1)
+        assert rc == 0 and np.array_equal(got, want)
+
+
+def test_gemv_one_scale_a_row_refusals(L):
+    """Rows whose blocks differ in scale, and more than one token, are
+    refused (cudaErrorInvalidValue)."""
+    from iris_b200 import _lib
+    rng = np.random.default_rng(6)
+    mixed = spread_matrix(rng, 32, 2048, 10, 3)
+    rc, _ = run(L, mixed, 32, 2048, full_range_acts(rng, 1, 2048), _lib.PATH_GEMV1)
+    assert rc == 1
+    ok = strict_row_matrix(rng, 32, 2048)
+    rc, _ = run(L, ok, 32, 2048, full_range_acts(rng, 2, 2048), _lib.PATH_GEMV1)
+    assert rc == 1
