@@ -364,14 +364,18 @@ IRIS_HD void sin_cos_q30(int64_t angle, int64_t* sin_out, int64_t* cos_out) {
   *sin_out = ss * s;
   *cos_out = cs * c;
 }
+// A pair rotated by an angle of Q2.30 sine s and cosine c (mistral.rs:120-127).
+IRIS_HD void rotate_pair_sc(int32_t* a, int32_t* b, int64_t s, int64_t c) {
+  int64_t x = *a, y = *b;
+  *a = clamp_i32(shift_round_even(x * c - y * s, 30));
+  *b = clamp_i32(shift_round_even(x * s + y * c, 30));
+}
 // One rotated pair (mistral.rs:114-128); position 0 leaves the pair alone.
 IRIS_HD void rotate_pair_q30(int32_t* a, int32_t* b, int64_t inverse_frequency, uint32_t position) {
   if (position == 0) return;
   int64_t s, c;
   sin_cos_q30((int64_t)position * inverse_frequency, &s, &c);
-  int64_t x = *a, y = *b;
-  *a = clamp_i32(shift_round_even(x * c - y * s, 30));
-  *b = clamp_i32(shift_round_even(x * s + y * c, 30));
+  rotate_pair_sc(a, b, s, c);
 }
 // mistral.rs:130-145 from the wrapping Q32.32 sum.
 IRIS_HD int32_t scaled_score_finish(int64_t sum, uint32_t scale_q32) {

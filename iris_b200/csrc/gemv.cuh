@@ -171,6 +171,28 @@ __device__ __forceinline__ void epi_pair(const ProductArgs& a, uint32_t t, uint3
   }
 }
 
+// The one-token RoPE epilogue with the sines and cosines of the token's
+// position precomputed (sc[i] = sin, cos of frequency i; none at position 0):
+// epi_pair<EPI_QKV_ROPE> for t = 0 with the same rotation.
+__device__ __forceinline__ void epi_pair_rope_sc(const ProductArgs& a, uint32_t pos, uint32_t row, int32_t v0,
+                                                 int32_t v1, const int64_t (*sc)[2]) {
+  if (row < a.qd + a.kvd) {
+    const uint32_t c = row < a.qd ? row : row - a.qd;
+    if (pos) {
+      const uint32_t f = (c % a.head_dim) >> 1;
+      rotate_pair_sc(&v0, &v1, sc[f][0], sc[f][1]);
+    }
+    int32_t* o = row < a.qd ? a.out + row : a.kcache + (size_t)pos * a.kvd + c;
+    o[0] = v0;
+    o[1] = v1;
+  } else {
+    int32_t* o = a.vcache + (size_t)pos * a.kvd + (row - a.qd - a.kvd);
+    o[0] = v0;
+    o[1] = v1;
+  }
+}
+constexpr uint32_t kRopeTablePairs = 128;  // head_dim <= 256
+
 // A finished single-row value for token t; returns the value written.
 template <int EPI>
 __device__ __forceinline__ int32_t epi_single(const ProductArgs& a, uint32_t t, uint32_t row, int32_t v) {
@@ -622,6 +644,18 @@ __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRin
   // coming exchange (epoch + 1)
   int64_t* part = a.partial;
   if (EPI == EPI_PARTIAL && a.xepoch) part += (size_t)((*a.xepoch + 1) & 1) * a.rows * 4;
+  // RoPE: the sine and cosine of every frequency at the token's position,
+  // once a call (the warp computes them while the first groups are consumed)
+  __shared__ int64_t rope_sc[kRopeTablePairs][2];
+  const bool rope_table = EPI == EPI_QKV_ROPE && a.head_dim / 2 <= kRopeTablePairs;
+  uint32_t rope_pos = 0;
+  if (EPI == EPI_QKV_ROPE && rope_table) {
+    rope_pos = token_position(a, 0);
+    if (rope_pos)
+      for (uint32_t i = lane; i < a.head_dim / 2; i += 32)
+        sin_cos_q30((int64_t)rope_pos * a.freqs[i], &rope_sc[i][0], &rope_sc[i][1]);
+    __syncwarp();
+  }
   unsigned long long best = 0;
   Acc128 squares{0, 0};  // EPI_RESID with a.sumsq: this lane's written values, squared
   bool ok = true;
@@ -684,7 +718,10 @@ __device__ __forceinline__ bool ring_epilogue(const ProductArgs& a, const SumRin
         if (qq == q) v0 = t0, v1 = t1;
       }
       const uint32_t row = (gfirst + k0 + q) * kQ8TileRows + 2 * pr;
-      if (q < nbat && ((fin >> q) & 1) && row + 1 < a.rows) epi_pair<EPI>(a, 0, row, v0, v1);
+      if (q < nbat && ((fin >> q) & 1) && row + 1 < a.rows) {
+        if (EPI == EPI_QKV_ROPE && rope_table) epi_pair_rope_sc(a, rope_pos, row, v0, v1, rope_sc);
+        else epi_pair<EPI>(a, 0, row, v0, v1);
+      }
       if (EPI == EPI_QKV_ROPE && a.gready) {
         // each finished group's rows, stored by this batch's lanes (ordered
         // before the adds by __syncwarp), to the attention groups reading them
