@@ -1408,14 +1408,76 @@ cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cud
   return launch_k(gemma_qkv_finish_kernel, grid, dim3(128), a.d * 4, s, a);
 }
 
-__global__ void gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
+// Sum of the squares of kPer register values a thread (saturating, as
+// block_sumsq: for non-negative terms the order does not matter), block-wide.
+template <uint32_t kPer>
+__device__ uint64_t block_sumsq_regs(const int32_t (&v)[kPer], uint64_t* red) {
+  uint64_t ss = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kPer; ++j) ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v[j] * v[j]));
+  ss = warp_sum_sat_nonneg(ss);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  uint64_t t = 0;
+  for (uint32_t w = 0; w < (blockDim.x + 31) / 32; ++w) t = add_sat_nonneg(t, red[w]);
+  return t;  // every thread
+}
+
+// Rows of at most kNormPer * blockDim.x values run from registers: each
+// thread's values i = threadIdx.x + j * blockDim.x (zero past H, which adds
+// nothing to a sum of squares). Few registers and no dynamic shared memory,
+// so that the block fits beside the product kernel still running before it
+// and its loads of weights overlap that kernel's end.
+constexpr uint32_t kNormPer = 8;
+constexpr uint32_t kNormThreads = 256;
+
+__global__ void __launch_bounds__(kNormThreads) gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
                                        const int32_t* w_pre_ffw, int64_t eps, uint32_t H,
                                        uint8_t* planes) {
+  __shared__ uint64_t red[32];
+  const uint32_t t = blockIdx.x, nt = blockDim.x;
+  if (H <= kNormPer * nt) {
+    // The norm weights never change and x was written two or more kernels
+    // earlier (the o product is the predecessor): both load before the wait.
+    int32_t w1[kNormPer], w2[kNormPer], xv[kNormPer], v[kNormPer];
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      const bool in = i < H;
+      w1[j] = in && w_post_attn ? w_post_attn[i] : 0;
+      w2[j] = in && w_pre_ffw ? w_pre_ffw[i] : 0;
+      xv[j] = in ? x[(size_t)t * H + i] : 0;
+    }
+    pdl_wait();
+    pdl_trigger();
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      v[j] = i < H ? o[(size_t)t * H + i] : 0;
+    }
+    int32_t sc = rms_scale_from_sumsq(block_sumsq_regs(v, red), H, eps);
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      const int32_t n = mul_sat(v[j], sc);
+      const int32_t y = add_sat(w_post_attn ? mul_sat(n, w1[j]) : n, xv[j]);
+      v[j] = i < H ? y : 0;
+      if (i < H) x[(size_t)t * H + i] = y;
+    }
+    sc = rms_scale_from_sumsq(block_sumsq_regs(v, red), H, eps);
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      const int32_t n = mul_sat(v[j], sc);
+      if (i < H) put_planes(planes + (size_t)t * 4 * H, H, i, w_pre_ffw ? mul_sat(n, w2[j]) : n);
+    }
+    return;
+  }
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) int32_t row[];  // [H]
-  __shared__ uint64_t red[32];
-  const uint32_t t = blockIdx.x;
   for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) row[i] = o[(size_t)t * H + i];
   __syncthreads();
   block_rms_norm(row, H, w_post_attn, eps, red);
@@ -1433,17 +1495,49 @@ cudaError_t launch_gemma_post_attn(const int32_t* o, int32_t* x, const int32_t* 
                                    const int32_t* w_pre_ffw, int64_t eps, uint32_t tokens,
                                    uint32_t hidden, uint8_t* planes, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  return launch_k(gemma_post_attn_kernel, dim3(tokens), dim3(256), hidden * 4, s, o, x, w_post_attn, w_pre_ffw, eps,
-                  hidden, planes);
+  const size_t smem = hidden <= kNormPer * kNormThreads ? 0 : hidden * 4;
+  return launch_k(gemma_post_attn_kernel, dim3(tokens), dim3(kNormThreads), smem, s, o, x, w_post_attn, w_pre_ffw,
+                  eps, hidden, planes);
 }
 
-__global__ void gemma_norm_add_kernel(const int32_t* v_in, const int32_t* add, const int32_t* w,
+__global__ void __launch_bounds__(kNormThreads) gemma_norm_add_kernel(const int32_t* v_in, const int32_t* add, const int32_t* w,
                                       int64_t eps, int32_t scalar, uint32_t H, int32_t* out) {
+  __shared__ uint64_t red[32];
+  const uint32_t t = blockIdx.x, nt = blockDim.x;
+  if (H <= kNormPer * nt) {
+    // The norm weights never change and `add` was written two or more
+    // kernels earlier (x after the FFN, xs after the PLE products): both
+    // load before the wait.
+    int32_t wv[kNormPer], av[kNormPer], v[kNormPer];
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      const bool in = i < H;
+      wv[j] = in && w ? w[i] : 0;
+      av[j] = in ? add[(size_t)t * H + i] : 0;
+    }
+    pdl_wait();
+    pdl_trigger();
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      v[j] = i < H ? v_in[(size_t)t * H + i] : 0;
+    }
+    const int32_t sc = rms_scale_from_sumsq(block_sumsq_regs(v, red), H, eps);
+#pragma unroll
+    for (uint32_t j = 0; j < kNormPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      if (i >= H) continue;
+      const int32_t y = mul_sat(v[j], sc);
+      int32_t r = add_sat(w ? mul_sat(y, wv[j]) : y, av[j]);
+      if (scalar != 0) r = mul_sat(r, scalar);  // scale_row (finish_layer, :953-955)
+      out[(size_t)t * H + i] = r;
+    }
+    return;
+  }
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) int32_t row[];
-  __shared__ uint64_t red[32];
-  const uint32_t t = blockIdx.x;
   for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) row[i] = v_in[(size_t)t * H + i];
   __syncthreads();
   block_rms_norm(row, H, w, eps, red);
@@ -1458,15 +1552,17 @@ cudaError_t launch_gemma_post_ffw(const int32_t* ff, const int32_t* x, const int
                                   int64_t eps, uint32_t tokens, uint32_t hidden, int32_t* xs,
                                   cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(256), hidden * 4, s, ff, x, w_post_ffw, eps, (int32_t)0,
-                  hidden, xs);
+  const size_t smem = hidden <= kNormPer * kNormThreads ? 0 : hidden * 4;
+  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(kNormThreads), smem, s, ff, x, w_post_ffw, eps,
+                  (int32_t)0, hidden, xs);
 }
 
 cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const int32_t* w_ple_post,
                                 int64_t eps, int32_t layer_scalar, uint32_t tokens, uint32_t hidden,
                                 int32_t* x_out, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
-  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(256), hidden * 4, s, proj, xs, w_ple_post, eps,
+  const size_t smem = hidden <= kNormPer * kNormThreads ? 0 : hidden * 4;
+  return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(kNormThreads), smem, s, proj, xs, w_ple_post, eps,
                   layer_scalar, hidden, x_out);
 }
 
