@@ -309,21 +309,46 @@ static constexpr uint64_t kLn2Q32 = 2977044472ull;
 static constexpr int64_t kHalfPi = 6746518852ll, kPi = 13493037705ll,
                          kThreeHalfPi = 20239556557ll, kTwoPi = 26986075409ll;
 
-// mistral.rs:43-56 e^-a in Q32 (Horner, products rounded down).
+IRIS_HD uint32_t mulhi_u32(uint32_t a, uint32_t b) {
+#if defined(__CUDA_ARCH__)
+  return __umulhi(a, b);
+#else
+  return (uint32_t)(((uint64_t)a * b) >> 32);
+#endif
+}
+// mistral.rs:43-56 e^-a in Q32 (Horner, products rounded down): acc_15 = 2^32,
+// acc_n = 2^32 - floor(floor(r acc_{n+1} / 2^32) / n) for n = 14 .. 1, then
+// acc_1 / 2^k. With r < ln 2 in Q32 (below 2^32) and acc <= 2^32 every step
+// fits 32-bit halves: floor(r acc / 2^32) is r when acc = 2^32, else the high
+// word of the 32 x 32-bit product, and it is below 2^32.
 IRIS_HD uint64_t exp_neg_q32(uint64_t a) {
   uint64_t k = a / kLn2Q32;
   if (k >= 32) return 0;
-  uint64_t r = a - k * kLn2Q32;
-  uint64_t acc = kOneQ32;
+  const uint32_t r = (uint32_t)(a - k * kLn2Q32);
+  uint32_t lo = 0;  // acc = 2^32 - d as its low word (0 while acc = 2^32)
+  bool top = true;  // acc = 2^32
 #pragma unroll
-  for (uint64_t n = 14; n >= 1; --n) acc = kOneQ32 - ((r * acc) >> 32) / n;
-  return acc >> k;
+  for (uint32_t n = 14; n >= 1; --n) {
+    const uint32_t t = top ? r : mulhi_u32(r, lo);
+    const uint32_t d = t / n;
+    top = d == 0;
+    lo = 0u - d;
+  }
+  return (top ? kOneQ32 : (uint64_t)lo) >> k;
 }
-// mistral.rs:59-69
+// mistral.rs:59-69. The quotient floor(2^63 / divisor), divisor in
+// [2^32, 2^33], is below 2^31 + 1: the double-precision quotient (the
+// operands exact, the result correctly rounded with 22 bits below the unit)
+// is within one of it, and one integer correction makes it exact.
 IRIS_HD uint64_t sigmoid_q32(int32_t x) {
   uint64_t mag = x < 0 ? (uint64_t)0 - (uint64_t)(int64_t)x : (uint64_t)x;
-  uint64_t divisor = kOneQ32 + exp_neg_q32(mag << 16);
-  uint64_t positive = (((uint64_t)1 << 63) / divisor) << 1;
+  const uint64_t divisor = kOneQ32 + exp_neg_q32(mag << 16);
+  const uint64_t two63 = (uint64_t)1 << 63;
+  uint64_t q = (uint64_t)(9223372036854775808.0 / (double)divisor);
+  const uint64_t p = q * divisor;  // below 2^64: q is at most one too large
+  if (p > two63) --q;
+  else if (two63 - p >= divisor) ++q;
+  const uint64_t positive = q << 1;
   return x < 0 ? kOneQ32 - positive : positive;
 }
 // mistral.rs:72-77
