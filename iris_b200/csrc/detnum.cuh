@@ -515,14 +515,18 @@ IRIS_HD void sin_cos_acc(int64_t angle, int32_t* cos_out, int32_t* sin_out) {
   *sin_out = ss < 0 ? sat_neg32(s) : s;
   *cos_out = cs < 0 ? sat_neg32(c) : c;
 }
+// One rotate-half pair (ops.rs:186-197) by an angle of cosine c and sine s.
+IRIS_HD void rotate_half_pair_cs(int32_t* lhs, int32_t* rhs, int32_t c, int32_t s) {
+  int32_t l = *lhs, r = *rhs;
+  *lhs = sub_sat(mul_sat(l, c), mul_sat(r, s));
+  *rhs = add_sat(mul_sat(r, c), mul_sat(l, s));
+}
 // One rotate-half pair (ops.rs:186-197) with a precomputed inverse frequency.
 IRIS_HD void rotate_half_pair(int32_t* lhs, int32_t* rhs, int64_t inv_frequency, uint32_t position) {
   int64_t angle = (int64_t)position * inv_frequency;  // < 2^63 for positions < 2^31
   int32_t c, s;
   sin_cos_acc(angle, &c, &s);
-  int32_t l = *lhs, r = *rhs;
-  *lhs = sub_sat(mul_sat(l, c), mul_sat(r, s));
-  *rhs = add_sat(mul_sat(r, c), mul_sat(l, s));
+  rotate_half_pair_cs(lhs, rhs, c, s);
 }
 
 }  // namespace iris

@@ -1367,23 +1367,63 @@ __device__ void block_rms_norm(int32_t* v, uint32_t n, const int32_t* w, int64_t
   __syncthreads();
 }
 
-__global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
-  pdl_wait();
-  pdl_trigger();
+// Heads of at most kQkvPer * kQkvThreads values; the norm weights (they
+// never change), the position (advanced two or more kernels earlier) and the
+// rotation's cosines and sines come before the dependent-launch wait, so that
+// they overlap the end of the q|k|v product.
+constexpr uint32_t kQkvThreads = 128, kQkvPer = 4;
+__global__ void __launch_bounds__(kQkvThreads) gemma_qkv_finish_kernel(QkvFinishArgs a) {
   extern __shared__ __align__(16) int32_t hv[];  // [d]
   __shared__ uint64_t red[32];
-  const uint32_t tok = blockIdx.x, which = blockIdx.y, d = a.d;
+  const uint32_t tok = blockIdx.x, which = blockIdx.y, d = a.d, nt = blockDim.x;
   const uint32_t qd = a.heads * d, kvd = a.kv_heads * d;
+  const bool is_q = which < a.heads, is_k = !is_q && which < a.heads + a.kv_heads;
+  const int32_t* w = is_q ? a.q_norm : is_k ? a.k_norm : nullptr;
+  const bool regs = d <= kQkvPer * nt && a.rotary_dim / 2 <= kQkvPer * nt;
   const uint32_t pos = (a.pos_ptr ? *a.pos_ptr : a.pos0) + tok;
+  const uint32_t half = a.rotary_dim / 2;
+  int32_t wv[kQkvPer], cv[kQkvPer], sv[kQkvPer];
+  if (regs) {
+#pragma unroll
+    for (uint32_t j = 0; j < kQkvPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      wv[j] = w && i < d ? w[i] : 0;
+      cv[j] = sv[j] = 0;
+      if ((is_q || is_k) && pos && i < half) sin_cos_acc((int64_t)pos * a.inv_freq[i], &cv[j], &sv[j]);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
   const int32_t* src = a.qkv + (size_t)tok * (qd + 2 * kvd) + (size_t)which * d;
-  for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) hv[i] = src[i];
+  for (uint32_t i = threadIdx.x; i < d; i += nt) hv[i] = src[i];
   __syncthreads();
-  bool is_q = which < a.heads, is_k = !is_q && which < a.heads + a.kv_heads;
-  if (is_q || is_k) {
-    block_rms_norm(hv, d, is_q ? a.q_norm : a.k_norm, a.eps, red);  // prefill_range.rs:617-624
-    uint32_t half = a.rotary_dim / 2;
+  if (regs) {
+    // block_rms_norm with the weights from registers (prefill_range.rs:617-627)
+    const int32_t scale = rms_scale_from_sumsq(block_sumsq(hv, d, red), d, a.eps);
+#pragma unroll
+    for (uint32_t j = 0; j < kQkvPer; ++j) {
+      const uint32_t i = threadIdx.x + j * nt;
+      if (i >= d) continue;
+      const int32_t y = mul_sat(hv[i], scale);
+      hv[i] = w ? mul_sat(y, wv[j]) : y;
+    }
+    __syncthreads();
+    if ((is_q || is_k) && half && pos) {  // apply_rope, prefill_range.rs:631-647
+#pragma unroll
+      for (uint32_t j = 0; j < kQkvPer; ++j) {
+        const uint32_t i = threadIdx.x + j * nt;
+        if (i >= half) continue;
+        int32_t l = hv[i], r = hv[i + half];
+        rotate_half_pair_cs(&l, &r, cv[j], sv[j]);
+        hv[i] = l;
+        hv[i + half] = r;
+      }
+      __syncthreads();
+    }
+  } else if (is_q || is_k) {
+    block_rms_norm(hv, d, w, a.eps, red);  // prefill_range.rs:617-624
     if (half && pos) {  // apply_rope, prefill_range.rs:631-647
-      for (uint32_t i = threadIdx.x; i < half; i += blockDim.x) {
+      for (uint32_t i = threadIdx.x; i < half; i += nt) {
         int32_t l = hv[i], r = hv[i + half];
         rotate_half_pair(&l, &r, a.inv_freq[i], pos);
         hv[i] = l;
@@ -1399,13 +1439,13 @@ __global__ void gemma_qkv_finish_kernel(QkvFinishArgs a) {
   else if (is_k) dst = a.kcache ? a.kcache + (size_t)pos * kvd + (size_t)(which - a.heads) * d : nullptr;
   else dst = a.vcache ? a.vcache + (size_t)pos * kvd + (size_t)(which - a.heads - a.kv_heads) * d : nullptr;
   if (dst)
-    for (uint32_t i = threadIdx.x; i < d; i += blockDim.x) dst[i] = hv[i];
+    for (uint32_t i = threadIdx.x; i < d; i += nt) dst[i] = hv[i];
 }
 
 cudaError_t launch_gemma_qkv_finish(const QkvFinishArgs& a, uint32_t tokens, cudaStream_t s) {
   if (tokens == 0) return cudaSuccess;
   dim3 grid(tokens, a.heads + 2 * a.kv_heads);
-  return launch_k(gemma_qkv_finish_kernel, grid, dim3(128), a.d * 4, s, a);
+  return launch_k(gemma_qkv_finish_kernel, grid, dim3(kQkvThreads), a.d * 4, s, a);
 }
 
 // Sum of the squares of kPer register values a thread (saturating, as
