@@ -152,6 +152,36 @@ def prefill(args):
     return {"layers": args.layers, "context": args.context, "ms": best * 1e3, "tok_s": args.context / best}
 
 
+def decode(args):
+    """Greedy decode of the Gemma-2B architecture (seeded weights) after a
+    --context-token prompt: one warm pass, then --iters passes inside an
+    NVTX range named "decode" (for ncu's --nvtx-include "decode/"), timed by
+    the host around a synchronisation."""
+    import time
+    import torch
+    from iris_b200.model import DeviceModel
+    from iris_b200.shapes import gemma_2b
+    cfg = gemma_2b()
+    model = DeviceModel(cfg, seed=args.seed)
+    model.prepare_gemm()
+    prompt = np.random.default_rng(args.seed).integers(0, cfg.vocab, size=args.context).tolist()
+    sess = model.session(args.context + args.iters + 8)
+    sess.prefill(prompt)
+    sess.decode_steps(1)
+    sess.synchronize()
+    torch.cuda.nvtx.range_push("decode")
+    t0 = time.perf_counter()
+    sess.decode_steps(args.iters)
+    sess.synchronize()
+    dt = time.perf_counter() - t0
+    torch.cuda.nvtx.range_pop()
+    out = {"model": cfg.name, "context": args.context, "steps": args.iters, "ms_per_step": dt * 1e3 / args.iters,
+           "tok_s": args.iters / dt, "kernels_per_step": sess.kernels_per_pass}
+    sess.close()
+    model.close()
+    return out
+
+
 def gemm(args):
     import torch
     from iris_b200 import _lib
@@ -355,7 +385,8 @@ def step(args):
 
 def main():
     p = argparse.ArgumentParser()
-    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep", "step", "prefill"])
+    p.add_argument("which", choices=["gemv", "attention", "gemm", "product", "sweep", "step", "prefill",
+                                      "decode"])
     p.add_argument("--product", type=int, default=2, dest="product_which")
     p.add_argument("--rows", type=int, default=28672)
     p.add_argument("--cols", type=int, default=4096)
@@ -374,7 +405,8 @@ def main():
     args = p.parse_args()
     from iris_b200 import build
     build.build()
-    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep, "step": step, "prefill": prefill}[args.which](args)), flush=True)
+    print(json.dumps({"gemv": gemv, "attention": attention, "gemm": gemm, "product": product, "sweep": sweep, "step": step, "prefill": prefill,
+                      "decode": decode}[args.which](args)), flush=True)
 
 
 if __name__ == "__main__":
