@@ -1469,10 +1469,8 @@ __device__ uint64_t block_sumsq_regs(const int32_t (&v)[kPer], uint64_t* red) {
 // thread's values i = threadIdx.x + j * blockDim.x (zero past H, which adds
 // nothing to a sum of squares). Few registers and no dynamic shared memory,
 // so that the block fits beside the product kernel still running before it
-// and its loads of weights overlap that kernel's end.
-constexpr uint32_t kNormPer = 8;
-constexpr uint32_t kNormThreads = 256;
-
+// and its loads of weights overlap that kernel's end (kNormPer, kNormThreads:
+// layers.cuh).
 __global__ void __launch_bounds__(kNormThreads) gemma_post_attn_kernel(const int32_t* o, int32_t* x, const int32_t* w_post_attn,
                                        const int32_t* w_pre_ffw, int64_t eps, uint32_t H,
                                        uint8_t* planes) {
@@ -1604,6 +1602,62 @@ cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const in
   const size_t smem = hidden <= kNormPer * kNormThreads ? 0 : hidden * 4;
   return launch_k(gemma_norm_add_kernel, dim3(tokens), dim3(kNormThreads), smem, s, proj, xs, w_ple_post, eps,
                   layer_scalar, hidden, x_out);
+}
+
+// post_ffw (gemma_norm_add_kernel with no scale) and the PLE gate product
+// for one token: each block of kNormThreads threads normalises the whole row
+// into shared memory (x and the norm weights load before the wait: x was
+// written two or more kernels earlier), block 0 stores xs, then each warp
+// takes rows of the gate product (dense_kernel's sum and gating).
+__global__ void __launch_bounds__(kNormThreads)
+    gemma_post_ffw_ple_gate_kernel(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw, int64_t eps,
+                                   uint32_t H, int32_t* xs_out, const int32_t* __restrict__ w_gate, uint32_t P,
+                                   const int32_t* gate_rows, int32_t* pg) {
+  __shared__ uint64_t red[32];
+  __shared__ __align__(16) int32_t xs[kNormPer * kNormThreads];
+  const uint32_t nt = blockDim.x;
+  int32_t wv[kNormPer], av[kNormPer], v[kNormPer];
+#pragma unroll
+  for (uint32_t j = 0; j < kNormPer; ++j) {
+    const uint32_t i = threadIdx.x + j * nt;
+    wv[j] = i < H && w_post_ffw ? w_post_ffw[i] : 0;
+    av[j] = i < H ? x[i] : 0;
+  }
+  pdl_wait();
+  pdl_trigger();
+#pragma unroll
+  for (uint32_t j = 0; j < kNormPer; ++j) {
+    const uint32_t i = threadIdx.x + j * nt;
+    v[j] = i < H ? ff[i] : 0;
+  }
+  const int32_t sc = rms_scale_from_sumsq(block_sumsq_regs(v, red), H, eps);
+#pragma unroll
+  for (uint32_t j = 0; j < kNormPer; ++j) {
+    const uint32_t i = threadIdx.x + j * nt;
+    if (i >= H) continue;
+    const int32_t y = mul_sat(v[j], sc);
+    const int32_t r = add_sat(w_post_ffw ? mul_sat(y, wv[j]) : y, av[j]);
+    xs[i] = r;
+    if (blockIdx.x == 0) xs_out[i] = r;
+  }
+  __syncthreads();
+  const uint32_t lane = threadIdx.x & 31, warps = nt / 32;
+  for (uint32_t r = blockIdx.x * warps + (threadIdx.x >> 5); r < P; r += gridDim.x * warps) {
+    const int32_t* wr = w_gate + (size_t)r * H;
+    int64_t acc = 0;
+    for (uint32_t i = lane; i < H; i += 32) acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)xs[i] * wr[i]));
+    acc = warp_sum_i64(acc);
+    if (lane == 0) pg[r] = mul_sat(gelu_tanh(requantize(acc)), gate_rows[r]);  // ple_gate_mul :931-944
+  }
+}
+
+cudaError_t launch_gemma_post_ffw_ple_gate(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw,
+                                          int64_t eps, uint32_t hidden, int32_t* xs, const int32_t* w_gate,
+                                          uint32_t P, const int32_t* gate_rows, int32_t* pg, cudaStream_t s) {
+  if (hidden > kNormPer * kNormThreads || P == 0) return cudaErrorInvalidValue;
+  const uint32_t warps = kNormThreads / 32, blocks = (P + warps - 1) / warps;
+  return launch_k(gemma_post_ffw_ple_gate_kernel, dim3(blocks), dim3(kNormThreads), 0, s, ff, x, w_post_ffw, eps,
+                  hidden, xs, w_gate, P, gate_rows, pg);
 }
 
 // Warp per (token, row) dense product.

@@ -146,6 +146,18 @@ cudaError_t launch_gemma_post_ffw(const int32_t* ff, const int32_t* x, const int
 cudaError_t launch_gemma_finish(const int32_t* proj, const int32_t* xs, const int32_t* w_ple_post,
                                 int64_t eps, int32_t layer_scalar, uint32_t tokens, uint32_t hidden,
                                 int32_t* x_out, cudaStream_t s);
+// The gemma norm kernels hold a row of at most kNormPer * kNormThreads values
+// in registers (larger rows go through shared memory).
+constexpr uint32_t kNormPer = 8;
+constexpr uint32_t kNormThreads = 256;
+// One token: post_ffw and the PLE gate product in one launch. Every block
+// computes xs = add_sat(rms_norm(ff, w_post_ffw), x) itself (block 0 also
+// stores it), then its rows of pg = mul_sat(gelu(dot_bits(xs, w_gate[r])),
+// gate_rows[r]). hidden <= 2048 (kNormPer * kNormThreads), else refused
+// with cudaErrorInvalidValue (the two-launch path serves it).
+cudaError_t launch_gemma_post_ffw_ple_gate(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw,
+                                          int64_t eps, uint32_t hidden, int32_t* xs, const int32_t* w_gate,
+                                          uint32_t P, const int32_t* gate_rows, int32_t* pg, cudaStream_t s);
 // Dense Q16.16 products: out[t][r] = dot_bits(in[t], w[r]) (tensor.rs:522-528),
 // optionally gated: out = mul_sat(gelu(dot), gate_rows[t][r]).
 cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const int32_t* in,

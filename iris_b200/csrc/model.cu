@@ -716,10 +716,16 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   dn.planes = s->planes2;
   dn.out = s->tmp;
   e = launch_product(dn, IN_PLANES, EPI_STORE, st);
-  if (e == cudaSuccess) e = launch_gemma_post_ffw(s->tmp, s->x, L.norm_post_ffw, m->eps, tokens, m->H, s->xs, st);
-  if (e == cudaSuccess)
-    e = launch_dense(L.ple_gate, m->P, m->H, s->xs, m->H, tokens, s->pg, m->P,
-                     s->ple_rows + (size_t)l * m->P, m->L * m->P, st);
+  if (e != cudaSuccess) return e;
+  if (tokens == 1 && m->P && m->H <= kNormPer * kNormThreads) {  // one launch for post_ffw and the PLE gate
+    e = launch_gemma_post_ffw_ple_gate(s->tmp, s->x, L.norm_post_ffw, m->eps, m->H, s->xs, L.ple_gate, m->P,
+                                       s->ple_rows + (size_t)l * m->P, s->pg, st);
+  } else {
+    e = launch_gemma_post_ffw(s->tmp, s->x, L.norm_post_ffw, m->eps, tokens, m->H, s->xs, st);
+    if (e == cudaSuccess)
+      e = launch_dense(L.ple_gate, m->P, m->H, s->xs, m->H, tokens, s->pg, m->P,
+                       s->ple_rows + (size_t)l * m->P, m->L * m->P, st);
+  }
   if (e == cudaSuccess) e = launch_dense(L.ple_proj, m->H, m->P, s->pg, m->P, tokens, s->tmp, m->H, nullptr, 0, st);
   if (e == cudaSuccess)
     e = launch_gemma_finish(s->tmp, s->xs, L.ple_post_norm, m->eps, L.layer_scalar, tokens, m->H, s->x, st);
