@@ -1660,6 +1660,66 @@ cudaError_t launch_gemma_post_ffw_ple_gate(const int32_t* ff, const int32_t* x, 
                   hidden, xs, w_gate, P, gate_rows, pg);
 }
 
+// The PLE projection's rows (a warp a row, dense_kernel's sum) and, in the
+// block that completes the row, gemma_norm_add_kernel's layer finish. The
+// completion count is a release/acquire pair on *done (no block waits for
+// another), and the finishing block reads the other blocks' rows through L2.
+__global__ void __launch_bounds__(kNormThreads)
+    gemma_ple_proj_finish_kernel(const int32_t* pg, const int32_t* __restrict__ w_proj, uint32_t P, uint32_t H,
+                                 int32_t* proj, const int32_t* xs, const int32_t* w_ple_post, int64_t eps,
+                                 int32_t scalar, int32_t* x_out, unsigned int* done) {
+  __shared__ uint64_t red[32];
+  __shared__ bool last;
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t lane = threadIdx.x & 31, nt = blockDim.x;
+  const uint32_t r = blockIdx.x * (nt / 32) + (threadIdx.x >> 5);
+  if (r < H) {
+    const int32_t* wr = w_proj + (size_t)r * P;
+    int64_t acc = 0;
+    for (uint32_t i = lane; i < P; i += 32) acc = (int64_t)((uint64_t)acc + (uint64_t)((int64_t)pg[i] * wr[i]));
+    acc = warp_sum_i64(acc);
+    if (lane == 0) proj[r] = requantize(acc);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atom_add_acq_rel(done, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  int32_t wv[kNormPer], av[kNormPer], v[kNormPer];
+#pragma unroll
+  for (uint32_t j = 0; j < kNormPer; ++j) {
+    const uint32_t i = threadIdx.x + j * nt;
+    const bool in = i < H;
+    wv[j] = in && w_ple_post ? w_ple_post[i] : 0;
+    av[j] = in ? xs[i] : 0;
+    v[j] = in ? __ldcg(proj + i) : 0;
+  }
+  const int32_t sc = rms_scale_from_sumsq(block_sumsq_regs(v, red), H, eps);
+#pragma unroll
+  for (uint32_t j = 0; j < kNormPer; ++j) {
+    const uint32_t i = threadIdx.x + j * nt;
+    if (i >= H) continue;
+    const int32_t y = mul_sat(v[j], sc);
+    int32_t o = add_sat(w_ple_post ? mul_sat(y, wv[j]) : y, av[j]);
+    if (scalar != 0) o = mul_sat(o, scalar);  // scale_row (finish_layer, :953-955)
+    x_out[i] = o;
+  }
+  if (threadIdx.x == 0) *done = 0;
+}
+
+cudaError_t launch_gemma_ple_proj_finish(const int32_t* pg, const int32_t* w_proj, uint32_t P, uint32_t hidden,
+                                         int32_t* proj, const int32_t* xs, const int32_t* w_ple_post, int64_t eps,
+                                         int32_t layer_scalar, int32_t* x_out, unsigned int* done,
+                                         cudaStream_t s) {
+  if (hidden > kNormPer * kNormThreads || P == 0 || hidden == 0) return cudaErrorInvalidValue;
+  const uint32_t warps = kNormThreads / 32, blocks = (hidden + warps - 1) / warps;
+  return launch_k(gemma_ple_proj_finish_kernel, dim3(blocks), dim3(kNormThreads), 0, s, pg, w_proj, P, hidden, proj,
+                  xs, w_ple_post, eps, layer_scalar, x_out, done);
+}
+
 // Warp per (token, row) dense product.
 __global__ void dense_kernel(const int32_t* __restrict__ w, uint32_t rows, uint32_t cols,
                              const int32_t* __restrict__ in, uint32_t in_stride, uint32_t tokens,

@@ -158,6 +158,15 @@ constexpr uint32_t kNormThreads = 256;
 cudaError_t launch_gemma_post_ffw_ple_gate(const int32_t* ff, const int32_t* x, const int32_t* w_post_ffw,
                                           int64_t eps, uint32_t hidden, int32_t* xs, const int32_t* w_gate,
                                           uint32_t P, const int32_t* gate_rows, int32_t* pg, cudaStream_t s);
+// One token: the PLE projection and the layer finish in one launch. Each
+// warp writes rows proj[r] = dot_bits(pg, w_proj[r]); the block that
+// completes the row (the last to add to *done, which it clears again) then
+// writes x = [layer_scalar *] add_sat(rms_norm(proj, w_ple_post), xs).
+// hidden <= kNormPer * kNormThreads, else refused with cudaErrorInvalidValue.
+cudaError_t launch_gemma_ple_proj_finish(const int32_t* pg, const int32_t* w_proj, uint32_t P, uint32_t hidden,
+                                         int32_t* proj, const int32_t* xs, const int32_t* w_ple_post, int64_t eps,
+                                         int32_t layer_scalar, int32_t* x_out, unsigned int* done,
+                                         cudaStream_t s);
 // Dense Q16.16 products: out[t][r] = dot_bits(in[t], w[r]) (tensor.rs:522-528),
 // optionally gated: out = mul_sat(gelu(dot), gate_rows[t][r]).
 cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const int32_t* in,
