@@ -204,6 +204,83 @@ __device__ __forceinline__ int32_t epi_single(const ProductArgs& a, uint32_t t, 
 }
 
 
+// IN_POST_ATTN (gemma's post-attention step, prefill_range.rs post_attention
+// and pre_feedforward norms) fused into the gate|up product's prologue:
+// x' = add_sat(rms_norm(o, post_w), x), then the byte planes of
+// rms_norm(x', norm_w), each norm as row_to_planes' (two mul_sat a value).
+// Every block computes the row itself; block 0 stores x' to post_x. The row
+// is held in registers: K <= 2 * 4 * part_threads<NT>() (the host checks).
+template <uint32_t NT = 0>
+__device__ __forceinline__ bool post_attn_to_planes(const ProductArgs& a, uint32_t K, uint8_t* planes,
+                                                    uint64_t* red, int32_t* s_scale) {
+  constexpr uint32_t kHeld = 2;
+  const uint32_t step = part_threads<NT>() * 4;
+  const int4 z = make_int4(0, 0, 0, 0);
+  int4 ov[kHeld], xv[kHeld], w1[kHeld], w2[kHeld];
+#pragma unroll
+  for (uint32_t j = 0; j < kHeld; ++j) {
+    const uint32_t i = threadIdx.x * 4 + j * step;
+    const bool in = i < K;
+    ov[j] = in ? __ldcg((const int4*)(a.post_o + i)) : z;
+    xv[j] = in ? __ldcg((const int4*)(a.x + i)) : z;
+    w1[j] = in && a.post_w ? *(const int4*)(a.post_w + i) : z;
+    w2[j] = in && a.norm_w ? *(const int4*)(a.norm_w + i) : z;
+  }
+  auto sq4 = [](uint64_t ss, int4 v) {
+    ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.x * v.x));
+    ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.y * v.y));
+    ss = add_sat_nonneg(ss, (uint64_t)((int64_t)v.z * v.z));
+    return add_sat_nonneg(ss, (uint64_t)((int64_t)v.w * v.w));
+  };
+  auto row_scale = [&](uint64_t ss) {
+    const uint64_t total = block_sum_sat<NT>(ss, red);  // in every lane of warp 0
+    if (threadIdx.x < 32) {
+      const int32_t sc = inv_sqrt_acc_fast(acc_add_sat((int64_t)div_round_even_width(total, K), a.eps));
+      if (threadIdx.x == 0) *s_scale = sc;
+    }
+    part_sync<NT>();
+    return *s_scale;
+  };
+  auto norm1 = [](int32_t v, int32_t sc, int32_t w, bool weighted) {
+    const int32_t y = mul_sat(v, sc);
+    return weighted ? mul_sat(y, w) : y;
+  };
+  uint64_t ss = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kHeld; ++j) ss = sq4(ss, ov[j]);
+  const int32_t sc1 = row_scale(ss);
+  const bool wp = a.post_w != nullptr, wn = a.norm_w != nullptr;
+  ss = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kHeld; ++j) {
+    const uint32_t i = threadIdx.x * 4 + j * step;
+    int4 v = xv[j];
+    v.x = add_sat(norm1(ov[j].x, sc1, w1[j].x, wp), v.x);
+    v.y = add_sat(norm1(ov[j].y, sc1, w1[j].y, wp), v.y);
+    v.z = add_sat(norm1(ov[j].z, sc1, w1[j].z, wp), v.z);
+    v.w = add_sat(norm1(ov[j].w, sc1, w1[j].w, wp), v.w);
+    if (i >= K) v = z;
+    xv[j] = v;
+    if (blockIdx.x == 0 && i < K) *(int4*)(a.post_x + i) = v;
+    ss = sq4(ss, v);
+  }
+  const int32_t sc2 = row_scale(ss);
+  int wide = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < kHeld; ++j) {
+    const uint32_t i = threadIdx.x * 4 + j * step;
+    if (i >= K) continue;
+    int4 v = xv[j];
+    v.x = norm1(v.x, sc2, w2[j].x, wn);
+    v.y = norm1(v.y, sc2, w2[j].y, wn);
+    v.z = norm1(v.z, sc2, w2[j].z, wn);
+    v.w = norm1(v.w, sc2, w2[j].w, wn);
+    wide |= !fits_three_planes(v.x) | !fits_three_planes(v.y) | !fits_three_planes(v.z) | !fits_three_planes(v.w);
+    put_planes4(planes, K, i, v);
+  }
+  return part_or<NT>(wide);
+}
+
 // ---------------------------------------------------------------------------
 // Decode GEMV pieces
 // ---------------------------------------------------------------------------

@@ -159,7 +159,8 @@ struct IrisSession {
   int32_t* wsum = nullptr;
   int64_t* acc = nullptr;
   unsigned int* counters = nullptr;
-  unsigned int* ple_done = nullptr;  // gemma: blocks done with the PLE projection (zero between launches)
+  unsigned int* ple_done = nullptr;
+  int32_t* xa = nullptr;  // gemma, one token: the residual row after attention (IN_POST_ATTN)  // gemma: blocks done with the PLE projection (zero between launches)
   uint32_t nchunks = 0, hpc = 1;
   uint32_t cluster = 0, chpc = 1, span = 0, ring = 0;  // one-launch cluster decode attention
   uint32_t chunks = 0, ghpc = 1, gspan = 0;               // one-launch whole-GPU decode attention
@@ -221,7 +222,7 @@ void free_session(IrisSession* s) {
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
                   s->stages, s->sync, s->gready, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf,
-                  s->ple_done};
+                  s->ple_done, s->xa};
   if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
   for (int b = 0; b < 2; ++b) cudaFree(s->stage_leaves[b]);
   for (void* p : ptrs) cudaFree(p);
@@ -433,6 +434,7 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
     if (e == cudaSuccess) e = dalloc(&s->ple_rows, (size_t)R * m->L * m->P);
     if (e == cudaSuccess) e = dalloc(&s->ple_proj, (size_t)R * m->L * m->P);
     if (e == cudaSuccess) e = dalloc(&s->ple_done, 1);
+    if (e == cudaSuccess) e = dalloc(&s->xa, (size_t)m->H);
     if (e == cudaSuccess) e = cudaMemset(s->ple_done, 0, sizeof(unsigned int));
   }
   s->nchunks = attention_chunks(cap);
@@ -708,13 +710,26 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   o.planes = s->planes;
   o.out = s->tmp;
   e = launch_product(o, IN_PLANES, EPI_STORE, st);
-  if (e == cudaSuccess)
-    e = launch_gemma_post_attn(s->tmp, s->x, L.norm_post_attn, L.norm_ffn, m->eps, tokens, m->H, s->planes, st);
   if (e != cudaSuccess) return e;
   ProductArgs g = session_product_args(s, L.gu, tokens);
-  g.planes = s->planes;
   g.out_planes = s->planes2;
-  e = launch_product(g, IN_PLANES, EPI_GELU_MUL, st);
+  // One token: the post-attention norms run in the gate|up product's
+  // prologue (IN_POST_ATTN), the new residual row going to xa
+  const bool post_fused = tokens == 1 && m->H <= kPostAttnMaxCols;
+  const int32_t* x_attn = post_fused ? s->xa : s->x;  // the residual row after attention
+  if (post_fused) {
+    g.post_o = s->tmp;
+    g.post_w = L.norm_post_attn;
+    g.post_x = s->xa;
+    g.x = s->x;
+    g.norm_w = L.norm_ffn;
+    g.eps = m->eps;
+    e = launch_product(g, IN_POST_ATTN, EPI_GELU_MUL, st);
+  } else {
+    e = launch_gemma_post_attn(s->tmp, s->x, L.norm_post_attn, L.norm_ffn, m->eps, tokens, m->H, s->planes, st);
+    g.planes = s->planes;
+    if (e == cudaSuccess) e = launch_product(g, IN_PLANES, EPI_GELU_MUL, st);
+  }
   if (e != cudaSuccess) return e;
   ProductArgs dn = session_product_args(s, L.down, tokens);
   dn.planes = s->planes2;
@@ -722,10 +737,10 @@ cudaError_t gemma_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uint3
   e = launch_product(dn, IN_PLANES, EPI_STORE, st);
   if (e != cudaSuccess) return e;
   if (tokens == 1 && m->P && m->H <= kNormPer * kNormThreads) {  // one launch for post_ffw and the PLE gate
-    e = launch_gemma_post_ffw_ple_gate(s->tmp, s->x, L.norm_post_ffw, m->eps, m->H, s->xs, L.ple_gate, m->P,
+    e = launch_gemma_post_ffw_ple_gate(s->tmp, x_attn, L.norm_post_ffw, m->eps, m->H, s->xs, L.ple_gate, m->P,
                                        s->ple_rows + (size_t)l * m->P, s->pg, st);
   } else {
-    e = launch_gemma_post_ffw(s->tmp, s->x, L.norm_post_ffw, m->eps, tokens, m->H, s->xs, st);
+    e = launch_gemma_post_ffw(s->tmp, x_attn, L.norm_post_ffw, m->eps, tokens, m->H, s->xs, st);
     if (e == cudaSuccess)
       e = launch_dense(L.ple_gate, m->P, m->H, s->xs, m->H, tokens, s->pg, m->P,
                        s->ple_rows + (size_t)l * m->P, m->L * m->P, st);

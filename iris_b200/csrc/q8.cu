@@ -454,6 +454,8 @@ __global__ void __launch_bounds__(kTmaThreads, 1) q8_gemv_tma_kernel(ProductArgs
            !planes_sign_extended(v2.z, v3.z) | !planes_sign_extended(v2.w, v3.w);
     }
     wide = __syncthreads_or(w) != 0;
+  } else if (IN == IN_POST_ATTN) {
+    wide = post_attn_to_planes(a, K, planes, red, &s_scale);
   } else {
     wide = row_to_planes(a.x, IN == IN_NORM ? a.norm_w : nullptr, a.eps, K, planes, red, &s_scale);
   }
@@ -900,6 +902,7 @@ cudaError_t prepare_product_kernels() {
   cudaError_t e = prepare_gemv_in<IN_PLANES>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_NORM>();
   if (e == cudaSuccess) e = prepare_gemv_in<IN_RAW>();
+  if (e == cudaSuccess) e = prepare_gemv_one<IN_POST_ATTN, EPI_GELU_MUL>();
   if (e == cudaSuccess) e = prepare_tc_kernels();
   return e;
 }
@@ -946,6 +949,10 @@ cudaError_t launch_product(const ProductArgs& a0, InMode in, EpiMode epi, cudaSt
       case IN_PLANES: return dispatch_gemv<IN_PLANES>(a, epi, stream);
       case IN_NORM: return dispatch_gemv<IN_NORM>(a, epi, stream);
       case IN_RAW: return dispatch_gemv<IN_RAW>(a, epi, stream);
+      case IN_POST_ATTN:
+        static_assert(kPostAttnMaxCols == 2 * 4 * kTmaThreads, "IN_POST_ATTN holds two int4 a thread");
+        if (epi != EPI_GELU_MUL || a.cols > kPostAttnMaxCols) return cudaErrorInvalidValue;
+        return launch_gemv<IN_POST_ATTN, EPI_GELU_MUL>(a, stream);
     }
     return cudaErrorInvalidValue;
   }

@@ -81,7 +81,15 @@ __host__ __device__ inline size_t q8_scale_offset(uint32_t kc, uint32_t nslices,
   return (tile * kQ8TileRows + row % kQ8TileRows) * bps + block % bps;
 }
 
-enum InMode { IN_PLANES = 0, IN_NORM = 1, IN_RAW = 2 };
+enum InMode {
+  IN_PLANES = 0,
+  IN_NORM = 1,
+  IN_RAW = 2,
+  // gemma, one token: planes of rms_norm(x', norm_w), x' = add_sat(rms_norm(post_o,
+  // post_w), x); block 0 stores x' to post_x (decode GEMV with EPI_GELU_MUL only)
+  IN_POST_ATTN = 3
+};
+constexpr uint32_t kPostAttnMaxCols = 4608;  // IN_POST_ATTN rows: two int4 a thread of the decode GEMV
 enum EpiMode {
   EPI_STORE = 0,     // out[row] = v
   EPI_RESID = 1,     // out[row] = add_sat(v, resid[row])
@@ -138,6 +146,11 @@ struct ProductArgs {
   // group of gready_hpc query heads that reads those rows
   unsigned int* gready;
   uint32_t gready_hpc;
+  // IN_POST_ATTN: the attention output product's row, its norm weights, and
+  // where block 0 stores the new residual row (not x: other blocks read x)
+  const int32_t* post_o;
+  const int32_t* post_w;
+  int32_t* post_x;
 };
 
 ProductArgs product_args(const Q8GpuMatrix* w, uint32_t tokens);
