@@ -102,9 +102,30 @@ IRIS_HD int64_t div_round_even_s64(int64_t n, int64_t d) {
   return neg ? -(int64_t)q : (int64_t)q;
 }
 
-// ops.rs:53-64 div_act: (n << 16) / d, ties to even, saturated to i32.
+// ops.rs:53-64 div_act: (n << 16) / d, ties to even, saturated to i32. The
+// magnitudes are below 2^48 and 2^32, exact in double precision, so the
+// correctly rounded double quotient is within one of floor(|n 2^16| / |d|);
+// one integer correction makes it exact, then the remainder rounds it (ties
+// to even) as div_round_even_s64 does.
 IRIS_HD int32_t div_act(int32_t n, int32_t d) {
-  return clamp_i32(div_round_even_s64((int64_t)n * 65536, (int64_t)d));
+  if (d == 0) return clamp_i32(div_round_even_s64((int64_t)n * 65536, (int64_t)d));
+  const int64_t num = (int64_t)n * 65536;
+  const bool neg = (num < 0) != (d < 0);
+  const uint64_t un = num < 0 ? (uint64_t)0 - (uint64_t)num : (uint64_t)num;
+  const uint64_t ud = d < 0 ? (uint64_t)0 - (uint64_t)(int64_t)d : (uint64_t)d;
+  uint64_t q = (uint64_t)((double)un / (double)ud);
+  int64_t r = (int64_t)(un - q * ud);
+  if (r < 0) {
+    --q;
+    r += (int64_t)ud;
+  } else if ((uint64_t)r >= ud) {
+    ++q;
+    r -= (int64_t)ud;
+  }
+  const uint64_t other = ud - (uint64_t)r;  // distance to the next multiple
+  if ((uint64_t)r > other) ++q;
+  else if ((uint64_t)r == other) q += q & 1;
+  return clamp_i32(neg ? -(int64_t)q : (int64_t)q);
 }
 
 // ops.rs:685-689 acc_mul for non-negative operands whose product is below
