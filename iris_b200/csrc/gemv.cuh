@@ -146,14 +146,24 @@ __device__ __forceinline__ void epi_pair(const ProductArgs& a, uint32_t t, uint3
                                          int32_t v1) {
   if (EPI == EPI_QKV_ROPE) {
     uint32_t pos = token_position(a, t);
+    // the rotation of frequency f at this token's position: from the
+    // precomputed table when there is one (the same sin_cos_q30 values)
+    auto rotate = [&](uint32_t f) {
+      if (!a.rope_sc) {
+        rotate_pair_q30(&v0, &v1, a.freqs[f], pos);
+      } else if (pos) {
+        const int64_t* sc = a.rope_sc + ((size_t)t * (a.head_dim / 2) + f) * 2;
+        rotate_pair_sc(&v0, &v1, sc[0], sc[1]);
+      }
+    };
     if (row < a.qd) {
-      rotate_pair_q30(&v0, &v1, a.freqs[(row % a.head_dim) >> 1], pos);
+      rotate((row % a.head_dim) >> 1);
       int32_t* o = a.out + (size_t)t * a.out_stride + row;
       o[0] = v0;
       o[1] = v1;
     } else if (row < a.qd + a.kvd) {
       uint32_t c = row - a.qd;
-      rotate_pair_q30(&v0, &v1, a.freqs[(c % a.head_dim) >> 1], pos);
+      rotate((c % a.head_dim) >> 1);
       int32_t* o = a.kcache + (size_t)pos * a.kvd + c;
       o[0] = v0;
       o[1] = v1;

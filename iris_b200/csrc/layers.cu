@@ -1720,6 +1720,24 @@ cudaError_t launch_gemma_ple_proj_finish(const int32_t* pg, const int32_t* w_pro
                   xs, w_ple_post, eps, layer_scalar, x_out, done);
 }
 
+__global__ void rope_table_kernel(const int64_t* freqs, uint32_t half, const uint32_t* pos_ptr, uint32_t pos0,
+                                  uint32_t tokens, int64_t* out) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= tokens * half) return;
+  const uint32_t t = j / half, i = j % half;
+  const uint32_t pos = (pos_ptr ? *pos_ptr : pos0) + t;
+  sin_cos_q30((int64_t)pos * freqs[i], out + 2 * (size_t)j, out + 2 * (size_t)j + 1);
+}
+
+cudaError_t launch_rope_table(const int64_t* freqs, uint32_t half, const uint32_t* pos_ptr, uint32_t pos0,
+                              uint32_t tokens, int64_t* out, cudaStream_t s) {
+  const uint32_t n = tokens * half;
+  if (n == 0) return cudaSuccess;
+  return launch_k(rope_table_kernel, dim3((n + 255) / 256), dim3(256), 0, s, freqs, half, pos_ptr, pos0, tokens, out);
+}
+
 // Warp per (token, row) dense product.
 __global__ void dense_kernel(const int32_t* __restrict__ w, uint32_t rows, uint32_t cols,
                              const int32_t* __restrict__ in, uint32_t in_stride, uint32_t tokens,

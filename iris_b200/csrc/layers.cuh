@@ -167,6 +167,11 @@ cudaError_t launch_gemma_ple_proj_finish(const int32_t* pg, const int32_t* w_pro
                                          int32_t* proj, const int32_t* xs, const int32_t* w_ple_post, int64_t eps,
                                          int32_t layer_scalar, int32_t* x_out, unsigned int* done,
                                          cudaStream_t s);
+// The Q2.30 sine and cosine (sin_cos_q30, mistral.rs:84-110) of each of
+// `half` inverse frequencies at the positions of `tokens` tokens from
+// (*pos_ptr or pos0): out[t][i][0..1], for the many-token q|k|v epilogue.
+cudaError_t launch_rope_table(const int64_t* freqs, uint32_t half, const uint32_t* pos_ptr, uint32_t pos0,
+                              uint32_t tokens, int64_t* out, cudaStream_t s);
 // Dense Q16.16 products: out[t][r] = dot_bits(in[t], w[r]) (tensor.rs:522-528),
 // optionally gated: out = mul_sat(gelu(dot), gate_rows[t][r]).
 cudaError_t launch_dense(const int32_t* w, uint32_t rows, uint32_t cols, const int32_t* in,

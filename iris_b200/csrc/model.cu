@@ -160,7 +160,8 @@ struct IrisSession {
   int64_t* acc = nullptr;
   unsigned int* counters = nullptr;
   unsigned int* ple_done = nullptr;
-  int32_t* xa = nullptr;  // gemma, one token: the residual row after attention (IN_POST_ATTN)  // gemma: blocks done with the PLE projection (zero between launches)
+  int32_t* xa = nullptr;  // gemma, one token: the residual row after attention (IN_POST_ATTN)
+  int64_t* rope_sc = nullptr;  // mistral: [rows][d / 2][2] sines and cosines of a range's positions  // gemma: blocks done with the PLE projection (zero between launches)
   uint32_t nchunks = 0, hpc = 1;
   uint32_t cluster = 0, chpc = 1, span = 0, ring = 0;  // one-launch cluster decode attention
   uint32_t chunks = 0, ghpc = 1, gspan = 0;               // one-launch whole-GPU decode attention
@@ -222,7 +223,7 @@ void free_session(IrisSession* s) {
                   s->d_history, s->scores, s->terms, s->chunk_best, s->chunk_sum, s->wsum,
                   s->acc, s->counters, s->split_acc, s->split_count, s->gbest, s->gsum, s->gbar, s->partial, s->logits_full,
                   s->stages, s->sync, s->gready, s->trace, s->sumsq, s->kslots, s->sslots, s->attn_tc_buf,
-                  s->ple_done, s->xa};
+                  s->ple_done, s->xa, s->rope_sc};
   if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
   for (int b = 0; b < 2; ++b) cudaFree(s->stage_leaves[b]);
   for (void* p : ptrs) cudaFree(p);
@@ -436,6 +437,8 @@ int create_session(IrisModel* m, uint32_t cap, IrisSession** out) {
     if (e == cudaSuccess) e = dalloc(&s->ple_done, 1);
     if (e == cudaSuccess) e = dalloc(&s->xa, (size_t)m->H);
     if (e == cudaSuccess) e = cudaMemset(s->ple_done, 0, sizeof(unsigned int));
+  } else if (m->freqs) {
+    if (e == cudaSuccess) e = dalloc(&s->rope_sc, (size_t)R * (m->d / 2) * 2);
   }
   s->nchunks = attention_chunks(cap);
   s->hpc = attention_hpc(m->heads, m->kvh);
@@ -627,6 +630,10 @@ cudaError_t mistral_layer(IrisSession* s, uint32_t l, uint32_t tokens, const uin
   } else {
     e = launch_planes(s->x, L.norm_attn, m->eps, tokens, m->H, s->planes, st);
     a.planes = s->planes;
+    if (e == cudaSuccess && s->rope_sc) {  // each position's rotations once, not once a row pair
+      e = launch_rope_table(m->freqs, m->d / 2, pos_ptr, pos0, tokens, s->rope_sc, st);
+      a.rope_sc = s->rope_sc;
+    }
     if (e == cudaSuccess) e = launch_product(a, IN_PLANES, EPI_QKV_ROPE, st);
   }
   if (e != cudaSuccess) return e;

@@ -146,6 +146,9 @@ struct ProductArgs {
   // group of gready_hpc query heads that reads those rows
   unsigned int* gready;
   uint32_t gready_hpc;
+  // Many-token EPI_QKV_ROPE (optional): the Q2.30 sine and cosine of every
+  // frequency at each token's position, [tokens][head_dim / 2][2]
+  const int64_t* rope_sc;
   // IN_POST_ATTN: the attention output product's row, its norm weights, and
   // where block 0 stores the new residual row (not x: other blocks read x)
   const int32_t* post_o;
